@@ -1,0 +1,439 @@
+"""Benchmark of the EWS hot path (forward + custom-VJP backward) on 1..8 B200 GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl b200|reference]
+
+One step = one forward + backward of the EWS layer over one batch of the configuration's synthetic
+inputs through the package's public API (EWS / LogEWS with the fused lift), the loss sum(w * out), and
+for N > 1 the single NCCL allreduce of the parameter gradients. Prints one JSON line on rank 0.
+`value` is whole-job batch*steps/s with inputs resident in HBM; `e2e` is the same metric with the
+inputs copied from pinned host memory and the loss read back inside every timed step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "EWS fwd+bwd (batch·steps)/s at 1/2/4/8 B200, % HBM/TC roofline vs JAX CPU"
+UNIT = "batch·steps/s"
+L2_BYTES = 126 * 1024 * 1024
+KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 2}
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------ workloads
+
+
+def _diag_setup(cfg, rank, world, device, precision):
+    """Per-rank inputs and model of a diagonal-engine configuration (config1, config5)."""
+    from exponentially_weighted_signature_b200 import EWS, LogEWS, AParamDiag, B as Lift, workloads, series
+    from exponentially_weighted_signature_b200.parallel import shard_range
+
+    case = getattr(workloads, cfg)()
+    Bg, T, N = case["B"], case["T"], case["N"]
+    if Bg % world == 0:
+        s0, s1 = shard_range(Bg, rank, world)
+        scaling = "strong"
+    else:  # too few samples to shard: every rank runs the whole batch
+        s0, s1 = 0, Bg
+        scaling = "weak"
+    x_max = float(np.max(case["lam"])) / T
+    q = max(2, series.suggest_series_q(x_max, 2, 1e-14))
+    A = AParamDiag(torch.tensor(case["lam"], dtype=torch.float32))
+    lift = Lift(torch.tensor(case["lift"], dtype=torch.float32), preserve_first_channel=False)
+    kw = dict(reweighting_mode="displacement_uniform", series_q=q)
+    if cfg == "config5":
+        layer = LogEWS(A, N=2, **kw)
+        readout = "terminal"
+        increments = True
+        x_host = torch.from_numpy(case["increments"][s0:s1])
+        if precision == "bf16":
+            x_host = x_host.to(torch.bfloat16)
+    else:
+        layer = EWS(A, N=2, **kw)
+        readout = "prefix"
+        increments = False
+        x_host = torch.tensor(case["path"][s0:s1], dtype=torch.float32)
+    clock_host = torch.tensor(case["clock"][s0:s1], dtype=torch.float32)
+    layer = layer.to(device)
+    lift = lift.to(device)
+    params = list(layer.parameters()) + list(lift.parameters())
+    Bl = s1 - s0
+    D = N + N * N
+    out_shape = (Bl, 528) if cfg == "config5" else (Bl, T, 1 + D)
+    g = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    w = torch.randn(out_shape, generator=g).to(device)
+
+    def step(x, clock):
+        out = layer(x, clock, readout=readout, lift=lift.full_matrix(), increments=increments)
+        loss = (out * w).sum()
+        loss.backward()
+        return loss
+
+    d_in = x_host.shape[-1]
+    in_bytes = 2 if x_host.dtype == torch.bfloat16 else 4
+    # algorithmic bytes per unit (one sample-interval) of each kernel: inputs read once, outputs written
+    # once; the backward reads the output gradient and writes the input-increment gradient
+    out_row = 4 * (1 + D) if readout == "prefix" else 0
+    alg = {
+        "ews_diag_fwd": in_bytes * d_in + out_row,
+        "ews_diag_bwd": in_bytes * d_in + out_row + 4 * d_in,
+    }
+    meta = dict(B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout=readout, dtype="f32",
+                precision=("bf16 increments, f32 accumulation" if in_bytes == 2 else "f32"))
+    ws_bytes = x_host.numel() * in_bytes + (Bl * T * out_row)
+    return dict(step=step, params=params, x_host=x_host, clock_host=clock_host, alg=alg, meta=meta,
+                ws_bytes=ws_bytes, units=Bl * T, case=case)
+
+
+# ------------------------------------------------------------------------------------ helpers
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
+                                     hw=parts[5], hwt=parts[6], swt=parts[7], swp=parts[8]))
+                except ValueError:
+                    continue
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        loaded = [r for r in rows if r["power"] > 200.0] or rows
+        reasons = []
+        for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"), ("swp", "sw_power_cap")):
+            if any(r[key].lower() == "active" for r in loaded):
+                reasons.append(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": reasons, "samples": len(loaded)}
+
+
+def _flush_l2(buf):
+    if buf is not None:
+        buf.add_(1.0)
+
+
+def _cpu_baseline(cfg, precision, budget_s=20.0):
+    """The oracle port of the reference's CPU path (series leaf + associative modified-Chen scan, autograd
+    backward; float32 as the reference's f32 layer) timed on the host cores over a bounded sample."""
+    from oracle import ews_oracle as O
+    from exponentially_weighted_signature_b200 import workloads, series
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    case = getattr(workloads, cfg)(B=1)
+    T = case["T"]
+    lam = torch.tensor(case["lam"], dtype=torch.float32)
+    lift = torch.tensor(case["lift"], dtype=torch.float32)
+    q = max(2, series.suggest_series_q(float(case["lam"].max()) / T, 2, 1e-14))
+    if cfg == "config5":
+        inc = torch.tensor(case["increments"][:1], dtype=torch.float32)
+        path = torch.cat([torch.zeros(1, 1, inc.shape[-1]), torch.cumsum(inc, 1)], 1)
+    else:
+        path = torch.tensor(case["path"][:1], dtype=torch.float32)
+    clock = torch.tensor(case["clock"][:1], dtype=torch.float32)
+    # sample: the first Ts intervals of one path, grown until the run takes a measurable time
+    Ts = min(T, 256)
+    done_units, spent, runs = 0, 0.0, 0
+    while spent < budget_s and runs < 50:
+        p = path[:, : Ts + 1].clone().requires_grad_(True)
+        A = lam.clone().requires_grad_(True)
+        Bm = lift.clone().requires_grad_(True)
+        t0 = time.perf_counter()
+        y = O.lift(p, Bm)
+        if cfg == "config5":
+            out = O.log_ews_layer(y, clock[:, : Ts + 1], torch.diag(A), 2, series_q=q, reweighting_mode="displacement_uniform", readout="terminal", terminal_reduce="assoc")
+        else:
+            out = O.ews_layer(y, clock[:, : Ts + 1], torch.diag(A), 2, series_q=q, reweighting_mode="displacement_uniform", readout="prefix")
+        out.sum().backward()
+        dt = time.perf_counter() - t0
+        spent += dt
+        done_units += Ts
+        runs += 1
+        if dt < 2.0 and Ts < T:
+            Ts = min(T, Ts * 2)
+    return {"value": done_units / spent, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{runs} runs of 1 path x up to {Ts} intervals of {cfg} (float32 oracle port: series leaf + "
+                      f"associative Chen scan + autograd backward), {spent:.1f} s"}
+
+
+# ------------------------------------------------------------------------------------ arms
+
+
+def run_b200(args, rank, world, local_rank):
+    from exponentially_weighted_signature_b200 import engine, parallel
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    setup = _diag_setup(args.config, rank, world, device, args.precision)
+    step, params = setup["step"], setup["params"]
+    x = setup["x_host"].to(device)
+    clock = setup["clock_host"].to(device)
+    flush = None
+    if setup["ws_bytes"] < 2 * L2_BYTES:
+        flush = torch.zeros(2 * L2_BYTES // 4, device=device)
+
+    def one(xx, cc):
+        for p in params:
+            p.grad = None
+        loss = step(xx, cc)
+        if world > 1:
+            parallel.allreduce_gradients(params)
+        return loss
+
+    for _ in range(args.warmup):
+        one(x, clock)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    engine.PROFILE = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        _flush_l2(flush)
+        ev[i][0].record()
+        one(x, clock)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    prof = engine.PROFILE
+    engine.PROFILE = None
+    if world > 1:
+        dist.barrier()
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t = torch.tensor([total_ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    clocks = sampler.stop() if sampler else None
+
+    # kernel timing from the launching stream
+    per = {}
+    for name, e0, e1, units in prof:
+        d = per.setdefault(name, [0.0, 0, 0])
+        d[0] += e0.elapsed_time(e1)
+        d[1] += 1
+        d[2] = units
+    launches = sum(KERNELS_PER_CALL.get(n, 1) * v[1] for n, v in per.items())
+    dom = max(per.items(), key=lambda kv: kv[1][0])
+    dom_name, (dom_ms, dom_n, dom_units) = dom
+    avg_s = dom_ms / dom_n / 1e3
+    hbm, _, peak_kind = _peaks()
+    alg_bytes = setup["alg"][dom_name] * dom_units
+    achieved = alg_bytes / avg_s / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            tr = json.load(f)
+        per_unit = tr.get(args.config, {}).get(dom_name)
+        if per_unit:
+            traffic = per_unit * dom_units
+    except Exception:
+        pass
+
+    # end to end: host inputs copied in, loss read back, every step
+    xh = setup["x_host"].pin_memory()
+    ch = setup["clock_host"].pin_memory()
+    xd = torch.empty_like(x)
+    cd = torch.empty_like(clock)
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    for _ in range(max(1, args.warmup)):
+        xd.copy_(xh, non_blocking=True)
+        cd.copy_(ch, non_blocking=True)
+        loss_h.copy_(one(xd, cd).detach(), non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        _flush_l2(flush)
+        e2e_ev[i][0].record()
+        xd.copy_(xh, non_blocking=True)
+        cd.copy_(ch, non_blocking=True)
+        loss = one(xd, cd)
+        loss_h.copy_(loss.detach(), non_blocking=True)
+        e2e_ev[i][1].record()
+    torch.cuda.synchronize()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
+    t = torch.tensor([e2e_ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+
+    meta = setup["meta"]
+    units_per_step = meta["B_local"] * meta["T"] * world
+    value = units_per_step * args.steps / (total_ms / 1e3)
+    if rank != 0:
+        return
+    cpu = _cpu_baseline(args.config, args.precision) if world == 1 and not args.no_cpu_baseline else None
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": meta["scaling"],
+        "vs_baseline": None,
+        "dtype": meta["dtype"],
+        "data": "synthetic (seeded, BASELINE.json shapes and distributions)",
+        "config": {
+            "workload": args.config,
+            "global_batch": meta["B_global"],
+            "seq_len": meta["T"],
+            "state_dim": meta["N"],
+            "depth": 2,
+            "readout": meta["readout"],
+            "series_q": meta["q"],
+            "inputs": meta["precision"],
+            "parallelism": f"dp{world}",
+            "l2": "flushed between timed steps" if flush is not None else "working set larger than L2",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": dom_name,
+            "achieved": achieved,
+            "peak": hbm,
+            "unit": "GB/s",
+            "frac": achieved / hbm,
+            "peak_source": peak_kind,
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": alg_bytes,
+            "avg_launch_ms": avg_s * 1e3,
+        },
+        "e2e": {
+            "value": units_per_step * args.steps / (e2e_ms / 1e3),
+            "unit": UNIT,
+            "h2d_bytes_per_step": int(xh.numel() * xh.element_size() + ch.numel() * ch.element_size()) * world,
+            "d2h_bytes_per_step": 4 * world,
+        },
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU path (its oracle port: JAX is not installable here) on the host cores."""
+    if rank != 0:
+        return
+    cpu = _cpu_baseline(args.config, args.precision, budget_s=max(10.0, 4.0 * args.steps))
+    line = {
+        "metric": METRIC,
+        "value": cpu["value"],
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "impl": "reference",
+        "dtype": "f32",
+        "data": "synthetic (seeded, BASELINE.json shapes and distributions)",
+        "config": {"workload": args.config, "parallelism": "host cores"},
+        "cpu_baseline": {"value": cpu["value"], "unit": UNIT, "cores": cpu["cores"], "kind": cpu["kind"], "sample": cpu["sample"]},
+        "e2e": {"value": cpu["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "vs_baseline": None,
+        "note": "jax/equinox/signax (the reference's stack) cannot be installed offline on these machines; "
+                "the timed path is the float32 oracle port of the reference's series leaf + associative scan",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="config5", choices=["config1", "config5"])
+    ap.add_argument("--precision", default="f32", choices=["f32", "bf16"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    try:
+        run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,138 @@
+// Shared device helpers of the EWS kernels: look-back flags with bounded waits, warp span copies
+// between global memory and shared memory, and input loads.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/ews_b200.h"
+
+namespace ews {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// Look-back slot states. A chunk publishes its aggregate (AGG) before it knows its carry, then its
+// inclusive value (INCL) once it does.
+constexpr int kFlagEmpty = 0;
+constexpr int kFlagAgg = 1;
+constexpr int kFlagIncl = 2;
+
+// Device status block at the start of every workspace: a tile ticket counter and an error word.
+struct DeviceStatus {
+    int ticket;
+    int error;
+    int err_tile;
+    int pad;
+};
+
+constexpr int kDefaultSpinLimit = 1 << 21;
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release(int* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Warp-wide: take the next tile ticket (lane 0 increments, all lanes receive it).
+__device__ __forceinline__ int next_ticket(DeviceStatus* st) {
+    int t = 0;
+    if ((threadIdx.x & 31) == 0) t = atomicAdd(&st->ticket, 1);
+    return __shfl_sync(kFull, t, 0);
+}
+
+// Warp-wide publish: every lane has stored its part of the slot; make the stores visible, then set the flag.
+__device__ __forceinline__ void publish(int* flag, int value) {
+    __threadfence();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) st_release(flag, value);
+}
+
+// Warp-wide bounded wait for a slot to leave kFlagEmpty. Returns the flag value, or -1 when the wait ran
+// out (the error word is then set) or another tile already failed. Never spins without a limit.
+__device__ __forceinline__ int wait_slot(const int* flag, DeviceStatus* st, int limit, int tile) {
+    int v = kFlagEmpty;
+    if ((threadIdx.x & 31) == 0) {
+        unsigned ns = 32;
+        int it = 0;
+        for (; it < limit; ++it) {
+            v = ld_acquire(flag);
+            if (v != kFlagEmpty) break;
+            if (*((volatile int*)&st->error) != 0) {
+                v = -1;
+                break;
+            }
+            __nanosleep(ns);
+            if (ns < 2048) ns <<= 1;
+        }
+        if (v == kFlagEmpty) {
+            if (atomicCAS(&st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) st->err_tile = tile;
+            v = -1;
+        }
+    }
+    v = __shfl_sync(kFull, v, 0);
+    __threadfence();
+    return v;
+}
+
+// Loads that bypass L1: look-back slots written by other SMs.
+__device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
+
+// Warp copy of n contiguous floats from shared memory to global memory. The global span may start at
+// any 4-byte offset: the head up to the first 16-byte boundary and the tail are scalar stores, the body
+// 16-byte vector stores (shared memory is read with scalar loads, since its offset need not be aligned).
+__device__ __forceinline__ void warp_store_span(float* __restrict__ g, const float* __restrict__ s, int n) {
+    const int lane = threadIdx.x & 31;
+    int head = (int)(((16u - ((uintptr_t)g & 15u)) & 15u) >> 2);
+    if (head > n) head = n;
+    if (lane < head) g[lane] = s[lane];
+    const int nvec = (n - head) >> 2;
+    float4* gv = reinterpret_cast<float4*>(g + head);
+    for (int v = lane; v < nvec; v += 32) {
+        const float* sp = s + head + 4 * v;
+        gv[v] = make_float4(sp[0], sp[1], sp[2], sp[3]);
+    }
+    const int done = head + 4 * nvec;
+    if (lane < n - done) g[done + lane] = s[done + lane];
+}
+
+// Warp copy of n contiguous floats from global memory to shared memory (L2-cached loads: the backward
+// reads its gradient rows twice).
+__device__ __forceinline__ void warp_load_span(float* __restrict__ s, const float* __restrict__ g, int n) {
+    const int lane = threadIdx.x & 31;
+    int head = (int)(((16u - ((uintptr_t)g & 15u)) & 15u) >> 2);
+    if (head > n) head = n;
+    if (lane < head) s[lane] = __ldcg(g + lane);
+    const int nvec = (n - head) >> 2;
+    const float4* gv = reinterpret_cast<const float4*>(g + head);
+    for (int v = lane; v < nvec; v += 32) {
+        float4 q = __ldcg(gv + v);
+        float* sp = s + head + 4 * v;
+        sp[0] = q.x;
+        sp[1] = q.y;
+        sp[2] = q.z;
+        sp[3] = q.w;
+    }
+    const int done = head + 4 * nvec;
+    if (lane < n - done) s[done + lane] = __ldcg(g + done + lane);
+}
+
+__device__ __forceinline__ float load_in(const void* p, size_t idx, bool bf16) {
+    if (bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[idx]);
+    return reinterpret_cast<const float*>(p)[idx];
+}
+
+// Increment dx_t (d_in values) of sample b at interval t, from knots or from stored increments.
+__device__ __forceinline__ float input_increment(const void* path, int b, int t, int c, int T, int d_in,
+                                                 unsigned flags) {
+    const bool bf16 = (flags & EWS_F_BF16) != 0;
+    if (flags & EWS_F_INCREMENTS) return load_in(path, ((size_t)b * T + t) * d_in + c, bf16);
+    const size_t k0 = ((size_t)b * (T + 1) + t) * d_in + c;
+    return load_in(path, k0 + d_in, bf16) - load_in(path, k0, bf16);
+}
+
+}  // namespace ews

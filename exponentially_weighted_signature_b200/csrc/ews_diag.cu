@@ -1,0 +1,1104 @@
+// Diagonal engine of the EWS hot path (A = diag(lambda)), depth 2, state dimension N <= 32, fp32.
+//
+// Per interval t of sample b (x = -h lambda, rho = exp(x), dy = lift @ dx):
+//     S1' = rho o S1 + s1,                 s1_i  = Q1_i dy_i
+//     S2' = (rho rho^T) o S2 + (rho o S1) s1^T + s2,   s2_ij = Q2_ij dy_i dy_j
+// which is the modified-Chen recursion of ews/core/chen_scan.py:124-152 for a diagonal flow
+// (ews/core/kernels/pallas_combine.py:1804-1834 is the same recursion sequentially), with the series
+// local terms of ews/core/series_leaf.py:72-113 folded into the tables Q1, Q2.
+//
+// Work decomposition. One warp owns one tile = (sample, chunk of Lc intervals). Lane (ti, tj), ti in
+// [0,4), tj in [0,8), owns the RI x RJ block (RI = NP/4, RJ = NP/8) of the level-2 state with rows
+// ti*RI.. and columns tj*RJ.., plus the level-1 entries of its rows (kept redundantly by the 8 lanes of
+// a row group). Row sums are xor-shuffles over lane bits 0-2, column sums over bits 3-4. Tiles are
+// taken in order from an atomic ticket, so every tile a chunk waits for is already running: chunks
+// publish their aggregate, look back over their predecessors (decoupled look-back) and re-run the
+// recursion from the carry to emit the prefix rows. Every wait is bounded.
+//
+// Backward: the adjoint of step t is lambda2 <- rho rho^T o lambda2, lambda1 <- rho o (lambda1 +
+// lambda2 s1). Chunks compute a zero-carry local adjoint, look back over the later chunks (whose
+// transposed chunk maps come from the forward aggregates) and then run the exact adjoint from the
+// carry, accumulating the gradients. Prefix readouts read S_{t-1} back from the forward output;
+// terminal readouts use the closed form lambda2_t = e^{(T-1-t)(x_i+x_j)} g2 and recompute S forward.
+#include <algorithm>
+#include <cstdio>
+
+#include "ews_common.cuh"
+
+namespace ews {
+namespace diag {
+
+constexpr int kWarps = 4;  // warps per CTA; each warp is an independent tile worker
+
+struct Geom {
+    int B, T, d_in, N, NP, Lc, C, W, SW, readout;
+    unsigned flags;
+    int spin_limit;
+    int SR;      // prefix rows staged per span store
+    int ntiles;  // B * C
+};
+
+struct Params {
+    Geom g;
+    const void* path;
+    const float* lift;
+    const float* tab_x;
+    const float* tab_q1;
+    const float* tab_q2;
+    float* out;
+    // backward
+    const float* grad_out;
+    float* grad_dx;
+    float* partials;  // per tile: gx (NP), dq1 (NP), dq2 (NP*NP), dlift (NP*d_in)
+    // look-back state
+    DeviceStatus* st;
+    int* flags;
+    float* agg;     // forward: chunk aggregates; backward: local adjoints
+    float* incl;    // inclusive values
+    float* carry;   // forward: exclusive prefix per chunk (kept for the backward)
+    const float* fagg;    // backward: the forward aggregates
+    const float* fcarry;  // backward: the forward carries
+};
+
+__host__ __device__ inline int align4(int n) { return (n + 3) & ~3; }
+
+// --------------------------------------------------------------------------------- lane elements
+
+template <int RI, int RJ>
+struct Elem {  // a Chen group element restricted to a lane's block: flows, level 1, level 2
+    float Pr[RI], Pc[RJ], S1r[RI], S1c[RJ], S2[RI][RJ];
+    __device__ void identity() {
+#pragma unroll
+        for (int r = 0; r < RI; ++r) {
+            Pr[r] = 1.f;
+            S1r[r] = 0.f;
+#pragma unroll
+            for (int c = 0; c < RJ; ++c) S2[r][c] = 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            Pc[c] = 1.f;
+            S1c[c] = 0.f;
+        }
+    }
+};
+
+// res = L (x) R: L flowed by R's flow, then the truncated tensor product (ews/core/chen_scan.py:124-152).
+template <int RI, int RJ>
+__device__ __forceinline__ void chen_mul(const Elem<RI, RJ>& L, const Elem<RI, RJ>& R, Elem<RI, RJ>& out) {
+    Elem<RI, RJ> o;
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const float u = R.Pr[r] * L.S1r[r];
+#pragma unroll
+        for (int c = 0; c < RJ; ++c)
+            o.S2[r][c] = fmaf(R.Pr[r] * R.Pc[c], L.S2[r][c], fmaf(u, R.S1c[c], R.S2[r][c]));
+        o.S1r[r] = u + R.S1r[r];
+        o.Pr[r] = L.Pr[r] * R.Pr[r];
+    }
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        o.S1c[c] = fmaf(R.Pc[c], L.S1c[c], R.S1c[c]);
+        o.Pc[c] = L.Pc[c] * R.Pc[c];
+    }
+    out = o;
+}
+
+// Slot layout (floats): [P (NP) | S1 (NP) | S2 (NP x NP)].
+template <int RI, int RJ>
+__device__ __forceinline__ void store_elem(float* slot, const Elem<RI, RJ>& e, int NP, int i0, int j0, int tj) {
+    if (tj == 0) {
+#pragma unroll
+        for (int r = 0; r < RI; ++r) {
+            slot[i0 + r] = e.Pr[r];
+            slot[NP + i0 + r] = e.S1r[r];
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RI; ++r)
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) slot[2 * NP + (i0 + r) * NP + j0 + c] = e.S2[r][c];
+}
+
+template <int RI, int RJ>
+__device__ __forceinline__ void load_elem(const float* slot, Elem<RI, RJ>& e, int NP, int i0, int j0) {
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        e.Pr[r] = ldcg(slot + i0 + r);
+        e.S1r[r] = ldcg(slot + NP + i0 + r);
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) e.S2[r][c] = ldcg(slot + 2 * NP + (i0 + r) * NP + j0 + c);
+    }
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        e.Pc[c] = ldcg(slot + j0 + c);
+        e.S1c[c] = ldcg(slot + NP + j0 + c);
+    }
+}
+
+// --------------------------------------------------------------------------------- tables, inputs
+
+template <int RI, int RJ>
+struct Tables {
+    float xr[RI], xc[RJ], rho_r[RI], rho_c[RJ], q1r[RI], q1c[RJ], q2[RI][RJ];
+    __device__ void load(const Params& p, int b, int i0, int j0) {
+        const int N = p.g.N;
+        const float* tx = p.tab_x + (size_t)b * N;
+        const float* t1 = p.tab_q1 + (size_t)b * N;
+        const float* t2 = p.tab_q2 + (size_t)b * N * N;
+#pragma unroll
+        for (int r = 0; r < RI; ++r) {
+            const int i = i0 + r;
+            xr[r] = i < N ? tx[i] : 0.f;
+            rho_r[r] = expf(xr[r]);
+            q1r[r] = i < N ? t1[i] : 0.f;
+#pragma unroll
+            for (int c = 0; c < RJ; ++c) {
+                const int j = j0 + c;
+                q2[r][c] = (i < N && j < N) ? t2[i * N + j] : 0.f;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            const int j = j0 + c;
+            xc[c] = j < N ? tx[j] : 0.f;
+            rho_c[c] = expf(xc[c]);
+            q1c[c] = j < N ? t1[j] : 0.f;
+        }
+    }
+};
+
+// Lifted increments of steps [t0, t0 + n) into dys[k * NP + i] (zero for padded i >= N). The increments
+// themselves go to dxs[k * d_in + c] first.
+__device__ void load_increments(const Params& p, const float* liftS, float* dxs, float* dys, int b, int t0,
+                                int n) {
+    const Geom& g = p.g;
+    const int lane = threadIdx.x & 31;
+    for (int e = lane; e < n * g.d_in; e += 32) {
+        const int k = e / g.d_in, cc = e - k * g.d_in;
+        dxs[e] = input_increment(p.path, b, t0 + k, cc, g.T, g.d_in, g.flags);
+    }
+    __syncwarp();
+    for (int e = lane; e < n * g.NP; e += 32) {
+        const int k = e / g.NP, i = e - k * g.NP;
+        float v = 0.f;
+        if (i < g.N) {
+            if (p.lift) {
+                const float* wr = liftS + i * g.d_in;
+                const float* xr = dxs + k * g.d_in;
+                for (int cc = 0; cc < g.d_in; ++cc) v = fmaf(wr[cc], xr[cc], v);
+            } else {
+                v = dxs[k * g.d_in + i];
+            }
+        }
+        dys[e] = v;
+    }
+    __syncwarp();
+}
+
+// --------------------------------------------------------------------------------- the step
+
+// The flow of a step: rho, except the identity for the basepoint interval (ews/core/chen_scan.py:160-166).
+template <int RI, int RJ>
+__device__ __forceinline__ void step_flow(const Tables<RI, RJ>& tb, bool identity, float fr[RI], float fc[RJ]) {
+#pragma unroll
+    for (int r = 0; r < RI; ++r) fr[r] = identity ? 1.f : tb.rho_r[r];
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) fc[c] = identity ? 1.f : tb.rho_c[c];
+}
+
+// One modified-Chen step S <- flow(S) (x) (s1, s2) on a lane's block, also accumulating the flow product.
+template <int RI, int RJ>
+__device__ __forceinline__ void chen_step(const Tables<RI, RJ>& tb, const float* dyk, int i0, int j0,
+                                          Elem<RI, RJ>& S, const float fr[RI], const float fc[RJ]) {
+    float dyr[RI], dyc[RJ], s1c[RJ];
+#pragma unroll
+    for (int r = 0; r < RI; ++r) dyr[r] = dyk[i0 + r];
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        dyc[c] = dyk[j0 + c];
+        s1c[c] = tb.q1c[c] * dyc[c];
+    }
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const float u = fr[r] * S.S1r[r];
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            const float loc = tb.q2[r][c] * (dyr[r] * dyc[c]);
+            S.S2[r][c] = fmaf(fr[r] * fc[c], S.S2[r][c], fmaf(u, s1c[c], loc));
+        }
+        S.S1r[r] = fmaf(tb.q1r[r], dyr[r], u);
+        S.Pr[r] *= fr[r];
+    }
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        S.S1c[c] = fmaf(fc[c], S.S1c[c], s1c[c]);
+        S.Pc[c] *= fc[c];
+    }
+}
+
+// Writes row [1, S1, S2] of a lane element into a staged row (real dimension N, row width W).
+template <int RI, int RJ>
+__device__ __forceinline__ void stage_row(float* row, const Elem<RI, RJ>& S, int N, int i0, int j0, int tj,
+                                          int lane) {
+    if (lane == 0) row[0] = 1.f;
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const int i = i0 + r;
+        if (i < N) {
+            if (tj == 0) row[1 + i] = S.S1r[r];
+#pragma unroll
+            for (int c = 0; c < RJ; ++c) {
+                const int j = j0 + c;
+                if (j < N) row[1 + N + i * N + j] = S.S2[r][c];
+            }
+        }
+    }
+}
+
+// --------------------------------------------------------------------------------- forward kernel
+
+template <int NP>
+__global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
+    constexpr int RI = NP / 4, RJ = NP / 8;
+    extern __shared__ float smem[];
+    const Geom& g = p.g;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int liftN = align4(NP * g.d_in);
+    float* liftS = smem;
+    for (int e = threadIdx.x; e < NP * g.d_in; e += blockDim.x) {
+        const int r = e / g.d_in, cc = e - r * g.d_in;
+        liftS[e] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
+    }
+    __syncthreads();
+    const int per_warp = align4(g.Lc * g.d_in) + align4(g.Lc * NP) + align4(g.SR * g.W);
+    float* dxs = smem + liftN + warp * per_warp;
+    float* dys = dxs + align4(g.Lc * g.d_in);
+    float* stage = dys + align4(g.Lc * NP);
+
+    const int ti = lane >> 3, tj = lane & 7;
+    const int i0 = ti * RI, j0 = tj * RJ;
+    const bool basepoint = (g.flags & EWS_F_BASEPOINT) != 0;
+
+    for (;;) {
+        const int tile = next_ticket(p.st);
+        if (tile >= g.ntiles) break;
+        const int c = tile / g.B, b = tile - c * g.B;
+        const int t0 = c * g.Lc;
+        const int len = min(g.Lc, g.T - t0);
+        Tables<RI, RJ> tb;
+        tb.load(p, b, i0, j0);
+        load_increments(p, liftS, dxs, dys, b, t0, len);
+
+        // pass 1: the chunk's aggregate from the identity
+        Elem<RI, RJ> A;
+        A.identity();
+        for (int k = 0; k < len; ++k) {
+            float fr[RI], fc[RJ];
+            step_flow(tb, basepoint && (t0 + k == 0), fr, fc);
+            chen_step(tb, dys + k * NP, i0, j0, A, fr, fc);
+        }
+        const size_t slot = ((size_t)b * g.C + c) * g.SW;
+        int* flag = p.flags + (size_t)b * g.C + c;
+        Elem<RI, RJ> excl;
+        excl.identity();
+        if (c == 0) {
+            store_elem(p.incl + slot, A, NP, i0, j0, tj);
+            publish(flag, kFlagIncl);
+        } else {
+            store_elem(p.agg + slot, A, NP, i0, j0, tj);
+            publish(flag, kFlagAgg);
+            // look back over the predecessors: excl = incl_j (x) agg_{j+1} (x) ... (x) agg_{c-1}
+            Elem<RI, RJ> acc;
+            acc.identity();
+            int j = c - 1;
+            for (;;) {
+                const int f = wait_slot(p.flags + (size_t)b * g.C + j, p.st, g.spin_limit, tile);
+                if (f < 0) return;  // timeout or another tile failed: the error word is set
+                Elem<RI, RJ> X;
+                const size_t sj = ((size_t)b * g.C + j) * g.SW;
+                if (f == kFlagIncl) {
+                    load_elem(p.incl + sj, X, NP, i0, j0);
+                    chen_mul(X, acc, excl);
+                    break;
+                }
+                load_elem(p.agg + sj, X, NP, i0, j0);
+                chen_mul(X, acc, acc);
+                --j;
+            }
+            Elem<RI, RJ> inc;
+            chen_mul(excl, A, inc);
+            store_elem(p.incl + slot, inc, NP, i0, j0, tj);
+            publish(flag, kFlagIncl);
+        }
+        store_elem(p.carry + slot, excl, NP, i0, j0, tj);
+        // the forward aggregates are kept for the backward: chunk 0 stored it as incl
+        if (c == 0) store_elem(p.agg + slot, A, NP, i0, j0, tj);
+
+        if (g.readout == EWS_READOUT_TERMINAL) {
+            if (c == g.C - 1) {
+                Elem<RI, RJ> fin;
+                chen_mul(excl, A, fin);
+                stage_row(stage, fin, g.N, i0, j0, tj, lane);
+                __syncwarp();
+                warp_store_span(p.out + (size_t)b * g.W, stage, g.W);
+                __syncwarp();
+            }
+            continue;
+        }
+        // pass 2: re-run the chunk from its carry and emit the prefix rows
+        Elem<RI, RJ> S = excl;
+        int k0 = 0;
+        for (int k = 0; k < len; ++k) {
+            float fr[RI], fc[RJ];
+            step_flow(tb, basepoint && (t0 + k == 0), fr, fc);
+            chen_step(tb, dys + k * NP, i0, j0, S, fr, fc);
+            stage_row(stage + (k - k0) * g.W, S, g.N, i0, j0, tj, lane);
+            if (k - k0 == g.SR - 1 || k == len - 1) {
+                __syncwarp();
+                warp_store_span(p.out + ((size_t)b * g.T + t0 + k0) * g.W, stage, (k - k0 + 1) * g.W);
+                __syncwarp();
+                k0 = k + 1;
+            }
+        }
+    }
+}
+
+// --------------------------------------------------------------------------------- backward
+
+// Adjoint lane element: cotangents of S1 (rows) and S2 (block).
+template <int RI, int RJ>
+struct Adj {
+    float L1r[RI], L2[RI][RJ];
+    __device__ void zero() {
+#pragma unroll
+        for (int r = 0; r < RI; ++r) {
+            L1r[r] = 0.f;
+#pragma unroll
+            for (int c = 0; c < RJ; ++c) L2[r][c] = 0.f;
+        }
+    }
+};
+
+__device__ __forceinline__ float row_sum(float v) {  // over the 8 lanes of a row group
+    v += __shfl_xor_sync(kFull, v, 1);
+    v += __shfl_xor_sync(kFull, v, 2);
+    v += __shfl_xor_sync(kFull, v, 4);
+    return v;
+}
+
+__device__ __forceinline__ float col_sum(float v) {  // over the 4 lanes of a column group
+    v += __shfl_xor_sync(kFull, v, 8);
+    v += __shfl_xor_sync(kFull, v, 16);
+    return v;
+}
+
+// Values a lane holds for its rows, delivered to the lanes whose columns they are: column j0 + c lives in
+// row group tj/2 at offset (tj&1)*RJ + c; the source lane with the same tj sends it.
+template <int RI, int RJ>
+__device__ __forceinline__ void rows_to_cols(const float vr[RI], float vc[RJ], int tj) {
+    const int src = (tj >> 1) * 8 + tj;
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        const float send = (tj & 1) ? vr[RJ + c] : vr[c];
+        vc[c] = __shfl_sync(kFull, send, src);
+    }
+}
+
+// Transposed Jacobian of right-multiplication by G = (P, U1, U2): mu2 = P P^T o l2,
+// mu1 = P o (l1 + l2 U1). Applied in place.
+template <int RI, int RJ>
+__device__ __forceinline__ void apply_JT(const Elem<RI, RJ>& G, Adj<RI, RJ>& a) {
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        float w = 0.f;
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) w = fmaf(a.L2[r][c], G.S1c[c], w);
+        w = row_sum(w);
+        a.L1r[r] = G.Pr[r] * (a.L1r[r] + w);
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] *= G.Pr[r] * G.Pc[c];
+    }
+}
+
+// Adjoint slot layout (floats): [L1 (NP) | pad (NP) | L2 (NP x NP)] (same size as a forward slot).
+template <int RI, int RJ>
+__device__ __forceinline__ void store_adj(float* slot, const Adj<RI, RJ>& a, int NP, int i0, int j0, int tj) {
+    if (tj == 0) {
+#pragma unroll
+        for (int r = 0; r < RI; ++r) slot[i0 + r] = a.L1r[r];
+    }
+#pragma unroll
+    for (int r = 0; r < RI; ++r)
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) slot[2 * NP + (i0 + r) * NP + j0 + c] = a.L2[r][c];
+}
+
+template <int RI, int RJ>
+__device__ __forceinline__ void load_adj(const float* slot, Adj<RI, RJ>& a, int NP, int i0, int j0) {
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        a.L1r[r] = ldcg(slot + i0 + r);
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] = ldcg(slot + 2 * NP + (i0 + r) * NP + j0 + c);
+    }
+}
+
+template <int RI, int RJ>
+__device__ __forceinline__ void adj_add(Adj<RI, RJ>& a, const Adj<RI, RJ>& b) {
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        a.L1r[r] += b.L1r[r];
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] += b.L2[r][c];
+    }
+}
+
+// Reads row t of a (B, T, W) stream into a lane's (level-1 rows, level-2 block) pieces; real dims N.
+template <int RI, int RJ>
+__device__ __forceinline__ void read_row(const float* row, float v1[RI], float v2[RI][RJ], int N, int i0, int j0) {
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const int i = i0 + r;
+        v1[r] = i < N ? row[1 + i] : 0.f;
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            const int j = j0 + c;
+            v2[r][c] = (i < N && j < N) ? row[1 + N + i * N + j] : 0.f;
+        }
+    }
+}
+
+// Gradient accumulators of a lane.
+template <int RI, int RJ>
+struct Grads {
+    float gxr[RI], gxc[RJ], dq1c[RJ], dq2[RI][RJ];
+    __device__ void zero() {
+#pragma unroll
+        for (int r = 0; r < RI; ++r) {
+            gxr[r] = 0.f;
+#pragma unroll
+            for (int c = 0; c < RJ; ++c) dq2[r][c] = 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            gxc[c] = 0.f;
+            dq1c[c] = 0.f;
+        }
+    }
+};
+
+// One exact adjoint step at interval t: a holds the cotangent of S_t (g_t already added); S1p/S2p are
+// S_{t-1}. Accumulates the gradients, writes dy_t to dyg[0..NP) and turns a into the cotangent of S_{t-1}.
+template <int RI, int RJ>
+__device__ __forceinline__ void bwd_step(const Tables<RI, RJ>& tb, const float fr[RI], const float fc[RJ],
+                                         const float* dyk, const float S1p[RI], const float S2p[RI][RJ],
+                                         Adj<RI, RJ>& a, Grads<RI, RJ>& gr, float* dyg, int i0, int j0, int ti,
+                                         int tj) {
+    float dyr[RI], dyc[RJ], s1c[RJ], u[RI];
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        dyr[r] = dyk[i0 + r];
+        u[r] = fr[r] * S1p[r];
+    }
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        dyc[c] = dyk[j0 + c];
+        s1c[c] = tb.q1c[c] * dyc[c];
+    }
+    // row sums: w (adjoint recursion), z (dy from s2, row side)
+    float w[RI], z[RI];
+    // column partials: y (ds1), v (dy from s2, column side), e (flow gradient, column side)
+    float y[RJ], v[RJ];
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        y[c] = 0.f;
+        v[c] = 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        float wr = 0.f, zr = 0.f, fx = 0.f;
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            const float l2 = a.L2[r][c];
+            const float l2q = l2 * tb.q2[r][c];
+            wr = fmaf(l2, s1c[c], wr);
+            zr = fmaf(l2q, dyc[c], zr);
+            y[c] = fmaf(l2, u[r], y[c]);
+            v[c] = fmaf(l2q, dyr[r], v[c]);
+            // flow gradient (w.r.t. x = log rho) of rho_i rho_j S2_ij, credited to i and to j
+            const float fl = l2 * (fr[r] * fc[c]) * S2p[r][c];
+            fx = fmaf(l2, u[r] * s1c[c], fx + fl);
+            gr.gxc[c] += fl;
+            gr.dq2[r][c] = fmaf(l2, dyr[r] * dyc[c], gr.dq2[r][c]);
+        }
+        w[r] = row_sum(wr);
+        z[r] = row_sum(zr);
+        gr.gxr[r] += fx + (tj == 0 ? a.L1r[r] * u[r] : 0.f);
+    }
+    float l1c[RJ], zc[RJ];
+    rows_to_cols<RI, RJ>(a.L1r, l1c, tj);
+    rows_to_cols<RI, RJ>(z, zc, tj);
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        const float ds1 = l1c[c] + col_sum(y[c]);
+        const float vv = col_sum(v[c]);
+        gr.dq1c[c] = fmaf(ds1, dyc[c], gr.dq1c[c]);
+        if (ti == 0) dyg[j0 + c] = fmaf(ds1, tb.q1c[c], vv + zc[c]);
+    }
+    // cotangent of S_{t-1}
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        a.L1r[r] = fr[r] * (a.L1r[r] + w[r]);
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] *= fr[r] * fc[c];
+    }
+}
+
+// The transposed step alone (no gradients): used for the zero-carry local adjoint.
+template <int RI, int RJ>
+__device__ __forceinline__ void adj_step(const Tables<RI, RJ>& tb, const float fr[RI], const float fc[RJ],
+                                         const float* dyk, Adj<RI, RJ>& a, int j0) {
+    float s1c[RJ];
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) s1c[c] = tb.q1c[c] * dyk[j0 + c];
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        float wr = 0.f;
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) wr = fmaf(a.L2[r][c], s1c[c], wr);
+        wr = row_sum(wr);
+        a.L1r[r] = fr[r] * (a.L1r[r] + wr);
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] *= fr[r] * fc[c];
+    }
+}
+
+template <int RI, int RJ>
+__device__ __forceinline__ void add_grad_row(Adj<RI, RJ>& a, const float* row, int N, int i0, int j0) {
+    float g1[RI], g2[RI][RJ];
+    read_row<RI, RJ>(row, g1, g2, N, i0, j0);
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        a.L1r[r] += g1[r];
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] += g2[r][c];
+    }
+}
+
+// Writes dx (the gradient of the input increments) of the chunk and accumulates the lift gradient.
+template <int RI, int RJ>
+__device__ void finish_chunk(const Params& p, const float* liftS, const float* dxs, const float* dyg, float* stage,
+                             int b, int t0, int len, int tile, const Grads<RI, RJ>& gr, int i0, int j0, int ti,
+                             int tj) {
+    const Geom& g = p.g;
+    const int lane = threadIdx.x & 31;
+    const int NP = g.NP;
+    __syncwarp();
+    // dx_t = lift^T dy_t, staged contiguously, then one span store
+    for (int e = lane; e < len * g.d_in; e += 32) {
+        const int k = e / g.d_in, cc = e - k * g.d_in;
+        float acc = 0.f;
+        if (p.lift) {
+            for (int i = 0; i < g.N; ++i) acc = fmaf(liftS[i * g.d_in + cc], dyg[k * NP + i], acc);
+        } else {
+            acc = dyg[k * NP + cc];
+        }
+        stage[e] = acc;
+    }
+    __syncwarp();
+    warp_store_span(p.grad_dx + ((size_t)b * g.T + t0) * g.d_in, stage, len * g.d_in);
+    __syncwarp();
+    float* part = p.partials + (size_t)tile * (2 * NP + NP * NP + NP * g.d_in);
+    // lift gradient: sum_t dy_t dx_t^T (dx recomputed from the input)
+    if (p.lift) {
+        for (int e = lane; e < NP * g.d_in; e += 32) {
+            const int i = e / g.d_in, cc = e - i * g.d_in;
+            float acc = 0.f;
+            if (i < g.N)
+                for (int k = 0; k < len; ++k)
+                    acc = fmaf(dyg[k * NP + i], dxs[k * g.d_in + cc], acc);
+            part[2 * NP + NP * NP + e] = acc;
+        }
+    }
+    // flow gradient = row part (summed over the row group's lanes) + column part (over the column group's);
+    // the row owner (tj == 0) writes first, the column owner (ti == 0) adds after a warp barrier
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const float s = row_sum(gr.gxr[r]);
+        if (tj == 0) part[i0 + r] = s;
+    }
+    float colpart[RJ];
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) colpart[c] = col_sum(gr.gxc[c]);
+    __syncwarp();
+    if (ti == 0) {
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            part[j0 + c] += colpart[c];
+            part[NP + j0 + c] = gr.dq1c[c];  // identical on the 4 lanes of a column group
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RI; ++r)
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) part[2 * NP + (i0 + r) * NP + j0 + c] = gr.dq2[r][c];
+}
+
+template <int NP>
+__global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
+    constexpr int RI = NP / 4, RJ = NP / 8;
+    extern __shared__ float smem[];
+    const Geom& g = p.g;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int liftN = align4(NP * g.d_in);
+    float* liftS = smem;
+    for (int e = threadIdx.x; e < NP * g.d_in; e += blockDim.x) {
+        const int r = e / g.d_in, cc = e - r * g.d_in;
+        liftS[e] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
+    }
+    __syncthreads();
+    // per warp: dxs, dys, dyg (Lc x NP), lam1 (Lc x NP, terminal), gstage (SR x W), sstage (SR x W)
+    const int stage_n = align4(max(g.SR * g.W, g.Lc * g.d_in));
+    const int per_warp = align4(g.Lc * g.d_in) + 3 * align4(g.Lc * NP) + 2 * stage_n;
+    float* dxs = smem + liftN + warp * per_warp;
+    float* dys = dxs + align4(g.Lc * g.d_in);
+    float* dyg = dys + align4(g.Lc * NP);
+    float* lam1 = dyg + align4(g.Lc * NP);
+    float* gst = lam1 + align4(g.Lc * NP);
+    float* sst = gst + stage_n;
+
+    const int ti = lane >> 3, tj = lane & 7;
+    const int i0 = ti * RI, j0 = tj * RJ;
+    const bool basepoint = (g.flags & EWS_F_BASEPOINT) != 0;
+    const bool terminal = g.readout == EWS_READOUT_TERMINAL;
+
+    for (;;) {
+        const int tile = next_ticket(p.st);
+        if (tile >= g.ntiles) break;
+        const int cr = tile / g.B, b = tile - cr * g.B;
+        const int c = g.C - 1 - cr;
+        const int t0 = c * g.Lc;
+        const int len = min(g.Lc, g.T - t0);
+        Tables<RI, RJ> tb;
+        tb.load(p, b, i0, j0);
+        load_increments(p, liftS, dxs, dys, b, t0, len);
+        const size_t slot = ((size_t)b * g.C + c) * g.SW;
+        int* flag = p.flags + (size_t)b * g.C + c;
+
+        // terminal readout: lambda2_t = E_i E_j g2 with E = e^{(T-1-t) x}; load g once
+        float tg1[RI], tg2[RI][RJ];
+        if (terminal) read_row<RI, RJ>(p.grad_out + (size_t)b * g.W, tg1, tg2, g.N, i0, j0);
+
+        // ---- 1. zero-carry local adjoint over the chunk (reverse)
+        Adj<RI, RJ> mu;
+        mu.zero();
+        if (!terminal) {
+            for (int kb = len; kb > 0; kb -= g.SR) {
+                const int k0 = max(0, kb - g.SR);
+                __syncwarp();
+                warp_load_span(gst, p.grad_out + ((size_t)b * g.T + t0 + k0) * g.W, (kb - k0) * g.W);
+                __syncwarp();
+                for (int k = kb - 1; k >= k0; --k) {
+                    add_grad_row(mu, gst + (k - k0) * g.W, g.N, i0, j0);
+                    float fr[RI], fc[RJ];
+                    step_flow(tb, basepoint && (t0 + k == 0), fr, fc);
+                    adj_step(tb, fr, fc, dys + k * NP, mu, j0);
+                }
+            }
+        } else {
+            // lambda1 only (lambda2 is closed form): mu1_{t-1} = rho (mu1_t + lambda2_t s1_t); g1 enters at T-1
+            for (int k = len - 1; k >= 0; --k) {
+                const int t = t0 + k;
+                if (t == g.T - 1) {
+#pragma unroll
+                    for (int r = 0; r < RI; ++r) mu.L1r[r] += tg1[r];
+                }
+                if (tj == 0) {
+#pragma unroll
+                    for (int r = 0; r < RI; ++r) lam1[k * NP + i0 + r] = mu.L1r[r];
+                }
+                float fr[RI], fc[RJ];
+                step_flow(tb, basepoint && (t == 0), fr, fc);
+                const float steps_after = (float)(g.T - 1 - t);
+                float ecs[RJ];
+#pragma unroll
+                for (int cc = 0; cc < RJ; ++cc) ecs[cc] = expf(steps_after * tb.xc[cc]) * tb.q1c[cc] * dys[k * NP + j0 + cc];
+#pragma unroll
+                for (int r = 0; r < RI; ++r) {
+                    const float er = expf(steps_after * tb.xr[r]);
+                    float wr = 0.f;
+#pragma unroll
+                    for (int cc = 0; cc < RJ; ++cc) wr = fmaf(er * tg2[r][cc], ecs[cc], wr);
+                    wr = row_sum(wr);
+                    mu.L1r[r] = fr[r] * (mu.L1r[r] + wr);
+                }
+            }
+        }
+
+        // ---- 2. look-back over the later chunks for the carry cotangent Lam_in (of S at the chunk's end)
+        Adj<RI, RJ> lam_in;
+        lam_in.zero();
+        Elem<RI, RJ> Gc;
+        load_elem(p.fagg + slot, Gc, NP, i0, j0);
+        if (c == g.C - 1) {
+            store_adj(p.incl + slot, mu, NP, i0, j0, tj);
+            publish(flag, kFlagIncl);
+        } else {
+            store_adj(p.agg + slot, mu, NP, i0, j0, tj);
+            publish(flag, kFlagAgg);
+            Adj<RI, RJ> acc;
+            acc.zero();
+            Elem<RI, RJ> Gacc;
+            Gacc.identity();
+            int j = c + 1;
+            for (;;) {
+                const int f = wait_slot(p.flags + (size_t)b * g.C + j, p.st, g.spin_limit, tile);
+                if (f < 0) return;
+                const size_t sj = ((size_t)b * g.C + j) * g.SW;
+                Adj<RI, RJ> X;
+                if (f == kFlagIncl) {
+                    load_adj(p.incl + sj, X, NP, i0, j0);
+                    apply_JT(Gacc, X);
+                    adj_add(acc, X);
+                    break;
+                }
+                load_adj(p.agg + sj, X, NP, i0, j0);
+                apply_JT(Gacc, X);
+                adj_add(acc, X);
+                Elem<RI, RJ> Gj;
+                load_elem(p.fagg + sj, Gj, NP, i0, j0);
+                chen_mul(Gacc, Gj, Gacc);
+                ++j;
+            }
+            lam_in = acc;
+            Adj<RI, RJ> out = lam_in;
+            apply_JT(Gc, out);
+            adj_add(out, mu);
+            store_adj(p.incl + slot, out, NP, i0, j0, tj);
+            publish(flag, kFlagIncl);
+        }
+
+        // ---- 3. exact adjoint from the carry, with the gradients
+        Grads<RI, RJ> gr;
+        gr.zero();
+        if (!terminal) {
+            Adj<RI, RJ> a = lam_in;
+            for (int kb = len; kb > 0; kb -= g.SR) {
+                const int k0 = max(0, kb - g.SR);
+                const int n = kb - k0;
+                __syncwarp();
+                warp_load_span(gst, p.grad_out + ((size_t)b * g.T + t0 + k0) * g.W, n * g.W);
+                // S_{t-1} rows: rows t0+k0-1 .. t0+kb-2 of the forward output (row -1 is the zero state)
+                const int first = t0 + k0 - 1;
+                if (first >= 0) {
+                    warp_load_span(sst, p.out + ((size_t)b * g.T + first) * g.W, n * g.W);
+                } else {
+                    for (int e = lane; e < g.W; e += 32) sst[e] = 0.f;
+                    if (n > 1) warp_load_span(sst + g.W, p.out + (size_t)b * g.T * g.W, (n - 1) * g.W);
+                }
+                __syncwarp();
+                for (int k = kb - 1; k >= k0; --k) {
+                    add_grad_row(a, gst + (k - k0) * g.W, g.N, i0, j0);
+                    float S1p[RI], S2p[RI][RJ];
+                    read_row<RI, RJ>(sst + (k - k0) * g.W, S1p, S2p, g.N, i0, j0);
+                    float fr[RI], fc[RJ];
+                    step_flow(tb, basepoint && (t0 + k == 0), fr, fc);
+                    bwd_step(tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, i0, j0, ti, tj);
+                }
+            }
+        } else {
+            // forward sweep from the carry with lambda2 in closed form and lambda1 = mu1 + rho^{end-t} Lam1_in
+            Elem<RI, RJ> S;
+            load_elem(p.fcarry + slot, S, NP, i0, j0);
+            for (int k = 0; k < len; ++k) {
+                const int t = t0 + k;
+                const float steps_after = (float)(g.T - 1 - t);
+                const float steps_to_end = (float)(len - 1 - k);
+                Adj<RI, RJ> a;
+                float ecs[RJ];
+#pragma unroll
+                for (int cc = 0; cc < RJ; ++cc) ecs[cc] = expf(steps_after * tb.xc[cc]);
+#pragma unroll
+                for (int r = 0; r < RI; ++r) {
+                    const float er = expf(steps_after * tb.xr[r]);
+                    a.L1r[r] = lam1[k * NP + i0 + r] + expf(steps_to_end * tb.xr[r]) * lam_in.L1r[r];
+#pragma unroll
+                    for (int cc = 0; cc < RJ; ++cc) a.L2[r][cc] = er * ecs[cc] * tg2[r][cc];
+                }
+                float S1p[RI], S2p[RI][RJ];
+#pragma unroll
+                for (int r = 0; r < RI; ++r) {
+                    S1p[r] = S.S1r[r];
+#pragma unroll
+                    for (int cc = 0; cc < RJ; ++cc) S2p[r][cc] = S.S2[r][cc];
+                }
+                float fr[RI], fc[RJ];
+                step_flow(tb, basepoint && (t == 0), fr, fc);
+                bwd_step(tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, i0, j0, ti, tj);
+                chen_step(tb, dys + k * NP, i0, j0, S, fr, fc);
+            }
+        }
+        finish_chunk<RI, RJ>(p, liftS, dxs, dyg, gst, b, t0, len, tile, gr, i0, j0, ti, tj);
+    }
+}
+
+// Deterministic reduction of the per-tile partials: per sample over its chunks (tables), and over all
+// tiles (lift). One thread per output value, fixed summation order.
+__global__ void reduce_kernel(Params p, float* grad_x, float* grad_q1, float* grad_q2, float* grad_lift) {
+    const Geom& g = p.g;
+    const int NP = g.NP, N = g.N;
+    const int stride = 2 * NP + NP * NP + NP * g.d_in;
+    const int per_sample = 2 * N + N * N;
+    const int total = g.B * per_sample + (grad_lift ? N * g.d_in : 0);
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+        if (e < g.B * per_sample) {
+            const int b = e / per_sample, r = e - b * per_sample;
+            int off;
+            float* dst;
+            if (r < N) {
+                off = r;
+                dst = grad_x + (size_t)b * N + r;
+            } else if (r < 2 * N) {
+                off = NP + (r - N);
+                dst = grad_q1 + (size_t)b * N + (r - N);
+            } else {
+                const int q = r - 2 * N, i = q / N, j = q - i * N;
+                off = 2 * NP + i * NP + j;
+                dst = grad_q2 + (size_t)b * N * N + q;
+            }
+            float acc = 0.f;
+            for (int c = 0; c < g.C; ++c) acc += p.partials[(size_t)(c * g.B + b) * stride + off];
+            *dst = acc;
+        } else {
+            const int q = e - g.B * per_sample, i = q / g.d_in, cc = q - i * g.d_in;
+            float acc = 0.f;
+            for (int t = 0; t < g.ntiles; ++t) acc += p.partials[(size_t)t * stride + 2 * NP + NP * NP + i * g.d_in + cc];
+            grad_lift[q] = acc;
+        }
+    }
+}
+
+// --------------------------------------------------------------------------------- host side
+
+static int pick_chunk(int B, int T) {
+    const int want_tiles = 148 * 16;
+    int C = (want_tiles + B - 1) / B;
+    if (C < 1) C = 1;
+    int Lc = (T + C - 1) / C;
+    if (Lc < 16) Lc = 16;
+    if (Lc > 64) Lc = 64;
+    return Lc;
+}
+
+static int make_geom(const ews_diag_args* a, Geom* g) {
+    if (!a || a->batch <= 0 || a->steps <= 0 || a->d_in <= 0 || a->dim <= 0) return EWS_ERR_INVALID_ARGUMENT;
+    if (a->depth != 2) return EWS_ERR_UNSUPPORTED;
+    if (a->dim > 32) return EWS_ERR_UNSUPPORTED;
+    if (!(a->flags & EWS_F_UNIFORM)) return EWS_ERR_UNSUPPORTED;
+    if (a->readout != EWS_READOUT_PREFIX && a->readout != EWS_READOUT_TERMINAL) return EWS_ERR_INVALID_ARGUMENT;
+    if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
+    if ((a->flags & EWS_F_BF16) && !(a->flags & EWS_F_INCREMENTS)) return EWS_ERR_INVALID_ARGUMENT;
+    g->B = a->batch;
+    g->T = a->steps;
+    g->d_in = a->d_in;
+    g->N = a->dim;
+    g->NP = (a->dim + 7) / 8 * 8;
+    g->Lc = a->chunk > 0 ? a->chunk : pick_chunk(a->batch, a->steps);
+    g->C = (g->T + g->Lc - 1) / g->Lc;
+    g->W = 1 + g->N + g->N * g->N;
+    g->SW = 2 * g->NP + g->NP * g->NP;
+    g->readout = a->readout;
+    g->flags = a->flags;
+    g->spin_limit = a->spin_limit > 0 ? a->spin_limit : kDefaultSpinLimit;
+    g->SR = g->W >= 1024 ? 1 : (1024 + g->W - 1) / g->W;
+    if (g->SR > g->Lc) g->SR = g->Lc;
+    g->ntiles = g->B * g->C;
+    return EWS_OK;
+}
+
+static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+struct WsLayout {
+    size_t status, flags, agg, incl, carry, partials, total;
+};
+
+static WsLayout fwd_layout(const Geom& g) {
+    WsLayout L{};
+    size_t o = 0;
+    L.status = o;
+    o += al256(sizeof(DeviceStatus));
+    L.flags = o;
+    o += al256(sizeof(int) * (size_t)g.ntiles);
+    const size_t slots = al256(sizeof(float) * (size_t)g.ntiles * g.SW);
+    L.agg = o;
+    o += slots;
+    L.incl = o;
+    o += slots;
+    L.carry = o;
+    o += slots;
+    L.total = o;
+    return L;
+}
+
+static WsLayout bwd_layout(const Geom& g) {
+    WsLayout L{};
+    size_t o = 0;
+    L.status = o;
+    o += al256(sizeof(DeviceStatus));
+    L.flags = o;
+    o += al256(sizeof(int) * (size_t)g.ntiles);
+    const size_t slots = al256(sizeof(float) * (size_t)g.ntiles * g.SW);
+    L.agg = o;
+    o += slots;
+    L.incl = o;
+    o += slots;
+    L.partials = o;
+    o += al256(sizeof(float) * (size_t)g.ntiles * (2 * g.NP + g.NP * g.NP + g.NP * g.d_in));
+    L.total = o;
+    return L;
+}
+
+static size_t fwd_smem(const Geom& g) {
+    const size_t per_warp = align4(g.Lc * g.d_in) + align4(g.Lc * g.NP) + align4(g.SR * g.W);
+    return sizeof(float) * (align4(g.NP * g.d_in) + kWarps * per_warp);
+}
+
+static size_t bwd_smem(const Geom& g) {
+    const int stage_n = align4(std::max(g.SR * g.W, g.Lc * g.d_in));
+    const size_t per_warp = align4(g.Lc * g.d_in) + 3 * align4(g.Lc * g.NP) + 2 * stage_n;
+    return sizeof(float) * (align4(g.NP * g.d_in) + kWarps * per_warp);
+}
+
+static int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int NP>
+static int launch_fwd(const Params& p, cudaStream_t s) {
+    const size_t smem = fwd_smem(p.g);
+    cudaFuncSetAttribute(fwd_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_kernel<NP>, kWarps * 32, smem);
+    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
+    int grid = per_sm * num_sms();
+    const int need = (p.g.ntiles + kWarps - 1) / kWarps;
+    if (grid > need) grid = need;
+    fwd_kernel<NP><<<grid, kWarps * 32, smem, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+template <int NP>
+static int launch_bwd(const Params& p, cudaStream_t s) {
+    const size_t smem = bwd_smem(p.g);
+    cudaFuncSetAttribute(bwd_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_kernel<NP>, kWarps * 32, smem);
+    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
+    int grid = per_sm * num_sms();
+    const int need = (p.g.ntiles + kWarps - 1) / kWarps;
+    if (grid > need) grid = need;
+    bwd_kernel<NP><<<grid, kWarps * 32, smem, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+}  // namespace diag
+}  // namespace ews
+
+using namespace ews;
+using namespace ews::diag;
+
+extern "C" int ews_diag_workspace_size(const ews_diag_args* a, size_t* fwd_bytes, size_t* bwd_bytes) {
+    Geom g;
+    const int rc = make_geom(a, &g);
+    if (rc != EWS_OK) return rc;
+    if (fwd_bytes) *fwd_bytes = fwd_layout(g).total;
+    if (bwd_bytes) *bwd_bytes = bwd_layout(g).total;
+    return EWS_OK;
+}
+
+extern "C" int ews_diag_fwd(const ews_diag_args* a, ews_stream_t stream) {
+    Geom g;
+    int rc = make_geom(a, &g);
+    if (rc != EWS_OK) return rc;
+    if (!a->path || !a->out || !a->tab_x || !a->tab_q1 || !a->tab_q2) return EWS_ERR_INVALID_ARGUMENT;
+    const WsLayout L = fwd_layout(g);
+    if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    char* ws = (char*)a->fwd_ws;
+    if (cudaMemsetAsync(ws, 0, L.agg, s) != cudaSuccess) return EWS_ERR_LAUNCH;
+    Params p{};
+    p.g = g;
+    p.path = a->path;
+    p.lift = a->lift;
+    p.tab_x = a->tab_x;
+    p.tab_q1 = a->tab_q1;
+    p.tab_q2 = a->tab_q2;
+    p.out = a->out;
+    p.st = (DeviceStatus*)(ws + L.status);
+    p.flags = (int*)(ws + L.flags);
+    p.agg = (float*)(ws + L.agg);
+    p.incl = (float*)(ws + L.incl);
+    p.carry = (float*)(ws + L.carry);
+    switch (g.NP) {
+        case 8: return launch_fwd<8>(p, s);
+        case 16: return launch_fwd<16>(p, s);
+        case 24: return launch_fwd<24>(p, s);
+        case 32: return launch_fwd<32>(p, s);
+    }
+    return EWS_ERR_UNSUPPORTED;
+}
+
+extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
+    Geom g;
+    int rc = make_geom(a, &g);
+    if (rc != EWS_OK) return rc;
+    if (!a->path || !a->grad_out || !a->grad_dx || !a->grad_x || !a->grad_q1 || !a->grad_q2)
+        return EWS_ERR_INVALID_ARGUMENT;
+    if (g.readout == EWS_READOUT_PREFIX && !a->out) return EWS_ERR_INVALID_ARGUMENT;
+    const WsLayout F = fwd_layout(g);
+    const WsLayout L = bwd_layout(g);
+    if (!a->fwd_ws || a->fwd_ws_bytes < F.total) return EWS_ERR_WORKSPACE;
+    if (!a->bwd_ws || a->bwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    char* ws = (char*)a->bwd_ws;
+    const char* fws = (const char*)a->fwd_ws;
+    if (cudaMemsetAsync(ws, 0, L.agg, s) != cudaSuccess) return EWS_ERR_LAUNCH;
+    Params p{};
+    p.g = g;
+    p.path = a->path;
+    p.lift = a->lift;
+    p.tab_x = a->tab_x;
+    p.tab_q1 = a->tab_q1;
+    p.tab_q2 = a->tab_q2;
+    p.out = a->out;
+    p.grad_out = a->grad_out;
+    p.grad_dx = a->grad_dx;
+    p.partials = (float*)(ws + L.partials);
+    p.st = (DeviceStatus*)(ws + L.status);
+    p.flags = (int*)(ws + L.flags);
+    p.agg = (float*)(ws + L.agg);
+    p.incl = (float*)(ws + L.incl);
+    p.fagg = (const float*)(fws + F.agg);
+    p.fcarry = (const float*)(fws + F.carry);
+    switch (g.NP) {
+        case 8: rc = launch_bwd<8>(p, s); break;
+        case 16: rc = launch_bwd<16>(p, s); break;
+        case 24: rc = launch_bwd<24>(p, s); break;
+        case 32: rc = launch_bwd<32>(p, s); break;
+        default: rc = EWS_ERR_UNSUPPORTED;
+    }
+    if (rc != EWS_OK) return rc;
+    const int total = g.B * (2 * g.N + g.N * g.N) + (a->grad_lift ? g.N * g.d_in : 0);
+    const int threads = 256;
+    const int blocks = (total + threads - 1) / threads;
+    reduce_kernel<<<blocks, threads, 0, s>>>(p, a->grad_x, a->grad_q1, a->grad_q2, a->grad_lift);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}

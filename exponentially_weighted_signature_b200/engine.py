@@ -1,0 +1,124 @@
+"""torch.autograd bindings of the CUDA engines (through the C ABI in _lib).
+
+Each engine is one autograd Function whose forward calls the library's *_fwd entry point and whose
+backward calls *_bwd. The per-sample parameter tables (log-flows and series tables) are ordinary
+differentiable torch tensors built from the generator and the clock, so their tiny maps back to the
+generator parameters and the clock run through torch autograd; the kernels return the gradients of
+the tables, of the input increments and of the lift.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream_ptr(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                "the EWS B200 engines run on CUDA tensors only (no CPU fallback); move the inputs to a GPU"
+            )
+
+
+# When set to a list, every library call appends (entry point, start event, end event, units) recorded on
+# the launching stream: bench.py reads the kernels' device time from it.
+PROFILE = None
+
+
+class _timed:
+    def __init__(self, name, device, units):
+        self.name, self.device, self.units = name, device, units
+
+    def __enter__(self):
+        if PROFILE is not None:
+            self.e0 = torch.cuda.Event(enable_timing=True)
+            self.e1 = torch.cuda.Event(enable_timing=True)
+            self.e0.record(torch.cuda.current_stream(self.device))
+        return self
+
+    def __exit__(self, *exc):
+        if PROFILE is not None:
+            self.e1.record(torch.cuda.current_stream(self.device))
+            PROFILE.append((self.name, self.e0, self.e1, self.units))
+        return False
+
+
+def increments_to_knots_grad(gdx: torch.Tensor) -> torch.Tensor:
+    """Adjoint of dx_t = x_{t+1} - x_t: (B, T, d) -> (B, T+1, d)."""
+    return F.pad(gdx, (0, 0, 1, 0)) - F.pad(gdx, (0, 0, 0, 1))
+
+
+class DiagScan(torch.autograd.Function):
+    """Diagonal engine, uniform clock: (path, x, Q1, Q2, lift) -> flat EWS (prefix or terminal)."""
+
+    @staticmethod
+    def forward(ctx, path, x, q1, q2, lift, readout, flags, chunk, increments):
+        _require_cuda(path, x, q1, q2, lift)
+        lib = _lib.load()
+        B = path.shape[0]
+        T = path.shape[1] if increments else path.shape[1] - 1
+        d_in = path.shape[2]
+        N = x.shape[-1]
+        D = N + N * N
+        dev = path.device
+        path_c = path.contiguous()
+        x_c, q1_c, q2_c = x.contiguous().float(), q1.contiguous().float(), q2.contiguous().float()
+        lift_c = None if lift is None else lift.contiguous().float()
+        out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
+        a = _lib.DiagArgs()
+        a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, 0, 0
+        fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        _lib.check(lib.ews_diag_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_diag_workspace_size")
+        fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
+        a.path, a.lift = _ptr(path_c), _ptr(lift_c)
+        a.tab_x, a.tab_q1, a.tab_q2 = _ptr(x_c), _ptr(q1_c), _ptr(q2_c)
+        a.out = _ptr(out)
+        a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
+        with _timed("ews_diag_fwd", dev, B * T):
+            _lib.check(lib.ews_diag_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_fwd")
+        ctx.meta = (readout, flags, chunk, increments, B, T, d_in, N, bb.value, path.dtype)
+        ctx.has_lift = lift is not None
+        ctx.save_for_backward(path_c, x_c, q1_c, q2_c, lift_c if lift_c is not None else torch.empty(0, device=dev), out, fwd_ws)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        readout, flags, chunk, increments, B, T, d_in, N, bwd_bytes, path_dtype = ctx.meta
+        path, x, q1, q2, lift, out, fwd_ws = ctx.saved_tensors
+        lift = lift if ctx.has_lift else None
+        lib = _lib.load()
+        dev = path.device
+        g = grad_out.contiguous().float()
+        bwd_ws = torch.empty(bwd_bytes, dtype=torch.uint8, device=dev)
+        gdx = torch.empty((B, T, d_in), device=dev, dtype=torch.float32)
+        gx = torch.empty((B, N), device=dev, dtype=torch.float32)
+        gq1 = torch.empty((B, N), device=dev, dtype=torch.float32)
+        gq2 = torch.empty((B, N, N), device=dev, dtype=torch.float32)
+        glift = torch.empty((N, d_in), device=dev, dtype=torch.float32) if lift is not None else None
+        a = _lib.DiagArgs()
+        a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, 0, 0
+        a.path, a.lift = _ptr(path), _ptr(lift)
+        a.tab_x, a.tab_q1, a.tab_q2 = _ptr(x), _ptr(q1), _ptr(q2)
+        a.out, a.grad_out = _ptr(out), _ptr(g)
+        a.grad_dx, a.grad_lift, a.grad_x, a.grad_q1, a.grad_q2 = _ptr(gdx), _ptr(glift), _ptr(gx), _ptr(gq1), _ptr(gq2)
+        a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fwd_ws.numel()
+        a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
+        with _timed("ews_diag_bwd", dev, B * T):
+            _lib.check(lib.ews_diag_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_bwd")
+        gpath = gdx if increments else increments_to_knots_grad(gdx)
+        return gpath.to(path_dtype), gx, gq1, gq2, glift, None, None, None, None

@@ -1,0 +1,232 @@
+"""The EWS layer on the B200 engines: same constructor and call as the reference's ews/layer.py.
+
+``EWS(A, N, ..., combine="b200")`` keeps the reference's options and validation
+(ews/layer.py:82-152) and its call ``layer(path, clock, return_terminal, output_format, readout,
+a_scale)`` (ews/layer.py:267-302), with the flat output layout [1, level 1, ..., level N]
+(ews/core/output_format.py:12-30). The combine value "b200" selects the CUDA engines; the reference's
+own JAX engines ("assoc", "lean", "block_kernel", "dense_kernel") are not part of this package, and
+there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch import nn
+
+from . import _lib, engine, logsig, series
+from .params import AParamConstant, B, block_sizes_of, is_diagonal
+
+COMBINE_KINDS = ("assoc", "lean", "block_kernel", "dense_kernel", "b200")
+LEAF_KINDS = ("van_loan", "series", "plane_closed", "block_series", "jordan_closed", "jordan_closed_tables")
+MODES = ("displacement", "displacement_uniform", "displacement_uniform_basepoint")
+READOUTS = ("terminal", "prefix", "mean", "max")
+
+
+def _normalize_expm_method(method: str) -> str:
+    method = method.lower()
+    if method in {"pade_lite", "pade-lite"}:
+        return "pade"
+    if method not in {"exact", "euler", "cayley", "pade"}:
+        raise ValueError("expm method must be one of 'exact', 'euler', 'cayley', 'pade'")
+    return method
+
+
+class EWS(nn.Module):
+    """Exponentially weighted signature layer on the B200 engines.
+
+    Engine dispatch follows A's structure (ews/core/kernels/combine.py:37-63): a diagonal
+    parametrisation runs the diagonal engine. Local terms are the series leaf's at order ``series_q``
+    (``leaf="series"``; ``"block_series"`` is accepted for diagonal A, where both leaves agree to the
+    series truncation).
+    """
+
+    def __init__(
+        self,
+        A,
+        N: int,
+        M: int = 20,
+        dtype: torch.dtype = torch.float32,
+        reweighting_mode: str = "displacement",
+        terminal_reduce: str = "tree",
+        van_loan_expm: str = "cayley",
+        chen_expm: str = "exact",
+        leaf: str = "series",
+        series_q: Optional[int] = 8,
+        combine: str = "b200",
+        combine_chunk: int = 0,
+        combine_tile: int = 4,
+        jordan_flows: bool = False,
+    ):
+        super().__init__()
+        self.A_param = A if isinstance(A, nn.Module) else AParamConstant(torch.as_tensor(A, dtype=dtype))
+        self.d = int(self.A_param.dim)
+        self.N = int(N)
+        self.M = int(M)
+        self.dtype = dtype
+        if reweighting_mode not in MODES:
+            raise ValueError(f"reweighting_mode must be one of {MODES}, got {reweighting_mode!r}")
+        self.reweighting_mode = reweighting_mode
+        if terminal_reduce not in {"tree", "assoc"}:
+            raise ValueError("terminal_reduce must be 'tree' or 'assoc'")
+        self.terminal_reduce = terminal_reduce
+        self.van_loan_expm = _normalize_expm_method(van_loan_expm)
+        self.chen_expm = _normalize_expm_method(chen_expm)
+        if leaf not in LEAF_KINDS:
+            raise ValueError(f"leaf must be one of {LEAF_KINDS}, got {leaf!r}")
+        if leaf in ("series", "block_series") and series_q is None:
+            raise ValueError(f"leaf={leaf!r} requires series_q (see check_series_q)")
+        if combine not in COMBINE_KINDS:
+            raise ValueError(f"combine must be one of {COMBINE_KINDS}, got {combine!r}")
+        if combine != "b200":
+            raise NotImplementedError(
+                f"combine={combine!r} is one of the reference's JAX engines; this package implements combine='b200'"
+            )
+        if leaf not in ("series", "block_series"):
+            raise NotImplementedError(f"leaf={leaf!r} is not built on the B200 engines; use leaf='series'")
+        self.leaf = leaf
+        self.series_q = int(series_q)
+        self.combine = combine
+        self.combine_chunk = int(combine_chunk)
+        self.combine_tile = int(combine_tile)
+        self.block_sizes = block_sizes_of(self.A_param)
+        if leaf == "block_series" and self.block_sizes is None:
+            raise ValueError("leaf='block_series' needs a block-diagonal A parametrisation")
+        if jordan_flows:
+            raise ValueError("jordan_flows needs combine='block_kernel' and a jordan_repeated A with uniform chains")
+        self.jordan_flows = False
+        if is_diagonal(self.A_param):
+            self.engine = "diag"
+        else:
+            self.engine = "dense"
+        if self.engine == "diag" and self.N != 2:
+            raise NotImplementedError("the diagonal engine is built for depth N=2")
+
+    @property
+    def signature_dim(self) -> int:
+        return sum(self.d**k for k in range(1, self.N + 1))
+
+    # ------------------------------------------------------------------ the engine call
+
+    def _flat(self, path, clock, readout, a_scale=1.0, lift=None, increments=False):
+        """Batched flat EWS: path (B, L, d_in) knots [(B, L-1, d_in) increments], clock (B, L)."""
+        uniform = self.reweighting_mode != "displacement"
+        basepoint = self.reweighting_mode == "displacement_uniform_basepoint"
+        if self.engine != "diag":
+            raise NotImplementedError("this build runs the diagonal engine; dense and block engines are not built yet")
+        if not uniform:
+            raise NotImplementedError("the diagonal engine is built for the uniform-clock reweighting modes")
+        kernel_readout = _lib.EWS_READOUT_TERMINAL if readout == "terminal" else _lib.EWS_READOUT_PREFIX
+        lam = self.A_param.diag_values().to(torch.float32) * a_scale
+        clock = clock.to(torch.float32)
+        h = (clock[:, 2] - clock[:, 1]) if basepoint else (clock[:, 1] - clock[:, 0])
+        x = -h[:, None] * lam[None, :]
+        q1, q2 = series.diag_tables(x, self.series_q)
+        flags = _lib.EWS_F_UNIFORM | (_lib.EWS_F_BASEPOINT if basepoint else 0)
+        if increments:
+            flags |= _lib.EWS_F_INCREMENTS
+            if path.dtype == torch.bfloat16:
+                flags |= _lib.EWS_F_BF16
+            else:
+                path = path.to(torch.float32)
+        else:
+            path = path.to(torch.float32)
+        return engine.DiagScan.apply(path, x, q1, q2, lift, kernel_readout, flags, self.combine_chunk, increments)
+
+    def forward(
+        self,
+        path: torch.Tensor,
+        clock: torch.Tensor,
+        return_terminal: bool = True,
+        output_format: str = "flat",
+        readout: Optional[str] = None,
+        a_scale=1.0,
+        *,
+        lift: Optional[torch.Tensor] = None,
+        increments: bool = False,
+    ):
+        """path (L, d) or (B, L, d) knots, clock (L,) or (B, L) (ews/layer.py:267-302).
+
+        Extensions for fused callers: ``lift`` (w, d) applies the lift B inside the kernel
+        (ews/params.py:1181-1192); ``increments=True`` takes path as (B, L-1, d) increments (float32 or
+        bfloat16) instead of knots."""
+        if readout is None:
+            readout = "terminal" if return_terminal else "prefix"
+        if readout not in READOUTS:
+            raise ValueError("readout must be 'terminal', 'prefix', 'mean', or 'max'")
+        if output_format not in ("flat", "list"):
+            raise ValueError("output_format must be 'flat' or 'list'")
+        if output_format == "list" and readout in ("mean", "max"):
+            raise ValueError(f"readout='{readout}' requires output_format='flat'")
+        single = path.dim() == 2
+        if single:
+            if clock.dim() != 1 or clock.shape[0] != path.shape[0] + (1 if increments else 0):
+                raise ValueError("clock must be 1D and aligned with path length")
+            path, clock = path[None], clock[None]
+        elif path.dim() == 3:
+            if clock.dim() != 2:
+                raise ValueError("clock must be 2D for batched paths")
+        else:
+            raise ValueError(f"Path must be 2D or 3D, got shape {tuple(path.shape)}")
+        kernel_readout = "terminal" if readout == "terminal" else "prefix"
+        flat = self._flat(path, clock, kernel_readout, a_scale, lift, increments)
+        if readout == "mean":
+            flat = flat.mean(dim=1)
+        elif readout == "max":
+            flat = flat.max(dim=1).values
+        if output_format == "list":
+            d = self.d
+            out = logsig.split_levels(flat[..., 1:], d, self.N)
+            lead = flat.shape[:-1]
+            out = [lv.reshape(lead + (d,) * k) for k, lv in enumerate(out, start=1)]
+            return [o[0] for o in out] if single else out
+        return flat[0] if single else flat
+
+
+class BToSignature(nn.Module):
+    """Optional lift B + EWS (ews/layer.py:310-341); the lift runs inside the kernel."""
+
+    def __init__(self, b: Optional[B], ewms: EWS):
+        super().__init__()
+        self.b = b
+        self.ewms = ewms
+
+    def forward(self, path, clock, return_terminal=True, output_format="flat", readout=None):
+        lift = None if self.b is None else self.b.full_matrix()
+        return self.ewms(path, clock, return_terminal=return_terminal, output_format=output_format, readout=readout, lift=lift)
+
+
+class LogEWS(nn.Module):
+    """log(EWS) in the Lyndon-word coordinates (ews/layer.py:440-556)."""
+
+    def __init__(self, A, N: int, **kw):
+        super().__init__()
+        self.ewms = EWS(A, N, **kw)
+        self.d = self.ewms.d
+        self.N = self.ewms.N
+
+    @property
+    def log_signature_dim(self) -> int:
+        return logsig.log_signature_dim(self.d, self.N)
+
+    def forward(self, path, clock, return_terminal=True, output_format="flat", readout=None, *, lift=None, increments=False):
+        if readout is None:
+            readout = "terminal" if return_terminal else "prefix"
+        if readout not in READOUTS:
+            raise ValueError("readout must be 'terminal', 'prefix', 'mean', or 'max'")
+        inner = "terminal" if readout == "terminal" else "prefix"
+        flat = self.ewms(path, clock, readout=inner, output_format="flat", lift=lift, increments=increments)
+        levels = logsig.split_levels(flat[..., 1:], self.d, self.N)
+        log_levels = logsig.tensor_log(levels)
+        if output_format == "list":
+            if readout in ("mean", "max"):
+                raise ValueError(f"readout='{readout}' requires output_format='flat'")
+            idx = [torch.as_tensor(ix, device=flat.device) for ix in logsig._flat_indices(self.N, self.d)]
+            return [lv[..., ix] for lv, ix in zip(log_levels, idx)]
+        feat = logsig.compress(log_levels, self.d)
+        if readout == "mean":
+            return feat.mean(dim=-2)
+        if readout == "max":
+            return feat.max(dim=-2).values
+        return feat

@@ -1,0 +1,115 @@
+/*
+ * ews_b200.h — C ABI of the B200 (sm_100a) EWS hot-path library, libews_b200.so.
+ *
+ * The exponentially weighted signature (EWS) of a path x with clock theta and generator A is the
+ * modified-Chen prefix scan of per-interval local terms: with M_t = exp(-dtheta_t A),
+ *
+ *     S_k,t = M_t^{(x)k} S_k,t-1 + sum_{i=1}^{k-1} (M_t^{(x)i} S_i,t-1) (x) s_{k-i},t + s_k,t,
+ *
+ * and the local terms s_k,t come from the series leaf (letters b_p = (-dtheta/p) A b_{p-1}, b_0 = dx).
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t, never allocates, and
+ * returns EWS_OK or an error code. Buffers are stream-ordered; the caller owns all memory,
+ * including the workspaces whose sizes the *_workspace_size queries return.
+ *
+ * The reference interface these replace is the combine engine boundary
+ *     combine_packed(kind, local_signatures, A, interval_times, N, chen_expm, cached, basepoint,
+ *                    *, terminal, block_sizes, chunk_target, tile, jordan_chain)
+ * (ews/core/kernels/combine.py:193-224 of alexandre-bloch/exponentially-weighted-signature) together
+ * with the leaf it is fed by (ews/core/leaf.py:50-198) and the custom VJPs of its kernels
+ * (ews/core/kernels/pallas_combine.py:1673-1801 block, :2628-2711 dense). Unlike the reference, the
+ * local terms and the lift B (ews/params.py:1181-1192) are fused into the kernels, so the VJP returns
+ * gradients for the increments, the clock steps and the generator tables directly.
+ */
+#ifndef EWS_B200_H
+#define EWS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ews_stream_t; /* = cudaStream_t */
+
+/* ---- status codes ---------------------------------------------------------------------------- */
+#define EWS_OK 0
+#define EWS_ERR_INVALID_ARGUMENT 1   /* bad shape, null pointer, unsupported combination */
+#define EWS_ERR_UNSUPPORTED 2        /* valid but not built: e.g. dim above the engine's limit */
+#define EWS_ERR_WORKSPACE 3          /* workspace missing or smaller than the query returned */
+#define EWS_ERR_LAUNCH 4             /* a CUDA launch failed (cudaGetLastError after the launch) */
+#define EWS_ERR_LOOKBACK_TIMEOUT 5   /* a device-side wait for a neighbouring chunk ran out (read
+                                        with ews_read_device_status; the outputs are then invalid) */
+
+/* ---- flags ----------------------------------------------------------------------------------- */
+#define EWS_F_UNIFORM 1u        /* uniform clock: per-sample constant flow/local tables (cached flows,
+                                   ews/core/chen_scan.py:155-168 cached=True) */
+#define EWS_F_INCREMENTS 2u     /* `path` holds increments (B, T, d_in) instead of knots (B, T+1, d_in) */
+#define EWS_F_BF16 4u           /* `path` is bfloat16 (accumulation stays float32) */
+#define EWS_F_BASEPOINT 8u      /* uniform with basepoint: step 0 has the identity flow
+                                   (ews/core/chen_scan.py:160-166) */
+
+#define EWS_READOUT_PREFIX 0    /* out: (B, T, 1 + D), row t = [1, S_1,t, ..., S_n,t] */
+#define EWS_READOUT_TERMINAL 1  /* out: (B, 1 + D), the last row only */
+
+/* ---- diagonal engine: A = diag(lambda) --------------------------------------------------------
+ * Replaces combine_packed(kind="block_kernel", block_sizes=(1,)*N) fed by leaf="series" /
+ * "block_series" (ews/core/kernels/combine.py:233-258, ews/core/kernels/blockdiag_engine.py:88-163,
+ * ews/core/series_leaf.py:72-127). Depth 2, dim <= 32.
+ *
+ * Uniform clock (EWS_F_UNIFORM): with x_b = -h_b lambda (h_b the shared clock step of sample b),
+ *   tab_x  (B, dim)       log-flows x, flow rho = exp(x)
+ *   tab_q1 (B, dim)       Q1_i  = sum_{p<=q} c1_p x_i^p / p!             (s1_i = Q1_i dy_i)
+ *   tab_q2 (B, dim, dim)  Q2_ij = sum_{a+b<=q} c2_ab x_i^a x_j^b / a!b!  (s2_ij = Q2_ij dy_i dy_j)
+ * where dy = lift @ dx. The backward returns dL/dx (grad_x), dL/dQ1, dL/dQ2 per sample, so the caller
+ * chains them to lambda and the clock with the (tiny) table maps. */
+typedef struct ews_diag_args {
+    int batch;         /* B */
+    int steps;         /* T: intervals per path */
+    int d_in;          /* input channels (before the lift) */
+    int dim;           /* N: state dimension (after the lift) */
+    int depth;         /* truncation depth (2) */
+    int chunk;         /* chunk length (0: the library's choice) */
+    int readout;       /* EWS_READOUT_* */
+    unsigned flags;    /* EWS_F_* */
+    int series_q;      /* series order (non-uniform tables) */
+    int spin_limit;    /* polls before a look-back wait gives up (0: default) */
+    /* inputs */
+    const void* path;        /* (B, T+1, d_in) knots or (B, T, d_in) increments; f32 or bf16 */
+    const float* clock;      /* (B, T+1) clock knots (non-uniform) or NULL */
+    const float* lift;       /* (dim, d_in) lift B, or NULL for the identity (d_in == dim) */
+    const float* tab_x;      /* see above */
+    const float* tab_q1;
+    const float* tab_q2;
+    /* forward output */
+    float* out;
+    /* backward */
+    const float* grad_out;   /* same shape as out */
+    float* grad_dx;          /* (B, T, d_in): dL/d(increments) */
+    float* grad_lift;        /* (dim, d_in) or NULL */
+    float* grad_x;           /* (B, dim) */
+    float* grad_q1;          /* (B, dim) */
+    float* grad_q2;          /* (B, dim, dim) */
+    /* workspaces: fwd_ws is written by the forward and read by the backward (chunk aggregates and
+       carries); bwd_ws is private to the backward */
+    void* fwd_ws;
+    size_t fwd_ws_bytes;
+    void* bwd_ws;
+    size_t bwd_ws_bytes;
+} ews_diag_args;
+
+int ews_diag_workspace_size(const ews_diag_args* a, size_t* fwd_bytes, size_t* bwd_bytes);
+int ews_diag_fwd(const ews_diag_args* a, ews_stream_t stream);
+int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream);
+
+/* ---- utilities --------------------------------------------------------------------------------- */
+/* Copies the device-side status word of a workspace (EWS_OK or EWS_ERR_LOOKBACK_TIMEOUT) to the host;
+ * synchronises the stream. */
+int ews_read_device_status(const void* workspace, ews_stream_t stream, int* status);
+const char* ews_error_string(int code);
+int ews_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EWS_B200_H */

@@ -299,13 +299,14 @@ def pack(levels):
 
 
 def apply_flow(M, level, k, d):
-    """M applied along every axis of a flat level-k tensor (``ews/core/chen_scan.py:98-111``)."""
+    """M applied along every axis of a flat level-k tensor (``ews/core/chen_scan.py:98-111``), one axis at a
+    time (the contraction order jnp.einsum's path optimiser picks: d^{k+1} per tensor)."""
     lead = level.shape[:-1]
     T = level.reshape(lead + (d,) * k)
-    outs = "ABCDEFGH"[:k]
-    ins = "abcdefgh"[:k]
-    eq = ",".join(f"...{outs[j]}{ins[j]}" for j in range(k)) + f",...{ins}->...{outs}"
-    return torch.einsum(eq, *([M] * k), T).reshape(lead + (d**k,))
+    for ax in range(k):
+        # contract axis ax of T with M's second index, put the new index back in place
+        T = torch.movedim(torch.einsum("...ij,...j->...i", M[(...,) + (None,) * (k - 1) + (slice(None), slice(None))], torch.movedim(T, len(lead) + ax, -1)), -1, len(lead) + ax)
+    return T.reshape(lead + (d**k,))
 
 
 def tensor_mult(X, Y):
