@@ -46,12 +46,12 @@ def _peaks():
 # ------------------------------------------------------------------------------------ workloads
 
 
-def _diag_setup(cfg, rank, world, device, precision):
+def _diag_setup(cfg, rank, world, device, precision, batch=None):
     """Per-rank inputs and model of a diagonal-engine configuration (config1, config5)."""
     from exponentially_weighted_signature_b200 import EWS, LogEWS, AParamDiag, B as Lift, workloads, series
     from exponentially_weighted_signature_b200.parallel import shard_range
 
-    case = getattr(workloads, cfg)()
+    case = getattr(workloads, cfg)(**({"B": batch} if batch else {}))
     Bg, T, N = case["B"], case["T"], case["N"]
     if Bg % world == 0:
         s0, s1 = shard_range(Bg, rank, world)
@@ -220,7 +220,7 @@ def run_b200(args, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    setup = _diag_setup(args.config, rank, world, device, args.precision)
+    setup = _diag_setup(args.config, rank, world, device, args.precision, args.batch)
     step, params = setup["step"], setup["params"]
     x = setup["x_host"].to(device)
     clock = setup["clock_host"].to(device)
@@ -341,7 +341,7 @@ def run_b200(args, rank, world, local_rank):
         "dtype": meta["dtype"],
         "data": "synthetic (seeded, BASELINE.json shapes and distributions)",
         "config": {
-            "workload": args.config,
+            "workload": args.config + (f" (batch {args.batch})" if args.batch else ""),
             "global_batch": meta["B_global"],
             "seq_len": meta["T"],
             "state_dim": meta["N"],
@@ -413,6 +413,7 @@ def main():
     ap.add_argument("--config", default="config5", choices=["config1", "config5"])
     ap.add_argument("--precision", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling on a smaller case)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

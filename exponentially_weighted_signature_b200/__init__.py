@@ -6,7 +6,7 @@ the reference's layer API (alexandre-bloch/exponentially-weighted-signature, ews
 """
 
 from . import params, series
-from .layer import COMBINE_KINDS, EWS, BToSignature, LogEWS
+from .layer import COMBINE_KINDS, EWS, BToSignature, LogEWS, configure
 from .logsig import log_level_sizes, log_signature_dim
 from .params import AParamBlockDiag, AParamConstant, AParamDiag, AParamEFM, AParamGeneral, B
 from .series import check_series_q, series_error_bound, suggest_series_q
@@ -16,6 +16,7 @@ __all__ = [
     "EWS",
     "BToSignature",
     "LogEWS",
+    "configure",
     "AParamBlockDiag",
     "AParamConstant",
     "AParamDiag",

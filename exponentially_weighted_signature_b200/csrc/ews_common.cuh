@@ -52,16 +52,17 @@ __device__ __forceinline__ void publish(int* flag, int value) {
     if ((threadIdx.x & 31) == 0) st_release(flag, value);
 }
 
-// Warp-wide bounded wait for a slot to leave kFlagEmpty. Returns the flag value, or -1 when the wait ran
-// out (the error word is then set) or another tile already failed. Never spins without a limit.
-__device__ __forceinline__ int wait_slot(const int* flag, DeviceStatus* st, int limit, int tile) {
+// Warp-wide bounded wait for a slot's flag to reach at least `want` (kFlagAgg: any published value;
+// kFlagIncl: the inclusive value). Returns the flag value, or -1 when the wait ran out (the error word is
+// then set) or another tile already failed. Never spins without a limit.
+__device__ __forceinline__ int wait_slot(const int* flag, DeviceStatus* st, int limit, int tile, int want = kFlagAgg) {
     int v = kFlagEmpty;
     if ((threadIdx.x & 31) == 0) {
         unsigned ns = 32;
         int it = 0;
         for (; it < limit; ++it) {
             v = ld_acquire(flag);
-            if (v != kFlagEmpty) break;
+            if (v >= want) break;
             if (*((volatile int*)&st->error) != 0) {
                 v = -1;
                 break;
@@ -69,7 +70,7 @@ __device__ __forceinline__ int wait_slot(const int* flag, DeviceStatus* st, int 
             __nanosleep(ns);
             if (ns < 2048) ns <<= 1;
         }
-        if (v == kFlagEmpty) {
+        if (v >= 0 && v < want) {
             if (atomicCAS(&st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) st->err_tile = tile;
             v = -1;
         }

@@ -15,6 +15,11 @@
 // publish their aggregate, look back over their predecessors (decoupled look-back) and re-run the
 // recursion from the carry to emit the prefix rows. Every wait is bounded.
 //
+// Flows are carried as complements delta = 1 - rho = -expm1(x): S rho = S - delta S and
+// rho_i rho_j = 1 - (delta_i + delta_j - delta_i delta_j). A rho within 1e-4 of one, rounded once and applied
+// T times, drifts by ~T 2^-24 (the reference's float32 path loses 5e-5 relative at T = 4096 that way); the
+// complement keeps the flow's rounding relative to delta instead.
+//
 // Backward: the adjoint of step t is lambda2 <- rho rho^T o lambda2, lambda1 <- rho o (lambda1 +
 // lambda2 s1). Chunks compute a zero-carry local adjoint, look back over the later chunks (whose
 // transposed chunk maps come from the forward aggregates) and then run the exact adjoint from the
@@ -36,6 +41,10 @@ struct Geom {
     int spin_limit;
     int SR;      // prefix rows staged per span store
     int ntiles;  // B * C
+    // per-warp shared-memory carve-up (floats), after the CTA's lift matrix (lift_n floats)
+    int lift_n;
+    int f_dys, f_stage, f_per_warp;                            // forward: dxs at 0
+    int b_dys, b_dyg, b_lam1, b_gst, b_sst, b_per_warp;        // backward: dxs at 0
 };
 
 struct Params {
@@ -65,23 +74,26 @@ __host__ __device__ inline int align4(int n) { return (n + 3) & ~3; }
 // --------------------------------------------------------------------------------- lane elements
 
 template <int RI, int RJ>
-struct Elem {  // a Chen group element restricted to a lane's block: flows, level 1, level 2
-    float Pr[RI], Pc[RJ], S1r[RI], S1c[RJ], S2[RI][RJ];
+struct Elem {  // a Chen group element restricted to a lane's block: flow complements, level 1, level 2
+    float Dr[RI], Dc[RJ], S1r[RI], S1c[RJ], S2[RI][RJ];
     __device__ void identity() {
 #pragma unroll
         for (int r = 0; r < RI; ++r) {
-            Pr[r] = 1.f;
+            Dr[r] = 0.f;
             S1r[r] = 0.f;
 #pragma unroll
             for (int c = 0; c < RJ; ++c) S2[r][c] = 0.f;
         }
 #pragma unroll
         for (int c = 0; c < RJ; ++c) {
-            Pc[c] = 1.f;
+            Dc[c] = 0.f;
             S1c[c] = 0.f;
         }
     }
 };
+
+// Complement of a product of flows: 1 - (1-a)(1-b) = a + b - ab.
+__device__ __forceinline__ float comp_mul(float a, float b) { return fmaf(-a, b, a + b); }
 
 // res = L (x) R: L flowed by R's flow, then the truncated tensor product (ews/core/chen_scan.py:124-152).
 template <int RI, int RJ>
@@ -89,28 +101,30 @@ __device__ __forceinline__ void chen_mul(const Elem<RI, RJ>& L, const Elem<RI, R
     Elem<RI, RJ> o;
 #pragma unroll
     for (int r = 0; r < RI; ++r) {
-        const float u = R.Pr[r] * L.S1r[r];
+        const float u = fmaf(-R.Dr[r], L.S1r[r], L.S1r[r]);
 #pragma unroll
-        for (int c = 0; c < RJ; ++c)
-            o.S2[r][c] = fmaf(R.Pr[r] * R.Pc[c], L.S2[r][c], fmaf(u, R.S1c[c], R.S2[r][c]));
+        for (int c = 0; c < RJ; ++c) {
+            const float dd = comp_mul(R.Dr[r], R.Dc[c]);
+            o.S2[r][c] = fmaf(-dd, L.S2[r][c], L.S2[r][c] + fmaf(u, R.S1c[c], R.S2[r][c]));
+        }
         o.S1r[r] = u + R.S1r[r];
-        o.Pr[r] = L.Pr[r] * R.Pr[r];
+        o.Dr[r] = comp_mul(L.Dr[r], R.Dr[r]);
     }
 #pragma unroll
     for (int c = 0; c < RJ; ++c) {
-        o.S1c[c] = fmaf(R.Pc[c], L.S1c[c], R.S1c[c]);
-        o.Pc[c] = L.Pc[c] * R.Pc[c];
+        o.S1c[c] = fmaf(-R.Dc[c], L.S1c[c], L.S1c[c] + R.S1c[c]);
+        o.Dc[c] = comp_mul(L.Dc[c], R.Dc[c]);
     }
     out = o;
 }
 
-// Slot layout (floats): [P (NP) | S1 (NP) | S2 (NP x NP)].
+// Slot layout (floats): [flow complement (NP) | S1 (NP) | S2 (NP x NP)].
 template <int RI, int RJ>
 __device__ __forceinline__ void store_elem(float* slot, const Elem<RI, RJ>& e, int NP, int i0, int j0, int tj) {
     if (tj == 0) {
 #pragma unroll
         for (int r = 0; r < RI; ++r) {
-            slot[i0 + r] = e.Pr[r];
+            slot[i0 + r] = e.Dr[r];
             slot[NP + i0 + r] = e.S1r[r];
         }
     }
@@ -124,14 +138,14 @@ template <int RI, int RJ>
 __device__ __forceinline__ void load_elem(const float* slot, Elem<RI, RJ>& e, int NP, int i0, int j0) {
 #pragma unroll
     for (int r = 0; r < RI; ++r) {
-        e.Pr[r] = ldcg(slot + i0 + r);
+        e.Dr[r] = ldcg(slot + i0 + r);
         e.S1r[r] = ldcg(slot + NP + i0 + r);
 #pragma unroll
         for (int c = 0; c < RJ; ++c) e.S2[r][c] = ldcg(slot + 2 * NP + (i0 + r) * NP + j0 + c);
     }
 #pragma unroll
     for (int c = 0; c < RJ; ++c) {
-        e.Pc[c] = ldcg(slot + j0 + c);
+        e.Dc[c] = ldcg(slot + j0 + c);
         e.S1c[c] = ldcg(slot + NP + j0 + c);
     }
 }
@@ -140,7 +154,7 @@ __device__ __forceinline__ void load_elem(const float* slot, Elem<RI, RJ>& e, in
 
 template <int RI, int RJ>
 struct Tables {
-    float xr[RI], xc[RJ], rho_r[RI], rho_c[RJ], q1r[RI], q1c[RJ], q2[RI][RJ];
+    float xr[RI], xc[RJ], dr[RI], dc[RJ], q1r[RI], q1c[RJ], q2[RI][RJ];  // d = 1 - rho = -expm1(x)
     __device__ void load(const Params& p, int b, int i0, int j0) {
         const int N = p.g.N;
         const float* tx = p.tab_x + (size_t)b * N;
@@ -150,7 +164,7 @@ struct Tables {
         for (int r = 0; r < RI; ++r) {
             const int i = i0 + r;
             xr[r] = i < N ? tx[i] : 0.f;
-            rho_r[r] = expf(xr[r]);
+            dr[r] = -expm1f(xr[r]);
             q1r[r] = i < N ? t1[i] : 0.f;
 #pragma unroll
             for (int c = 0; c < RJ; ++c) {
@@ -162,7 +176,7 @@ struct Tables {
         for (int c = 0; c < RJ; ++c) {
             const int j = j0 + c;
             xc[c] = j < N ? tx[j] : 0.f;
-            rho_c[c] = expf(xc[c]);
+            dc[c] = -expm1f(xc[c]);
             q1c[c] = j < N ? t1[j] : 0.f;
         }
     }
@@ -198,42 +212,45 @@ __device__ void load_increments(const Params& p, const float* liftS, float* dxs,
 
 // --------------------------------------------------------------------------------- the step
 
-// The flow of a step: rho, except the identity for the basepoint interval (ews/core/chen_scan.py:160-166).
+// The flow complement of a step: delta, except the identity (delta = 0) for the basepoint interval
+// (ews/core/chen_scan.py:160-166).
 template <int RI, int RJ>
 __device__ __forceinline__ void step_flow(const Tables<RI, RJ>& tb, bool identity, float fr[RI], float fc[RJ]) {
 #pragma unroll
-    for (int r = 0; r < RI; ++r) fr[r] = identity ? 1.f : tb.rho_r[r];
+    for (int r = 0; r < RI; ++r) fr[r] = identity ? 0.f : tb.dr[r];
 #pragma unroll
-    for (int c = 0; c < RJ; ++c) fc[c] = identity ? 1.f : tb.rho_c[c];
+    for (int c = 0; c < RJ; ++c) fc[c] = identity ? 0.f : tb.dc[c];
 }
 
 // One modified-Chen step S <- flow(S) (x) (s1, s2) on a lane's block, also accumulating the flow product.
+// bp: the basepoint interval (dtheta = 0), whose series local terms are those of x = 0: Q1 = 1, Q2 = 1/2.
 template <int RI, int RJ>
 __device__ __forceinline__ void chen_step(const Tables<RI, RJ>& tb, const float* dyk, int i0, int j0,
-                                          Elem<RI, RJ>& S, const float fr[RI], const float fc[RJ]) {
+                                          Elem<RI, RJ>& S, const float fr[RI], const float fc[RJ], bool bp = false) {
     float dyr[RI], dyc[RJ], s1c[RJ];
 #pragma unroll
     for (int r = 0; r < RI; ++r) dyr[r] = dyk[i0 + r];
 #pragma unroll
     for (int c = 0; c < RJ; ++c) {
         dyc[c] = dyk[j0 + c];
-        s1c[c] = tb.q1c[c] * dyc[c];
+        s1c[c] = (bp ? 1.f : tb.q1c[c]) * dyc[c];
     }
 #pragma unroll
     for (int r = 0; r < RI; ++r) {
-        const float u = fr[r] * S.S1r[r];
+        const float u = fmaf(-fr[r], S.S1r[r], S.S1r[r]);
 #pragma unroll
         for (int c = 0; c < RJ; ++c) {
-            const float loc = tb.q2[r][c] * (dyr[r] * dyc[c]);
-            S.S2[r][c] = fmaf(fr[r] * fc[c], S.S2[r][c], fmaf(u, s1c[c], loc));
+            const float loc = (bp ? 0.5f : tb.q2[r][c]) * (dyr[r] * dyc[c]);
+            const float dd = comp_mul(fr[r], fc[c]);
+            S.S2[r][c] = fmaf(-dd, S.S2[r][c], S.S2[r][c] + fmaf(u, s1c[c], loc));
         }
-        S.S1r[r] = fmaf(tb.q1r[r], dyr[r], u);
-        S.Pr[r] *= fr[r];
+        S.S1r[r] = fmaf(bp ? 1.f : tb.q1r[r], dyr[r], u);
+        S.Dr[r] = comp_mul(S.Dr[r], fr[r]);
     }
 #pragma unroll
     for (int c = 0; c < RJ; ++c) {
-        S.S1c[c] = fmaf(fc[c], S.S1c[c], s1c[c]);
-        S.Pc[c] *= fc[c];
+        S.S1c[c] = fmaf(-fc[c], S.S1c[c], S.S1c[c] + s1c[c]);
+        S.Dc[c] = comp_mul(S.Dc[c], fc[c]);
     }
 }
 
@@ -264,17 +281,15 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
     extern __shared__ float smem[];
     const Geom& g = p.g;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int liftN = align4(NP * g.d_in);
     float* liftS = smem;
     for (int e = threadIdx.x; e < NP * g.d_in; e += blockDim.x) {
         const int r = e / g.d_in, cc = e - r * g.d_in;
         liftS[e] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
     }
     __syncthreads();
-    const int per_warp = align4(g.Lc * g.d_in) + align4(g.Lc * NP) + align4(g.SR * g.W);
-    float* dxs = smem + liftN + warp * per_warp;
-    float* dys = dxs + align4(g.Lc * g.d_in);
-    float* stage = dys + align4(g.Lc * NP);
+    float* dxs = smem + g.lift_n + warp * g.f_per_warp;
+    float* dys = dxs + g.f_dys;
+    float* stage = dxs + g.f_stage;
 
     const int ti = lane >> 3, tj = lane & 7;
     const int i0 = ti * RI, j0 = tj * RJ;
@@ -295,8 +310,9 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
         A.identity();
         for (int k = 0; k < len; ++k) {
             float fr[RI], fc[RJ];
-            step_flow(tb, basepoint && (t0 + k == 0), fr, fc);
-            chen_step(tb, dys + k * NP, i0, j0, A, fr, fc);
+            const bool bp = basepoint && (t0 + k == 0);
+            step_flow(tb, bp, fr, fc);
+            chen_step(tb, dys + k * NP, i0, j0, A, fr, fc, bp);
         }
         const size_t slot = ((size_t)b * g.C + c) * g.SW;
         int* flag = p.flags + (size_t)b * g.C + c;
@@ -304,7 +320,7 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
         excl.identity();
         if (c == 0) {
             store_elem(p.incl + slot, A, NP, i0, j0, tj);
-            publish(flag, kFlagIncl);
+            if (!(g.flags & EWS_F_TEST_WITHHOLD)) publish(flag, kFlagIncl);
         } else {
             store_elem(p.agg + slot, A, NP, i0, j0, tj);
             publish(flag, kFlagAgg);
@@ -312,8 +328,9 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
             Elem<RI, RJ> acc;
             acc.identity();
             int j = c - 1;
+            const int want = (g.flags & EWS_F_DETERMINISTIC) ? kFlagIncl : kFlagAgg;
             for (;;) {
-                const int f = wait_slot(p.flags + (size_t)b * g.C + j, p.st, g.spin_limit, tile);
+                const int f = wait_slot(p.flags + (size_t)b * g.C + j, p.st, g.spin_limit, tile, want);
                 if (f < 0) return;  // timeout or another tile failed: the error word is set
                 Elem<RI, RJ> X;
                 const size_t sj = ((size_t)b * g.C + j) * g.SW;
@@ -351,8 +368,9 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
         int k0 = 0;
         for (int k = 0; k < len; ++k) {
             float fr[RI], fc[RJ];
-            step_flow(tb, basepoint && (t0 + k == 0), fr, fc);
-            chen_step(tb, dys + k * NP, i0, j0, S, fr, fc);
+            const bool bp = basepoint && (t0 + k == 0);
+            step_flow(tb, bp, fr, fc);
+            chen_step(tb, dys + k * NP, i0, j0, S, fr, fc, bp);
             stage_row(stage + (k - k0) * g.W, S, g.N, i0, j0, tj, lane);
             if (k - k0 == g.SR - 1 || k == len - 1) {
                 __syncwarp();
@@ -406,7 +424,7 @@ __device__ __forceinline__ void rows_to_cols(const float vr[RI], float vc[RJ], i
 }
 
 // Transposed Jacobian of right-multiplication by G = (P, U1, U2): mu2 = P P^T o l2,
-// mu1 = P o (l1 + l2 U1). Applied in place.
+// mu1 = P o (l1 + l2 U1), with P = 1 - D. Applied in place.
 template <int RI, int RJ>
 __device__ __forceinline__ void apply_JT(const Elem<RI, RJ>& G, Adj<RI, RJ>& a) {
 #pragma unroll
@@ -414,10 +432,10 @@ __device__ __forceinline__ void apply_JT(const Elem<RI, RJ>& G, Adj<RI, RJ>& a) 
         float w = 0.f;
 #pragma unroll
         for (int c = 0; c < RJ; ++c) w = fmaf(a.L2[r][c], G.S1c[c], w);
-        w = row_sum(w);
-        a.L1r[r] = G.Pr[r] * (a.L1r[r] + w);
+        w = row_sum(w) + a.L1r[r];
+        a.L1r[r] = fmaf(-G.Dr[r], w, w);
 #pragma unroll
-        for (int c = 0; c < RJ; ++c) a.L2[r][c] *= G.Pr[r] * G.Pc[c];
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] = fmaf(-comp_mul(G.Dr[r], G.Dc[c]), a.L2[r][c], a.L2[r][c]);
     }
 }
 
@@ -494,18 +512,21 @@ template <int RI, int RJ>
 __device__ __forceinline__ void bwd_step(const Tables<RI, RJ>& tb, const float fr[RI], const float fc[RJ],
                                          const float* dyk, const float S1p[RI], const float S2p[RI][RJ],
                                          Adj<RI, RJ>& a, Grads<RI, RJ>& gr, float* dyg, int i0, int j0, int ti,
-                                         int tj) {
+                                         int tj, bool bp = false) {
     float dyr[RI], dyc[RJ], s1c[RJ], u[RI];
 #pragma unroll
     for (int r = 0; r < RI; ++r) {
         dyr[r] = dyk[i0 + r];
-        u[r] = fr[r] * S1p[r];
+        u[r] = fmaf(-fr[r], S1p[r], S1p[r]);
     }
+    float q1c[RJ];
 #pragma unroll
     for (int c = 0; c < RJ; ++c) {
         dyc[c] = dyk[j0 + c];
-        s1c[c] = tb.q1c[c] * dyc[c];
+        q1c[c] = bp ? 1.f : tb.q1c[c];
+        s1c[c] = q1c[c] * dyc[c];
     }
+    const float table_w = bp ? 0.f : 1.f;  // the basepoint interval does not read the tables
     // row sums: w (adjoint recursion), z (dy from s2, row side)
     float w[RI], z[RI];
     // column partials: y (ds1), v (dy from s2, column side), e (flow gradient, column side)
@@ -521,16 +542,16 @@ __device__ __forceinline__ void bwd_step(const Tables<RI, RJ>& tb, const float f
 #pragma unroll
         for (int c = 0; c < RJ; ++c) {
             const float l2 = a.L2[r][c];
-            const float l2q = l2 * tb.q2[r][c];
+            const float l2q = l2 * (bp ? 0.5f : tb.q2[r][c]);
             wr = fmaf(l2, s1c[c], wr);
             zr = fmaf(l2q, dyc[c], zr);
             y[c] = fmaf(l2, u[r], y[c]);
             v[c] = fmaf(l2q, dyr[r], v[c]);
             // flow gradient (w.r.t. x = log rho) of rho_i rho_j S2_ij, credited to i and to j
-            const float fl = l2 * (fr[r] * fc[c]) * S2p[r][c];
+            const float fl = l2 * (1.f - comp_mul(fr[r], fc[c])) * S2p[r][c];
             fx = fmaf(l2, u[r] * s1c[c], fx + fl);
             gr.gxc[c] += fl;
-            gr.dq2[r][c] = fmaf(l2, dyr[r] * dyc[c], gr.dq2[r][c]);
+            gr.dq2[r][c] = fmaf(table_w * l2, dyr[r] * dyc[c], gr.dq2[r][c]);
         }
         w[r] = row_sum(wr);
         z[r] = row_sum(zr);
@@ -543,34 +564,35 @@ __device__ __forceinline__ void bwd_step(const Tables<RI, RJ>& tb, const float f
     for (int c = 0; c < RJ; ++c) {
         const float ds1 = l1c[c] + col_sum(y[c]);
         const float vv = col_sum(v[c]);
-        gr.dq1c[c] = fmaf(ds1, dyc[c], gr.dq1c[c]);
-        if (ti == 0) dyg[j0 + c] = fmaf(ds1, tb.q1c[c], vv + zc[c]);
+        gr.dq1c[c] = fmaf(table_w * ds1, dyc[c], gr.dq1c[c]);
+        if (ti == 0) dyg[j0 + c] = fmaf(ds1, q1c[c], vv + zc[c]);
     }
     // cotangent of S_{t-1}
 #pragma unroll
     for (int r = 0; r < RI; ++r) {
-        a.L1r[r] = fr[r] * (a.L1r[r] + w[r]);
+        const float lw = a.L1r[r] + w[r];
+        a.L1r[r] = fmaf(-fr[r], lw, lw);
 #pragma unroll
-        for (int c = 0; c < RJ; ++c) a.L2[r][c] *= fr[r] * fc[c];
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] = fmaf(-comp_mul(fr[r], fc[c]), a.L2[r][c], a.L2[r][c]);
     }
 }
 
 // The transposed step alone (no gradients): used for the zero-carry local adjoint.
 template <int RI, int RJ>
 __device__ __forceinline__ void adj_step(const Tables<RI, RJ>& tb, const float fr[RI], const float fc[RJ],
-                                         const float* dyk, Adj<RI, RJ>& a, int j0) {
+                                         const float* dyk, Adj<RI, RJ>& a, int j0, bool bp = false) {
     float s1c[RJ];
 #pragma unroll
-    for (int c = 0; c < RJ; ++c) s1c[c] = tb.q1c[c] * dyk[j0 + c];
+    for (int c = 0; c < RJ; ++c) s1c[c] = (bp ? 1.f : tb.q1c[c]) * dyk[j0 + c];
 #pragma unroll
     for (int r = 0; r < RI; ++r) {
         float wr = 0.f;
 #pragma unroll
         for (int c = 0; c < RJ; ++c) wr = fmaf(a.L2[r][c], s1c[c], wr);
-        wr = row_sum(wr);
-        a.L1r[r] = fr[r] * (a.L1r[r] + wr);
+        wr = row_sum(wr) + a.L1r[r];
+        a.L1r[r] = fmaf(-fr[r], wr, wr);
 #pragma unroll
-        for (int c = 0; c < RJ; ++c) a.L2[r][c] *= fr[r] * fc[c];
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] = fmaf(-comp_mul(fr[r], fc[c]), a.L2[r][c], a.L2[r][c]);
     }
 }
 
@@ -651,22 +673,20 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     extern __shared__ float smem[];
     const Geom& g = p.g;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int liftN = align4(NP * g.d_in);
     float* liftS = smem;
     for (int e = threadIdx.x; e < NP * g.d_in; e += blockDim.x) {
         const int r = e / g.d_in, cc = e - r * g.d_in;
         liftS[e] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
     }
     __syncthreads();
-    // per warp: dxs, dys, dyg (Lc x NP), lam1 (Lc x NP, terminal), gstage (SR x W), sstage (SR x W)
-    const int stage_n = align4(max(g.SR * g.W, g.Lc * g.d_in));
-    const int per_warp = align4(g.Lc * g.d_in) + 3 * align4(g.Lc * NP) + 2 * stage_n;
-    float* dxs = smem + liftN + warp * per_warp;
-    float* dys = dxs + align4(g.Lc * g.d_in);
-    float* dyg = dys + align4(g.Lc * NP);
-    float* lam1 = dyg + align4(g.Lc * NP);
-    float* gst = lam1 + align4(g.Lc * NP);
-    float* sst = gst + stage_n;
+    // per warp: dxs, dys, dyg (Lc x NP), lam1 (Lc x NP, terminal only), gst (gradient rows, and the dx
+    // staging), sst (forward rows, prefix only)
+    float* dxs = smem + g.lift_n + warp * g.b_per_warp;
+    float* dys = dxs + g.b_dys;
+    float* dyg = dxs + g.b_dyg;
+    float* lam1 = dxs + g.b_lam1;
+    float* gst = dxs + g.b_gst;
+    float* sst = dxs + g.b_sst;
 
     const int ti = lane >> 3, tj = lane & 7;
     const int i0 = ti * RI, j0 = tj * RJ;
@@ -702,8 +722,9 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                 for (int k = kb - 1; k >= k0; --k) {
                     add_grad_row(mu, gst + (k - k0) * g.W, g.N, i0, j0);
                     float fr[RI], fc[RJ];
-                    step_flow(tb, basepoint && (t0 + k == 0), fr, fc);
-                    adj_step(tb, fr, fc, dys + k * NP, mu, j0);
+                    const bool bp = basepoint && (t0 + k == 0);
+                    step_flow(tb, bp, fr, fc);
+                    adj_step(tb, fr, fc, dys + k * NP, mu, j0, bp);
                 }
             }
         } else {
@@ -719,19 +740,21 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                     for (int r = 0; r < RI; ++r) lam1[k * NP + i0 + r] = mu.L1r[r];
                 }
                 float fr[RI], fc[RJ];
-                step_flow(tb, basepoint && (t == 0), fr, fc);
+                const bool bp = basepoint && (t == 0);
+                step_flow(tb, bp, fr, fc);
                 const float steps_after = (float)(g.T - 1 - t);
                 float ecs[RJ];
 #pragma unroll
-                for (int cc = 0; cc < RJ; ++cc) ecs[cc] = expf(steps_after * tb.xc[cc]) * tb.q1c[cc] * dys[k * NP + j0 + cc];
+                for (int cc = 0; cc < RJ; ++cc)
+                    ecs[cc] = expf(steps_after * tb.xc[cc]) * (bp ? 1.f : tb.q1c[cc]) * dys[k * NP + j0 + cc];
 #pragma unroll
                 for (int r = 0; r < RI; ++r) {
                     const float er = expf(steps_after * tb.xr[r]);
                     float wr = 0.f;
 #pragma unroll
                     for (int cc = 0; cc < RJ; ++cc) wr = fmaf(er * tg2[r][cc], ecs[cc], wr);
-                    wr = row_sum(wr);
-                    mu.L1r[r] = fr[r] * (mu.L1r[r] + wr);
+                    wr = row_sum(wr) + mu.L1r[r];
+                    mu.L1r[r] = fmaf(-fr[r], wr, wr);
                 }
             }
         }
@@ -743,7 +766,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         load_elem(p.fagg + slot, Gc, NP, i0, j0);
         if (c == g.C - 1) {
             store_adj(p.incl + slot, mu, NP, i0, j0, tj);
-            publish(flag, kFlagIncl);
+            if (!(g.flags & EWS_F_TEST_WITHHOLD)) publish(flag, kFlagIncl);
         } else {
             store_adj(p.agg + slot, mu, NP, i0, j0, tj);
             publish(flag, kFlagAgg);
@@ -752,8 +775,9 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
             Elem<RI, RJ> Gacc;
             Gacc.identity();
             int j = c + 1;
+            const int want = (g.flags & EWS_F_DETERMINISTIC) ? kFlagIncl : kFlagAgg;
             for (;;) {
-                const int f = wait_slot(p.flags + (size_t)b * g.C + j, p.st, g.spin_limit, tile);
+                const int f = wait_slot(p.flags + (size_t)b * g.C + j, p.st, g.spin_limit, tile, want);
                 if (f < 0) return;
                 const size_t sj = ((size_t)b * g.C + j) * g.SW;
                 Adj<RI, RJ> X;
@@ -803,8 +827,9 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                     float S1p[RI], S2p[RI][RJ];
                     read_row<RI, RJ>(sst + (k - k0) * g.W, S1p, S2p, g.N, i0, j0);
                     float fr[RI], fc[RJ];
-                    step_flow(tb, basepoint && (t0 + k == 0), fr, fc);
-                    bwd_step(tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, i0, j0, ti, tj);
+                    const bool bp = basepoint && (t0 + k == 0);
+                    step_flow(tb, bp, fr, fc);
+                    bwd_step(tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, i0, j0, ti, tj, bp);
                 }
             }
         } else {
@@ -834,9 +859,10 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                     for (int cc = 0; cc < RJ; ++cc) S2p[r][cc] = S.S2[r][cc];
                 }
                 float fr[RI], fc[RJ];
-                step_flow(tb, basepoint && (t == 0), fr, fc);
-                bwd_step(tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, i0, j0, ti, tj);
-                chen_step(tb, dys + k * NP, i0, j0, S, fr, fc);
+                const bool bp = basepoint && (t == 0);
+                step_flow(tb, bp, fr, fc);
+                bwd_step(tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, i0, j0, ti, tj, bp);
+                chen_step(tb, dys + k * NP, i0, j0, S, fr, fc, bp);
             }
         }
         finish_chunk<RI, RJ>(p, liftS, dxs, dyg, gst, b, t0, len, tile, gr, i0, j0, ti, tj);
@@ -891,13 +917,33 @@ static int pick_chunk(int B, int T) {
     return Lc;
 }
 
+constexpr int kWarpFloatBudget = 4096;  // 16 KB of shared memory per warp
+
+static void carve(Geom* g) {
+    const int Lc = g->Lc, NP = g->NP;
+    const int SR = g->SR < Lc ? g->SR : Lc;
+    g->SR = SR;
+    g->lift_n = align4(NP * g->d_in);
+    const int xs = align4(Lc * g->d_in), ys = align4(Lc * NP);
+    g->f_dys = xs;
+    g->f_stage = xs + ys;
+    g->f_per_warp = xs + ys + align4(SR * g->W);
+    const bool terminal = g->readout == EWS_READOUT_TERMINAL;
+    const int gst_n = align4(std::max(terminal ? 0 : SR * g->W, Lc * g->d_in));
+    g->b_dys = xs;
+    g->b_dyg = xs + ys;
+    g->b_lam1 = xs + 2 * ys;
+    g->b_gst = g->b_lam1 + (terminal ? ys : 0);
+    g->b_sst = g->b_gst + gst_n;
+    g->b_per_warp = g->b_sst + (terminal ? 0 : align4(SR * g->W));
+}
+
 static int make_geom(const ews_diag_args* a, Geom* g) {
     if (!a || a->batch <= 0 || a->steps <= 0 || a->d_in <= 0 || a->dim <= 0) return EWS_ERR_INVALID_ARGUMENT;
     if (a->depth != 2) return EWS_ERR_UNSUPPORTED;
     if (a->dim > 32) return EWS_ERR_UNSUPPORTED;
     if (!(a->flags & EWS_F_UNIFORM)) return EWS_ERR_UNSUPPORTED;
     if (a->readout != EWS_READOUT_PREFIX && a->readout != EWS_READOUT_TERMINAL) return EWS_ERR_INVALID_ARGUMENT;
-    if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
     if ((a->flags & EWS_F_BF16) && !(a->flags & EWS_F_INCREMENTS)) return EWS_ERR_INVALID_ARGUMENT;
     g->B = a->batch;
     g->T = a->steps;
@@ -911,8 +957,14 @@ static int make_geom(const ews_diag_args* a, Geom* g) {
     g->readout = a->readout;
     g->flags = a->flags;
     g->spin_limit = a->spin_limit > 0 ? a->spin_limit : kDefaultSpinLimit;
-    g->SR = g->W >= 1024 ? 1 : (1024 + g->W - 1) / g->W;
-    if (g->SR > g->Lc) g->SR = g->Lc;
+    g->SR = g->W >= 512 ? 1 : (512 + g->W - 1) / g->W;
+    // shrink the chunk until the backward's per-warp buffers fit the budget (>= 3 CTAs of kWarps per SM)
+    for (;;) {
+        carve(g);
+        if (a->chunk > 0 || g->b_per_warp <= kWarpFloatBudget || g->Lc <= 8) break;
+        g->Lc = g->Lc > 16 ? g->Lc - 8 : 8;
+    }
+    g->C = (g->T + g->Lc - 1) / g->Lc;
     g->ntiles = g->B * g->C;
     return EWS_OK;
 }
@@ -959,16 +1011,9 @@ static WsLayout bwd_layout(const Geom& g) {
     return L;
 }
 
-static size_t fwd_smem(const Geom& g) {
-    const size_t per_warp = align4(g.Lc * g.d_in) + align4(g.Lc * g.NP) + align4(g.SR * g.W);
-    return sizeof(float) * (align4(g.NP * g.d_in) + kWarps * per_warp);
-}
+static size_t fwd_smem(const Geom& g) { return sizeof(float) * ((size_t)g.lift_n + (size_t)kWarps * g.f_per_warp); }
 
-static size_t bwd_smem(const Geom& g) {
-    const int stage_n = align4(std::max(g.SR * g.W, g.Lc * g.d_in));
-    const size_t per_warp = align4(g.Lc * g.d_in) + 3 * align4(g.Lc * g.NP) + 2 * stage_n;
-    return sizeof(float) * (align4(g.NP * g.d_in) + kWarps * per_warp);
-}
+static size_t bwd_smem(const Geom& g) { return sizeof(float) * ((size_t)g.lift_n + (size_t)kWarps * g.b_per_warp); }
 
 static int num_sms() {
     static int n = 0;
@@ -1029,6 +1074,7 @@ extern "C" int ews_diag_fwd(const ews_diag_args* a, ews_stream_t stream) {
     int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
     if (!a->path || !a->out || !a->tab_x || !a->tab_q1 || !a->tab_q2) return EWS_ERR_INVALID_ARGUMENT;
+    if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
     const WsLayout L = fwd_layout(g);
     if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
@@ -1063,6 +1109,7 @@ extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
     if (!a->path || !a->grad_out || !a->grad_dx || !a->grad_x || !a->grad_q1 || !a->grad_q2)
         return EWS_ERR_INVALID_ARGUMENT;
     if (g.readout == EWS_READOUT_PREFIX && !a->out) return EWS_ERR_INVALID_ARGUMENT;
+    if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
     const WsLayout F = fwd_layout(g);
     const WsLayout L = bwd_layout(g);
     if (!a->fwd_ws || a->fwd_ws_bytes < F.total) return EWS_ERR_WORKSPACE;

@@ -21,6 +21,18 @@ from .params import AParamConstant, B, block_sizes_of, is_diagonal
 COMBINE_KINDS = ("assoc", "lean", "block_kernel", "dense_kernel", "b200")
 LEAF_KINDS = ("van_loan", "series", "plane_closed", "block_series", "jordan_closed", "jordan_closed_tables")
 MODES = ("displacement", "displacement_uniform", "displacement_uniform_basepoint")
+
+_DETERMINISTIC = False
+
+
+def configure(deterministic: bool = False) -> None:
+    """Bit-reproducible engine results (the counterpart of the reference's XLA determinism switch,
+    ews/determinism.py:32-106): chunks then wait for their neighbour's inclusive carry instead of
+    folding in whatever aggregates are ready, which fixes the rounding of the carries."""
+    global _DETERMINISTIC
+    _DETERMINISTIC = bool(deterministic)
+
+
 READOUTS = ("terminal", "prefix", "mean", "max")
 
 
@@ -124,6 +136,8 @@ class EWS(nn.Module):
         x = -h[:, None] * lam[None, :]
         q1, q2 = series.diag_tables(x, self.series_q)
         flags = _lib.EWS_F_UNIFORM | (_lib.EWS_F_BASEPOINT if basepoint else 0)
+        if _DETERMINISTIC:
+            flags |= _lib.EWS_F_DETERMINISTIC
         if increments:
             flags |= _lib.EWS_F_INCREMENTS
             if path.dtype == torch.bfloat16:

@@ -48,6 +48,12 @@ typedef struct CUstream_st* ews_stream_t; /* = cudaStream_t */
 #define EWS_F_BF16 4u           /* `path` is bfloat16 (accumulation stays float32) */
 #define EWS_F_BASEPOINT 8u      /* uniform with basepoint: step 0 has the identity flow
                                    (ews/core/chen_scan.py:160-166) */
+#define EWS_F_DETERMINISTIC 16u /* bit-reproducible results: every chunk waits for its neighbour's inclusive
+                                   value instead of folding in whatever aggregates are ready (the grouping of
+                                   a decoupled look-back depends on timing, hence so does its rounding) */
+#define EWS_F_TEST_WITHHOLD 32u /* failure-detection test: the chunk every other chunk depends on never
+                                   publishes, so their bounded waits run out and the call reports
+                                   EWS_ERR_LOOKBACK_TIMEOUT through ews_read_device_status */
 
 #define EWS_READOUT_PREFIX 0    /* out: (B, T, 1 + D), row t = [1, S_1,t, ..., S_n,t] */
 #define EWS_READOUT_TERMINAL 1  /* out: (B, 1 + D), the last row only */

@@ -65,13 +65,15 @@ def test_workspace_query_and_argument_errors():
     assert lib.ews_diag_workspace_size(ctypes.byref(_args(dim=33)), ctypes.byref(fb), ctypes.byref(bb)) == 2
     assert lib.ews_diag_workspace_size(ctypes.byref(_args(depth=3)), ctypes.byref(fb), ctypes.byref(bb)) == 2
     assert lib.ews_diag_workspace_size(ctypes.byref(_args(readout=7)), ctypes.byref(fb), ctypes.byref(bb)) == 1
-    # identity lift needs d_in == dim; bf16 needs stored increments
-    assert lib.ews_diag_workspace_size(ctypes.byref(_args(d_in=4)), ctypes.byref(fb), ctypes.byref(bb)) == 1
+    # bf16 needs stored increments
     assert lib.ews_diag_workspace_size(ctypes.byref(_args(flags=_lib.EWS_F_UNIFORM | _lib.EWS_F_BF16)), ctypes.byref(fb), ctypes.byref(bb)) == 1
     # a launch with a missing workspace is refused before touching the device
     a = _args()
     a.path = a.out = a.tab_x = a.tab_q1 = a.tab_q2 = ctypes.c_void_p(16)
     assert lib.ews_diag_fwd(ctypes.byref(a), None) == 3
+    # the identity lift needs d_in == dim
+    a.d_in = 4
+    assert lib.ews_diag_fwd(ctypes.byref(a), None) == 1
 
 
 def test_diag_tables_match_the_series_leaf():
