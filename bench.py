@@ -31,7 +31,7 @@ sys.path.insert(0, ROOT)
 METRIC = "EWS fwd+bwd (batch·steps)/s at 1/2/4/8 B200, % HBM/TC roofline vs JAX CPU"
 UNIT = "batch·steps/s"
 L2_BYTES = 126 * 1024 * 1024
-KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 2}
+KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3}
 
 
 def _peaks():

@@ -869,9 +869,25 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     }
 }
 
-// Deterministic reduction of the per-tile partials: per sample over its chunks (tables), and over all
-// tiles (lift). One thread per output value, fixed summation order.
-__global__ void reduce_kernel(Params p, float* grad_x, float* grad_q1, float* grad_q2, float* grad_lift) {
+// Deterministic two-stage reduction of the per-tile partials (fixed summation orders, coalesced reads).
+// Stage 1: per sample, over its chunks -> sp (B, stride).
+__global__ void reduce_chunks_kernel(Params p, float* sp) {
+    const Geom& g = p.g;
+    const int NP = g.NP;
+    const int stride = 2 * NP + NP * NP + NP * g.d_in;
+    const size_t total = (size_t)g.B * stride;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const int b = (int)(e / stride), off = (int)(e - (size_t)b * stride);
+        float acc = 0.f;
+        for (int cr = 0; cr < g.C; ++cr) acc += p.partials[((size_t)cr * g.B + b) * stride + off];
+        sp[e] = acc;
+    }
+}
+
+// Stage 2: per-sample table gradients (compacted to the real dimension N) and the lift gradient summed
+// over the samples in order.
+__global__ void reduce_samples_kernel(Params p, const float* sp, float* grad_x, float* grad_q1, float* grad_q2,
+                                      float* grad_lift) {
     const Geom& g = p.g;
     const int NP = g.NP, N = g.N;
     const int stride = 2 * NP + NP * NP + NP * g.d_in;
@@ -880,26 +896,19 @@ __global__ void reduce_kernel(Params p, float* grad_x, float* grad_q1, float* gr
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
         if (e < g.B * per_sample) {
             const int b = e / per_sample, r = e - b * per_sample;
-            int off;
-            float* dst;
+            const float* row = sp + (size_t)b * stride;
             if (r < N) {
-                off = r;
-                dst = grad_x + (size_t)b * N + r;
+                grad_x[(size_t)b * N + r] = row[r];
             } else if (r < 2 * N) {
-                off = NP + (r - N);
-                dst = grad_q1 + (size_t)b * N + (r - N);
+                grad_q1[(size_t)b * N + (r - N)] = row[NP + (r - N)];
             } else {
                 const int q = r - 2 * N, i = q / N, j = q - i * N;
-                off = 2 * NP + i * NP + j;
-                dst = grad_q2 + (size_t)b * N * N + q;
+                grad_q2[(size_t)b * N * N + q] = row[2 * NP + i * NP + j];
             }
-            float acc = 0.f;
-            for (int c = 0; c < g.C; ++c) acc += p.partials[(size_t)(c * g.B + b) * stride + off];
-            *dst = acc;
         } else {
-            const int q = e - g.B * per_sample, i = q / g.d_in, cc = q - i * g.d_in;
+            const int q = e - g.B * per_sample;
             float acc = 0.f;
-            for (int t = 0; t < g.ntiles; ++t) acc += p.partials[(size_t)t * stride + 2 * NP + NP * NP + i * g.d_in + cc];
+            for (int b = 0; b < g.B; ++b) acc += sp[(size_t)b * stride + 2 * NP + NP * NP + q];
             grad_lift[q] = acc;
         }
     }
@@ -972,7 +981,7 @@ static int make_geom(const ews_diag_args* a, Geom* g) {
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 struct WsLayout {
-    size_t status, flags, agg, incl, carry, partials, total;
+    size_t status, flags, agg, incl, carry, partials, sample_partials, total;
 };
 
 static WsLayout fwd_layout(const Geom& g) {
@@ -1005,8 +1014,11 @@ static WsLayout bwd_layout(const Geom& g) {
     o += slots;
     L.incl = o;
     o += slots;
+    const size_t stride = 2 * g.NP + g.NP * g.NP + g.NP * g.d_in;
     L.partials = o;
-    o += al256(sizeof(float) * (size_t)g.ntiles * (2 * g.NP + g.NP * g.NP + g.NP * g.d_in));
+    o += al256(sizeof(float) * (size_t)g.ntiles * stride);
+    L.sample_partials = o;
+    o += al256(sizeof(float) * (size_t)g.B * stride);
     L.total = o;
     return L;
 }
@@ -1143,9 +1155,12 @@ extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
         default: rc = EWS_ERR_UNSUPPORTED;
     }
     if (rc != EWS_OK) return rc;
-    const int total = g.B * (2 * g.N + g.N * g.N) + (a->grad_lift ? g.N * g.d_in : 0);
+    float* sp = (float*)(ws + L.sample_partials);
+    const size_t n1 = (size_t)g.B * (2 * g.NP + g.NP * g.NP + g.NP * g.d_in);
     const int threads = 256;
-    const int blocks = (total + threads - 1) / threads;
-    reduce_kernel<<<blocks, threads, 0, s>>>(p, a->grad_x, a->grad_q1, a->grad_q2, a->grad_lift);
+    reduce_chunks_kernel<<<(int)std::min<size_t>((n1 + threads - 1) / threads, 65535), threads, 0, s>>>(p, sp);
+    const int total = g.B * (2 * g.N + g.N * g.N) + (a->grad_lift ? g.N * g.d_in : 0);
+    reduce_samples_kernel<<<(total + threads - 1) / threads, threads, 0, s>>>(p, sp, a->grad_x, a->grad_q1, a->grad_q2,
+                                                                            a->grad_lift);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
