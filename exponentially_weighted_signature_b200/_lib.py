@@ -14,7 +14,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libews_b200.so")
 
 EWS_OK = 0
+EWS_ERR_WORKSPACE = 3
 EWS_ERR_LOOKBACK_TIMEOUT = 5
+EWS_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 EWS_F_UNIFORM = 1
 EWS_F_INCREMENTS = 2
@@ -30,6 +32,7 @@ EXPORTED = (
     "ews_diag_workspace_size",
     "ews_diag_fwd",
     "ews_diag_bwd",
+    "ews_diag_fwd_noalloc",
     "ews_read_device_status",
     "ews_error_string",
     "ews_version",
@@ -98,7 +101,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.POINTER(DiagArgs), ctypes.POINTER(_c_size), ctypes.POINTER(_c_size)]
             fn.restype = _c_int
-        for name in ("ews_diag_fwd", "ews_diag_bwd"):
+        for name in ("ews_diag_fwd", "ews_diag_bwd", "ews_diag_fwd_noalloc"):
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.POINTER(DiagArgs), _vp]
             fn.restype = _c_int

@@ -27,6 +27,7 @@
 // terminal readouts use the closed form lambda2_t = e^{(T-1-t)(x_i+x_j)} g2 and recompute S forward.
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "ews_common.cuh"
 
@@ -1163,4 +1164,52 @@ extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
     reduce_samples_kernel<<<(total + threads - 1) / threads, threads, 0, s>>>(p, sp, a->grad_x, a->grad_q1, a->grad_q2,
                                                                             a->grad_lift);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+// ---------------------------------------------------------------------------------------------------
+// Forward without a caller-provided workspace (see ews_diag_fwd_noalloc in include/ews_b200.h).
+//
+// Some callers cannot allocate device memory for us: a plugin host that hands a kernel only its input
+// and output buffers, or a serving loop that forbids cudaMalloc on its hot path because an allocation
+// can synchronise the device. For them the forward's look-back workspace lives in this file-scope
+// device array instead, EWS_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the library until
+// the process exits. In host code the array's name is only a host-side stand-in, so its device address
+// is looked up once per device with cudaGetSymbolAddress (with that device current) and cached.
+namespace {
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[EWS_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return EWS_ERR_LAUNCH;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_addr[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return EWS_ERR_LAUNCH;
+        g_noalloc_addr[dev] = ptr;
+    }
+    *out = g_noalloc_addr[dev];
+    return EWS_OK;
+}
+
+}  // namespace
+
+extern "C" int ews_diag_fwd_noalloc(const ews_diag_args* a, ews_stream_t stream) {
+    Geom g;
+    const int rc = make_geom(a, &g);
+    if (rc != EWS_OK) return rc;
+    if (fwd_layout(g).total > (size_t)EWS_NOALLOC_SCRATCH_BYTES) return EWS_ERR_WORKSPACE;
+    void* scratch = nullptr;
+    const int sc = noalloc_scratch(&scratch);
+    if (sc != EWS_OK) return sc;
+    ews_diag_args b = *a;
+    b.fwd_ws = scratch;
+    b.fwd_ws_bytes = EWS_NOALLOC_SCRATCH_BYTES;
+    // ews_diag_fwd clears the status block and flags it needs zeroed before its kernel runs, allocates
+    // nothing, and leaves the aggregates and carries in the array until the next call overwrites them.
+    return ews_diag_fwd(&b, stream);
 }

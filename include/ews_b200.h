@@ -108,6 +108,22 @@ int ews_diag_workspace_size(const ews_diag_args* a, size_t* fwd_bytes, size_t* b
 int ews_diag_fwd(const ews_diag_args* a, ews_stream_t stream);
 int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream);
 
+/* Forward that allocates nothing and needs no workspace from the caller. This entry point has no
+ * counterpart in the reference. It is for callers that cannot allocate device memory for the library:
+ * a plugin host that passes a kernel only its inputs and outputs, or a serving loop that forbids
+ * cudaMalloc because an allocation can synchronise the device. Same arguments and results as
+ * ews_diag_fwd, except that fwd_ws / fwd_ws_bytes are ignored: the look-back workspace is a file-scope
+ * device array of EWS_NOALLOC_SCRATCH_BYTES (16 MiB) that every GPU loading the library holds until the
+ * process exits. Problems whose forward workspace (ews_diag_workspace_size) exceeds that return
+ * EWS_ERR_WORKSPACE before anything runs. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress, with that device current); make that first call before any stream
+ * capture. Every call shares the one array and it keeps the last call's contents (the call clears what
+ * must start at zero), so calls whose executions overlap on the GPU race on it: serialise them, e.g. on
+ * one stream. Because the array is reused, a backward (ews_diag_bwd) cannot consume this forward's
+ * workspace; use ews_diag_fwd when gradients are needed. */
+#define EWS_NOALLOC_SCRATCH_BYTES (16u << 20)
+int ews_diag_fwd_noalloc(const ews_diag_args* a, ews_stream_t stream);
+
 /* ---- utilities --------------------------------------------------------------------------------- */
 /* Copies the device-side status word of a workspace (EWS_OK or EWS_ERR_LOOKBACK_TIMEOUT) to the host;
  * synchronises the stream. */
