@@ -31,7 +31,7 @@ sys.path.insert(0, ROOT)
 METRIC = "EWS fwd+bwd (batch·steps)/s at 1/2/4/8 B200, % HBM/TC roofline vs JAX CPU"
 UNIT = "batch·steps/s"
 L2_BYTES = 126 * 1024 * 1024
-KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3}
+KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 1, "ews_dense_bwd": 2}
 
 
 def _peaks():
@@ -108,6 +108,48 @@ def _diag_setup(cfg, rank, world, device, precision, batch=None):
                 ws_bytes=ws_bytes, units=Bl * T, case=case)
 
 
+def _dense_setup(cfg, rank, world, device, precision, batch=None):
+    """Per-rank inputs and model of the dense-A configuration (config2)."""
+    from exponentially_weighted_signature_b200 import EWS, AParamGeneral, B as Lift, workloads, series
+    from exponentially_weighted_signature_b200.parallel import shard_range
+
+    case = getattr(workloads, cfg)(**({"B": batch} if batch else {}))
+    Bg, T, N = case["B"], case["T"], case["N"]
+    if Bg % world == 0:
+        s0, s1 = shard_range(Bg, rank, world)
+        scaling = "strong"
+    else:
+        s0, s1 = 0, Bg
+        scaling = "weak"
+    x_max = float(np.linalg.norm(case["A"], 2)) / T
+    q = max(2, series.suggest_series_q(x_max, 2, 1e-14))
+    A = AParamGeneral(torch.tensor(case["A"], dtype=torch.float32))
+    lift = Lift(torch.tensor(case["lift"], dtype=torch.float32), preserve_first_channel=False)
+    layer = EWS(A, N=2, reweighting_mode="displacement_uniform", series_q=q).to(device)
+    lift = lift.to(device)
+    x_host = torch.tensor(case["path"][s0:s1], dtype=torch.float32)
+    clock_host = torch.tensor(case["clock"][s0:s1], dtype=torch.float32)
+    params = list(layer.parameters()) + list(lift.parameters())
+    Bl = s1 - s0
+    D = N + N * N
+    g = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    w = torch.randn((Bl, T, 1 + D), generator=g).to(device)
+
+    def step(x, clock):
+        out = layer(x, clock, readout="prefix", lift=lift.full_matrix())
+        loss = (out * w).sum()
+        loss.backward()
+        return loss
+
+    d_in = x_host.shape[-1]
+    out_row = 4 * (1 + D)
+    alg = {"ews_dense_fwd": 4 * d_in + out_row, "ews_dense_bwd": 4 * d_in + out_row + 4 * d_in}
+    meta = dict(B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout="prefix", dtype="f32", precision="f32")
+    ws_bytes = x_host.numel() * 4 + Bl * T * out_row
+    return dict(step=step, params=params, x_host=x_host, clock_host=clock_host, alg=alg, meta=meta,
+                ws_bytes=ws_bytes, units=Bl * T, case=case)
+
+
 # ------------------------------------------------------------------------------------ helpers
 
 
@@ -178,9 +220,16 @@ def _cpu_baseline(cfg, precision, budget_s=20.0):
     torch.set_num_threads(threads)
     case = getattr(workloads, cfg)(B=1)
     T = case["T"]
-    lam = torch.tensor(case["lam"], dtype=torch.float32)
+    if "lam" in case:
+        gen = torch.tensor(case["lam"], dtype=torch.float32)
+        to_matrix = torch.diag
+        x_max = float(case["lam"].max()) / T
+    else:
+        gen = torch.tensor(case["A"], dtype=torch.float32)
+        to_matrix = lambda m: m
+        x_max = float(np.linalg.norm(case["A"], 2)) / T
     lift = torch.tensor(case["lift"], dtype=torch.float32)
-    q = max(2, series.suggest_series_q(float(case["lam"].max()) / T, 2, 1e-14))
+    q = max(2, series.suggest_series_q(x_max, 2, 1e-14))
     if cfg == "config5":
         inc = torch.tensor(case["increments"][:1], dtype=torch.float32)
         path = torch.cat([torch.zeros(1, 1, inc.shape[-1]), torch.cumsum(inc, 1)], 1)
@@ -192,14 +241,14 @@ def _cpu_baseline(cfg, precision, budget_s=20.0):
     done_units, spent, runs = 0, 0.0, 0
     while spent < budget_s and runs < 50:
         p = path[:, : Ts + 1].clone().requires_grad_(True)
-        A = lam.clone().requires_grad_(True)
+        A = gen.clone().requires_grad_(True)
         Bm = lift.clone().requires_grad_(True)
         t0 = time.perf_counter()
         y = O.lift(p, Bm)
         if cfg == "config5":
-            out = O.log_ews_layer(y, clock[:, : Ts + 1], torch.diag(A), 2, series_q=q, reweighting_mode="displacement_uniform", readout="terminal", terminal_reduce="assoc")
+            out = O.log_ews_layer(y, clock[:, : Ts + 1], to_matrix(A), 2, series_q=q, reweighting_mode="displacement_uniform", readout="terminal", terminal_reduce="assoc")
         else:
-            out = O.ews_layer(y, clock[:, : Ts + 1], torch.diag(A), 2, series_q=q, reweighting_mode="displacement_uniform", readout="prefix")
+            out = O.ews_layer(y, clock[:, : Ts + 1], to_matrix(A), 2, series_q=q, reweighting_mode="displacement_uniform", readout="prefix")
         out.sum().backward()
         dt = time.perf_counter() - t0
         spent += dt
@@ -220,7 +269,8 @@ def run_b200(args, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    setup = _diag_setup(args.config, rank, world, device, args.precision, args.batch)
+    setup_fn = _dense_setup if args.config == "config2" else _diag_setup
+    setup = setup_fn(args.config, rank, world, device, args.precision, args.batch)
     step, params = setup["step"], setup["params"]
     x = setup["x_host"].to(device)
     clock = setup["clock_host"].to(device)
@@ -410,7 +460,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="config5", choices=["config1", "config5"])
+    ap.add_argument("--config", default="config5", choices=["config1", "config2", "config5"])
     ap.add_argument("--precision", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling on a smaller case)")

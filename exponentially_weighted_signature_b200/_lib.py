@@ -33,6 +33,9 @@ EXPORTED = (
     "ews_diag_fwd",
     "ews_diag_bwd",
     "ews_diag_fwd_noalloc",
+    "ews_dense_workspace_size",
+    "ews_dense_fwd",
+    "ews_dense_bwd",
     "ews_read_device_status",
     "ews_error_string",
     "ews_version",
@@ -77,6 +80,39 @@ class DiagArgs(ctypes.Structure):
     ]
 
 
+class DenseArgs(ctypes.Structure):
+    """Mirror of ``ews_dense_args``."""
+
+    _fields_ = [
+        ("batch", _c_int),
+        ("steps", _c_int),
+        ("d_in", _c_int),
+        ("dim", _c_int),
+        ("depth", _c_int),
+        ("chunk", _c_int),
+        ("readout", _c_int),
+        ("flags", ctypes.c_uint),
+        ("series_q", _c_int),
+        ("spin_limit", _c_int),
+        ("path", _vp),
+        ("tab_m", _vp),
+        ("tab_f", _vp),
+        ("tab_g", _vp),
+        ("tab_h", _vp),
+        ("out", _vp),
+        ("grad_out", _vp),
+        ("grad_dx", _vp),
+        ("grad_m", _vp),
+        ("grad_f", _vp),
+        ("grad_g", _vp),
+        ("grad_h", _vp),
+        ("fwd_ws", _vp),
+        ("fwd_ws_bytes", _c_size),
+        ("bwd_ws", _vp),
+        ("bwd_ws_bytes", _c_size),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -104,6 +140,12 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         for name in ("ews_diag_fwd", "ews_diag_bwd", "ews_diag_fwd_noalloc"):
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.POINTER(DiagArgs), _vp]
+            fn.restype = _c_int
+        lib.ews_dense_workspace_size.argtypes = [ctypes.POINTER(DenseArgs), ctypes.POINTER(_c_size), ctypes.POINTER(_c_size)]
+        lib.ews_dense_workspace_size.restype = _c_int
+        for name in ("ews_dense_fwd", "ews_dense_bwd"):
+            fn = getattr(lib, name)
+            fn.argtypes = [ctypes.POINTER(DenseArgs), _vp]
             fn.restype = _c_int
         lib.ews_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(_c_int)]
         lib.ews_read_device_status.restype = _c_int

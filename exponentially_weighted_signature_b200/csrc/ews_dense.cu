@@ -1,0 +1,1007 @@
+// Dense-A engine of the EWS hot path (any generator A, uniform clock), depth 2, N <= 32, fp32.
+//
+// Per interval t of sample b, with the flow M = exp(-h A) and the increment dx_t (before the lift):
+//     S1' = u + s1,                      u  = M S1,   s1 = F dx
+//     S2' = M S2 M^T + u s1^T + U V^T,   U = [G_a dx]_a,  V = [H_a dx]_a   (a = 0..q)
+// This is the modified-Chen recursion of ews/core/chen_scan.py:124-152 (sequentially:
+// ews/core/kernels/pallas_combine.py:1804-1834) with the series leaf of ews/core/series_leaf.py:72-113:
+// for a uniform clock the letters are b_a = P_a dy with P_a = (-hA)^a / a!, so
+// s1 = sum_p c_p P_p dy = K1 dy and s2 = sum_a (P_a dy)(K2_a dy)^T with K2_a = sum_b c_ab P_b; the lift W
+// is folded into F = K1 W, G_a = P_a W, H_a = K2_a W by the caller.
+//
+// Work decomposition: one CTA of 64 threads owns one tile (sample, chunk). Thread (bi, bj) holds the 4x4
+// block (rows 4bi.., cols 4bj..) of every 32x32 matrix; a 32x32x32 product reads two float4 operands per k
+// from shared memory (A k-major, B row-major) into 16 FMAs. Chunks are combined with the decoupled
+// look-back of the diagonal engine (chunk aggregates (M^L, S1, S2), Chen products by GEMMs).
+#include <algorithm>
+#include <cstdio>
+
+#include "ews_common.cuh"
+
+namespace ews {
+namespace dense {
+
+constexpr int NP = 32;   // padded state dimension
+constexpr int NT = 64;   // threads per tile
+constexpr int MM = NP * NP;
+constexpr int QMAX = 12; // series order q <= 11
+
+struct Geom {
+    int B, T, d_in, N, Lc, C, W, SW, QP, readout;
+    unsigned flags;
+    int spin_limit;
+    int SR, ntiles;
+    int tab_n;        // floats of the F, G, H tables (N x d_in each, padded to NP rows)
+    int smem_floats;  // forward
+    int bsmem_floats; // backward
+};
+
+struct Params {
+    Geom g;
+    const void* path;
+    const float* tab_m;  // (B, N, N)
+    const float* tab_f;  // (B, N, d_in)
+    const float* tab_g;  // (B, QP, N, d_in)
+    const float* tab_h;  // (B, QP, N, d_in)
+    float* out;
+    const float* grad_out;
+    float* grad_dx;
+    float* partials;  // per tile: dM (NP*NP) | dF (NP*d_in) | dG (QP*NP*d_in) | dH (QP*NP*d_in)
+    DeviceStatus* st;
+    int* flags;
+    float* agg;
+    float* incl;
+    float* carry;
+    const float* fagg;
+};
+
+__host__ __device__ inline int align4(int n) { return (n + 3) & ~3; }
+__host__ __device__ inline int imax(int a, int b) { return a > b ? a : b; }
+
+// ---------------------------------------------------------------------------------- 4x4 block GEMM
+
+// acc (+)= A B for the thread's 4x4 block: At is A stored k-major (At[k*32+i] = A[i][k]), Bm row-major.
+__device__ __forceinline__ void gemm44(const float* __restrict__ At, const float* __restrict__ Bm, float acc[4][4],
+                                       int i0, int j0, bool accumulate) {
+    if (!accumulate) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[r][c] = 0.f;
+    }
+#pragma unroll 8
+    for (int k = 0; k < NP; ++k) {
+        const float4 a = *reinterpret_cast<const float4*>(At + k * NP + i0);
+        const float4 b = *reinterpret_cast<const float4*>(Bm + k * NP + j0);
+        const float av[4] = {a.x, a.y, a.z, a.w};
+        const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(av[r], bv[c], acc[r][c]);
+    }
+}
+
+__device__ __forceinline__ void store_rowmajor(float* M, const float blk[4][4], int i0, int j0) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+        *reinterpret_cast<float4*>(M + (i0 + r) * NP + j0) = make_float4(blk[r][0], blk[r][1], blk[r][2], blk[r][3]);
+}
+
+__device__ __forceinline__ void store_kmajor(float* Mt, const float blk[4][4], int i0, int j0) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<float4*>(Mt + (j0 + c) * NP + i0) = make_float4(blk[0][c], blk[1][c], blk[2][c], blk[3][c]);
+}
+
+__device__ __forceinline__ void load_rowmajor(const float* M, float blk[4][4], int i0, int j0) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const float4 v = *reinterpret_cast<const float4*>(M + (i0 + r) * NP + j0);
+        blk[r][0] = v.x;
+        blk[r][1] = v.y;
+        blk[r][2] = v.z;
+        blk[r][3] = v.w;
+    }
+}
+
+// ---------------------------------------------------------------------------------- shared memory
+
+struct Smem {
+    float* Mr;   // M row-major
+    float* Mt;   // M k-major
+    float* A0;   // work matrices
+    float* A1;
+    float* A2;
+    float* A3;
+    float* A4;
+    float* A5;
+    float* S1;   // level 1 (NP)
+    float* u;    // M S1 (NP)
+    float* s1;   // local level 1 (NP)
+    float* v0;   // scratch vectors (NP each)
+    float* v1;
+    float* U;    // NP x QP (row-major, stride QMAX)
+    float* V;
+    float* F;    // NP x d_in
+    float* G;    // QP x NP x d_in
+    float* H;
+    float* dx;   // Lc x d_in
+    float* stage;
+    float* stage2;
+    float* red;  // backward: [du (NP) | dU (NP*QMAX) | ds1 (NP) | dV (NP*QMAX)]
+    float* tacc; // backward: table-gradient accumulators of the tile ((1+2QP) NP d_in)
+    float* ddx;  // backward: dx gradient rows of the chunk (Lc x d_in)
+    int* bcast;
+};
+
+__device__ Smem carve(float* base, const Geom& g, bool bwd) {
+    Smem s;
+    float* p = base;
+    s.Mr = p; p += MM;
+    s.Mt = p; p += MM;
+    s.A0 = p; p += MM;
+    s.A1 = p; p += MM;
+    s.A2 = p; p += MM;
+    s.A3 = p; p += MM;
+    s.A4 = p; p += MM;
+    s.A5 = p; p += MM;
+    s.S1 = p; p += NP;
+    s.u = p; p += NP;
+    s.s1 = p; p += NP;
+    s.v0 = p; p += NP;
+    s.v1 = p; p += NP;
+    s.U = p; p += NP * QMAX;
+    s.V = p; p += NP * QMAX;
+    s.F = p; p += align4(NP * g.d_in);
+    s.G = p; p += align4(g.QP * NP * g.d_in);
+    s.H = p; p += align4(g.QP * NP * g.d_in);
+    s.dx = p; p += align4(g.Lc * g.d_in);
+    const int st_n = align4(imax(imax(g.SR * g.W, g.Lc * g.d_in), 2 * MM));
+    s.stage = p; p += st_n;
+    s.stage2 = p; p += bwd ? align4(g.SR * g.W) : 0;
+    s.red = p; p += bwd ? 2 * NP * (QMAX + 1) : 0;
+    s.tacc = p; p += bwd ? align4((1 + 2 * g.QP) * NP * g.d_in) : 0;
+    s.ddx = p; p += bwd ? align4(g.Lc * g.d_in) : 0;
+    s.bcast = reinterpret_cast<int*>(p);
+    return s;
+}
+
+__host__ int smem_floats(const Geom& g, bool bwd) {
+    int n = 8 * MM + 5 * NP + 2 * NP * QMAX + align4(NP * g.d_in) + 2 * align4(g.QP * NP * g.d_in) +
+            align4(g.Lc * g.d_in) + align4(imax(imax(g.SR * g.W, g.Lc * g.d_in), 2 * MM));
+    if (bwd)
+        n += align4(g.SR * g.W) + 2 * NP * (QMAX + 1) + align4((1 + 2 * g.QP) * NP * g.d_in) + align4(g.Lc * g.d_in);
+    return n + 4;
+}
+
+// Loads the per-sample tables (M padded with the identity, F/G/H padded with zero rows).
+__device__ void load_tables(const Params& p, const Smem& s, int b) {
+    const Geom& g = p.g;
+    const int N = g.N, d = g.d_in;
+    const float* m = p.tab_m + (size_t)b * N * N;
+    for (int e = threadIdx.x; e < MM; e += NT) {
+        const int i = e / NP, k = e - i * NP;
+        const float v = (i < N && k < N) ? m[i * N + k] : (i == k ? 1.f : 0.f);
+        s.Mr[i * NP + k] = v;
+        s.Mt[k * NP + i] = v;
+    }
+    const float* f = p.tab_f + (size_t)b * N * d;
+    for (int e = threadIdx.x; e < NP * d; e += NT) {
+        const int i = e / d;
+        s.F[e] = i < N ? f[e - i * d + i * d] : 0.f;
+    }
+    const size_t gq = (size_t)g.QP * N * d;
+    const float* gg = p.tab_g + (size_t)b * gq;
+    const float* hh = p.tab_h + (size_t)b * gq;
+    for (int e = threadIdx.x; e < g.QP * NP * d; e += NT) {
+        const int a = e / (NP * d), r = e - a * NP * d, i = r / d, c = r - i * d;
+        const bool ok = i < N;
+        s.G[e] = ok ? gg[((size_t)a * N + i) * d + c] : 0.f;
+        s.H[e] = ok ? hh[((size_t)a * N + i) * d + c] : 0.f;
+    }
+}
+
+__device__ void load_dx(const Params& p, const Smem& s, int b, int t0, int n) {
+    const Geom& g = p.g;
+    for (int e = threadIdx.x; e < n * g.d_in; e += NT) {
+        const int k = e / g.d_in, c = e - k * g.d_in;
+        s.dx[e] = input_increment(p.path, b, t0 + k, c, g.T, g.d_in, g.flags);
+    }
+}
+
+// Local vectors of step k: s1 = F dx, U = [G_a dx], V = [H_a dx]; and u = M S1 (from s.S1).
+__device__ void local_terms(const Geom& g, const Smem& s, int k) {
+    const float* x = s.dx + k * g.d_in;
+    const int tid = threadIdx.x;
+    // thread i < 32: s1_i and u_i; threads handle U/V entries round robin
+    if (tid < NP) {
+        float acc = 0.f;
+        for (int c = 0; c < g.d_in; ++c) acc = fmaf(s.F[tid * g.d_in + c], x[c], acc);
+        s.s1[tid] = acc;
+    } else {
+        const int i = tid - NP;
+        float acc = 0.f;
+#pragma unroll 8
+        for (int kk = 0; kk < NP; ++kk) acc = fmaf(s.Mt[kk * NP + i], s.S1[kk], acc);
+        s.u[i] = acc;
+    }
+    for (int e = tid; e < 2 * g.QP * NP; e += NT) {
+        const int which = e / (g.QP * NP), r = e - which * g.QP * NP, a = r / NP, i = r - a * NP;
+        const float* T = (which == 0 ? s.G : s.H) + ((size_t)a * NP + i) * g.d_in;
+        float acc = 0.f;
+        for (int c = 0; c < g.d_in; ++c) acc = fmaf(T[c], x[c], acc);
+        (which == 0 ? s.U : s.V)[i * QMAX + a] = acc;
+    }
+}
+
+// One forward step on the thread's block: S2 (regs, also s.A0 k-major) <- M S2 M^T + u s1^T + U V^T.
+// Uses s.A1 for X = S2 M^T. Three barriers.
+__device__ void fwd_step(const Geom& g, const Smem& s, int k, float S2[4][4], int i0, int j0) {
+    local_terms(g, s, k);
+    __syncthreads();
+    float X[4][4];
+    gemm44(s.A0, s.Mt, X, i0, j0, false);  // X = S2 M^T   (A = S2 k-major, B[k][j] = M[j][k])
+    store_rowmajor(s.A1, X, i0, j0);
+    __syncthreads();
+    gemm44(s.Mt, s.A1, S2, i0, j0, false);  // M X         (A = M k-major, B = X row-major)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const float ur = s.u[i0 + r];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            float acc = fmaf(ur, s.s1[j0 + c], S2[r][c]);
+            for (int a = 0; a < g.QP; ++a) acc = fmaf(s.U[(i0 + r) * QMAX + a], s.V[(j0 + c) * QMAX + a], acc);
+            S2[r][c] = acc;
+        }
+    }
+    if (threadIdx.x < NP) s.S1[threadIdx.x] = s.u[threadIdx.x] + s.s1[threadIdx.x];
+    store_kmajor(s.A0, S2, i0, j0);
+    __syncthreads();
+}
+
+// Writes row [1, S1, S2] (real dimension N) into a staged row.
+__device__ void stage_row(const Geom& g, const Smem& s, float* row, const float S2[4][4], int i0, int j0) {
+    const int N = g.N;
+    if (threadIdx.x == 0) row[0] = 1.f;
+    if (threadIdx.x < N) row[1 + threadIdx.x] = s.S1[threadIdx.x];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int i = i0 + r;
+        if (i >= N) continue;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int j = j0 + c;
+            if (j < N) row[1 + N + i * N + j] = S2[r][c];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------- Chen elements
+// Slot layout (floats): [P row-major (NP*NP) | S1 (NP) | S2 row-major (NP*NP)].
+
+__device__ void store_slot(float* slot, const float* Pr, const float* S1, const float* S2r) {
+    for (int e = threadIdx.x; e < MM; e += NT) {
+        slot[e] = Pr[e];
+        slot[MM + NP + e] = S2r[e];
+    }
+    if (threadIdx.x < NP) slot[MM + threadIdx.x] = S1[threadIdx.x];
+}
+
+// out = L (x) R with L, R given as (P row-major, S1, S2 row-major) in shared memory; result written to
+// (Po, S1o, S2o) row-major. Needs two scratch matrices T0, T1. Barrier-complete on return.
+__device__ void chen_mul_smem(const float* PL, const float* L1, const float* L2, const float* PR, const float* R1,
+                              const float* R2, float* Po, float* S1o, float* S2o, float* T0, float* T1, float* vtmp,
+                              int i0, int j0) {
+    // T0 = PR^T (k-major of PR), T1 = L2^T... we need: S2 = PR L2 PR^T + (PR L1) R1^T + R2
+    //   X = L2 PR^T: A = L2 (k-major = L2^T), B[k][j] = PR[j][k] (= PR^T row-major)
+    for (int e = threadIdx.x; e < MM; e += NT) {
+        const int i = e / NP, k = e - i * NP;
+        T0[k * NP + i] = L2[e];   // L2 k-major
+        T1[k * NP + i] = PR[e];   // PR k-major = PR^T row-major
+    }
+    if (threadIdx.x < NP) {
+        float acc = 0.f;
+        for (int k = 0; k < NP; ++k) acc = fmaf(PR[threadIdx.x * NP + k], L1[k], acc);
+        vtmp[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    float X[4][4], Y[4][4], P[4][4];
+    gemm44(T0, T1, X, i0, j0, false);  // X = L2 PR^T
+    gemm44(T1, PL, P, i0, j0, false);  // P = PR PL     (A = PR k-major, B = PL row-major)
+    __syncthreads();
+    store_rowmajor(T0, X, i0, j0);
+    __syncthreads();
+    gemm44(T1, T0, Y, i0, j0, false);  // Y = PR X
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            Y[r][c] += fmaf(vtmp[i0 + r], R1[j0 + c], R2[(i0 + r) * NP + j0 + c]);
+    __syncthreads();
+    store_rowmajor(S2o, Y, i0, j0);
+    store_rowmajor(Po, P, i0, j0);
+    if (threadIdx.x < NP) S1o[threadIdx.x] = vtmp[threadIdx.x] + R1[threadIdx.x];
+    __syncthreads();
+}
+
+__device__ void load_slot_smem(const float* slot, float* P, float* S1, float* S2) {
+    for (int e = threadIdx.x; e < MM; e += NT) {
+        P[e] = ldcg(slot + e);
+        S2[e] = ldcg(slot + MM + NP + e);
+    }
+    if (threadIdx.x < NP) S1[threadIdx.x] = ldcg(slot + MM + threadIdx.x);
+}
+
+__device__ void identity_smem(float* P, float* S1, float* S2) {
+    for (int e = threadIdx.x; e < MM; e += NT) {
+        const int i = e / NP, k = e - i * NP;
+        P[e] = i == k ? 1.f : 0.f;
+        S2[e] = 0.f;
+    }
+    if (threadIdx.x < NP) S1[threadIdx.x] = 0.f;
+}
+
+// CTA-wide ticket and bounded flag wait (thread 0 polls; the warp-level helpers act on warp 0).
+__device__ int cta_ticket(const Params& p, const Smem& s) {
+    if (threadIdx.x == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
+    __syncthreads();
+    const int t = s.bcast[0];
+    __syncthreads();
+    return t;
+}
+
+__device__ int cta_wait(const Params& p, const Smem& s, const int* flag, int want, int tile) {
+    if (threadIdx.x < 32) {
+        const int v = wait_slot(flag, p.st, p.g.spin_limit, tile, want);
+        if (threadIdx.x == 0) s.bcast[0] = v;
+    }
+    __syncthreads();
+    const int v = s.bcast[0];
+    __threadfence();
+    __syncthreads();
+    return v;
+}
+
+__device__ void cta_publish(int* flag, int value) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) st_release(flag, value);
+}
+
+// ---------------------------------------------------------------------------------- forward kernel
+
+__global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
+    extern __shared__ float smem[];
+    const Geom& g = p.g;
+    Smem s = carve(smem, g, false);
+    const int bi = threadIdx.x >> 3, bj = threadIdx.x & 7;
+    const int i0 = 4 * bi, j0 = 4 * bj;
+    const bool deterministic = (g.flags & EWS_F_DETERMINISTIC) != 0;
+    for (;;) {
+        const int tile = cta_ticket(p, s);
+        if (tile >= g.ntiles) break;
+        const int c = tile / g.B, b = tile - c * g.B;
+        const int t0 = c * g.Lc;
+        const int len = min(g.Lc, g.T - t0);
+        load_tables(p, s, b);
+        load_dx(p, s, b, t0, len);
+        // pass 1: aggregate from the identity (state S2 in regs + s.A0 k-major, S1 in s.S1)
+        float S2[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) S2[r][q] = 0.f;
+        store_kmajor(s.A0, S2, i0, j0);
+        if (threadIdx.x < NP) s.S1[threadIdx.x] = 0.f;
+        __syncthreads();
+        for (int k = 0; k < len; ++k) fwd_step(g, s, k, S2, i0, j0);
+        // aggregate (P = M^len by binary powering, S1, S2) -> A2 (P), v0 (S1), A3 (S2 row-major)
+        store_rowmajor(s.A3, S2, i0, j0);
+        if (threadIdx.x < NP) s.v0[threadIdx.x] = s.S1[threadIdx.x];
+        {
+            // P = I; base = M (row-major in A4, k-major in A5)
+            for (int e = threadIdx.x; e < MM; e += NT) {
+                const int i = e / NP, k = e - i * NP;
+                s.A2[e] = i == k ? 1.f : 0.f;
+                s.A4[e] = s.Mr[e];
+                s.A5[e] = s.Mt[e];
+            }
+            __syncthreads();
+            int e = len;
+            while (e > 0) {
+                float blk[4][4];
+                if (e & 1) {
+                    gemm44(s.A5, s.A2, blk, i0, j0, false);  // P <- base P
+                    __syncthreads();
+                    store_rowmajor(s.A2, blk, i0, j0);
+                    __syncthreads();
+                }
+                e >>= 1;
+                if (e > 0) {
+                    gemm44(s.A5, s.A4, blk, i0, j0, false);  // base <- base base
+                    __syncthreads();
+                    store_rowmajor(s.A4, blk, i0, j0);
+                    store_kmajor(s.A5, blk, i0, j0);
+                    __syncthreads();
+                }
+            }
+        }
+        const size_t slot = ((size_t)b * g.C + c) * g.SW;
+        int* flag = p.flags + (size_t)b * g.C + c;
+        store_slot(p.agg + slot, s.A2, s.v0, s.A3);
+        // exclusive prefix -> (A4 P, v1 S1, A5 S2) via look-back
+        if (c == 0) {
+            store_slot(p.incl + slot, s.A2, s.v0, s.A3);
+            if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(flag, kFlagIncl);
+            identity_smem(s.A4, s.v1, s.A5);
+            __syncthreads();
+        } else {
+            cta_publish(flag, kFlagAgg);
+            // acc (A4, v1, A5) = identity; X loaded into (A0.., ) -- A0 is free now
+            identity_smem(s.A4, s.v1, s.A5);
+            __syncthreads();
+            int j = c - 1;
+            for (;;) {
+                const int f = cta_wait(p, s, p.flags + (size_t)b * g.C + j, deterministic ? kFlagIncl : kFlagAgg, tile);
+                if (f < 0) return;
+                const size_t sj = ((size_t)b * g.C + j) * g.SW;
+                // X -> (A0 P, u S1, A1 S2); acc <- X (x) acc
+                load_slot_smem((f == kFlagIncl ? p.incl : p.agg) + sj, s.A0, s.u, s.A1);
+                __syncthreads();
+                chen_mul_smem(s.A0, s.u, s.A1, s.A4, s.v1, s.A5, s.A4, s.v1, s.A5, s.stage, s.stage + MM, s.s1, i0, j0);
+                if (f == kFlagIncl) break;
+                --j;
+            }
+            // incl = excl (x) agg -> (A0, u, A1)
+            chen_mul_smem(s.A4, s.v1, s.A5, s.A2, s.v0, s.A3, s.A0, s.u, s.A1, s.stage, s.stage + MM, s.s1, i0, j0);
+            store_slot(p.incl + slot, s.A0, s.u, s.A1);
+            cta_publish(flag, kFlagIncl);
+        }
+        __syncthreads();
+        store_slot(p.carry + slot, s.A4, s.v1, s.A5);
+        if (g.readout == EWS_READOUT_TERMINAL) {
+            if (c == g.C - 1) {
+                // final = excl (x) agg, staged as one row
+                chen_mul_smem(s.A4, s.v1, s.A5, s.A2, s.v0, s.A3, s.A0, s.u, s.A1, s.stage, s.stage + MM, s.s1, i0, j0);
+                float fin[4][4];
+                load_rowmajor(s.A1, fin, i0, j0);
+                if (threadIdx.x < NP) s.S1[threadIdx.x] = s.u[threadIdx.x];
+                __syncthreads();
+                stage_row(g, s, s.stage, fin, i0, j0);
+                __syncthreads();
+                if (threadIdx.x < 32) warp_store_span(p.out + (size_t)b * g.W, s.stage, g.W);
+                __syncthreads();
+            }
+            continue;
+        }
+        // pass 2 from the carry, emitting prefix rows
+        load_rowmajor(s.A5, S2, i0, j0);
+        __syncthreads();
+        store_kmajor(s.A0, S2, i0, j0);
+        if (threadIdx.x < NP) s.S1[threadIdx.x] = s.v1[threadIdx.x];
+        __syncthreads();
+        int k0 = 0;
+        for (int k = 0; k < len; ++k) {
+            fwd_step(g, s, k, S2, i0, j0);
+            stage_row(g, s, s.stage + (k - k0) * g.W, S2, i0, j0);
+            if (k - k0 == g.SR - 1 || k == len - 1) {
+                __syncthreads();
+                if (threadIdx.x < 32)
+                    warp_store_span(p.out + ((size_t)b * g.T + t0 + k0) * g.W, s.stage, (k - k0 + 1) * g.W);
+                __syncthreads();
+                k0 = k + 1;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------- backward
+
+// Transposed map of right-multiplication by G = (P, U1, U2) applied to the cotangent (L1 in v, L2 block
+// regs + row-major copy in L2r): L2 <- P^T L2 P, L1 <- P^T (L1 + L2 U1). P row-major in Pr, U1 in U1v.
+// Scratch T0, T1, vt. Barrier-complete on return; L2 block regs and L2r updated.
+__device__ void apply_JT_smem(const float* Pr, const float* U1v, float* L1, float L2[4][4], float* L2r, float* T0,
+                              float* T1, float* vt, int i0, int j0) {
+    // w = L2 U1 (row sums), then L1 <- P^T (L1 + w)
+    if (threadIdx.x < NP) {
+        float acc = 0.f;
+        for (int k = 0; k < NP; ++k) acc = fmaf(L2r[threadIdx.x * NP + k], U1v[k], acc);
+        vt[threadIdx.x] = L1[threadIdx.x] + acc;
+    }
+    // Z = P^T L2: A = P^T, A k-major: At[k][i] = P^T[i][k] = P[k][i] = Pr ; B = L2 row-major
+    float Z[4][4];
+    gemm44(Pr, L2r, Z, i0, j0, false);
+    __syncthreads();
+    store_kmajor(T0, Z, i0, j0);  // Z k-major
+    if (threadIdx.x < NP) {
+        float acc = 0.f;
+        for (int k = 0; k < NP; ++k) acc = fmaf(Pr[k * NP + threadIdx.x], vt[k], acc);
+        T1[threadIdx.x] = acc;  // P^T (L1 + w), parked in T1's first row
+    }
+    __syncthreads();
+    gemm44(T0, Pr, L2, i0, j0, false);  // L2 <- Z P   (A = Z k-major, B = P row-major)
+    __syncthreads();
+    store_rowmajor(L2r, L2, i0, j0);
+    if (threadIdx.x < NP) L1[threadIdx.x] = T1[threadIdx.x];
+    __syncthreads();
+}
+
+// Adds a gradient row (real dims) to the cotangent (L1 vector, L2 block regs).
+__device__ void add_grad_row(const Geom& g, const float* row, float* L1, float L2[4][4], int i0, int j0) {
+    const int N = g.N;
+    if (threadIdx.x < N) L1[threadIdx.x] += row[1 + threadIdx.x];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int i = i0 + r;
+        if (i >= N) continue;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int j = j0 + c;
+            if (j < N) L2[r][c] += row[1 + N + i * N + j];
+        }
+    }
+}
+
+__device__ void read_state_row(const Geom& g, const float* row, float* S1, float S2[4][4], int i0, int j0) {
+    const int N = g.N;
+    if (threadIdx.x < NP) S1[threadIdx.x] = threadIdx.x < N ? row[1 + threadIdx.x] : 0.f;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int i = i0 + r, j = j0 + c;
+            S2[r][c] = (i < N && j < N) ? row[1 + N + i * N + j] : 0.f;
+        }
+}
+
+// The transposed step alone: L2 <- M^T L2 M, L1 <- M^T (L1 + L2 s1). Uses local_terms for s1.
+__device__ void adj_step(const Geom& g, const Smem& s, int k, float* L1, float L2[4][4], int i0, int j0) {
+    local_terms(g, s, k);  // s1 (and u, U, V, unused here)
+    store_rowmajor(s.A1, L2, i0, j0);
+    __syncthreads();
+    apply_JT_smem(s.Mr, s.s1, L1, L2, s.A1, s.A2, s.A3, s.v0, i0, j0);
+}
+
+__global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
+    extern __shared__ float smem[];
+    const Geom& g = p.g;
+    Smem s = carve(smem, g, true);
+    const int bi = threadIdx.x >> 3, bj = threadIdx.x & 7;
+    const int i0 = 4 * bi, j0 = 4 * bj;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool deterministic = (g.flags & EWS_F_DETERMINISTIC) != 0;
+    float* L1 = s.v1;  // cotangent of level 1
+    for (;;) {
+        const int tile = cta_ticket(p, s);
+        if (tile >= g.ntiles) break;
+        const int cr = tile / g.B, b = tile - cr * g.B;
+        const int c = g.C - 1 - cr;
+        const int t0 = c * g.Lc;
+        const int len = min(g.Lc, g.T - t0);
+        load_tables(p, s, b);
+        load_dx(p, s, b, t0, len);
+        __syncthreads();
+        const size_t slot = ((size_t)b * g.C + c) * g.SW;
+        int* flag = p.flags + (size_t)b * g.C + c;
+
+        // ---- 1. zero-carry local adjoint (mu): L1 in s.v1, L2 block regs (+ row-major in A1 inside adj_step)
+        float L2[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) L2[r][q] = 0.f;
+        if (threadIdx.x < NP) L1[threadIdx.x] = 0.f;
+        __syncthreads();
+        for (int kb = len; kb > 0; kb -= g.SR) {
+            const int k0 = max(0, kb - g.SR);
+            __syncthreads();
+            if (threadIdx.x < 32) warp_load_span(s.stage, p.grad_out + ((size_t)b * g.T + t0 + k0) * g.W, (kb - k0) * g.W);
+            __syncthreads();
+            for (int k = kb - 1; k >= k0; --k) {
+                add_grad_row(g, s.stage + (k - k0) * g.W, L1, L2, i0, j0);
+                __syncthreads();
+                adj_step(g, s, k, L1, L2, i0, j0);
+            }
+        }
+        // mu -> slot layout [L1 (NP) in the S1 position, L2 row-major in the S2 position]
+        store_rowmajor(s.A1, L2, i0, j0);
+        __syncthreads();
+        {
+            float* dst = (c == g.C - 1 ? p.incl : p.agg) + slot;
+            for (int e = threadIdx.x; e < MM; e += NT) dst[MM + NP + e] = s.A1[e];
+            if (threadIdx.x < NP) dst[MM + threadIdx.x] = L1[threadIdx.x];
+        }
+        // ---- 2. look-back over later chunks: Lam_in (L1 in s.u, L2 row-major in s.A4)
+        for (int e = threadIdx.x; e < MM; e += NT) s.A4[e] = 0.f;
+        if (threadIdx.x < NP) s.u[threadIdx.x] = 0.f;
+        if (c == g.C - 1) {
+            if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(flag, kFlagIncl);
+            __syncthreads();
+        } else {
+            cta_publish(flag, kFlagAgg);
+            __syncthreads();
+            // Gacc = identity in (A5 P, v0 S1, A0 S2)
+            identity_smem(s.A5, s.v0, s.A0);
+            __syncthreads();
+            int j = c + 1;
+            for (;;) {
+                const int f = cta_wait(p, s, p.flags + (size_t)b * g.C + j, deterministic ? kFlagIncl : kFlagAgg, tile);
+                if (f < 0) return;
+                const size_t sj = ((size_t)b * g.C + j) * g.SW;
+                // X (cotangent) -> (s1 L1, A1 L2 row-major), then X <- J(Gacc)^T X, acc += X
+                {
+                    const float* src = (f == kFlagIncl ? p.incl : p.agg) + sj;
+                    for (int e = threadIdx.x; e < MM; e += NT) s.A1[e] = ldcg(src + MM + NP + e);
+                    if (threadIdx.x < NP) s.s1[threadIdx.x] = ldcg(src + MM + threadIdx.x);
+                }
+                __syncthreads();
+                float X2[4][4];
+                load_rowmajor(s.A1, X2, i0, j0);
+                __syncthreads();
+                apply_JT_smem(s.A5, s.v0, s.s1, X2, s.A1, s.A2, s.A3, s.stage, i0, j0);
+                for (int e = threadIdx.x; e < MM; e += NT) s.A4[e] += s.A1[e];
+                if (threadIdx.x < NP) s.u[threadIdx.x] += s.s1[threadIdx.x];
+                __syncthreads();
+                if (f == kFlagIncl) break;
+                // Gacc <- Gacc (x) G_j (forward aggregate of chunk j), G_j into (A1 P, s1 S1, A2 S2)
+                load_slot_smem(p.fagg + sj, s.A1, s.s1, s.A2);
+                __syncthreads();
+                chen_mul_smem(s.A5, s.v0, s.A0, s.A1, s.s1, s.A2, s.A5, s.v0, s.A0, s.A3, s.stage, s.stage + MM, i0, j0);
+                ++j;
+            }
+            // Lam_out = mu + J(G_c)^T Lam_in : G_c -> (A1 P, s1 S1, A2 S2)
+            load_slot_smem(p.fagg + slot, s.A1, s.s1, s.A2);
+            __syncthreads();
+            float X2[4][4];
+            load_rowmajor(s.A4, X2, i0, j0);
+            for (int e = threadIdx.x; e < MM; e += NT) s.A3[e] = s.A4[e];
+            if (threadIdx.x < NP) s.v0[threadIdx.x] = s.u[threadIdx.x];
+            __syncthreads();
+            apply_JT_smem(s.A1, s.s1, s.v0, X2, s.A3, s.A5, s.A0, s.stage, i0, j0);
+            {
+                float* dst = p.incl + slot;
+                const float* mu = p.agg + slot;
+                for (int e = threadIdx.x; e < MM; e += NT) dst[MM + NP + e] = s.A3[e] + ldcg(mu + MM + NP + e);
+                if (threadIdx.x < NP) dst[MM + threadIdx.x] = s.v0[threadIdx.x] + ldcg(mu + MM + threadIdx.x);
+            }
+            cta_publish(flag, kFlagIncl);
+            __syncthreads();
+        }
+
+        // ---- 3. exact adjoint from Lam_in with the gradients
+        load_rowmajor(s.A4, L2, i0, j0);
+        if (threadIdx.x < NP) L1[threadIdx.x] = s.u[threadIdx.x];
+        const int tabn = (1 + 2 * g.QP) * NP * g.d_in;
+        for (int e = threadIdx.x; e < tabn; e += NT) s.tacc[e] = 0.f;
+        __syncthreads();
+        float dM[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dM[r][q] = 0.f;
+        float* du = s.red;                       // NP
+        float* dU = s.red + NP;                  // NP x QMAX
+        float* ds1 = s.red + NP + NP * QMAX;     // NP
+        float* dV = s.red + 2 * NP + NP * QMAX;  // NP x QMAX
+        for (int kb = len; kb > 0; kb -= g.SR) {
+            const int k0 = max(0, kb - g.SR);
+            const int n = kb - k0;
+            __syncthreads();
+            if (threadIdx.x < 32) {
+                warp_load_span(s.stage, p.grad_out + ((size_t)b * g.T + t0 + k0) * g.W, n * g.W);
+                const int first = t0 + k0 - 1;  // S_{t-1} rows; row -1 is the zero state
+                if (first >= 0) {
+                    warp_load_span(s.stage2, p.out + ((size_t)b * g.T + first) * g.W, n * g.W);
+                } else {
+                    for (int e = lane; e < g.W; e += 32) s.stage2[e] = 0.f;
+                    if (n > 1) warp_load_span(s.stage2 + g.W, p.out + (size_t)b * g.T * g.W, (n - 1) * g.W);
+                }
+            }
+            __syncthreads();
+            for (int k = kb - 1; k >= k0; --k) {
+                // (1) cotangent of S_t and the state S_{t-1}
+                add_grad_row(g, s.stage + (k - k0) * g.W, L1, L2, i0, j0);
+                float S2p[4][4];
+                read_state_row(g, s.stage2 + (k - k0) * g.W, s.S1, S2p, i0, j0);
+                __syncthreads();
+                local_terms(g, s, k);               // s1, U, V, u = M S1p
+                store_kmajor(s.A0, S2p, i0, j0);    // S2p k-major
+                store_rowmajor(s.A1, L2, i0, j0);   // L2 row-major
+                store_kmajor(s.A2, L2, i0, j0);     // L2 k-major
+                __syncthreads();
+                // (2) X = S2p M^T, Z = M^T L2
+                float X[4][4], Z[4][4];
+                gemm44(s.A0, s.Mt, X, i0, j0, false);
+                gemm44(s.Mr, s.A1, Z, i0, j0, false);
+                // (3) contractions of L2 with the local vectors: w = L2 s1, dU = L2 V, y = L2^T u, dV = L2^T U
+                for (int o = threadIdx.x; o < 2 * NP * (g.QP + 1); o += NT) {
+                    const int side = o / (NP * (g.QP + 1)), rem = o - side * NP * (g.QP + 1);
+                    const int i = rem / (g.QP + 1), col = rem - i * (g.QP + 1);
+                    float acc = 0.f;
+                    if (side == 0) {  // row i of L2 against s1 / V[:, col-1]
+                        const float* Lr = s.A1 + i * NP;
+                        if (col == 0) {
+                            for (int j = 0; j < NP; ++j) acc = fmaf(Lr[j], s.s1[j], acc);
+                            du[i] = L1[i] + acc;
+                        } else {
+                            for (int j = 0; j < NP; ++j) acc = fmaf(Lr[j], s.V[j * QMAX + col - 1], acc);
+                            dU[i * QMAX + col - 1] = acc;
+                        }
+                    } else {  // column i of L2 against u / U[:, col-1]
+                        const float* Lc = s.A2 + i * NP;
+                        if (col == 0) {
+                            for (int j = 0; j < NP; ++j) acc = fmaf(Lc[j], s.u[j], acc);
+                            ds1[i] = L1[i] + acc;
+                        } else {
+                            for (int j = 0; j < NP; ++j) acc = fmaf(Lc[j], s.U[j * QMAX + col - 1], acc);
+                            dV[i * QMAX + col - 1] = acc;
+                        }
+                    }
+                }
+                __syncthreads();  // A0..A2 reads done, contractions visible
+                store_kmajor(s.A3, X, i0, j0);      // X k-major: B[k][j] = X[j][k]
+                store_rowmajor(s.A4, Z, i0, j0);    // Z row-major = (Z^T) k-major
+                store_kmajor(s.A5, Z, i0, j0);      // Z k-major
+                store_rowmajor(s.A1, S2p, i0, j0);  // S2p row-major
+                __syncthreads();
+                // (4) dM += L2 X^T + Z^T S2p + du S1p^T
+                gemm44(s.A2, s.A3, dM, i0, j0, true);
+                gemm44(s.A4, s.A1, dM, i0, j0, true);
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) dM[r][q] = fmaf(du[i0 + r], s.S1[j0 + q], dM[r][q]);
+                // (5) table gradients: dF += ds1 dx^T, dG_a += dU_a dx^T, dH_a += dV_a dx^T
+                const float* x = s.dx + k * g.d_in;
+                for (int e = threadIdx.x; e < tabn; e += NT) {
+                    const int blk = e / (NP * g.d_in), rem = e - blk * NP * g.d_in, i = rem / g.d_in, cc = rem - i * g.d_in;
+                    const float coef = blk == 0 ? ds1[i] : (blk <= g.QP ? dU[i * QMAX + blk - 1] : dV[i * QMAX + blk - 1 - g.QP]);
+                    s.tacc[e] = fmaf(coef, x[cc], s.tacc[e]);
+                }
+                // (6) dx_t = F^T ds1 + sum_a G_a^T dU_a + H_a^T dV_a (warp per channel, lane per row)
+                for (int cc = warp; cc < g.d_in; cc += NT / 32) {
+                    const int i = lane;
+                    float acc = s.F[i * g.d_in + cc] * ds1[i];
+                    for (int a = 0; a < g.QP; ++a) {
+                        acc = fmaf(s.G[((size_t)a * NP + i) * g.d_in + cc], dU[i * QMAX + a], acc);
+                        acc = fmaf(s.H[((size_t)a * NP + i) * g.d_in + cc], dV[i * QMAX + a], acc);
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+                    if (lane == 0) s.ddx[k * g.d_in + cc] = acc;
+                }
+                // (7) cotangent of S_{t-1}: L1 <- M^T du, L2 <- Z M
+                if (threadIdx.x < NP) {
+                    float acc = 0.f;
+                    for (int kk = 0; kk < NP; ++kk) acc = fmaf(s.Mr[kk * NP + threadIdx.x], du[kk], acc);
+                    s.v0[threadIdx.x] = acc;
+                }
+                gemm44(s.A5, s.Mr, L2, i0, j0, false);
+                __syncthreads();
+                if (threadIdx.x < NP) L1[threadIdx.x] = s.v0[threadIdx.x];
+                __syncthreads();
+            }
+        }
+        // chunk outputs: dx rows (one span) and the tile's gradient partials
+        if (threadIdx.x < 32) warp_store_span(p.grad_dx + ((size_t)b * g.T + t0) * g.d_in, s.ddx, len * g.d_in);
+        float* part = p.partials + (size_t)tile * (MM + tabn);
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) part[(i0 + r) * NP + j0 + q] = dM[r][q];
+        for (int e = threadIdx.x; e < tabn; e += NT) part[MM + e] = s.tacc[e];
+        __syncthreads();
+    }
+}
+
+// Deterministic per-sample reduction over chunks, compacted to the real dimensions.
+__global__ void reduce_kernel(Params p, float* grad_m, float* grad_f, float* grad_g, float* grad_h) {
+    const Geom& g = p.g;
+    const int N = g.N, d = g.d_in;
+    const int tabn = (1 + 2 * g.QP) * NP * d;
+    const int stride = MM + tabn;
+    const int per_sample = N * N + (1 + 2 * g.QP) * N * d;
+    const size_t total = (size_t)g.B * per_sample;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const int b = (int)(e / per_sample), r = (int)(e - (size_t)b * per_sample);
+        int off;
+        float* dst;
+        if (r < N * N) {
+            const int i = r / N, j = r - i * N;
+            off = i * NP + j;
+            dst = grad_m + (size_t)b * N * N + r;
+        } else {
+            const int q = r - N * N, blk = q / (N * d), rem = q - blk * N * d, i = rem / d, cc = rem - i * d;
+            off = MM + blk * NP * d + i * d + cc;
+            if (blk == 0) dst = grad_f + (size_t)b * N * d + rem;
+            else if (blk <= g.QP) dst = grad_g + ((size_t)b * g.QP + (blk - 1)) * N * d + rem;
+            else dst = grad_h + ((size_t)b * g.QP + (blk - 1 - g.QP)) * N * d + rem;
+        }
+        float acc = 0.f;
+        for (int cr = 0; cr < g.C; ++cr) acc += p.partials[((size_t)cr * g.B + b) * stride + off];
+        *dst = acc;
+    }
+}
+
+// ---------------------------------------------------------------------------------- host side
+
+static int make_geom(const ews_dense_args* a, Geom* g) {
+    if (!a || a->batch <= 0 || a->steps <= 0 || a->d_in <= 0 || a->dim <= 0) return EWS_ERR_INVALID_ARGUMENT;
+    if (a->depth != 2 || a->dim > NP || a->d_in > 32) return EWS_ERR_UNSUPPORTED;
+    if (a->series_q < 0 || a->series_q + 1 > QMAX) return EWS_ERR_UNSUPPORTED;
+    if (!(a->flags & EWS_F_UNIFORM)) return EWS_ERR_UNSUPPORTED;
+    if (a->readout != EWS_READOUT_PREFIX && a->readout != EWS_READOUT_TERMINAL) return EWS_ERR_INVALID_ARGUMENT;
+    if ((a->flags & EWS_F_BF16) && !(a->flags & EWS_F_INCREMENTS)) return EWS_ERR_INVALID_ARGUMENT;
+    g->B = a->batch;
+    g->T = a->steps;
+    g->d_in = a->d_in;
+    g->N = a->dim;
+    g->QP = a->series_q + 1;
+    g->W = 1 + g->N + g->N * g->N;
+    g->SW = MM + NP + MM;
+    g->readout = a->readout;
+    g->flags = a->flags;
+    g->spin_limit = a->spin_limit > 0 ? a->spin_limit : kDefaultSpinLimit;
+    if (a->chunk > 0) {
+        g->Lc = a->chunk;
+    } else {
+        const int want = 148 * 8;
+        int C = (want + g->B - 1) / g->B;
+        int Lc = (g->T + C - 1) / C;
+        g->Lc = std::max(16, std::min(256, Lc));
+    }
+    g->C = (g->T + g->Lc - 1) / g->Lc;
+    g->SR = 1;
+    g->ntiles = g->B * g->C;
+    g->smem_floats = smem_floats(*g, false);
+    g->bsmem_floats = smem_floats(*g, true);
+    return EWS_OK;
+}
+
+static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+struct WsLayout {
+    size_t status, flags, agg, incl, carry, partials, total;
+};
+
+static WsLayout fwd_layout(const Geom& g) {
+    WsLayout L{};
+    size_t o = 0;
+    L.status = o;
+    o += al256(sizeof(DeviceStatus));
+    L.flags = o;
+    o += al256(sizeof(int) * (size_t)g.ntiles);
+    const size_t slots = al256(sizeof(float) * (size_t)g.ntiles * g.SW);
+    L.agg = o;
+    o += slots;
+    L.incl = o;
+    o += slots;
+    L.carry = o;
+    o += slots;
+    L.total = o;
+    return L;
+}
+
+static WsLayout bwd_layout(const Geom& g) {
+    WsLayout L{};
+    size_t o = 0;
+    L.status = o;
+    o += al256(sizeof(DeviceStatus));
+    L.flags = o;
+    o += al256(sizeof(int) * (size_t)g.ntiles);
+    const size_t slots = al256(sizeof(float) * (size_t)g.ntiles * g.SW);
+    L.agg = o;
+    o += slots;
+    L.incl = o;
+    o += slots;
+    L.partials = o;
+    o += al256(sizeof(float) * (size_t)g.ntiles * (MM + (1 + 2 * g.QP) * NP * g.d_in));
+    L.total = o;
+    return L;
+}
+
+static int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <typename K>
+static int launch(K kernel, const Params& p, size_t smem, cudaStream_t s) {
+    if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, NT, smem);
+    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
+    int grid = per_sm * num_sms();
+    if (grid > p.g.ntiles) grid = p.g.ntiles;
+    kernel<<<grid, NT, smem, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+}  // namespace dense
+}  // namespace ews
+
+using namespace ews;
+using namespace ews::dense;
+
+extern "C" int ews_dense_workspace_size(const ews_dense_args* a, size_t* fwd_bytes, size_t* bwd_bytes) {
+    Geom g;
+    const int rc = make_geom(a, &g);
+    if (rc != EWS_OK) return rc;
+    if (fwd_bytes) *fwd_bytes = fwd_layout(g).total;
+    if (bwd_bytes) *bwd_bytes = bwd_layout(g).total;
+    return EWS_OK;
+}
+
+extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
+    Geom g;
+    const int rc = make_geom(a, &g);
+    if (rc != EWS_OK) return rc;
+    if (!a->path || !a->out || !a->tab_m || !a->tab_f || !a->tab_g || !a->tab_h) return EWS_ERR_INVALID_ARGUMENT;
+    const WsLayout L = fwd_layout(g);
+    if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    char* ws = (char*)a->fwd_ws;
+    if (cudaMemsetAsync(ws, 0, L.agg, s) != cudaSuccess) return EWS_ERR_LAUNCH;
+    Params p{};
+    p.g = g;
+    p.path = a->path;
+    p.tab_m = a->tab_m;
+    p.tab_f = a->tab_f;
+    p.tab_g = a->tab_g;
+    p.tab_h = a->tab_h;
+    p.out = a->out;
+    p.st = (DeviceStatus*)(ws + L.status);
+    p.flags = (int*)(ws + L.flags);
+    p.agg = (float*)(ws + L.agg);
+    p.incl = (float*)(ws + L.incl);
+    p.carry = (float*)(ws + L.carry);
+    return launch(fwd_kernel, p, sizeof(float) * g.smem_floats, s);
+}
+
+extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
+    Geom g;
+    int rc = make_geom(a, &g);
+    if (rc != EWS_OK) return rc;
+    if (g.readout != EWS_READOUT_PREFIX) return EWS_ERR_UNSUPPORTED;
+    if (!a->path || !a->out || !a->grad_out || !a->grad_dx || !a->grad_m || !a->grad_f || !a->grad_g || !a->grad_h)
+        return EWS_ERR_INVALID_ARGUMENT;
+    const WsLayout F = fwd_layout(g);
+    const WsLayout L = bwd_layout(g);
+    if (!a->fwd_ws || a->fwd_ws_bytes < F.total) return EWS_ERR_WORKSPACE;
+    if (!a->bwd_ws || a->bwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    char* ws = (char*)a->bwd_ws;
+    const char* fws = (const char*)a->fwd_ws;
+    if (cudaMemsetAsync(ws, 0, L.agg, s) != cudaSuccess) return EWS_ERR_LAUNCH;
+    Params p{};
+    p.g = g;
+    p.path = a->path;
+    p.tab_m = a->tab_m;
+    p.tab_f = a->tab_f;
+    p.tab_g = a->tab_g;
+    p.tab_h = a->tab_h;
+    p.out = a->out;
+    p.grad_out = a->grad_out;
+    p.grad_dx = a->grad_dx;
+    p.partials = (float*)(ws + L.partials);
+    p.st = (DeviceStatus*)(ws + L.status);
+    p.flags = (int*)(ws + L.flags);
+    p.agg = (float*)(ws + L.agg);
+    p.incl = (float*)(ws + L.incl);
+    p.fagg = (const float*)(fws + F.agg);
+    rc = launch(bwd_kernel, p, sizeof(float) * g.bsmem_floats, s);
+    if (rc != EWS_OK) return rc;
+    const size_t total = (size_t)g.B * (g.N * g.N + (1 + 2 * g.QP) * g.N * g.d_in);
+    const int threads = 256;
+    reduce_kernel<<<(int)std::min<size_t>((total + threads - 1) / threads, 65535), threads, 0, s>>>(
+        p, a->grad_m, a->grad_f, a->grad_g, a->grad_h);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}

@@ -122,3 +122,66 @@ class DiagScan(torch.autograd.Function):
             _lib.check(lib.ews_diag_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_bwd")
         gpath = gdx if increments else increments_to_knots_grad(gdx)
         return gpath.to(path_dtype), gx, gq1, gq2, glift, None, None, None, None
+
+
+class DenseScan(torch.autograd.Function):
+    """Dense engine, uniform clock: (path, M, F, G, H) -> flat EWS (prefix or terminal)."""
+
+    @staticmethod
+    def forward(ctx, path, M, F, G, H, readout, flags, chunk, increments):
+        _require_cuda(path, M, F, G, H)
+        lib = _lib.load()
+        B = path.shape[0]
+        T = path.shape[1] if increments else path.shape[1] - 1
+        d_in = path.shape[2]
+        N = M.shape[-1]
+        QP = G.shape[1]
+        D = N + N * N
+        dev = path.device
+        path_c = path.contiguous()
+        tabs = [t.contiguous().float() for t in (M, F, G, H)]
+        out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
+        a = _lib.DenseArgs()
+        a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, QP - 1, 0
+        fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        _lib.check(lib.ews_dense_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_dense_workspace_size")
+        fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
+        a.path = _ptr(path_c)
+        a.tab_m, a.tab_f, a.tab_g, a.tab_h = (_ptr(t) for t in tabs)
+        a.out = _ptr(out)
+        a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
+        with _timed("ews_dense_fwd", dev, B * T):
+            _lib.check(lib.ews_dense_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_dense_fwd")
+        ctx.meta = (readout, flags, chunk, increments, B, T, d_in, N, QP, bb.value, path.dtype)
+        ctx.save_for_backward(path_c, *tabs, out, fwd_ws)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        readout, flags, chunk, increments, B, T, d_in, N, QP, bwd_bytes, path_dtype = ctx.meta
+        path, M, F, G, H, out, fwd_ws = ctx.saved_tensors
+        if readout != _lib.EWS_READOUT_PREFIX:
+            raise NotImplementedError("the dense engine's backward runs on the prefix readout")
+        lib = _lib.load()
+        dev = path.device
+        g = grad_out.contiguous().float()
+        bwd_ws = torch.empty(bwd_bytes, dtype=torch.uint8, device=dev)
+        gdx = torch.empty((B, T, d_in), device=dev, dtype=torch.float32)
+        gM = torch.empty_like(M)
+        gF = torch.empty_like(F)
+        gG = torch.empty_like(G)
+        gH = torch.empty_like(H)
+        a = _lib.DenseArgs()
+        a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, QP - 1, 0
+        a.path = _ptr(path)
+        a.tab_m, a.tab_f, a.tab_g, a.tab_h = (_ptr(t) for t in (M, F, G, H))
+        a.out, a.grad_out, a.grad_dx = _ptr(out), _ptr(g), _ptr(gdx)
+        a.grad_m, a.grad_f, a.grad_g, a.grad_h = (_ptr(t) for t in (gM, gF, gG, gH))
+        a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fwd_ws.numel()
+        a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
+        with _timed("ews_dense_bwd", dev, B * T):
+            _lib.check(lib.ews_dense_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_dense_bwd")
+        gpath = gdx if increments else increments_to_knots_grad(gdx)
+        return gpath.to(path_dtype), gM, gF, gG, gH, None, None, None, None

@@ -112,8 +112,8 @@ class EWS(nn.Module):
             self.engine = "diag"
         else:
             self.engine = "dense"
-        if self.engine == "diag" and self.N != 2:
-            raise NotImplementedError("the diagonal engine is built for depth N=2")
+        if self.N != 2:
+            raise NotImplementedError(f"the {self.engine} engine is built for depth N=2")
 
     @property
     def signature_dim(self) -> int:
@@ -125,10 +125,10 @@ class EWS(nn.Module):
         """Batched flat EWS: path (B, L, d_in) knots [(B, L-1, d_in) increments], clock (B, L)."""
         uniform = self.reweighting_mode != "displacement"
         basepoint = self.reweighting_mode == "displacement_uniform_basepoint"
-        if self.engine != "diag":
-            raise NotImplementedError("this build runs the diagonal engine; dense and block engines are not built yet")
         if not uniform:
-            raise NotImplementedError("the diagonal engine is built for the uniform-clock reweighting modes")
+            raise NotImplementedError(f"the {self.engine} engine is built for the uniform-clock reweighting modes")
+        if self.engine == "dense":
+            return self._flat_dense(path, clock, readout, a_scale, lift, increments, basepoint)
         kernel_readout = _lib.EWS_READOUT_TERMINAL if readout == "terminal" else _lib.EWS_READOUT_PREFIX
         lam = self.A_param.diag_values().to(torch.float32) * a_scale
         clock = clock.to(torch.float32)
@@ -147,6 +147,29 @@ class EWS(nn.Module):
         else:
             path = path.to(torch.float32)
         return engine.DiagScan.apply(path, x, q1, q2, lift, kernel_readout, flags, self.combine_chunk, increments)
+
+    def _flat_dense(self, path, clock, readout, a_scale, lift, increments, basepoint):
+        if basepoint:
+            raise NotImplementedError("the dense engine runs the displacement_uniform mode")
+        A = self.A_param().to(torch.float32) * a_scale
+        clock = clock.to(torch.float32)
+        h = clock[:, 1] - clock[:, 0]
+        M, F, G, H = series.dense_tables(A, h, self.series_q, lift)
+        flags = _lib.EWS_F_UNIFORM | (_lib.EWS_F_DETERMINISTIC if _DETERMINISTIC else 0)
+        if increments:
+            flags |= _lib.EWS_F_INCREMENTS
+            if path.dtype == torch.bfloat16:
+                flags |= _lib.EWS_F_BF16
+            else:
+                path = path.to(torch.float32)
+        else:
+            path = path.to(torch.float32)
+        needs_grad = torch.is_grad_enabled() and any(t.requires_grad for t in (path, M, F, G, H))
+        if readout == "terminal" and not needs_grad:
+            return engine.DenseScan.apply(path, M, F, G, H, _lib.EWS_READOUT_TERMINAL, flags, self.combine_chunk, increments)
+        # the dense backward runs on the prefix stream (the terminal value is its last row)
+        out = engine.DenseScan.apply(path, M, F, G, H, _lib.EWS_READOUT_PREFIX, flags, self.combine_chunk, increments)
+        return out[:, -1] if readout == "terminal" else out
 
     def forward(
         self,

@@ -101,3 +101,29 @@ def diag_tables(x: torch.Tensor, q: int):
     q1 = powers @ c1
     q2 = torch.einsum("...ia,ab,...jb->...ij", powers, c2, powers)
     return q1.to(x.dtype), q2.to(x.dtype)
+
+
+def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None):
+    """Per-sample tables of the dense engine for generator A (N, N), clock steps h (B,) and lift W (N, d_in):
+    M = expm(-hA), F = K1 W, G_a = P_a W, H_a = K2_a W with P_a = (-hA)^a / a!, K1 = sum_p c_p P_p,
+    K2_a = sum_b c_ab P_b (the series leaf with shared letters, ews/core/series_leaf.py:72-113).
+    Differentiable; evaluated in float64 and returned in float32."""
+    Ad = A.to(torch.float64)
+    X = -h.to(torch.float64)[:, None, None] * Ad  # (B, N, N)
+    M = torch.linalg.matrix_exp(X)
+    N = A.shape[-1]
+    eye = torch.eye(N, dtype=torch.float64, device=A.device).expand_as(X)
+    P = [eye]
+    for a in range(1, q + 1):
+        P.append(P[-1] @ X / a)
+    P = torch.stack(P, dim=1)  # (B, q+1, N, N)
+    C1, C2 = series_coeffs(2, q)
+    c1 = torch.tensor(C1, dtype=torch.float64, device=A.device)
+    c2 = torch.tensor(C2, dtype=torch.float64, device=A.device)
+    K1 = torch.einsum("p,bpij->bij", c1, P)
+    K2 = torch.einsum("ab,zbij->zaij", c2, P)
+    W = torch.eye(N, dtype=torch.float64, device=A.device) if lift is None else lift.to(torch.float64)
+    F = K1 @ W
+    G = P @ W
+    H = K2 @ W
+    return M.float(), F.float(), G.float(), H.float()

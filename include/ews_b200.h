@@ -124,6 +124,45 @@ int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream);
 #define EWS_NOALLOC_SCRATCH_BYTES (16u << 20)
 int ews_diag_fwd_noalloc(const ews_diag_args* a, ews_stream_t stream);
 
+/* ---- dense engine: any generator A (uniform clock) --------------------------------------------
+ * Replaces combine_packed(kind="dense_kernel" / "lean") fed by leaf="series" (ews/core/kernels/combine.py:
+ * 260-269, ews/core/kernels/pallas_combine.py:803-858 forward, :2628-2711 custom VJP) with the series
+ * local terms fused. Depth 2, dim <= 32, d_in <= 32, series_q <= 11. With the sample's shared clock step h,
+ * P_a = (-hA)^a / a!, K1 = sum_p c_p P_p and K2_a = sum_b c_ab P_b (ews/core/series_leaf.py:45-113), and the
+ * lift W, the per-sample tables are
+ *   tab_m (B, N, N)          the flow M = expm(-h A)
+ *   tab_f (B, N, d_in)       F = K1 W            (s1 = F dx)
+ *   tab_g (B, q+1, N, d_in)  G_a = P_a W         (s2 = sum_a (G_a dx)(H_a dx)^T)
+ *   tab_h (B, q+1, N, d_in)  H_a = K2_a W
+ * The backward returns dL/d(tables) per sample and dL/d(increments); prefix readout only (the terminal
+ * value is the prefix's last row, as in the reference's dense kernel). */
+typedef struct ews_dense_args {
+    int batch, steps, d_in, dim, depth, chunk, readout;
+    unsigned flags;
+    int series_q;
+    int spin_limit;
+    const void* path;        /* (B, T+1, d_in) knots or (B, T, d_in) increments */
+    const float* tab_m;
+    const float* tab_f;
+    const float* tab_g;
+    const float* tab_h;
+    float* out;              /* (B, T, 1 + D) prefix or (B, 1 + D) terminal (forward only) */
+    const float* grad_out;
+    float* grad_dx;          /* (B, T, d_in) */
+    float* grad_m;           /* (B, N, N) */
+    float* grad_f;           /* (B, N, d_in) */
+    float* grad_g;           /* (B, q+1, N, d_in) */
+    float* grad_h;           /* (B, q+1, N, d_in) */
+    void* fwd_ws;
+    size_t fwd_ws_bytes;
+    void* bwd_ws;
+    size_t bwd_ws_bytes;
+} ews_dense_args;
+
+int ews_dense_workspace_size(const ews_dense_args* a, size_t* fwd_bytes, size_t* bwd_bytes);
+int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream);
+int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream);
+
 /* ---- utilities --------------------------------------------------------------------------------- */
 /* Copies the device-side status word of a workspace (EWS_OK or EWS_ERR_LOOKBACK_TIMEOUT) to the host;
  * synchronises the stream. */

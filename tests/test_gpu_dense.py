@@ -1,0 +1,140 @@
+"""Parity of the dense engine (CUDA, fp32) with the float64 CPU oracle, through the C ABI.
+
+Same inputs on both sides (float32-rounded, evaluated by the oracle in float64), same tolerances as
+tests/test_gpu_diag.py: global relerr <= 1e-5 against the float64 oracle and <= 4x the reference
+algorithm's own float32 error + 1e-5 for outputs and gradients; for paths of at most 256 intervals the
+forward also elementwise |out - ref| <= 1e-6 + 1e-5 |ref|.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ews_oracle as O
+from tests.conftest import relerr
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _f32(a):
+    return None if a is None else np.asarray(a, dtype=np.float32).astype(np.float64)
+
+
+def _require_gpu():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test run without a CUDA device")
+
+
+def _case(B, T, N, d_in, seed=0, scale=0.1):
+    """Config-2 style: Brownian channels (N(0, 1/T) increments), A = 0.5 I - scale G / sqrt(N)."""
+    rng = np.random.default_rng(seed)
+    inc = rng.normal(size=(B, T, d_in)) / np.sqrt(T)
+    path = np.concatenate([np.zeros((B, 1, d_in)), np.cumsum(inc, 1)], 1)
+    A = 0.5 * np.eye(N) - scale * rng.normal(size=(N, N)) / np.sqrt(N)
+    lift = rng.normal(size=(N, d_in)) / np.sqrt(d_in)
+    clock = np.broadcast_to(np.arange(T + 1) / T, (B, T + 1)).copy()
+    return _f32(path), _f32(clock), _f32(A), _f32(lift)
+
+
+def _oracle(path, clock, A, lift, readout, q, w=None, dtype=torch.float64):
+    p = torch.tensor(path, dtype=dtype, requires_grad=True)
+    Am = torch.tensor(A, dtype=dtype, requires_grad=True)
+    Bm = None if lift is None else torch.tensor(lift, dtype=dtype, requires_grad=True)
+    y = p if Bm is None else O.lift(p, Bm)
+    out = O.ews_layer(y, torch.tensor(clock, dtype=dtype), Am, 2, series_q=q, reweighting_mode="displacement_uniform", readout=readout)
+    if w is None:
+        return out.detach().double(), None
+    (out * w.to(dtype)).sum().backward()
+    return out.detach().double(), (p.grad.double(), Am.grad.double(), None if Bm is None else Bm.grad.double())
+
+
+def _kernel(path, clock, A, lift, readout, q, w=None, chunk=0):
+    from exponentially_weighted_signature_b200 import EWS, AParamGeneral
+
+    Ap = AParamGeneral(torch.tensor(A, dtype=torch.float32)).to(DEV)
+    layer = EWS(Ap, N=2, reweighting_mode="displacement_uniform", series_q=q, combine_chunk=chunk)
+    p = torch.tensor(path, dtype=torch.float32, device=DEV, requires_grad=True)
+    Bm = None if lift is None else torch.tensor(lift, dtype=torch.float32, device=DEV, requires_grad=True)
+    out = layer(p, torch.tensor(clock, dtype=torch.float32, device=DEV), readout=readout, lift=Bm)
+    if w is None:
+        return out.detach().cpu().double(), None
+    (out * w.to(DEV, torch.float32)).sum().backward()
+    torch.cuda.synchronize()
+    return out.detach().cpu().double(), (p.grad.cpu().double(), Ap.matrix.grad.cpu().double(), None if Bm is None else Bm.grad.cpu().double())
+
+
+def _assert_close(name, out, ref, ref32=None):
+    assert out.shape == ref.shape, name
+    e = relerr(out, ref)
+    assert e <= 1e-5, f"{name}: relerr {e:.2e}"
+    if ref32 is not None:
+        e32 = relerr(ref32, ref)
+        assert e <= 4 * e32 + 1e-5, f"{name}: relerr {e:.2e} vs float32 reference {e32:.2e}"
+
+
+def _assert_fwd(out, ref, ref32=None, elementwise=True):
+    _assert_close("forward", out, ref, ref32)
+    if elementwise:
+        err = (out - ref).abs()
+        bound = 1e-6 + 1e-5 * ref.abs()
+        assert bool((err <= bound).all()), f"max excess {float((err - bound).max()):.3e}, relerr {relerr(out, ref):.2e}"
+
+
+@pytest.mark.parametrize("N", [5, 16, 32])
+@pytest.mark.parametrize("readout", ["prefix", "terminal", "mean"])
+def test_forward_matches_oracle(N, readout):
+    _require_gpu()
+    path, clock, A, lift = _case(3, 60, N, d_in=7, seed=N)
+    ref, _ = _oracle(path, clock, A, lift, readout, 6)
+    out, _ = _kernel(path, clock, A, lift, readout, 6, chunk=16)
+    _assert_fwd(out, ref)
+
+
+@pytest.mark.parametrize("chunk", [1, 7, 64, 0])
+def test_chunking_and_lookback(chunk):
+    _require_gpu()
+    path, clock, A, lift = _case(3, 130, 32, d_in=7, seed=3)
+    ref, _ = _oracle(path, clock, A, lift, "prefix", 5)
+    out, _ = _kernel(path, clock, A, lift, "prefix", 5, chunk=chunk)
+    _assert_fwd(out, ref)
+
+
+@pytest.mark.parametrize("N", [8, 32])
+@pytest.mark.parametrize("readout", ["prefix", "terminal"])
+def test_gradients_match_oracle(N, readout):
+    _require_gpu()
+    path, clock, A, lift = _case(2, 70, N, d_in=7, seed=20 + N)
+    ref, _ = _oracle(path, clock, A, lift, readout, 6)
+    w = torch.tensor(np.random.default_rng(3).normal(size=ref.shape))
+    _, (gp_r, ga_r, gb_r) = _oracle(path, clock, A, lift, readout, 6, w=w)
+    _, (gp_n, ga_n, gb_n) = _kernel(path, clock, A, lift, readout, 6, w=w, chunk=16)
+    for name, a, b in [("path", gp_n, gp_r), ("A", ga_n, ga_r), ("lift", gb_n, gb_r)]:
+        _assert_close(f"{name} grad", a, b)
+
+
+def test_identity_lift():
+    _require_gpu()
+    path, clock, A, _ = _case(2, 40, 12, d_in=12, seed=4, scale=0.5)
+    ref, _ = _oracle(path, clock, A, None, "prefix", 6)
+    out, _ = _kernel(path, clock, A, None, "prefix", 6, chunk=8)
+    _assert_fwd(out, ref)
+
+
+def test_config2_full_length():
+    """BASELINE config 2 at full length (T = 17984, N = 32, d = 7, q from the bound), batch reduced to 2
+    for the oracle's memory; forward and gradients."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import workloads
+
+    case = workloads.config2(B=2)
+    path, clock, A, lift = (_f32(case[k]) for k in ("path", "clock", "A", "lift"))
+    args = (path, clock, A, lift, "prefix", 4)
+    w = torch.tensor(np.random.default_rng(3).normal(size=(2, path.shape[1] - 1, 1 + 32 + 32 * 32)))
+    ref, g64 = _oracle(*args, w=w)
+    ref32, g32 = _oracle(*args, w=w, dtype=torch.float32)
+    out, gk = _kernel(*args, w=w)
+    _assert_fwd(out, ref, ref32, elementwise=False)
+    for name, a, b, c in zip(("path", "A", "lift"), gk, g64, g32):
+        _assert_close(f"{name} grad", a, b, c)
