@@ -95,14 +95,14 @@ class DenseArgs(ctypes.Structure):
         ("series_q", _c_int),
         ("spin_limit", _c_int),
         ("path", _vp),
-        ("tab_m", _vp),
+        ("tab_d", _vp),
         ("tab_f", _vp),
         ("tab_g", _vp),
         ("tab_h", _vp),
         ("out", _vp),
         ("grad_out", _vp),
         ("grad_dx", _vp),
-        ("grad_m", _vp),
+        ("grad_d", _vp),
         ("grad_f", _vp),
         ("grad_g", _vp),
         ("grad_h", _vp),

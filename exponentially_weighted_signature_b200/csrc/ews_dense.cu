@@ -1,6 +1,6 @@
 // Dense-A engine of the EWS hot path (any generator A, uniform clock), depth 2, N <= 32, fp32.
 //
-// Per interval t of sample b, with the flow M = exp(-h A) and the increment dx_t (before the lift):
+// Per interval t of sample b, with the flow M = exp(-h A) = I - D and the increment dx_t (before the lift):
 //     S1' = u + s1,                      u  = M S1,   s1 = F dx
 //     S2' = M S2 M^T + u s1^T + U V^T,   U = [G_a dx]_a,  V = [H_a dx]_a   (a = 0..q)
 // This is the modified-Chen recursion of ews/core/chen_scan.py:124-152 (sequentially:
@@ -12,7 +12,11 @@
 // Work decomposition: one CTA of 64 threads owns one tile (sample, chunk). Thread (bi, bj) holds the 4x4
 // block (rows 4bi.., cols 4bj..) of every 32x32 matrix; a 32x32x32 product reads two float4 operands per k
 // from shared memory (A k-major, B row-major) into 16 FMAs. Chunks are combined with the decoupled
-// look-back of the diagonal engine (chunk aggregates (M^L, S1, S2), Chen products by GEMMs).
+// look-back of the diagonal engine (chunk aggregates (I - M^L, S1, S2), Chen products by GEMMs).
+//
+// Flows are carried as complements D = I - M (the caller evaluates D in float64): M X = X - D X. An M
+// within 1e-4 of the identity, rounded once and applied T times, drifts by ~T 2^-24; the complement keeps
+// the rounding relative to D. Chunk flows compose as complements, I - (I-A)(I-B) = A + B - AB.
 #include <algorithm>
 #include <cstdio>
 
@@ -39,7 +43,7 @@ struct Geom {
 struct Params {
     Geom g;
     const void* path;
-    const float* tab_m;  // (B, N, N)
+    const float* tab_d;  // (B, N, N) flow complement D = I - M
     const float* tab_f;  // (B, N, d_in)
     const float* tab_g;  // (B, QP, N, d_in)
     const float* tab_h;  // (B, QP, N, d_in)
@@ -108,8 +112,8 @@ __device__ __forceinline__ void load_rowmajor(const float* M, float blk[4][4], i
 // ---------------------------------------------------------------------------------- shared memory
 
 struct Smem {
-    float* Mr;   // M row-major
-    float* Mt;   // M k-major
+    float* Mr;   // D = I - M row-major
+    float* Mt;   // D k-major
     float* A0;   // work matrices
     float* A1;
     float* A2;
@@ -175,14 +179,14 @@ __host__ int smem_floats(const Geom& g, bool bwd) {
     return n + 4;
 }
 
-// Loads the per-sample tables (M padded with the identity, F/G/H padded with zero rows).
+// Loads the per-sample tables (D padded with zeros, i.e. the identity flow, F/G/H with zero rows).
 __device__ void load_tables(const Params& p, const Smem& s, int b) {
     const Geom& g = p.g;
     const int N = g.N, d = g.d_in;
-    const float* m = p.tab_m + (size_t)b * N * N;
+    const float* m = p.tab_d + (size_t)b * N * N;
     for (int e = threadIdx.x; e < MM; e += NT) {
         const int i = e / NP, k = e - i * NP;
-        const float v = (i < N && k < N) ? m[i * N + k] : (i == k ? 1.f : 0.f);
+        const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
         s.Mr[i * NP + k] = v;
         s.Mt[k * NP + i] = v;
     }
@@ -224,7 +228,7 @@ __device__ void local_terms(const Geom& g, const Smem& s, int k) {
         float acc = 0.f;
 #pragma unroll 8
         for (int kk = 0; kk < NP; ++kk) acc = fmaf(s.Mt[kk * NP + i], s.S1[kk], acc);
-        s.u[i] = acc;
+        s.u[i] = s.S1[i] - acc;  // M S1 = S1 - D S1
     }
     for (int e = tid; e < 2 * g.QP * NP; e += NT) {
         const int which = e / (g.QP * NP), r = e - which * g.QP * NP, a = r / NP, i = r - a * NP;
@@ -240,17 +244,21 @@ __device__ void local_terms(const Geom& g, const Smem& s, int k) {
 __device__ void fwd_step(const Geom& g, const Smem& s, int k, float S2[4][4], int i0, int j0) {
     local_terms(g, s, k);
     __syncthreads();
-    float X[4][4];
-    gemm44(s.A0, s.Mt, X, i0, j0, false);  // X = S2 M^T   (A = S2 k-major, B[k][j] = M[j][k])
+    float X[4][4], Y[4][4];
+    gemm44(s.A0, s.Mt, X, i0, j0, false);  // S2 D^T   (A = S2 k-major, B[k][j] = D[j][k])
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) X[r][c] = S2[r][c] - X[r][c];  // X = S2 M^T
     store_rowmajor(s.A1, X, i0, j0);
     __syncthreads();
-    gemm44(s.Mt, s.A1, S2, i0, j0, false);  // M X         (A = M k-major, B = X row-major)
+    gemm44(s.Mt, s.A1, Y, i0, j0, false);  // D X      (A = D k-major, B = X row-major)
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         const float ur = s.u[i0 + r];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            float acc = fmaf(ur, s.s1[j0 + c], S2[r][c]);
+            float acc = fmaf(ur, s.s1[j0 + c], X[r][c] - Y[r][c]);  // M X = X - D X
             for (int a = 0; a < g.QP; ++a) acc = fmaf(s.U[(i0 + r) * QMAX + a], s.V[(j0 + c) * QMAX + a], acc);
             S2[r][c] = acc;
         }
@@ -288,36 +296,47 @@ __device__ void store_slot(float* slot, const float* Pr, const float* S1, const 
     if (threadIdx.x < NP) slot[MM + threadIdx.x] = S1[threadIdx.x];
 }
 
-// out = L (x) R with L, R given as (P row-major, S1, S2 row-major) in shared memory; result written to
-// (Po, S1o, S2o) row-major. Needs two scratch matrices T0, T1. Barrier-complete on return.
+// out = L (x) R with L, R given as (flow complement C row-major, S1, S2 row-major) in shared memory; result
+// written to (Co, S1o, S2o) row-major (outputs may alias the inputs). With P_R = I - C_R:
+//   S2 = P_R L2 P_R^T + (P_R L1) R1^T + R2,  S1 = P_R L1 + R1,  C = C_L + C_R - C_R C_L.
+// Needs two scratch matrices T0, T1 and a vector vtmp. Barrier-complete on return.
 __device__ void chen_mul_smem(const float* PL, const float* L1, const float* L2, const float* PR, const float* R1,
                               const float* R2, float* Po, float* S1o, float* S2o, float* T0, float* T1, float* vtmp,
                               int i0, int j0) {
-    // T0 = PR^T (k-major of PR), T1 = L2^T... we need: S2 = PR L2 PR^T + (PR L1) R1^T + R2
-    //   X = L2 PR^T: A = L2 (k-major = L2^T), B[k][j] = PR[j][k] (= PR^T row-major)
     for (int e = threadIdx.x; e < MM; e += NT) {
         const int i = e / NP, k = e - i * NP;
         T0[k * NP + i] = L2[e];   // L2 k-major
-        T1[k * NP + i] = PR[e];   // PR k-major = PR^T row-major
+        T1[k * NP + i] = PR[e];   // C_R k-major
     }
     if (threadIdx.x < NP) {
         float acc = 0.f;
         for (int k = 0; k < NP; ++k) acc = fmaf(PR[threadIdx.x * NP + k], L1[k], acc);
-        vtmp[threadIdx.x] = acc;
+        vtmp[threadIdx.x] = L1[threadIdx.x] - acc;  // P_R L1
     }
     __syncthreads();
+    float L2b[4][4], CLb[4][4], CRb[4][4];
+    load_rowmajor(L2, L2b, i0, j0);
+    load_rowmajor(PL, CLb, i0, j0);
+    load_rowmajor(PR, CRb, i0, j0);
     float X[4][4], Y[4][4], P[4][4];
-    gemm44(T0, T1, X, i0, j0, false);  // X = L2 PR^T
-    gemm44(T1, PL, P, i0, j0, false);  // P = PR PL     (A = PR k-major, B = PL row-major)
+    gemm44(T0, T1, X, i0, j0, false);  // L2 C_R^T
+    gemm44(T1, PL, P, i0, j0, false);  // C_R C_L
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            X[r][c] = L2b[r][c] - X[r][c];                  // X = L2 P_R^T
+            P[r][c] = CLb[r][c] + CRb[r][c] - P[r][c];      // complement of P_R P_L
+        }
     __syncthreads();
     store_rowmajor(T0, X, i0, j0);
     __syncthreads();
-    gemm44(T1, T0, Y, i0, j0, false);  // Y = PR X
+    gemm44(T1, T0, Y, i0, j0, false);  // C_R X
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-            Y[r][c] += fmaf(vtmp[i0 + r], R1[j0 + c], R2[(i0 + r) * NP + j0 + c]);
+            Y[r][c] = (X[r][c] - Y[r][c]) + fmaf(vtmp[i0 + r], R1[j0 + c], R2[(i0 + r) * NP + j0 + c]);
     __syncthreads();
     store_rowmajor(S2o, Y, i0, j0);
     store_rowmajor(Po, P, i0, j0);
@@ -335,8 +354,7 @@ __device__ void load_slot_smem(const float* slot, float* P, float* S1, float* S2
 
 __device__ void identity_smem(float* P, float* S1, float* S2) {
     for (int e = threadIdx.x; e < MM; e += NT) {
-        const int i = e / NP, k = e - i * NP;
-        P[e] = i == k ? 1.f : 0.f;
+        P[e] = 0.f;  // flow complement of the identity
         S2[e] = 0.f;
     }
     if (threadIdx.x < NP) S1[threadIdx.x] = 0.f;
@@ -396,31 +414,40 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
         if (threadIdx.x < NP) s.S1[threadIdx.x] = 0.f;
         __syncthreads();
         for (int k = 0; k < len; ++k) fwd_step(g, s, k, S2, i0, j0);
-        // aggregate (P = M^len by binary powering, S1, S2) -> A2 (P), v0 (S1), A3 (S2 row-major)
+        // aggregate (C = I - M^len by binary powering of complements, S1, S2) -> A2 (C), v0 (S1), A3 (S2)
         store_rowmajor(s.A3, S2, i0, j0);
         if (threadIdx.x < NP) s.v0[threadIdx.x] = s.S1[threadIdx.x];
         {
-            // P = I; base = M (row-major in A4, k-major in A5)
+            // R = 0 (identity); base = D (row-major in A4, k-major in A5)
             for (int e = threadIdx.x; e < MM; e += NT) {
-                const int i = e / NP, k = e - i * NP;
-                s.A2[e] = i == k ? 1.f : 0.f;
+                s.A2[e] = 0.f;
                 s.A4[e] = s.Mr[e];
                 s.A5[e] = s.Mt[e];
             }
             __syncthreads();
             int e = len;
             while (e > 0) {
-                float blk[4][4];
+                float blk[4][4], Rb[4][4], Bb[4][4];
+                load_rowmajor(s.A4, Bb, i0, j0);
                 if (e & 1) {
-                    gemm44(s.A5, s.A2, blk, i0, j0, false);  // P <- base P
+                    load_rowmajor(s.A2, Rb, i0, j0);
+                    gemm44(s.A5, s.A2, blk, i0, j0, false);  // base R
                     __syncthreads();
+#pragma unroll
+                    for (int r = 0; r < 4; ++r)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) blk[r][q] = Rb[r][q] + Bb[r][q] - blk[r][q];
                     store_rowmajor(s.A2, blk, i0, j0);
                     __syncthreads();
                 }
                 e >>= 1;
                 if (e > 0) {
-                    gemm44(s.A5, s.A4, blk, i0, j0, false);  // base <- base base
+                    gemm44(s.A5, s.A4, blk, i0, j0, false);  // base base
                     __syncthreads();
+#pragma unroll
+                    for (int r = 0; r < 4; ++r)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) blk[r][q] = 2.f * Bb[r][q] - blk[r][q];
                     store_rowmajor(s.A4, blk, i0, j0);
                     store_kmajor(s.A5, blk, i0, j0);
                     __syncthreads();
@@ -498,29 +525,36 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
 
 // ---------------------------------------------------------------------------------- backward
 
-// Transposed map of right-multiplication by G = (P, U1, U2) applied to the cotangent (L1 in v, L2 block
-// regs + row-major copy in L2r): L2 <- P^T L2 P, L1 <- P^T (L1 + L2 U1). P row-major in Pr, U1 in U1v.
-// Scratch T0, T1, vt. Barrier-complete on return; L2 block regs and L2r updated.
+// Transposed map of right-multiplication by G = (P, U1, U2), P = I - C, applied to the cotangent (L1 in
+// smem, L2 block regs + row-major copy in L2r): L2 <- P^T L2 P, L1 <- P^T (L1 + L2 U1). C row-major in Pr,
+// U1 in U1v. Scratch T0 (matrix), T1 (vector), vt. Barrier-complete on return.
 __device__ void apply_JT_smem(const float* Pr, const float* U1v, float* L1, float L2[4][4], float* L2r, float* T0,
                               float* T1, float* vt, int i0, int j0) {
-    // w = L2 U1 (row sums), then L1 <- P^T (L1 + w)
     if (threadIdx.x < NP) {
         float acc = 0.f;
         for (int k = 0; k < NP; ++k) acc = fmaf(L2r[threadIdx.x * NP + k], U1v[k], acc);
         vt[threadIdx.x] = L1[threadIdx.x] + acc;
     }
-    // Z = P^T L2: A = P^T, A k-major: At[k][i] = P^T[i][k] = P[k][i] = Pr ; B = L2 row-major
+    // Z = P^T L2 = L2 - C^T L2  (A = C^T: k-major of C^T is C row-major)
     float Z[4][4];
     gemm44(Pr, L2r, Z, i0, j0, false);
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) Z[r][c] = L2[r][c] - Z[r][c];
     __syncthreads();
-    store_kmajor(T0, Z, i0, j0);  // Z k-major
+    store_kmajor(T0, Z, i0, j0);
     if (threadIdx.x < NP) {
         float acc = 0.f;
         for (int k = 0; k < NP; ++k) acc = fmaf(Pr[k * NP + threadIdx.x], vt[k], acc);
-        T1[threadIdx.x] = acc;  // P^T (L1 + w), parked in T1's first row
+        T1[threadIdx.x] = vt[threadIdx.x] - acc;  // P^T (L1 + w)
     }
     __syncthreads();
-    gemm44(T0, Pr, L2, i0, j0, false);  // L2 <- Z P   (A = Z k-major, B = P row-major)
+    gemm44(T0, Pr, L2, i0, j0, false);  // Z C
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) L2[r][c] = Z[r][c] - L2[r][c];  // Z P
     __syncthreads();
     store_rowmajor(L2r, L2, i0, j0);
     if (threadIdx.x < NP) L1[threadIdx.x] = T1[threadIdx.x];
@@ -710,10 +744,17 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
                 store_rowmajor(s.A1, L2, i0, j0);   // L2 row-major
                 store_kmajor(s.A2, L2, i0, j0);     // L2 k-major
                 __syncthreads();
-                // (2) X = S2p M^T, Z = M^T L2
+                // (2) X = S2p M^T = S2p - S2p D^T, Z = M^T L2 = L2 - D^T L2
                 float X[4][4], Z[4][4];
                 gemm44(s.A0, s.Mt, X, i0, j0, false);
                 gemm44(s.Mr, s.A1, Z, i0, j0, false);
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        X[r][q] = S2p[r][q] - X[r][q];
+                        Z[r][q] = L2[r][q] - Z[r][q];
+                    }
                 // (3) contractions of L2 with the local vectors: w = L2 s1, dU = L2 V, y = L2^T u, dV = L2^T U
                 for (int o = threadIdx.x; o < 2 * NP * (g.QP + 1); o += NT) {
                     const int side = o / (NP * (g.QP + 1)), rem = o - side * NP * (g.QP + 1);
@@ -771,13 +812,17 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
                     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
                     if (lane == 0) s.ddx[k * g.d_in + cc] = acc;
                 }
-                // (7) cotangent of S_{t-1}: L1 <- M^T du, L2 <- Z M
+                // (7) cotangent of S_{t-1}: L1 <- M^T du = du - D^T du, L2 <- Z M = Z - Z D
                 if (threadIdx.x < NP) {
                     float acc = 0.f;
                     for (int kk = 0; kk < NP; ++kk) acc = fmaf(s.Mr[kk * NP + threadIdx.x], du[kk], acc);
-                    s.v0[threadIdx.x] = acc;
+                    s.v0[threadIdx.x] = du[threadIdx.x] - acc;
                 }
                 gemm44(s.A5, s.Mr, L2, i0, j0, false);
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) L2[r][q] = Z[r][q] - L2[r][q];
                 __syncthreads();
                 if (threadIdx.x < NP) L1[threadIdx.x] = s.v0[threadIdx.x];
                 __syncthreads();
@@ -796,7 +841,7 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
 }
 
 // Deterministic per-sample reduction over chunks, compacted to the real dimensions.
-__global__ void reduce_kernel(Params p, float* grad_m, float* grad_f, float* grad_g, float* grad_h) {
+__global__ void reduce_kernel(Params p, float* grad_d, float* grad_f, float* grad_g, float* grad_h) {
     const Geom& g = p.g;
     const int N = g.N, d = g.d_in;
     const int tabn = (1 + 2 * g.QP) * NP * d;
@@ -810,7 +855,7 @@ __global__ void reduce_kernel(Params p, float* grad_m, float* grad_f, float* gra
         if (r < N * N) {
             const int i = r / N, j = r - i * N;
             off = i * NP + j;
-            dst = grad_m + (size_t)b * N * N + r;
+            dst = grad_d + (size_t)b * N * N + r;
         } else {
             const int q = r - N * N, blk = q / (N * d), rem = q - blk * N * d, i = rem / d, cc = rem - i * d;
             off = MM + blk * NP * d + i * d + cc;
@@ -820,7 +865,7 @@ __global__ void reduce_kernel(Params p, float* grad_m, float* grad_f, float* gra
         }
         float acc = 0.f;
         for (int cr = 0; cr < g.C; ++cr) acc += p.partials[((size_t)cr * g.B + b) * stride + off];
-        *dst = acc;
+        *dst = r < N * N ? -acc : acc;  // the flow block accumulates dL/dM; dL/dD = -dL/dM
     }
 }
 
@@ -944,7 +989,7 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     Geom g;
     const int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
-    if (!a->path || !a->out || !a->tab_m || !a->tab_f || !a->tab_g || !a->tab_h) return EWS_ERR_INVALID_ARGUMENT;
+    if (!a->path || !a->out || !a->tab_d || !a->tab_f || !a->tab_g || !a->tab_h) return EWS_ERR_INVALID_ARGUMENT;
     const WsLayout L = fwd_layout(g);
     if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
@@ -953,7 +998,7 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     Params p{};
     p.g = g;
     p.path = a->path;
-    p.tab_m = a->tab_m;
+    p.tab_d = a->tab_d;
     p.tab_f = a->tab_f;
     p.tab_g = a->tab_g;
     p.tab_h = a->tab_h;
@@ -971,7 +1016,7 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
     if (g.readout != EWS_READOUT_PREFIX) return EWS_ERR_UNSUPPORTED;
-    if (!a->path || !a->out || !a->grad_out || !a->grad_dx || !a->grad_m || !a->grad_f || !a->grad_g || !a->grad_h)
+    if (!a->path || !a->out || !a->grad_out || !a->grad_dx || !a->grad_d || !a->grad_f || !a->grad_g || !a->grad_h)
         return EWS_ERR_INVALID_ARGUMENT;
     const WsLayout F = fwd_layout(g);
     const WsLayout L = bwd_layout(g);
@@ -984,7 +1029,7 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     Params p{};
     p.g = g;
     p.path = a->path;
-    p.tab_m = a->tab_m;
+    p.tab_d = a->tab_d;
     p.tab_f = a->tab_f;
     p.tab_g = a->tab_g;
     p.tab_h = a->tab_h;
@@ -1002,6 +1047,6 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     const size_t total = (size_t)g.B * (g.N * g.N + (1 + 2 * g.QP) * g.N * g.d_in);
     const int threads = 256;
     reduce_kernel<<<(int)std::min<size_t>((total + threads - 1) / threads, 65535), threads, 0, s>>>(
-        p, a->grad_m, a->grad_f, a->grad_g, a->grad_h);
+        p, a->grad_d, a->grad_f, a->grad_g, a->grad_h);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }

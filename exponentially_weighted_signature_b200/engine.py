@@ -125,7 +125,7 @@ class DiagScan(torch.autograd.Function):
 
 
 class DenseScan(torch.autograd.Function):
-    """Dense engine, uniform clock: (path, M, F, G, H) -> flat EWS (prefix or terminal)."""
+    """Dense engine, uniform clock: (path, D = I - M, F, G, H) -> flat EWS (prefix or terminal)."""
 
     @staticmethod
     def forward(ctx, path, M, F, G, H, readout, flags, chunk, increments):
@@ -148,7 +148,7 @@ class DenseScan(torch.autograd.Function):
         _lib.check(lib.ews_dense_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_dense_workspace_size")
         fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
         a.path = _ptr(path_c)
-        a.tab_m, a.tab_f, a.tab_g, a.tab_h = (_ptr(t) for t in tabs)
+        a.tab_d, a.tab_f, a.tab_g, a.tab_h = (_ptr(t) for t in tabs)
         a.out = _ptr(out)
         a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
         with _timed("ews_dense_fwd", dev, B * T):
@@ -176,9 +176,9 @@ class DenseScan(torch.autograd.Function):
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
         a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, QP - 1, 0
         a.path = _ptr(path)
-        a.tab_m, a.tab_f, a.tab_g, a.tab_h = (_ptr(t) for t in (M, F, G, H))
+        a.tab_d, a.tab_f, a.tab_g, a.tab_h = (_ptr(t) for t in (M, F, G, H))
         a.out, a.grad_out, a.grad_dx = _ptr(out), _ptr(g), _ptr(gdx)
-        a.grad_m, a.grad_f, a.grad_g, a.grad_h = (_ptr(t) for t in (gM, gF, gG, gH))
+        a.grad_d, a.grad_f, a.grad_g, a.grad_h = (_ptr(t) for t in (gM, gF, gG, gH))
         a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fwd_ws.numel()
         a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
         with _timed("ews_dense_bwd", dev, B * T):

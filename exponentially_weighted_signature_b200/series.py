@@ -105,13 +105,13 @@ def diag_tables(x: torch.Tensor, q: int):
 
 def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None):
     """Per-sample tables of the dense engine for generator A (N, N), clock steps h (B,) and lift W (N, d_in):
-    M = expm(-hA), F = K1 W, G_a = P_a W, H_a = K2_a W with P_a = (-hA)^a / a!, K1 = sum_p c_p P_p,
-    K2_a = sum_b c_ab P_b (the series leaf with shared letters, ews/core/series_leaf.py:72-113).
-    Differentiable; evaluated in float64 and returned in float32."""
+    the flow complement D = I - expm(-hA), F = K1 W, G_a = P_a W, H_a = K2_a W with P_a = (-hA)^a / a!,
+    K1 = sum_p c_p P_p, K2_a = sum_b c_ab P_b (the series leaf with shared letters,
+    ews/core/series_leaf.py:72-113). Differentiable; evaluated in float64 and returned in float32."""
     Ad = A.to(torch.float64)
     X = -h.to(torch.float64)[:, None, None] * Ad  # (B, N, N)
-    M = torch.linalg.matrix_exp(X)
     N = A.shape[-1]
+    Dc = torch.eye(N, dtype=torch.float64, device=A.device) - torch.linalg.matrix_exp(X)
     eye = torch.eye(N, dtype=torch.float64, device=A.device).expand_as(X)
     P = [eye]
     for a in range(1, q + 1):
@@ -126,4 +126,4 @@ def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None):
     F = K1 @ W
     G = P @ W
     H = K2 @ W
-    return M.float(), F.float(), G.float(), H.float()
+    return Dc.float(), F.float(), G.float(), H.float()

@@ -130,7 +130,8 @@ int ews_diag_fwd_noalloc(const ews_diag_args* a, ews_stream_t stream);
  * local terms fused. Depth 2, dim <= 32, d_in <= 32, series_q <= 11. With the sample's shared clock step h,
  * P_a = (-hA)^a / a!, K1 = sum_p c_p P_p and K2_a = sum_b c_ab P_b (ews/core/series_leaf.py:45-113), and the
  * lift W, the per-sample tables are
- *   tab_m (B, N, N)          the flow M = expm(-h A)
+ *   tab_d (B, N, N)          the flow complement D = I - expm(-h A) (evaluate it in float64: the engine
+ *                            applies M X as X - D X, so the rounding stays relative to D)
  *   tab_f (B, N, d_in)       F = K1 W            (s1 = F dx)
  *   tab_g (B, q+1, N, d_in)  G_a = P_a W         (s2 = sum_a (G_a dx)(H_a dx)^T)
  *   tab_h (B, q+1, N, d_in)  H_a = K2_a W
@@ -142,14 +143,14 @@ typedef struct ews_dense_args {
     int series_q;
     int spin_limit;
     const void* path;        /* (B, T+1, d_in) knots or (B, T, d_in) increments */
-    const float* tab_m;
+    const float* tab_d;
     const float* tab_f;
     const float* tab_g;
     const float* tab_h;
     float* out;              /* (B, T, 1 + D) prefix or (B, 1 + D) terminal (forward only) */
     const float* grad_out;
     float* grad_dx;          /* (B, T, d_in) */
-    float* grad_m;           /* (B, N, N) */
+    float* grad_d;           /* (B, N, N) */
     float* grad_f;           /* (B, N, d_in) */
     float* grad_g;           /* (B, q+1, N, d_in) */
     float* grad_h;           /* (B, q+1, N, d_in) */

@@ -110,7 +110,7 @@ def test_dense_tables_match_the_series_leaf():
     s2 = torch.einsum("tai,taj->tij", U, V).reshape(3, N * N)
     assert torch.allclose(s1.double(), ref[0], rtol=1e-5, atol=1e-6)
     assert torch.allclose(s2.double(), ref[1], rtol=1e-5, atol=1e-6)
-    assert torch.allclose(M[0].double(), torch.linalg.matrix_exp(-h * A), rtol=1e-6, atol=1e-7)
+    assert torch.allclose(M[0].double(), torch.eye(N, dtype=torch.float64) - torch.linalg.matrix_exp(-h * A), rtol=1e-6, atol=1e-7)
 
 
 def test_diag_tables_gradient_finite_at_zero():
