@@ -184,21 +184,21 @@ __device__ void load_tables(const Params& p, const Smem& s, int b) {
     const Geom& g = p.g;
     const int N = g.N, d = g.d_in;
     const float* m = p.tab_d + (size_t)b * N * N;
-    for (int e = threadIdx.x; e < MM; e += NT) {
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) {
         const int i = e / NP, k = e - i * NP;
         const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
         s.Mr[i * NP + k] = v;
         s.Mt[k * NP + i] = v;
     }
     const float* f = p.tab_f + (size_t)b * N * d;
-    for (int e = threadIdx.x; e < NP * d; e += NT) {
+    for (int e = threadIdx.x; e < NP * d; e += blockDim.x) {
         const int i = e / d;
         s.F[e] = i < N ? f[e - i * d + i * d] : 0.f;
     }
     const size_t gq = (size_t)g.QP * N * d;
     const float* gg = p.tab_g + (size_t)b * gq;
     const float* hh = p.tab_h + (size_t)b * gq;
-    for (int e = threadIdx.x; e < g.QP * NP * d; e += NT) {
+    for (int e = threadIdx.x; e < g.QP * NP * d; e += blockDim.x) {
         const int a = e / (NP * d), r = e - a * NP * d, i = r / d, c = r - i * d;
         const bool ok = i < N;
         s.G[e] = ok ? gg[((size_t)a * N + i) * d + c] : 0.f;
@@ -208,7 +208,7 @@ __device__ void load_tables(const Params& p, const Smem& s, int b) {
 
 __device__ void load_dx(const Params& p, const Smem& s, int b, int t0, int n) {
     const Geom& g = p.g;
-    for (int e = threadIdx.x; e < n * g.d_in; e += NT) {
+    for (int e = threadIdx.x; e < n * g.d_in; e += blockDim.x) {
         const int k = e / g.d_in, c = e - k * g.d_in;
         s.dx[e] = input_increment(p.path, b, t0 + k, c, g.T, g.d_in, g.flags);
     }
@@ -230,7 +230,7 @@ __device__ void local_terms(const Geom& g, const Smem& s, int k) {
         for (int kk = 0; kk < NP; ++kk) acc = fmaf(s.Mt[kk * NP + i], s.S1[kk], acc);
         s.u[i] = s.S1[i] - acc;  // M S1 = S1 - D S1
     }
-    for (int e = tid; e < 2 * g.QP * NP; e += NT) {
+    for (int e = tid; e < 2 * g.QP * NP; e += blockDim.x) {
         const int which = e / (g.QP * NP), r = e - which * g.QP * NP, a = r / NP, i = r - a * NP;
         const float* T = (which == 0 ? s.G : s.H) + ((size_t)a * NP + i) * g.d_in;
         float acc = 0.f;
@@ -289,7 +289,7 @@ __device__ void stage_row(const Geom& g, const Smem& s, float* row, const float 
 // Slot layout (floats): [P row-major (NP*NP) | S1 (NP) | S2 row-major (NP*NP)].
 
 __device__ void store_slot(float* slot, const float* Pr, const float* S1, const float* S2r) {
-    for (int e = threadIdx.x; e < MM; e += NT) {
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) {
         slot[e] = Pr[e];
         slot[MM + NP + e] = S2r[e];
     }
@@ -303,7 +303,7 @@ __device__ void store_slot(float* slot, const float* Pr, const float* S1, const 
 __device__ void chen_mul_smem(const float* PL, const float* L1, const float* L2, const float* PR, const float* R1,
                               const float* R2, float* Po, float* S1o, float* S2o, float* T0, float* T1, float* vtmp,
                               int i0, int j0) {
-    for (int e = threadIdx.x; e < MM; e += NT) {
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) {
         const int i = e / NP, k = e - i * NP;
         T0[k * NP + i] = L2[e];   // L2 k-major
         T1[k * NP + i] = PR[e];   // C_R k-major
@@ -314,38 +314,45 @@ __device__ void chen_mul_smem(const float* PL, const float* L1, const float* L2,
         vtmp[threadIdx.x] = L1[threadIdx.x] - acc;  // P_R L1
     }
     __syncthreads();
+    const bool act = threadIdx.x < NT;  // 4x4 blocks of the first 64 threads cover the 32x32 matrices
     float L2b[4][4], CLb[4][4], CRb[4][4];
-    load_rowmajor(L2, L2b, i0, j0);
-    load_rowmajor(PL, CLb, i0, j0);
-    load_rowmajor(PR, CRb, i0, j0);
     float X[4][4], Y[4][4], P[4][4];
-    gemm44(T0, T1, X, i0, j0, false);  // L2 C_R^T
-    gemm44(T1, PL, P, i0, j0, false);  // C_R C_L
+    if (act) {
+        load_rowmajor(L2, L2b, i0, j0);
+        load_rowmajor(PL, CLb, i0, j0);
+        load_rowmajor(PR, CRb, i0, j0);
+        gemm44(T0, T1, X, i0, j0, false);  // L2 C_R^T
+        gemm44(T1, PL, P, i0, j0, false);  // C_R C_L
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            X[r][c] = L2b[r][c] - X[r][c];                  // X = L2 P_R^T
-            P[r][c] = CLb[r][c] + CRb[r][c] - P[r][c];      // complement of P_R P_L
-        }
+            for (int c = 0; c < 4; ++c) {
+                X[r][c] = L2b[r][c] - X[r][c];                  // X = L2 P_R^T
+                P[r][c] = CLb[r][c] + CRb[r][c] - P[r][c];      // complement of P_R P_L
+            }
+    }
     __syncthreads();
-    store_rowmajor(T0, X, i0, j0);
+    if (act) store_rowmajor(T0, X, i0, j0);
     __syncthreads();
-    gemm44(T1, T0, Y, i0, j0, false);  // C_R X
+    if (act) {
+        gemm44(T1, T0, Y, i0, j0, false);  // C_R X
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-            Y[r][c] = (X[r][c] - Y[r][c]) + fmaf(vtmp[i0 + r], R1[j0 + c], R2[(i0 + r) * NP + j0 + c]);
+            for (int c = 0; c < 4; ++c)
+                Y[r][c] = (X[r][c] - Y[r][c]) + fmaf(vtmp[i0 + r], R1[j0 + c], R2[(i0 + r) * NP + j0 + c]);
+    }
     __syncthreads();
-    store_rowmajor(S2o, Y, i0, j0);
-    store_rowmajor(Po, P, i0, j0);
+    if (act) {
+        store_rowmajor(S2o, Y, i0, j0);
+        store_rowmajor(Po, P, i0, j0);
+    }
     if (threadIdx.x < NP) S1o[threadIdx.x] = vtmp[threadIdx.x] + R1[threadIdx.x];
     __syncthreads();
 }
 
 __device__ void load_slot_smem(const float* slot, float* P, float* S1, float* S2) {
-    for (int e = threadIdx.x; e < MM; e += NT) {
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) {
         P[e] = ldcg(slot + e);
         S2[e] = ldcg(slot + MM + NP + e);
     }
@@ -353,7 +360,7 @@ __device__ void load_slot_smem(const float* slot, float* P, float* S1, float* S2
 }
 
 __device__ void identity_smem(float* P, float* S1, float* S2) {
-    for (int e = threadIdx.x; e < MM; e += NT) {
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) {
         P[e] = 0.f;  // flow complement of the identity
         S2[e] = 0.f;
     }
@@ -419,7 +426,7 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
         if (threadIdx.x < NP) s.v0[threadIdx.x] = s.S1[threadIdx.x];
         {
             // R = 0 (identity); base = D (row-major in A4, k-major in A5)
-            for (int e = threadIdx.x; e < MM; e += NT) {
+            for (int e = threadIdx.x; e < MM; e += blockDim.x) {
                 s.A2[e] = 0.f;
                 s.A4[e] = s.Mr[e];
                 s.A5[e] = s.Mt[e];
@@ -521,6 +528,595 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
             }
         }
     }
+}
+
+// ---------------------------------------------------------------------------------- forward on tcgen05
+//
+// The flow products run on the 5th-generation tensor cores. A CTA of 4 warps stacks 4 consecutive chunks of
+// one sample (tile t = warp t); the two products of a step are single tcgen05.mma chains with M = 128 (the
+// 4 stacked 32-row tiles), N = 32, K = 32, in 3xTF32 (hi/lo splits, K-concatenated: a_hi b_hi + a_hi b_lo +
+// a_lo b_hi), accumulated in TMEM:
+//     P1 = S2 D^T        (A = S2, MN-major, written column by column)   -> X  = S2 - P1       (rows)
+//     P2 = (D X)^T       (A = X^T, MN-major, written row by row)        -> MX = X - P2^T      (columns)
+// The identity parts are exact fp32 subtractions on the CUDA cores, so the flow keeps its complement form.
+// After MMA1 lane i of warp t owns row i of tile t (TMEM lane 32t+i), after MMA2 it owns column i; both A
+// operands are therefore written MN-major with 16-byte stores, and the missing orientation comes through a
+// padded 33-stride buffer. One elected thread issues the MMAs and commits them to an mbarrier; the
+// waits are bounded.
+
+namespace tc {
+
+constexpr int TILES = 4;
+constexpr int NTH = 128;
+constexpr int RQS = 33;  // padded row stride of the row/column exchange buffer
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint32_t tf32_bits(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+// SM100 shared-memory matrix descriptor, no swizzle (start, leading / stride byte offsets, version 1).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    return d;
+}
+
+// Instruction descriptor: kind::tf32, f32 accumulator, A MN-major, B K-major, M = 128, N = 32.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 15) | (0u << 16) | ((32u >> 3) << 17) |
+                            ((128u >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t"
+        ".reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t"
+        "}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,"
+        "%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Offsets (floats) of the canonical no-swizzle layouts: B K-major (N = 32 rows, K = 32), core matrices of
+// 8 rows x 16 bytes, [k/4][n/8][n%8][k%4]  (SBO 128 B between row groups, LBO 512 B between K chunks);
+// A MN-major (M = 128, K = 32), core matrices of 4 columns x 8 K rows, [k/8][m/4][k%8][m%4]
+// (SBO 128 B between column groups, LBO 4096 B between K groups).
+__device__ __forceinline__ int bk_off(int n, int k) { return (((k >> 2) * 4 + (n >> 3)) * 32) + (n & 7) * 4 + (k & 3); }
+__device__ __forceinline__ int amn_off4(int m4, int k) { return ((k >> 3) * 32 + m4) * 32 + (k & 7) * 4; }
+
+struct TcSmem {
+    float* Bhi;   // D hi, K-major (MM)
+    float* Blo;   // D lo
+    float* Ahi;   // A operand hi, MN-major (4 MM); also look-back scratch
+    float* Alo;   // A operand lo
+    float* RQ;    // TILES x 32 x RQS exchange buffer
+    float* stage; // TILES x W prefix rows; also look-back scratch (>= 2 MM)
+    float* Dr;    // D row-major
+    float* Dt;    // D k-major
+    float* F;     // NP x d_in
+    float* G;     // QP x NP x d_in
+    float* H;
+    float* vec;   // per tile: S1, u, s1, x(d_in) | U, V (NP x QMAX each)
+    float* misc;  // small vectors for the look-back
+    uint64_t* bar;
+    uint32_t* tmem;
+    int* bcast;
+};
+
+constexpr int kVecPerTile = 3 * NP + 32 + 2 * NP * QMAX;
+
+__host__ __device__ inline int tc_stage_floats(int W) { return imax(TILES * W, 2 * MM); }
+
+__host__ __device__ inline size_t tc_smem_bytes(int W, int d_in, int QP) {
+    size_t f = 2 * MM + 2 * 4 * MM + TILES * 32 * RQS + align4(tc_stage_floats(W)) + 2 * MM + align4(NP * d_in) +
+               2 * align4(QP * NP * d_in) + TILES * kVecPerTile + 4 * NP;
+    return f * sizeof(float) + 64 + 128;  // + barrier / tmem slot / broadcast, + alignment slack
+}
+
+__device__ TcSmem tc_carve(unsigned char* raw, const Geom& g) {
+    uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 127) & ~(uintptr_t)127;
+    float* p = reinterpret_cast<float*>(base);
+    TcSmem s;
+    s.Bhi = p; p += MM;
+    s.Blo = p; p += MM;
+    s.Ahi = p; p += 4 * MM;
+    s.Alo = p; p += 4 * MM;
+    s.RQ = p; p += TILES * 32 * RQS;
+    s.stage = p; p += align4(tc_stage_floats(g.W));
+    s.Dr = p; p += MM;
+    s.Dt = p; p += MM;
+    s.F = p; p += align4(NP * g.d_in);
+    s.G = p; p += align4(g.QP * NP * g.d_in);
+    s.H = p; p += align4(g.QP * NP * g.d_in);
+    s.vec = p; p += TILES * kVecPerTile;
+    s.misc = p; p += 4 * NP;
+    s.bar = reinterpret_cast<uint64_t*>(p);
+    s.tmem = reinterpret_cast<uint32_t*>(p + 2);
+    s.bcast = reinterpret_cast<int*>(p + 4);
+    return s;
+}
+
+__device__ void tc_load_tables(const Params& p, const TcSmem& s, int b) {
+    const Geom& g = p.g;
+    const int N = g.N, d = g.d_in;
+    const float* m = p.tab_d + (size_t)b * N * N;
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) {
+        const int i = e / NP, k = e - i * NP;
+        const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
+        s.Dr[i * NP + k] = v;
+        s.Dt[k * NP + i] = v;
+        const float hi = __uint_as_float(tf32_bits(v));
+        s.Bhi[bk_off(i, k)] = hi;
+        s.Blo[bk_off(i, k)] = v - hi;
+    }
+    const float* f = p.tab_f + (size_t)b * N * d;
+    for (int e = threadIdx.x; e < NP * d; e += blockDim.x) s.F[e] = (e / d) < N ? f[e] : 0.f;
+    const size_t gq = (size_t)g.QP * N * d;
+    const float* gg = p.tab_g + (size_t)b * gq;
+    const float* hh = p.tab_h + (size_t)b * gq;
+    for (int e = threadIdx.x; e < g.QP * NP * d; e += blockDim.x) {
+        const int a = e / (NP * d), r = e - a * NP * d, i = r / d, c = r - i * d;
+        const bool ok = i < N;
+        s.G[e] = ok ? gg[((size_t)a * N + i) * d + c] : 0.f;
+        s.H[e] = ok ? hh[((size_t)a * N + i) * d + c] : 0.f;
+    }
+}
+
+// Per-tile vectors of a step (warp-local): x = dx_t, s1 = F x, U = [G_a x], V = [H_a x], u = S1 - D S1.
+__device__ void tc_local(const Params& p, const TcSmem& s, float* v, int b, int t_abs, bool valid) {
+    const Geom& g = p.g;
+    const int l = threadIdx.x & 31;
+    float* S1 = v;
+    float* u = v + NP;
+    float* s1 = v + 2 * NP;
+    float* x = v + 3 * NP;
+    float* U = v + 3 * NP + 32;
+    float* V = U + NP * QMAX;
+    if (l < g.d_in) x[l] = valid ? input_increment(p.path, b, t_abs, l, g.T, g.d_in, g.flags) : 0.f;
+    __syncwarp();
+    float acc = 0.f;
+    for (int c = 0; c < g.d_in; ++c) acc = fmaf(s.F[l * g.d_in + c], x[c], acc);
+    s1[l] = acc;
+    for (int a = 0; a < g.QP; ++a) {
+        const float* Ga = s.G + ((size_t)a * NP + l) * g.d_in;
+        const float* Ha = s.H + ((size_t)a * NP + l) * g.d_in;
+        float ga = 0.f, ha = 0.f;
+        for (int c = 0; c < g.d_in; ++c) {
+            ga = fmaf(Ga[c], x[c], ga);
+            ha = fmaf(Ha[c], x[c], ha);
+        }
+        U[l * QMAX + a] = ga;
+        V[l * QMAX + a] = ha;
+    }
+    float du = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < NP; ++k) du = fmaf(s.Dt[k * NP + l], S1[k], du);
+    u[l] = S1[l] - du;
+    __syncwarp();
+}
+
+// CTA-uniform bounded wait for the MMA commit of the given parity. Returns false on timeout.
+__device__ bool tc_wait(const TcSmem& s, uint32_t parity, int limit) {
+    if (threadIdx.x == 0) {
+        int ok = 0;
+        for (int it = 0; it < limit; ++it) {
+            if (mbar_try(s.bar, parity)) {
+                ok = 1;
+                break;
+            }
+        }
+        s.bcast[1] = ok;
+    }
+    __syncthreads();
+    const bool ok = s.bcast[1] != 0;
+    fence_after();
+    return ok;
+}
+
+__device__ int tc_cta_wait(const Params& p, const TcSmem& s, const int* flag, int want, int tile) {
+    if (threadIdx.x < 32) {
+        const int v = wait_slot(flag, p.st, p.g.spin_limit, tile, want);
+        if (threadIdx.x == 0) s.bcast[2] = v;
+    }
+    __syncthreads();
+    const int v = s.bcast[2];
+    __threadfence();
+    __syncthreads();
+    return v;
+}
+
+}  // namespace tc
+
+__global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
+    using namespace tc;
+    extern __shared__ unsigned char smem_raw[];
+    const Geom& g = p.g;
+    TcSmem s = tc_carve(smem_raw, g);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int bi = tid >> 3, bj = tid & 7;  // 4x4 blocks of the first 64 threads (look-back products)
+    const int i0 = 4 * (bi & 7), j0 = 4 * bj;
+    const bool deterministic = (g.flags & EWS_F_DETERMINISTIC) != 0;
+    const int N = g.N;
+    const int mbar_limit = 1 << 20;
+
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(s.bar)), "r"(1));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s.tmem)),
+                     "r"(64));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *s.tmem;
+    const uint32_t tP1 = tmem, tP2 = tmem + 32;
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    uint32_t phase = 0;
+    bool failed = false;
+    bool mma_pending = false;  // an MMA commit of `phase` may still be outstanding after a failed wait
+
+    const uint64_t dA_hi = smem_desc(smem_u32(s.Ahi), 4096, 128), dA_lo = smem_desc(smem_u32(s.Alo), 4096, 128);
+    const uint64_t dB_hi = smem_desc(smem_u32(s.Bhi), 512, 128), dB_lo = smem_desc(smem_u32(s.Blo), 512, 128);
+    const int groups = (g.C + TILES - 1) / TILES;
+    const int ntiles = g.B * groups;
+    float* vt = s.vec + warp * kVecPerTile;  // this warp's tile vectors
+    float* RQt = s.RQ + warp * 32 * RQS;
+
+    for (;;) {
+        if (tid == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
+        __syncthreads();
+        const int tile = s.bcast[0];
+        __syncthreads();
+        if (tile >= ntiles) break;
+        const int grp = tile / g.B, b = tile - grp * g.B;
+        const int c_me = grp * TILES + warp;
+        const bool valid_me = c_me < g.C;
+        const int t0_me = c_me * g.Lc;
+        const int len_me = valid_me ? min(g.Lc, g.T - t0_me) : 0;
+        int steps = 0;
+        for (int t = 0; t < TILES; ++t) {
+            const int c = grp * TILES + t;
+            if (c < g.C) steps = max(steps, min(g.Lc, g.T - c * g.Lc));
+        }
+        tc_load_tables(p, s, b);
+        __syncthreads();
+
+        float col[32];
+        for (int pass = 0; pass < 2 && !failed; ++pass) {
+            // ---- initial state: identity (pass 1) or the chunk's carry (pass 2)
+            if (pass == 0) {
+#pragma unroll
+                for (int n = 0; n < 32; ++n) col[n] = 0.f;
+                vt[lane] = 0.f;
+            } else {
+                const float* cs = p.carry + ((size_t)b * g.C + (valid_me ? c_me : 0)) * g.SW;
+#pragma unroll
+                for (int n = 0; n < 32; ++n) col[n] = valid_me ? ldcg(cs + MM + NP + n * NP + lane) : 0.f;
+                vt[lane] = valid_me ? ldcg(cs + MM + lane) : 0.f;
+            }
+            __syncwarp();
+            for (int k = 0; k < steps; ++k) {
+                const bool live = k < len_me;
+                // E0: A operand (S2 by columns, MN-major hi/lo) and the exchange buffer
+#pragma unroll
+                for (int nq = 0; nq < 8; ++nq) {
+                    float h[4], lo[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        h[q] = __uint_as_float(tf32_bits(col[4 * nq + q]));
+                        lo[q] = col[4 * nq + q] - h[q];
+                        RQt[(4 * nq + q) * RQS + lane] = col[4 * nq + q];
+                    }
+                    const int off = amn_off4(8 * warp + nq, lane);
+                    *reinterpret_cast<float4*>(s.Ahi + off) = make_float4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<float4*>(s.Alo + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                }
+                fence_proxy_async();
+                fence_before();
+                __syncthreads();
+                if (tid == 0) {
+                    fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
+                    mma_commit(s.bar);
+                }
+                // local terms of this step while the tensor core runs
+                tc_local(p, s, vt, b, t0_me + k, live);
+                if (!tc_wait(s, phase, mbar_limit)) {
+                    failed = mma_pending = true;
+                    break;
+                }
+                phase ^= 1;
+                // E1: row `lane` of X = S2 - S2 D^T; A operand for the second product (X by rows)
+                {
+                    float pr[32];
+                    tmem_ld32(tP1 + lane_off, pr);
+#pragma unroll
+                    for (int n = 0; n < 32; ++n) pr[n] = RQt[lane * RQS + n] - pr[n];
+#pragma unroll
+                    for (int nq = 0; nq < 8; ++nq) {
+                        float h[4], lo[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            h[q] = __uint_as_float(tf32_bits(pr[4 * nq + q]));
+                            lo[q] = pr[4 * nq + q] - h[q];
+                            RQt[lane * RQS + 4 * nq + q] = pr[4 * nq + q];
+                        }
+                        const int off = amn_off4(8 * warp + nq, lane);
+                        *reinterpret_cast<float4*>(s.Ahi + off) = make_float4(h[0], h[1], h[2], h[3]);
+                        *reinterpret_cast<float4*>(s.Alo + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                    }
+                }
+                fence_proxy_async();
+                fence_before();
+                __syncthreads();
+                if (tid == 0) {
+                    fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
+                    mma_commit(s.bar);
+                }
+                if (!tc_wait(s, phase, mbar_limit)) {
+                    failed = mma_pending = true;
+                    break;
+                }
+                phase ^= 1;
+                // E2: column `lane` of M X + u s1^T + U V^T
+                {
+                    float q2[32];
+                    tmem_ld32(tP2 + lane_off, q2);
+                    const float* u = vt + NP;
+                    const float* s1 = vt + 2 * NP;
+                    const float* U = vt + 3 * NP + 32;
+                    const float* V = U + NP * QMAX;
+                    const float s1l = s1[lane];
+                    float nc[32];
+#pragma unroll
+                    for (int n = 0; n < 32; ++n) {
+                        float acc = fmaf(u[n], s1l, RQt[n * RQS + lane] - q2[n]);
+                        for (int a = 0; a < g.QP; ++a) acc = fmaf(U[n * QMAX + a], V[lane * QMAX + a], acc);
+                        nc[n] = acc;
+                    }
+                    const float s1new = u[lane] + s1l;
+                    __syncwarp();
+                    if (live) {
+#pragma unroll
+                        for (int n = 0; n < 32; ++n) col[n] = nc[n];
+                        vt[lane] = s1new;
+                    }
+                    fence_before();
+                    __syncwarp();
+                    if (pass == 1 && live && g.readout == EWS_READOUT_PREFIX) {
+                        float* row = s.stage + warp * g.W;
+                        if (lane == 0) row[0] = 1.f;
+                        if (lane < N) {
+                            row[1 + lane] = vt[lane];
+#pragma unroll
+                            for (int n = 0; n < 32; ++n)
+                                if (n < N) row[1 + N + n * N + lane] = col[n];
+                        }
+                        __syncwarp();
+                        warp_store_span(p.out + ((size_t)b * g.T + t0_me + k) * g.W, row, g.W);
+                        __syncwarp();
+                    }
+                }
+            }
+            if (failed) break;
+            __syncthreads();
+            if (pass == 1) break;
+            // ---- aggregates of the 4 chunks (flow complement, S1, S2) -> agg slots
+            if (valid_me) {
+                float* as = p.agg + ((size_t)b * g.C + c_me) * g.SW;
+#pragma unroll
+                for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = col[n];
+                as[MM + lane] = vt[lane];
+            }
+            // flow complements C(len) for the full and the (possibly) short chunk, by powering complements
+            float* W0 = s.Ahi;            // scratch matrices live in the idle operand buffers
+            float* W1 = s.Ahi + MM;
+            float* W2 = s.Ahi + 2 * MM;
+            float* W3 = s.Ahi + 3 * MM;
+            float* W4 = s.Alo;
+            float* W5 = s.Alo + MM;
+            float* W6 = s.Alo + 2 * MM;   // C(Lc) row-major
+            float* W7 = s.Alo + 3 * MM;   // C(last) row-major
+            for (int which = 0; which < 2; ++which) {
+                const int e_len = which == 0 ? g.Lc : g.T - (g.C - 1) * g.Lc;
+                float* R = which == 0 ? W6 : W7;
+                for (int e = tid; e < MM; e += blockDim.x) {
+                    R[e] = 0.f;
+                    W0[e] = s.Dr[e];
+                    W1[e] = s.Dt[e];
+                }
+                __syncthreads();
+                int e = e_len;
+                while (e > 0) {
+                    float blk[4][4], Rb[4][4], Bb[4][4];
+                    const bool act = tid < NT;
+                    if (act) load_rowmajor(W0, Bb, i0, j0);
+                    if (e & 1) {
+                        if (act) {
+                            load_rowmajor(R, Rb, i0, j0);
+                            gemm44(W1, R, blk, i0, j0, false);
+                        }
+                        __syncthreads();
+                        if (act) {
+#pragma unroll
+                            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) blk[r][q] = Rb[r][q] + Bb[r][q] - blk[r][q];
+                            store_rowmajor(R, blk, i0, j0);
+                        }
+                        __syncthreads();
+                    }
+                    e >>= 1;
+                    if (e > 0) {
+                        if (act) gemm44(W1, W0, blk, i0, j0, false);
+                        __syncthreads();
+                        if (act) {
+#pragma unroll
+                            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) blk[r][q] = 2.f * Bb[r][q] - blk[r][q];
+                            store_rowmajor(W0, blk, i0, j0);
+                            store_kmajor(W1, blk, i0, j0);
+                        }
+                        __syncthreads();
+                    }
+                }
+            }
+            for (int t = 0; t < TILES; ++t) {
+                const int c = grp * TILES + t;
+                if (c >= g.C) break;
+                const float* C = (c == g.C - 1) ? W7 : W6;
+                float* as = p.agg + ((size_t)b * g.C + c) * g.SW;
+                for (int e = tid; e < MM; e += blockDim.x) as[e] = C[e];
+            }
+            __syncthreads();
+            // publish the aggregates (the first chunk of the sequence publishes its inclusive value)
+            for (int t = 0; t < TILES; ++t) {
+                const int c = grp * TILES + t;
+                if (c >= g.C) break;
+                if (c == 0) {
+                    float* is = p.incl + (size_t)b * g.C * g.SW;
+                    const float* as = p.agg + (size_t)b * g.C * g.SW;
+                    for (int e = tid; e < g.SW; e += blockDim.x) is[e] = as[e];
+                    __syncthreads();
+                    if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(p.flags + (size_t)b * g.C, kFlagIncl);
+                } else {
+                    cta_publish(p.flags + (size_t)b * g.C + c, kFlagAgg);
+                }
+                __syncthreads();
+            }
+            // ---- carries: look back for the group's first chunk, then fold the group's own aggregates
+            float* ve = s.misc;           // excl S1
+            float* va = s.misc + NP;      // acc / scratch S1
+            float* vx = s.misc + 2 * NP;  // loaded S1
+            float* vtmp = s.misc + 3 * NP;
+            float* T0 = s.stage;
+            float* T1 = s.stage + MM;
+            // excl -> (W2 C, ve S1, W3 S2)
+            identity_smem(W2, ve, W3);
+            __syncthreads();
+            const int c_first = grp * TILES;
+            if (c_first > 0) {
+                identity_smem(W4, va, W5);  // acc
+                __syncthreads();
+                int j = c_first - 1;
+                for (;;) {
+                    const int f = tc_cta_wait(p, s, p.flags + (size_t)b * g.C + j, deterministic ? kFlagIncl : kFlagAgg, tile);
+                    if (f < 0) {
+                        failed = true;
+                        break;
+                    }
+                    const size_t sj = ((size_t)b * g.C + j) * g.SW;
+                    load_slot_smem((f == kFlagIncl ? p.incl : p.agg) + sj, W0, vx, W1);
+                    __syncthreads();
+                    chen_mul_smem(W0, vx, W1, W4, va, W5, W4, va, W5, T0, T1, vtmp, i0, j0);  // acc = X (x) acc
+                    if (f == kFlagIncl) break;
+                    --j;
+                }
+                if (failed) break;
+                for (int e = tid; e < MM; e += blockDim.x) {
+                    W2[e] = W4[e];
+                    W3[e] = W5[e];
+                }
+                if (tid < NP) ve[tid] = va[tid];
+                __syncthreads();
+            }
+            for (int t = 0; t < TILES; ++t) {
+                const int c = c_first + t;
+                if (c >= g.C) break;
+                const size_t sc = ((size_t)b * g.C + c) * g.SW;
+                store_slot(p.carry + sc, W2, ve, W3);
+                // incl_c = excl (x) agg_c
+                load_slot_smem(p.agg + sc, W0, vx, W1);
+                __syncthreads();
+                chen_mul_smem(W2, ve, W3, W0, vx, W1, W2, ve, W3, T0, T1, vtmp, i0, j0);
+                if (c > 0) {
+                    store_slot(p.incl + sc, W2, ve, W3);
+                    cta_publish(p.flags + (size_t)b * g.C + c, kFlagIncl);
+                }
+                __syncthreads();
+                if (c == g.C - 1 && g.readout == EWS_READOUT_TERMINAL) {
+                    float* row = s.stage;
+                    if (tid == 0) row[0] = 1.f;
+                    for (int e = tid; e < N; e += blockDim.x) row[1 + e] = ve[e];
+                    for (int e = tid; e < N * N; e += blockDim.x) row[1 + N + e] = W3[(e / N) * NP + (e % N)];
+                    __syncthreads();
+                    if (warp == 0) warp_store_span(p.out + (size_t)b * g.W, row, g.W);
+                    __syncthreads();
+                }
+            }
+            __syncthreads();
+            if (g.readout == EWS_READOUT_TERMINAL) break;
+        }
+        if (failed) break;
+    }
+    // every exit drains the tensor core and frees TMEM
+    if (failed && tid == 0) {
+        if (atomicCAS(&p.st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) p.st->err_tile = -1;
+        if (mma_pending)
+            for (int it = 0; it < (1 << 20); ++it)
+                if (mbar_try(s.bar, phase)) break;
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64));
 }
 
 // ---------------------------------------------------------------------------------- backward
@@ -643,11 +1239,11 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
         __syncthreads();
         {
             float* dst = (c == g.C - 1 ? p.incl : p.agg) + slot;
-            for (int e = threadIdx.x; e < MM; e += NT) dst[MM + NP + e] = s.A1[e];
+            for (int e = threadIdx.x; e < MM; e += blockDim.x) dst[MM + NP + e] = s.A1[e];
             if (threadIdx.x < NP) dst[MM + threadIdx.x] = L1[threadIdx.x];
         }
         // ---- 2. look-back over later chunks: Lam_in (L1 in s.u, L2 row-major in s.A4)
-        for (int e = threadIdx.x; e < MM; e += NT) s.A4[e] = 0.f;
+        for (int e = threadIdx.x; e < MM; e += blockDim.x) s.A4[e] = 0.f;
         if (threadIdx.x < NP) s.u[threadIdx.x] = 0.f;
         if (c == g.C - 1) {
             if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(flag, kFlagIncl);
@@ -666,7 +1262,7 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
                 // X (cotangent) -> (s1 L1, A1 L2 row-major), then X <- J(Gacc)^T X, acc += X
                 {
                     const float* src = (f == kFlagIncl ? p.incl : p.agg) + sj;
-                    for (int e = threadIdx.x; e < MM; e += NT) s.A1[e] = ldcg(src + MM + NP + e);
+                    for (int e = threadIdx.x; e < MM; e += blockDim.x) s.A1[e] = ldcg(src + MM + NP + e);
                     if (threadIdx.x < NP) s.s1[threadIdx.x] = ldcg(src + MM + threadIdx.x);
                 }
                 __syncthreads();
@@ -674,7 +1270,7 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
                 load_rowmajor(s.A1, X2, i0, j0);
                 __syncthreads();
                 apply_JT_smem(s.A5, s.v0, s.s1, X2, s.A1, s.A2, s.A3, s.stage, i0, j0);
-                for (int e = threadIdx.x; e < MM; e += NT) s.A4[e] += s.A1[e];
+                for (int e = threadIdx.x; e < MM; e += blockDim.x) s.A4[e] += s.A1[e];
                 if (threadIdx.x < NP) s.u[threadIdx.x] += s.s1[threadIdx.x];
                 __syncthreads();
                 if (f == kFlagIncl) break;
@@ -689,14 +1285,14 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
             __syncthreads();
             float X2[4][4];
             load_rowmajor(s.A4, X2, i0, j0);
-            for (int e = threadIdx.x; e < MM; e += NT) s.A3[e] = s.A4[e];
+            for (int e = threadIdx.x; e < MM; e += blockDim.x) s.A3[e] = s.A4[e];
             if (threadIdx.x < NP) s.v0[threadIdx.x] = s.u[threadIdx.x];
             __syncthreads();
             apply_JT_smem(s.A1, s.s1, s.v0, X2, s.A3, s.A5, s.A0, s.stage, i0, j0);
             {
                 float* dst = p.incl + slot;
                 const float* mu = p.agg + slot;
-                for (int e = threadIdx.x; e < MM; e += NT) dst[MM + NP + e] = s.A3[e] + ldcg(mu + MM + NP + e);
+                for (int e = threadIdx.x; e < MM; e += blockDim.x) dst[MM + NP + e] = s.A3[e] + ldcg(mu + MM + NP + e);
                 if (threadIdx.x < NP) dst[MM + threadIdx.x] = s.v0[threadIdx.x] + ldcg(mu + MM + threadIdx.x);
             }
             cta_publish(flag, kFlagIncl);
@@ -707,7 +1303,7 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
         load_rowmajor(s.A4, L2, i0, j0);
         if (threadIdx.x < NP) L1[threadIdx.x] = s.u[threadIdx.x];
         const int tabn = (1 + 2 * g.QP) * NP * g.d_in;
-        for (int e = threadIdx.x; e < tabn; e += NT) s.tacc[e] = 0.f;
+        for (int e = threadIdx.x; e < tabn; e += blockDim.x) s.tacc[e] = 0.f;
         __syncthreads();
         float dM[4][4];
 #pragma unroll
@@ -795,7 +1391,7 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
                     for (int q = 0; q < 4; ++q) dM[r][q] = fmaf(du[i0 + r], s.S1[j0 + q], dM[r][q]);
                 // (5) table gradients: dF += ds1 dx^T, dG_a += dU_a dx^T, dH_a += dV_a dx^T
                 const float* x = s.dx + k * g.d_in;
-                for (int e = threadIdx.x; e < tabn; e += NT) {
+                for (int e = threadIdx.x; e < tabn; e += blockDim.x) {
                     const int blk = e / (NP * g.d_in), rem = e - blk * NP * g.d_in, i = rem / g.d_in, cc = rem - i * g.d_in;
                     const float coef = blk == 0 ? ds1[i] : (blk <= g.QP ? dU[i * QMAX + blk - 1] : dV[i * QMAX + blk - 1 - g.QP]);
                     s.tacc[e] = fmaf(coef, x[cc], s.tacc[e]);
@@ -835,7 +1431,7 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
         for (int r = 0; r < 4; ++r)
 #pragma unroll
             for (int q = 0; q < 4; ++q) part[(i0 + r) * NP + j0 + q] = dM[r][q];
-        for (int e = threadIdx.x; e < tabn; e += NT) part[MM + e] = s.tacc[e];
+        for (int e = threadIdx.x; e < tabn; e += blockDim.x) part[MM + e] = s.tacc[e];
         __syncthreads();
     }
 }
@@ -891,9 +1487,10 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
     if (a->chunk > 0) {
         g->Lc = a->chunk;
     } else {
-        const int want = 148 * 8;
-        int C = (want + g->B - 1) / g->B;
-        int Lc = (g->T + C - 1) / C;
+        // the forward stacks 4 chunks of a sample per CTA (2 CTAs per SM): aim for one wave of groups
+        const int groups = std::max(1, (2 * 148) / g->B);
+        const int C = 4 * groups;
+        const int Lc = (g->T + C - 1) / C;
         g->Lc = std::max(16, std::min(256, Lc));
     }
     g->C = (g->T + g->Lc - 1) / g->Lc;
@@ -1008,7 +1605,17 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     p.agg = (float*)(ws + L.agg);
     p.incl = (float*)(ws + L.incl);
     p.carry = (float*)(ws + L.carry);
-    return launch(fwd_kernel, p, sizeof(float) * g.smem_floats, s);
+    const size_t smem = tc::tc_smem_bytes(g.W, g.d_in, g.QP);
+    if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+    cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_tc_kernel, tc::NTH, smem);
+    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
+    const int groups = (g.C + tc::TILES - 1) / tc::TILES;
+    int grid = per_sm * num_sms();
+    if (grid > g.B * groups) grid = g.B * groups;
+    fwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 
 extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
