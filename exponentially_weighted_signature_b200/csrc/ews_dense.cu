@@ -539,10 +539,10 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
 //     P1 = S2 D^T        (A = S2, MN-major, written column by column)   -> X  = S2 - P1       (rows)
 //     P2 = (D X)^T       (A = X^T, MN-major, written row by row)        -> MX = X - P2^T      (columns)
 // The identity parts are exact fp32 subtractions on the CUDA cores, so the flow keeps its complement form.
-// After MMA1 lane i of warp t owns row i of tile t (TMEM lane 32t+i), after MMA2 it owns column i; both A
-// operands are therefore written MN-major with 16-byte stores, and the missing orientation comes through a
-// padded 33-stride buffer. One elected thread issues the MMAs and commits them to an mbarrier; the
-// waits are bounded.
+// After MMA1 lane i of warp t owns row i of tile t (TMEM lane 32t+i), after MMA2 it owns column i. Both A
+// operands are K-major (a row of A per lane, 16-byte stores); the orientation a lane needs next comes
+// through a warp-private padded 33-stride buffer (conflict-free by rows and by columns). One elected
+// thread issues the MMAs and commits them to an mbarrier; the waits are bounded.
 
 namespace tc {
 
@@ -568,8 +568,8 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     return d;
 }
 
-// Instruction descriptor: kind::tf32, f32 accumulator, A MN-major, B K-major, M = 128, N = 32.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 15) | (0u << 16) | ((32u >> 3) << 17) |
+// Instruction descriptor: kind::tf32, f32 accumulator, A and B K-major, M = 128, N = 32.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (0u << 16) | ((32u >> 3) << 17) |
                             ((128u >> 4) << 24);
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
@@ -619,17 +619,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Offsets (floats) of the canonical no-swizzle layouts: B K-major (N = 32 rows, K = 32), core matrices of
-// 8 rows x 16 bytes, [k/4][n/8][n%8][k%4]  (SBO 128 B between row groups, LBO 512 B between K chunks);
-// A MN-major (M = 128, K = 32), core matrices of 4 columns x 8 K rows, [k/8][m/4][k%8][m%4]
-// (SBO 128 B between column groups, LBO 4096 B between K groups).
+// Offsets (floats) of the canonical no-swizzle K-major layouts, core matrices of 8 rows x 16 bytes:
+// B (N = 32 rows, K = 32): [k/4][n/8][n%8][k%4]  (SBO 128 B between row groups, LBO 512 B between K chunks);
+// A (M = 128 rows, K = 32): [k/4][m/8][m%8][k%4] (SBO 128 B, LBO 2048 B); one K-step of 8 spans two chunks.
 __device__ __forceinline__ int bk_off(int n, int k) { return (((k >> 2) * 4 + (n >> 3)) * 32) + (n & 7) * 4 + (k & 3); }
-__device__ __forceinline__ int amn_off4(int m4, int k) { return ((k >> 3) * 32 + m4) * 32 + (k & 7) * 4; }
+__device__ __forceinline__ int ak_off4(int m, int kc) { return (kc * 16 + (m >> 3)) * 32 + (m & 7) * 4; }
+
+// Writes row m of a K-major A operand as tf32 hi / lo pieces (16-byte stores).
+__device__ __forceinline__ void store_a_row(float* Ahi, float* Alo, int m, const float v[32]) {
+#pragma unroll
+    for (int kc = 0; kc < 8; ++kc) {
+        float h[4], lo[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            h[q] = __uint_as_float(tf32_bits(v[4 * kc + q]));
+            lo[q] = v[4 * kc + q] - h[q];
+        }
+        const int off = ak_off4(m, kc);
+        *reinterpret_cast<float4*>(Ahi + off) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4*>(Alo + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
 
 struct TcSmem {
     float* Bhi;   // D hi, K-major (MM)
     float* Blo;   // D lo
-    float* Ahi;   // A operand hi, MN-major (4 MM); also look-back scratch
+    float* Ahi;   // A operand hi, K-major (4 MM); also look-back scratch
     float* Alo;   // A operand lo
     float* RQ;    // TILES x 32 x RQS exchange buffer
     float* stage; // TILES x W prefix rows; also look-back scratch (>= 2 MM)
@@ -647,7 +662,9 @@ struct TcSmem {
 
 constexpr int kVecPerTile = 3 * NP + 32 + 2 * NP * QMAX;
 
-__host__ __device__ inline int tc_stage_floats(int W) { return imax(TILES * W, 2 * MM); }
+// Per-tile stage stride: a prefix row, or the tile's saved level-2 state while its chunk has ended.
+__host__ __device__ inline int tc_stage_stride(int W) { return align4(imax(W, MM)); }
+__host__ __device__ inline int tc_stage_floats(int W) { return TILES * tc_stage_stride(W); }
 
 __host__ __device__ inline size_t tc_smem_bytes(int W, int d_in, int QP) {
     size_t f = 2 * MM + 2 * 4 * MM + TILES * 32 * RQS + align4(tc_stage_floats(W)) + 2 * MM + align4(NP * d_in) +
@@ -800,7 +817,7 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
     bool failed = false;
     bool mma_pending = false;  // an MMA commit of `phase` may still be outstanding after a failed wait
 
-    const uint64_t dA_hi = smem_desc(smem_u32(s.Ahi), 4096, 128), dA_lo = smem_desc(smem_u32(s.Alo), 4096, 128);
+    const uint64_t dA_hi = smem_desc(smem_u32(s.Ahi), 2048, 128), dA_lo = smem_desc(smem_u32(s.Alo), 2048, 128);
     const uint64_t dB_hi = smem_desc(smem_u32(s.Bhi), 512, 128), dB_lo = smem_desc(smem_u32(s.Blo), 512, 128);
     const int groups = (g.C + TILES - 1) / TILES;
     const int ntiles = g.B * groups;
@@ -840,22 +857,23 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                 vt[lane] = valid_me ? ldcg(cs + MM + lane) : 0.f;
             }
             __syncwarp();
+            float* saved = s.stage + warp * tc_stage_stride(g.W);
             for (int k = 0; k < steps; ++k) {
                 const bool live = k < len_me;
-                // E0: A operand (S2 by columns, MN-major hi/lo) and the exchange buffer
+                if (k == len_me) {
+                    // this tile's chunk has ended: park its state; the remaining steps only feed the MMAs
 #pragma unroll
-                for (int nq = 0; nq < 8; ++nq) {
-                    float h[4], lo[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        h[q] = __uint_as_float(tf32_bits(col[4 * nq + q]));
-                        lo[q] = col[4 * nq + q] - h[q];
-                        RQt[(4 * nq + q) * RQS + lane] = col[4 * nq + q];
-                    }
-                    const int off = amn_off4(8 * warp + nq, lane);
-                    *reinterpret_cast<float4*>(s.Ahi + off) = make_float4(h[0], h[1], h[2], h[3]);
-                    *reinterpret_cast<float4*>(s.Alo + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                    for (int n = 0; n < 32; ++n) saved[n * 32 + lane] = col[n];
                 }
+                // E0: the lane's column of S2 -> its row (through the exchange buffer) -> A operand row
+                float srow[32];
+#pragma unroll
+                for (int n = 0; n < 32; ++n) RQt[n * RQS + lane] = col[n];
+                __syncwarp();
+#pragma unroll
+                for (int n = 0; n < 32; ++n) srow[n] = RQt[lane * RQS + n];
+                __syncwarp();
+                store_a_row(s.Ahi, s.Alo, 32 * warp + lane, srow);
                 fence_proxy_async();
                 fence_before();
                 __syncthreads();
@@ -876,25 +894,18 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                     break;
                 }
                 phase ^= 1;
-                // E1: row `lane` of X = S2 - S2 D^T; A operand for the second product (X by rows)
+                // E1: row `lane` of X = S2 - S2 D^T -> column `lane` of X -> A operand row of X^T
+                float xcol[32];
                 {
                     float pr[32];
                     tmem_ld32(tP1 + lane_off, pr);
 #pragma unroll
-                    for (int n = 0; n < 32; ++n) pr[n] = RQt[lane * RQS + n] - pr[n];
+                    for (int n = 0; n < 32; ++n) RQt[lane * RQS + n] = srow[n] - pr[n];
+                    __syncwarp();
 #pragma unroll
-                    for (int nq = 0; nq < 8; ++nq) {
-                        float h[4], lo[4];
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            h[q] = __uint_as_float(tf32_bits(pr[4 * nq + q]));
-                            lo[q] = pr[4 * nq + q] - h[q];
-                            RQt[lane * RQS + 4 * nq + q] = pr[4 * nq + q];
-                        }
-                        const int off = amn_off4(8 * warp + nq, lane);
-                        *reinterpret_cast<float4*>(s.Ahi + off) = make_float4(h[0], h[1], h[2], h[3]);
-                        *reinterpret_cast<float4*>(s.Alo + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
-                    }
+                    for (int n = 0; n < 32; ++n) xcol[n] = RQt[n * RQS + lane];
+                    __syncwarp();
+                    store_a_row(s.Ahi, s.Alo, 32 * warp + lane, xcol);
                 }
                 fence_proxy_async();
                 fence_before();
@@ -923,24 +934,20 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                     const float* U = vt + 3 * NP + 32;
                     const float* V = U + NP * QMAX;
                     const float s1l = s1[lane];
-                    float nc[32];
 #pragma unroll
-                    for (int n = 0; n < 32; ++n) {
-                        float acc = fmaf(u[n], s1l, RQt[n * RQS + lane] - q2[n]);
-                        for (int a = 0; a < g.QP; ++a) acc = fmaf(U[n * QMAX + a], V[lane * QMAX + a], acc);
-                        nc[n] = acc;
+                    for (int n = 0; n < 32; ++n) col[n] = fmaf(u[n], s1l, xcol[n] - q2[n]);
+                    for (int a = 0; a < g.QP; ++a) {
+                        const float va = V[lane * QMAX + a];
+#pragma unroll
+                        for (int n = 0; n < 32; ++n) col[n] = fmaf(U[n * QMAX + a], va, col[n]);
                     }
                     const float s1new = u[lane] + s1l;
                     __syncwarp();
-                    if (live) {
-#pragma unroll
-                        for (int n = 0; n < 32; ++n) col[n] = nc[n];
-                        vt[lane] = s1new;
-                    }
+                    if (live) vt[lane] = s1new;
                     fence_before();
                     __syncwarp();
                     if (pass == 1 && live && g.readout == EWS_READOUT_PREFIX) {
-                        float* row = s.stage + warp * g.W;
+                        float* row = saved;
                         if (lane == 0) row[0] = 1.f;
                         if (lane < N) {
                             row[1 + lane] = vt[lane];
@@ -955,6 +962,10 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                 }
             }
             if (failed) break;
+            if (len_me < steps) {
+#pragma unroll
+                for (int n = 0; n < 32; ++n) col[n] = saved[n * 32 + lane];
+            }
             __syncthreads();
             if (pass == 1) break;
             // ---- aggregates of the 4 chunks (flow complement, S1, S2) -> agg slots
