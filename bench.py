@@ -31,7 +31,7 @@ sys.path.insert(0, ROOT)
 METRIC = "EWS fwd+bwd (batch·steps)/s at 1/2/4/8 B200, % HBM/TC roofline vs JAX CPU"
 UNIT = "batch·steps/s"
 L2_BYTES = 126 * 1024 * 1024
-KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 1, "ews_dense_bwd": 2}
+KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 2, "ews_dense_bwd": 2}
 
 
 def _peaks():
@@ -143,8 +143,10 @@ def _dense_setup(cfg, rank, world, device, precision, batch=None):
 
     d_in = x_host.shape[-1]
     out_row = 4 * (1 + D)
-    alg = {"ews_dense_fwd": 4 * d_in + out_row, "ews_dense_bwd": 4 * d_in + out_row + 4 * d_in}
-    meta = dict(B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout="prefix", dtype="f32", precision="f32")
+    # the dense path is tensor-core bound: algorithmic GEMM flops per unit (one sample-interval) are two
+    # N^3 flow products in the forward (2 * 2N^3) and four N^2 x N products in the backward (4 * 2N^3 / 2)
+    alg = {"ews_dense_fwd": 2 * 2 * N**3, "ews_dense_bwd": 4 * 2 * N**3}
+    meta = dict(bound="tensor", B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout="prefix", dtype="f32", precision="f32")
     ws_bytes = x_host.numel() * 4 + Bl * T * out_row
     return dict(step=step, params=params, x_host=x_host, clock_host=clock_host, alg=alg, meta=meta,
                 ws_bytes=ws_bytes, units=Bl * T, case=case)
@@ -331,7 +333,10 @@ def run_b200(args, rank, world, local_rank):
     avg_s = dom_ms / dom_n / 1e3
     hbm, _, peak_kind = _peaks()
     alg_bytes = setup["alg"][dom_name] * dom_units
-    achieved = alg_bytes / avg_s / 1e9
+    tensor_bound = setup["meta"].get("bound") == "tensor"
+    achieved = alg_bytes / avg_s / (1e12 if tensor_bound else 1e9)
+    _, tflops, _ = _peaks()
+    peak = tflops if tensor_bound else hbm
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
@@ -403,17 +408,19 @@ def run_b200(args, rank, world, local_rank):
             "l2": "flushed between timed steps" if flush is not None else "working set larger than L2",
         },
         "roofline": {
-            "bound": "hbm",
+            "bound": "tensor" if tensor_bound else "hbm",
             "kernel": dom_name,
             "achieved": achieved,
-            "peak": hbm,
-            "unit": "GB/s",
-            "frac": achieved / hbm,
-            "peak_source": peak_kind,
+            "peak": peak,
+            "unit": "TFLOP/s" if tensor_bound else "GB/s",
+            "frac": achieved / peak,
+            "peak_source": peak_kind + (" cuBLAS bf16 dense burst; tf32 runs at half that rate and 3xTF32 "
+                                        "issues three MMAs per product" if tensor_bound else " copy bandwidth"),
             "traffic": traffic,
-            "algorithmic_bytes_per_launch": alg_bytes,
+            ("algorithmic_flops_per_launch" if tensor_bound else "algorithmic_bytes_per_launch"): alg_bytes,
             "avg_launch_ms": avg_s * 1e3,
         },
+        "kernel_ms": {n: v[0] / v[1] for n, v in per.items()},
         "e2e": {
             "value": units_per_step * args.steps / (e2e_ms / 1e3),
             "unit": UNIT,

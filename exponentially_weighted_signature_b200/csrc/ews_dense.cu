@@ -57,6 +57,7 @@ struct Params {
     float* incl;
     float* carry;
     const float* fagg;
+    float* pw;  // per sample: flow complements C(Lc) and C(last chunk), row-major (2 MM)
 };
 
 __host__ __device__ inline int align4(int n) { return (n + 3) & ~3; }
@@ -721,36 +722,58 @@ __device__ void tc_load_tables(const Params& p, const TcSmem& s, int b) {
     }
 }
 
-// Per-tile vectors of a step (warp-local): x = dx_t, s1 = F x, U = [G_a x], V = [H_a x], u = S1 - D S1.
-__device__ void tc_local(const Params& p, const TcSmem& s, float* v, int b, int t_abs, bool valid) {
-    const Geom& g = p.g;
+// Per-tile vectors of a step (warp-local): x = dx_t (the lane's channel, loaded one step ahead),
+// s1 = F x, U = [G_a x], V = [H_a x], u = S1 - D S1. Independent accumulators keep the FMA chains short.
+__device__ void tc_local(const TcSmem& s, const Geom& g, float* v, float xl) {
     const int l = threadIdx.x & 31;
+    const int d = g.d_in;
     float* S1 = v;
     float* u = v + NP;
     float* s1 = v + 2 * NP;
     float* x = v + 3 * NP;
     float* U = v + 3 * NP + 32;
     float* V = U + NP * QMAX;
-    if (l < g.d_in) x[l] = valid ? input_increment(p.path, b, t_abs, l, g.T, g.d_in, g.flags) : 0.f;
+    if (l < d) x[l] = xl;
     __syncwarp();
-    float acc = 0.f;
-    for (int c = 0; c < g.d_in; ++c) acc = fmaf(s.F[l * g.d_in + c], x[c], acc);
-    s1[l] = acc;
-    for (int a = 0; a < g.QP; ++a) {
-        const float* Ga = s.G + ((size_t)a * NP + l) * g.d_in;
-        const float* Ha = s.H + ((size_t)a * NP + l) * g.d_in;
-        float ga = 0.f, ha = 0.f;
-        for (int c = 0; c < g.d_in; ++c) {
-            ga = fmaf(Ga[c], x[c], ga);
-            ha = fmaf(Ha[c], x[c], ha);
+    {
+        const float* Fl = s.F + l * d;
+        float a0 = 0.f, a1 = 0.f;
+        int c = 0;
+        for (; c + 1 < d; c += 2) {
+            a0 = fmaf(Fl[c], x[c], a0);
+            a1 = fmaf(Fl[c + 1], x[c + 1], a1);
         }
-        U[l * QMAX + a] = ga;
-        V[l * QMAX + a] = ha;
+        if (c < d) a0 = fmaf(Fl[c], x[c], a0);
+        s1[l] = a0 + a1;
     }
-    float du = 0.f;
-#pragma unroll 8
-    for (int k = 0; k < NP; ++k) du = fmaf(s.Dt[k * NP + l], S1[k], du);
-    u[l] = S1[l] - du;
+    for (int a = 0; a < g.QP; ++a) {
+        const float* Ga = s.G + ((size_t)a * NP + l) * d;
+        const float* Ha = s.H + ((size_t)a * NP + l) * d;
+        float g0 = 0.f, g1 = 0.f, h0 = 0.f, h1 = 0.f;
+        int c = 0;
+        for (; c + 1 < d; c += 2) {
+            const float x0 = x[c], x1 = x[c + 1];
+            g0 = fmaf(Ga[c], x0, g0);
+            h0 = fmaf(Ha[c], x0, h0);
+            g1 = fmaf(Ga[c + 1], x1, g1);
+            h1 = fmaf(Ha[c + 1], x1, h1);
+        }
+        if (c < d) {
+            g0 = fmaf(Ga[c], x[c], g0);
+            h0 = fmaf(Ha[c], x[c], h0);
+        }
+        U[l * QMAX + a] = g0 + g1;
+        V[l * QMAX + a] = h0 + h1;
+    }
+    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+    for (int k = 0; k < NP; k += 4) {
+        d0 = fmaf(s.Dt[k * NP + l], S1[k], d0);
+        d1 = fmaf(s.Dt[(k + 1) * NP + l], S1[k + 1], d1);
+        d2 = fmaf(s.Dt[(k + 2) * NP + l], S1[k + 2], d2);
+        d3 = fmaf(s.Dt[(k + 3) * NP + l], S1[k + 3], d3);
+    }
+    u[l] = S1[l] - ((d0 + d1) + (d2 + d3));
     __syncwarp();
 }
 
@@ -785,6 +808,69 @@ __device__ int tc_cta_wait(const Params& p, const TcSmem& s, const int* flag, in
 }
 
 }  // namespace tc
+
+// Flow complements of whole chunks, per sample: C(e) = I - M^e for e = Lc and e = the last chunk's
+// length, by binary powering of complements (C(a + b) = C(a) + C(b) - C(a) C(b), C(2a) = 2 C(a) - C(a)^2),
+// so that no I - (a matrix near I) is ever formed. One CTA of NT threads per sample.
+__global__ void __launch_bounds__(NT) power_kernel(Params p) {
+    extern __shared__ float smem[];
+    const Geom& g = p.g;
+    const int b = blockIdx.x;
+    const int N = g.N;
+    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
+    float* Dr = smem;
+    float* Dt = smem + MM;
+    float* W0 = smem + 2 * MM;  // C(2^j) row-major
+    float* W1 = smem + 3 * MM;  // C(2^j) k-major
+    float* R = smem + 4 * MM;   // accumulated complement, row-major
+    const float* m = p.tab_d + (size_t)b * N * N;
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) {
+        const int i = e / NP, k = e - i * NP;
+        const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
+        Dr[i * NP + k] = v;
+        Dt[k * NP + i] = v;
+    }
+    for (int which = 0; which < 2; ++which) {
+        const int e_len = which == 0 ? g.Lc : g.T - (g.C - 1) * g.Lc;
+        __syncthreads();
+        for (int e = threadIdx.x; e < MM; e += blockDim.x) {
+            R[e] = 0.f;
+            W0[e] = Dr[e];
+            W1[e] = Dt[e];
+        }
+        __syncthreads();
+        int e = e_len;
+        while (e > 0) {
+            float blk[4][4], Rb[4][4], Bb[4][4];
+            load_rowmajor(W0, Bb, i0, j0);
+            if (e & 1) {
+                load_rowmajor(R, Rb, i0, j0);
+                gemm44(W1, R, blk, i0, j0, false);
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) blk[r][q] = Rb[r][q] + Bb[r][q] - blk[r][q];
+                store_rowmajor(R, blk, i0, j0);
+                __syncthreads();
+            }
+            e >>= 1;
+            if (e > 0) {
+                gemm44(W1, W0, blk, i0, j0, false);
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) blk[r][q] = 2.f * Bb[r][q] - blk[r][q];
+                store_rowmajor(W0, blk, i0, j0);
+                store_kmajor(W1, blk, i0, j0);
+                __syncthreads();
+            }
+        }
+        float* dst = p.pw + ((size_t)b * 2 + which) * MM;
+        for (int q = threadIdx.x; q < MM; q += blockDim.x) dst[q] = R[q];
+    }
+}
 
 __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
     using namespace tc;
@@ -858,6 +944,8 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
             }
             __syncwarp();
             float* saved = s.stage + warp * tc_stage_stride(g.W);
+            // the lane's input channel, one step ahead
+            float xnext = (lane < g.d_in && len_me > 0) ? input_increment(p.path, b, t0_me, lane, g.T, g.d_in, g.flags) : 0.f;
             for (int k = 0; k < steps; ++k) {
                 const bool live = k < len_me;
                 if (k == len_me) {
@@ -888,7 +976,10 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                     mma_commit(s.bar);
                 }
                 // local terms of this step while the tensor core runs
-                tc_local(p, s, vt, b, t0_me + k, live);
+                const float xcur = live ? xnext : 0.f;
+                if (lane < g.d_in && k + 1 < len_me)
+                    xnext = input_increment(p.path, b, t0_me + k + 1, lane, g.T, g.d_in, g.flags);
+                tc_local(s, g, vt, xcur);
                 if (!tc_wait(s, phase, mbar_limit)) {
                     failed = mma_pending = true;
                     break;
@@ -946,18 +1037,14 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                     if (live) vt[lane] = s1new;
                     fence_before();
                     __syncwarp();
-                    if (pass == 1 && live && g.readout == EWS_READOUT_PREFIX) {
-                        float* row = saved;
+                    if (pass == 1 && live && g.readout == EWS_READOUT_PREFIX && lane < N) {
+                        // the prefix row straight from registers: each level-2 row is one contiguous run
+                        float* row = p.out + ((size_t)b * g.T + t0_me + k) * g.W;
                         if (lane == 0) row[0] = 1.f;
-                        if (lane < N) {
-                            row[1 + lane] = vt[lane];
+                        row[1 + lane] = s1new;
 #pragma unroll
-                            for (int n = 0; n < 32; ++n)
-                                if (n < N) row[1 + N + n * N + lane] = col[n];
-                        }
-                        __syncwarp();
-                        warp_store_span(p.out + ((size_t)b * g.T + t0_me + k) * g.W, row, g.W);
-                        __syncwarp();
+                        for (int n = 0; n < 32; ++n)
+                            if (n < N) row[1 + N + n * N + lane] = col[n];
                     }
                 }
             }
@@ -975,7 +1062,7 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                 for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = col[n];
                 as[MM + lane] = vt[lane];
             }
-            // flow complements C(len) for the full and the (possibly) short chunk, by powering complements
+            // flow complements C(len) of the full and the last chunk (computed per sample by power_kernel)
             float* W0 = s.Ahi;            // scratch matrices live in the idle operand buffers
             float* W1 = s.Ahi + MM;
             float* W2 = s.Ahi + 2 * MM;
@@ -984,51 +1071,8 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
             float* W5 = s.Alo + MM;
             float* W6 = s.Alo + 2 * MM;   // C(Lc) row-major
             float* W7 = s.Alo + 3 * MM;   // C(last) row-major
-            for (int which = 0; which < 2; ++which) {
-                const int e_len = which == 0 ? g.Lc : g.T - (g.C - 1) * g.Lc;
-                float* R = which == 0 ? W6 : W7;
-                for (int e = tid; e < MM; e += blockDim.x) {
-                    R[e] = 0.f;
-                    W0[e] = s.Dr[e];
-                    W1[e] = s.Dt[e];
-                }
-                __syncthreads();
-                int e = e_len;
-                while (e > 0) {
-                    float blk[4][4], Rb[4][4], Bb[4][4];
-                    const bool act = tid < NT;
-                    if (act) load_rowmajor(W0, Bb, i0, j0);
-                    if (e & 1) {
-                        if (act) {
-                            load_rowmajor(R, Rb, i0, j0);
-                            gemm44(W1, R, blk, i0, j0, false);
-                        }
-                        __syncthreads();
-                        if (act) {
-#pragma unroll
-                            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                                for (int q = 0; q < 4; ++q) blk[r][q] = Rb[r][q] + Bb[r][q] - blk[r][q];
-                            store_rowmajor(R, blk, i0, j0);
-                        }
-                        __syncthreads();
-                    }
-                    e >>= 1;
-                    if (e > 0) {
-                        if (act) gemm44(W1, W0, blk, i0, j0, false);
-                        __syncthreads();
-                        if (act) {
-#pragma unroll
-                            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                                for (int q = 0; q < 4; ++q) blk[r][q] = 2.f * Bb[r][q] - blk[r][q];
-                            store_rowmajor(W0, blk, i0, j0);
-                            store_kmajor(W1, blk, i0, j0);
-                        }
-                        __syncthreads();
-                    }
-                }
-            }
+            for (int e = tid; e < 2 * MM; e += blockDim.x) W6[e] = p.pw[(size_t)b * 2 * MM + e];
+            __syncthreads();
             for (int t = 0; t < TILES; ++t) {
                 const int c = grp * TILES + t;
                 if (c >= g.C) break;
@@ -1515,7 +1559,7 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 struct WsLayout {
-    size_t status, flags, agg, incl, carry, partials, total;
+    size_t status, flags, agg, incl, carry, partials, pw, total;
 };
 
 static WsLayout fwd_layout(const Geom& g) {
@@ -1532,6 +1576,8 @@ static WsLayout fwd_layout(const Geom& g) {
     o += slots;
     L.carry = o;
     o += slots;
+    L.pw = o;
+    o += al256(sizeof(float) * (size_t)g.B * 2 * MM);
     L.total = o;
     return L;
 }
@@ -1616,6 +1662,9 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     p.agg = (float*)(ws + L.agg);
     p.incl = (float*)(ws + L.incl);
     p.carry = (float*)(ws + L.carry);
+    p.pw = (float*)(ws + L.pw);
+    power_kernel<<<g.B, NT, 5 * MM * sizeof(float), s>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     const size_t smem = tc::tc_smem_bytes(g.W, g.d_in, g.QP);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
