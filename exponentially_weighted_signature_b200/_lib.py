@@ -77,6 +77,7 @@ class DiagArgs(ctypes.Structure):
         ("fwd_ws_bytes", _c_size),
         ("bwd_ws", _vp),
         ("bwd_ws_bytes", _c_size),
+        ("grad_dtheta", _vp),
     ]
 
 

@@ -20,6 +20,10 @@
 // T times, drifts by ~T 2^-24 (the reference's float32 path loses 5e-5 relative at T = 4096 that way); the
 // complement keeps the flow's rounding relative to delta instead.
 //
+// Per-interval clock (the reference's "displacement" mode): x_t = dtheta_t r with the clock step of each
+// interval, and Q1(x_t), Q2(x_t) evaluated in the kernel from the series coefficients (Horner); the
+// backward also returns dL/d(dtheta_t) and dL/dr.
+//
 // Backward: the adjoint of step t is lambda2 <- rho rho^T o lambda2, lambda1 <- rho o (lambda1 +
 // lambda2 s1). Chunks compute a zero-carry local adjoint, look back over the later chunks (whose
 // transposed chunk maps come from the forward aggregates) and then run the exact adjoint from the
@@ -35,6 +39,7 @@ namespace ews {
 namespace diag {
 
 constexpr int kWarps = 4;  // warps per CTA; each warp is an independent tile worker
+constexpr int kQNU = 9;    // coefficient slots of the in-kernel series tables (series order <= 8)
 
 struct Geom {
     int B, T, d_in, N, NP, Lc, C, W, SW, readout;
@@ -42,10 +47,11 @@ struct Geom {
     int spin_limit;
     int SR;      // prefix rows staged per span store
     int ntiles;  // B * C
+    int nu;      // per-interval clock (tables evaluated per step)
     // per-warp shared-memory carve-up (floats), after the CTA's lift matrix (lift_n floats)
     int lift_n;
-    int f_dys, f_stage, f_per_warp;                            // forward: dxs at 0
-    int b_dys, b_dyg, b_lam1, b_gst, b_sst, b_per_warp;        // backward: dxs at 0
+    int f_dys, f_dts, f_stage, f_per_warp;                     // forward: dxs at 0
+    int b_dys, b_dts, b_dtg, b_dyg, b_lam1, b_gst, b_sst, b_per_warp;  // backward: dxs at 0
 };
 
 struct Params {
@@ -68,6 +74,11 @@ struct Params {
     float* carry;   // forward: exclusive prefix per chunk (kept for the backward)
     const float* fagg;    // backward: the forward aggregates
     const float* fcarry;  // backward: the forward carries
+    // per-interval clock
+    const float* clock;   // (B, T+1) knots
+    float* grad_dtheta;   // (B, T)
+    float c1[kQNU];       // Q1 coefficients c1_p / p!
+    float c2[kQNU * kQNU];  // Q2 coefficients c2_ab / (a! b!), row a
 };
 
 __host__ __device__ inline int align4(int n) { return (n + 3) & ~3; }
@@ -153,9 +164,60 @@ __device__ __forceinline__ void load_elem(const float* slot, Elem<RI, RJ>& e, in
 
 // --------------------------------------------------------------------------------- tables, inputs
 
+// Horner evaluation of sum_a coef[a] x^a over the kQNU slots (zero above the series order) and of its
+// derivative.
+__device__ __forceinline__ float poly(const float* coef, float x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int a = kQNU - 1; a >= 0; --a) acc = fmaf(acc, x, coef[a]);
+    return acc;
+}
+
+__device__ __forceinline__ float dpoly(const float* coef, float x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int a = kQNU - 1; a >= 1; --a) acc = fmaf(acc, x, (float)a * coef[a]);
+    return acc;
+}
+
 template <int RI, int RJ>
 struct Tables {
     float xr[RI], xc[RJ], dr[RI], dc[RJ], q1r[RI], q1c[RJ], q2[RI][RJ];  // d = 1 - rho = -expm1(x)
+    float rr[RI], rc[RJ];  // per-interval clock: rates r, x = dtheta r
+    __device__ void load_rates(const Params& p, int b, int i0, int j0) {
+        const int N = p.g.N;
+        const float* tr = p.tab_x + (size_t)b * N;
+#pragma unroll
+        for (int r = 0; r < RI; ++r) rr[r] = i0 + r < N ? tr[i0 + r] : 0.f;
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) rc[c] = j0 + c < N ? tr[j0 + c] : 0.f;
+    }
+    // The tables of one interval of clock step dth: Q1(x) = sum_p c1_p x^p, Q2(x, y) = sum_a x^a w_a(y)
+    // with w_a(y) = sum_b c2_ab y^b (the series leaf's coefficients, ews/core/series_leaf.py:72-113).
+    __device__ void at(const Params& p, float dth) {
+#pragma unroll
+        for (int r = 0; r < RI; ++r) {
+            xr[r] = dth * rr[r];
+            dr[r] = -expm1f(xr[r]);
+            q1r[r] = poly(p.c1, xr[r]);
+        }
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            xc[c] = dth * rc[c];
+            dc[c] = -expm1f(xc[c]);
+            q1c[c] = poly(p.c1, xc[c]);
+            float w[kQNU];
+#pragma unroll
+            for (int a = 0; a < kQNU; ++a) w[a] = poly(p.c2 + a * kQNU, xc[c]);
+#pragma unroll
+            for (int r = 0; r < RI; ++r) {
+                float acc = 0.f;
+#pragma unroll
+                for (int a = kQNU - 1; a >= 0; --a) acc = fmaf(acc, xr[r], w[a]);
+                q2[r][c] = acc;
+            }
+        }
+    }
     __device__ void load(const Params& p, int b, int i0, int j0) {
         const int N = p.g.N;
         const float* tx = p.tab_x + (size_t)b * N;
@@ -185,10 +247,14 @@ struct Tables {
 
 // Lifted increments of steps [t0, t0 + n) into dys[k * NP + i] (zero for padded i >= N). The increments
 // themselves go to dxs[k * d_in + c] first.
-__device__ void load_increments(const Params& p, const float* liftS, float* dxs, float* dys, int b, int t0,
-                                int n) {
+__device__ void load_increments(const Params& p, const float* liftS, float* dxs, float* dys, float* dts, int b,
+                                int t0, int n) {
     const Geom& g = p.g;
     const int lane = threadIdx.x & 31;
+    if (g.nu) {
+        const float* ck = p.clock + (size_t)b * (g.T + 1) + t0;
+        for (int k = lane; k < n; k += 32) dts[k] = ck[k + 1] - ck[k];  // the reference's clock[1:] - clock[:-1]
+    }
     for (int e = lane; e < n * g.d_in; e += 32) {
         const int k = e / g.d_in, cc = e - k * g.d_in;
         dxs[e] = input_increment(p.path, b, t0 + k, cc, g.T, g.d_in, g.flags);
@@ -276,7 +342,7 @@ __device__ __forceinline__ void stage_row(float* row, const Elem<RI, RJ>& S, int
 
 // --------------------------------------------------------------------------------- forward kernel
 
-template <int NP>
+template <int NP, bool NU>
 __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
     constexpr int RI = NP / 4, RJ = NP / 8;
     extern __shared__ float smem[];
@@ -290,6 +356,7 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
     __syncthreads();
     float* dxs = smem + g.lift_n + warp * g.f_per_warp;
     float* dys = dxs + g.f_dys;
+    float* dts = dxs + g.f_dts;
     float* stage = dxs + g.f_stage;
 
     const int ti = lane >> 3, tj = lane & 7;
@@ -303,14 +370,18 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
         const int t0 = c * g.Lc;
         const int len = min(g.Lc, g.T - t0);
         Tables<RI, RJ> tb;
-        tb.load(p, b, i0, j0);
-        load_increments(p, liftS, dxs, dys, b, t0, len);
+        if (NU)
+            tb.load_rates(p, b, i0, j0);
+        else
+            tb.load(p, b, i0, j0);
+        load_increments(p, liftS, dxs, dys, dts, b, t0, len);
 
         // pass 1: the chunk's aggregate from the identity
         Elem<RI, RJ> A;
         A.identity();
         for (int k = 0; k < len; ++k) {
             float fr[RI], fc[RJ];
+            if (NU) tb.at(p, dts[k]);
             const bool bp = basepoint && (t0 + k == 0);
             step_flow(tb, bp, fr, fc);
             chen_step(tb, dys + k * NP, i0, j0, A, fr, fc, bp);
@@ -369,6 +440,7 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
         int k0 = 0;
         for (int k = 0; k < len; ++k) {
             float fr[RI], fc[RJ];
+            if (NU) tb.at(p, dts[k]);
             const bool bp = basepoint && (t0 + k == 0);
             step_flow(tb, bp, fr, fc);
             chen_step(tb, dys + k * NP, i0, j0, S, fr, fc, bp);
@@ -509,11 +581,13 @@ struct Grads {
 
 // One exact adjoint step at interval t: a holds the cotangent of S_t (g_t already added); S1p/S2p are
 // S_{t-1}. Accumulates the gradients, writes dy_t to dyg[0..NP) and turns a into the cotangent of S_{t-1}.
-template <int RI, int RJ>
-__device__ __forceinline__ void bwd_step(const Tables<RI, RJ>& tb, const float fr[RI], const float fc[RJ],
-                                         const float* dyk, const float S1p[RI], const float S2p[RI][RJ],
-                                         Adj<RI, RJ>& a, Grads<RI, RJ>& gr, float* dyg, int i0, int j0, int ti,
-                                         int tj, bool bp = false) {
+// Per-interval clock (NU): the x-gradient of the step (flow and tables) goes to dL/d(dtheta_t) = r . gx
+// (written by lane 0 to *dtg) and to dL/dr += dtheta_t gx (row / column partials in gr.gxr / gr.gxc).
+template <int RI, int RJ, bool NU>
+__device__ __forceinline__ void bwd_step(const Params& p, const Tables<RI, RJ>& tb, const float fr[RI],
+                                         const float fc[RJ], const float* dyk, const float S1p[RI],
+                                         const float S2p[RI][RJ], Adj<RI, RJ>& a, Grads<RI, RJ>& gr, float* dyg,
+                                         float dth, float* dtg, int i0, int j0, int ti, int tj, bool bp = false) {
     float dyr[RI], dyc[RJ], s1c[RJ], u[RI];
 #pragma unroll
     for (int r = 0; r < RI; ++r) {
@@ -530,12 +604,14 @@ __device__ __forceinline__ void bwd_step(const Tables<RI, RJ>& tb, const float f
     const float table_w = bp ? 0.f : 1.f;  // the basepoint interval does not read the tables
     // row sums: w (adjoint recursion), z (dy from s2, row side)
     float w[RI], z[RI];
-    // column partials: y (ds1), v (dy from s2, column side), e (flow gradient, column side)
+    // column partials: y (ds1), v (dy from s2, column side)
     float y[RJ], v[RJ];
+    float rowx[RI], colx[RJ];  // NU: this step's x-gradient partials
 #pragma unroll
     for (int c = 0; c < RJ; ++c) {
         y[c] = 0.f;
         v[c] = 0.f;
+        colx[c] = 0.f;
     }
 #pragma unroll
     for (int r = 0; r < RI; ++r) {
@@ -551,12 +627,44 @@ __device__ __forceinline__ void bwd_step(const Tables<RI, RJ>& tb, const float f
             // flow gradient (w.r.t. x = log rho) of rho_i rho_j S2_ij, credited to i and to j
             const float fl = l2 * (1.f - comp_mul(fr[r], fc[c])) * S2p[r][c];
             fx = fmaf(l2, u[r] * s1c[c], fx + fl);
-            gr.gxc[c] += fl;
-            gr.dq2[r][c] = fmaf(table_w * l2, dyr[r] * dyc[c], gr.dq2[r][c]);
+            if (NU) {
+                colx[c] += fl;
+            } else {
+                gr.gxc[c] += fl;
+                gr.dq2[r][c] = fmaf(table_w * l2, dyr[r] * dyc[c], gr.dq2[r][c]);
+            }
         }
         w[r] = row_sum(wr);
         z[r] = row_sum(zr);
-        gr.gxr[r] += fx + (tj == 0 ? a.L1r[r] * u[r] : 0.f);
+        const float rx = fx + (tj == 0 ? a.L1r[r] * u[r] : 0.f);
+        if (NU)
+            rowx[r] = rx;
+        else
+            gr.gxr[r] += rx;
+    }
+    if (NU) {
+        // table derivatives: dQ2/dx_i = sum_a a x_i^(a-1) w_a(x_j), dQ2/dx_j = sum_a x_i^a w'_a(x_j)
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            float wv[kQNU], wd[kQNU];
+#pragma unroll
+            for (int q = 0; q < kQNU; ++q) {
+                wv[q] = poly(p.c2 + q * kQNU, tb.xc[c]);
+                wd[q] = dpoly(p.c2 + q * kQNU, tb.xc[c]);
+            }
+#pragma unroll
+            for (int r = 0; r < RI; ++r) {
+                const float L = a.L2[r][c] * (dyr[r] * dyc[c]);
+                const float x = tb.xr[r];
+                float gxv = 0.f, gyv = 0.f;
+#pragma unroll
+                for (int q = kQNU - 1; q >= 1; --q) gxv = fmaf(gxv, x, (float)q * wv[q]);
+#pragma unroll
+                for (int q = kQNU - 1; q >= 0; --q) gyv = fmaf(gyv, x, wd[q]);
+                rowx[r] = fmaf(L, gxv, rowx[r]);
+                colx[c] = fmaf(L, gyv, colx[c]);
+            }
+        }
     }
     float l1c[RJ], zc[RJ];
     rows_to_cols<RI, RJ>(a.L1r, l1c, tj);
@@ -565,8 +673,28 @@ __device__ __forceinline__ void bwd_step(const Tables<RI, RJ>& tb, const float f
     for (int c = 0; c < RJ; ++c) {
         const float ds1 = l1c[c] + col_sum(y[c]);
         const float vv = col_sum(v[c]);
-        gr.dq1c[c] = fmaf(table_w * ds1, dyc[c], gr.dq1c[c]);
+        if (NU) {
+            if (ti == 0) colx[c] = fmaf(ds1 * dyc[c], dpoly(p.c1, tb.xc[c]), colx[c]);
+        } else {
+            gr.dq1c[c] = fmaf(table_w * ds1, dyc[c], gr.dq1c[c]);
+        }
         if (ti == 0) dyg[j0 + c] = fmaf(ds1, q1c[c], vv + zc[c]);
+    }
+    if (NU) {
+        float contrib = 0.f;
+#pragma unroll
+        for (int r = 0; r < RI; ++r) {
+            contrib = fmaf(tb.rr[r], rowx[r], contrib);
+            gr.gxr[r] = fmaf(dth, rowx[r], gr.gxr[r]);
+        }
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            contrib = fmaf(tb.rc[c], colx[c], contrib);
+            gr.gxc[c] = fmaf(dth, colx[c], gr.gxc[c]);
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) contrib += __shfl_xor_sync(kFull, contrib, o);
+        if ((threadIdx.x & 31) == 0) *dtg = contrib;
     }
     // cotangent of S_{t-1}
 #pragma unroll
@@ -611,13 +739,14 @@ __device__ __forceinline__ void add_grad_row(Adj<RI, RJ>& a, const float* row, i
 
 // Writes dx (the gradient of the input increments) of the chunk and accumulates the lift gradient.
 template <int RI, int RJ>
-__device__ void finish_chunk(const Params& p, const float* liftS, const float* dxs, const float* dyg, float* stage,
-                             int b, int t0, int len, int tile, const Grads<RI, RJ>& gr, int i0, int j0, int ti,
-                             int tj) {
+__device__ void finish_chunk(const Params& p, const float* liftS, const float* dxs, const float* dyg, const float* dtg,
+                             float* stage, int b, int t0, int len, int tile, const Grads<RI, RJ>& gr, int i0, int j0,
+                             int ti, int tj) {
     const Geom& g = p.g;
     const int lane = threadIdx.x & 31;
     const int NP = g.NP;
     __syncwarp();
+    if (g.nu) warp_store_span(p.grad_dtheta + (size_t)b * g.T + t0, dtg, len);
     // dx_t = lift^T dy_t, staged contiguously, then one span store
     for (int e = lane; e < len * g.d_in; e += 32) {
         const int k = e / g.d_in, cc = e - k * g.d_in;
@@ -668,7 +797,7 @@ __device__ void finish_chunk(const Params& p, const float* liftS, const float* d
         for (int c = 0; c < RJ; ++c) part[2 * NP + (i0 + r) * NP + j0 + c] = gr.dq2[r][c];
 }
 
-template <int NP>
+template <int NP, bool NU>
 __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     constexpr int RI = NP / 4, RJ = NP / 8;
     extern __shared__ float smem[];
@@ -684,6 +813,8 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     // staging), sst (forward rows, prefix only)
     float* dxs = smem + g.lift_n + warp * g.b_per_warp;
     float* dys = dxs + g.b_dys;
+    float* dts = dxs + g.b_dts;  // per-interval clock steps
+    float* dtg = dxs + g.b_dtg;  // dL/d(dtheta) of the chunk's intervals
     float* dyg = dxs + g.b_dyg;
     float* lam1 = dxs + g.b_lam1;
     float* gst = dxs + g.b_gst;
@@ -702,10 +833,22 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         const int t0 = c * g.Lc;
         const int len = min(g.Lc, g.T - t0);
         Tables<RI, RJ> tb;
-        tb.load(p, b, i0, j0);
-        load_increments(p, liftS, dxs, dys, b, t0, len);
+        if (NU)
+            tb.load_rates(p, b, i0, j0);
+        else
+            tb.load(p, b, i0, j0);
+        load_increments(p, liftS, dxs, dys, dts, b, t0, len);
         const size_t slot = ((size_t)b * g.C + c) * g.SW;
         int* flag = p.flags + (size_t)b * g.C + c;
+        // elapsed clock from the end of interval t to the end of the path (NU), else a step count
+        const float* ck = NU ? p.clock + (size_t)b * (g.T + 1) : nullptr;
+        const float clock_end = NU ? ck[g.T] : 0.f;
+        const float clock_chunk_end = NU ? ck[t0 + len] : 0.f;
+        float ur[RI], uc[RJ];  // rates (NU) or log-flows: exponents are elapsed x these
+#pragma unroll
+        for (int r = 0; r < RI; ++r) ur[r] = NU ? tb.rr[r] : tb.xr[r];
+#pragma unroll
+        for (int cc = 0; cc < RJ; ++cc) uc[cc] = NU ? tb.rc[cc] : tb.xc[cc];
 
         // terminal readout: lambda2_t = E_i E_j g2 with E = e^{(T-1-t) x}; load g once
         float tg1[RI], tg2[RI][RJ];
@@ -723,6 +866,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                 for (int k = kb - 1; k >= k0; --k) {
                     add_grad_row(mu, gst + (k - k0) * g.W, g.N, i0, j0);
                     float fr[RI], fc[RJ];
+                    if (NU) tb.at(p, dts[k]);
                     const bool bp = basepoint && (t0 + k == 0);
                     step_flow(tb, bp, fr, fc);
                     adj_step(tb, fr, fc, dys + k * NP, mu, j0, bp);
@@ -741,16 +885,17 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                     for (int r = 0; r < RI; ++r) lam1[k * NP + i0 + r] = mu.L1r[r];
                 }
                 float fr[RI], fc[RJ];
+                if (NU) tb.at(p, dts[k]);
                 const bool bp = basepoint && (t == 0);
                 step_flow(tb, bp, fr, fc);
-                const float steps_after = (float)(g.T - 1 - t);
+                const float steps_after = NU ? clock_end - ck[t + 1] : (float)(g.T - 1 - t);
                 float ecs[RJ];
 #pragma unroll
                 for (int cc = 0; cc < RJ; ++cc)
-                    ecs[cc] = expf(steps_after * tb.xc[cc]) * (bp ? 1.f : tb.q1c[cc]) * dys[k * NP + j0 + cc];
+                    ecs[cc] = expf(steps_after * uc[cc]) * (bp ? 1.f : tb.q1c[cc]) * dys[k * NP + j0 + cc];
 #pragma unroll
                 for (int r = 0; r < RI; ++r) {
-                    const float er = expf(steps_after * tb.xr[r]);
+                    const float er = expf(steps_after * ur[r]);
                     float wr = 0.f;
 #pragma unroll
                     for (int cc = 0; cc < RJ; ++cc) wr = fmaf(er * tg2[r][cc], ecs[cc], wr);
@@ -828,9 +973,11 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                     float S1p[RI], S2p[RI][RJ];
                     read_row<RI, RJ>(sst + (k - k0) * g.W, S1p, S2p, g.N, i0, j0);
                     float fr[RI], fc[RJ];
+                    if (NU) tb.at(p, dts[k]);
                     const bool bp = basepoint && (t0 + k == 0);
                     step_flow(tb, bp, fr, fc);
-                    bwd_step(tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, i0, j0, ti, tj, bp);
+                    bwd_step<RI, RJ, NU>(p, tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, NU ? dts[k] : 0.f,
+                                         dtg + k, i0, j0, ti, tj, bp);
                 }
             }
         } else {
@@ -839,16 +986,16 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
             load_elem(p.fcarry + slot, S, NP, i0, j0);
             for (int k = 0; k < len; ++k) {
                 const int t = t0 + k;
-                const float steps_after = (float)(g.T - 1 - t);
-                const float steps_to_end = (float)(len - 1 - k);
+                const float steps_after = NU ? clock_end - ck[t + 1] : (float)(g.T - 1 - t);
+                const float steps_to_end = NU ? clock_chunk_end - ck[t + 1] : (float)(len - 1 - k);
                 Adj<RI, RJ> a;
                 float ecs[RJ];
 #pragma unroll
-                for (int cc = 0; cc < RJ; ++cc) ecs[cc] = expf(steps_after * tb.xc[cc]);
+                for (int cc = 0; cc < RJ; ++cc) ecs[cc] = expf(steps_after * uc[cc]);
 #pragma unroll
                 for (int r = 0; r < RI; ++r) {
-                    const float er = expf(steps_after * tb.xr[r]);
-                    a.L1r[r] = lam1[k * NP + i0 + r] + expf(steps_to_end * tb.xr[r]) * lam_in.L1r[r];
+                    const float er = expf(steps_after * ur[r]);
+                    a.L1r[r] = lam1[k * NP + i0 + r] + expf(steps_to_end * ur[r]) * lam_in.L1r[r];
 #pragma unroll
                     for (int cc = 0; cc < RJ; ++cc) a.L2[r][cc] = er * ecs[cc] * tg2[r][cc];
                 }
@@ -860,13 +1007,15 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                     for (int cc = 0; cc < RJ; ++cc) S2p[r][cc] = S.S2[r][cc];
                 }
                 float fr[RI], fc[RJ];
+                if (NU) tb.at(p, dts[k]);
                 const bool bp = basepoint && (t == 0);
                 step_flow(tb, bp, fr, fc);
-                bwd_step(tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, i0, j0, ti, tj, bp);
+                bwd_step<RI, RJ, NU>(p, tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, NU ? dts[k] : 0.f,
+                                     dtg + k, i0, j0, ti, tj, bp);
                 chen_step(tb, dys + k * NP, i0, j0, S, fr, fc, bp);
             }
         }
-        finish_chunk<RI, RJ>(p, liftS, dxs, dyg, gst, b, t0, len, tile, gr, i0, j0, ti, tj);
+        finish_chunk<RI, RJ>(p, liftS, dxs, dyg, dtg, gst, b, t0, len, tile, gr, i0, j0, ti, tj);
     }
 }
 
@@ -901,10 +1050,10 @@ __global__ void reduce_samples_kernel(Params p, const float* sp, float* grad_x, 
             if (r < N) {
                 grad_x[(size_t)b * N + r] = row[r];
             } else if (r < 2 * N) {
-                grad_q1[(size_t)b * N + (r - N)] = row[NP + (r - N)];
+                if (grad_q1) grad_q1[(size_t)b * N + (r - N)] = row[NP + (r - N)];
             } else {
                 const int q = r - 2 * N, i = q / N, j = q - i * N;
-                grad_q2[(size_t)b * N * N + q] = row[2 * NP + i * NP + j];
+                if (grad_q2) grad_q2[(size_t)b * N * N + q] = row[2 * NP + i * NP + j];
             }
         } else {
             const int q = e - g.B * per_sample;
@@ -934,15 +1083,18 @@ static void carve(Geom* g) {
     const int SR = g->SR < Lc ? g->SR : Lc;
     g->SR = SR;
     g->lift_n = align4(NP * g->d_in);
-    const int xs = align4(Lc * g->d_in), ys = align4(Lc * NP);
+    const int xs = align4(Lc * g->d_in), ys = align4(Lc * NP), ts = g->nu ? align4(Lc) : 0;
     g->f_dys = xs;
-    g->f_stage = xs + ys;
-    g->f_per_warp = xs + ys + align4(SR * g->W);
+    g->f_dts = xs + ys;
+    g->f_stage = xs + ys + ts;
+    g->f_per_warp = g->f_stage + align4(SR * g->W);
     const bool terminal = g->readout == EWS_READOUT_TERMINAL;
     const int gst_n = align4(std::max(terminal ? 0 : SR * g->W, Lc * g->d_in));
     g->b_dys = xs;
-    g->b_dyg = xs + ys;
-    g->b_lam1 = xs + 2 * ys;
+    g->b_dts = xs + ys;
+    g->b_dtg = g->b_dts + ts;
+    g->b_dyg = g->b_dtg + ts;
+    g->b_lam1 = g->b_dyg + ys;
     g->b_gst = g->b_lam1 + (terminal ? ys : 0);
     g->b_sst = g->b_gst + gst_n;
     g->b_per_warp = g->b_sst + (terminal ? 0 : align4(SR * g->W));
@@ -952,9 +1104,12 @@ static int make_geom(const ews_diag_args* a, Geom* g) {
     if (!a || a->batch <= 0 || a->steps <= 0 || a->d_in <= 0 || a->dim <= 0) return EWS_ERR_INVALID_ARGUMENT;
     if (a->depth != 2) return EWS_ERR_UNSUPPORTED;
     if (a->dim > 32) return EWS_ERR_UNSUPPORTED;
-    if (!(a->flags & EWS_F_UNIFORM)) return EWS_ERR_UNSUPPORTED;
+    const bool nu = !(a->flags & EWS_F_UNIFORM);
+    if (nu && (a->flags & EWS_F_BASEPOINT)) return EWS_ERR_INVALID_ARGUMENT;
+    if (nu && (a->series_q < 0 || a->series_q >= kQNU)) return EWS_ERR_UNSUPPORTED;
     if (a->readout != EWS_READOUT_PREFIX && a->readout != EWS_READOUT_TERMINAL) return EWS_ERR_INVALID_ARGUMENT;
     if ((a->flags & EWS_F_BF16) && !(a->flags & EWS_F_INCREMENTS)) return EWS_ERR_INVALID_ARGUMENT;
+    g->nu = nu ? 1 : 0;
     g->B = a->batch;
     g->T = a->steps;
     g->d_in = a->d_in;
@@ -1039,32 +1194,55 @@ static int num_sms() {
     return n;
 }
 
-template <int NP>
-static int launch_fwd(const Params& p, cudaStream_t s) {
+template <int NP, bool NU>
+static int launch_fwd_t(const Params& p, cudaStream_t s) {
     const size_t smem = fwd_smem(p.g);
-    cudaFuncSetAttribute(fwd_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(fwd_kernel<NP, NU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_kernel<NP>, kWarps * 32, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_kernel<NP, NU>, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     int grid = per_sm * num_sms();
     const int need = (p.g.ntiles + kWarps - 1) / kWarps;
     if (grid > need) grid = need;
-    fwd_kernel<NP><<<grid, kWarps * 32, smem, s>>>(p);
+    fwd_kernel<NP, NU><<<grid, kWarps * 32, smem, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+template <int NP>
+static int launch_fwd(const Params& p, cudaStream_t s) {
+    return p.g.nu ? launch_fwd_t<NP, true>(p, s) : launch_fwd_t<NP, false>(p, s);
+}
+
+template <int NP, bool NU>
+static int launch_bwd_t(const Params& p, cudaStream_t s) {
+    const size_t smem = bwd_smem(p.g);
+    cudaFuncSetAttribute(bwd_kernel<NP, NU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_kernel<NP, NU>, kWarps * 32, smem);
+    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
+    int grid = per_sm * num_sms();
+    const int need = (p.g.ntiles + kWarps - 1) / kWarps;
+    if (grid > need) grid = need;
+    bwd_kernel<NP, NU><<<grid, kWarps * 32, smem, s>>>(p);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 
 template <int NP>
 static int launch_bwd(const Params& p, cudaStream_t s) {
-    const size_t smem = bwd_smem(p.g);
-    cudaFuncSetAttribute(bwd_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_kernel<NP>, kWarps * 32, smem);
-    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
-    int grid = per_sm * num_sms();
-    const int need = (p.g.ntiles + kWarps - 1) / kWarps;
-    if (grid > need) grid = need;
-    bwd_kernel<NP><<<grid, kWarps * 32, smem, s>>>(p);
-    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+    return p.g.nu ? launch_bwd_t<NP, true>(p, s) : launch_bwd_t<NP, false>(p, s);
+}
+
+// Coefficients of the in-kernel series tables: c1_p / p! = 1 / ((p+1) p!) and
+// c2_ab / (a! b!) = 1 / ((a+b+2)(b+1) a! b!) for a + b <= q (ews/core/series_leaf.py:45-66), zero above.
+static void series_coefficients(int q, Params* p) {
+    double fact[kQNU];
+    fact[0] = 1.0;
+    for (int i = 1; i < kQNU; ++i) fact[i] = fact[i - 1] * i;
+    for (int a = 0; a < kQNU; ++a) {
+        p->c1[a] = a <= q ? (float)(1.0 / ((a + 1) * fact[a])) : 0.f;
+        for (int b = 0; b < kQNU; ++b)
+            p->c2[a * kQNU + b] = a + b <= q ? (float)(1.0 / ((double)(a + b + 2) * (b + 1) * fact[a] * fact[b])) : 0.f;
+    }
 }
 
 }  // namespace diag
@@ -1086,7 +1264,8 @@ extern "C" int ews_diag_fwd(const ews_diag_args* a, ews_stream_t stream) {
     Geom g;
     int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
-    if (!a->path || !a->out || !a->tab_x || !a->tab_q1 || !a->tab_q2) return EWS_ERR_INVALID_ARGUMENT;
+    if (!a->path || !a->out || !a->tab_x) return EWS_ERR_INVALID_ARGUMENT;
+    if (g.nu ? !a->clock : (!a->tab_q1 || !a->tab_q2)) return EWS_ERR_INVALID_ARGUMENT;
     if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
     const WsLayout L = fwd_layout(g);
     if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
@@ -1106,6 +1285,8 @@ extern "C" int ews_diag_fwd(const ews_diag_args* a, ews_stream_t stream) {
     p.agg = (float*)(ws + L.agg);
     p.incl = (float*)(ws + L.incl);
     p.carry = (float*)(ws + L.carry);
+    p.clock = a->clock;
+    series_coefficients(a->series_q, &p);
     switch (g.NP) {
         case 8: return launch_fwd<8>(p, s);
         case 16: return launch_fwd<16>(p, s);
@@ -1119,7 +1300,8 @@ extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
     Geom g;
     int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
-    if (!a->path || !a->grad_out || !a->grad_dx || !a->grad_x || !a->grad_q1 || !a->grad_q2)
+    if (!a->path || !a->grad_out || !a->grad_dx || !a->grad_x || !a->tab_x) return EWS_ERR_INVALID_ARGUMENT;
+    if (g.nu ? (!a->clock || !a->grad_dtheta) : (!a->grad_q1 || !a->grad_q2 || !a->tab_q1 || !a->tab_q2))
         return EWS_ERR_INVALID_ARGUMENT;
     if (g.readout == EWS_READOUT_PREFIX && !a->out) return EWS_ERR_INVALID_ARGUMENT;
     if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
@@ -1148,6 +1330,9 @@ extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
     p.incl = (float*)(ws + L.incl);
     p.fagg = (const float*)(fws + F.agg);
     p.fcarry = (const float*)(fws + F.carry);
+    p.clock = a->clock;
+    p.grad_dtheta = a->grad_dtheta;
+    series_coefficients(a->series_q, &p);
     switch (g.NP) {
         case 8: rc = launch_bwd<8>(p, s); break;
         case 16: rc = launch_bwd<16>(p, s); break;
@@ -1161,8 +1346,8 @@ extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
     const int threads = 256;
     reduce_chunks_kernel<<<(int)std::min<size_t>((n1 + threads - 1) / threads, 65535), threads, 0, s>>>(p, sp);
     const int total = g.B * (2 * g.N + g.N * g.N) + (a->grad_lift ? g.N * g.d_in : 0);
-    reduce_samples_kernel<<<(total + threads - 1) / threads, threads, 0, s>>>(p, sp, a->grad_x, a->grad_q1, a->grad_q2,
-                                                                            a->grad_lift);
+    reduce_samples_kernel<<<(total + threads - 1) / threads, threads, 0, s>>>(
+        p, sp, a->grad_x, g.nu ? nullptr : a->grad_q1, g.nu ? nullptr : a->grad_q2, a->grad_lift);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 

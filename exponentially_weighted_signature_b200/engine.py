@@ -185,3 +185,69 @@ class DenseScan(torch.autograd.Function):
             _lib.check(lib.ews_dense_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_dense_bwd")
         gpath = gdx if increments else increments_to_knots_grad(gdx)
         return gpath.to(path_dtype), gM, gF, gG, gH, None, None, None, None
+
+
+class DiagScanClock(torch.autograd.Function):
+    """Diagonal engine, per-interval clock (the reference's "displacement" mode): (path, clock knots,
+    rates r = -lambda, lift) -> flat EWS. Interval t uses x_t = (clock[t+1] - clock[t]) r with its own
+    series tables, evaluated in the kernel; the backward returns the gradients of the path, the clock,
+    the rates and the lift."""
+
+    @staticmethod
+    def forward(ctx, path, clock, rates, lift, readout, flags, chunk, increments, series_q):
+        _require_cuda(path, clock, rates, lift)
+        lib = _lib.load()
+        B = path.shape[0]
+        T = path.shape[1] if increments else path.shape[1] - 1
+        d_in = path.shape[2]
+        N = rates.shape[-1]
+        D = N + N * N
+        dev = path.device
+        path_c = path.contiguous()
+        clock_c = clock.contiguous().float()
+        rates_c = rates.contiguous().float()
+        lift_c = None if lift is None else lift.contiguous().float()
+        out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
+        a = _lib.DiagArgs()
+        a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, 0
+        fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        _lib.check(lib.ews_diag_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_diag_workspace_size")
+        fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
+        a.path, a.clock, a.lift, a.tab_x = _ptr(path_c), _ptr(clock_c), _ptr(lift_c), _ptr(rates_c)
+        a.out = _ptr(out)
+        a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
+        with _timed("ews_diag_fwd", dev, B * T):
+            _lib.check(lib.ews_diag_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_fwd")
+        ctx.meta = (readout, flags, chunk, increments, series_q, B, T, d_in, N, bb.value, path.dtype, clock.dtype)
+        ctx.has_lift = lift is not None
+        empty = torch.empty(0, device=dev)
+        ctx.save_for_backward(path_c, clock_c, rates_c, lift_c if lift_c is not None else empty, out, fwd_ws)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        readout, flags, chunk, increments, series_q, B, T, d_in, N, bwd_bytes, path_dtype, clock_dtype = ctx.meta
+        path, clock, rates, lift, out, fwd_ws = ctx.saved_tensors
+        lift = lift if ctx.has_lift else None
+        lib = _lib.load()
+        dev = path.device
+        g = grad_out.contiguous().float()
+        bwd_ws = torch.empty(bwd_bytes, dtype=torch.uint8, device=dev)
+        gdx = torch.empty((B, T, d_in), device=dev, dtype=torch.float32)
+        gr = torch.empty((B, N), device=dev, dtype=torch.float32)
+        gdt = torch.empty((B, T), device=dev, dtype=torch.float32)
+        glift = torch.empty((N, d_in), device=dev, dtype=torch.float32) if lift is not None else None
+        a = _lib.DiagArgs()
+        a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, 0
+        a.path, a.clock, a.lift, a.tab_x = _ptr(path), _ptr(clock), _ptr(lift), _ptr(rates)
+        a.out, a.grad_out = _ptr(out), _ptr(g)
+        a.grad_dx, a.grad_lift, a.grad_x, a.grad_dtheta = _ptr(gdx), _ptr(glift), _ptr(gr), _ptr(gdt)
+        a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fwd_ws.numel()
+        a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
+        with _timed("ews_diag_bwd", dev, B * T):
+            _lib.check(lib.ews_diag_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_bwd")
+        gpath = gdx if increments else increments_to_knots_grad(gdx)
+        gclock = increments_to_knots_grad(gdt[..., None])[..., 0]
+        return gpath.to(path_dtype), gclock.to(clock_dtype), gr, glift, None, None, None, None, None

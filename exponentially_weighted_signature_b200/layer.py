@@ -125,11 +125,13 @@ class EWS(nn.Module):
         """Batched flat EWS: path (B, L, d_in) knots [(B, L-1, d_in) increments], clock (B, L)."""
         uniform = self.reweighting_mode != "displacement"
         basepoint = self.reweighting_mode == "displacement_uniform_basepoint"
-        if not uniform:
-            raise NotImplementedError(f"the {self.engine} engine is built for the uniform-clock reweighting modes")
         if self.engine == "dense":
+            if not uniform:
+                raise NotImplementedError("the dense engine is built for the uniform-clock reweighting modes")
             return self._flat_dense(path, clock, readout, a_scale, lift, increments, basepoint)
         kernel_readout = _lib.EWS_READOUT_TERMINAL if readout == "terminal" else _lib.EWS_READOUT_PREFIX
+        if not uniform:
+            return self._flat_diag_clock(path, clock, kernel_readout, a_scale, lift, increments)
         lam = self.A_param.diag_values().to(torch.float32) * a_scale
         clock = clock.to(torch.float32)
         h = (clock[:, 2] - clock[:, 1]) if basepoint else (clock[:, 1] - clock[:, 0])
@@ -147,6 +149,27 @@ class EWS(nn.Module):
         else:
             path = path.to(torch.float32)
         return engine.DiagScan.apply(path, x, q1, q2, lift, kernel_readout, flags, self.combine_chunk, increments)
+
+    def _flat_diag_clock(self, path, clock, kernel_readout, a_scale, lift, increments):
+        """The "displacement" mode: every interval has its own clock step, flow and series tables
+        (ews/core/chen_scan.py:155-168 with cached=False; ews/core/series_leaf.py:72-127 per interval)."""
+        if self.series_q > 8:
+            raise NotImplementedError("the per-interval diagonal engine evaluates series tables up to series_q=8")
+        rates = -(self.A_param.diag_values().to(torch.float32) * a_scale)
+        B = path.shape[0]
+        rates = rates[None, :].expand(B, -1)
+        flags = _lib.EWS_F_DETERMINISTIC if _DETERMINISTIC else 0
+        if increments:
+            flags |= _lib.EWS_F_INCREMENTS
+            if path.dtype == torch.bfloat16:
+                flags |= _lib.EWS_F_BF16
+            else:
+                path = path.to(torch.float32)
+        else:
+            path = path.to(torch.float32)
+        return engine.DiagScanClock.apply(
+            path, clock.to(torch.float32), rates, lift, kernel_readout, flags, self.combine_chunk, increments, self.series_q
+        )
 
     def _flat_dense(self, path, clock, readout, a_scale, lift, increments, basepoint):
         if basepoint:

@@ -68,7 +68,17 @@ typedef struct CUstream_st* ews_stream_t; /* = cudaStream_t */
  *   tab_q1 (B, dim)       Q1_i  = sum_{p<=q} c1_p x_i^p / p!             (s1_i = Q1_i dy_i)
  *   tab_q2 (B, dim, dim)  Q2_ij = sum_{a+b<=q} c2_ab x_i^a x_j^b / a!b!  (s2_ij = Q2_ij dy_i dy_j)
  * where dy = lift @ dx. The backward returns dL/dx (grad_x), dL/dQ1, dL/dQ2 per sample, so the caller
- * chains them to lambda and the clock with the (tiny) table maps. */
+ * chains them to lambda and the clock with the (tiny) table maps.
+ *
+ * Per-interval clock (flags without EWS_F_UNIFORM; the reference's default reweighting mode
+ * "displacement", ews/layer.py:154-169 with ews/core/chen_scan.py:155-168 cached=False): interval t of
+ * sample b has its own step dtheta_t = clock[b, t+1] - clock[b, t] and log-flow x_t = dtheta_t r_b with
+ *   clock  (B, T+1)       clock knots
+ *   tab_x  (B, dim)       rates r = -lambda (per sample)
+ * and the series tables Q1(x_t), Q2(x_t) of order series_q (<= 8) are evaluated in the kernel for every
+ * interval (tab_q1 / tab_q2 unused). The backward returns dL/dr in grad_x and dL/d(dtheta) in
+ * grad_dtheta (B, T); grad_q1 / grad_q2 are unused. EWS_F_BASEPOINT does not apply: a basepoint interval
+ * is an interval with dtheta = 0. */
 typedef struct ews_diag_args {
     int batch;         /* B */
     int steps;         /* T: intervals per path */
@@ -93,15 +103,17 @@ typedef struct ews_diag_args {
     const float* grad_out;   /* same shape as out */
     float* grad_dx;          /* (B, T, d_in): dL/d(increments) */
     float* grad_lift;        /* (dim, d_in) or NULL */
-    float* grad_x;           /* (B, dim) */
-    float* grad_q1;          /* (B, dim) */
-    float* grad_q2;          /* (B, dim, dim) */
+    float* grad_x;           /* (B, dim): dL/dx (uniform) or dL/dr (per-interval clock) */
+    float* grad_q1;          /* (B, dim), uniform only */
+    float* grad_q2;          /* (B, dim, dim), uniform only */
     /* workspaces: fwd_ws is written by the forward and read by the backward (chunk aggregates and
        carries); bwd_ws is private to the backward */
     void* fwd_ws;
     size_t fwd_ws_bytes;
     void* bwd_ws;
     size_t bwd_ws_bytes;
+    /* backward, per-interval clock only */
+    float* grad_dtheta;      /* (B, T): dL/d(dtheta_t) */
 } ews_diag_args;
 
 int ews_diag_workspace_size(const ews_diag_args* a, size_t* fwd_bytes, size_t* bwd_bytes);
