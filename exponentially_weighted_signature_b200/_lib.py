@@ -36,6 +36,9 @@ EXPORTED = (
     "ews_dense_workspace_size",
     "ews_dense_fwd",
     "ews_dense_bwd",
+    "ews_block_workspace_size",
+    "ews_block_fwd",
+    "ews_block_bwd",
     "ews_read_device_status",
     "ews_error_string",
     "ews_version",
@@ -78,6 +81,37 @@ class DiagArgs(ctypes.Structure):
         ("bwd_ws", _vp),
         ("bwd_ws_bytes", _c_size),
         ("grad_dtheta", _vp),
+    ]
+
+
+class BlockArgs(ctypes.Structure):
+    """Mirror of ``ews_block_args``."""
+
+    _fields_ = [
+        ("batch", _c_int),
+        ("steps", _c_int),
+        ("d_in", _c_int),
+        ("dim", _c_int),
+        ("depth", _c_int),
+        ("chunk", _c_int),
+        ("readout", _c_int),
+        ("flags", ctypes.c_uint),
+        ("series_q", _c_int),
+        ("spin_limit", _c_int),
+        ("path", _vp),
+        ("clock", _vp),
+        ("blocks", _vp),
+        ("lift", _vp),
+        ("out", _vp),
+        ("grad_out", _vp),
+        ("grad_dx", _vp),
+        ("grad_dtheta", _vp),
+        ("grad_blocks", _vp),
+        ("grad_lift", _vp),
+        ("fwd_ws", _vp),
+        ("fwd_ws_bytes", _c_size),
+        ("bwd_ws", _vp),
+        ("bwd_ws_bytes", _c_size),
     ]
 
 
@@ -147,6 +181,12 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         for name in ("ews_dense_fwd", "ews_dense_bwd"):
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.POINTER(DenseArgs), _vp]
+            fn.restype = _c_int
+        lib.ews_block_workspace_size.argtypes = [ctypes.POINTER(BlockArgs), ctypes.POINTER(_c_size), ctypes.POINTER(_c_size)]
+        lib.ews_block_workspace_size.restype = _c_int
+        for name in ("ews_block_fwd", "ews_block_bwd"):
+            fn = getattr(lib, name)
+            fn.argtypes = [ctypes.POINTER(BlockArgs), _vp]
             fn.restype = _c_int
         lib.ews_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(_c_int)]
         lib.ews_read_device_status.restype = _c_int

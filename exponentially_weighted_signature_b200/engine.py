@@ -251,3 +251,68 @@ class DiagScanClock(torch.autograd.Function):
         gpath = gdx if increments else increments_to_knots_grad(gdx)
         gclock = increments_to_knots_grad(gdt[..., None])[..., 0]
         return gpath.to(path_dtype), gclock.to(clock_dtype), gr, glift, None, None, None, None, None
+
+
+class BlockScan(torch.autograd.Function):
+    """Block engine (2x2 blocks, depth 3, per-interval clock): (path, clock knots, blocks (K, 2, 2), lift)
+    -> flat EWS (prefix or terminal). The backward returns the gradients of the path, the clock, the
+    blocks and the lift."""
+
+    @staticmethod
+    def forward(ctx, path, clock, blocks, lift, readout, flags, chunk, increments, series_q):
+        _require_cuda(path, clock, blocks, lift)
+        lib = _lib.load()
+        B = path.shape[0]
+        T = path.shape[1] if increments else path.shape[1] - 1
+        d_in = path.shape[2]
+        N = 2 * blocks.shape[0]
+        D = N + N * N + N * N * N
+        dev = path.device
+        path_c = path.contiguous()
+        clock_c = clock.contiguous().float()
+        blocks_c = blocks.contiguous().float()
+        lift_c = None if lift is None else lift.contiguous().float()
+        out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
+        a = _lib.BlockArgs()
+        a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 3
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, 0
+        fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        _lib.check(lib.ews_block_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_block_workspace_size")
+        fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
+        a.path, a.clock, a.blocks, a.lift = _ptr(path_c), _ptr(clock_c), _ptr(blocks_c), _ptr(lift_c)
+        a.out = _ptr(out)
+        a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
+        with _timed("ews_block_fwd", dev, B * T):
+            _lib.check(lib.ews_block_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_block_fwd")
+        ctx.meta = (readout, flags, chunk, increments, series_q, B, T, d_in, N, bb.value, path.dtype, clock.dtype)
+        ctx.has_lift = lift is not None
+        empty = torch.empty(0, device=dev)
+        ctx.save_for_backward(path_c, clock_c, blocks_c, lift_c if lift_c is not None else empty, out, fwd_ws)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        readout, flags, chunk, increments, series_q, B, T, d_in, N, bwd_bytes, path_dtype, clock_dtype = ctx.meta
+        path, clock, blocks, lift, out, fwd_ws = ctx.saved_tensors
+        lift = lift if ctx.has_lift else None
+        lib = _lib.load()
+        dev = path.device
+        g = grad_out.contiguous().float()
+        bwd_ws = torch.empty(bwd_bytes, dtype=torch.uint8, device=dev)
+        gdx = torch.empty((B, T, d_in), device=dev, dtype=torch.float32)
+        gdt = torch.empty((B, T), device=dev, dtype=torch.float32)
+        gblk = torch.empty_like(blocks)
+        glift = torch.empty((N, d_in), device=dev, dtype=torch.float32) if lift is not None else None
+        a = _lib.BlockArgs()
+        a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 3
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, 0
+        a.path, a.clock, a.blocks, a.lift = _ptr(path), _ptr(clock), _ptr(blocks), _ptr(lift)
+        a.out, a.grad_out = _ptr(out), _ptr(g)
+        a.grad_dx, a.grad_dtheta, a.grad_blocks, a.grad_lift = _ptr(gdx), _ptr(gdt), _ptr(gblk), _ptr(glift)
+        a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fwd_ws.numel()
+        a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
+        with _timed("ews_block_bwd", dev, B * T):
+            _lib.check(lib.ews_block_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_block_bwd")
+        gpath = gdx if increments else increments_to_knots_grad(gdx)
+        gclock = increments_to_knots_grad(gdt[..., None])[..., 0]
+        return gpath.to(path_dtype), gclock.to(clock_dtype), gblk, glift, None, None, None, None, None

@@ -108,12 +108,16 @@ class EWS(nn.Module):
         if jordan_flows:
             raise ValueError("jordan_flows needs combine='block_kernel' and a jordan_repeated A with uniform chains")
         self.jordan_flows = False
-        if is_diagonal(self.A_param):
-            self.engine = "diag"
+        sizes = self.block_sizes
+        if self.N == 3:
+            pairs = sizes is not None and (all(s == 2 for s in sizes) or all(s == 1 for s in sizes))
+            if not (pairs and self.d % 2 == 0 and self.d <= 8):
+                raise NotImplementedError("depth N=3 runs on the block engine: 2x2 (or 1x1) blocks, state dim even and <= 8")
+            self.engine = "block"
+        elif self.N == 2:
+            self.engine = "diag" if is_diagonal(self.A_param) else "dense"
         else:
-            self.engine = "dense"
-        if self.N != 2:
-            raise NotImplementedError(f"the {self.engine} engine is built for depth N=2")
+            raise NotImplementedError("the B200 engines are built for depths N=2 and N=3")
 
     @property
     def signature_dim(self) -> int:
@@ -129,6 +133,10 @@ class EWS(nn.Module):
             if not uniform:
                 raise NotImplementedError("the dense engine is built for the uniform-clock reweighting modes")
             return self._flat_dense(path, clock, readout, a_scale, lift, increments, basepoint)
+        if self.engine == "block":
+            if basepoint:
+                raise NotImplementedError("the block engine runs the displacement and displacement_uniform modes")
+            return self._flat_block(path, clock, readout, a_scale, lift, increments)
         kernel_readout = _lib.EWS_READOUT_TERMINAL if readout == "terminal" else _lib.EWS_READOUT_PREFIX
         if not uniform:
             return self._flat_diag_clock(path, clock, kernel_readout, a_scale, lift, increments)
@@ -149,6 +157,39 @@ class EWS(nn.Module):
         else:
             path = path.to(torch.float32)
         return engine.DiagScan.apply(path, x, q1, q2, lift, kernel_readout, flags, self.combine_chunk, increments)
+
+    def _flat_block(self, path, clock, readout, a_scale, lift, increments):
+        """Depth 3 on 2x2 blocks: every interval has its own clock step (ews/core/chen_scan.py:155-168); a
+        uniform clock is that with equal steps (the cached flow of displacement_uniform agrees with the
+        per-interval one up to the rounding of the clock steps)."""
+        if self.series_q > 8:
+            raise NotImplementedError("the block engine evaluates series local terms up to series_q=8")
+        A = self.A_param().to(torch.float32) * a_scale
+        K = self.d // 2
+        blocks = torch.stack([A[2 * k : 2 * k + 2, 2 * k : 2 * k + 2] for k in range(K)])
+        kernel_readout = _lib.EWS_READOUT_TERMINAL if readout == "terminal" else _lib.EWS_READOUT_PREFIX
+        flags = _lib.EWS_F_DETERMINISTIC if _DETERMINISTIC else 0
+        if increments:
+            flags |= _lib.EWS_F_INCREMENTS
+            if path.dtype == torch.bfloat16:
+                flags |= _lib.EWS_F_BF16
+            else:
+                path = path.to(torch.float32)
+        else:
+            path = path.to(torch.float32)
+        clock = clock.to(torch.float32)
+        needs_grad = torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (path, clock, blocks, lift)
+        )
+        if kernel_readout == _lib.EWS_READOUT_TERMINAL and needs_grad:
+            # the block backward runs on the prefix stream (the terminal value is its last row)
+            out = engine.BlockScan.apply(
+                path, clock, blocks, lift, _lib.EWS_READOUT_PREFIX, flags, self.combine_chunk, increments, self.series_q
+            )
+            return out[:, -1]
+        return engine.BlockScan.apply(
+            path, clock, blocks, lift, kernel_readout, flags, self.combine_chunk, increments, self.series_q
+        )
 
     def _flat_diag_clock(self, path, clock, kernel_readout, a_scale, lift, increments):
         """The "displacement" mode: every interval has its own clock step, flow and series tables

@@ -176,6 +176,46 @@ int ews_dense_workspace_size(const ews_dense_args* a, size_t* fwd_bytes, size_t*
 int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream);
 int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream);
 
+/* ---- block engine: A block-diagonal with 2x2 blocks, depth 3, per-interval clock ----------------
+ * Replaces combine_packed(kind="block_kernel", block_sizes=(2,)*K) fed by leaf="series"
+ * (ews/core/kernels/combine.py:233-258; forward ews/core/kernels/pallas_combine.py:1342-1422 and
+ * :1221-1289, custom VJP :1698-1801; series leaf ews/core/series_leaf.py:72-127). dim = 2K <= 8, depth 3.
+ * Interval t of sample b has clock step dtheta_t = clock[b, t+1] - clock[b, t], flow expm(-dtheta_t A)
+ * and series local terms of order series_q (<= 8) built in the kernel from the letters
+ * b_p = (-dtheta_t A / p) b_{p-1}, b_0 = lift @ dx_t. A uniform clock is passed as evenly spaced knots.
+ *   blocks (K, 2, 2)  the diagonal blocks A_k of the generator, shared by the batch
+ * The backward returns dL/d(increments), dL/d(dtheta) (B, T), dL/dA_k (K, 2, 2) and dL/dlift. */
+typedef struct ews_block_args {
+    int batch;         /* B */
+    int steps;         /* T */
+    int d_in;          /* input channels (before the lift) */
+    int dim;           /* N = 2K <= 8 */
+    int depth;         /* 3 */
+    int chunk;         /* chunk length (0: the library's choice) */
+    int readout;       /* EWS_READOUT_* */
+    unsigned flags;    /* EWS_F_INCREMENTS, EWS_F_BF16, EWS_F_DETERMINISTIC, EWS_F_TEST_WITHHOLD */
+    int series_q;      /* series order, 0..8 */
+    int spin_limit;    /* polls before a look-back wait gives up (0: default) */
+    const void* path;        /* (B, T+1, d_in) knots or (B, T, d_in) increments; f32 or bf16 */
+    const float* clock;      /* (B, T+1) clock knots */
+    const float* blocks;     /* (K, 2, 2) */
+    const float* lift;       /* (dim, d_in), or NULL for the identity (d_in == dim) */
+    float* out;              /* (B, T, 1 + N + N^2 + N^3) prefix or (B, 1 + ...) terminal */
+    const float* grad_out;   /* same shape as out */
+    float* grad_dx;          /* (B, T, d_in) */
+    float* grad_dtheta;      /* (B, T) */
+    float* grad_blocks;      /* (K, 2, 2) */
+    float* grad_lift;        /* (dim, d_in) or NULL */
+    void* fwd_ws;
+    size_t fwd_ws_bytes;
+    void* bwd_ws;
+    size_t bwd_ws_bytes;
+} ews_block_args;
+
+int ews_block_workspace_size(const ews_block_args* a, size_t* fwd_bytes, size_t* bwd_bytes);
+int ews_block_fwd(const ews_block_args* a, ews_stream_t stream);
+int ews_block_bwd(const ews_block_args* a, ews_stream_t stream);
+
 /* ---- utilities --------------------------------------------------------------------------------- */
 /* Copies the device-side status word of a workspace (EWS_OK or EWS_ERR_LOOKBACK_TIMEOUT) to the host;
  * synchronises the stream. */
