@@ -31,7 +31,8 @@ sys.path.insert(0, ROOT)
 METRIC = "EWS fwd+bwd (batch·steps)/s at 1/2/4/8 B200, % HBM/TC roofline vs JAX CPU"
 UNIT = "batch·steps/s"
 L2_BYTES = 126 * 1024 * 1024
-KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 2, "ews_dense_bwd": 2}
+KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 2, "ews_dense_bwd": 2,
+                    "ews_block_fwd": 1, "ews_block_bwd": 2}
 
 
 def _peaks():
@@ -143,10 +144,56 @@ def _dense_setup(cfg, rank, world, device, precision, batch=None):
 
     d_in = x_host.shape[-1]
     out_row = 4 * (1 + D)
-    # the dense path is tensor-core bound: algorithmic GEMM flops per unit (one sample-interval) are two
-    # N^3 flow products in the forward (2 * 2N^3) and four N^2 x N products in the backward (4 * 2N^3 / 2)
+    # the dense path is tensor-core bound: algorithmic GEMM flops per unit (one sample-interval) are the
+    # two N x N x N flow products of the forward and the four of the backward, 2 N^3 flops each
     alg = {"ews_dense_fwd": 2 * 2 * N**3, "ews_dense_bwd": 4 * 2 * N**3}
     meta = dict(bound="tensor", B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout="prefix", dtype="f32", precision="f32")
+    ws_bytes = x_host.numel() * 4 + Bl * T * out_row
+    return dict(step=step, params=params, x_host=x_host, clock_host=clock_host, alg=alg, meta=meta,
+                ws_bytes=ws_bytes, units=Bl * T, case=case)
+
+
+def _block_setup(cfg, rank, world, device, precision, batch=None):
+    """Per-rank inputs and model of the 2x2-block, depth-3 configuration (config3)."""
+    from exponentially_weighted_signature_b200 import EWS, AParamBlockDiag, B as Lift, workloads, series
+    from exponentially_weighted_signature_b200.parallel import shard_range
+
+    case = getattr(workloads, cfg)(**({"B": batch} if batch else {}))
+    Bg, T, N = case["B"], case["T"], case["N"]
+    if Bg % world == 0:
+        s0, s1 = shard_range(Bg, rank, world)
+        scaling = "strong"
+    else:
+        s0, s1 = 0, Bg
+        scaling = "weak"
+    A = case["A"]
+    x_max = float(np.linalg.norm(A, 2)) * float(np.diff(case["clock"], axis=1).max())
+    q = min(8, max(2, series.suggest_series_q(x_max, 3, 1e-14)))
+    blocks = [torch.tensor(A[2 * k : 2 * k + 2, 2 * k : 2 * k + 2], dtype=torch.float32) for k in range(N // 2)]
+    layer = EWS(AParamBlockDiag(blocks, (2,) * (N // 2)), N=3, reweighting_mode="displacement", series_q=q).to(device)
+    lift = Lift(torch.tensor(case["lift"], dtype=torch.float32), preserve_first_channel=False).to(device)
+    x_host = torch.tensor(case["path"][s0:s1], dtype=torch.float32)
+    clock_host = torch.tensor(case["clock"][s0:s1], dtype=torch.float32)
+    params = list(layer.parameters()) + list(lift.parameters())
+    Bl = s1 - s0
+    D = N + N * N + N * N * N
+    g = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    w = torch.randn((Bl, T, 1 + D), generator=g).to(device)
+
+    def step(x, clock):
+        clock = clock.detach().requires_grad_(True)  # the input-dependent clock: d/dtheta flows back
+        out = layer(x, clock, readout="prefix", lift=lift.full_matrix())
+        loss = (out * w).sum()
+        loss.backward()
+        return loss
+
+    d_in = x_host.shape[-1]
+    out_row = 4 * (1 + D)
+    # algorithmic bytes per unit: increments and clock step in, prefix row out; the backward reads the
+    # output gradient and writes the increment and clock-step gradients
+    alg = {"ews_block_fwd": 4 * d_in + 4 + out_row, "ews_block_bwd": out_row + 4 * d_in + 4 + 4 * d_in + 4}
+    meta = dict(B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout="prefix", dtype="f32",
+                precision="f32", depth=3)
     ws_bytes = x_host.numel() * 4 + Bl * T * out_row
     return dict(step=step, params=params, x_host=x_host, clock_host=clock_host, alg=alg, meta=meta,
                 ws_bytes=ws_bytes, units=Bl * T, case=case)
@@ -231,7 +278,11 @@ def _cpu_baseline(cfg, precision, budget_s=20.0):
         to_matrix = lambda m: m
         x_max = float(np.linalg.norm(case["A"], 2)) / T
     lift = torch.tensor(case["lift"], dtype=torch.float32)
-    q = max(2, series.suggest_series_q(x_max, 2, 1e-14))
+    depth = case.get("depth", 2)
+    mode = "displacement" if cfg == "config3" else "displacement_uniform"
+    if cfg == "config3":
+        x_max = float(np.linalg.norm(case["A"], 2)) * float(np.diff(case["clock"], axis=1).max())
+    q = min(8, max(2, series.suggest_series_q(x_max, depth, 1e-14)))
     if cfg == "config5":
         inc = torch.tensor(case["increments"][:1], dtype=torch.float32)
         path = torch.cat([torch.zeros(1, 1, inc.shape[-1]), torch.cumsum(inc, 1)], 1)
@@ -250,7 +301,7 @@ def _cpu_baseline(cfg, precision, budget_s=20.0):
         if cfg == "config5":
             out = O.log_ews_layer(y, clock[:, : Ts + 1], to_matrix(A), 2, series_q=q, reweighting_mode="displacement_uniform", readout="terminal", terminal_reduce="assoc")
         else:
-            out = O.ews_layer(y, clock[:, : Ts + 1], to_matrix(A), 2, series_q=q, reweighting_mode="displacement_uniform", readout="prefix")
+            out = O.ews_layer(y, clock[:, : Ts + 1], to_matrix(A), depth, series_q=q, reweighting_mode=mode, readout="prefix")
         out.sum().backward()
         dt = time.perf_counter() - t0
         spent += dt
@@ -271,7 +322,7 @@ def run_b200(args, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    setup_fn = _dense_setup if args.config == "config2" else _diag_setup
+    setup_fn = {"config2": _dense_setup, "config3": _block_setup}.get(args.config, _diag_setup)
     setup = setup_fn(args.config, rank, world, device, args.precision, args.batch)
     step, params = setup["step"], setup["params"]
     x = setup["x_host"].to(device)
@@ -400,7 +451,7 @@ def run_b200(args, rank, world, local_rank):
             "global_batch": meta["B_global"],
             "seq_len": meta["T"],
             "state_dim": meta["N"],
-            "depth": 2,
+            "depth": meta.get("depth", 2),
             "readout": meta["readout"],
             "series_q": meta["q"],
             "inputs": meta["precision"],
@@ -467,7 +518,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="config2", choices=["config1", "config2", "config5"])
+    ap.add_argument("--config", default="config2", choices=["config1", "config2", "config3", "config5"])
     ap.add_argument("--precision", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling on a smaller case)")
