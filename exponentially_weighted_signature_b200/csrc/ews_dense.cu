@@ -58,6 +58,8 @@ struct Params {
     float* carry;
     const float* fagg;
     float* pw;  // per sample: flow complements C(Lc) and C(last chunk), row-major (2 MM)
+    float* lam;        // backward: the cotangent stream l~_t = l_t + g_t, same layout as the prefix output
+    float* lcarry;     // backward: per chunk the cotangent arriving at its end [- | L1 | L2] (SW)
 };
 
 __host__ __device__ inline int align4(int n) { return (n + 3) & ~3; }
@@ -669,7 +671,7 @@ __host__ __device__ inline int tc_stage_floats(int W) { return TILES * tc_stage_
 
 __host__ __device__ inline size_t tc_smem_bytes(int W, int d_in, int QP) {
     size_t f = 2 * MM + 2 * 4 * MM + TILES * 32 * RQS + align4(tc_stage_floats(W)) + 2 * MM + align4(NP * d_in) +
-               2 * align4(QP * NP * d_in) + TILES * kVecPerTile + 4 * NP;
+               2 * align4(QP * NP * d_in) + TILES * kVecPerTile + 8 * NP;
     return f * sizeof(float) + 64 + 128;  // + barrier / tmem slot / broadcast, + alignment slack
 }
 
@@ -689,14 +691,15 @@ __device__ TcSmem tc_carve(unsigned char* raw, const Geom& g) {
     s.G = p; p += align4(g.QP * NP * g.d_in);
     s.H = p; p += align4(g.QP * NP * g.d_in);
     s.vec = p; p += TILES * kVecPerTile;
-    s.misc = p; p += 4 * NP;
+    s.misc = p; p += 8 * NP;
     s.bar = reinterpret_cast<uint64_t*>(p);
     s.tmem = reinterpret_cast<uint32_t*>(p + 2);
     s.bcast = reinterpret_cast<int*>(p + 4);
     return s;
 }
 
-__device__ void tc_load_tables(const Params& p, const TcSmem& s, int b) {
+// Tables of sample b; the B operand is D (forward) or D^T (the adjoint chain, transpose = true).
+__device__ void tc_load_tables(const Params& p, const TcSmem& s, int b, bool transpose = false) {
     const Geom& g = p.g;
     const int N = g.N, d = g.d_in;
     const float* m = p.tab_d + (size_t)b * N * N;
@@ -706,8 +709,9 @@ __device__ void tc_load_tables(const Params& p, const TcSmem& s, int b) {
         s.Dr[i * NP + k] = v;
         s.Dt[k * NP + i] = v;
         const float hi = __uint_as_float(tf32_bits(v));
-        s.Bhi[bk_off(i, k)] = hi;
-        s.Blo[bk_off(i, k)] = v - hi;
+        const int o = transpose ? bk_off(k, i) : bk_off(i, k);
+        s.Bhi[o] = hi;
+        s.Blo[o] = v - hi;
     }
     const float* f = p.tab_f + (size_t)b * N * d;
     for (int e = threadIdx.x; e < NP * d; e += blockDim.x) s.F[e] = (e / d) < N ? f[e] : 0.f;
@@ -1491,6 +1495,532 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
     }
 }
 
+
+// ---------------------------------------------------------------------------------- tensor-core backward
+//
+// The adjoint chain. With l~_t = l_t + g_t (the cotangent of S_t after adding row t of the output
+// gradient) the reverse recursion of one interval is
+//     l~2_{t-1} = M^T l~2_t M + g2_{t-1},      l~1_{t-1} = M^T (l~1_t + l~2_t s1_t) + g1_{t-1},
+// the forward's M S M^T with D replaced by D^T: the same two tcgen05 products per step (B operand D^T),
+// four chunks of one sample stacked into M = 128. Chunks run in reverse; the zero-carry pass gives the
+// chunk's local adjoint mu, a look-back over the later chunks (transposed chunk maps from the forward
+// aggregates) gives the cotangent arriving at the chunk's end, and the exact pass writes l~_t for every
+// interval. The gradients are then a parallel map over (sample, interval): grad_kernel.
+__global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
+    using namespace tc;
+    extern __shared__ unsigned char smem_raw[];
+    const Geom& g = p.g;
+    TcSmem s = tc_carve(smem_raw, g);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int bi = tid >> 3, bj = tid & 7;
+    const int i0 = 4 * (bi & 7), j0 = 4 * bj;
+    const bool deterministic = (g.flags & EWS_F_DETERMINISTIC) != 0;
+    const int N = g.N;
+    const int mbar_limit = 1 << 20;
+
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(s.bar)), "r"(1));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s.tmem)),
+                     "r"(64));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *s.tmem;
+    const uint32_t tP1 = tmem, tP2 = tmem + 32;
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    uint32_t phase = 0;
+    bool failed = false;
+    bool mma_pending = false;
+
+    const uint64_t dA_hi = smem_desc(smem_u32(s.Ahi), 2048, 128), dA_lo = smem_desc(smem_u32(s.Alo), 2048, 128);
+    const uint64_t dB_hi = smem_desc(smem_u32(s.Bhi), 512, 128), dB_lo = smem_desc(smem_u32(s.Blo), 512, 128);
+    const int groups = (g.C + TILES - 1) / TILES;
+    const int ntiles = g.B * groups;
+    float* vt = s.vec + warp * kVecPerTile;  // L1 (NP) | v (NP) | s1 (NP) | x (32) | U, V
+    float* RQt = s.RQ + warp * 32 * RQS;
+
+    for (;;) {
+        if (tid == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
+        __syncthreads();
+        const int tile = s.bcast[0];
+        __syncthreads();
+        if (tile >= ntiles) break;
+        const int grp_r = tile / g.B, b = tile - grp_r * g.B;
+        const int grp = groups - 1 - grp_r;  // later groups first: the look-back reads later chunks
+        const int c_me = grp * TILES + warp;
+        const bool valid_me = c_me < g.C;
+        const int t0_me = c_me * g.Lc;
+        const int len_me = valid_me ? min(g.Lc, g.T - t0_me) : 0;
+        int steps = 0;
+        for (int t = 0; t < TILES; ++t) {
+            const int c = grp * TILES + t;
+            if (c < g.C) steps = max(steps, min(g.Lc, g.T - c * g.Lc));
+        }
+        tc_load_tables(p, s, b, true);
+        __syncthreads();
+
+        float col[32];  // column `lane` of l2
+        for (int pass = 0; pass < 2 && !failed; ++pass) {
+            if (pass == 0) {
+#pragma unroll
+                for (int n = 0; n < 32; ++n) col[n] = 0.f;
+                vt[lane] = 0.f;
+            } else {
+                const float* cs = p.lcarry + ((size_t)b * g.C + (valid_me ? c_me : 0)) * g.SW;
+#pragma unroll
+                for (int n = 0; n < 32; ++n) col[n] = valid_me ? ldcg(cs + MM + NP + n * NP + lane) : 0.f;
+                vt[lane] = valid_me ? ldcg(cs + MM + lane) : 0.f;
+            }
+            __syncwarp();
+            // steps run in reverse; the chunk's last interval is len_me - 1 (shorter chunks idle on zero state)
+            float xnext = (lane < g.d_in && len_me > 0)
+                              ? input_increment(p.path, b, t0_me + len_me - 1, lane, g.T, g.d_in, g.flags) : 0.f;
+            for (int k = steps - 1; k >= 0; --k) {
+                const bool live = k < len_me;
+                const int t = t0_me + k;
+                // E0: l~ = l + g_t; the exact pass writes l~_t; rows of l~2 -> A operand
+                if (live && lane < N) {
+                    const float* grow = p.grad_out + ((size_t)b * g.T + t) * g.W;
+#pragma unroll
+                    for (int n = 0; n < 32; ++n)
+                        if (n < N) col[n] += ldcg(grow + 1 + N + n * N + lane);
+                    vt[lane] += ldcg(grow + 1 + lane);
+                }
+                __syncwarp();
+                if (pass == 1 && live && lane < N) {
+                    float* row = p.lam + ((size_t)b * g.T + t) * g.W;
+                    if (lane == 0) row[0] = 0.f;
+                    row[1 + lane] = vt[lane];
+#pragma unroll
+                    for (int n = 0; n < 32; ++n)
+                        if (n < N) row[1 + N + n * N + lane] = col[n];
+                }
+                float srow[32];
+#pragma unroll
+                for (int n = 0; n < 32; ++n) RQt[n * RQS + lane] = col[n];
+                __syncwarp();
+#pragma unroll
+                for (int n = 0; n < 32; ++n) srow[n] = RQt[lane * RQS + n];
+                __syncwarp();
+                store_a_row(s.Ahi, s.Alo, 32 * warp + lane, srow);
+                fence_proxy_async();
+                fence_before();
+                __syncthreads();
+                if (tid == 0) {
+                    fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
+                    mma_commit(s.bar);
+                }
+                // s1_t of this interval, then v = l~1 + l~2 s1 (row `lane` of l~2 against s1)
+                {
+                    const float xcur = live ? xnext : 0.f;
+                    if (lane < g.d_in && k - 1 >= 0 && k - 1 < len_me)
+                        xnext = input_increment(p.path, b, t - 1, lane, g.T, g.d_in, g.flags);
+                    tc_local(s, g, vt, xcur);
+                    const float* s1 = vt + 2 * NP;
+                    float w0 = 0.f, w1 = 0.f;
+#pragma unroll
+                    for (int n = 0; n < 32; n += 2) {
+                        w0 = fmaf(srow[n], s1[n], w0);
+                        w1 = fmaf(srow[n + 1], s1[n + 1], w1);
+                    }
+                    vt[NP + lane] = vt[lane] + (w0 + w1);
+                    __syncwarp();
+                }
+                if (!tc_wait(s, phase, mbar_limit)) {
+                    failed = mma_pending = true;
+                    break;
+                }
+                phase ^= 1;
+                // E1: row `lane` of X = l~2 - l~2 D = l~2 M -> column `lane` -> A operand row of X^T
+                float xcol[32];
+                {
+                    float pr[32];
+                    tmem_ld32(tP1 + lane_off, pr);
+#pragma unroll
+                    for (int n = 0; n < 32; ++n) RQt[lane * RQS + n] = srow[n] - pr[n];
+                    __syncwarp();
+#pragma unroll
+                    for (int n = 0; n < 32; ++n) xcol[n] = RQt[n * RQS + lane];
+                    __syncwarp();
+                    store_a_row(s.Ahi, s.Alo, 32 * warp + lane, xcol);
+                }
+                fence_proxy_async();
+                fence_before();
+                __syncthreads();
+                if (tid == 0) {
+                    fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
+                    mma_commit(s.bar);
+                }
+                // l1 <- M^T v = v - D^T v while the tensor core runs
+                {
+                    const float* v = vt + NP;
+                    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+                    for (int kk = 0; kk < NP; kk += 4) {
+                        d0 = fmaf(s.Dr[kk * NP + lane], v[kk], d0);
+                        d1 = fmaf(s.Dr[(kk + 1) * NP + lane], v[kk + 1], d1);
+                        d2 = fmaf(s.Dr[(kk + 2) * NP + lane], v[kk + 2], d2);
+                        d3 = fmaf(s.Dr[(kk + 3) * NP + lane], v[kk + 3], d3);
+                    }
+                    const float nv = v[lane] - ((d0 + d1) + (d2 + d3));
+                    __syncwarp();
+                    vt[lane] = nv;
+                    __syncwarp();
+                }
+                if (!tc_wait(s, phase, mbar_limit)) {
+                    failed = mma_pending = true;
+                    break;
+                }
+                phase ^= 1;
+                // E2: column `lane` of M^T X = X - D^T X
+                {
+                    float q2[32];
+                    tmem_ld32(tP2 + lane_off, q2);
+#pragma unroll
+                    for (int n = 0; n < 32; ++n) col[n] = xcol[n] - q2[n];
+                    fence_before();
+                    __syncwarp();
+                }
+            }
+            if (failed) break;
+            __syncthreads();
+            if (pass == 1) break;
+            // ---- local adjoints mu of the 4 chunks -> adjoint slots (the sequence's last chunk: inclusive)
+            if (valid_me) {
+                float* as = (c_me == g.C - 1 ? p.incl : p.agg) + ((size_t)b * g.C + c_me) * g.SW;
+#pragma unroll
+                for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = col[n];
+                as[MM + lane] = vt[lane];
+            }
+            __syncthreads();
+            for (int t = 0; t < TILES; ++t) {
+                const int c = grp * TILES + t;
+                if (c >= g.C) break;
+                if (c == g.C - 1) {
+                    if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(p.flags + (size_t)b * g.C + c, kFlagIncl);
+                } else {
+                    cta_publish(p.flags + (size_t)b * g.C + c, kFlagAgg);
+                }
+                __syncthreads();
+            }
+            // ---- look-back from the group's last chunk over the later chunks
+            float* W0 = s.Ahi;            // G_j (C)
+            float* W1 = s.Ahi + MM;       // X (l2 row-major)
+            float* W2 = s.Ahi + 2 * MM;   // G_j (S2)
+            float* W3 = s.Ahi + 3 * MM;   // lam (l2 row-major)
+            float* W4 = s.Alo;            // Gacc (C)
+            float* W5 = s.Alo + MM;       // Gacc (S2)
+            float* ve = s.misc;           // lam l1
+            float* va = s.misc + NP;      // Gacc S1
+            float* vx = s.misc + 2 * NP;  // X l1
+            float* vg = s.misc + 3 * NP;  // G_j S1
+            float* v1 = s.misc + 4 * NP;  // scratch
+            float* v2 = s.misc + 5 * NP;  // scratch
+            float* v3 = s.misc + 6 * NP;  // scratch
+            float* T0 = s.stage;
+            float* T1 = s.stage + MM;
+            for (int e = tid; e < MM; e += blockDim.x) W3[e] = 0.f;
+            if (tid < NP) ve[tid] = 0.f;
+            __syncthreads();
+            const int c_last = min(grp * TILES + TILES - 1, g.C - 1);
+            if (c_last < g.C - 1) {
+                identity_smem(W4, va, W5);
+                __syncthreads();
+                int j = c_last + 1;
+                for (;;) {
+                    const int f = tc_cta_wait(p, s, p.flags + (size_t)b * g.C + j, deterministic ? kFlagIncl : kFlagAgg, tile);
+                    if (f < 0) {
+                        failed = true;
+                        break;
+                    }
+                    const size_t sj = ((size_t)b * g.C + j) * g.SW;
+                    {
+                        const float* src = (f == kFlagIncl ? p.incl : p.agg) + sj;
+                        for (int e = tid; e < MM; e += blockDim.x) W1[e] = ldcg(src + MM + NP + e);
+                        if (tid < NP) vx[tid] = ldcg(src + MM + tid);
+                    }
+                    __syncthreads();
+                    float X2[4][4];
+                    load_rowmajor(W1, X2, i0, j0);
+                    __syncthreads();
+                    apply_JT_smem(W4, va, vx, X2, W1, T0, v1, v2, i0, j0);  // X <- J(Gacc)^T X
+                    for (int e = tid; e < MM; e += blockDim.x) W3[e] += W1[e];
+                    if (tid < NP) ve[tid] += vx[tid];
+                    __syncthreads();
+                    if (f == kFlagIncl) break;
+                    load_slot_smem(p.fagg + sj, W0, vg, W2);
+                    __syncthreads();
+                    chen_mul_smem(W4, va, W5, W0, vg, W2, W4, va, W5, T0, T1, v3, i0, j0);  // Gacc <- Gacc (x) G_j
+                    ++j;
+                }
+                if (failed) break;
+            }
+            // ---- the group's chunks, last to first: lam_in(c) -> carry slot; incl(c) = J(G_c)^T lam + mu_c
+            for (int t = TILES - 1; t >= 0; --t) {
+                const int c = grp * TILES + t;
+                if (c >= g.C) continue;
+                const size_t sc = ((size_t)b * g.C + c) * g.SW;
+                for (int e = tid; e < MM; e += blockDim.x) p.lcarry[sc + MM + NP + e] = W3[e];
+                if (tid < NP) p.lcarry[sc + MM + tid] = ve[tid];
+                if (c == g.C - 1) {
+                    // nothing arrives after the last chunk: incl = mu (already published)
+                    const float* mu = p.incl + sc;
+                    for (int e = tid; e < MM; e += blockDim.x) W3[e] = ldcg(mu + MM + NP + e);
+                    if (tid < NP) ve[tid] = ldcg(mu + MM + tid);
+                    __syncthreads();
+                    continue;
+                }
+                load_slot_smem(p.fagg + sc, W0, vg, W2);
+                __syncthreads();
+                float X2[4][4];
+                load_rowmajor(W3, X2, i0, j0);
+                __syncthreads();
+                apply_JT_smem(W0, vg, ve, X2, W3, T0, v1, v2, i0, j0);  // lam <- J(G_c)^T lam
+                {
+                    const float* mu = p.agg + sc;
+                    for (int e = tid; e < MM; e += blockDim.x) W3[e] += ldcg(mu + MM + NP + e);
+                    if (tid < NP) ve[tid] += ldcg(mu + MM + tid);
+                }
+                __syncthreads();
+                {
+                    float* is = p.incl + sc;
+                    for (int e = tid; e < MM; e += blockDim.x) is[MM + NP + e] = W3[e];
+                    if (tid < NP) is[MM + tid] = ve[tid];
+                }
+                __syncthreads();
+                cta_publish(p.flags + (size_t)b * g.C + c, kFlagIncl);
+                __syncthreads();
+            }
+            __syncthreads();
+        }
+        if (failed) break;
+    }
+    if (failed && tid == 0) {
+        if (atomicCAS(&p.st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) p.st->err_tile = -1;
+        if (mma_pending)
+            for (int it = 0; it < (1 << 20); ++it)
+                if (mbar_try(s.bar, phase)) break;
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64));
+}
+
+// The gradients as a parallel map over (sample, interval), from the cotangent stream l~_t and the forward
+// states S_{t-1} (prefix output row t-1): with u = M S1p, X = S2p M^T, Z = M^T l~2,
+//   dM += l~2 X^T + Z^T S2p + du S1p^T,   du = l~1 + l~2 s1,   ds1 = l~1 + l~2^T u,
+//   dU_a = l~2 V_a,  dV_a = l~2^T U_a,    dF += ds1 dx^T,  dG_a += dU_a dx^T,  dH_a += dV_a dx^T,
+//   dx_t = F^T ds1 + sum_a G_a^T dU_a + H_a^T dV_a.
+// One CTA of 128 threads per (chunk, sample); thread (r, c) owns the 4 x 2 block at rows 4r, columns 2c.
+constexpr int GNT = 128;
+
+__device__ __forceinline__ void gemm42(const float* __restrict__ At, const float* __restrict__ Bm, float acc[4][2],
+                                       int i0, int j0) {
+#pragma unroll 8
+    for (int k = 0; k < NP; ++k) {
+        const float4 a = *reinterpret_cast<const float4*>(At + k * NP + i0);
+        const float2 b = *reinterpret_cast<const float2*>(Bm + k * NP + j0);
+        const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            acc[r][0] = fmaf(av[r], b.x, acc[r][0]);
+            acc[r][1] = fmaf(av[r], b.y, acc[r][1]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
+    extern __shared__ float smem[];
+    const Geom& g = p.g;
+    const int N = g.N, d = g.d_in, QP = g.QP;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int i0 = 4 * (tid >> 4), j0 = 2 * (tid & 15);
+    float* Lr = smem;            // l~2 row-major
+    float* Lk = Lr + MM;         // l~2 k-major
+    float* Sr = Lk + MM;         // S2p row-major
+    float* Sk = Sr + MM;         // S2p k-major
+    float* Xk = Sk + MM;         // X k-major
+    float* Zr = Xk + MM;         // Z row-major
+    float* Dr = Zr + MM;         // D row-major
+    float* Dt = Dr + MM;         // D k-major
+    float* vec = Dt + MM;        // L1, S1p, u, s1, du, ds1 (NP each)
+    float* L1 = vec, *S1p = vec + NP, *u = vec + 2 * NP, *s1 = vec + 3 * NP, *du = vec + 4 * NP, *ds1 = vec + 5 * NP;
+    float* UV = vec + 6 * NP;    // U, V, dU, dV (NP x QMAX each)
+    float* U = UV, *V = UV + NP * QMAX, *dU = UV + 2 * NP * QMAX, *dV = UV + 3 * NP * QMAX;
+    float* x = UV + 4 * NP * QMAX;                 // 32
+    float* F = x + 32;                             // NP x d
+    float* Gt = F + align4(NP * d);                // QP x NP x d
+    float* Ht = Gt + align4(QP * NP * d);
+    float* tacc = Ht + align4(QP * NP * d);        // (1 + 2 QP) x NP x d
+    const int tabn = (1 + 2 * QP) * NP * d;
+
+    const int tile = blockIdx.x;  // c * B + b, the reduction's order
+    const int c = tile / g.B, b = tile - c * g.B;
+    const int t0 = c * g.Lc;
+    const int len = min(g.Lc, g.T - t0);
+    {
+        const float* m = p.tab_d + (size_t)b * N * N;
+        for (int e = tid; e < MM; e += GNT) {
+            const int i = e / NP, k = e - i * NP;
+            const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
+            Dr[e] = v;
+            Dt[k * NP + i] = v;
+            Lr[e] = Lk[e] = Sr[e] = Sk[e] = 0.f;
+        }
+        const float* f = p.tab_f + (size_t)b * N * d;
+        for (int e = tid; e < NP * d; e += GNT) F[e] = (e / d) < N ? f[e] : 0.f;
+        const size_t gq = (size_t)QP * N * d;
+        for (int e = tid; e < QP * NP * d; e += GNT) {
+            const int a = e / (NP * d), r = e - a * NP * d, i = r / d, cc = r - i * d;
+            const bool ok = i < N;
+            Gt[e] = ok ? p.tab_g[(size_t)b * gq + ((size_t)a * N + i) * d + cc] : 0.f;
+            Ht[e] = ok ? p.tab_h[(size_t)b * gq + ((size_t)a * N + i) * d + cc] : 0.f;
+        }
+        for (int e = tid; e < tabn; e += GNT) tacc[e] = 0.f;
+        for (int e = tid; e < 6 * NP; e += GNT) vec[e] = 0.f;
+    }
+    float dM[4][2];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) dM[r][0] = dM[r][1] = 0.f;
+    __syncthreads();
+    for (int k = 0; k < len; ++k) {
+        const int t = t0 + k;
+        // (1) l~_t and S_{t-1} into shared memory (padded entries stay zero), dx_t
+        const float* lrow = p.lam + ((size_t)b * g.T + t) * g.W;
+        const float* srow = t > 0 ? p.out + ((size_t)b * g.T + t - 1) * g.W : nullptr;
+        for (int e = tid; e < N * N; e += GNT) {
+            const int i = e / N, j = e - i * N;
+            const float lv = ldcg(lrow + 1 + N + e);
+            const float sv = srow ? ldcg(srow + 1 + N + e) : 0.f;
+            Lr[i * NP + j] = lv;
+            Lk[j * NP + i] = lv;
+            Sr[i * NP + j] = sv;
+            Sk[j * NP + i] = sv;
+        }
+        if (tid < N) {
+            L1[tid] = ldcg(lrow + 1 + tid);
+            S1p[tid] = srow ? ldcg(srow + 1 + tid) : 0.f;
+        }
+        if (tid < d) x[tid] = input_increment(p.path, b, t, tid, g.T, d, g.flags);
+        __syncthreads();
+        // (2) X = S2p - S2p D^T, Z = l~2 - D^T l~2 (blocks); local vectors (warp 0)
+        float X[4][2] = {}, Z[4][2] = {};
+        gemm42(Sk, Dt, X, i0, j0);
+        gemm42(Dr, Lr, Z, i0, j0);
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                X[r][q] = Sr[(i0 + r) * NP + j0 + q] - X[r][q];
+                Z[r][q] = Lr[(i0 + r) * NP + j0 + q] - Z[r][q];
+            }
+        if (warp == 0) {
+            const int l = lane;
+            float acc = 0.f;
+            for (int kk = 0; kk < NP; ++kk) acc = fmaf(Dr[l * NP + kk], S1p[kk], acc);
+            u[l] = S1p[l] - acc;
+            float a1 = 0.f;
+            for (int cc = 0; cc < d; ++cc) a1 = fmaf(F[l * d + cc], x[cc], a1);
+            s1[l] = a1;
+            for (int a = 0; a < QP; ++a) {
+                float ga = 0.f, ha = 0.f;
+                for (int cc = 0; cc < d; ++cc) {
+                    ga = fmaf(Gt[((size_t)a * NP + l) * d + cc], x[cc], ga);
+                    ha = fmaf(Ht[((size_t)a * NP + l) * d + cc], x[cc], ha);
+                }
+                U[l * QMAX + a] = ga;
+                V[l * QMAX + a] = ha;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                Xk[(j0 + q) * NP + i0 + r] = X[r][q];
+                Zr[(i0 + r) * NP + j0 + q] = Z[r][q];
+            }
+        // (3) vector cotangents: warp 0 du, dU (rows of l~2); warp 1 ds1, dV (columns)
+        if (warp == 0) {
+            const int i = lane;
+            float acc = L1[i];
+            for (int j = 0; j < NP; ++j) acc = fmaf(Lr[i * NP + j], s1[j], acc);
+            du[i] = acc;
+            for (int a = 0; a < QP; ++a) {
+                float e = 0.f;
+                for (int j = 0; j < NP; ++j) e = fmaf(Lr[i * NP + j], V[j * QMAX + a], e);
+                dU[i * QMAX + a] = e;
+            }
+        } else if (warp == 1) {
+            const int j = lane;
+            float acc = L1[j];
+            for (int i = 0; i < NP; ++i) acc = fmaf(Lk[j * NP + i], u[i], acc);
+            ds1[j] = acc;
+            for (int a = 0; a < QP; ++a) {
+                float e = 0.f;
+                for (int i = 0; i < NP; ++i) e = fmaf(Lk[j * NP + i], U[i * QMAX + a], e);
+                dV[j * QMAX + a] = e;
+            }
+        }
+        __syncthreads();
+        // (4) dM += l~2 X^T + Z^T S2p + du S1p^T
+        gemm42(Lk, Xk, dM, i0, j0);
+        gemm42(Zr, Sr, dM, i0, j0);
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int q = 0; q < 2; ++q) dM[r][q] = fmaf(du[i0 + r], S1p[j0 + q], dM[r][q]);
+        // (5) table gradients and dx_t
+        for (int e = tid; e < tabn; e += GNT) {
+            const int blk = e / (NP * d), rem = e - blk * NP * d, i = rem / d, cc = rem - i * d;
+            const float coef = blk == 0 ? ds1[i] : (blk <= QP ? dU[i * QMAX + blk - 1] : dV[i * QMAX + blk - 1 - QP]);
+            tacc[e] = fmaf(coef, x[cc], tacc[e]);
+        }
+        for (int cc = warp; cc < d; cc += GNT / 32) {
+            const int i = lane;
+            float acc = F[i * d + cc] * ds1[i];
+            for (int a = 0; a < QP; ++a) {
+                acc = fmaf(Gt[((size_t)a * NP + i) * d + cc], dU[i * QMAX + a], acc);
+                acc = fmaf(Ht[((size_t)a * NP + i) * d + cc], dV[i * QMAX + a], acc);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+            if (lane == 0) p.grad_dx[((size_t)b * g.T + t) * d + cc] = acc;
+        }
+        __syncthreads();
+    }
+    float* part = p.partials + (size_t)tile * (MM + tabn);
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) part[(i0 + r) * NP + j0 + q] = dM[r][q];
+    for (int e = tid; e < tabn; e += GNT) part[MM + e] = tacc[e];
+}
+
+static size_t grad_smem_bytes(const Geom& g) {
+    const size_t f = 8 * (size_t)MM + 6 * NP + 4 * NP * QMAX + 32 + align4(NP * g.d_in) + 2 * align4(g.QP * NP * g.d_in) +
+                     (size_t)(1 + 2 * g.QP) * NP * g.d_in;
+    return f * sizeof(float);
+}
+
 // Deterministic per-sample reduction over chunks, compacted to the real dimensions.
 __global__ void reduce_kernel(Params p, float* grad_d, float* grad_f, float* grad_g, float* grad_h) {
     const Geom& g = p.g;
@@ -1596,6 +2126,10 @@ static WsLayout bwd_layout(const Geom& g) {
     o += slots;
     L.partials = o;
     o += al256(sizeof(float) * (size_t)g.ntiles * (MM + (1 + 2 * g.QP) * NP * g.d_in));
+    L.carry = o;  // per chunk: the cotangent arriving at its end
+    o += slots;
+    L.pw = o;     // the cotangent stream l~_t, laid out as the prefix output
+    o += al256(sizeof(float) * (size_t)g.B * g.T * g.W);
     L.total = o;
     return L;
 }
@@ -1709,8 +2243,28 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     p.agg = (float*)(ws + L.agg);
     p.incl = (float*)(ws + L.incl);
     p.fagg = (const float*)(fws + F.agg);
-    rc = launch(bwd_kernel, p, sizeof(float) * g.bsmem_floats, s);
-    if (rc != EWS_OK) return rc;
+    p.lcarry = (float*)(ws + L.carry);
+    p.lam = (float*)(ws + L.pw);
+    {
+        const size_t smem = tc::tc_smem_bytes(g.W, g.d_in, g.QP);
+        if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+        cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        int per_sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_tc_kernel, tc::NTH, smem);
+        if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
+        const int groups = (g.C + tc::TILES - 1) / tc::TILES;
+        int grid = per_sm * num_sms();
+        if (grid > g.B * groups) grid = g.B * groups;
+        bwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
+        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    }
+    {
+        const size_t smem = grad_smem_bytes(g);
+        if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+        cudaFuncSetAttribute(grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        grad_kernel<<<g.C * g.B, GNT, smem, s>>>(p);
+        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    }
     const size_t total = (size_t)g.B * (g.N * g.N + (1 + 2 * g.QP) * g.N * g.d_in);
     const int threads = 256;
     reduce_kernel<<<(int)std::min<size_t>((total + threads - 1) / threads, 65535), threads, 0, s>>>(
