@@ -1851,6 +1851,7 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
     extern __shared__ float smem[];
     const Geom& g = p.g;
     const int N = g.N, d = g.d_in, QP = g.QP;
+    const int N2 = N * N;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int i0 = 4 * (tid >> 4), j0 = 2 * (tid & 15);
     float* Lr = smem;            // l~2 row-major
@@ -1895,100 +1896,129 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
             Ht[e] = ok ? p.tab_h[(size_t)b * gq + ((size_t)a * N + i) * d + cc] : 0.f;
         }
         for (int e = tid; e < tabn; e += GNT) tacc[e] = 0.f;
-        for (int e = tid; e < 6 * NP; e += GNT) vec[e] = 0.f;
+        for (int e = tid; e < 6 * NP + 4 * NP * QMAX + 32; e += GNT) vec[e] = 0.f;
     }
     float dM[4][2];
 #pragma unroll
     for (int r = 0; r < 4; ++r) dM[r][0] = dM[r][1] = 0.f;
+    // the next interval's rows, prefetched into registers (entries tid + 128 m of the level-2 block)
+    float pl[8], ps[8], pl1 = 0.f, ps1 = 0.f, px = 0.f;
+    auto prefetch = [&](int t) {
+        const float* lrow = p.lam + ((size_t)b * g.T + t) * g.W;
+        const float* srow = t > 0 ? p.out + ((size_t)b * g.T + t - 1) * g.W : nullptr;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int e = tid + GNT * m;
+            pl[m] = e < N2 ? ldcg(lrow + 1 + N + e) : 0.f;
+            ps[m] = (e < N2 && srow) ? ldcg(srow + 1 + N + e) : 0.f;
+        }
+        pl1 = tid < N ? ldcg(lrow + 1 + tid) : 0.f;
+        ps1 = (tid < N && srow) ? ldcg(srow + 1 + tid) : 0.f;
+        px = tid < d ? input_increment(p.path, b, t, tid, g.T, d, g.flags) : 0.f;
+    };
+    if (len > 0) prefetch(t0);
     __syncthreads();
     for (int k = 0; k < len; ++k) {
         const int t = t0 + k;
-        // (1) l~_t and S_{t-1} into shared memory (padded entries stay zero), dx_t
-        const float* lrow = p.lam + ((size_t)b * g.T + t) * g.W;
-        const float* srow = t > 0 ? p.out + ((size_t)b * g.T + t - 1) * g.W : nullptr;
-        for (int e = tid; e < N * N; e += GNT) {
-            const int i = e / N, j = e - i * N;
-            const float lv = ldcg(lrow + 1 + N + e);
-            const float sv = srow ? ldcg(srow + 1 + N + e) : 0.f;
-            Lr[i * NP + j] = lv;
-            Lk[j * NP + i] = lv;
-            Sr[i * NP + j] = sv;
-            Sk[j * NP + i] = sv;
+        // (1) the prefetched interval into shared memory; the next one's loads go out
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int e = tid + GNT * m;
+            if (e < N2) {
+                const int i = e / N, j = e - i * N;
+                Lr[i * NP + j] = pl[m];
+                Lk[j * NP + i] = pl[m];
+                Sr[i * NP + j] = ps[m];
+                Sk[j * NP + i] = ps[m];
+            }
         }
         if (tid < N) {
-            L1[tid] = ldcg(lrow + 1 + tid);
-            S1p[tid] = srow ? ldcg(srow + 1 + tid) : 0.f;
+            L1[tid] = pl1;
+            S1p[tid] = ps1;
         }
-        if (tid < d) x[tid] = input_increment(p.path, b, t, tid, g.T, d, g.flags);
+        if (tid < d) x[tid] = px;
         __syncthreads();
-        // (2) X = S2p - S2p D^T, Z = l~2 - D^T l~2 (blocks); local vectors (warp 0)
-        float X[4][2] = {}, Z[4][2] = {};
-        gemm42(Sk, Dt, X, i0, j0);
-        gemm42(Dr, Lr, Z, i0, j0);
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                X[r][q] = Sr[(i0 + r) * NP + j0 + q] - X[r][q];
-                Z[r][q] = Lr[(i0 + r) * NP + j0 + q] - Z[r][q];
-            }
+        if (k + 1 < len) prefetch(t + 1);
+        // (2) local vectors, one per warp, then X = S2p - S2p D^T, Z = l~2 - D^T l~2
         if (warp == 0) {
-            const int l = lane;
-            float acc = 0.f;
-            for (int kk = 0; kk < NP; ++kk) acc = fmaf(Dr[l * NP + kk], S1p[kk], acc);
-            u[l] = S1p[l] - acc;
-            float a1 = 0.f;
-            for (int cc = 0; cc < d; ++cc) a1 = fmaf(F[l * d + cc], x[cc], a1);
-            s1[l] = a1;
-            for (int a = 0; a < QP; ++a) {
-                float ga = 0.f, ha = 0.f;
-                for (int cc = 0; cc < d; ++cc) {
-                    ga = fmaf(Gt[((size_t)a * NP + l) * d + cc], x[cc], ga);
-                    ha = fmaf(Ht[((size_t)a * NP + l) * d + cc], x[cc], ha);
-                }
-                U[l * QMAX + a] = ga;
-                V[l * QMAX + a] = ha;
-            }
-        }
-        __syncthreads();
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                Xk[(j0 + q) * NP + i0 + r] = X[r][q];
-                Zr[(i0 + r) * NP + j0 + q] = Z[r][q];
+            for (int kk = 0; kk < NP; kk += 4) {
+                a0 = fmaf(Dr[lane * NP + kk], S1p[kk], a0);
+                a1 = fmaf(Dr[lane * NP + kk + 1], S1p[kk + 1], a1);
+                a2 = fmaf(Dr[lane * NP + kk + 2], S1p[kk + 2], a2);
+                a3 = fmaf(Dr[lane * NP + kk + 3], S1p[kk + 3], a3);
             }
-        // (3) vector cotangents: warp 0 du, dU (rows of l~2); warp 1 ds1, dV (columns)
-        if (warp == 0) {
-            const int i = lane;
-            float acc = L1[i];
-            for (int j = 0; j < NP; ++j) acc = fmaf(Lr[i * NP + j], s1[j], acc);
-            du[i] = acc;
-            for (int a = 0; a < QP; ++a) {
-                float e = 0.f;
-                for (int j = 0; j < NP; ++j) e = fmaf(Lr[i * NP + j], V[j * QMAX + a], e);
-                dU[i * QMAX + a] = e;
-            }
+            u[lane] = S1p[lane] - ((a0 + a1) + (a2 + a3));
         } else if (warp == 1) {
-            const int j = lane;
-            float acc = L1[j];
-            for (int i = 0; i < NP; ++i) acc = fmaf(Lk[j * NP + i], u[i], acc);
-            ds1[j] = acc;
+            float a1 = 0.f;
+            for (int cc = 0; cc < d; ++cc) a1 = fmaf(F[lane * d + cc], x[cc], a1);
+            s1[lane] = a1;
+        } else {
+            float* out = warp == 2 ? U : V;
+            const float* tab = warp == 2 ? Gt : Ht;
             for (int a = 0; a < QP; ++a) {
-                float e = 0.f;
-                for (int i = 0; i < NP; ++i) e = fmaf(Lk[j * NP + i], U[i * QMAX + a], e);
-                dV[j * QMAX + a] = e;
+                float acc = 0.f;
+                for (int cc = 0; cc < d; ++cc) acc = fmaf(tab[((size_t)a * NP + lane) * d + cc], x[cc], acc);
+                out[lane * QMAX + a] = acc;
             }
         }
+        {
+            float X[4][2] = {}, Z[4][2] = {};
+            gemm42(Sk, Dt, X, i0, j0);
+            gemm42(Dr, Lr, Z, i0, j0);
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    Xk[(j0 + q) * NP + i0 + r] = Sr[(i0 + r) * NP + j0 + q] - X[r][q];
+                    Zr[(i0 + r) * NP + j0 + q] = Lr[(i0 + r) * NP + j0 + q] - Z[r][q];
+                }
+        }
         __syncthreads();
-        // (4) dM += l~2 X^T + Z^T S2p + du S1p^T
+        // (3) vector cotangents, one per warp: du, ds1 (then dU, dV) with independent accumulators
+        if (warp == 0) {
+            float a0 = L1[lane], a1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < NP; j += 2) {
+                a0 = fmaf(Lr[lane * NP + j], s1[j], a0);
+                a1 = fmaf(Lr[lane * NP + j + 1], s1[j + 1], a1);
+            }
+            du[lane] = a0 + a1;
+        } else if (warp == 1) {
+            float a0 = L1[lane], a1 = 0.f;
+#pragma unroll
+            for (int i = 0; i < NP; i += 2) {
+                a0 = fmaf(Lk[lane * NP + i], u[i], a0);
+                a1 = fmaf(Lk[lane * NP + i + 1], u[i + 1], a1);
+            }
+            ds1[lane] = a0 + a1;
+        } else {
+            // warp 2: dU_a = l~2 V_a (rows of l~2), warp 3: dV_a = l~2^T U_a (columns)
+            const float* Lm = warp == 2 ? Lr : Lk;
+            const float* W = warp == 2 ? V : U;
+            float* out = warp == 2 ? dU : dV;
+            float acc[QMAX];
+#pragma unroll
+            for (int a = 0; a < QMAX; ++a) acc[a] = 0.f;
+            for (int j = 0; j < NP; ++j) {
+                const float l = Lm[lane * NP + j];
+#pragma unroll
+                for (int a = 0; a < QMAX; ++a)
+                    if (a < QP) acc[a] = fmaf(l, W[j * QMAX + a], acc[a]);
+            }
+#pragma unroll
+            for (int a = 0; a < QMAX; ++a)
+                if (a < QP) out[lane * QMAX + a] = acc[a];
+        }
+        __syncthreads();
+        // (4) dM += l~2 X^T + Z^T S2p + du S1p^T; table gradients; dx_t
         gemm42(Lk, Xk, dM, i0, j0);
         gemm42(Zr, Sr, dM, i0, j0);
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
             for (int q = 0; q < 2; ++q) dM[r][q] = fmaf(du[i0 + r], S1p[j0 + q], dM[r][q]);
-        // (5) table gradients and dx_t
         for (int e = tid; e < tabn; e += GNT) {
             const int blk = e / (NP * d), rem = e - blk * NP * d, i = rem / d, cc = rem - i * d;
             const float coef = blk == 0 ? ds1[i] : (blk <= QP ? dU[i * QMAX + blk - 1] : dV[i * QMAX + blk - 1 - QP]);
@@ -1996,11 +2026,12 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
         }
         for (int cc = warp; cc < d; cc += GNT / 32) {
             const int i = lane;
-            float acc = F[i * d + cc] * ds1[i];
+            float a0 = F[i * d + cc] * ds1[i], a1 = 0.f;
             for (int a = 0; a < QP; ++a) {
-                acc = fmaf(Gt[((size_t)a * NP + i) * d + cc], dU[i * QMAX + a], acc);
-                acc = fmaf(Ht[((size_t)a * NP + i) * d + cc], dV[i * QMAX + a], acc);
+                a0 = fmaf(Gt[((size_t)a * NP + i) * d + cc], dU[i * QMAX + a], a0);
+                a1 = fmaf(Ht[((size_t)a * NP + i) * d + cc], dV[i * QMAX + a], a1);
             }
+            float acc = a0 + a1;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
             if (lane == 0) p.grad_dx[((size_t)b * g.T + t) * d + cc] = acc;
