@@ -1537,6 +1537,7 @@ extern "C" int ews_block_fwd(const ews_block_args* a, ews_stream_t stream) {
     const size_t smem = fwd_smem(g);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_kernel, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
@@ -1584,6 +1585,7 @@ extern "C" int ews_block_bwd(const ews_block_args* a, ews_stream_t stream) {
     const size_t smem = bwd_smem(g);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_kernel, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;

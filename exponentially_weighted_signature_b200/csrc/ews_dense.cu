@@ -2180,6 +2180,7 @@ template <typename K>
 static int launch(K kernel, const Params& p, size_t smem, cudaStream_t s) {
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, NT, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
@@ -2233,6 +2234,7 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     const size_t smem = tc::tc_smem_bytes(g.W, g.d_in, g.QP);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_tc_kernel, tc::NTH, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
@@ -2280,6 +2282,7 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         const size_t smem = tc::tc_smem_bytes(g.W, g.d_in, g.QP);
         if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
         cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
         int per_sm = 0;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_tc_kernel, tc::NTH, smem);
         if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
@@ -2293,6 +2296,7 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         const size_t smem = grad_smem_bytes(g);
         if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
         cudaFuncSetAttribute(grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(grad_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
         grad_kernel<<<g.C * g.B, GNT, smem, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     }
