@@ -1832,12 +1832,17 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
 // One CTA of 128 threads per (chunk, sample); thread (r, c) owns the 4 x 2 block at rows 4r, columns 2c.
 constexpr int GNT = 128;
 
+// k-major buffers written by transposed stores are swizzled at float4 granularity (group g of row k at
+// g ^ (k & 7)), which cuts the stores' bank conflicts from 32-way to 4-way; reads apply the same map.
+__device__ __forceinline__ int swz(int k, int i) { return k * NP + ((((i >> 2) ^ (k & 7)) << 2) | (i & 3)); }
+
+template <bool SA, bool SB>
 __device__ __forceinline__ void gemm42(const float* __restrict__ At, const float* __restrict__ Bm, float acc[4][2],
                                        int i0, int j0) {
 #pragma unroll 8
     for (int k = 0; k < NP; ++k) {
-        const float4 a = *reinterpret_cast<const float4*>(At + k * NP + i0);
-        const float2 b = *reinterpret_cast<const float2*>(Bm + k * NP + j0);
+        const float4 a = *reinterpret_cast<const float4*>(At + (SA ? swz(k, i0) : k * NP + i0));
+        const float2 b = *reinterpret_cast<const float2*>(Bm + (SB ? swz(k, j0) : k * NP + j0));
         const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
@@ -1851,7 +1856,6 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
     extern __shared__ float smem[];
     const Geom& g = p.g;
     const int N = g.N, d = g.d_in, QP = g.QP;
-    const int N2 = N * N;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int i0 = 4 * (tid >> 4), j0 = 2 * (tid & 15);
     float* Lr = smem;            // l~2 row-major
@@ -1903,14 +1907,16 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
     for (int r = 0; r < 4; ++r) dM[r][0] = dM[r][1] = 0.f;
     // the next interval's rows, prefetched into registers (entries tid + 128 m of the level-2 block)
     float pl[8], ps[8], pl1 = 0.f, ps1 = 0.f, px = 0.f;
+    // entry m of this thread: (i, j) = (4m + tid / 32, tid % 32) on the padded 32 x 32 grid
     auto prefetch = [&](int t) {
         const float* lrow = p.lam + ((size_t)b * g.T + t) * g.W;
         const float* srow = t > 0 ? p.out + ((size_t)b * g.T + t - 1) * g.W : nullptr;
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
-            const int e = tid + GNT * m;
-            pl[m] = e < N2 ? ldcg(lrow + 1 + N + e) : 0.f;
-            ps[m] = (e < N2 && srow) ? ldcg(srow + 1 + N + e) : 0.f;
+            const int i = 4 * m + warp, j = lane;
+            const bool ok = i < N && j < N;
+            pl[m] = ok ? ldcg(lrow + 1 + N + i * N + j) : 0.f;
+            ps[m] = (ok && srow) ? ldcg(srow + 1 + N + i * N + j) : 0.f;
         }
         pl1 = tid < N ? ldcg(lrow + 1 + tid) : 0.f;
         ps1 = (tid < N && srow) ? ldcg(srow + 1 + tid) : 0.f;
@@ -1923,14 +1929,11 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
         // (1) the prefetched interval into shared memory; the next one's loads go out
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
-            const int e = tid + GNT * m;
-            if (e < N2) {
-                const int i = e / N, j = e - i * N;
-                Lr[i * NP + j] = pl[m];
-                Lk[j * NP + i] = pl[m];
-                Sr[i * NP + j] = ps[m];
-                Sk[j * NP + i] = ps[m];
-            }
+            const int i = 4 * m + warp, j = lane;
+            Lr[i * NP + j] = pl[m];
+            Lk[swz(j, i)] = pl[m];
+            Sr[i * NP + j] = ps[m];
+            Sk[swz(j, i)] = ps[m];
         }
         if (tid < N) {
             L1[tid] = pl1;
@@ -1965,13 +1968,13 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
         }
         {
             float X[4][2] = {}, Z[4][2] = {};
-            gemm42(Sk, Dt, X, i0, j0);
-            gemm42(Dr, Lr, Z, i0, j0);
+            gemm42<true, false>(Sk, Dt, X, i0, j0);
+            gemm42<false, false>(Dr, Lr, Z, i0, j0);
 #pragma unroll
             for (int r = 0; r < 4; ++r)
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
-                    Xk[(j0 + q) * NP + i0 + r] = Sr[(i0 + r) * NP + j0 + q] - X[r][q];
+                    Xk[swz(j0 + q, i0 + r)] = Sr[(i0 + r) * NP + j0 + q] - X[r][q];
                     Zr[(i0 + r) * NP + j0 + q] = Lr[(i0 + r) * NP + j0 + q] - Z[r][q];
                 }
         }
@@ -1989,40 +1992,42 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
             float a0 = L1[lane], a1 = 0.f;
 #pragma unroll
             for (int i = 0; i < NP; i += 2) {
-                a0 = fmaf(Lk[lane * NP + i], u[i], a0);
-                a1 = fmaf(Lk[lane * NP + i + 1], u[i + 1], a1);
+                a0 = fmaf(Lk[swz(lane, i)], u[i], a0);
+                a1 = fmaf(Lk[swz(lane, i + 1)], u[i + 1], a1);
             }
             ds1[lane] = a0 + a1;
         } else {
-            // warp 2: dU_a = l~2 V_a (rows of l~2), warp 3: dV_a = l~2^T U_a (columns)
-            const float* Lm = warp == 2 ? Lr : Lk;
-            const float* W = warp == 2 ? V : U;
-            float* out = warp == 2 ? dU : dV;
-            float acc[QMAX];
+            // warp 2: dU_a = l~2 V_a (row `lane` of l~2), warp 3: dV_a = l~2^T U_a (column `lane`)
+            const bool rows = warp == 2;
+            const float* W = rows ? V : U;
+            float* out = rows ? dU : dV;
+            float lv[NP];
 #pragma unroll
-            for (int a = 0; a < QMAX; ++a) acc[a] = 0.f;
-            for (int j = 0; j < NP; ++j) {
-                const float l = Lm[lane * NP + j];
+            for (int j = 0; j < NP; ++j) lv[j] = rows ? Lr[lane * NP + j] : Lk[swz(lane, j)];
+            for (int a = 0; a < QP; ++a) {
+                float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-                for (int a = 0; a < QMAX; ++a)
-                    if (a < QP) acc[a] = fmaf(l, W[j * QMAX + a], acc[a]);
+                for (int j = 0; j < NP; j += 2) {
+                    a0 = fmaf(lv[j], W[j * QMAX + a], a0);
+                    a1 = fmaf(lv[j + 1], W[(j + 1) * QMAX + a], a1);
+                }
+                out[lane * QMAX + a] = a0 + a1;
             }
-#pragma unroll
-            for (int a = 0; a < QMAX; ++a)
-                if (a < QP) out[lane * QMAX + a] = acc[a];
         }
         __syncthreads();
         // (4) dM += l~2 X^T + Z^T S2p + du S1p^T; table gradients; dx_t
-        gemm42(Lk, Xk, dM, i0, j0);
-        gemm42(Zr, Sr, dM, i0, j0);
+        gemm42<true, true>(Lk, Xk, dM, i0, j0);
+        gemm42<false, false>(Zr, Sr, dM, i0, j0);
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
             for (int q = 0; q < 2; ++q) dM[r][q] = fmaf(du[i0 + r], S1p[j0 + q], dM[r][q]);
-        for (int e = tid; e < tabn; e += GNT) {
-            const int blk = e / (NP * d), rem = e - blk * NP * d, i = rem / d, cc = rem - i * d;
+        // table gradients: warp w takes blocks w, w + 4, ...; lane = row
+        for (int blk = warp; blk <= 2 * QP; blk += GNT / 32) {
+            const int i = lane;
             const float coef = blk == 0 ? ds1[i] : (blk <= QP ? dU[i * QMAX + blk - 1] : dV[i * QMAX + blk - 1 - QP]);
-            tacc[e] = fmaf(coef, x[cc], tacc[e]);
+            float* ta = tacc + ((size_t)blk * NP + i) * d;
+            for (int cc = 0; cc < d; ++cc) ta[cc] = fmaf(coef, x[cc], ta[cc]);
         }
         for (int cc = warp; cc < d; cc += GNT / 32) {
             const int i = lane;
