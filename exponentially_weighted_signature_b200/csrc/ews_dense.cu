@@ -1946,11 +1946,11 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
         if (warp == 0) {
             float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
-            for (int kk = 0; kk < NP; kk += 4) {
-                a0 = fmaf(Dr[lane * NP + kk], S1p[kk], a0);
-                a1 = fmaf(Dr[lane * NP + kk + 1], S1p[kk + 1], a1);
-                a2 = fmaf(Dr[lane * NP + kk + 2], S1p[kk + 2], a2);
-                a3 = fmaf(Dr[lane * NP + kk + 3], S1p[kk + 3], a3);
+            for (int kk = 0; kk < NP; kk += 4) {  // (D S1p)[lane] from D k-major: consecutive lanes, no conflicts
+                a0 = fmaf(Dt[kk * NP + lane], S1p[kk], a0);
+                a1 = fmaf(Dt[(kk + 1) * NP + lane], S1p[kk + 1], a1);
+                a2 = fmaf(Dt[(kk + 2) * NP + lane], S1p[kk + 2], a2);
+                a3 = fmaf(Dt[(kk + 3) * NP + lane], S1p[kk + 3], a3);
             }
             u[lane] = S1p[lane] - ((a0 + a1) + (a2 + a3));
         } else if (warp == 1) {
@@ -1979,21 +1979,23 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
                 }
         }
         __syncthreads();
-        // (3) vector cotangents, one per warp: du, ds1 (then dU, dV) with independent accumulators
+        // (3) vector cotangents, one per warp: du, ds1 (then dU, dV) with independent accumulators. Row
+        // `lane` of l~2 is read from the k-major copy and column `lane` from the row-major one, so the 32
+        // lanes always read 32 different banks.
         if (warp == 0) {
             float a0 = L1[lane], a1 = 0.f;
 #pragma unroll
             for (int j = 0; j < NP; j += 2) {
-                a0 = fmaf(Lr[lane * NP + j], s1[j], a0);
-                a1 = fmaf(Lr[lane * NP + j + 1], s1[j + 1], a1);
+                a0 = fmaf(Lk[swz(j, lane)], s1[j], a0);
+                a1 = fmaf(Lk[swz(j + 1, lane)], s1[j + 1], a1);
             }
             du[lane] = a0 + a1;
         } else if (warp == 1) {
             float a0 = L1[lane], a1 = 0.f;
 #pragma unroll
             for (int i = 0; i < NP; i += 2) {
-                a0 = fmaf(Lk[swz(lane, i)], u[i], a0);
-                a1 = fmaf(Lk[swz(lane, i + 1)], u[i + 1], a1);
+                a0 = fmaf(Lr[i * NP + lane], u[i], a0);
+                a1 = fmaf(Lr[(i + 1) * NP + lane], u[i + 1], a1);
             }
             ds1[lane] = a0 + a1;
         } else {
@@ -2003,7 +2005,7 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
             float* out = rows ? dU : dV;
             float lv[NP];
 #pragma unroll
-            for (int j = 0; j < NP; ++j) lv[j] = rows ? Lr[lane * NP + j] : Lk[swz(lane, j)];
+            for (int j = 0; j < NP; ++j) lv[j] = rows ? Lk[swz(j, lane)] : Lr[j * NP + lane];
             for (int a = 0; a < QP; ++a) {
                 float a0 = 0.f, a1 = 0.f;
 #pragma unroll
