@@ -1539,7 +1539,7 @@ extern "C" int ews_block_fwd(const ews_block_args* a, ews_stream_t stream) {
     cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_kernel, kWarps * 32, smem);
+    per_sm = resident_ctas((const void*)fwd_kernel, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     int grid = per_sm * num_sms();
     const int need = (g.ntiles + kWarps - 1) / kWarps;
@@ -1587,7 +1587,7 @@ extern "C" int ews_block_bwd(const ews_block_args* a, ews_stream_t stream) {
     cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_kernel, kWarps * 32, smem);
+    per_sm = resident_ctas((const void*)bwd_kernel, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     int grid = per_sm * num_sms();
     const int need = (g.ntiles + kWarps - 1) / kWarps;

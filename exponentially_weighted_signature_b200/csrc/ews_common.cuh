@@ -136,4 +136,31 @@ __device__ __forceinline__ float input_increment(const void* path, int b, int t,
     return load_in(path, k0 + d_in, bf16) - load_in(path, k0, bf16);
 }
 
+// CTAs of `kernel` that fit on one SM with `threads` threads and `smem` bytes of dynamic shared memory,
+// from the device's register, shared-memory and thread limits (the occupancy query is taken too and the
+// larger answer kept: on this part it has answered 1 where 2 CTAs fit). Grids of these kernels take
+// work from an ordered ticket and only wait on lower tickets, so a CTA that is not resident never
+// blocks a resident one.
+inline int resident_ctas(const void* kernel, int threads, size_t smem) {
+    int api = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&api, kernel, threads, smem);
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess) return api;
+    int dev = 0, smem_sm = 0, reserved = 0, regs_sm = 0, thr_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&thr_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev);
+    const long per_cta_smem = (long)smem + (long)fa.sharedSizeBytes + reserved;
+    const int by_smem = per_cta_smem > 0 ? (int)(smem_sm / per_cta_smem) : 32;
+    const int regs_warp = ((fa.numRegs + 7) / 8) * 8 * 32;  // registers are allocated per warp, 256 at a time
+    const int warps = (threads + 31) / 32;
+    const int by_regs = regs_warp > 0 ? regs_sm / (regs_warp * warps) : 32;
+    const int by_threads = thr_sm / threads;
+    int mine = by_smem < by_regs ? by_smem : by_regs;
+    if (by_threads < mine) mine = by_threads;
+    return api > mine ? api : mine;
+}
+
 }  // namespace ews

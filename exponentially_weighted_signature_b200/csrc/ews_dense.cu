@@ -2189,7 +2189,7 @@ static int launch(K kernel, const Params& p, size_t smem, cudaStream_t s) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, NT, smem);
+    per_sm = resident_ctas((const void*)kernel, NT, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     int grid = per_sm * num_sms();
     if (grid > p.g.ntiles) grid = p.g.ntiles;
@@ -2243,7 +2243,7 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_tc_kernel, tc::NTH, smem);
+    per_sm = resident_ctas((const void*)fwd_tc_kernel, tc::NTH, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     const int groups = (g.C + tc::TILES - 1) / tc::TILES;
     int grid = per_sm * num_sms();
@@ -2291,7 +2291,7 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
         int per_sm = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_tc_kernel, tc::NTH, smem);
+        per_sm = resident_ctas((const void*)bwd_tc_kernel, tc::NTH, smem);
         if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
         const int groups = (g.C + tc::TILES - 1) / tc::TILES;
         int grid = per_sm * num_sms();

@@ -1199,7 +1199,7 @@ static int launch_fwd_t(const Params& p, cudaStream_t s) {
     const size_t smem = fwd_smem(p.g);
     cudaFuncSetAttribute(fwd_kernel<NP, NU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_kernel<NP, NU>, kWarps * 32, smem);
+    per_sm = resident_ctas((const void*)fwd_kernel<NP, NU>, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     int grid = per_sm * num_sms();
     const int need = (p.g.ntiles + kWarps - 1) / kWarps;
@@ -1218,7 +1218,7 @@ static int launch_bwd_t(const Params& p, cudaStream_t s) {
     const size_t smem = bwd_smem(p.g);
     cudaFuncSetAttribute(bwd_kernel<NP, NU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_kernel<NP, NU>, kWarps * 32, smem);
+    per_sm = resident_ctas((const void*)bwd_kernel<NP, NU>, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     int grid = per_sm * num_sms();
     const int need = (p.g.ntiles + kWarps - 1) / kWarps;
