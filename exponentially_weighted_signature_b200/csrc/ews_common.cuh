@@ -122,6 +122,36 @@ __device__ __forceinline__ void warp_load_span(float* __restrict__ s, const floa
     if (lane < n - done) s[done + lane] = __ldcg(g + done + lane);
 }
 
+// Asynchronous global -> shared copies (cp.async); each warp tracks its own groups.
+__device__ __forceinline__ unsigned smem_addr(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void cp_async4(float* s, const float* g) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(s)), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async16(float* s, const float* g) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s)), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int K>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(K) : "memory"); }
+
+// Starts a warp copy of n contiguous floats from global memory into buf (16-byte aligned, n + 3 floats):
+// the span lands at buf + shift with the same 16-byte phase as the source, so its body moves as 16-byte
+// copies and only the head and tail as 4-byte ones. Returns the span's shared-memory start. The caller
+// commits the group and waits for it (cp_async_wait, then __syncwarp) before reading.
+__device__ __forceinline__ float* warp_load_span_async(float* __restrict__ buf, const float* __restrict__ g, int n) {
+    const int lane = threadIdx.x & 31;
+    const int shift = (int)(((uintptr_t)g & 15u) >> 2);
+    float* s = buf + shift;
+    int head = (4 - shift) & 3;
+    if (head > n) head = n;
+    if (lane < head) cp_async4(s + lane, g + lane);
+    const int nvec = (n - head) >> 2;
+    for (int v = lane; v < nvec; v += 32) cp_async16(s + head + 4 * v, g + head + 4 * v);
+    const int done = head + 4 * nvec;
+    if (lane < n - done) cp_async4(s + done + lane, g + done + lane);
+    return s;
+}
+
 __device__ __forceinline__ float load_in(const void* p, size_t idx, bool bf16) {
     if (bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[idx]);
     return reinterpret_cast<const float*>(p)[idx];

@@ -51,7 +51,7 @@ struct Geom {
     // per-warp shared-memory carve-up (floats), after the CTA's lift matrix (lift_n floats)
     int lift_n;
     int f_dys, f_dts, f_stage, f_per_warp;                     // forward: dxs at 0
-    int b_dys, b_dts, b_dtg, b_dyg, b_lam1, b_gst, b_sst, b_per_warp;  // backward: dxs at 0
+    int b_dys, b_dts, b_dtg, b_dyg, b_lam1, b_gst, b_gst2, b_sst, b_sst2, b_per_warp;  // backward: dxs at 0
 };
 
 struct Params {
@@ -818,7 +818,8 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     float* dyg = dxs + g.b_dyg;
     float* lam1 = dxs + g.b_lam1;
     float* gst = dxs + g.b_gst;
-    float* sst = dxs + g.b_sst;
+    float* gbuf[2] = {gst, dxs + g.b_gst2};
+    float* sbuf[2] = {dxs + g.b_sst, dxs + g.b_sst2};
 
     const int ti = lane >> 3, tj = lane & 7;
     const int i0 = ti * RI, j0 = tj * RJ;
@@ -858,20 +859,35 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         Adj<RI, RJ> mu;
         mu.zero();
         if (!terminal) {
+            // gradient rows in blocks of SR, the next block copied in while this one runs
+            int slot = 0;
+            float* cur = warp_load_span_async(gbuf[0], p.grad_out + ((size_t)b * g.T + t0 + max(0, len - g.SR)) * g.W,
+                                              (len - max(0, len - g.SR)) * g.W);
+            cp_async_commit();
             for (int kb = len; kb > 0; kb -= g.SR) {
                 const int k0 = max(0, kb - g.SR);
-                __syncwarp();
-                warp_load_span(gst, p.grad_out + ((size_t)b * g.T + t0 + k0) * g.W, (kb - k0) * g.W);
+                float* nxt = nullptr;
+                if (k0 > 0) {
+                    const int k1 = max(0, k0 - g.SR);
+                    nxt = warp_load_span_async(gbuf[slot ^ 1], p.grad_out + ((size_t)b * g.T + t0 + k1) * g.W, (k0 - k1) * g.W);
+                }
+                cp_async_commit();
+                cp_async_wait<1>();
                 __syncwarp();
                 for (int k = kb - 1; k >= k0; --k) {
-                    add_grad_row(mu, gst + (k - k0) * g.W, g.N, i0, j0);
+                    add_grad_row(mu, cur + (k - k0) * g.W, g.N, i0, j0);
                     float fr[RI], fc[RJ];
                     if (NU) tb.at(p, dts[k]);
                     const bool bp = basepoint && (t0 + k == 0);
                     step_flow(tb, bp, fr, fc);
                     adj_step(tb, fr, fc, dys + k * NP, mu, j0, bp);
                 }
+                __syncwarp();
+                cur = nxt;
+                slot ^= 1;
             }
+            cp_async_wait<0>();
+            __syncwarp();
         } else {
             // lambda1 only (lambda2 is closed form): mu1_{t-1} = rho (mu1_t + lambda2_t s1_t); g1 enters at T-1
             for (int k = len - 1; k >= 0; --k) {
@@ -954,24 +970,37 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         gr.zero();
         if (!terminal) {
             Adj<RI, RJ> a = lam_in;
+            // block [k0, kb): gradient rows t0+k0.. and S_{t-1} rows t0+k0-1.. (row -1 is the zero state),
+            // the next block copied in while this one runs
+            auto stage = [&](int k0s, int kbs, int sl, float*& gs, float*& ss) {
+                const int ns = kbs - k0s;
+                gs = warp_load_span_async(gbuf[sl], p.grad_out + ((size_t)b * g.T + t0 + k0s) * g.W, ns * g.W);
+                const int first = t0 + k0s - 1;
+                if (first >= 0) {
+                    ss = warp_load_span_async(sbuf[sl], p.out + ((size_t)b * g.T + first) * g.W, ns * g.W);
+                } else {
+                    // row -1 is zero; rows 0.. follow it, placed at the source's 16-byte phase
+                    const int shift = (int)(((uintptr_t)(p.out + (size_t)b * g.T * g.W) & 15u) >> 2);
+                    const int lead = (shift - g.W % 4 + 8) % 4;  // so that ss + W has the source's phase
+                    ss = sbuf[sl] + lead;
+                    for (int e = lane; e < g.W; e += 32) ss[e] = 0.f;
+                    if (ns > 1) warp_load_span_async(ss + g.W - shift, p.out + (size_t)b * g.T * g.W, (ns - 1) * g.W);
+                }
+            };
+            int slot = 0;
+            float *gcur, *scur, *gnxt = nullptr, *snxt = nullptr;
+            stage(max(0, len - g.SR), len, 0, gcur, scur);
+            cp_async_commit();
             for (int kb = len; kb > 0; kb -= g.SR) {
                 const int k0 = max(0, kb - g.SR);
-                const int n = kb - k0;
-                __syncwarp();
-                warp_load_span(gst, p.grad_out + ((size_t)b * g.T + t0 + k0) * g.W, n * g.W);
-                // S_{t-1} rows: rows t0+k0-1 .. t0+kb-2 of the forward output (row -1 is the zero state)
-                const int first = t0 + k0 - 1;
-                if (first >= 0) {
-                    warp_load_span(sst, p.out + ((size_t)b * g.T + first) * g.W, n * g.W);
-                } else {
-                    for (int e = lane; e < g.W; e += 32) sst[e] = 0.f;
-                    if (n > 1) warp_load_span(sst + g.W, p.out + (size_t)b * g.T * g.W, (n - 1) * g.W);
-                }
+                if (k0 > 0) stage(max(0, k0 - g.SR), k0, slot ^ 1, gnxt, snxt);
+                cp_async_commit();
+                cp_async_wait<1>();
                 __syncwarp();
                 for (int k = kb - 1; k >= k0; --k) {
-                    add_grad_row(a, gst + (k - k0) * g.W, g.N, i0, j0);
+                    add_grad_row(a, gcur + (k - k0) * g.W, g.N, i0, j0);
                     float S1p[RI], S2p[RI][RJ];
-                    read_row<RI, RJ>(sst + (k - k0) * g.W, S1p, S2p, g.N, i0, j0);
+                    read_row<RI, RJ>(scur + (k - k0) * g.W, S1p, S2p, g.N, i0, j0);
                     float fr[RI], fc[RJ];
                     if (NU) tb.at(p, dts[k]);
                     const bool bp = basepoint && (t0 + k == 0);
@@ -979,7 +1008,13 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                     bwd_step<RI, RJ, NU>(p, tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, NU ? dts[k] : 0.f,
                                          dtg + k, i0, j0, ti, tj, bp);
                 }
+                __syncwarp();
+                gcur = gnxt;
+                scur = snxt;
+                slot ^= 1;
             }
+            cp_async_wait<0>();
+            __syncwarp();
         } else {
             // forward sweep from the carry with lambda2 in closed form and lambda1 = mu1 + rho^{end-t} Lam1_in
             Elem<RI, RJ> S;
@@ -1089,15 +1124,19 @@ static void carve(Geom* g) {
     g->f_stage = xs + ys + ts;
     g->f_per_warp = g->f_stage + align4(SR * g->W);
     const bool terminal = g->readout == EWS_READOUT_TERMINAL;
-    const int gst_n = align4(std::max(terminal ? 0 : SR * g->W, Lc * g->d_in));
+    const int span = align4(SR * g->W + 4);  // SR rows at any 16-byte phase
+    const int gst_n = align4(std::max(terminal ? 0 : span, Lc * g->d_in));
     g->b_dys = xs;
     g->b_dts = xs + ys;
     g->b_dtg = g->b_dts + ts;
     g->b_dyg = g->b_dtg + ts;
     g->b_lam1 = g->b_dyg + ys;
     g->b_gst = g->b_lam1 + (terminal ? ys : 0);
-    g->b_sst = g->b_gst + gst_n;
-    g->b_per_warp = g->b_sst + (terminal ? 0 : align4(SR * g->W));
+    // prefix readouts double-buffer the gradient rows and the S_{t-1} rows (two slots each)
+    g->b_gst2 = g->b_gst + gst_n;
+    g->b_sst = g->b_gst2 + (terminal ? 0 : span);
+    g->b_sst2 = g->b_sst + (terminal ? 0 : span);
+    g->b_per_warp = g->b_sst2 + (terminal ? 0 : span);
 }
 
 static int make_geom(const ews_diag_args* a, Geom* g) {
