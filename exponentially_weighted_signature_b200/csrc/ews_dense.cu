@@ -1536,6 +1536,7 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
     uint32_t phase = 0;
     bool failed = false;
     bool mma_pending = false;
+    int b_cur = 0;
 
     const uint64_t dA_hi = smem_desc(smem_u32(s.Ahi), 2048, 128), dA_lo = smem_desc(smem_u32(s.Alo), 2048, 128);
     const uint64_t dB_hi = smem_desc(smem_u32(s.Bhi), 512, 128), dB_lo = smem_desc(smem_u32(s.Blo), 512, 128);
@@ -1543,6 +1544,19 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
     const int ntiles = g.B * groups;
     float* vt = s.vec + warp * kVecPerTile;  // L1 (NP) | v (NP) | s1 (NP) | x (32) | U, V
     float* RQt = s.RQ + warp * 32 * RQS;
+    // the next interval's gradient row, copied in (cp.async) while the current one runs:
+    // gb[0..N) level 1, gb[32 + 32 n + j] level 2 (idle stage space during the passes)
+    float* gb = s.stage + warp * tc_stage_stride(g.W);
+    auto fetch_grad = [&](int t) {
+        const float* grow = p.grad_out + ((size_t)b_cur * g.T + t) * g.W;
+        if (lane < N) {
+#pragma unroll
+            for (int n = 0; n < 32; ++n)
+                if (n < N) cp_async4(gb + 32 + 32 * n + lane, grow + 1 + N + n * N + lane);
+            cp_async4(gb + lane, grow + 1 + lane);
+        }
+        cp_async_commit();
+    };
 
     for (;;) {
         if (tid == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
@@ -1551,6 +1565,7 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
         __syncthreads();
         if (tile >= ntiles) break;
         const int grp_r = tile / g.B, b = tile - grp_r * g.B;
+        b_cur = b;
         const int grp = groups - 1 - grp_r;  // later groups first: the look-back reads later chunks
         const int c_me = grp * TILES + warp;
         const bool valid_me = c_me < g.C;
@@ -1580,16 +1595,22 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
             // steps run in reverse; the chunk's last interval is len_me - 1 (shorter chunks idle on zero state)
             float xnext = (lane < g.d_in && len_me > 0)
                               ? input_increment(p.path, b, t0_me + len_me - 1, lane, g.T, g.d_in, g.flags) : 0.f;
+            if (len_me > 0) fetch_grad(t0_me + len_me - 1);
             for (int k = steps - 1; k >= 0; --k) {
                 const bool live = k < len_me;
                 const int t = t0_me + k;
                 // E0: l~ = l + g_t; the exact pass writes l~_t; rows of l~2 -> A operand
-                if (live && lane < N) {
-                    const float* grow = p.grad_out + ((size_t)b * g.T + t) * g.W;
+                if (live) {
+                    cp_async_wait<0>();
+                    __syncwarp();
+                    if (lane < N) {
 #pragma unroll
-                    for (int n = 0; n < 32; ++n)
-                        if (n < N) col[n] += ldcg(grow + 1 + N + n * N + lane);
-                    vt[lane] += ldcg(grow + 1 + lane);
+                        for (int n = 0; n < 32; ++n)
+                            if (n < N) col[n] += gb[32 + 32 * n + lane];
+                        vt[lane] += gb[lane];
+                    }
+                    __syncwarp();
+                    if (k >= 1) fetch_grad(t - 1);
                 }
                 __syncwarp();
                 if (pass == 1 && live && lane < N) {
