@@ -479,9 +479,9 @@ __device__ void load_chunk(const Params& p, const float* liftS, float* dxs, floa
         float v = 0.f;
         if (a < g.N) {
             if (p.lift) {
-                const float* wr = liftS + a * g.d_in;
+                // lift stored channel-major (liftS[cc * NB + a]): consecutive lanes, consecutive banks
                 const float* xr = dxs + k * g.d_in;
-                for (int cc = 0; cc < g.d_in; ++cc) v = fmaf(wr[cc], xr[cc], v);
+                for (int cc = 0; cc < g.d_in; ++cc) v = fmaf(liftS[cc * NB + a], xr[cc], v);
             } else {
                 v = dxs[k * g.d_in + a];
             }
@@ -502,7 +502,7 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
     float* Ablk = smem + g.lift_n;  // 16
     for (int e = threadIdx.x; e < NB * g.d_in; e += blockDim.x) {
         const int r = e / g.d_in, cc = e - r * g.d_in;
-        liftS[e] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
+        liftS[cc * NB + r] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
     }
     for (int e = threadIdx.x; e < 16; e += blockDim.x) Ablk[e] = (e >> 2) < g.N / 2 ? p.blocks[e] : 0.f;
     __syncthreads();
@@ -1229,7 +1229,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     float* Ablk = smem + g.lift_n;
     for (int e = threadIdx.x; e < NB * g.d_in; e += blockDim.x) {
         const int r = e / g.d_in, cc = e - r * g.d_in;
-        liftS[e] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
+        liftS[cc * NB + r] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
     }
     for (int e = threadIdx.x; e < 16; e += blockDim.x) Ablk[e] = (e >> 2) < g.N / 2 ? p.blocks[e] : 0.f;
     __syncthreads();
@@ -1325,7 +1325,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
             const int k = e / g.d_in, cc = e - k * g.d_in;
             float acc = 0.f;
             if (p.lift) {
-                for (int r = 0; r < g.N; ++r) acc = fmaf(liftS[r * g.d_in + cc], dyg[k * NB + r], acc);
+                for (int r = 0; r < g.N; ++r) acc = fmaf(liftS[cc * NB + r], dyg[k * NB + r], acc);
             } else {
                 acc = dyg[k * NB + cc];
             }

@@ -265,9 +265,9 @@ __device__ void load_increments(const Params& p, const float* liftS, float* dxs,
         float v = 0.f;
         if (i < g.N) {
             if (p.lift) {
-                const float* wr = liftS + i * g.d_in;
+                // lift stored channel-major (liftS[cc * NP + i]): consecutive lanes, consecutive banks
                 const float* xr = dxs + k * g.d_in;
-                for (int cc = 0; cc < g.d_in; ++cc) v = fmaf(wr[cc], xr[cc], v);
+                for (int cc = 0; cc < g.d_in; ++cc) v = fmaf(liftS[cc * g.NP + i], xr[cc], v);
             } else {
                 v = dxs[k * g.d_in + i];
             }
@@ -351,7 +351,9 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
     float* liftS = smem;
     for (int e = threadIdx.x; e < NP * g.d_in; e += blockDim.x) {
         const int r = e / g.d_in, cc = e - r * g.d_in;
-        liftS[e] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
+        const float w = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
+        liftS[cc * NP + r] = w;                    // channel-major: the lift of the increments
+        liftS[g.lift_n / 2 + r * g.d_in + cc] = w;  // row-major: the gradient's map back to dx
     }
     __syncthreads();
     float* dxs = smem + g.lift_n + warp * g.f_per_warp;
@@ -752,7 +754,8 @@ __device__ void finish_chunk(const Params& p, const float* liftS, const float* d
         const int k = e / g.d_in, cc = e - k * g.d_in;
         float acc = 0.f;
         if (p.lift) {
-            for (int i = 0; i < g.N; ++i) acc = fmaf(liftS[i * g.d_in + cc], dyg[k * NP + i], acc);
+            const float* liftR = liftS + g.lift_n / 2;
+            for (int i = 0; i < g.N; ++i) acc = fmaf(liftR[i * g.d_in + cc], dyg[k * NP + i], acc);
         } else {
             acc = dyg[k * NP + cc];
         }
@@ -806,7 +809,9 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     float* liftS = smem;
     for (int e = threadIdx.x; e < NP * g.d_in; e += blockDim.x) {
         const int r = e / g.d_in, cc = e - r * g.d_in;
-        liftS[e] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
+        const float w = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
+        liftS[cc * NP + r] = w;                    // channel-major: the lift of the increments
+        liftS[g.lift_n / 2 + r * g.d_in + cc] = w;  // row-major: the gradient's map back to dx
     }
     __syncthreads();
     // per warp: dxs, dys, dyg (Lc x NP), lam1 (Lc x NP, terminal only), gst (gradient rows, and the dx
@@ -1117,7 +1122,7 @@ static void carve(Geom* g) {
     const int Lc = g->Lc, NP = g->NP;
     const int SR = g->SR < Lc ? g->SR : Lc;
     g->SR = SR;
-    g->lift_n = align4(NP * g->d_in);
+    g->lift_n = 2 * align4(NP * g->d_in);  // channel-major and row-major copies
     const int xs = align4(Lc * g->d_in), ys = align4(Lc * NP), ts = g->nu ? align4(Lc) : 0;
     g->f_dys = xs;
     g->f_dts = xs + ys;
