@@ -199,6 +199,52 @@ def _block_setup(cfg, rank, world, device, precision, batch=None):
                 ws_bytes=ws_bytes, units=Bl * T, case=case)
 
 
+def _stacked_setup(cfg, rank, world, device, precision, batch=None):
+    """Per-rank inputs and model of the StackedEWS training step (config4): 4 pre-norm EWSBlocks (hidden
+    128, lift 128 -> 16, depth 2, diagonal A = diag(e^u), u ~ U(-3, 1), token-gated learned clock), a
+    Linear encoder 21 -> 128, a per-position head 128 -> 21, MSE, Adam; the gradients of every parameter
+    are allreduced (one bucket) before the optimizer step."""
+    from exponentially_weighted_signature_b200 import parallel, workloads
+    from exponentially_weighted_signature_b200.block import StackedEWS
+
+    case = getattr(workloads, cfg)(**({"B": batch} if batch else {}))
+    Bg, T = case["B"], case["T"]
+    if Bg % world == 0:
+        s0, s1 = parallel.shard_range(Bg, rank, world)
+        scaling = "strong"
+    else:
+        s0, s1 = 0, Bg
+        scaling = "weak"
+    q = 8
+    model = StackedEWS(4, 21, 128, 21, block_kwargs=dict(m=16, n=2, series_q=q, clock_norm_constant=float(T),
+                                                          dropout_rate=0.01), seed=1).to(device)
+    opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True)
+    params = list(model.parameters())
+    x_host = torch.tensor(case["inputs"][s0:s1])
+    y_host = torch.tensor(case["targets"][s0:s1])
+    Bl = s1 - s0
+
+    def step(x, y):
+        opt.zero_grad(set_to_none=True)
+        loss = torch.nn.functional.mse_loss(model(x), y)
+        loss.backward()
+        if world > 1:
+            parallel.allreduce_gradients(params, average=True)
+        opt.step()
+        return loss
+
+    D = 16 + 16 * 16
+    out_row = 4 * (1 + D)
+    # per block, per unit: the lifted increments (16 floats) and the clock step in, the prefix row out; the
+    # backward reads the output gradient and writes the increment and clock-step gradients
+    alg = {"ews_diag_fwd": 4 * 16 + 4 + out_row, "ews_diag_bwd": out_row + 4 * 16 + 4 * 16 + 4}
+    meta = dict(B_global=Bg, B_local=Bl, T=T, N=16, scaling=scaling, q=q, readout="prefix", dtype="f32",
+                precision="f32", depth=2, blocks=4, optimizer_in_step=True)
+    ws_bytes = 4 * Bl * T * out_row * 4
+    return dict(step=step, params=[], x_host=x_host, clock_host=y_host, alg=alg, meta=meta,
+                ws_bytes=ws_bytes, units=Bl * T, case=case)
+
+
 # ------------------------------------------------------------------------------------ helpers
 
 
@@ -267,6 +313,8 @@ def _cpu_baseline(cfg, precision, budget_s=20.0):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
+    if cfg == "config4":
+        return _cpu_baseline_stacked(budget_s, threads)
     case = getattr(workloads, cfg)(B=1)
     T = case["T"]
     if "lam" in case:
@@ -314,6 +362,53 @@ def _cpu_baseline(cfg, precision, budget_s=20.0):
                       f"associative Chen scan + autograd backward), {spent:.1f} s"}
 
 
+def _cpu_baseline_stacked(budget_s, threads):
+    """Config 4 on the host cores: the same StackedEWS training step in float32 torch with each block's EWS
+    layer replaced by the oracle port (the reference's CPU path), one sample over a growing prefix."""
+    import copy
+
+    from torch import nn
+    from oracle import ews_oracle as O
+    from exponentially_weighted_signature_b200 import workloads
+    from exponentially_weighted_signature_b200.block import StackedEWS
+
+    class OracleEWS(nn.Module):
+        def __init__(self, a_param, q):
+            super().__init__()
+            self.A_param, self.q = a_param, q
+
+        def forward(self, path, clock, readout="prefix", output_format="flat"):
+            return O.ews_layer(path, clock, torch.diag(self.A_param.values), 2, series_q=self.q,
+                               reweighting_mode="displacement", readout=readout)
+
+    case = workloads.config4(B=1)
+    T = case["T"]
+    model = StackedEWS(4, 21, 128, 21, block_kwargs=dict(m=16, n=2, series_q=8, clock_norm_constant=float(T),
+                                                          dropout_rate=0.01), seed=1)
+    for blk in model.blocks:
+        blk.ewms = OracleEWS(blk.ewms.A_param, 8)
+    opt = torch.optim.Adam(model.parameters(), lr=1e-3)
+    X = torch.tensor(case["inputs"])
+    Y = torch.tensor(case["targets"])
+    Ts = min(T, 128)
+    done_units, spent, runs = 0, 0.0, 0
+    while spent < budget_s and runs < 50:
+        t0 = time.perf_counter()
+        opt.zero_grad(set_to_none=True)
+        loss = nn.functional.mse_loss(model(X[:, :Ts]), Y[:, :Ts])
+        loss.backward()
+        opt.step()
+        dt = time.perf_counter() - t0
+        spent += dt
+        done_units += Ts
+        runs += 1
+        if dt < 2.0 and Ts < T:
+            Ts = min(T, Ts * 2)
+    return {"value": done_units / spent, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{runs} training steps of 1 sequence x up to {Ts} positions of config4 (float32 torch "
+                      f"scaffold + the oracle port of the EWS layer per block, Adam), {spent:.1f} s"}
+
+
 # ------------------------------------------------------------------------------------ arms
 
 
@@ -322,7 +417,7 @@ def run_b200(args, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    setup_fn = {"config2": _dense_setup, "config3": _block_setup}.get(args.config, _diag_setup)
+    setup_fn = {"config2": _dense_setup, "config3": _block_setup, "config4": _stacked_setup}.get(args.config, _diag_setup)
     setup = setup_fn(args.config, rank, world, device, args.precision, args.batch)
     step, params = setup["step"], setup["params"]
     x = setup["x_host"].to(device)
@@ -518,7 +613,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="config2", choices=["config1", "config2", "config3", "config5"])
+    ap.add_argument("--config", default="config2", choices=["config1", "config2", "config3", "config4", "config5"])
     ap.add_argument("--precision", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling on a smaller case)")

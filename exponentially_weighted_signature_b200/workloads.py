@@ -71,6 +71,18 @@ def config3(seed=0, B=64, T=2048):
     return dict(name="config3", path=x, clock=clock, A=A, lift=lift, B=B, T=T, N=8, depth=3)
 
 
+def config4(seed=0, B=128, T=1440):
+    """StackedEWS training data: 21 channels of Gaussian AR(1) with coefficient 0.95 and unit-variance noise;
+    the model reads positions 0..T-1 and predicts the next value of every channel (MSE)."""
+    rng = np.random.default_rng(seed)
+    x = np.zeros((B, T + 1, 21), dtype=np.float64)
+    eps = rng.normal(size=(B, T + 1, 21))
+    for t in range(1, T + 1):
+        x[:, t] = 0.95 * x[:, t - 1] + eps[:, t]
+    return dict(name="config4", inputs=x[:, :T].astype(np.float32), targets=x[:, 1:].astype(np.float32),
+                B=B, T=T, N=16, depth=2, hidden=128, blocks=4)
+
+
 def config5(seed=0, B=1024, T=8192):
     """LogEWS depth 2, diagonal N=32, A = diag(e^u), u ~ U(-4, 0): 16 channels of i.i.d. N(0, 1/T)
     increments (stored as increments), lift 16 -> 32 ~ N(0, 1/16), uniform clock, terminal readout."""
