@@ -321,6 +321,52 @@ __device__ __forceinline__ void chen_step(const Tables<RI, RJ>& tb, const float*
     }
 }
 
+// The emitting pass's step: as chen_step without the flow-product bookkeeping (the carry already holds
+// the chunk's start), with the pair complements dd = 1 - rho_i rho_j given (constant under a uniform clock).
+template <int RI, int RJ>
+__device__ __forceinline__ void chen_step_emit(const Tables<RI, RJ>& tb, const float* dyk, int i0, int j0,
+                                               Elem<RI, RJ>& S, const float fr[RI], const float fc[RJ],
+                                               const float dd[RI][RJ], bool bp) {
+    float dyr[RI], s1c[RJ], dq[RJ];
+#pragma unroll
+    for (int r = 0; r < RI; ++r) dyr[r] = dyk[i0 + r];
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        const float dyc = dyk[j0 + c];
+        s1c[c] = (bp ? 1.f : tb.q1c[c]) * dyc;
+        dq[c] = dyc;
+    }
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const float u = fmaf(-fr[r], S.S1r[r], S.S1r[r]);
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            const float loc = (bp ? 0.5f : tb.q2[r][c]) * (dyr[r] * dq[c]);
+            S.S2[r][c] = fmaf(-dd[r][c], S.S2[r][c], S.S2[r][c] + fmaf(u, s1c[c], loc));
+        }
+        S.S1r[r] = fmaf(bp ? 1.f : tb.q1r[r], dyr[r], u);
+    }
+}
+
+// Writes prefix row [1, S1, S2] of a lane element straight to global memory (real dimension N).
+template <int RI, int RJ>
+__device__ __forceinline__ void emit_row(float* row, const Elem<RI, RJ>& S, int N, int i0, int j0, int tj,
+                                         int lane) {
+    if (lane == 0) row[0] = 1.f;
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const int i = i0 + r;
+        if (i < N) {
+            if (tj == 0) row[1 + i] = S.S1r[r];
+#pragma unroll
+            for (int c = 0; c < RJ; ++c) {
+                const int j = j0 + c;
+                if (j < N) row[1 + N + i * N + j] = S.S2[r][c];
+            }
+        }
+    }
+}
+
 // Writes row [1, S1, S2] of a lane element into a staged row (real dimension N, row width W).
 template <int RI, int RJ>
 __device__ __forceinline__ void stage_row(float* row, const Elem<RI, RJ>& S, int N, int i0, int j0, int tj,
@@ -437,22 +483,35 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
             }
             continue;
         }
-        // pass 2: re-run the chunk from its carry and emit the prefix rows
+        // pass 2: re-run the chunk from its carry and write the prefix rows from registers
         Elem<RI, RJ> S = excl;
-        int k0 = 0;
-        for (int k = 0; k < len; ++k) {
+        float dd[RI][RJ];
+        if (!NU) {
+#pragma unroll
+            for (int r = 0; r < RI; ++r)
+#pragma unroll
+                for (int c = 0; c < RJ; ++c) dd[r][c] = comp_mul(tb.dr[r], tb.dc[c]);
+        }
+        float* orow = p.out + ((size_t)b * g.T + t0) * g.W;
+        for (int k = 0; k < len; ++k, orow += g.W) {
             float fr[RI], fc[RJ];
             if (NU) tb.at(p, dts[k]);
             const bool bp = basepoint && (t0 + k == 0);
             step_flow(tb, bp, fr, fc);
-            chen_step(tb, dys + k * NP, i0, j0, S, fr, fc, bp);
-            stage_row(stage + (k - k0) * g.W, S, g.N, i0, j0, tj, lane);
-            if (k - k0 == g.SR - 1 || k == len - 1) {
-                __syncwarp();
-                warp_store_span(p.out + ((size_t)b * g.T + t0 + k0) * g.W, stage, (k - k0 + 1) * g.W);
-                __syncwarp();
-                k0 = k + 1;
+            if (NU || bp) {
+#pragma unroll
+                for (int r = 0; r < RI; ++r)
+#pragma unroll
+                    for (int c = 0; c < RJ; ++c) dd[r][c] = comp_mul(fr[r], fc[c]);
             }
+            chen_step_emit(tb, dys + k * NP, i0, j0, S, fr, fc, dd, bp);
+            if (bp && !NU) {
+#pragma unroll
+                for (int r = 0; r < RI; ++r)
+#pragma unroll
+                    for (int c = 0; c < RJ; ++c) dd[r][c] = comp_mul(tb.dr[r], tb.dc[c]);
+            }
+            emit_row(orow, S, g.N, i0, j0, tj, lane);
         }
     }
 }
