@@ -424,15 +424,54 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
             tb.load(p, b, i0, j0);
         load_increments(p, liftS, dxs, dys, dts, b, t0, len);
 
-        // pass 1: the chunk's aggregate from the identity
+        // pass 1: the chunk's aggregate from the identity. Under a uniform clock the aggregate's flow
+        // complement is 1 - rho^n = -expm1(n x) for the n non-basepoint intervals, so the steps skip the
+        // flow bookkeeping and use the constant pair complements.
         Elem<RI, RJ> A;
         A.identity();
-        for (int k = 0; k < len; ++k) {
-            float fr[RI], fc[RJ];
-            if (NU) tb.at(p, dts[k]);
-            const bool bp = basepoint && (t0 + k == 0);
-            step_flow(tb, bp, fr, fc);
-            chen_step(tb, dys + k * NP, i0, j0, A, fr, fc, bp);
+        if (NU) {
+            for (int k = 0; k < len; ++k) {
+                float fr[RI], fc[RJ];
+                tb.at(p, dts[k]);
+                step_flow(tb, false, fr, fc);
+                chen_step(tb, dys + k * NP, i0, j0, A, fr, fc, false);
+            }
+        } else {
+            float dd[RI][RJ];
+#pragma unroll
+            for (int r = 0; r < RI; ++r)
+#pragma unroll
+                for (int cc = 0; cc < RJ; ++cc) dd[r][cc] = comp_mul(tb.dr[r], tb.dc[cc]);
+            int nflow = 0;
+            for (int k = 0; k < len; ++k) {
+                float fr[RI], fc[RJ];
+                const bool bp = basepoint && (t0 + k == 0);
+                step_flow(tb, bp, fr, fc);
+                if (bp) {
+                    float d0[RI][RJ];
+#pragma unroll
+                    for (int r = 0; r < RI; ++r)
+#pragma unroll
+                        for (int cc = 0; cc < RJ; ++cc) d0[r][cc] = 0.f;
+                    chen_step_emit(tb, dys + k * NP, i0, j0, A, fr, fc, d0, true);
+                } else {
+                    chen_step_emit(tb, dys + k * NP, i0, j0, A, fr, fc, dd, false);
+                    ++nflow;
+                }
+            }
+            const float fn = (float)nflow;
+#pragma unroll
+            for (int r = 0; r < RI; ++r) A.Dr[r] = -expm1f(fn * tb.xr[r]);
+#pragma unroll
+            for (int cc = 0; cc < RJ; ++cc) A.Dc[cc] = -expm1f(fn * tb.xc[cc]);
+            // level 1 by columns, from the lanes holding those rows (column j0 + c is row (tj&1)*RJ + c of
+            // row group tj/2, on the lane of that group with the same tj)
+            const int src = (tj >> 1) * 8 + tj;
+#pragma unroll
+            for (int cc = 0; cc < RJ; ++cc) {
+                const float send = (tj & 1) ? A.S1r[RJ + cc] : A.S1r[cc];
+                A.S1c[cc] = __shfl_sync(kFull, send, src);
+            }
         }
         const size_t slot = ((size_t)b * g.C + c) * g.SW;
         int* flag = p.flags + (size_t)b * g.C + c;
