@@ -388,11 +388,13 @@ __device__ __forceinline__ void stage_row(float* row, const Elem<RI, RJ>& S, int
 
 // --------------------------------------------------------------------------------- forward kernel
 
-template <int NP, bool NU>
+template <int NP, bool NU, bool FULL>
 __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
+    // FULL: N == NP, so row indices and bounds are compile-time constants
     constexpr int RI = NP / 4, RJ = NP / 8;
     extern __shared__ float smem[];
     const Geom& g = p.g;
+    const int Nr = FULL ? NP : g.N;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* liftS = smem;
     for (int e = threadIdx.x; e < NP * g.d_in; e += blockDim.x) {
@@ -515,7 +517,7 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
             if (c == g.C - 1) {
                 Elem<RI, RJ> fin;
                 chen_mul(excl, A, fin);
-                stage_row(stage, fin, g.N, i0, j0, tj, lane);
+                stage_row(stage, fin, Nr, i0, j0, tj, lane);
                 __syncwarp();
                 warp_store_span(p.out + (size_t)b * g.W, stage, g.W);
                 __syncwarp();
@@ -550,7 +552,7 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
 #pragma unroll
                     for (int c = 0; c < RJ; ++c) dd[r][c] = comp_mul(tb.dr[r], tb.dc[c]);
             }
-            emit_row(orow, S, g.N, i0, j0, tj, lane);
+            emit_row(orow, S, Nr, i0, j0, tj, lane);
         }
     }
 }
@@ -898,11 +900,13 @@ __device__ void finish_chunk(const Params& p, const float* liftS, const float* d
         for (int c = 0; c < RJ; ++c) part[2 * NP + (i0 + r) * NP + j0 + c] = gr.dq2[r][c];
 }
 
-template <int NP, bool NU>
+template <int NP, bool NU, bool FULL>
 __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
+    // FULL: N == NP, so row indices and bounds are compile-time constants
     constexpr int RI = NP / 4, RJ = NP / 8;
     extern __shared__ float smem[];
     const Geom& g = p.g;
+    const int Nr = FULL ? NP : g.N;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* liftS = smem;
     for (int e = threadIdx.x; e < NP * g.d_in; e += blockDim.x) {
@@ -956,7 +960,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
 
         // terminal readout: lambda2_t = E_i E_j g2 with E = e^{(T-1-t) x}; load g once
         float tg1[RI], tg2[RI][RJ];
-        if (terminal) read_row<RI, RJ>(p.grad_out + (size_t)b * g.W, tg1, tg2, g.N, i0, j0);
+        if (terminal) read_row<RI, RJ>(p.grad_out + (size_t)b * g.W, tg1, tg2, Nr, i0, j0);
 
         // ---- 1. zero-carry local adjoint over the chunk (reverse)
         Adj<RI, RJ> mu;
@@ -978,7 +982,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                 cp_async_wait<1>();
                 __syncwarp();
                 for (int k = kb - 1; k >= k0; --k) {
-                    add_grad_row(mu, cur + (k - k0) * g.W, g.N, i0, j0);
+                    add_grad_row(mu, cur + (k - k0) * g.W, Nr, i0, j0);
                     float fr[RI], fc[RJ];
                     if (NU) tb.at(p, dts[k]);
                     const bool bp = basepoint && (t0 + k == 0);
@@ -1101,9 +1105,9 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                 cp_async_wait<1>();
                 __syncwarp();
                 for (int k = kb - 1; k >= k0; --k) {
-                    add_grad_row(a, gcur + (k - k0) * g.W, g.N, i0, j0);
+                    add_grad_row(a, gcur + (k - k0) * g.W, Nr, i0, j0);
                     float S1p[RI], S2p[RI][RJ];
-                    read_row<RI, RJ>(scur + (k - k0) * g.W, S1p, S2p, g.N, i0, j0);
+                    read_row<RI, RJ>(scur + (k - k0) * g.W, S1p, S2p, Nr, i0, j0);
                     float fr[RI], fc[RJ];
                     if (NU) tb.at(p, dts[k]);
                     const bool bp = basepoint && (t0 + k == 0);
@@ -1336,42 +1340,46 @@ static int num_sms() {
     return n;
 }
 
-template <int NP, bool NU>
+template <int NP, bool NU, bool FULL>
 static int launch_fwd_t(const Params& p, cudaStream_t s) {
     const size_t smem = fwd_smem(p.g);
-    cudaFuncSetAttribute(fwd_kernel<NP, NU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(fwd_kernel<NP, NU, FULL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int per_sm = 0;
-    per_sm = resident_ctas((const void*)fwd_kernel<NP, NU>, kWarps * 32, smem);
+    per_sm = resident_ctas((const void*)fwd_kernel<NP, NU, FULL>, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     int grid = per_sm * num_sms();
     const int need = (p.g.ntiles + kWarps - 1) / kWarps;
     if (grid > need) grid = need;
-    fwd_kernel<NP, NU><<<grid, kWarps * 32, smem, s>>>(p);
+    fwd_kernel<NP, NU, FULL><<<grid, kWarps * 32, smem, s>>>(p);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 
 template <int NP>
 static int launch_fwd(const Params& p, cudaStream_t s) {
-    return p.g.nu ? launch_fwd_t<NP, true>(p, s) : launch_fwd_t<NP, false>(p, s);
+    const bool full = p.g.N == NP;
+    if (p.g.nu) return full ? launch_fwd_t<NP, true, true>(p, s) : launch_fwd_t<NP, true, false>(p, s);
+    return full ? launch_fwd_t<NP, false, true>(p, s) : launch_fwd_t<NP, false, false>(p, s);
 }
 
-template <int NP, bool NU>
+template <int NP, bool NU, bool FULL>
 static int launch_bwd_t(const Params& p, cudaStream_t s) {
     const size_t smem = bwd_smem(p.g);
-    cudaFuncSetAttribute(bwd_kernel<NP, NU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(bwd_kernel<NP, NU, FULL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int per_sm = 0;
-    per_sm = resident_ctas((const void*)bwd_kernel<NP, NU>, kWarps * 32, smem);
+    per_sm = resident_ctas((const void*)bwd_kernel<NP, NU, FULL>, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     int grid = per_sm * num_sms();
     const int need = (p.g.ntiles + kWarps - 1) / kWarps;
     if (grid > need) grid = need;
-    bwd_kernel<NP, NU><<<grid, kWarps * 32, smem, s>>>(p);
+    bwd_kernel<NP, NU, FULL><<<grid, kWarps * 32, smem, s>>>(p);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 
 template <int NP>
 static int launch_bwd(const Params& p, cudaStream_t s) {
-    return p.g.nu ? launch_bwd_t<NP, true>(p, s) : launch_bwd_t<NP, false>(p, s);
+    const bool full = p.g.N == NP;
+    if (p.g.nu) return full ? launch_bwd_t<NP, true, true>(p, s) : launch_bwd_t<NP, true, false>(p, s);
+    return full ? launch_bwd_t<NP, false, true>(p, s) : launch_bwd_t<NP, false, false>(p, s);
 }
 
 // Coefficients of the in-kernel series tables: c1_p / p! = 1 / ((p+1) p!) and
