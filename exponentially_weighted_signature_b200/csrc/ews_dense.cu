@@ -60,7 +60,11 @@ struct Params {
     float* pw;  // per sample: flow complements C(Lc) and C(last chunk), row-major (2 MM)
     float* lam;        // backward: the cotangent stream l~_t = l_t + g_t, same layout as the prefix output
     float* lcarry;     // backward: per chunk the cotangent arriving at its end [- | L1 | L2] (SW)
+    float* loc;        // local terms per (sample, interval): [s1 | U_0..U_{QP-1} | V_0..V_{QP-1}], NP each
 };
+
+// Width (floats) of one interval's local terms in `loc`.
+__host__ __device__ inline int loc_width(int QP) { return (1 + 2 * QP) * 32; }
 
 __host__ __device__ inline int align4(int n) { return (n + 3) & ~3; }
 __host__ __device__ inline int imax(int a, int b) { return a > b ? a : b; }
@@ -653,25 +657,23 @@ struct TcSmem {
     float* stage; // TILES x W prefix rows; also look-back scratch (>= 2 MM)
     float* Dr;    // D row-major
     float* Dt;    // D k-major
-    float* F;     // NP x d_in
-    float* G;     // QP x NP x d_in
-    float* H;
-    float* vec;   // per tile: S1, u, s1, x(d_in) | U, V (NP x QMAX each)
+    float* vec;   // per tile: S1 (l1) | u (v) | two staging slots of local terms
     float* misc;  // small vectors for the look-back
     uint64_t* bar;
     uint32_t* tmem;
     int* bcast;
 };
 
-constexpr int kVecPerTile = 3 * NP + 32 + 2 * NP * QMAX;
+// Per-tile vectors: S1 (or l1) | u (or v) | two staging slots for an interval's local terms.
+__host__ __device__ inline int vec_per_tile(int QP) { return 2 * NP + 2 * loc_width(QP); }
 
 // Per-tile stage stride: a prefix row, or the tile's saved level-2 state while its chunk has ended.
 __host__ __device__ inline int tc_stage_stride(int W) { return align4(imax(W, MM)); }
 __host__ __device__ inline int tc_stage_floats(int W) { return TILES * tc_stage_stride(W); }
 
-__host__ __device__ inline size_t tc_smem_bytes(int W, int d_in, int QP) {
-    size_t f = 2 * MM + 2 * 4 * MM + TILES * 32 * RQS + align4(tc_stage_floats(W)) + 2 * MM + align4(NP * d_in) +
-               2 * align4(QP * NP * d_in) + TILES * kVecPerTile + 8 * NP;
+__host__ __device__ inline size_t tc_smem_bytes(int W, int QP) {
+    size_t f = 2 * MM + 2 * 4 * MM + TILES * 32 * RQS + align4(tc_stage_floats(W)) + 2 * MM +
+               TILES * vec_per_tile(QP) + 8 * NP;
     return f * sizeof(float) + 64 + 128;  // + barrier / tmem slot / broadcast, + alignment slack
 }
 
@@ -687,10 +689,7 @@ __device__ TcSmem tc_carve(unsigned char* raw, const Geom& g) {
     s.stage = p; p += align4(tc_stage_floats(g.W));
     s.Dr = p; p += MM;
     s.Dt = p; p += MM;
-    s.F = p; p += align4(NP * g.d_in);
-    s.G = p; p += align4(g.QP * NP * g.d_in);
-    s.H = p; p += align4(g.QP * NP * g.d_in);
-    s.vec = p; p += TILES * kVecPerTile;
+    s.vec = p; p += TILES * vec_per_tile(g.QP);
     s.misc = p; p += 8 * NP;
     s.bar = reinterpret_cast<uint64_t*>(p);
     s.tmem = reinterpret_cast<uint32_t*>(p + 2);
@@ -698,10 +697,9 @@ __device__ TcSmem tc_carve(unsigned char* raw, const Geom& g) {
     return s;
 }
 
-// Tables of sample b; the B operand is D (forward) or D^T (the adjoint chain, transpose = true).
+// Flow table of sample b; the B operand is D (forward) or D^T (the adjoint chain, transpose = true).
 __device__ void tc_load_tables(const Params& p, const TcSmem& s, int b, bool transpose = false) {
-    const Geom& g = p.g;
-    const int N = g.N, d = g.d_in;
+    const int N = p.g.N;
     const float* m = p.tab_d + (size_t)b * N * N;
     for (int e = threadIdx.x; e < MM; e += blockDim.x) {
         const int i = e / NP, k = e - i * NP;
@@ -713,62 +711,12 @@ __device__ void tc_load_tables(const Params& p, const TcSmem& s, int b, bool tra
         s.Bhi[o] = hi;
         s.Blo[o] = v - hi;
     }
-    const float* f = p.tab_f + (size_t)b * N * d;
-    for (int e = threadIdx.x; e < NP * d; e += blockDim.x) s.F[e] = (e / d) < N ? f[e] : 0.f;
-    const size_t gq = (size_t)g.QP * N * d;
-    const float* gg = p.tab_g + (size_t)b * gq;
-    const float* hh = p.tab_h + (size_t)b * gq;
-    for (int e = threadIdx.x; e < g.QP * NP * d; e += blockDim.x) {
-        const int a = e / (NP * d), r = e - a * NP * d, i = r / d, c = r - i * d;
-        const bool ok = i < N;
-        s.G[e] = ok ? gg[((size_t)a * N + i) * d + c] : 0.f;
-        s.H[e] = ok ? hh[((size_t)a * N + i) * d + c] : 0.f;
-    }
 }
 
-// Per-tile vectors of a step (warp-local): x = dx_t (the lane's channel, loaded one step ahead),
-// s1 = F x, U = [G_a x], V = [H_a x], u = S1 - D S1. Independent accumulators keep the FMA chains short.
-__device__ void tc_local(const TcSmem& s, const Geom& g, float* v, float xl) {
+// u = S1 - D S1 for the lane's row (v: S1 (NP) | u (NP)); independent accumulators.
+__device__ __forceinline__ void tc_u(const TcSmem& s, float* v) {
     const int l = threadIdx.x & 31;
-    const int d = g.d_in;
-    float* S1 = v;
-    float* u = v + NP;
-    float* s1 = v + 2 * NP;
-    float* x = v + 3 * NP;
-    float* U = v + 3 * NP + 32;
-    float* V = U + NP * QMAX;
-    if (l < d) x[l] = xl;
-    __syncwarp();
-    {
-        const float* Fl = s.F + l * d;
-        float a0 = 0.f, a1 = 0.f;
-        int c = 0;
-        for (; c + 1 < d; c += 2) {
-            a0 = fmaf(Fl[c], x[c], a0);
-            a1 = fmaf(Fl[c + 1], x[c + 1], a1);
-        }
-        if (c < d) a0 = fmaf(Fl[c], x[c], a0);
-        s1[l] = a0 + a1;
-    }
-    for (int a = 0; a < g.QP; ++a) {
-        const float* Ga = s.G + ((size_t)a * NP + l) * d;
-        const float* Ha = s.H + ((size_t)a * NP + l) * d;
-        float g0 = 0.f, g1 = 0.f, h0 = 0.f, h1 = 0.f;
-        int c = 0;
-        for (; c + 1 < d; c += 2) {
-            const float x0 = x[c], x1 = x[c + 1];
-            g0 = fmaf(Ga[c], x0, g0);
-            h0 = fmaf(Ha[c], x0, h0);
-            g1 = fmaf(Ga[c + 1], x1, g1);
-            h1 = fmaf(Ha[c + 1], x1, h1);
-        }
-        if (c < d) {
-            g0 = fmaf(Ga[c], x[c], g0);
-            h0 = fmaf(Ha[c], x[c], h0);
-        }
-        U[l * QMAX + a] = g0 + g1;
-        V[l * QMAX + a] = h0 + h1;
-    }
+    const float* S1 = v;
     float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll
     for (int k = 0; k < NP; k += 4) {
@@ -777,9 +725,74 @@ __device__ void tc_local(const TcSmem& s, const Geom& g, float* v, float xl) {
         d2 = fmaf(s.Dt[(k + 2) * NP + l], S1[k + 2], d2);
         d3 = fmaf(s.Dt[(k + 3) * NP + l], S1[k + 3], d3);
     }
-    u[l] = S1[l] - ((d0 + d1) + (d2 + d3));
+    v[NP + l] = S1[l] - ((d0 + d1) + (d2 + d3));
     __syncwarp();
 }
+
+// Starts the warp's copy of interval t's local terms (the first n floats of its `loc` row) into dst.
+__device__ __forceinline__ void fetch_loc(const Params& p, int b, int t, float* dst, int n) {
+    const float* src = p.loc + ((size_t)b * p.g.T + t) * loc_width(p.g.QP);
+    for (int v = threadIdx.x & 31; v < n / 4; v += 32) cp_async16(dst + 4 * v, src + 4 * v);
+}
+
+}  // namespace tc
+
+// The local terms of every interval, a parallel map over (sample, interval) run ahead of the chains:
+// s1 = F dx, U_a = G_a dx, V_a = H_a dx, the lifted increment and the two factor families of the series
+// leaf's level-2 term s2 = sum_a U_a V_a^T (ews/core/series_leaf.py:72-127 with the lift folded into the
+// tables). One warp per interval, lane = state row; the sample's tables sit in shared memory channel-major
+// (entry (m, c, i) at (m d + c) NP + i) so the lanes read consecutive words.
+constexpr int LNT = 256;   // threads per CTA
+constexpr int LSPAN = 64;  // intervals per CTA
+
+__host__ __device__ inline size_t local_smem_bytes(int d_in, int QP) {
+    return sizeof(float) * ((size_t)(1 + 2 * QP) * d_in * NP + (size_t)LSPAN * d_in);
+}
+
+__global__ void __launch_bounds__(LNT) local_kernel(Params p) {
+    extern __shared__ float lsm[];
+    const Geom& g = p.g;
+    const int N = g.N, d = g.d_in, QP = g.QP, LW = loc_width(QP);
+    const int nt = 1 + 2 * QP;  // tables F, G_0..G_{QP-1}, H_0..H_{QP-1}
+    const int spans = (g.T + LSPAN - 1) / LSPAN;
+    const int b = blockIdx.x / spans, t0 = (blockIdx.x - b * spans) * LSPAN;
+    float* tab = lsm;
+    float* X = tab + (size_t)nt * d * NP;  // LSPAN x d increments
+    const size_t gq = (size_t)QP * N * d;
+    for (int e = threadIdx.x; e < nt * NP * d; e += LNT) {
+        const int m = e / (NP * d), r = e - m * NP * d, i = r / d, c = r - i * d;
+        float v = 0.f;
+        if (i < N) {
+            if (m == 0) v = p.tab_f[((size_t)b * N + i) * d + c];
+            else if (m <= QP) v = p.tab_g[(size_t)b * gq + ((size_t)(m - 1) * N + i) * d + c];
+            else v = p.tab_h[(size_t)b * gq + ((size_t)(m - 1 - QP) * N + i) * d + c];
+        }
+        tab[(m * d + c) * NP + i] = v;
+    }
+    for (int e = threadIdx.x; e < LSPAN * d; e += LNT) {
+        const int tt = e / d, c = e - tt * d, t = t0 + tt;
+        X[e] = t < g.T ? input_increment(p.path, b, t, c, g.T, d, g.flags) : 0.f;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int tt = warp; tt < LSPAN && t0 + tt < g.T; tt += LNT / 32) {
+        const float* x = X + tt * d;
+        float* dst = p.loc + ((size_t)b * g.T + t0 + tt) * LW;
+        for (int m = 0; m < nt; ++m) {
+            const float* tm = tab + (size_t)m * d * NP + lane;
+            float a0 = 0.f, a1 = 0.f;
+            int c = 0;
+            for (; c + 1 < d; c += 2) {
+                a0 = fmaf(tm[c * NP], x[c], a0);
+                a1 = fmaf(tm[(c + 1) * NP], x[c + 1], a1);
+            }
+            if (c < d) a0 = fmaf(tm[c * NP], x[c], a0);
+            dst[m * NP + lane] = a0 + a1;  // [s1 | U_0 .. U_{QP-1} | V_0 .. V_{QP-1}]
+        }
+    }
+}
+
+namespace tc {
 
 // CTA-uniform bounded wait for the MMA commit of the given parity. Returns false on timeout.
 __device__ bool tc_wait(const TcSmem& s, uint32_t parity, int limit) {
@@ -911,8 +924,9 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
     const uint64_t dB_hi = smem_desc(smem_u32(s.Bhi), 512, 128), dB_lo = smem_desc(smem_u32(s.Blo), 512, 128);
     const int groups = (g.C + TILES - 1) / TILES;
     const int ntiles = g.B * groups;
-    float* vt = s.vec + warp * kVecPerTile;  // this warp's tile vectors
+    float* vt = s.vec + warp * vec_per_tile(g.QP);  // S1 | u | two local-term slots
     float* RQt = s.RQ + warp * 32 * RQS;
+    const int LW = loc_width(g.QP);
 
     for (;;) {
         if (tid == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
@@ -948,10 +962,16 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
             }
             __syncwarp();
             float* saved = s.stage + warp * tc_stage_stride(g.W);
-            // the lane's input channel, one step ahead
-            float xnext = (lane < g.d_in && len_me > 0) ? input_increment(p.path, b, t0_me, lane, g.T, g.d_in, g.flags) : 0.f;
+            // the intervals' local terms (computed by local_kernel), copied in one interval ahead
+            if (len_me > 0) fetch_loc(p, b, t0_me, vt + 2 * NP, LW);
+            cp_async_commit();
             for (int k = 0; k < steps; ++k) {
                 const bool live = k < len_me;
+                cp_async_wait<0>();
+                __syncwarp();
+                const float* stg = vt + 2 * NP + (k & 1) * LW;  // this interval's [s1 | U | V]
+                if (k + 1 < len_me) fetch_loc(p, b, t0_me + k + 1, vt + 2 * NP + ((k + 1) & 1) * LW, LW);
+                cp_async_commit();
                 if (k == len_me) {
                     // this tile's chunk has ended: park its state; the remaining steps only feed the MMAs
 #pragma unroll
@@ -979,11 +999,8 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                     for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
                     mma_commit(s.bar);
                 }
-                // local terms of this step while the tensor core runs
-                const float xcur = live ? xnext : 0.f;
-                if (lane < g.d_in && k + 1 < len_me)
-                    xnext = input_increment(p.path, b, t0_me + k + 1, lane, g.T, g.d_in, g.flags);
-                tc_local(s, g, vt, xcur);
+                // u = M S1 while the tensor core runs
+                tc_u(s, vt);
                 if (!tc_wait(s, phase, mbar_limit)) {
                     failed = mma_pending = true;
                     break;
@@ -1025,16 +1042,15 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                     float q2[32];
                     tmem_ld32(tP2 + lane_off, q2);
                     const float* u = vt + NP;
-                    const float* s1 = vt + 2 * NP;
-                    const float* U = vt + 3 * NP + 32;
-                    const float* V = U + NP * QMAX;
+                    const float* s1 = stg;
                     const float s1l = s1[lane];
 #pragma unroll
                     for (int n = 0; n < 32; ++n) col[n] = fmaf(u[n], s1l, xcol[n] - q2[n]);
                     for (int a = 0; a < g.QP; ++a) {
-                        const float va = V[lane * QMAX + a];
+                        const float* Ua = stg + NP + a * NP;
+                        const float va = stg[NP + g.QP * NP + a * NP + lane];
 #pragma unroll
-                        for (int n = 0; n < 32; ++n) col[n] = fmaf(U[n * QMAX + a], va, col[n]);
+                        for (int n = 0; n < 32; ++n) col[n] = fmaf(Ua[n], va, col[n]);
                     }
                     const float s1new = u[lane] + s1l;
                     __syncwarp();
@@ -1542,12 +1558,13 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
     const uint64_t dB_hi = smem_desc(smem_u32(s.Bhi), 512, 128), dB_lo = smem_desc(smem_u32(s.Blo), 512, 128);
     const int groups = (g.C + TILES - 1) / TILES;
     const int ntiles = g.B * groups;
-    float* vt = s.vec + warp * kVecPerTile;  // L1 (NP) | v (NP) | s1 (NP) | x (32) | U, V
+    float* vt = s.vec + warp * vec_per_tile(g.QP);  // L1 (NP) | v (NP) | s1 of two intervals (NP each)
     float* RQt = s.RQ + warp * 32 * RQS;
-    // the next interval's gradient row, copied in (cp.async) while the current one runs:
-    // gb[0..N) level 1, gb[32 + 32 n + j] level 2 (idle stage space during the passes)
+    // the next interval's gradient row and s1, copied in (cp.async) while the current one runs:
+    // gb[0..N) level 1, gb[32 + 32 n + j] level 2 (idle stage space during the passes); s1 of interval
+    // t0_me + k in vt[2 NP + (k & 1) NP ..]
     float* gb = s.stage + warp * tc_stage_stride(g.W);
-    auto fetch_grad = [&](int t) {
+    auto fetch_grad = [&](int t, int k) {
         const float* grow = p.grad_out + ((size_t)b_cur * g.T + t) * g.W;
         if (lane < N) {
 #pragma unroll
@@ -1555,6 +1572,7 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
                 if (n < N) cp_async4(gb + 32 + 32 * n + lane, grow + 1 + N + n * N + lane);
             cp_async4(gb + lane, grow + 1 + lane);
         }
+        fetch_loc(p, b_cur, t, vt + 2 * NP + (k & 1) * NP, NP);
         cp_async_commit();
     };
 
@@ -1593,9 +1611,7 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
             }
             __syncwarp();
             // steps run in reverse; the chunk's last interval is len_me - 1 (shorter chunks idle on zero state)
-            float xnext = (lane < g.d_in && len_me > 0)
-                              ? input_increment(p.path, b, t0_me + len_me - 1, lane, g.T, g.d_in, g.flags) : 0.f;
-            if (len_me > 0) fetch_grad(t0_me + len_me - 1);
+            if (len_me > 0) fetch_grad(t0_me + len_me - 1, len_me - 1);
             for (int k = steps - 1; k >= 0; --k) {
                 const bool live = k < len_me;
                 const int t = t0_me + k;
@@ -1610,7 +1626,7 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
                         vt[lane] += gb[lane];
                     }
                     __syncwarp();
-                    if (k >= 1) fetch_grad(t - 1);
+                    if (k >= 1) fetch_grad(t - 1, k - 1);
                 }
                 __syncwarp();
                 if (pass == 1 && live && lane < N) {
@@ -1642,20 +1658,16 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
                     for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
                     mma_commit(s.bar);
                 }
-                // s1_t of this interval, then v = l~1 + l~2 s1 (row `lane` of l~2 against s1)
+                // v = l~1 + l~2 s1_t (row `lane` of l~2 against this interval's s1; idle steps add nothing)
                 {
-                    const float xcur = live ? xnext : 0.f;
-                    if (lane < g.d_in && k - 1 >= 0 && k - 1 < len_me)
-                        xnext = input_increment(p.path, b, t - 1, lane, g.T, g.d_in, g.flags);
-                    tc_local(s, g, vt, xcur);
-                    const float* s1 = vt + 2 * NP;
+                    const float* s1 = vt + 2 * NP + (k & 1) * NP;
                     float w0 = 0.f, w1 = 0.f;
 #pragma unroll
                     for (int n = 0; n < 32; n += 2) {
                         w0 = fmaf(srow[n], s1[n], w0);
                         w1 = fmaf(srow[n + 1], s1[n + 1], w1);
                     }
-                    vt[NP + lane] = vt[lane] + (w0 + w1);
+                    vt[NP + lane] = vt[lane] + (live ? w0 + w1 : 0.f);
                     __syncwarp();
                 }
                 if (!tc_wait(s, phase, mbar_limit)) {
@@ -1887,16 +1899,18 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
     float* Zr = Xk + MM;         // Z row-major
     float* Dr = Zr + MM;         // D row-major
     float* Dt = Dr + MM;         // D k-major
-    float* vec = Dt + MM;        // L1, S1p, u, s1, du, ds1 (NP each)
-    float* L1 = vec, *S1p = vec + NP, *u = vec + 2 * NP, *s1 = vec + 3 * NP, *du = vec + 4 * NP, *ds1 = vec + 5 * NP;
-    float* UV = vec + 6 * NP;    // U, V, dU, dV (NP x QMAX each)
-    float* U = UV, *V = UV + NP * QMAX, *dU = UV + 2 * NP * QMAX, *dV = UV + 3 * NP * QMAX;
-    float* x = UV + 4 * NP * QMAX;                 // 32
+    float* vec = Dt + MM;        // L1, S1p, u, du, ds1 (NP each)
+    float* L1 = vec, *S1p = vec + NP, *u = vec + 2 * NP, *du = vec + 3 * NP, *ds1 = vec + 4 * NP;
+    float* UV = vec + 5 * NP;    // dU, dV (NP x QMAX each)
+    float* dU = UV, *dV = UV + NP * QMAX;
+    float* x = UV + 2 * NP * QMAX;                 // 32
     float* F = x + 32;                             // NP x d
     float* Gt = F + align4(NP * d);                // QP x NP x d
     float* Ht = Gt + align4(QP * NP * d);
     float* tacc = Ht + align4(QP * NP * d);        // (1 + 2 QP) x NP x d
     const int tabn = (1 + 2 * QP) * NP * d;
+    const int LW = loc_width(QP);
+    float* locb = tacc + align4(tabn);             // two intervals' local terms [s1 | U_a | V_a]
 
     const int tile = blockIdx.x;  // c * B + b, the reduction's order
     const int c = tile / g.B, b = tile - c * g.B;
@@ -1921,7 +1935,7 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
             Ht[e] = ok ? p.tab_h[(size_t)b * gq + ((size_t)a * N + i) * d + cc] : 0.f;
         }
         for (int e = tid; e < tabn; e += GNT) tacc[e] = 0.f;
-        for (int e = tid; e < 6 * NP + 4 * NP * QMAX + 32; e += GNT) vec[e] = 0.f;
+        for (int e = tid; e < 5 * NP + 2 * NP * QMAX + 32; e += GNT) vec[e] = 0.f;
     }
     float dM[4][2];
 #pragma unroll
@@ -1942,6 +1956,10 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
         pl1 = tid < N ? ldcg(lrow + 1 + tid) : 0.f;
         ps1 = (tid < N && srow) ? ldcg(srow + 1 + tid) : 0.f;
         px = tid < d ? input_increment(p.path, b, t, tid, g.T, d, g.flags) : 0.f;
+        const float* lsrc = p.loc + ((size_t)b * g.T + t) * LW;
+        float* ldst = locb + ((t - t0) & 1) * LW;
+        for (int v = tid; v < LW / 4; v += GNT) cp_async16(ldst + 4 * v, lsrc + 4 * v);
+        cp_async_commit();
     };
     if (len > 0) prefetch(t0);
     __syncthreads();
@@ -1961,9 +1979,13 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
             S1p[tid] = ps1;
         }
         if (tid < d) x[tid] = px;
+        cp_async_wait<0>();
         __syncthreads();
+        const float* s1 = locb + (k & 1) * LW;  // this interval's s1, U_a = s1 + NP + a NP, V_a = U_a + QP NP
+        const float* U = s1 + NP;
+        const float* V = U + QP * NP;
         if (k + 1 < len) prefetch(t + 1);
-        // (2) local vectors, one per warp, then X = S2p - S2p D^T, Z = l~2 - D^T l~2
+        // (2) u = M S1p (warp 0), then X = S2p - S2p D^T, Z = l~2 - D^T l~2
         if (warp == 0) {
             float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
@@ -1974,18 +1996,6 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
                 a3 = fmaf(Dt[(kk + 3) * NP + lane], S1p[kk + 3], a3);
             }
             u[lane] = S1p[lane] - ((a0 + a1) + (a2 + a3));
-        } else if (warp == 1) {
-            float a1 = 0.f;
-            for (int cc = 0; cc < d; ++cc) a1 = fmaf(F[lane * d + cc], x[cc], a1);
-            s1[lane] = a1;
-        } else {
-            float* out = warp == 2 ? U : V;
-            const float* tab = warp == 2 ? Gt : Ht;
-            for (int a = 0; a < QP; ++a) {
-                float acc = 0.f;
-                for (int cc = 0; cc < d; ++cc) acc = fmaf(tab[((size_t)a * NP + lane) * d + cc], x[cc], acc);
-                out[lane * QMAX + a] = acc;
-            }
         }
         {
             float X[4][2] = {}, Z[4][2] = {};
@@ -2031,8 +2041,8 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
                 float a0 = 0.f, a1 = 0.f;
 #pragma unroll
                 for (int j = 0; j < NP; j += 2) {
-                    a0 = fmaf(lv[j], W[j * QMAX + a], a0);
-                    a1 = fmaf(lv[j + 1], W[(j + 1) * QMAX + a], a1);
+                    a0 = fmaf(lv[j], W[a * NP + j], a0);
+                    a1 = fmaf(lv[j + 1], W[a * NP + j + 1], a1);
                 }
                 out[lane * QMAX + a] = a0 + a1;
             }
@@ -2075,8 +2085,8 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
 }
 
 static size_t grad_smem_bytes(const Geom& g) {
-    const size_t f = 8 * (size_t)MM + 6 * NP + 4 * NP * QMAX + 32 + align4(NP * g.d_in) + 2 * align4(g.QP * NP * g.d_in) +
-                     (size_t)(1 + 2 * g.QP) * NP * g.d_in;
+    const size_t f = 8 * (size_t)MM + 5 * NP + 2 * NP * QMAX + 32 + align4(NP * g.d_in) + 2 * align4(g.QP * NP * g.d_in) +
+                     align4((1 + 2 * g.QP) * NP * g.d_in) + 2 * (size_t)loc_width(g.QP);
     return f * sizeof(float);
 }
 
@@ -2148,7 +2158,7 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 struct WsLayout {
-    size_t status, flags, agg, incl, carry, partials, pw, total;
+    size_t status, flags, agg, incl, carry, partials, pw, loc, total;
 };
 
 static WsLayout fwd_layout(const Geom& g) {
@@ -2167,6 +2177,8 @@ static WsLayout fwd_layout(const Geom& g) {
     o += slots;
     L.pw = o;
     o += al256(sizeof(float) * (size_t)g.B * 2 * MM);
+    L.loc = o;  // the intervals' local terms, written by local_kernel and read by both chains and grad_kernel
+    o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
     L.total = o;
     return L;
 }
@@ -2257,9 +2269,18 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     p.incl = (float*)(ws + L.incl);
     p.carry = (float*)(ws + L.carry);
     p.pw = (float*)(ws + L.pw);
+    p.loc = (float*)(ws + L.loc);
     power_kernel<<<g.B, NT, 5 * MM * sizeof(float), s>>>(p);
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
-    const size_t smem = tc::tc_smem_bytes(g.W, g.d_in, g.QP);
+    {
+        const size_t lsmem = local_smem_bytes(g.d_in, g.QP);
+        if (lsmem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+        cudaFuncSetAttribute(local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem);
+        const int spans = (g.T + LSPAN - 1) / LSPAN;
+        local_kernel<<<g.B * spans, LNT, lsmem, s>>>(p);
+        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    }
+    const size_t smem = tc::tc_smem_bytes(g.W, g.QP);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
@@ -2304,10 +2325,11 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     p.agg = (float*)(ws + L.agg);
     p.incl = (float*)(ws + L.incl);
     p.fagg = (const float*)(fws + F.agg);
+    p.loc = (float*)(fws + F.loc);
     p.lcarry = (float*)(ws + L.carry);
     p.lam = (float*)(ws + L.pw);
     {
-        const size_t smem = tc::tc_smem_bytes(g.W, g.d_in, g.QP);
+        const size_t smem = tc::tc_smem_bytes(g.W, g.QP);
         if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
         cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
