@@ -39,6 +39,8 @@ EXPORTED = (
     "ews_block_workspace_size",
     "ews_block_fwd",
     "ews_block_bwd",
+    "ews_expm_batched",
+    "ews_expm_adjoint_batched",
     "ews_read_device_status",
     "ews_error_string",
     "ews_version",
@@ -188,6 +190,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.POINTER(BlockArgs), _vp]
             fn.restype = _c_int
+        lib.ews_expm_batched.argtypes = [_vp, _vp, _c_int, _c_int, _vp]
+        lib.ews_expm_batched.restype = _c_int
+        lib.ews_expm_adjoint_batched.argtypes = [_vp, _vp, _vp, _c_int, _c_int, _vp]
+        lib.ews_expm_adjoint_batched.restype = _c_int
         lib.ews_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(_c_int)]
         lib.ews_read_device_status.restype = _c_int
         lib.ews_error_string.argtypes = [_c_int]

@@ -124,6 +124,38 @@ class DiagScan(torch.autograd.Function):
         return gpath.to(path_dtype), gx, gq1, gq2, glift, None, None, None, None
 
 
+class Expm(torch.autograd.Function):
+    """Batched float64 matrix exponential (B, n, n) on the device, n <= 64 (the adjoint: n <= 32). The
+    forward and the VJP (the Frechet derivative L(X^T, G)) run in the library, so the dense engine's
+    tables are built without a host round trip."""
+
+    @staticmethod
+    def forward(ctx, X):
+        _require_cuda(X)
+        if X.dtype != torch.float64:
+            raise TypeError("Expm takes float64 matrices")
+        Xc = X.contiguous()
+        out = torch.empty_like(Xc)
+        n = Xc.shape[-1]
+        batch = Xc.numel() // (n * n) if n else 0
+        _lib.check(_lib.load().ews_expm_batched(_ptr(Xc), _ptr(out), batch, n, _stream_ptr(Xc.device)), "ews_expm_batched")
+        ctx.save_for_backward(Xc)
+        return out
+
+    @staticmethod
+    def backward(ctx, G):
+        (X,) = ctx.saved_tensors
+        Gc = G.to(torch.float64).contiguous()
+        out = torch.empty_like(X)
+        n = X.shape[-1]
+        batch = X.numel() // (n * n) if n else 0
+        _lib.check(
+            _lib.load().ews_expm_adjoint_batched(_ptr(X), _ptr(Gc), _ptr(out), batch, n, _stream_ptr(X.device)),
+            "ews_expm_adjoint_batched",
+        )
+        return out
+
+
 class DenseScan(torch.autograd.Function):
     """Dense engine, uniform clock: (path, D = I - M, F, G, H) -> flat EWS (prefix or terminal)."""
 

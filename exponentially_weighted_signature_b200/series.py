@@ -103,27 +103,40 @@ def diag_tables(x: torch.Tensor, q: int):
     return q1.to(x.dtype), q2.to(x.dtype)
 
 
-def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None):
-    """Per-sample tables of the dense engine for generator A (N, N), clock steps h (B,) and lift W (N, d_in):
-    the flow complement D = I - expm(-hA), F = K1 W, G_a = P_a W, H_a = K2_a W with P_a = (-hA)^a / a!,
-    K1 = sum_p c_p P_p, K2_a = sum_b c_ab P_b (the series leaf with shared letters,
-    ews/core/series_leaf.py:72-113). Differentiable; evaluated in float64 and returned in float32."""
-    Ad = A.to(torch.float64)
-    X = -h.to(torch.float64)[:, None, None] * Ad  # (B, N, N)
-    N = A.shape[-1]
-    Dc = torch.eye(N, dtype=torch.float64, device=A.device) - torch.linalg.matrix_exp(X)
-    eye = torch.eye(N, dtype=torch.float64, device=A.device).expand_as(X)
+@lru_cache(maxsize=None)
+def _leaf_coeffs(q: int, device: str):
+    """c_p (q+1,) and c_ab (q+1, q+1) of the depth-2 series leaf as float64 tensors on ``device``, made
+    once per (q, device) so that building the tables issues no host-to-device copy."""
+    C1, C2 = series_coeffs(2, q)
+    return (torch.tensor(C1, dtype=torch.float64, device=device), torch.tensor(C2, dtype=torch.float64, device=device))
+
+
+def dense_leaf_tables(X: torch.Tensor, q: int, lift=None):
+    """The series-leaf tables of the dense engine at X = -h A (B, N, N), float64: F = K1 W, G_a = P_a W,
+    H_a = K2_a W with P_a = X^a / a!, K1 = sum_p c_p P_p, K2_a = sum_b c_ab P_b (the series leaf with
+    shared letters, ews/core/series_leaf.py:72-113) and the lift W (identity when None). Differentiable."""
+    N = X.shape[-1]
+    eye = torch.eye(N, dtype=X.dtype, device=X.device).expand_as(X)
     P = [eye]
     for a in range(1, q + 1):
         P.append(P[-1] @ X / a)
     P = torch.stack(P, dim=1)  # (B, q+1, N, N)
-    C1, C2 = series_coeffs(2, q)
-    c1 = torch.tensor(C1, dtype=torch.float64, device=A.device)
-    c2 = torch.tensor(C2, dtype=torch.float64, device=A.device)
+    c1, c2 = _leaf_coeffs(int(q), str(X.device))
     K1 = torch.einsum("p,bpij->bij", c1, P)
     K2 = torch.einsum("ab,zbij->zaij", c2, P)
-    W = torch.eye(N, dtype=torch.float64, device=A.device) if lift is None else lift.to(torch.float64)
-    F = K1 @ W
-    G = P @ W
-    H = K2 @ W
+    W = torch.eye(N, dtype=X.dtype, device=X.device) if lift is None else lift.to(X.dtype)
+    return K1 @ W, P @ W, K2 @ W
+
+
+def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None):
+    """Per-sample tables of the dense engine for generator A (N, N), clock steps h (B,) and lift W (N, d_in):
+    the flow complement D = I - expm(-hA) and the series-leaf tables F, G, H (dense_leaf_tables).
+    Differentiable; evaluated in float64 and returned in float32. The exponential
+    (ews/core/chen_scan.py:155-168) and its VJP run in the library's expm kernels (CUDA tensors only)."""
+    from .engine import Expm
+
+    X = -h.to(torch.float64)[:, None, None] * A.to(torch.float64)  # (B, N, N)
+    N = A.shape[-1]
+    Dc = torch.eye(N, dtype=torch.float64, device=A.device) - Expm.apply(X)
+    F, G, H = dense_leaf_tables(X, q, lift)
     return Dc.float(), F.float(), G.float(), H.float()

@@ -216,6 +216,16 @@ int ews_block_workspace_size(const ews_block_args* a, size_t* fwd_bytes, size_t*
 int ews_block_fwd(const ews_block_args* a, ews_stream_t stream);
 int ews_block_bwd(const ews_block_args* a, ews_stream_t stream);
 
+/* ---- flow tables of the dense engine ---------------------------------------------------------------
+ * Replaces expm_matrix(-h A, "exact") (ews/core/chen_scan.py:155-168, ews/core/expm_approx.py:34-41),
+ * the dense flow the reference builds per clock step, and its VJP. Row-major float64 matrices on the
+ * device; one CTA per matrix, scaling and squaring with a degree-14 Taylor polynomial (the scaling is
+ * chosen in the kernel, nothing is read back to the host).
+ *   ews_expm_batched:          out_b = expm(x_b),            x, out (batch, n, n), n <= 64
+ *   ews_expm_adjoint_batched:  out_b = d<g_b, expm(x_b)>/dx_b = L(x_b^T, g_b), n <= 32 */
+int ews_expm_batched(const double* x, double* out, int batch, int n, ews_stream_t stream);
+int ews_expm_adjoint_batched(const double* x, const double* g, double* out, int batch, int n, ews_stream_t stream);
+
 /* ---- utilities --------------------------------------------------------------------------------- */
 /* Copies the device-side status word of a workspace (EWS_OK or EWS_ERR_LOOKBACK_TIMEOUT) to the host;
  * synchronises the stream. */
