@@ -114,6 +114,19 @@ def test_gradients_match_oracle(N, readout):
         _assert_close(f"{name} grad", a, b)
 
 
+@pytest.mark.parametrize("N,d_in,q,T,chunk", [(32, 7, 6, 75, 7), (5, 3, 2, 33, 5), (16, 11, 8, 40, 8)])
+def test_gradients_odd_chunks_and_table_sizes(N, d_in, q, T, chunk):
+    """Odd chunk lengths, a padded state (N = 5) and large series tables (q = 8, d_in = 11)."""
+    _require_gpu()
+    path, clock, A, lift = _case(2, T, N, d_in=d_in, seed=40 + N)
+    ref, _ = _oracle(path, clock, A, lift, "prefix", q)
+    w = torch.tensor(np.random.default_rng(5).normal(size=ref.shape))
+    _, (gp_r, ga_r, gb_r) = _oracle(path, clock, A, lift, "prefix", q, w=w)
+    _, (gp_n, ga_n, gb_n) = _kernel(path, clock, A, lift, "prefix", q, w=w, chunk=chunk)
+    for name, a, b in [("path", gp_n, gp_r), ("A", ga_n, ga_r), ("lift", gb_n, gb_r)]:
+        _assert_close(f"{name} grad", a, b)
+
+
 def test_identity_lift():
     _require_gpu()
     path, clock, A, _ = _case(2, 40, 12, d_in=12, seed=4, scale=0.5)
