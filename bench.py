@@ -218,20 +218,19 @@ def _stacked_setup(cfg, rank, world, device, precision, batch=None):
     q = 8
     model = StackedEWS(4, 21, 128, 21, block_kwargs=dict(m=16, n=2, series_q=q, clock_norm_constant=float(T),
                                                           dropout_rate=0.01), seed=1).to(device)
-    opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True)
+    opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True, capturable=True)
     params = list(model.parameters())
     x_host = torch.tensor(case["inputs"][s0:s1])
     y_host = torch.tensor(case["targets"][s0:s1])
     Bl = s1 - s0
 
     def step(x, y):
-        opt.zero_grad(set_to_none=True)
         loss = torch.nn.functional.mse_loss(model(x), y)
         loss.backward()
-        if world > 1:
-            parallel.allreduce_gradients(params, average=True)
-        opt.step()
         return loss
+
+    def post():  # after the gradients are reduced across ranks
+        opt.step()
 
     D = 16 + 16 * 16
     out_row = 4 * (1 + D)
@@ -241,8 +240,8 @@ def _stacked_setup(cfg, rank, world, device, precision, batch=None):
     meta = dict(B_global=Bg, B_local=Bl, T=T, N=16, scaling=scaling, q=q, readout="prefix", dtype="f32",
                 precision="f32", depth=2, blocks=4, optimizer_in_step=True)
     ws_bytes = 4 * Bl * T * out_row * 4
-    return dict(step=step, params=[], x_host=x_host, clock_host=y_host, alg=alg, meta=meta,
-                ws_bytes=ws_bytes, units=Bl * T, case=case)
+    return dict(step=step, params=params, post=post, average=True, x_host=x_host, clock_host=y_host, alg=alg,
+                meta=meta, ws_bytes=ws_bytes, units=Bl * T, case=case)
 
 
 # ------------------------------------------------------------------------------------ helpers
@@ -426,12 +425,20 @@ def run_b200(args, rank, world, local_rank):
     if setup["ws_bytes"] < 2 * L2_BYTES:
         flush = torch.zeros(2 * L2_BYTES // 4, device=device)
 
+    post = setup.get("post")
+    average = setup.get("average", False)
+
+    def reduce_and_update():
+        if world > 1:
+            parallel.allreduce_gradients(params, average=average)
+        if post is not None:
+            post()
+
     def one(xx, cc):
         for p in params:
             p.grad = None
         loss = step(xx, cc)
-        if world > 1:
-            parallel.allreduce_gradients(params)
+        reduce_and_update()
         return loss
 
     for _ in range(args.warmup):
@@ -440,30 +447,77 @@ def run_b200(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
 
+    def timed(run, n):
+        """n steps of run() between events on the current stream; the max over ranks of the sum (ms)."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        for i in range(n):
+            _flush_l2(flush)
+            evs[i][0].record()
+            run()
+            evs[i][1].record()
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in evs)
+        tt = torch.tensor([ms], device=device)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    # eager pass: the engines' device times per call (recorded on the launching stream)
+    engine.PROFILE = []
+    eager_ms = timed(lambda: one(x, clock), args.steps)
+    prof = engine.PROFILE
+    engine.PROFILE = None
+
+    # the training step captured once as CUDA graphs (the compute, then the optimizer when there is one;
+    # the cross-rank gradient allreduce runs between them, outside the graphs) and replayed: the
+    # launch-for-launch equivalent of the reference's jit-compiled step
+    replay, graph_note = None, None
+    if args.graph:
+        try:
+            side = torch.cuda.Stream(device)
+            side.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    one(x, clock)
+            torch.cuda.current_stream(device).wait_stream(side)
+            torch.cuda.synchronize()
+            for p in params:
+                p.grad = None
+            g_step = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_step):
+                loss_static = step(x, clock)
+            g_post = None
+            if post is not None:
+                g_post = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g_post):
+                    post()
+
+            def replay():
+                g_step.replay()
+                if world > 1:
+                    parallel.allreduce_gradients(params, average=average)
+                if g_post is not None:
+                    g_post.replay()
+                return loss_static
+
+            for _ in range(args.warmup):
+                replay()
+            torch.cuda.synchronize()
+        except Exception as exc:  # capture failed: the eager step is the measured one
+            graph_note = f"{type(exc).__name__}: {exc}"[:300]
+            replay = None
+            torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
     sampler = ClockSampler(local_rank) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
-    engine.PROFILE = []
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    for i in range(args.steps):
-        _flush_l2(flush)
-        ev[i][0].record()
-        one(x, clock)
-        ev[i][1].record()
-    torch.cuda.synchronize()
-    prof = engine.PROFILE
-    engine.PROFILE = None
-    if world > 1:
-        dist.barrier()
-    total_ms = sum(a.elapsed_time(b) for a, b in ev)
-    t = torch.tensor([total_ms], device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
+    total_ms = timed(replay if replay is not None else (lambda: one(x, clock)), args.steps)
     clocks = sampler.stop() if sampler else None
 
     # kernel timing from the launching stream
@@ -496,31 +550,21 @@ def run_b200(args, rank, world, local_rank):
     # end to end: host inputs copied in, loss read back, every step
     xh = setup["x_host"].pin_memory()
     ch = setup["clock_host"].pin_memory()
-    xd = torch.empty_like(x)
-    cd = torch.empty_like(clock)
+    # the graphs read x and clock: the end-to-end step refills those buffers from pinned host memory
+    xd = x if replay is not None else torch.empty_like(x)
+    cd = clock if replay is not None else torch.empty_like(clock)
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
-    for _ in range(max(1, args.warmup)):
+
+    def e2e_step():
         xd.copy_(xh, non_blocking=True)
         cd.copy_(ch, non_blocking=True)
-        loss_h.copy_(one(xd, cd).detach(), non_blocking=True)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for i in range(args.steps):
-        _flush_l2(flush)
-        e2e_ev[i][0].record()
-        xd.copy_(xh, non_blocking=True)
-        cd.copy_(ch, non_blocking=True)
-        loss = one(xd, cd)
+        loss = replay() if replay is not None else one(xd, cd)
         loss_h.copy_(loss.detach(), non_blocking=True)
-        e2e_ev[i][1].record()
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
     torch.cuda.synchronize()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
-    t = torch.tensor([e2e_ms], device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t.item())
+    e2e_ms = timed(e2e_step, args.steps)
 
     meta = setup["meta"]
     units_per_step = meta["B_local"] * meta["T"] * world
@@ -575,7 +619,11 @@ def run_b200(args, rank, world, local_rank):
         },
         "gpu_launches": launches,
         "clocks": clocks,
+        "graph": replay is not None,
+        "ms_per_step_eager": eager_ms / args.steps,
     }
+    if graph_note:
+        line["graph_error"] = graph_note
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
@@ -617,6 +665,8 @@ def main():
     ap.add_argument("--precision", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling on a smaller case)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="time the eager step instead of its CUDA-graph replay")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -323,7 +323,7 @@ class LogEWS(nn.Module):
         if output_format == "list":
             if readout in ("mean", "max"):
                 raise ValueError(f"readout='{readout}' requires output_format='flat'")
-            idx = [torch.as_tensor(ix, device=flat.device) for ix in logsig._flat_indices(self.N, self.d)]
+            idx = logsig.flat_index_tensors(self.N, self.d, str(flat.device))
             return [lv[..., ix] for lv, ix in zip(log_levels, idx)]
         feat = logsig.compress(log_levels, self.d)
         if readout == "mean":

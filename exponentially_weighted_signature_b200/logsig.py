@@ -71,11 +71,17 @@ def tensor_log(levels):
     return out
 
 
+@lru_cache(maxsize=None)
+def flat_index_tensors(depth: int, dim: int, device: str):
+    """The Lyndon-word gather indices of every level as int64 tensors on ``device``, made once per
+    (depth, dim, device) so that a forward issues no host-to-device copy."""
+    return tuple(torch.as_tensor(ix, device=device) for ix in _flat_indices(depth, dim))
+
+
 def compress(log_levels, dim: int):
     """Lyndon-word coordinates (..., sum_k W_d(k)) of an expanded log."""
-    n = len(log_levels)
-    idx = _flat_indices(n, dim)
-    return torch.cat([lv[..., torch.as_tensor(ix, device=lv.device)] for lv, ix in zip(log_levels, idx)], dim=-1)
+    idx = flat_index_tensors(len(log_levels), dim, str(log_levels[0].device))
+    return torch.cat([lv[..., ix] for lv, ix in zip(log_levels, idx)], dim=-1)
 
 
 def split_levels(flat, dim: int, depth: int):
