@@ -1401,10 +1401,22 @@ static void series_coefficients(int q, Params* p) {
 using namespace ews;
 using namespace ews::diag;
 
+// The closed-form terminal path of the uniform clock (ews_diag_term.cu).
+namespace ews {
+bool diag_term_applies(const ews_diag_args* a);
+void diag_term_workspace(const ews_diag_args* a, size_t* fwd_bytes, size_t* bwd_bytes);
+int diag_term_fwd(const ews_diag_args* a, cudaStream_t s);
+int diag_term_bwd(const ews_diag_args* a, cudaStream_t s);
+}  // namespace ews
+
 extern "C" int ews_diag_workspace_size(const ews_diag_args* a, size_t* fwd_bytes, size_t* bwd_bytes) {
     Geom g;
     const int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
+    if (diag_term_applies(a)) {
+        diag_term_workspace(a, fwd_bytes, bwd_bytes);
+        return EWS_OK;
+    }
     if (fwd_bytes) *fwd_bytes = fwd_layout(g).total;
     if (bwd_bytes) *bwd_bytes = bwd_layout(g).total;
     return EWS_OK;
@@ -1417,6 +1429,7 @@ extern "C" int ews_diag_fwd(const ews_diag_args* a, ews_stream_t stream) {
     if (!a->path || !a->out || !a->tab_x) return EWS_ERR_INVALID_ARGUMENT;
     if (g.nu ? !a->clock : (!a->tab_q1 || !a->tab_q2)) return EWS_ERR_INVALID_ARGUMENT;
     if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
+    if (diag_term_applies(a)) return diag_term_fwd(a, (cudaStream_t)stream);
     const WsLayout L = fwd_layout(g);
     if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
@@ -1455,6 +1468,7 @@ extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
         return EWS_ERR_INVALID_ARGUMENT;
     if (g.readout == EWS_READOUT_PREFIX && !a->out) return EWS_ERR_INVALID_ARGUMENT;
     if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
+    if (diag_term_applies(a)) return diag_term_bwd(a, (cudaStream_t)stream);
     const WsLayout F = fwd_layout(g);
     const WsLayout L = bwd_layout(g);
     if (!a->fwd_ws || a->fwd_ws_bytes < F.total) return EWS_ERR_WORKSPACE;
@@ -1544,6 +1558,7 @@ extern "C" int ews_diag_fwd_noalloc(const ews_diag_args* a, ews_stream_t stream)
     ews_diag_args b = *a;
     b.fwd_ws = scratch;
     b.fwd_ws_bytes = EWS_NOALLOC_SCRATCH_BYTES;
+    b.flags |= EWS_F_TERMINAL_SCAN;  // the scan's workspace is the one sized against the array above
     // ews_diag_fwd clears the status block and flags it needs zeroed before its kernel runs, allocates
     // nothing, and leaves the aggregates and carries in the array until the next call overwrites them.
     return ews_diag_fwd(&b, stream);

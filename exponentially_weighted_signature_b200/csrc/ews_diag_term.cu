@@ -1,0 +1,555 @@
+// Diagonal engine, uniform clock, terminal readout: the terminal value in closed form.
+//
+// With the per-step flow rho = exp(x) (x = -h lambda per sample), the series tables Q1, Q2 and the lifted
+// increments dy_t, the depth-2 recursion of the uniform diagonal engine
+//     S1_t = rho S1_{t-1} + Q1 dy_t,
+//     S2_t = (rho rho^T) S2_{t-1} + (rho S1_{t-1}) (Q1 dy_t)^T + Q2 (dy_t dy_t^T)      (elementwise products)
+// unrolls, with the interval weights w_t = rho^(T-1-t) and r_t = w_t dy_t, into
+//     S1_T = Q1 sum_t r_t,     S2_T = diag(Q1) M diag(Q1) + Q2 G,
+//     M = sum_t (sum_{tau < t} r_tau) r_t^T,    G = sum_t r_t r_t^T:
+// the decay of every earlier interval cancels against the weights (rho^(t-1-tau) w_t rho = w_tau), so the
+// terminal value is a reweighted depth-2 signature, two Gram-type products over the path and a running sum,
+// with no sequential dependence but the running sum. It is the same value as the reference's terminal
+// reduction of the Chen products (ews/core/chen_scan.py:218-298 with the series leaf
+// ews/core/series_leaf.py:72-127 and cached uniform flows, chen_scan.py:155-168), evaluated in another order.
+//
+// The backward, with G1 = dL/dS1_T and G2 = dL/dS2_T: dM = diag(Q1) G2 diag(Q1), dG = Q2 G2,
+//     dr_t = dM^T P_t + dM Z_t + (dG + dG^T) r_t + Q1 G1,    P_t = sum_{tau < t} r_tau,  Z_t = sum_{tau > t} r_tau,
+//     d(dy_t) = w_t dr_t,   dL/dx += sum_t (T-1-t) dr_t r_t,   dL/dQ2 = G2 G,
+//     dL/dQ1_i = sum_j G2_ij M_ij Q1_j + G2_ji Q1_j M_ji + G1_i s_i   (s = sum_t r_t).
+//
+// Work: one CTA per (sample, segment of the path); a segment runs in chunks of TL intervals through shared
+// memory, its own running sum starting at zero; a finishing kernel combines the segments in order
+// (M = sum_seg (P_seg s_seg^T + M_seg), P_seg the sum of the earlier segments). Float32 throughout; the
+// weights are exp(x k) with the product x k split exactly (x k = hi + lo) so their error stays at a few
+// ulps for every k.
+
+#include <cuda_runtime.h>
+
+#include "../../include/ews_b200.h"
+#include "ews_common.cuh"
+
+namespace ews {
+namespace diagterm {
+
+constexpr int NP = 32;   // padded state dimension
+constexpr int MM = NP * NP;
+constexpr int TL = 128;  // intervals per chunk
+constexpr int TNT = 256; // threads per CTA
+constexpr int PW = 2 * MM + NP;  // per-segment partial: M | G | s
+
+struct TP {
+    int B, T, d_in, N, S, seg;  // S segments of `seg` intervals per sample
+    unsigned flags;
+    const void* path;
+    const float* lift;
+    const float* tab_x;
+    const float* tab_q1;
+    const float* tab_q2;
+    float* out;
+    float* part;   // (B, S, PW): per segment M | G | s from a zero running sum
+    float* save;   // (B, PW): M | G | s of the whole path
+    float* spre;   // (B, S, NP): sum of r over the earlier segments
+    const float* grad_out;
+    float* grad_dx;
+    float* grad_lift;
+    float* grad_x;
+    float* grad_q1;
+    float* grad_q2;
+    float* dmat;   // (B, 2 MM + NP): dM | dG + dG^T | Q1 G1
+    float* bpart;  // (B, S, NP + NP d_in): dL/dx partial | lift-gradient partial
+};
+
+// Shared-memory layout shared by both directions (floats).
+struct TS {
+    float *liftT, *xs, *dxs, *R, *P, *Z, *tot, *carry, *stot;
+};
+
+__device__ __forceinline__ TS carve(float* sm, int d_in) {
+    TS s;
+    float* q = sm;
+    s.R = q; q += TL * NP;
+    s.P = q; q += TL * NP;
+    s.Z = q; q += TL * NP;
+    s.liftT = q; q += 32 * NP;
+    s.dxs = q; q += TL * 32;
+    s.xs = q; q += NP;
+    s.tot = q; q += 8 * NP;
+    s.carry = q; q += NP;
+    s.stot = q; q += NP;
+    return s;
+}
+
+__host__ __device__ inline size_t smem_bytes() { return sizeof(float) * (3 * TL * NP + 32 * NP + TL * 32 + 11 * NP); }
+
+// w = exp(x k) for an integer k >= 0: x k = hi + lo exactly, exp(hi) (1 + lo).
+__device__ __forceinline__ float weight(float x, int k) {
+    const float kf = (float)k;
+    const float hi = x * kf;
+    const float lo = fmaf(x, kf, -hi);
+    return expf(hi) * (1.f + lo);
+}
+
+// The chunk's increments into dxs[t * d_in + c], then r_t = w_t (lift dx_t) into R (rows t < len; zeros
+// beyond, and in the padded columns).
+__device__ void chunk_r(const TP& p, const TS& s, int b, int t0, int len) {
+    const int d = p.d_in, N = p.N;
+    for (int e = threadIdx.x; e < TL * d; e += TNT) {
+        const int t = e / d, c = e - t * d;
+        s.dxs[e] = t < len ? input_increment(p.path, b, t0 + t, c, p.T, d, p.flags) : 0.f;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < TL * NP; e += TNT) {
+        const int t = e >> 5, i = e & 31;
+        float r = 0.f;
+        if (t < len && i < N) {
+            float dy;
+            if (p.lift) {
+                const float* xr = s.dxs + t * d;
+                float a0 = 0.f, a1 = 0.f;
+                int c = 0;
+                for (; c + 1 < d; c += 2) {
+                    a0 = fmaf(s.liftT[c * NP + i], xr[c], a0);
+                    a1 = fmaf(s.liftT[(c + 1) * NP + i], xr[c + 1], a1);
+                }
+                if (c < d) a0 = fmaf(s.liftT[c * NP + i], xr[c], a0);
+                dy = a0 + a1;
+            } else {
+                dy = s.dxs[t * d + i];
+            }
+            r = weight(s.xs[i], p.T - 1 - (t0 + t)) * dy;
+        }
+        s.R[e] = r;
+    }
+    __syncthreads();
+}
+
+// P[t] = carry + sum_{tau < t} R[tau] (exclusive, within the chunk), then carry += sum_t R[t]. Thread
+// (g, i) sums rows 16 g .. 16 g + 15 of column i; the 8 group totals are combined in order.
+__device__ void chunk_prefix(const TS& s) {
+    const int g = threadIdx.x >> 5, i = threadIdx.x & 31;
+    float run = 0.f;
+    for (int t = 16 * g; t < 16 * g + 16; ++t) {
+        s.P[t * NP + i] = run;
+        run += s.R[t * NP + i];
+    }
+    s.tot[g * NP + i] = run;
+    __syncthreads();
+    float base = s.carry[i];
+    for (int h = 0; h < g; ++h) base += s.tot[h * NP + i];
+    for (int t = 16 * g; t < 16 * g + 16; ++t) s.P[t * NP + i] += base;
+    __syncthreads();
+    if (g == 0) {
+        float c = s.carry[i];
+        for (int h = 0; h < 8; ++h) c += s.tot[h * NP + i];
+        s.carry[i] = c;
+    }
+    __syncthreads();
+}
+
+__device__ void load_common(const TP& p, const TS& s, int b) {
+    const int d = p.d_in, N = p.N;
+    for (int e = threadIdx.x; e < 32 * NP; e += TNT) {
+        const int c = e >> 5, i = e & 31;
+        s.liftT[e] = (p.lift && c < d && i < N) ? p.lift[i * d + c] : 0.f;
+    }
+    if (threadIdx.x < NP) s.xs[threadIdx.x] = threadIdx.x < N ? p.tab_x[(size_t)b * N + threadIdx.x] : 0.f;
+}
+
+// ---------------------------------------------------------------------------------- forward
+
+__global__ void __launch_bounds__(TNT) fwd_kernel(TP p) {
+    extern __shared__ __align__(16) float sm[];
+    const TS s = carve(sm, p.d_in);
+    const int b = blockIdx.x / p.S, sg = blockIdx.x - b * p.S;
+    const int tb = sg * p.seg, te = min(p.T, tb + p.seg);
+    load_common(p, s, b);
+    if (threadIdx.x < NP) s.carry[threadIdx.x] = 0.f;
+    // thread (a, q): a < 32 accumulates row a of M, a >= 32 row a - 32 of G; columns 8 q .. 8 q + 7
+    const int a = threadIdx.x >> 2, j0 = 8 * (threadIdx.x & 3);
+    const bool mrow = a < 32;
+    const float* Arow = mrow ? s.P + a : s.R + (a - 32);
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+    for (int t0 = tb; t0 < te; t0 += TL) {
+        const int len = min(TL, te - t0);
+        __syncthreads();
+        chunk_r(p, s, b, t0, len);
+        chunk_prefix(s);
+        for (int k = 0; k < len; ++k) {
+            const float av = Arow[k * NP];
+            const float4 b0 = *reinterpret_cast<const float4*>(s.R + k * NP + j0);
+            const float4 b1 = *reinterpret_cast<const float4*>(s.R + k * NP + j0 + 4);
+            acc[0] = fmaf(av, b0.x, acc[0]);
+            acc[1] = fmaf(av, b0.y, acc[1]);
+            acc[2] = fmaf(av, b0.z, acc[2]);
+            acc[3] = fmaf(av, b0.w, acc[3]);
+            acc[4] = fmaf(av, b1.x, acc[4]);
+            acc[5] = fmaf(av, b1.y, acc[5]);
+            acc[6] = fmaf(av, b1.z, acc[6]);
+            acc[7] = fmaf(av, b1.w, acc[7]);
+        }
+    }
+    float* pp = p.part + ((size_t)b * p.S + sg) * PW;
+    float* dst = pp + (mrow ? a * NP : MM + (a - 32) * NP) + j0;
+    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    __syncthreads();
+    if (threadIdx.x < NP) pp[2 * MM + threadIdx.x] = s.carry[threadIdx.x];
+}
+
+// Combines the segments of sample b in order and writes its terminal row [1, Q1 s, Q1 M Q1 + Q2 G].
+__global__ void __launch_bounds__(TNT) fin_kernel(TP p) {
+    __shared__ float Sc[NP], ss[NP];
+    const int b = blockIdx.x, N = p.N;
+    float M[4], G[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) M[m] = G[m] = 0.f;
+    if (threadIdx.x < NP) Sc[threadIdx.x] = 0.f;
+    __syncthreads();
+    for (int sg = 0; sg < p.S; ++sg) {
+        const float* pp = p.part + ((size_t)b * p.S + sg) * PW;
+        if (threadIdx.x < NP) {
+            ss[threadIdx.x] = pp[2 * MM + threadIdx.x];
+            p.spre[((size_t)b * p.S + sg) * NP + threadIdx.x] = Sc[threadIdx.x];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const int e = threadIdx.x + TNT * m, i = e >> 5, j = e & 31;
+            M[m] += fmaf(Sc[i], ss[j], pp[e]);
+            G[m] += pp[MM + e];
+        }
+        __syncthreads();
+        if (threadIdx.x < NP) Sc[threadIdx.x] += ss[threadIdx.x];
+        __syncthreads();
+    }
+    float* sv = p.save + (size_t)b * PW;
+    const float* q1 = p.tab_q1 + (size_t)b * N;
+    const float* q2 = p.tab_q2 + (size_t)b * N * N;
+    float* row = p.out + (size_t)b * (1 + N + N * N);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int e = threadIdx.x + TNT * m, i = e >> 5, j = e & 31;
+        sv[e] = M[m];
+        sv[MM + e] = G[m];
+        if (i < N && j < N) row[1 + N + i * N + j] = fmaf(q1[i] * M[m], q1[j], q2[i * N + j] * G[m]);
+    }
+    if (threadIdx.x < NP) {
+        sv[2 * MM + threadIdx.x] = Sc[threadIdx.x];
+        if (threadIdx.x < N) row[1 + threadIdx.x] = q1[threadIdx.x] * Sc[threadIdx.x];
+    }
+    if (threadIdx.x == 0) row[0] = 1.f;
+}
+
+// ---------------------------------------------------------------------------------- backward
+
+// Per sample: the cotangent matrices of M, G and s, and the table gradients dL/dQ1, dL/dQ2.
+__global__ void __launch_bounds__(TNT) prep_kernel(TP p) {
+    __shared__ float G2[MM], Ms[MM], q1s[NP];
+    const int b = blockIdx.x, N = p.N, W = 1 + N + N * N;
+    const float* go = p.grad_out + (size_t)b * W;
+    const float* sv = p.save + (size_t)b * PW;
+    const float* q2 = p.tab_q2 + (size_t)b * N * N;
+    float* dm = p.dmat + (size_t)b * (2 * MM + NP);
+    if (threadIdx.x < NP) q1s[threadIdx.x] = threadIdx.x < N ? p.tab_q1[(size_t)b * N + threadIdx.x] : 0.f;
+    for (int e = threadIdx.x; e < MM; e += TNT) {
+        const int i = e >> 5, j = e & 31;
+        G2[e] = (i < N && j < N) ? go[1 + N + i * N + j] : 0.f;
+        Ms[e] = sv[e];
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < MM; e += TNT) {
+        const int i = e >> 5, j = e & 31;
+        const bool ok = i < N && j < N;
+        dm[e] = q1s[i] * G2[e] * q1s[j];
+        const float hij = ok ? q2[i * N + j] * G2[e] : 0.f;
+        const float hji = ok ? q2[j * N + i] * G2[j * NP + i] : 0.f;
+        dm[MM + e] = hij + hji;
+        if (ok) p.grad_q2[((size_t)b * N + i) * N + j] = G2[e] * sv[MM + e];
+    }
+    if (threadIdx.x < NP) {
+        const int i = threadIdx.x;
+        const float g1 = i < N ? go[1 + i] : 0.f;
+        dm[2 * MM + i] = q1s[i] * g1;
+        if (i < N) {
+            float acc = g1 * sv[2 * MM + i];
+            for (int j = 0; j < N; ++j)
+                acc += G2[i * NP + j] * Ms[i * NP + j] * q1s[j] + G2[j * NP + i] * q1s[j] * Ms[j * NP + i];
+            p.grad_q1[(size_t)b * N + i] = acc;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(TNT) bwd_kernel(TP p) {
+    extern __shared__ __align__(16) float sm[];
+    const TS s = carve(sm, p.d_in);
+    const int b = blockIdx.x / p.S, sg = blockIdx.x - b * p.S;
+    const int tb = sg * p.seg, te = min(p.T, tb + p.seg);
+    const int N = p.N, d = p.d_in;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    load_common(p, s, b);
+    const float* dm = p.dmat + (size_t)b * (2 * MM + NP);
+    if (threadIdx.x < NP) {
+        s.carry[threadIdx.x] = p.spre[((size_t)b * p.S + sg) * NP + threadIdx.x];
+        s.stot[threadIdx.x] = p.save[(size_t)b * PW + 2 * MM + threadIdx.x];
+    }
+    // lane j: column j and row j of dM, row j of dG + dG^T, (Q1 G1)_j
+    float dMc[32], dMr[32], dGr[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        dMc[i] = dm[i * NP + lane];
+        dMr[i] = dm[lane * NP + i];
+        dGr[i] = dm[MM + lane * NP + i];
+    }
+    const float dsj = dm[2 * MM + lane];
+    const float xj = lane < N ? p.tab_x[(size_t)b * N + lane] : 0.f;
+    float xlog = 0.f;  // lane j: sum_t (T-1-t) dr_t[j] r_t[j]
+    // lift gradient entries (i, c) = e of this thread, e = tid + TNT m
+    const int nl = p.lift ? N * d : 0;
+    float dl[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int t0 = tb; t0 < te; t0 += TL) {
+        const int len = min(TL, te - t0);
+        __syncthreads();
+        chunk_r(p, s, b, t0, len);
+        chunk_prefix(s);
+        for (int e = threadIdx.x; e < TL * NP; e += TNT) {
+            const int i = e & 31;
+            s.Z[e] = s.stot[i] - s.P[e] - s.R[e];  // sum over the later intervals
+        }
+        __syncthreads();
+        // dr_t[j] for the warp's rows t = warp, warp + 8, ...; d(dy_t) = w_t dr_t replaces R[t] after use
+        for (int t = warp; t < len; t += TNT / 32) {
+            const float* Pt = s.P + t * NP;
+            const float* Zt = s.Z + t * NP;
+            const float* Rt = s.R + t * NP;
+            float a0 = dsj, a1 = 0.f, a2 = 0.f;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 pv = *reinterpret_cast<const float4*>(Pt + 4 * q);
+                const float4 zv = *reinterpret_cast<const float4*>(Zt + 4 * q);
+                const float4 rv = *reinterpret_cast<const float4*>(Rt + 4 * q);
+                a0 = fmaf(dMc[4 * q], pv.x, a0);
+                a1 = fmaf(dMr[4 * q], zv.x, a1);
+                a2 = fmaf(dGr[4 * q], rv.x, a2);
+                a0 = fmaf(dMc[4 * q + 1], pv.y, a0);
+                a1 = fmaf(dMr[4 * q + 1], zv.y, a1);
+                a2 = fmaf(dGr[4 * q + 1], rv.y, a2);
+                a0 = fmaf(dMc[4 * q + 2], pv.z, a0);
+                a1 = fmaf(dMr[4 * q + 2], zv.z, a1);
+                a2 = fmaf(dGr[4 * q + 2], rv.z, a2);
+                a0 = fmaf(dMc[4 * q + 3], pv.w, a0);
+                a1 = fmaf(dMr[4 * q + 3], zv.w, a1);
+                a2 = fmaf(dGr[4 * q + 3], rv.w, a2);
+            }
+            const float dr = a0 + a1 + a2;
+            const int k = p.T - 1 - (t0 + t);
+            const float rj = Rt[lane];
+            xlog = fmaf(dr * rj, (float)k, xlog);
+            __syncwarp();
+            s.R[t * NP + lane] = lane < N ? weight(xj, k) * dr : 0.f;  // d(dy_t)
+        }
+        __syncthreads();
+        // dL/d(increment) = lift^T d(dy_t): thread per (t, c)
+        for (int e = threadIdx.x; e < len * d; e += TNT) {
+            const int t = e / d, c = e - t * d;
+            float v;
+            if (p.lift) {
+                const float* gr = s.R + t * NP;
+                float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                for (int i = 0; i < NP; i += 2) {
+                    a0 = fmaf(s.liftT[c * NP + i], gr[i], a0);
+                    a1 = fmaf(s.liftT[c * NP + i + 1], gr[i + 1], a1);
+                }
+                v = a0 + a1;
+            } else {
+                v = s.R[t * NP + c];
+            }
+            p.grad_dx[((size_t)b * p.T + t0 + t) * d + c] = v;
+        }
+        // lift gradient: entry (i, c) += sum_t d(dy_t)[i] dx_t[c]
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const int e = threadIdx.x + TNT * m;
+            if (e < nl) {
+                const int i = e / d, c = e - i * d;
+                float acc = dl[m];
+                for (int t = 0; t < len; ++t) acc = fmaf(s.R[t * NP + i], s.dxs[t * d + c], acc);
+                dl[m] = acc;
+            }
+        }
+    }
+    // partials: dL/dx (lanes summed over the warps) and the lift gradient
+    __syncthreads();
+    s.tot[warp * NP + lane] = xlog;
+    __syncthreads();
+    float* bp = p.bpart + ((size_t)b * p.S + sg) * (NP + NP * d);
+    if (threadIdx.x < NP) {
+        float v = 0.f;
+        for (int w = 0; w < TNT / 32; ++w) v += s.tot[w * NP + threadIdx.x];
+        bp[threadIdx.x] = v;
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int e = threadIdx.x + TNT * m;
+        if (e < nl) bp[NP + e] = dl[m];
+    }
+}
+
+// dL/dx per sample (its segments in order) and the lift gradient (all samples and segments in order).
+__global__ void reduce_kernel(TP p) {
+    const int N = p.N, d = p.d_in;
+    const int pw = NP + NP * d;
+    const int nx = p.B * N, nl = p.lift ? N * d : 0;
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < nx + nl; e += gridDim.x * blockDim.x) {
+        if (e < nx) {
+            const int b = e / N, i = e - b * N;
+            float v = 0.f;
+            for (int sg = 0; sg < p.S; ++sg) v += p.bpart[((size_t)b * p.S + sg) * pw + i];
+            p.grad_x[e] = v;
+        } else {
+            const int o = e - nx;
+            float v = 0.f;
+            for (size_t u = 0; u < (size_t)p.B * p.S; ++u) v += p.bpart[u * pw + NP + o];
+            p.grad_lift[o] = v;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------- host side
+
+static int segments(int B, int T) {
+    int sms = 148;
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0) sms = n;
+    }
+    const int want = 4 * 3 * sms;  // about four waves of three CTAs per SM
+    const int maxS = (T + TL - 1) / TL;
+    int S = (want + B - 1) / B;
+    return S < 1 ? 1 : (S > maxS ? maxS : S);
+}
+
+static TP make_tp(const ews_diag_args* a) {
+    TP p{};
+    p.B = a->batch;
+    p.T = a->steps;
+    p.d_in = a->d_in;
+    p.N = a->dim;
+    p.flags = a->flags;
+    p.S = segments(p.B, p.T);
+    const int chunks = (p.T + TL - 1) / TL;
+    p.seg = ((chunks + p.S - 1) / p.S) * TL;
+    p.S = (p.T + p.seg - 1) / p.seg;
+    return p;
+}
+
+static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+struct TLay {
+    size_t part, save, spre, total;       // forward workspace
+    size_t dmat, bpart, btotal;           // backward workspace
+};
+
+static TLay layout(const TP& p) {
+    TLay L{};
+    size_t o = 0;
+    L.part = o;
+    o += al256(sizeof(float) * (size_t)p.B * p.S * PW);
+    L.save = o;
+    o += al256(sizeof(float) * (size_t)p.B * PW);
+    L.spre = o;
+    o += al256(sizeof(float) * (size_t)p.B * p.S * NP);
+    L.total = o;
+    o = 0;
+    L.dmat = o;
+    o += al256(sizeof(float) * (size_t)p.B * (2 * MM + NP));
+    L.bpart = o;
+    o += al256(sizeof(float) * (size_t)p.B * p.S * (NP + NP * p.d_in));
+    L.btotal = o;
+    return L;
+}
+
+}  // namespace diagterm
+
+// The closed-form terminal path applies to the uniform clock, depth 2, terminal readout, d_in <= 32 and
+// (with a lift) dim * d_in <= 1024, without a basepoint, unless EWS_F_TERMINAL_SCAN asks for the scan.
+bool diag_term_applies(const ews_diag_args* a) {
+    if (!a || a->depth != 2 || a->readout != EWS_READOUT_TERMINAL) return false;
+    if (!(a->flags & EWS_F_UNIFORM)) return false;
+    if (a->flags & (EWS_F_BASEPOINT | EWS_F_TERMINAL_SCAN | EWS_F_TEST_WITHHOLD)) return false;
+    if (a->dim > 32 || a->d_in > 32 || a->dim * a->d_in > 4 * diagterm::TNT) return false;
+    return true;
+}
+
+void diag_term_workspace(const ews_diag_args* a, size_t* fwd_bytes, size_t* bwd_bytes) {
+    const diagterm::TP p = diagterm::make_tp(a);
+    const diagterm::TLay L = diagterm::layout(p);
+    if (fwd_bytes) *fwd_bytes = L.total;
+    if (bwd_bytes) *bwd_bytes = L.btotal;
+}
+
+int diag_term_fwd(const ews_diag_args* a, cudaStream_t s) {
+    using namespace diagterm;
+    TP p = make_tp(a);
+    const TLay L = layout(p);
+    if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
+    char* ws = (char*)a->fwd_ws;
+    p.path = a->path;
+    p.lift = a->lift;
+    p.tab_x = a->tab_x;
+    p.tab_q1 = a->tab_q1;
+    p.tab_q2 = a->tab_q2;
+    p.out = a->out;
+    p.part = (float*)(ws + L.part);
+    p.save = (float*)(ws + L.save);
+    p.spre = (float*)(ws + L.spre);
+    const size_t smem = smem_bytes();
+    cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    fwd_kernel<<<p.B * p.S, TNT, smem, s>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    fin_kernel<<<p.B, TNT, 0, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+int diag_term_bwd(const ews_diag_args* a, cudaStream_t s) {
+    using namespace diagterm;
+    TP p = make_tp(a);
+    const TLay L = layout(p);
+    if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
+    if (!a->bwd_ws || a->bwd_ws_bytes < L.btotal) return EWS_ERR_WORKSPACE;
+    if (a->lift && !a->grad_lift) return EWS_ERR_INVALID_ARGUMENT;
+    char* fws = (char*)a->fwd_ws;
+    char* ws = (char*)a->bwd_ws;
+    p.path = a->path;
+    p.lift = a->lift;
+    p.tab_x = a->tab_x;
+    p.tab_q1 = a->tab_q1;
+    p.tab_q2 = a->tab_q2;
+    p.part = (float*)(fws + L.part);
+    p.save = (float*)(fws + L.save);
+    p.spre = (float*)(fws + L.spre);
+    p.grad_out = a->grad_out;
+    p.grad_dx = a->grad_dx;
+    p.grad_lift = a->grad_lift;
+    p.grad_x = a->grad_x;
+    p.grad_q1 = a->grad_q1;
+    p.grad_q2 = a->grad_q2;
+    p.dmat = (float*)(ws + L.dmat);
+    p.bpart = (float*)(ws + L.bpart);
+    prep_kernel<<<p.B, TNT, 0, s>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    const size_t smem = smem_bytes();
+    cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    bwd_kernel<<<p.B * p.S, TNT, smem, s>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    const int total = p.B * p.N + (p.lift ? p.N * p.d_in : 0);
+    reduce_kernel<<<(total + 255) / 256, 256, 0, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+}  // namespace ews

@@ -54,6 +54,8 @@ typedef struct CUstream_st* ews_stream_t; /* = cudaStream_t */
 #define EWS_F_TEST_WITHHOLD 32u /* failure-detection test: the chunk every other chunk depends on never
                                    publishes, so their bounded waits run out and the call reports
                                    EWS_ERR_LOOKBACK_TIMEOUT through ews_read_device_status */
+#define EWS_F_TERMINAL_SCAN 64u /* diagonal engine, uniform clock, terminal readout: evaluate the terminal
+                                   value with the chunked scan instead of its closed form (see below) */
 
 #define EWS_READOUT_PREFIX 0    /* out: (B, T, 1 + D), row t = [1, S_1,t, ..., S_n,t] */
 #define EWS_READOUT_TERMINAL 1  /* out: (B, 1 + D), the last row only */
@@ -78,7 +80,14 @@ typedef struct CUstream_st* ews_stream_t; /* = cudaStream_t */
  * and the series tables Q1(x_t), Q2(x_t) of order series_q (<= 8) are evaluated in the kernel for every
  * interval (tab_q1 / tab_q2 unused). The backward returns dL/dr in grad_x and dL/d(dtheta) in
  * grad_dtheta (B, T); grad_q1 / grad_q2 are unused. EWS_F_BASEPOINT does not apply: a basepoint interval
- * is an interval with dtheta = 0. */
+ * is an interval with dtheta = 0.
+ *
+ * Uniform clock with the terminal readout (no basepoint, d_in <= 32, dim * d_in <= 1024): the terminal
+ * value is evaluated in closed form, as a reweighted depth-2 signature. With r_t = exp(x (T-1-t)) dy_t,
+ *   S1_T = Q1 sum_t r_t,   S2_T = diag(Q1) M diag(Q1) + Q2 G,   M = sum_t (sum_{tau<t} r_tau) r_t^T,
+ *   G = sum_t r_t r_t^T
+ * (the reference reduces the Chen products in a tree, ews/core/chen_scan.py:218-298: the same value in
+ * another order). EWS_F_TERMINAL_SCAN selects the chunked scan instead. */
 typedef struct ews_diag_args {
     int batch;         /* B */
     int steps;         /* T: intervals per path */
