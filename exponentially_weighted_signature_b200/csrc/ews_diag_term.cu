@@ -15,6 +15,8 @@
 //
 // The backward, with G1 = dL/dS1_T and G2 = dL/dS2_T: dM = diag(Q1) G2 diag(Q1), dG = Q2 G2,
 //     dr_t = dM^T P_t + dM Z_t + (dG + dG^T) r_t + Q1 G1,    P_t = sum_{tau < t} r_tau,  Z_t = sum_{tau > t} r_tau,
+// and since P_t + r_t + Z_t = s,  dr_t = (dM^T - dM) P_t + (dG + dG^T - dM) r_t + dM s + Q1 G1: two
+// matrix-vector products per interval,
 //     d(dy_t) = w_t dr_t,   dL/dx += sum_t (T-1-t) dr_t r_t,   dL/dQ2 = G2 G,
 //     dL/dQ1_i = sum_j G2_ij M_ij Q1_j + G2_ji Q1_j M_ji + G1_i s_i   (s = sum_t r_t).
 //
@@ -56,13 +58,13 @@ struct TP {
     float* grad_x;
     float* grad_q1;
     float* grad_q2;
-    float* dmat;   // (B, 2 MM + NP): dM | dG + dG^T | Q1 G1
+    float* dmat;   // (B, 2 MM + NP): A1 = dM^T - dM | A2 = dG + dG^T - dM | c = dM s + Q1 G1 (rows j)
     float* bpart;  // (B, S, NP + NP d_in): dL/dx partial | lift-gradient partial
 };
 
 // Shared-memory layout shared by both directions (floats).
 struct TS {
-    float *liftT, *xs, *dxs, *R, *P, *Z, *tot, *carry, *stot;
+    float *liftT, *xs, *dxs, *R, *P, *tot, *carry;
 };
 
 __device__ __forceinline__ TS carve(float* sm, int d_in) {
@@ -70,17 +72,15 @@ __device__ __forceinline__ TS carve(float* sm, int d_in) {
     float* q = sm;
     s.R = q; q += TL * NP;
     s.P = q; q += TL * NP;
-    s.Z = q; q += TL * NP;
     s.liftT = q; q += 32 * NP;
     s.dxs = q; q += TL * 32;
     s.xs = q; q += NP;
     s.tot = q; q += 8 * NP;
     s.carry = q; q += NP;
-    s.stot = q; q += NP;
     return s;
 }
 
-__host__ __device__ inline size_t smem_bytes() { return sizeof(float) * (3 * TL * NP + 32 * NP + TL * 32 + 11 * NP); }
+__host__ __device__ inline size_t smem_bytes() { return sizeof(float) * (2 * TL * NP + 32 * NP + TL * 32 + 10 * NP); }
 
 // w = exp(x k) for an integer k >= 0: x k = hi + lo exactly, exp(hi) (1 + lo).
 __device__ __forceinline__ float weight(float x, int k) {
@@ -245,9 +245,9 @@ __global__ void __launch_bounds__(TNT) fin_kernel(TP p) {
 
 // ---------------------------------------------------------------------------------- backward
 
-// Per sample: the cotangent matrices of M, G and s, and the table gradients dL/dQ1, dL/dQ2.
+// Per sample: the coefficients of dr_t (A1, A2, c) and the table gradients dL/dQ1, dL/dQ2.
 __global__ void __launch_bounds__(TNT) prep_kernel(TP p) {
-    __shared__ float G2[MM], Ms[MM], q1s[NP];
+    __shared__ float G2[MM], Ms[MM], dMs[MM], q1s[NP];
     const int b = blockIdx.x, N = p.N, W = 1 + N + N * N;
     const float* go = p.grad_out + (size_t)b * W;
     const float* sv = p.save + (size_t)b * PW;
@@ -262,17 +262,25 @@ __global__ void __launch_bounds__(TNT) prep_kernel(TP p) {
     __syncthreads();
     for (int e = threadIdx.x; e < MM; e += TNT) {
         const int i = e >> 5, j = e & 31;
+        dMs[e] = q1s[i] * G2[e] * q1s[j];
+    }
+    __syncthreads();
+    // entry e = (j, i) of the rows-j layout
+    for (int e = threadIdx.x; e < MM; e += TNT) {
+        const int j = e >> 5, i = e & 31;
         const bool ok = i < N && j < N;
-        dm[e] = q1s[i] * G2[e] * q1s[j];
-        const float hij = ok ? q2[i * N + j] * G2[e] : 0.f;
         const float hji = ok ? q2[j * N + i] * G2[j * NP + i] : 0.f;
-        dm[MM + e] = hij + hji;
-        if (ok) p.grad_q2[((size_t)b * N + i) * N + j] = G2[e] * sv[MM + e];
+        const float hij = ok ? q2[i * N + j] * G2[i * NP + j] : 0.f;
+        dm[e] = dMs[i * NP + j] - dMs[j * NP + i];
+        dm[MM + e] = hji + hij - dMs[j * NP + i];
+        if (ok) p.grad_q2[((size_t)b * N + j) * N + i] = G2[j * NP + i] * sv[MM + j * NP + i];
     }
     if (threadIdx.x < NP) {
         const int i = threadIdx.x;
         const float g1 = i < N ? go[1 + i] : 0.f;
-        dm[2 * MM + i] = q1s[i] * g1;
+        float cs = q1s[i] * g1;
+        for (int k = 0; k < NP; ++k) cs = fmaf(dMs[i * NP + k], sv[2 * MM + k], cs);
+        dm[2 * MM + i] = cs;
         if (i < N) {
             float acc = g1 * sv[2 * MM + i];
             for (int j = 0; j < N; ++j)
@@ -282,7 +290,7 @@ __global__ void __launch_bounds__(TNT) prep_kernel(TP p) {
     }
 }
 
-__global__ void __launch_bounds__(TNT) bwd_kernel(TP p) {
+__global__ void __launch_bounds__(TNT, 2) bwd_kernel(TP p) {
     extern __shared__ __align__(16) float sm[];
     const TS s = carve(sm, p.d_in);
     const int b = blockIdx.x / p.S, sg = blockIdx.x - b * p.S;
@@ -291,19 +299,15 @@ __global__ void __launch_bounds__(TNT) bwd_kernel(TP p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     load_common(p, s, b);
     const float* dm = p.dmat + (size_t)b * (2 * MM + NP);
-    if (threadIdx.x < NP) {
-        s.carry[threadIdx.x] = p.spre[((size_t)b * p.S + sg) * NP + threadIdx.x];
-        s.stot[threadIdx.x] = p.save[(size_t)b * PW + 2 * MM + threadIdx.x];
-    }
-    // lane j: column j and row j of dM, row j of dG + dG^T, (Q1 G1)_j
-    float dMc[32], dMr[32], dGr[32];
+    if (threadIdx.x < NP) s.carry[threadIdx.x] = p.spre[((size_t)b * p.S + sg) * NP + threadIdx.x];
+    // lane j: row j of A1 and of A2, and c_j
+    float A1[32], A2[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        dMc[i] = dm[i * NP + lane];
-        dMr[i] = dm[lane * NP + i];
-        dGr[i] = dm[MM + lane * NP + i];
+        A1[i] = dm[lane * NP + i];
+        A2[i] = dm[MM + lane * NP + i];
     }
-    const float dsj = dm[2 * MM + lane];
+    const float cj = dm[2 * MM + lane];
     const float xj = lane < N ? p.tab_x[(size_t)b * N + lane] : 0.f;
     float xlog = 0.f;  // lane j: sum_t (T-1-t) dr_t[j] r_t[j]
     // lift gradient entries (i, c) = e of this thread, e = tid + TNT m
@@ -314,36 +318,25 @@ __global__ void __launch_bounds__(TNT) bwd_kernel(TP p) {
         __syncthreads();
         chunk_r(p, s, b, t0, len);
         chunk_prefix(s);
-        for (int e = threadIdx.x; e < TL * NP; e += TNT) {
-            const int i = e & 31;
-            s.Z[e] = s.stot[i] - s.P[e] - s.R[e];  // sum over the later intervals
-        }
-        __syncthreads();
         // dr_t[j] for the warp's rows t = warp, warp + 8, ...; d(dy_t) = w_t dr_t replaces R[t] after use
         for (int t = warp; t < len; t += TNT / 32) {
             const float* Pt = s.P + t * NP;
-            const float* Zt = s.Z + t * NP;
             const float* Rt = s.R + t * NP;
-            float a0 = dsj, a1 = 0.f, a2 = 0.f;
+            float a0 = cj, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 const float4 pv = *reinterpret_cast<const float4*>(Pt + 4 * q);
-                const float4 zv = *reinterpret_cast<const float4*>(Zt + 4 * q);
                 const float4 rv = *reinterpret_cast<const float4*>(Rt + 4 * q);
-                a0 = fmaf(dMc[4 * q], pv.x, a0);
-                a1 = fmaf(dMr[4 * q], zv.x, a1);
-                a2 = fmaf(dGr[4 * q], rv.x, a2);
-                a0 = fmaf(dMc[4 * q + 1], pv.y, a0);
-                a1 = fmaf(dMr[4 * q + 1], zv.y, a1);
-                a2 = fmaf(dGr[4 * q + 1], rv.y, a2);
-                a0 = fmaf(dMc[4 * q + 2], pv.z, a0);
-                a1 = fmaf(dMr[4 * q + 2], zv.z, a1);
-                a2 = fmaf(dGr[4 * q + 2], rv.z, a2);
-                a0 = fmaf(dMc[4 * q + 3], pv.w, a0);
-                a1 = fmaf(dMr[4 * q + 3], zv.w, a1);
-                a2 = fmaf(dGr[4 * q + 3], rv.w, a2);
+                a0 = fmaf(A1[4 * q], pv.x, a0);
+                a1 = fmaf(A2[4 * q], rv.x, a1);
+                a2 = fmaf(A1[4 * q + 1], pv.y, a2);
+                a3 = fmaf(A2[4 * q + 1], rv.y, a3);
+                a0 = fmaf(A1[4 * q + 2], pv.z, a0);
+                a1 = fmaf(A2[4 * q + 2], rv.z, a1);
+                a2 = fmaf(A1[4 * q + 3], pv.w, a2);
+                a3 = fmaf(A2[4 * q + 3], rv.w, a3);
             }
-            const float dr = a0 + a1 + a2;
+            const float dr = (a0 + a1) + (a2 + a3);
             const int k = p.T - 1 - (t0 + t);
             const float rj = Rt[lane];
             xlog = fmaf(dr * rj, (float)k, xlog);
