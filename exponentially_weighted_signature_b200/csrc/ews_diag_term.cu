@@ -64,7 +64,7 @@ struct TP {
 
 // Shared-memory layout shared by both directions (floats).
 struct TS {
-    float *liftT, *xs, *dxs, *R, *P, *tot, *carry;
+    float *liftT, *liftR, *xs, *dxs, *R, *P, *tot, *carry;
 };
 
 __device__ __forceinline__ TS carve(float* sm, int d_in) {
@@ -72,7 +72,8 @@ __device__ __forceinline__ TS carve(float* sm, int d_in) {
     float* q = sm;
     s.R = q; q += TL * NP;
     s.P = q; q += TL * NP;
-    s.liftT = q; q += 32 * NP;
+    s.liftT = q; q += 32 * NP;   // lift^T: liftT[c NP + i]
+    s.liftR = q; q += NP * 33;   // lift:   liftR[i 33 + c]
     s.dxs = q; q += TL * 32;
     s.xs = q; q += NP;
     s.tot = q; q += 8 * NP;
@@ -80,7 +81,7 @@ __device__ __forceinline__ TS carve(float* sm, int d_in) {
     return s;
 }
 
-__host__ __device__ inline size_t smem_bytes() { return sizeof(float) * (2 * TL * NP + 32 * NP + TL * 32 + 10 * NP); }
+__host__ __device__ inline size_t smem_bytes() { return sizeof(float) * (2 * TL * NP + 32 * NP + 33 * NP + TL * 32 + 10 * NP); }
 
 // w = exp(x k) for an integer k >= 0: x k = hi + lo exactly, exp(hi) (1 + lo).
 __device__ __forceinline__ float weight(float x, int k) {
@@ -151,7 +152,9 @@ __device__ void load_common(const TP& p, const TS& s, int b) {
     const int d = p.d_in, N = p.N;
     for (int e = threadIdx.x; e < 32 * NP; e += TNT) {
         const int c = e >> 5, i = e & 31;
-        s.liftT[e] = (p.lift && c < d && i < N) ? p.lift[i * d + c] : 0.f;
+        const float v = (p.lift && c < d && i < N) ? p.lift[i * d + c] : 0.f;
+        s.liftT[e] = v;
+        s.liftR[i * 33 + c] = v;
     }
     if (threadIdx.x < NP) s.xs[threadIdx.x] = threadIdx.x < N ? p.tab_x[(size_t)b * N + threadIdx.x] : 0.f;
 }
@@ -165,37 +168,53 @@ __global__ void __launch_bounds__(TNT) fwd_kernel(TP p) {
     const int tb = sg * p.seg, te = min(p.T, tb + p.seg);
     load_common(p, s, b);
     if (threadIdx.x < NP) s.carry[threadIdx.x] = 0.f;
-    // thread (a, q): a < 32 accumulates row a of M, a >= 32 row a - 32 of G; columns 8 q .. 8 q + 7
-    const int a = threadIdx.x >> 2, j0 = 8 * (threadIdx.x & 3);
-    const bool mrow = a < 32;
-    const float* Arow = mrow ? s.P + a : s.R + (a - 32);
-    float acc[8];
+    // [M; G] (64 x 32) in 4 x 4 blocks: thread (h, rb, cb) owns rows 4 rb (M for rb < 8, G beyond) and
+    // columns 4 cb over the chunk rows k of half h; the halves are added at the end
+    const int h = threadIdx.x >> 7, u = threadIdx.x & 127;
+    const int a0 = 4 * (u >> 3), j0 = 4 * (u & 7);
+    const float* Abase = a0 < 32 ? s.P + a0 : s.R + (a0 - 32);
+    float acc[4][4];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = 0.f;
     for (int t0 = tb; t0 < te; t0 += TL) {
         const int len = min(TL, te - t0);
         __syncthreads();
         chunk_r(p, s, b, t0, len);
         chunk_prefix(s);
-        for (int k = 0; k < len; ++k) {
-            const float av = Arow[k * NP];
-            const float4 b0 = *reinterpret_cast<const float4*>(s.R + k * NP + j0);
-            const float4 b1 = *reinterpret_cast<const float4*>(s.R + k * NP + j0 + 4);
-            acc[0] = fmaf(av, b0.x, acc[0]);
-            acc[1] = fmaf(av, b0.y, acc[1]);
-            acc[2] = fmaf(av, b0.z, acc[2]);
-            acc[3] = fmaf(av, b0.w, acc[3]);
-            acc[4] = fmaf(av, b1.x, acc[4]);
-            acc[5] = fmaf(av, b1.y, acc[5]);
-            acc[6] = fmaf(av, b1.z, acc[6]);
-            acc[7] = fmaf(av, b1.w, acc[7]);
+        const int k1 = min(len, (h + 1) * (TL / 2));
+#pragma unroll 4
+        for (int k = h * (TL / 2); k < k1; ++k) {
+            const float4 av = *reinterpret_cast<const float4*>(Abase + k * NP);
+            const float4 bv = *reinterpret_cast<const float4*>(s.R + k * NP + j0);
+            const float ar[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                acc[r][0] = fmaf(ar[r], bv.x, acc[r][0]);
+                acc[r][1] = fmaf(ar[r], bv.y, acc[r][1]);
+                acc[r][2] = fmaf(ar[r], bv.z, acc[r][2]);
+                acc[r][3] = fmaf(ar[r], bv.w, acc[r][3]);
+            }
         }
     }
-    float* pp = p.part + ((size_t)b * p.S + sg) * PW;
-    float* dst = pp + (mrow ? a * NP : MM + (a - 32) * NP) + j0;
-    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
     __syncthreads();
+    float* red = s.P;  // the second half's blocks, then added by the first half
+    if (h == 1)
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            *reinterpret_cast<float4*>(red + (a0 + r) * NP + j0) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    __syncthreads();
+    float* pp = p.part + ((size_t)b * p.S + sg) * PW;
+    if (h == 0) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float4 o = *reinterpret_cast<const float4*>(red + (a0 + r) * NP + j0);
+            const int a = a0 + r;
+            float* dst = pp + (a < 32 ? a * NP : MM + (a - 32) * NP) + j0;
+            *reinterpret_cast<float4*>(dst) = make_float4(acc[r][0] + o.x, acc[r][1] + o.y, acc[r][2] + o.z, acc[r][3] + o.w);
+        }
+    }
     if (threadIdx.x < NP) pp[2 * MM + threadIdx.x] = s.carry[threadIdx.x];
 }
 
@@ -318,30 +337,47 @@ __global__ void __launch_bounds__(TNT, 2) bwd_kernel(TP p) {
         __syncthreads();
         chunk_r(p, s, b, t0, len);
         chunk_prefix(s);
-        // dr_t[j] for the warp's rows t = warp, warp + 8, ...; d(dy_t) = w_t dr_t replaces R[t] after use
-        for (int t = warp; t < len; t += TNT / 32) {
-            const float* Pt = s.P + t * NP;
-            const float* Rt = s.R + t * NP;
-            float a0 = cj, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        // dr_t[j] for the warp's rows t = warp, warp + 8, ..., two rows at a time; d(dy_t) = w_t dr_t replaces
+        // R[t] after use
+        for (int t = warp; t < len; t += 2 * (TNT / 32)) {
+            const int t2 = t + TNT / 32;
+            const bool two = t2 < len;
+            const int u2 = two ? t2 : t;
+            float x0 = cj, x1 = 0.f, x2 = 0.f, x3 = 0.f, y0 = cj, y1 = 0.f, y2 = 0.f, y3 = 0.f;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-                const float4 pv = *reinterpret_cast<const float4*>(Pt + 4 * q);
-                const float4 rv = *reinterpret_cast<const float4*>(Rt + 4 * q);
-                a0 = fmaf(A1[4 * q], pv.x, a0);
-                a1 = fmaf(A2[4 * q], rv.x, a1);
-                a2 = fmaf(A1[4 * q + 1], pv.y, a2);
-                a3 = fmaf(A2[4 * q + 1], rv.y, a3);
-                a0 = fmaf(A1[4 * q + 2], pv.z, a0);
-                a1 = fmaf(A2[4 * q + 2], rv.z, a1);
-                a2 = fmaf(A1[4 * q + 3], pv.w, a2);
-                a3 = fmaf(A2[4 * q + 3], rv.w, a3);
+                const float4 pv = *reinterpret_cast<const float4*>(s.P + t * NP + 4 * q);
+                const float4 rv = *reinterpret_cast<const float4*>(s.R + t * NP + 4 * q);
+                const float4 pw = *reinterpret_cast<const float4*>(s.P + u2 * NP + 4 * q);
+                const float4 rw = *reinterpret_cast<const float4*>(s.R + u2 * NP + 4 * q);
+                x0 = fmaf(A1[4 * q], pv.x, x0);
+                x1 = fmaf(A2[4 * q], rv.x, x1);
+                y0 = fmaf(A1[4 * q], pw.x, y0);
+                y1 = fmaf(A2[4 * q], rw.x, y1);
+                x2 = fmaf(A1[4 * q + 1], pv.y, x2);
+                x3 = fmaf(A2[4 * q + 1], rv.y, x3);
+                y2 = fmaf(A1[4 * q + 1], pw.y, y2);
+                y3 = fmaf(A2[4 * q + 1], rw.y, y3);
+                x0 = fmaf(A1[4 * q + 2], pv.z, x0);
+                x1 = fmaf(A2[4 * q + 2], rv.z, x1);
+                y0 = fmaf(A1[4 * q + 2], pw.z, y0);
+                y1 = fmaf(A2[4 * q + 2], rw.z, y1);
+                x2 = fmaf(A1[4 * q + 3], pv.w, x2);
+                x3 = fmaf(A2[4 * q + 3], rv.w, x3);
+                y2 = fmaf(A1[4 * q + 3], pw.w, y2);
+                y3 = fmaf(A2[4 * q + 3], rw.w, y3);
             }
-            const float dr = (a0 + a1) + (a2 + a3);
+            const float dr = (x0 + x1) + (x2 + x3);
+            const float dr2 = (y0 + y1) + (y2 + y3);
             const int k = p.T - 1 - (t0 + t);
-            const float rj = Rt[lane];
+            const int k2 = p.T - 1 - (t0 + u2);
+            const float rj = s.R[t * NP + lane];
+            const float rj2 = s.R[u2 * NP + lane];
             xlog = fmaf(dr * rj, (float)k, xlog);
+            if (two) xlog = fmaf(dr2 * rj2, (float)k2, xlog);
             __syncwarp();
             s.R[t * NP + lane] = lane < N ? weight(xj, k) * dr : 0.f;  // d(dy_t)
+            if (two) s.R[t2 * NP + lane] = lane < N ? weight(xj, k2) * dr2 : 0.f;
         }
         __syncthreads();
         // dL/d(increment) = lift^T d(dy_t): thread per (t, c)
@@ -353,8 +389,8 @@ __global__ void __launch_bounds__(TNT, 2) bwd_kernel(TP p) {
                 float a0 = 0.f, a1 = 0.f;
 #pragma unroll
                 for (int i = 0; i < NP; i += 2) {
-                    a0 = fmaf(s.liftT[c * NP + i], gr[i], a0);
-                    a1 = fmaf(s.liftT[c * NP + i + 1], gr[i + 1], a1);
+                    a0 = fmaf(s.liftR[i * 33 + c], gr[i], a0);
+                    a1 = fmaf(s.liftR[(i + 1) * 33 + c], gr[i + 1], a1);
                 }
                 v = a0 + a1;
             } else {
