@@ -39,6 +39,8 @@ constexpr int MM = NP * NP;
 constexpr int TL = 128;  // intervals per chunk
 constexpr int TNT = 256; // threads per CTA
 constexpr int PW = 2 * MM + NP;  // per-segment partial: M | G | s
+constexpr int LTS = NP + 4;      // row stride of lift^T in shared memory (float4 rows, 2-way banks at most)
+constexpr int XTS = TL + 4;      // row stride of the channel-major increments
 
 struct TP {
     int B, T, d_in, N, S, seg;  // S segments of `seg` intervals per sample
@@ -64,7 +66,7 @@ struct TP {
 
 // Shared-memory layout shared by both directions (floats).
 struct TS {
-    float *liftT, *liftR, *xs, *dxs, *R, *P, *tot, *carry;
+    float *liftT, *xs, *dxs, *R, *P, *tot, *carry;
 };
 
 __device__ __forceinline__ TS carve(float* sm, int d_in) {
@@ -72,16 +74,15 @@ __device__ __forceinline__ TS carve(float* sm, int d_in) {
     float* q = sm;
     s.R = q; q += TL * NP;
     s.P = q; q += TL * NP;
-    s.liftT = q; q += 32 * NP;   // lift^T: liftT[c NP + i]
-    s.liftR = q; q += NP * 33;   // lift:   liftR[i 33 + c]
-    s.dxs = q; q += TL * 32;
+    s.liftT = q; q += 32 * LTS;  // lift^T: liftT[c LTS + i]
+    s.dxs = q; q += 32 * XTS;    // increments, channel-major: dxs[c XTS + t]
     s.xs = q; q += NP;
     s.tot = q; q += 8 * NP;
     s.carry = q; q += NP;
     return s;
 }
 
-__host__ __device__ inline size_t smem_bytes() { return sizeof(float) * (2 * TL * NP + 32 * NP + 33 * NP + TL * 32 + 10 * NP); }
+__host__ __device__ inline size_t smem_bytes() { return sizeof(float) * (2 * TL * NP + 32 * LTS + 32 * XTS + 10 * NP); }
 
 // w = exp(x k) for an integer k >= 0: x k = hi + lo exactly, exp(hi) (1 + lo).
 __device__ __forceinline__ float weight(float x, int k) {
@@ -91,36 +92,43 @@ __device__ __forceinline__ float weight(float x, int k) {
     return expf(hi) * (1.f + lo);
 }
 
-// The chunk's increments into dxs[t * d_in + c], then r_t = w_t (lift dx_t) into R (rows t < len; zeros
-// beyond, and in the padded columns).
+// The chunk's increments into dxs[c XTS + t] (channel-major), then r_t = w_t (lift dx_t) into R (rows
+// t < len; zeros beyond, and in the padded columns). Thread (g, i) forms rows 4 g + 32 m .. + 3 of column
+// i: one lift entry and one float4 of increments per 4 FMAs.
 __device__ void chunk_r(const TP& p, const TS& s, int b, int t0, int len) {
     const int d = p.d_in, N = p.N;
     for (int e = threadIdx.x; e < TL * d; e += TNT) {
-        const int t = e / d, c = e - t * d;
-        s.dxs[e] = t < len ? input_increment(p.path, b, t0 + t, c, p.T, d, p.flags) : 0.f;
+        const int c = e / TL, t = e - c * TL;
+        s.dxs[c * XTS + t] = t < len ? input_increment(p.path, b, t0 + t, c, p.T, d, p.flags) : 0.f;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < TL * NP; e += TNT) {
-        const int t = e >> 5, i = e & 31;
-        float r = 0.f;
-        if (t < len && i < N) {
-            float dy;
-            if (p.lift) {
-                const float* xr = s.dxs + t * d;
-                float a0 = 0.f, a1 = 0.f;
-                int c = 0;
-                for (; c + 1 < d; c += 2) {
-                    a0 = fmaf(s.liftT[c * NP + i], xr[c], a0);
-                    a1 = fmaf(s.liftT[(c + 1) * NP + i], xr[c + 1], a1);
-                }
-                if (c < d) a0 = fmaf(s.liftT[c * NP + i], xr[c], a0);
-                dy = a0 + a1;
-            } else {
-                dy = s.dxs[t * d + i];
+    const int g = threadIdx.x >> 5, i = threadIdx.x & 31;
+    const float xi = s.xs[i];
+#pragma unroll
+    for (int m = 0; m < TL / 32; ++m) {
+        const int tb = 4 * g + 32 * m;
+        float dy[4] = {0.f, 0.f, 0.f, 0.f};
+        if (p.lift) {
+            for (int c = 0; c < d; ++c) {
+                const float l = s.liftT[c * LTS + i];
+                const float4 x = *reinterpret_cast<const float4*>(s.dxs + c * XTS + tb);
+                dy[0] = fmaf(l, x.x, dy[0]);
+                dy[1] = fmaf(l, x.y, dy[1]);
+                dy[2] = fmaf(l, x.z, dy[2]);
+                dy[3] = fmaf(l, x.w, dy[3]);
             }
-            r = weight(s.xs[i], p.T - 1 - (t0 + t)) * dy;
+        } else if (i < d) {
+            const float4 x = *reinterpret_cast<const float4*>(s.dxs + i * XTS + tb);
+            dy[0] = x.x;
+            dy[1] = x.y;
+            dy[2] = x.z;
+            dy[3] = x.w;
         }
-        s.R[e] = r;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int t = tb + u;
+            s.R[t * NP + i] = (t < len && i < N) ? weight(xi, p.T - 1 - (t0 + t)) * dy[u] : 0.f;
+        }
     }
     __syncthreads();
 }
@@ -152,9 +160,7 @@ __device__ void load_common(const TP& p, const TS& s, int b) {
     const int d = p.d_in, N = p.N;
     for (int e = threadIdx.x; e < 32 * NP; e += TNT) {
         const int c = e >> 5, i = e & 31;
-        const float v = (p.lift && c < d && i < N) ? p.lift[i * d + c] : 0.f;
-        s.liftT[e] = v;
-        s.liftR[i * 33 + c] = v;
+        s.liftT[c * LTS + i] = (p.lift && c < d && i < N) ? p.lift[i * d + c] : 0.f;
     }
     if (threadIdx.x < NP) s.xs[threadIdx.x] = threadIdx.x < N ? p.tab_x[(size_t)b * N + threadIdx.x] : 0.f;
 }
@@ -329,9 +335,11 @@ __global__ void __launch_bounds__(TNT, 2) bwd_kernel(TP p) {
     const float cj = dm[2 * MM + lane];
     const float xj = lane < N ? p.tab_x[(size_t)b * N + lane] : 0.f;
     float xlog = 0.f;  // lane j: sum_t (T-1-t) dr_t[j] r_t[j]
-    // lift gradient entries (i, c) = e of this thread, e = tid + TNT m
+    // lift gradient: thread tid = (lh, liq, lc) of 2 x 8 x 16 owns entries (4 liq + u, lc) for chunk rows in
+    // half lh (d_in <= 16 here; larger d_in loops over channel groups below)
     const int nl = p.lift ? N * d : 0;
-    float dl[4] = {0.f, 0.f, 0.f, 0.f};
+    const int lh = threadIdx.x >> 7, liq = (threadIdx.x >> 4) & 7, lc0 = threadIdx.x & 15;
+    float dlg[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     for (int t0 = tb; t0 < te; t0 += TL) {
         const int len = min(TL, te - t0);
         __syncthreads();
@@ -380,17 +388,22 @@ __global__ void __launch_bounds__(TNT, 2) bwd_kernel(TP p) {
             if (two) s.R[t2 * NP + lane] = lane < N ? weight(xj, k2) * dr2 : 0.f;
         }
         __syncthreads();
-        // dL/d(increment) = lift^T d(dy_t): thread per (t, c)
+        // dL/d(increment) = lift^T d(dy_t): thread per (t, c), rows of d(dy_t) and of lift^T as float4
         for (int e = threadIdx.x; e < len * d; e += TNT) {
             const int t = e / d, c = e - t * d;
             float v;
             if (p.lift) {
                 const float* gr = s.R + t * NP;
+                const float* lr = s.liftT + c * LTS;
                 float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-                for (int i = 0; i < NP; i += 2) {
-                    a0 = fmaf(s.liftR[i * 33 + c], gr[i], a0);
-                    a1 = fmaf(s.liftR[(i + 1) * 33 + c], gr[i + 1], a1);
+                for (int i = 0; i < NP; i += 4) {
+                    const float4 gv = *reinterpret_cast<const float4*>(gr + i);
+                    const float4 lv = *reinterpret_cast<const float4*>(lr + i);
+                    a0 = fmaf(lv.x, gv.x, a0);
+                    a1 = fmaf(lv.y, gv.y, a1);
+                    a0 = fmaf(lv.z, gv.z, a0);
+                    a1 = fmaf(lv.w, gv.w, a1);
                 }
                 v = a0 + a1;
             } else {
@@ -398,15 +411,22 @@ __global__ void __launch_bounds__(TNT, 2) bwd_kernel(TP p) {
             }
             p.grad_dx[((size_t)b * p.T + t0 + t) * d + c] = v;
         }
-        // lift gradient: entry (i, c) += sum_t d(dy_t)[i] dx_t[c]
+        // lift gradient: thread (h, iq, c) accumulates entries (4 iq .. 4 iq + 3, c) over the chunk rows of
+        // half h: one float4 of d(dy_t) and one increment per 4 FMAs
+        if (nl) {
+            const int t1 = min(len, (lh + 1) * (TL / 2));
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            const int e = threadIdx.x + TNT * m;
-            if (e < nl) {
-                const int i = e / d, c = e - i * d;
-                float acc = dl[m];
-                for (int t = 0; t < len; ++t) acc = fmaf(s.R[t * NP + i], s.dxs[t * d + c], acc);
-                dl[m] = acc;
+            for (int cg = 0; cg < 2; ++cg) {
+                const int c = lc0 + 16 * cg;
+                if (c < d)
+                    for (int t = lh * (TL / 2); t < t1; ++t) {
+                        const float4 gv = *reinterpret_cast<const float4*>(s.R + t * NP + 4 * liq);
+                        const float xv = s.dxs[c * XTS + t];
+                        dlg[cg][0] = fmaf(gv.x, xv, dlg[cg][0]);
+                        dlg[cg][1] = fmaf(gv.y, xv, dlg[cg][1]);
+                        dlg[cg][2] = fmaf(gv.z, xv, dlg[cg][2]);
+                        dlg[cg][3] = fmaf(gv.w, xv, dlg[cg][3]);
+                    }
             }
         }
     }
@@ -420,10 +440,24 @@ __global__ void __launch_bounds__(TNT, 2) bwd_kernel(TP p) {
         for (int w = 0; w < TNT / 32; ++w) v += s.tot[w * NP + threadIdx.x];
         bp[threadIdx.x] = v;
     }
+    if (nl) {
+        // the two halves' lift-gradient blocks, added in order
+        float* red = s.P;
+        __syncthreads();
+        if (lh == 1)
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        const int e = threadIdx.x + TNT * m;
-        if (e < nl) bp[NP + e] = dl[m];
+            for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+                for (int u = 0; u < 4; ++u) red[(4 * liq + u) * NP + lc0 + 16 * cg] = dlg[cg][u];
+        __syncthreads();
+        if (lh == 0)
+#pragma unroll
+            for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int i = 4 * liq + u, c = lc0 + 16 * cg;
+                    if (i < N && c < d) bp[NP + i * d + c] = dlg[cg][u] + red[i * NP + c];
+                }
     }
 }
 
