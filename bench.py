@@ -31,8 +31,10 @@ sys.path.insert(0, ROOT)
 METRIC = "EWS fwd+bwd (batch·steps)/s at 1/2/4/8 B200, % HBM/TC roofline vs JAX CPU"
 UNIT = "batch·steps/s"
 L2_BYTES = 126 * 1024 * 1024
-KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 2, "ews_dense_bwd": 2,
-                    "ews_block_fwd": 1, "ews_block_bwd": 2}
+# kernels each library call launches (the diagonal engine's closed-form terminal path: fwd 2, bwd 4)
+KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 3, "ews_dense_bwd": 3,
+                    "ews_block_fwd": 1, "ews_block_bwd": 2, "ews_expm": 1, "ews_expm_adjoint": 1}
+TERMINAL_KERNELS = {"ews_diag_fwd": 2, "ews_diag_bwd": 4}
 
 
 def _peaks():
@@ -527,7 +529,10 @@ def run_b200(args, rank, world, local_rank):
         d[0] += e0.elapsed_time(e1)
         d[1] += 1
         d[2] = units
-    launches = sum(KERNELS_PER_CALL.get(n, 1) * v[1] for n, v in per.items())
+    counts = dict(KERNELS_PER_CALL)
+    if setup["meta"].get("readout") == "terminal":
+        counts.update(TERMINAL_KERNELS)
+    launches = sum(counts.get(n, 1) * v[1] for n, v in per.items())
     dom = max(per.items(), key=lambda kv: kv[1][0])
     dom_name, (dom_ms, dom_n, dom_units) = dom
     avg_s = dom_ms / dom_n / 1e3

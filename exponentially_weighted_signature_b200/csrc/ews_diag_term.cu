@@ -461,24 +461,31 @@ __global__ void __launch_bounds__(TNT, 2) bwd_kernel(TP p) {
     }
 }
 
-// dL/dx per sample (its segments in order) and the lift gradient (all samples and segments in order).
-__global__ void reduce_kernel(TP p) {
-    const int N = p.N, d = p.d_in;
-    const int pw = NP + NP * d;
-    const int nx = p.B * N, nl = p.lift ? N * d : 0;
-    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < nx + nl; e += gridDim.x * blockDim.x) {
-        if (e < nx) {
-            const int b = e / N, i = e - b * N;
-            float v = 0.f;
-            for (int sg = 0; sg < p.S; ++sg) v += p.bpart[((size_t)b * p.S + sg) * pw + i];
-            p.grad_x[e] = v;
-        } else {
-            const int o = e - nx;
-            float v = 0.f;
-            for (size_t u = 0; u < (size_t)p.B * p.S; ++u) v += p.bpart[u * pw + NP + o];
-            p.grad_lift[o] = v;
-        }
+// dL/dx per sample (its segments in order): one thread per entry.
+__global__ void reduce_x_kernel(TP p) {
+    const int N = p.N, pw = NP + NP * p.d_in;
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= p.B * N) return;
+    const int b = e / N, i = e - b * N;
+    float v = 0.f;
+    for (int sg = 0; sg < p.S; ++sg) v += p.bpart[((size_t)b * p.S + sg) * pw + i];
+    p.grad_x[e] = v;
+}
+
+// The lift gradient: one CTA per entry, a fixed-order tree over all (sample, segment) partials.
+__global__ void __launch_bounds__(TNT) reduce_lift_kernel(TP p) {
+    __shared__ float red[TNT];
+    const int pw = NP + NP * p.d_in, o = blockIdx.x;
+    const size_t n = (size_t)p.B * p.S;
+    float v = 0.f;
+    for (size_t u = threadIdx.x; u < n; u += TNT) v += p.bpart[u * pw + NP + o];
+    red[threadIdx.x] = v;
+    __syncthreads();
+    for (int w = TNT / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+        __syncthreads();
     }
+    if (threadIdx.x == 0) p.grad_lift[o] = red[0];
 }
 
 // ---------------------------------------------------------------------------------- host side
@@ -610,8 +617,9 @@ int diag_term_bwd(const ews_diag_args* a, cudaStream_t s) {
     cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     bwd_kernel<<<p.B * p.S, TNT, smem, s>>>(p);
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
-    const int total = p.B * p.N + (p.lift ? p.N * p.d_in : 0);
-    reduce_kernel<<<(total + 255) / 256, 256, 0, s>>>(p);
+    reduce_x_kernel<<<(p.B * p.N + 255) / 256, 256, 0, s>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    if (p.lift) reduce_lift_kernel<<<p.N * p.d_in, TNT, 0, s>>>(p);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 

@@ -138,7 +138,8 @@ class Expm(torch.autograd.Function):
         out = torch.empty_like(Xc)
         n = Xc.shape[-1]
         batch = Xc.numel() // (n * n) if n else 0
-        _lib.check(_lib.load().ews_expm_batched(_ptr(Xc), _ptr(out), batch, n, _stream_ptr(Xc.device)), "ews_expm_batched")
+        with _timed("ews_expm", Xc.device, batch):
+            _lib.check(_lib.load().ews_expm_batched(_ptr(Xc), _ptr(out), batch, n, _stream_ptr(Xc.device)), "ews_expm_batched")
         ctx.save_for_backward(Xc)
         return out
 
@@ -149,10 +150,11 @@ class Expm(torch.autograd.Function):
         out = torch.empty_like(X)
         n = X.shape[-1]
         batch = X.numel() // (n * n) if n else 0
-        _lib.check(
-            _lib.load().ews_expm_adjoint_batched(_ptr(X), _ptr(Gc), _ptr(out), batch, n, _stream_ptr(X.device)),
-            "ews_expm_adjoint_batched",
-        )
+        with _timed("ews_expm_adjoint", X.device, batch):
+            _lib.check(
+                _lib.load().ews_expm_adjoint_batched(_ptr(X), _ptr(Gc), _ptr(out), batch, n, _stream_ptr(X.device)),
+                "ews_expm_adjoint_batched",
+            )
         return out
 
 
