@@ -36,6 +36,7 @@ constexpr int NB = 8;        // padded state dimension: 4 blocks of 2
 constexpr int KQ = 9;        // coefficient slots: series order <= 8
 constexpr int kWarps = 4;    // warps per CTA, each an independent tile worker
 constexpr int SLOT = 16 + 8 + 64 + 512;  // chunk element: D blocks | S1 | S2 | S3
+constexpr int LROW = 608;                // an interval's local element D | s1 | s2 | s3, padded to 16 B rows
 constexpr int NPAIR = KQ * (KQ + 1) / 2;  // (p, r) with p + r <= 8
 
 struct Geom {
@@ -44,7 +45,7 @@ struct Geom {
     int spin_limit, q, ntiles, SR;
     int lift_n;
     // per-warp shared memory (floats)
-    int f_dys, f_dts, f_loc, f_stage, f_per_warp;
+    int f_dys, f_dts, f_loc, f_stage, f_per_warp;  // f_loc: two staged local rows in the forward
     int b_dys, b_dts, b_dtg, b_dyg, b_loc, b_adj, b_gst, b_sst, b_per_warp;
 };
 
@@ -66,6 +67,7 @@ struct Params {
     float* grad_dtheta;
     float* partials;       // per tile: dA blocks (16) | dlift (8 x d_in)
     const float* fagg;     // the forward aggregates
+    float* loc;            // (B, T, LROW): every interval's local element, written by local_kernel
     float c1[KQ];             // c1_p = 1 / (p + 1)
     float c2[KQ * KQ];        // c2_pr = 1 / ((p + r + 2)(r + 1))
     float c3[KQ * KQ * KQ];   // c3_prs = 1 / ((p + r + s + 3)(r + s + 2)(s + 1))
@@ -493,6 +495,75 @@ __device__ void load_chunk(const Params& p, const float* liftS, float* dxs, floa
 
 // ------------------------------------------------------------------------------ forward kernel
 
+// The local element of every interval, a parallel map ahead of the chains: one warp per chunk of one
+// sample builds each interval's flow complement, letters and series terms (build_local, as the chain did)
+// and writes [D | s1 | s2 | s3] (s3[i][j][k] at 88 + 64 i + 8 j + k) to p.loc.
+__global__ void __launch_bounds__(kWarps * 32) local_kernel(Params p) {
+    extern __shared__ float smem[];
+    const Geom& g = p.g;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int i = lane >> 2, jb = lane & 3;
+    float* liftS = smem;
+    float* Ablk = smem + g.lift_n;
+    for (int e = threadIdx.x; e < NB * g.d_in; e += blockDim.x) {
+        const int r = e / g.d_in, cc = e - r * g.d_in;
+        liftS[cc * NB + r] = (p.lift && r < g.N) ? p.lift[r * g.d_in + cc] : 0.f;
+    }
+    for (int e = threadIdx.x; e < 16; e += blockDim.x) Ablk[e] = (e >> 2) < g.N / 2 ? p.blocks[e] : 0.f;
+    __syncthreads();
+    float* dxs = smem + g.lift_n + 16 + warp * g.f_per_warp;
+    float* dys = dxs + g.f_dys;
+    float* dts = dxs + g.f_dts;
+    const Loc lc(dxs + g.f_loc);  // the forward's two staged rows hold one Loc
+    const int job = blockIdx.x * kWarps + warp;
+    if (job >= g.B * g.C) return;
+    const int b = job / g.C, t0 = (job - b * g.C) * g.Lc;
+    const int n = min(g.Lc, g.T - t0);
+    load_chunk(p, liftS, dxs, dys, dts, b, t0, n);
+    for (int k = 0; k < n; ++k) {
+        build_local(p, Ablk, dys + k * NB, dts[k], lc);
+        float s2a[2], s2b[2][8], s3[2][8];
+        local_view(p, lc, i, jb, s2a, s2b, s3);
+        float* row = p.loc + ((size_t)b * g.T + t0 + k) * LROW;
+        if (lane < 16) row[lane] = lc.D[lane];
+        if (lane < 8) row[16 + lane] = lc.s1[lane];
+        row[24 + lane] = lc.s2[lane];
+        row[56 + lane] = lc.s2[32 + lane];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            float* d3 = row + 88 + 64 * i + 8 * (2 * jb + r);
+            *reinterpret_cast<float4*>(d3) = make_float4(s3[r][0], s3[r][1], s3[r][2], s3[r][3]);
+            *reinterpret_cast<float4*>(d3 + 4) = make_float4(s3[r][4], s3[r][5], s3[r][6], s3[r][7]);
+        }
+        __syncwarp();
+    }
+}
+
+// Copies interval t's local element (LROW floats) into dst (one cp.async group).
+__device__ __forceinline__ void fetch_local(const Params& p, int b, int t, float* dst) {
+    const float* src = p.loc + ((size_t)b * p.g.T + t) * LROW;
+    for (int v = threadIdx.x & 31; v < LROW / 4; v += 32) cp_async16(dst + 4 * v, src + 4 * v);
+    cp_async_commit();
+}
+
+// One interval from a staged local element: S <- S (x) local.
+__device__ __forceinline__ void chen_step_row(const float* row, E3& S, int i, int jb) {
+    float s2a[2], s2b[2][8], s3[2][8];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int j = 2 * jb + r;
+        s2a[r] = row[24 + 8 * i + j];
+        const float4* b2 = reinterpret_cast<const float4*>(row + 24 + 8 * j);
+        const float4* b3 = reinterpret_cast<const float4*>(row + 88 + 64 * i + 8 * j);
+        const float4 u0 = b2[0], u1 = b2[1], w0 = b3[0], w1 = b3[1];
+        s2b[r][0] = u0.x; s2b[r][1] = u0.y; s2b[r][2] = u0.z; s2b[r][3] = u0.w;
+        s2b[r][4] = u1.x; s2b[r][5] = u1.y; s2b[r][6] = u1.z; s2b[r][7] = u1.w;
+        s3[r][0] = w0.x; s3[r][1] = w0.y; s3[r][2] = w0.z; s3[r][3] = w0.w;
+        s3[r][4] = w1.x; s3[r][5] = w1.y; s3[r][6] = w1.z; s3[r][7] = w1.w;
+    }
+    chen_mul_r(S, row, row + 16, s2a, s2b, s3, i, jb);
+}
+
 __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
     extern __shared__ float smem[];
     const Geom& g = p.g;
@@ -507,9 +578,7 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
     for (int e = threadIdx.x; e < 16; e += blockDim.x) Ablk[e] = (e >> 2) < g.N / 2 ? p.blocks[e] : 0.f;
     __syncthreads();
     float* dxs = smem + g.lift_n + 16 + warp * g.f_per_warp;
-    float* dys = dxs + g.f_dys;
-    float* dts = dxs + g.f_dts;
-    const Loc lc(dxs + g.f_loc);
+    float* lrow = dxs + g.f_loc;  // two staged local elements
     float* stage = dxs + g.f_stage;
 
     for (;;) {
@@ -518,7 +587,6 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
         const int c = tile / g.B, b = tile - c * g.B;
         const int t0 = c * g.Lc;
         const int len = min(g.Lc, g.T - t0);
-        load_chunk(p, liftS, dxs, dys, dts, b, t0, len);
 
         // pass 1: the chunk's aggregate from the identity, kept in the workspace (agg, and incl for chunk 0)
         const size_t slot = ((size_t)b * g.C + c) * SLOT;
@@ -526,9 +594,12 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
         {
             E3 A;
             A.identity();
+            fetch_local(p, b, t0, lrow);
             for (int k = 0; k < len; ++k) {
-                build_local(p, Ablk, dys + k * NB, dts[k], lc);
-                chen_step(p, lc, A, i, jb);
+                cp_async_wait<0>();
+                __syncwarp();
+                if (k + 1 < len) fetch_local(p, b, t0 + k + 1, lrow + ((k + 1) & 1) * LROW);
+                chen_step_row(lrow + (k & 1) * LROW, A, i, jb);
                 __syncwarp();
             }
             store_e3(p.agg + slot, A, i, jb);
@@ -588,9 +659,12 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
         // pass 2: re-run the chunk from its carry and emit the prefix rows
         E3 S = excl;
         int k0 = 0;
+        fetch_local(p, b, t0, lrow);
         for (int k = 0; k < len; ++k) {
-            build_local(p, Ablk, dys + k * NB, dts[k], lc);
-            chen_step(p, lc, S, i, jb);
+            cp_async_wait<0>();
+            __syncwarp();
+            if (k + 1 < len) fetch_local(p, b, t0 + k + 1, lrow + ((k + 1) & 1) * LROW);
+            chen_step_row(lrow + (k & 1) * LROW, S, i, jb);
             stage_row(stage + (k - k0) * g.W, S, g.N, i, jb);
             if (k - k0 == g.SR - 1 || k == len - 1) {
                 __syncwarp();
@@ -1417,7 +1491,7 @@ int make_geom(const ews_block_args* a, Geom* g) {
     g->f_dys = xs;
     g->f_dts = xs + ys;
     g->f_loc = g->f_dts + ts;
-    g->f_stage = g->f_loc + align4(Loc::floats);
+    g->f_stage = g->f_loc + align4(std::max(2 * LROW, (int)Loc::floats));
     g->f_per_warp = g->f_stage + align4(g->SR * g->W);
     g->b_dys = xs;
     g->b_dts = xs + ys;
@@ -1434,7 +1508,7 @@ int make_geom(const ews_block_args* a, Geom* g) {
 size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 struct WsLayout {
-    size_t status, flags, agg, incl, carry, partials, total;
+    size_t status, flags, agg, incl, carry, partials, loc, total;
 };
 
 WsLayout bwd_layout(const Geom& g) {
@@ -1469,6 +1543,8 @@ WsLayout fwd_layout(const Geom& g) {
     o += slots;
     L.carry = o;
     o += slots;
+    L.loc = o;
+    o += al256(sizeof(float) * (size_t)g.B * g.T * LROW);
     L.total = o;
     return L;
 }
@@ -1533,9 +1609,16 @@ extern "C" int ews_block_fwd(const ews_block_args* a, ews_stream_t stream) {
     p.agg = (float*)(ws + L.agg);
     p.incl = (float*)(ws + L.incl);
     p.carry = (float*)(ws + L.carry);
+    p.loc = (float*)(ws + L.loc);
     series_coefficients(g.q, &p);
     const size_t smem = fwd_smem(g);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+    {
+        // every interval's local element first: a parallel map
+        cudaFuncSetAttribute(local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        local_kernel<<<(g.B * g.C + kWarps - 1) / kWarps, kWarps * 32, smem, s>>>(p);
+        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    }
     cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
