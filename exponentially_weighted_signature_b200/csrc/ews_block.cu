@@ -1294,6 +1294,16 @@ __device__ __forceinline__ void mu_step(const Loc& lc, A3& a, int i, int jb) {
     apply_JT(a, lc.D, lc.s1, U2b, i, jb);
 }
 
+// mu_step with the local element staged as a row [D | s1 | s2 | s3].
+__device__ __forceinline__ void mu_step_row(const float* row, A3& a, int i, int jb) {
+    float U2b[2][8];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) U2b[r][k] = row[24 + (2 * jb + r) * 8 + k];
+    apply_JT(a, row, row + 16, U2b, i, jb);
+}
+
 __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     extern __shared__ float smem[];
     const Geom& g = p.g;
@@ -1328,14 +1338,19 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         const size_t slot = ((size_t)b * g.C + c) * SLOT;
         int* flag = p.flags + (size_t)b * g.C + c;
 
-        // ---- 1. zero-carry local adjoint over the chunk (reverse)
+        // ---- 1. zero-carry local adjoint over the chunk (reverse); the local elements come from the forward's
+        // local_kernel, staged one interval ahead in the (idle) Loc / AdjBuf area
         A3 mu;
         mu.zero();
+        float* lst = dxs + g.b_loc;
+        fetch_local(p, b, t0 + len - 1, lst + ((len - 1) & 1) * LROW);
         for (int k = len - 1; k >= 0; --k) {
             warp_load_span(gst, p.grad_out + ((size_t)b * g.T + t0 + k) * g.W, g.W);
-            build_local(p, Ablk, dys + k * NB, dts[k], lc, false);
+            cp_async_wait<0>();
+            __syncwarp();
+            if (k >= 1) fetch_local(p, b, t0 + k - 1, lst + ((k - 1) & 1) * LROW);
             add_grad_row(mu, gst, g.N, i, jb);
-            mu_step(lc, mu, i, jb);
+            mu_step_row(lst + (k & 1) * LROW, mu, i, jb);
             __syncwarp();
         }
         // ---- 2. look-back over the later chunks: the cotangent at the chunk's end
@@ -1664,6 +1679,7 @@ extern "C" int ews_block_bwd(const ews_block_args* a, ews_stream_t stream) {
     p.incl = (float*)(ws + L.incl);
     p.partials = (float*)(ws + L.partials);
     p.fagg = (const float*)(fws + F.agg);
+    p.loc = (float*)(fws + F.loc);
     series_coefficients(g.q, &p);
     const size_t smem = bwd_smem(g);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
