@@ -152,6 +152,15 @@ __device__ __forceinline__ float* warp_load_span_async(float* __restrict__ buf, 
     return s;
 }
 
+// Asks L2 for the 128-byte lines that hold [p, p + n) (n <= 1024 floats; lane l takes line l). Only lines
+// that contain an element of the range are named, so every address lies inside the caller's buffer.
+__device__ __forceinline__ void prefetch_span_l2(const float* p, int n) {
+    const int lane = threadIdx.x & 31;
+    const uintptr_t first = reinterpret_cast<uintptr_t>(p) & ~static_cast<uintptr_t>(127);
+    const uintptr_t line = first + 128u * static_cast<uintptr_t>(lane);
+    if (line < reinterpret_cast<uintptr_t>(p + n)) asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
+}
+
 __device__ __forceinline__ float load_in(const void* p, size_t idx, bool bf16) {
     if (bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[idx]);
     return reinterpret_cast<const float*>(p)[idx];

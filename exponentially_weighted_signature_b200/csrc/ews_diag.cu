@@ -348,6 +348,48 @@ __device__ __forceinline__ void chen_step_emit(const Tables<RI, RJ>& tb, const f
     }
 }
 
+// Uniform clock, not the basepoint interval: S2' = S2 - dd o S2 + dy_j (u_i q1_j + q2_ij dy_i) with
+// u = rho o S1, the pair complements dd constant (four floating-point operations per entry).
+template <int RI, int RJ>
+__device__ __forceinline__ void chen_step_u(const Tables<RI, RJ>& tb, const float* dyk, int i0, int j0,
+                                            Elem<RI, RJ>& S, const float dd[RI][RJ]) {
+    float dyr[RI], dyc[RJ];
+#pragma unroll
+    for (int r = 0; r < RI; ++r) dyr[r] = dyk[i0 + r];
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) dyc[c] = dyk[j0 + c];
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const float u = fmaf(-tb.dr[r], S.S1r[r], S.S1r[r]);
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            const float t = fmaf(u, tb.q1c[c], tb.q2[r][c] * dyr[r]);
+            const float s2 = fmaf(t, dyc[c], S.S2[r][c]);
+            S.S2[r][c] = fmaf(-dd[r][c], S.S2[r][c], s2);
+        }
+        S.S1r[r] = fmaf(tb.q1r[r], dyr[r], u);
+    }
+}
+
+// Prefix row [1, S1, S2] of a lane element to global memory (real dimension N). Every lane of a row group
+// writes its rows' level-1 entries (same value, same address), so no store is predicated on the lane.
+template <int RI, int RJ>
+__device__ __forceinline__ void emit_row_all(float* row, const Elem<RI, RJ>& S, int N, int i0, int j0) {
+    row[0] = 1.f;
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const int i = i0 + r;
+        if (i < N) {
+            row[1 + i] = S.S1r[r];
+#pragma unroll
+            for (int c = 0; c < RJ; ++c) {
+                const int j = j0 + c;
+                if (j < N) row[1 + N + i * N + j] = S.S2[r][c];
+            }
+        }
+    }
+}
+
 // Writes prefix row [1, S1, S2] of a lane element straight to global memory (real dimension N).
 template <int RI, int RJ>
 __device__ __forceinline__ void emit_row(float* row, const Elem<RI, RJ>& S, int N, int i0, int j0, int tj,
@@ -444,24 +486,19 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
             for (int r = 0; r < RI; ++r)
 #pragma unroll
                 for (int cc = 0; cc < RJ; ++cc) dd[r][cc] = comp_mul(tb.dr[r], tb.dc[cc]);
-            int nflow = 0;
-            for (int k = 0; k < len; ++k) {
-                float fr[RI], fc[RJ];
-                const bool bp = basepoint && (t0 + k == 0);
-                step_flow(tb, bp, fr, fc);
-                if (bp) {
-                    float d0[RI][RJ];
+            // the basepoint interval (k = 0 of chunk 0) runs apart from the loop
+            const int kf = (basepoint && t0 == 0) ? 1 : 0;
+            if (kf) {
+                float fr[RI], fc[RJ], d0[RI][RJ];
+                step_flow(tb, true, fr, fc);
 #pragma unroll
-                    for (int r = 0; r < RI; ++r)
+                for (int r = 0; r < RI; ++r)
 #pragma unroll
-                        for (int cc = 0; cc < RJ; ++cc) d0[r][cc] = 0.f;
-                    chen_step_emit(tb, dys + k * NP, i0, j0, A, fr, fc, d0, true);
-                } else {
-                    chen_step_emit(tb, dys + k * NP, i0, j0, A, fr, fc, dd, false);
-                    ++nflow;
-                }
+                    for (int cc = 0; cc < RJ; ++cc) d0[r][cc] = 0.f;
+                chen_step_emit(tb, dys, i0, j0, A, fr, fc, d0, true);
             }
-            const float fn = (float)nflow;
+            for (int k = kf; k < len; ++k) chen_step_u(tb, dys + k * NP, i0, j0, A, dd);
+            const float fn = (float)(len - kf);
 #pragma unroll
             for (int r = 0; r < RI; ++r) A.Dr[r] = -expm1f(fn * tb.xr[r]);
 #pragma unroll
@@ -534,6 +571,25 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
                 for (int c = 0; c < RJ; ++c) dd[r][c] = comp_mul(tb.dr[r], tb.dc[c]);
         }
         float* orow = p.out + ((size_t)b * g.T + t0) * g.W;
+        if (!NU) {
+            const int kf = (basepoint && t0 == 0) ? 1 : 0;
+            if (kf) {
+                float fr[RI], fc[RJ], d0[RI][RJ];
+                step_flow(tb, true, fr, fc);
+#pragma unroll
+                for (int r = 0; r < RI; ++r)
+#pragma unroll
+                    for (int c = 0; c < RJ; ++c) d0[r][c] = 0.f;
+                chen_step_emit(tb, dys, i0, j0, S, fr, fc, d0, true);
+                emit_row_all(orow, S, Nr, i0, j0);
+                orow += g.W;
+            }
+            for (int k = kf; k < len; ++k, orow += g.W) {
+                chen_step_u(tb, dys + k * NP, i0, j0, S, dd);
+                emit_row_all(orow, S, Nr, i0, j0);
+            }
+            continue;
+        }
         for (int k = 0; k < len; ++k, orow += g.W) {
             float fr[RI], fc[RJ];
             if (NU) tb.at(p, dts[k]);
@@ -666,12 +722,16 @@ __device__ __forceinline__ void read_row(const float* row, float v1[RI], float v
 template <int RI, int RJ>
 struct Grads {
     float gxr[RI], gxc[RJ], dq1c[RJ], dq2[RI][RJ];
+    float F[RI][RJ];  // uniform clock: sum_t lambda2_t o S2_{t-1}, scaled by rho_i rho_j once per chunk
     __device__ void zero() {
 #pragma unroll
         for (int r = 0; r < RI; ++r) {
             gxr[r] = 0.f;
 #pragma unroll
-            for (int c = 0; c < RJ; ++c) dq2[r][c] = 0.f;
+            for (int c = 0; c < RJ; ++c) {
+                dq2[r][c] = 0.f;
+                F[r][c] = 0.f;
+            }
         }
 #pragma unroll
         for (int c = 0; c < RJ; ++c) {
@@ -827,6 +887,137 @@ __device__ __forceinline__ void adj_step(const Tables<RI, RJ>& tb, const float f
     }
 }
 
+// Uniform clock, not the basepoint interval: the transposed step with the pair complements dd = 1 - rho_i rho_j
+// given (they are constant over the path).
+template <int RI, int RJ>
+__device__ __forceinline__ void adj_step_u(const Tables<RI, RJ>& tb, const float dd[RI][RJ], const float* dyk,
+                                           Adj<RI, RJ>& a, int j0) {
+    float s1c[RJ];
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) s1c[c] = tb.q1c[c] * dyk[j0 + c];
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        float wr = 0.f;
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) wr = fmaf(a.L2[r][c], s1c[c], wr);
+        wr = row_sum(wr) + a.L1r[r];
+        a.L1r[r] = fmaf(-tb.dr[r], wr, wr);
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] = fmaf(-dd[r][c], a.L2[r][c], a.L2[r][c]);
+    }
+}
+
+// Uniform clock, not the basepoint interval: bwd_step with the pair complements given. The flow gradient's
+// level-2 part rho_i rho_j lambda2 S2_{t-1} is accumulated as sum_t lambda2 o S2_{t-1} (gr.F) and scaled by
+// the constant rho_i rho_j once per chunk (lane blocks up to 18 entries; larger ones credit it every step,
+// which needs no accumulator registers); its level-1 part sum_j lambda2_ij u_i s1_j = u_i (lambda2 s1)_i
+// reuses the adjoint recursion's row partials. l1w = 1 on the lane that credits lambda1 u (tj == 0).
+template <int RI, int RJ>
+__host__ __device__ constexpr bool accumulate_flow_terms() { return RI * RJ <= 18; }
+
+template <int RI, int RJ>
+__device__ __forceinline__ void bwd_step_u(const Tables<RI, RJ>& tb, const float dd[RI][RJ], const float* dyk,
+                                           const float S1p[RI], const float S2p[RI][RJ], Adj<RI, RJ>& a,
+                                           Grads<RI, RJ>& gr, float* dyg, int i0, int j0, int ti, int tj, float l1w) {
+    float dyr[RI], dyc[RJ], s1c[RJ], u[RI];
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        dyr[r] = dyk[i0 + r];
+        u[r] = fmaf(-tb.dr[r], S1p[r], S1p[r]);
+    }
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        dyc[c] = dyk[j0 + c];
+        s1c[c] = tb.q1c[c] * dyc[c];
+    }
+    float w[RI], z[RI], y[RJ], v[RJ];
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        y[c] = 0.f;
+        v[c] = 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        float wr = 0.f, zr = 0.f, fx = 0.f;
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) {
+            const float l2 = a.L2[r][c];
+            const float l2q = l2 * tb.q2[r][c];
+            wr = fmaf(l2, s1c[c], wr);
+            zr = fmaf(l2q, dyc[c], zr);
+            y[c] = fmaf(l2, u[r], y[c]);
+            v[c] = fmaf(l2q, dyr[r], v[c]);
+            if (accumulate_flow_terms<RI, RJ>()) {
+                gr.F[r][c] = fmaf(l2, S2p[r][c], gr.F[r][c]);
+            } else {
+                float fl = l2 * S2p[r][c];
+                fl = fmaf(-dd[r][c], fl, fl);
+                fx += fl;
+                gr.gxc[c] += fl;
+            }
+            gr.dq2[r][c] = fmaf(l2, dyr[r] * dyc[c], gr.dq2[r][c]);
+        }
+        gr.gxr[r] = fmaf(u[r], fmaf(l1w, a.L1r[r], wr), gr.gxr[r] + fx);
+        w[r] = row_sum(wr);
+        z[r] = row_sum(zr);
+    }
+    float l1c[RJ], zc[RJ];
+    rows_to_cols<RI, RJ>(a.L1r, l1c, tj);
+    rows_to_cols<RI, RJ>(z, zc, tj);
+#pragma unroll
+    for (int c = 0; c < RJ; ++c) {
+        const float ds1 = l1c[c] + col_sum(y[c]);
+        const float vv = col_sum(v[c]);
+        gr.dq1c[c] = fmaf(ds1, dyc[c], gr.dq1c[c]);
+        if (ti == 0) dyg[j0 + c] = fmaf(ds1, tb.q1c[c], vv + zc[c]);
+    }
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        const float lw = a.L1r[r] + w[r];
+        a.L1r[r] = fmaf(-tb.dr[r], lw, lw);
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] = fmaf(-dd[r][c], a.L2[r][c], a.L2[r][c]);
+    }
+}
+
+// Stages n floats from global memory at the shared-memory offset off (floats from base) with cp.async and
+// returns the offset of the first element (the copy keeps the source's 16-byte phase). Offsets rather than
+// pointers keep the later reads in the shared address space.
+__device__ __forceinline__ int stage_span(float* base, int off, const float* src, int n) {
+    const int shift = (int)(((uintptr_t)src & 15u) >> 2);
+    warp_load_span_async(base + off, src, n);
+    return off + shift;
+}
+
+// Under a uniform clock, lane blocks of up to 8 level-2 entries (N <= 16) read the backward's rows straight
+// into registers, one row ahead; larger blocks and the per-interval clock (whose tables take the registers)
+// stage blocks of rows in shared memory with cp.async.
+template <int RI, int RJ, bool NU>
+__host__ __device__ constexpr bool rows_in_registers() { return !NU && RI * RJ <= 8; }
+
+// Rows the register path asks L2 for ahead of its loads (the loads themselves run one row ahead).
+constexpr int kPrefetchRows = 6;
+
+template <int RI, int RJ>
+__device__ __forceinline__ void add_grad_vals(Adj<RI, RJ>& a, const float g1[RI], const float g2[RI][RJ]) {
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        a.L1r[r] += g1[r];
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) a.L2[r][c] += g2[r][c];
+    }
+}
+
+template <int RI, int RJ>
+__device__ __forceinline__ void copy_vals(float d1[RI], float d2[RI][RJ], const float s1[RI], const float s2[RI][RJ]) {
+#pragma unroll
+    for (int r = 0; r < RI; ++r) {
+        d1[r] = s1[r];
+#pragma unroll
+        for (int c = 0; c < RJ; ++c) d2[r][c] = s2[r][c];
+    }
+}
+
 template <int RI, int RJ>
 __device__ __forceinline__ void add_grad_row(Adj<RI, RJ>& a, const float* row, int N, int i0, int j0) {
     float g1[RI], g2[RI][RJ];
@@ -925,8 +1116,6 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     float* dyg = dxs + g.b_dyg;
     float* lam1 = dxs + g.b_lam1;
     float* gst = dxs + g.b_gst;
-    float* gbuf[2] = {gst, dxs + g.b_gst2};
-    float* sbuf[2] = {dxs + g.b_sst, dxs + g.b_sst2};
 
     const int ti = lane >> 3, tj = lane & 7;
     const int i0 = ti * RI, j0 = tj * RJ;
@@ -965,29 +1154,49 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         // ---- 1. zero-carry local adjoint over the chunk (reverse)
         Adj<RI, RJ> mu;
         mu.zero();
-        if (!terminal) {
+        // uniform clock: the pair complements 1 - rho_i rho_j are constant; the basepoint interval (k = 0 of
+        // chunk 0) runs apart from the loops
+        const bool bpc = basepoint && t0 == 0;
+        float dd[RI][RJ];
+#pragma unroll
+        for (int r = 0; r < RI; ++r)
+#pragma unroll
+            for (int cc = 0; cc < RJ; ++cc) dd[r][cc] = NU ? 0.f : comp_mul(tb.dr[r], tb.dc[cc]);
+        if (!terminal && !rows_in_registers<RI, RJ, NU>()) {
             // gradient rows in blocks of SR, the next block copied in while this one runs
             int slot = 0;
-            float* cur = warp_load_span_async(gbuf[0], p.grad_out + ((size_t)b * g.T + t0 + max(0, len - g.SR)) * g.W,
-                                              (len - max(0, len - g.SR)) * g.W);
+            int cur = stage_span(dxs, g.b_gst, p.grad_out + ((size_t)b * g.T + t0 + max(0, len - g.SR)) * g.W,
+                                 (len - max(0, len - g.SR)) * g.W);
             cp_async_commit();
             for (int kb = len; kb > 0; kb -= g.SR) {
                 const int k0 = max(0, kb - g.SR);
-                float* nxt = nullptr;
+                int nxt = 0;
                 if (k0 > 0) {
                     const int k1 = max(0, k0 - g.SR);
-                    nxt = warp_load_span_async(gbuf[slot ^ 1], p.grad_out + ((size_t)b * g.T + t0 + k1) * g.W, (k0 - k1) * g.W);
+                    nxt = stage_span(dxs, slot ? g.b_gst : g.b_gst2, p.grad_out + ((size_t)b * g.T + t0 + k1) * g.W,
+                                     (k0 - k1) * g.W);
                 }
                 cp_async_commit();
                 cp_async_wait<1>();
                 __syncwarp();
-                for (int k = kb - 1; k >= k0; --k) {
-                    add_grad_row(mu, cur + (k - k0) * g.W, Nr, i0, j0);
+                const float* rows = dxs + cur;
+                const int kl = (bpc && k0 == 0) ? 1 : k0;
+                for (int k = kb - 1; k >= kl; --k) {
+                    add_grad_row(mu, rows + (k - k0) * g.W, Nr, i0, j0);
+                    if (NU) {
+                        float fr[RI], fc[RJ];
+                        tb.at(p, dts[k]);
+                        step_flow(tb, false, fr, fc);
+                        adj_step(tb, fr, fc, dys + k * NP, mu, j0, false);
+                    } else {
+                        adj_step_u(tb, dd, dys + k * NP, mu, j0);
+                    }
+                }
+                if (kl > k0) {
+                    add_grad_row(mu, rows, Nr, i0, j0);
                     float fr[RI], fc[RJ];
-                    if (NU) tb.at(p, dts[k]);
-                    const bool bp = basepoint && (t0 + k == 0);
-                    step_flow(tb, bp, fr, fc);
-                    adj_step(tb, fr, fc, dys + k * NP, mu, j0, bp);
+                    step_flow(tb, true, fr, fc);
+                    adj_step(tb, fr, fc, dys, mu, j0, true);
                 }
                 __syncwarp();
                 cur = nxt;
@@ -995,6 +1204,35 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
             }
             cp_async_wait<0>();
             __syncwarp();
+        } else if (!terminal) {
+            // gradient rows straight into registers, the next row's loads in flight while this step runs
+            const float* grow = p.grad_out + ((size_t)b * g.T + t0) * g.W;
+            float g1[RI], g2[RI][RJ];
+            read_row<RI, RJ>(grow + (size_t)(len - 1) * g.W, g1, g2, Nr, i0, j0);
+            const int kl = bpc ? 1 : 0;
+            for (int k = len - 1; k >= len - kPrefetchRows && k >= 0; --k) prefetch_span_l2(grow + (size_t)k * g.W, g.W);
+#pragma unroll 2
+            for (int k = len - 1; k >= kl; --k) {
+                if (k >= kPrefetchRows) prefetch_span_l2(grow + (size_t)(k - kPrefetchRows) * g.W, g.W);
+                float n1[RI], n2[RI][RJ];
+                read_row<RI, RJ>(grow + (size_t)max(k - 1, 0) * g.W, n1, n2, Nr, i0, j0);
+                add_grad_vals(mu, g1, g2);
+                if (NU) {
+                    float fr[RI], fc[RJ];
+                    tb.at(p, dts[k]);
+                    step_flow(tb, false, fr, fc);
+                    adj_step(tb, fr, fc, dys + k * NP, mu, j0, false);
+                } else {
+                    adj_step_u(tb, dd, dys + k * NP, mu, j0);
+                }
+                copy_vals<RI, RJ>(g1, g2, n1, n2);
+            }
+            if (kl) {  // the basepoint interval; g1, g2 hold row 0
+                add_grad_vals(mu, g1, g2);
+                float fr[RI], fc[RJ];
+                step_flow(tb, true, fr, fc);
+                adj_step(tb, fr, fc, dys, mu, j0, true);
+            }
         } else {
             // lambda1 only (lambda2 is closed form): mu1_{t-1} = rho (mu1_t + lambda2_t s1_t); g1 enters at T-1
             for (int k = len - 1; k >= 0; --k) {
@@ -1077,25 +1315,29 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         gr.zero();
         if (!terminal) {
             Adj<RI, RJ> a = lam_in;
+            const float l1w = tj == 0 ? 1.f : 0.f;
+            if (!rows_in_registers<RI, RJ, NU>()) {
             // block [k0, kb): gradient rows t0+k0.. and S_{t-1} rows t0+k0-1.. (row -1 is the zero state),
             // the next block copied in while this one runs
-            auto stage = [&](int k0s, int kbs, int sl, float*& gs, float*& ss) {
+            auto stage = [&](int k0s, int kbs, int sl, int& gs, int& ss) {
                 const int ns = kbs - k0s;
-                gs = warp_load_span_async(gbuf[sl], p.grad_out + ((size_t)b * g.T + t0 + k0s) * g.W, ns * g.W);
+                gs = stage_span(dxs, sl ? g.b_gst2 : g.b_gst, p.grad_out + ((size_t)b * g.T + t0 + k0s) * g.W, ns * g.W);
                 const int first = t0 + k0s - 1;
+                const int soff = sl ? g.b_sst2 : g.b_sst;
                 if (first >= 0) {
-                    ss = warp_load_span_async(sbuf[sl], p.out + ((size_t)b * g.T + first) * g.W, ns * g.W);
+                    ss = stage_span(dxs, soff, p.out + ((size_t)b * g.T + first) * g.W, ns * g.W);
                 } else {
                     // row -1 is zero; rows 0.. follow it, placed at the source's 16-byte phase
                     const int shift = (int)(((uintptr_t)(p.out + (size_t)b * g.T * g.W) & 15u) >> 2);
-                    const int lead = (shift - g.W % 4 + 8) % 4;  // so that ss + W has the source's phase
-                    ss = sbuf[sl] + lead;
-                    for (int e = lane; e < g.W; e += 32) ss[e] = 0.f;
-                    if (ns > 1) warp_load_span_async(ss + g.W - shift, p.out + (size_t)b * g.T * g.W, (ns - 1) * g.W);
+                    const int lead = (shift - g.W % 4 + 8) % 4;  // so that row 0 has the source's phase
+                    ss = soff + lead;
+                    for (int e = lane; e < g.W; e += 32) dxs[ss + e] = 0.f;
+                    if (ns > 1)
+                        warp_load_span_async(dxs + ss + g.W - shift, p.out + (size_t)b * g.T * g.W, (ns - 1) * g.W);
                 }
             };
             int slot = 0;
-            float *gcur, *scur, *gnxt = nullptr, *snxt = nullptr;
+            int gcur, scur, gnxt = 0, snxt = 0;
             stage(max(0, len - g.SR), len, 0, gcur, scur);
             cp_async_commit();
             for (int kb = len; kb > 0; kb -= g.SR) {
@@ -1104,16 +1346,30 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                 cp_async_commit();
                 cp_async_wait<1>();
                 __syncwarp();
-                for (int k = kb - 1; k >= k0; --k) {
-                    add_grad_row(a, gcur + (k - k0) * g.W, Nr, i0, j0);
+                const float* grows = dxs + gcur;
+                const float* srows = dxs + scur;
+                const int kl = (bpc && k0 == 0) ? 1 : k0;
+                for (int k = kb - 1; k >= kl; --k) {
+                    add_grad_row(a, grows + (k - k0) * g.W, Nr, i0, j0);
                     float S1p[RI], S2p[RI][RJ];
-                    read_row<RI, RJ>(scur + (k - k0) * g.W, S1p, S2p, Nr, i0, j0);
+                    read_row<RI, RJ>(srows + (k - k0) * g.W, S1p, S2p, Nr, i0, j0);
+                    if (NU) {
+                        float fr[RI], fc[RJ];
+                        tb.at(p, dts[k]);
+                        step_flow(tb, false, fr, fc);
+                        bwd_step<RI, RJ, NU>(p, tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, dts[k],
+                                             dtg + k, i0, j0, ti, tj, false);
+                    } else {
+                        bwd_step_u<RI, RJ>(tb, dd, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, i0, j0, ti, tj, l1w);
+                    }
+                }
+                if (kl > k0) {
+                    add_grad_row(a, grows, Nr, i0, j0);
+                    float S1p[RI], S2p[RI][RJ];
+                    read_row<RI, RJ>(srows, S1p, S2p, Nr, i0, j0);
                     float fr[RI], fc[RJ];
-                    if (NU) tb.at(p, dts[k]);
-                    const bool bp = basepoint && (t0 + k == 0);
-                    step_flow(tb, bp, fr, fc);
-                    bwd_step<RI, RJ, NU>(p, tb, fr, fc, dys + k * NP, S1p, S2p, a, gr, dyg + k * NP, NU ? dts[k] : 0.f,
-                                         dtg + k, i0, j0, ti, tj, bp);
+                    step_flow(tb, true, fr, fc);
+                    bwd_step<RI, RJ, NU>(p, tb, fr, fc, dys, S1p, S2p, a, gr, dyg, 0.f, dtg, i0, j0, ti, tj, true);
                 }
                 __syncwarp();
                 gcur = gnxt;
@@ -1122,6 +1378,71 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
             }
             cp_async_wait<0>();
             __syncwarp();
+            } else {
+            // gradient row t and state row t-1 straight into registers, the next pair's loads in flight while
+            // this step runs; chunk 0's first interval (state row -1 = 0) runs after the loop
+            const size_t rb = (size_t)b * g.T + t0;
+            const float* grow = p.grad_out + rb * g.W;
+            const int klo = t0 == 0 ? 1 : 0;
+            float g1[RI], g2[RI][RJ], s1[RI], s2[RI][RJ];
+            for (int k = len - 1; k >= len - kPrefetchRows && k >= klo; --k) {
+                prefetch_span_l2(grow + (size_t)k * g.W, g.W);
+                prefetch_span_l2(p.out + (rb + k - 1) * g.W, g.W);
+            }
+            read_row<RI, RJ>(grow + (size_t)(len - 1) * g.W, g1, g2, Nr, i0, j0);
+            if (len - 1 >= klo) read_row<RI, RJ>(p.out + (rb + len - 2) * g.W, s1, s2, Nr, i0, j0);
+#pragma unroll 2
+            for (int k = len - 1; k >= klo; --k) {
+                if (k - kPrefetchRows >= klo) {
+                    prefetch_span_l2(grow + (size_t)(k - kPrefetchRows) * g.W, g.W);
+                    prefetch_span_l2(p.out + (rb + k - kPrefetchRows - 1) * g.W, g.W);
+                }
+                float n1[RI], n2[RI][RJ], m1[RI], m2[RI][RJ];
+                read_row<RI, RJ>(grow + (size_t)max(k - 1, 0) * g.W, n1, n2, Nr, i0, j0);
+                read_row<RI, RJ>(p.out + (rb + max(k - 1, klo) - 1) * g.W, m1, m2, Nr, i0, j0);
+                add_grad_vals(a, g1, g2);
+                if (NU) {
+                    float fr[RI], fc[RJ];
+                    tb.at(p, dts[k]);
+                    step_flow(tb, false, fr, fc);
+                    bwd_step<RI, RJ, NU>(p, tb, fr, fc, dys + k * NP, s1, s2, a, gr, dyg + k * NP, dts[k], dtg + k, i0,
+                                         j0, ti, tj, false);
+                } else {
+                    bwd_step_u<RI, RJ>(tb, dd, dys + k * NP, s1, s2, a, gr, dyg + k * NP, i0, j0, ti, tj, l1w);
+                }
+                copy_vals<RI, RJ>(g1, g2, n1, n2);
+                copy_vals<RI, RJ>(s1, s2, m1, m2);
+            }
+            if (klo) {  // interval 0: g1, g2 hold gradient row 0; the state before it is zero
+                add_grad_vals(a, g1, g2);
+#pragma unroll
+                for (int r = 0; r < RI; ++r) {
+                    s1[r] = 0.f;
+#pragma unroll
+                    for (int cc = 0; cc < RJ; ++cc) s2[r][cc] = 0.f;
+                }
+                float fr[RI], fc[RJ];
+                if (NU) tb.at(p, dts[0]);
+                step_flow(tb, bpc, fr, fc);
+                if (NU || bpc) {
+                    bwd_step<RI, RJ, NU>(p, tb, fr, fc, dys, s1, s2, a, gr, dyg, NU ? dts[0] : 0.f, dtg, i0, j0, ti, tj,
+                                         bpc);
+                } else {
+                    bwd_step_u<RI, RJ>(tb, dd, dys, s1, s2, a, gr, dyg, i0, j0, ti, tj, l1w);
+                }
+            }
+            }
+            if (!NU && accumulate_flow_terms<RI, RJ>()) {
+                // the flow gradient's level-2 part: rho_i rho_j sum_t lambda2 o S2_{t-1}, credited to i and to j
+#pragma unroll
+                for (int r = 0; r < RI; ++r)
+#pragma unroll
+                    for (int cc = 0; cc < RJ; ++cc) {
+                        const float fl = fmaf(-dd[r][cc], gr.F[r][cc], gr.F[r][cc]);
+                        gr.gxr[r] += fl;
+                        gr.gxc[cc] += fl;
+                    }
+            }
         } else {
             // forward sweep from the carry with lambda2 in closed form and lambda1 = mu1 + rho^{end-t} Lam1_in
             Elem<RI, RJ> S;
@@ -1231,7 +1552,8 @@ static void carve(Geom* g) {
     g->f_stage = xs + ys + ts;
     g->f_per_warp = g->f_stage + align4(SR * g->W);
     const bool terminal = g->readout == EWS_READOUT_TERMINAL;
-    const int span = align4(SR * g->W + 4);  // SR rows at any 16-byte phase
+    // SR rows at any 16-byte phase; N <= 16 under a uniform clock reads the backward's rows into registers
+    const int span = (NP > 16 || g->nu) ? align4(SR * g->W + 4) : 0;
     const int gst_n = align4(std::max(terminal ? 0 : span, Lc * g->d_in));
     g->b_dys = xs;
     g->b_dts = xs + ys;
