@@ -45,9 +45,9 @@ __device__ __forceinline__ int next_ticket(DeviceStatus* st) {
     return __shfl_sync(kFull, t, 0);
 }
 
-// Warp-wide publish: every lane has stored its part of the slot; make the stores visible, then set the flag.
+// Warp-wide publish: every lane has stored its part of the slot; the warp barrier orders those stores before
+// lane 0's release of the flag, whose release is cumulative over them (one fence per publish).
 __device__ __forceinline__ void publish(int* flag, int value) {
-    __threadfence();
     __syncwarp();
     if ((threadIdx.x & 31) == 0) st_release(flag, value);
 }
@@ -68,7 +68,7 @@ __device__ __forceinline__ int wait_slot(const int* flag, DeviceStatus* st, int 
                 break;
             }
             __nanosleep(ns);
-            if (ns < 2048) ns <<= 1;
+            if (ns < 256) ns <<= 1;
         }
         if (v >= 0 && v < want) {
             if (atomicCAS(&st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) st->err_tile = tile;
@@ -76,7 +76,9 @@ __device__ __forceinline__ int wait_slot(const int* flag, DeviceStatus* st, int 
         }
     }
     v = __shfl_sync(kFull, v, 0);
-    __threadfence();
+    // every lane acquires the flag itself (the value is at least what lane 0 saw), so each lane's reads of the
+    // slot are ordered after the publisher's writes without a full fence
+    if (v >= 0) (void)ld_acquire(flag);
     return v;
 }
 
