@@ -61,6 +61,7 @@ struct Params {
     float* lam;        // backward: the cotangent stream l~_t = l_t + g_t, same layout as the prefix output
     float* lcarry;     // backward: per chunk the cotangent arriving at its end [- | L1 | L2] (SW)
     float* loc;        // local terms per (sample, interval): [s1 | U_0..U_{QP-1} | V_0..V_{QP-1}], NP each
+    float* coef;       // backward: per (sample, interval) the vector cotangents [ds1 | dU_a | dV_a], NP each
 };
 
 // Width (floats) of one interval's local terms in `loc`.
@@ -1521,7 +1522,7 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
 // four chunks of one sample stacked into M = 128. Chunks run in reverse; the zero-carry pass gives the
 // chunk's local adjoint mu, a look-back over the later chunks (transposed chunk maps from the forward
 // aggregates) gives the cotangent arriving at the chunk's end, and the exact pass writes l~_t for every
-// interval. The gradients are then a parallel map over (sample, interval): grad_kernel.
+// interval. The gradients are then a parallel map over (sample, interval): grad_map_kernel, table_grad_kernel.
 __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
     using namespace tc;
     extern __shared__ unsigned char smem_raw[];
@@ -1862,55 +1863,73 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
 //   dM += l~2 X^T + Z^T S2p + du S1p^T,   du = l~1 + l~2 s1,   ds1 = l~1 + l~2^T u,
 //   dU_a = l~2 V_a,  dV_a = l~2^T U_a,    dF += ds1 dx^T,  dG_a += dU_a dx^T,  dH_a += dV_a dx^T,
 //   dx_t = F^T ds1 + sum_a G_a^T dU_a + H_a^T dV_a.
-// One CTA of 128 threads per (chunk, sample); thread (r, c) owns the 4 x 2 block at rows 4r, columns 2c.
-constexpr int GNT = 128;
+// One CTA of four warps per (chunk, sample), one warp per interval: the CTA's four warps take the chunk's intervals round robin and
+// lane (rb, cb) = (lane / 8, lane % 8) owns the 8 x 4 block at rows 8 rb, columns 4 cb of each 32 x 32 x 32
+// product, reading two float4s of A and one of B per k (32 FMAs per three shared loads). Each warp keeps its
+// own dM block in registers over its intervals (summed in warp order at the end) and writes the interval's
+// vector cotangents [ds1 | dU_a | dV_a] to a stream, from which table_grad_kernel forms the table gradients
+// and dx as small GEMMs per chunk.
+namespace gm {
+constexpr int NW = 4;  // warps per CTA
+constexpr int TB = 8;  // intervals per block of table_grad_kernel
 
-// k-major buffers written by transposed stores are swizzled at float4 granularity (group g of row k at
-// g ^ (k & 7)), which cuts the stores' bank conflicts from 32-way to 4-way; reads apply the same map.
-__device__ __forceinline__ int swz(int k, int i) { return k * NP + ((((i >> 2) ^ (k & 7)) << 2) | (i & 3)); }
+// 32 x 32 buffers with float4 groups permuted per row: element (r, c) at r * 32 + 4 (c / 4 ^ s(r)) + c % 4,
+// s = 0 (MODE 0), r % 8 (MODE 1: transposed scalar stores, 4-way), r / 4 % 8 (MODE 2: the float4 stores of
+// a transposed 8 x 4 block, conflict-free per quarter warp).
+template <int MODE>
+__device__ __forceinline__ int at(int r, int c) {
+    if (MODE == 0) return r * NP + c;
+    const int s = MODE == 1 ? (r & 7) : ((r >> 2) & 7);
+    return r * NP + ((((c >> 2) ^ s) << 2) | (c & 3));
+}
 
-template <bool SA, bool SB>
-__device__ __forceinline__ void gemm42(const float* __restrict__ At, const float* __restrict__ Bm, float acc[4][2],
-                                       int i0, int j0) {
-#pragma unroll 8
+// acc (+)= A B on the lane's 8 x 4 block; A given k-major (A[i][k] at a[at<MA>(k, i)]), B row-major.
+template <int MA, int MB>
+__device__ __forceinline__ void gemm84(const float* __restrict__ a, const float* __restrict__ b, float acc[8][4],
+                                       int rb, int cb) {
+#pragma unroll 4
     for (int k = 0; k < NP; ++k) {
-        const float4 a = *reinterpret_cast<const float4*>(At + (SA ? swz(k, i0) : k * NP + i0));
-        const float2 b = *reinterpret_cast<const float2*>(Bm + (SB ? swz(k, j0) : k * NP + j0));
-        const float av[4] = {a.x, a.y, a.z, a.w};
+        const float4 a0 = *reinterpret_cast<const float4*>(a + at<MA>(k, 8 * rb));
+        const float4 a1 = *reinterpret_cast<const float4*>(a + at<MA>(k, 8 * rb + 4));
+        const float4 bv = *reinterpret_cast<const float4*>(b + at<MB>(k, 4 * cb));
+        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            acc[r][0] = fmaf(av[r], b.x, acc[r][0]);
-            acc[r][1] = fmaf(av[r], b.y, acc[r][1]);
-        }
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(av[r], bw[c], acc[r][c]);
     }
 }
 
-__global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
-    extern __shared__ float smem[];
+__host__ __device__ inline int warp_floats(int QP) { return 4 * MM + 4 * NP + 2 * loc_width(QP); }
+inline size_t map_smem_bytes(const Geom& g) { return sizeof(float) * (2 * (size_t)MM + NW * (size_t)warp_floats(g.QP)); }
+__host__ __device__ inline int coef_stride(int QP) { return loc_width(QP) + 4; }  // padded row of a staged coefficient block
+inline size_t table_smem_bytes(const Geom& g) {
+    const size_t rows = (size_t)loc_width(g.QP);
+    return sizeof(float) * (2 * align4((int)(rows * g.d_in)) + TB * (size_t)coef_stride(g.QP) + align4(TB * g.d_in));
+}
+}  // namespace gm
+
+template <bool FULL>
+__global__ void __launch_bounds__(gm::NW * 32, 2) grad_map_kernel(Params p) {
+    using namespace gm;
+    extern __shared__ __align__(16) float smem[];
     const Geom& g = p.g;
-    const int N = g.N, d = g.d_in, QP = g.QP;
+    const int N = FULL ? NP : g.N;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int i0 = 4 * (tid >> 4), j0 = 2 * (tid & 15);
-    float* Lr = smem;            // l~2 row-major
-    float* Lk = Lr + MM;         // l~2 k-major
-    float* Sr = Lk + MM;         // S2p row-major
-    float* Sk = Sr + MM;         // S2p k-major
-    float* Xk = Sk + MM;         // X k-major
-    float* Zr = Xk + MM;         // Z row-major
-    float* Dr = Zr + MM;         // D row-major
-    float* Dt = Dr + MM;         // D k-major
-    float* vec = Dt + MM;        // L1, S1p, u, du, ds1 (NP each)
-    float* L1 = vec, *S1p = vec + NP, *u = vec + 2 * NP, *du = vec + 3 * NP, *ds1 = vec + 4 * NP;
-    float* UV = vec + 5 * NP;    // dU, dV (NP x QMAX each)
-    float* dU = UV, *dV = UV + NP * QMAX;
-    float* x = UV + 2 * NP * QMAX;                 // 32
-    float* F = x + 32;                             // NP x d
-    float* Gt = F + align4(NP * d);                // QP x NP x d
-    float* Ht = Gt + align4(QP * NP * d);
-    float* tacc = Ht + align4(QP * NP * d);        // (1 + 2 QP) x NP x d
-    const int tabn = (1 + 2 * QP) * NP * d;
-    const int LW = loc_width(QP);
-    float* locb = tacc + align4(tabn);             // two intervals' local terms [s1 | U_a | V_a]
+    const int rb = lane >> 3, cb = lane & 7;
+    const int QP = g.QP, LW = loc_width(QP);
+    float* Dr = smem;     // D row-major
+    float* Dt = Dr + MM;  // D k-major (Dt[k][j] = D[j][k])
+    float* Sr = Dt + MM + warp * warp_floats(QP);  // S2p row-major
+    float* Sk = Sr + MM;  // S2p k-major (MODE 1); then X^T (MODE 2)
+    float* Lr = Sk + MM;  // l~2 row-major; then Z row-major
+    float* Lk = Lr + MM;  // l~2 k-major (MODE 1)
+    float* S1v = Lk + MM;
+    float* L1v = S1v + NP;
+    float* uv = L1v + NP;
+    float* duv = uv + NP;
+    float* locb = duv + NP;  // two intervals' [s1 | U_a | V_a]
 
     const int tile = blockIdx.x;  // c * B + b, the reduction's order
     const int c = tile / g.B, b = tile - c * g.B;
@@ -1918,177 +1937,255 @@ __global__ void __launch_bounds__(GNT) grad_kernel(Params p) {
     const int len = min(g.Lc, g.T - t0);
     {
         const float* m = p.tab_d + (size_t)b * N * N;
-        for (int e = tid; e < MM; e += GNT) {
-            const int i = e / NP, k = e - i * NP;
+        for (int e = tid; e < MM; e += blockDim.x) {
+            const int i = e >> 5, k = e & 31;
             const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
             Dr[e] = v;
             Dt[k * NP + i] = v;
-            Lr[e] = Lk[e] = Sr[e] = Sk[e] = 0.f;
         }
-        const float* f = p.tab_f + (size_t)b * N * d;
-        for (int e = tid; e < NP * d; e += GNT) F[e] = (e / d) < N ? f[e] : 0.f;
-        const size_t gq = (size_t)QP * N * d;
-        for (int e = tid; e < QP * NP * d; e += GNT) {
-            const int a = e / (NP * d), r = e - a * NP * d, i = r / d, cc = r - i * d;
-            const bool ok = i < N;
-            Gt[e] = ok ? p.tab_g[(size_t)b * gq + ((size_t)a * N + i) * d + cc] : 0.f;
-            Ht[e] = ok ? p.tab_h[(size_t)b * gq + ((size_t)a * N + i) * d + cc] : 0.f;
-        }
-        for (int e = tid; e < tabn; e += GNT) tacc[e] = 0.f;
-        for (int e = tid; e < 5 * NP + 2 * NP * QMAX + 32; e += GNT) vec[e] = 0.f;
     }
-    float dM[4][2];
+    __syncthreads();
+    float dM[8][4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) dM[r][0] = dM[r][1] = 0.f;
-    // the next interval's rows, prefetched into registers (entries tid + 128 m of the level-2 block)
-    float pl[8], ps[8], pl1 = 0.f, ps1 = 0.f, px = 0.f;
-    // entry m of this thread: (i, j) = (4m + tid / 32, tid % 32) on the padded 32 x 32 grid
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dM[r][q] = 0.f;
+    // the warp's next interval, in flight while this one runs: lane j holds column j of S_{t-1} and of
+    // l~2_t, entry j of S1_{t-1} and of l~1_t; its local terms are copied in with cp.async
+    float ps[NP], pl[NP], ps1 = 0.f, pl1 = 0.f;
     auto prefetch = [&](int t) {
         const float* lrow = p.lam + ((size_t)b * g.T + t) * g.W;
-        const float* srow = t > 0 ? p.out + ((size_t)b * g.T + t - 1) * g.W : nullptr;
+        const bool has_s = t > 0;
+        const float* srow = has_s ? p.out + ((size_t)b * g.T + t - 1) * g.W : lrow;
+        const bool okj = lane < N;
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-            const int i = 4 * m + warp, j = lane;
-            const bool ok = i < N && j < N;
-            pl[m] = ok ? ldcg(lrow + 1 + N + i * N + j) : 0.f;
-            ps[m] = (ok && srow) ? ldcg(srow + 1 + N + i * N + j) : 0.f;
+        for (int i = 0; i < NP; ++i) {
+            const bool ok = okj && i < N;
+            pl[i] = ok ? ldcg(lrow + 1 + N + i * N + lane) : 0.f;
+            ps[i] = (ok && has_s) ? ldcg(srow + 1 + N + i * N + lane) : 0.f;
         }
-        pl1 = tid < N ? ldcg(lrow + 1 + tid) : 0.f;
-        ps1 = (tid < N && srow) ? ldcg(srow + 1 + tid) : 0.f;
-        px = tid < d ? input_increment(p.path, b, t, tid, g.T, d, g.flags) : 0.f;
+        pl1 = okj ? ldcg(lrow + 1 + lane) : 0.f;
+        ps1 = (okj && has_s) ? ldcg(srow + 1 + lane) : 0.f;
         const float* lsrc = p.loc + ((size_t)b * g.T + t) * LW;
-        float* ldst = locb + ((t - t0) & 1) * LW;
-        for (int v = tid; v < LW / 4; v += GNT) cp_async16(ldst + 4 * v, lsrc + 4 * v);
-        cp_async_commit();
+        float* ldst = locb + (((t - t0) >> 2) & 1) * LW;
+        for (int v = lane; v < LW / 4; v += 32) cp_async16(ldst + 4 * v, lsrc + 4 * v);
     };
-    if (len > 0) prefetch(t0);
-    __syncthreads();
-    for (int k = 0; k < len; ++k) {
+    if (warp < len) prefetch(t0 + warp);
+    cp_async_commit();
+    for (int k = warp; k < len; k += NW) {
         const int t = t0 + k;
-        // (1) the prefetched interval into shared memory; the next one's loads go out
+        __syncwarp();
+        // (1) the interval's rows into the warp's buffers; the warp's next interval goes out
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-            const int i = 4 * m + warp, j = lane;
-            Lr[i * NP + j] = pl[m];
-            Lk[swz(j, i)] = pl[m];
-            Sr[i * NP + j] = ps[m];
-            Sk[swz(j, i)] = ps[m];
+        for (int i = 0; i < NP; ++i) {
+            Sr[at<0>(i, lane)] = ps[i];
+            Sk[at<1>(lane, i)] = ps[i];
+            Lr[at<0>(i, lane)] = pl[i];
+            Lk[at<1>(lane, i)] = pl[i];
         }
-        if (tid < N) {
-            L1[tid] = pl1;
-            S1p[tid] = ps1;
-        }
-        if (tid < d) x[tid] = px;
-        cp_async_wait<0>();
-        __syncthreads();
-        const float* s1 = locb + (k & 1) * LW;  // this interval's s1, U_a = s1 + NP + a NP, V_a = U_a + QP NP
+        S1v[lane] = ps1;
+        L1v[lane] = pl1;
+        if (k + NW < len) prefetch(t + NW);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncwarp();
+        const float* s1 = locb + ((k >> 2) & 1) * LW;  // s1, U_a = s1 + NP + a NP, V_a = U_a + QP NP
         const float* U = s1 + NP;
         const float* V = U + QP * NP;
-        if (k + 1 < len) prefetch(t + 1);
-        // (2) u = M S1p (warp 0), then X = S2p - S2p D^T, Z = l~2 - D^T l~2
-        if (warp == 0) {
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-            for (int kk = 0; kk < NP; kk += 4) {  // (D S1p)[lane] from D k-major: consecutive lanes, no conflicts
-                a0 = fmaf(Dt[kk * NP + lane], S1p[kk], a0);
-                a1 = fmaf(Dt[(kk + 1) * NP + lane], S1p[kk + 1], a1);
-                a2 = fmaf(Dt[(kk + 2) * NP + lane], S1p[kk + 2], a2);
-                a3 = fmaf(Dt[(kk + 3) * NP + lane], S1p[kk + 3], a3);
-            }
-            u[lane] = S1p[lane] - ((a0 + a1) + (a2 + a3));
-        }
+        float* co = p.coef + ((size_t)b * g.T + t) * LW;
+        // (2) vectors: u = M S1p, du = l~1 + l~2 s1, dU_a = l~2 V_a (row `lane` of l~2)
         {
-            float X[4][2] = {}, Z[4][2] = {};
-            gemm42<true, false>(Sk, Dt, X, i0, j0);
-            gemm42<false, false>(Dr, Lr, Z, i0, j0);
+            float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    Xk[swz(j0 + q, i0 + r)] = Sr[(i0 + r) * NP + j0 + q] - X[r][q];
-                    Zr[(i0 + r) * NP + j0 + q] = Lr[(i0 + r) * NP + j0 + q] - Z[r][q];
-                }
-        }
-        __syncthreads();
-        // (3) vector cotangents, one per warp: du, ds1 (then dU, dV) with independent accumulators. Row
-        // `lane` of l~2 is read from the k-major copy and column `lane` from the row-major one, so the 32
-        // lanes always read 32 different banks.
-        if (warp == 0) {
-            float a0 = L1[lane], a1 = 0.f;
-#pragma unroll
-            for (int j = 0; j < NP; j += 2) {
-                a0 = fmaf(Lk[swz(j, lane)], s1[j], a0);
-                a1 = fmaf(Lk[swz(j + 1, lane)], s1[j + 1], a1);
+            for (int kk = 0; kk < NP; kk += 2) {
+                a0 = fmaf(Dt[kk * NP + lane], S1v[kk], a0);
+                a1 = fmaf(Dt[(kk + 1) * NP + lane], S1v[kk + 1], a1);
             }
-            du[lane] = a0 + a1;
-        } else if (warp == 1) {
-            float a0 = L1[lane], a1 = 0.f;
-#pragma unroll
-            for (int i = 0; i < NP; i += 2) {
-                a0 = fmaf(Lr[i * NP + lane], u[i], a0);
-                a1 = fmaf(Lr[(i + 1) * NP + lane], u[i + 1], a1);
-            }
-            ds1[lane] = a0 + a1;
-        } else {
-            // warp 2: dU_a = l~2 V_a (row `lane` of l~2), warp 3: dV_a = l~2^T U_a (column `lane`)
-            const bool rows = warp == 2;
-            const float* W = rows ? V : U;
-            float* out = rows ? dU : dV;
+            uv[lane] = S1v[lane] - (a0 + a1);
             float lv[NP];
 #pragma unroll
-            for (int j = 0; j < NP; ++j) lv[j] = rows ? Lk[swz(j, lane)] : Lr[j * NP + lane];
+            for (int j = 0; j < NP; ++j) lv[j] = Lk[at<1>(j, lane)];
+            a0 = L1v[lane];
+            a1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < NP; j += 2) {
+                a0 = fmaf(lv[j], s1[j], a0);
+                a1 = fmaf(lv[j + 1], s1[j + 1], a1);
+            }
+            duv[lane] = a0 + a1;
             for (int a = 0; a < QP; ++a) {
-                float a0 = 0.f, a1 = 0.f;
+                a0 = 0.f;
+                a1 = 0.f;
 #pragma unroll
                 for (int j = 0; j < NP; j += 2) {
-                    a0 = fmaf(lv[j], W[a * NP + j], a0);
-                    a1 = fmaf(lv[j + 1], W[a * NP + j + 1], a1);
+                    a0 = fmaf(lv[j], V[a * NP + j], a0);
+                    a1 = fmaf(lv[j + 1], V[a * NP + j + 1], a1);
                 }
-                out[lane * QMAX + a] = a0 + a1;
+                co[(1 + a) * NP + lane] = a0 + a1;
             }
         }
-        __syncthreads();
-        // (4) dM += l~2 X^T + Z^T S2p + du S1p^T; table gradients; dx_t
-        gemm42<true, true>(Lk, Xk, dM, i0, j0);
-        gemm42<false, false>(Zr, Sr, dM, i0, j0);
+        __syncwarp();
+        // ds1 = l~1 + l~2^T u, dV_a = l~2^T U_a (column `lane` of l~2)
+        {
+            float lv[NP];
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+            for (int i = 0; i < NP; ++i) lv[i] = Lr[at<0>(i, lane)];
+            float a0 = L1v[lane], a1 = 0.f;
 #pragma unroll
-            for (int q = 0; q < 2; ++q) dM[r][q] = fmaf(du[i0 + r], S1p[j0 + q], dM[r][q]);
-        // table gradients: warp w takes blocks w, w + 4, ...; lane = row
-        for (int blk = warp; blk <= 2 * QP; blk += GNT / 32) {
-            const int i = lane;
-            const float coef = blk == 0 ? ds1[i] : (blk <= QP ? dU[i * QMAX + blk - 1] : dV[i * QMAX + blk - 1 - QP]);
-            float* ta = tacc + ((size_t)blk * NP + i) * d;
-            for (int cc = 0; cc < d; ++cc) ta[cc] = fmaf(coef, x[cc], ta[cc]);
-        }
-        for (int cc = warp; cc < d; cc += GNT / 32) {
-            const int i = lane;
-            float a0 = F[i * d + cc] * ds1[i], a1 = 0.f;
+            for (int i = 0; i < NP; i += 2) {
+                a0 = fmaf(lv[i], uv[i], a0);
+                a1 = fmaf(lv[i + 1], uv[i + 1], a1);
+            }
+            co[lane] = a0 + a1;
             for (int a = 0; a < QP; ++a) {
-                a0 = fmaf(Gt[((size_t)a * NP + i) * d + cc], dU[i * QMAX + a], a0);
-                a1 = fmaf(Ht[((size_t)a * NP + i) * d + cc], dV[i * QMAX + a], a1);
+                a0 = 0.f;
+                a1 = 0.f;
+#pragma unroll
+                for (int i = 0; i < NP; i += 2) {
+                    a0 = fmaf(lv[i], U[a * NP + i], a0);
+                    a1 = fmaf(lv[i + 1], U[a * NP + i + 1], a1);
+                }
+                co[(1 + QP + a) * NP + lane] = a0 + a1;
             }
-            float acc = a0 + a1;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
-            if (lane == 0) p.grad_dx[((size_t)b * g.T + t) * d + cc] = acc;
         }
-        __syncthreads();
+        float acc[8][4];
+        // (3) X = S2p - S2p D^T, stored transposed over the k-major copy of S2p
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
+        gemm84<1, 0>(Sk, Dt, acc, rb, cb);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const float4 sv = *reinterpret_cast<const float4*>(Sr + at<0>(8 * rb + r, 4 * cb));
+            acc[r][0] = sv.x - acc[r][0];
+            acc[r][1] = sv.y - acc[r][1];
+            acc[r][2] = sv.z - acc[r][2];
+            acc[r][3] = sv.w - acc[r][3];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            *reinterpret_cast<float4*>(Sk + at<2>(4 * cb + q, 8 * rb)) =
+                make_float4(acc[0][q], acc[1][q], acc[2][q], acc[3][q]);
+            *reinterpret_cast<float4*>(Sk + at<2>(4 * cb + q, 8 * rb + 4)) =
+                make_float4(acc[4][q], acc[5][q], acc[6][q], acc[7][q]);
+        }
+        // (4) Z = l~2 - D^T l~2, stored row-major over l~2's row-major copy
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
+        gemm84<0, 0>(Dr, Lr, acc, rb, cb);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const float4 lv = *reinterpret_cast<const float4*>(Lr + at<0>(8 * rb + r, 4 * cb));
+            acc[r][0] = lv.x - acc[r][0];
+            acc[r][1] = lv.y - acc[r][1];
+            acc[r][2] = lv.z - acc[r][2];
+            acc[r][3] = lv.w - acc[r][3];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            *reinterpret_cast<float4*>(Lr + at<0>(8 * rb + r, 4 * cb)) =
+                make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        __syncwarp();
+        // (5) dM += l~2 X^T + Z^T S2p + du S1p^T
+        gemm84<1, 2>(Lk, Sk, dM, rb, cb);
+        gemm84<0, 0>(Lr, Sr, dM, rb, cb);
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dM[r][q] = fmaf(duv[8 * rb + r], S1v[4 * cb + q], dM[r][q]);
     }
-    float* part = p.partials + (size_t)tile * (MM + tabn);
+    cp_async_wait<0>();
+    // the warps' dM blocks, summed in warp order
+    __syncthreads();
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int q = 0; q < 2; ++q) part[(i0 + r) * NP + j0 + q] = dM[r][q];
-    for (int e = tid; e < tabn; e += GNT) part[MM + e] = tacc[e];
+    for (int r = 0; r < 8; ++r)
+        *reinterpret_cast<float4*>(Sr + at<0>(8 * rb + r, 4 * cb)) = make_float4(dM[r][0], dM[r][1], dM[r][2], dM[r][3]);
+    __syncthreads();
+    float* part = p.partials + (size_t)tile * (MM + (size_t)LW * g.d_in);
+    const float* base = Dt + MM;
+    for (int e = tid; e < MM; e += blockDim.x) {
+        float v = 0.f;
+        for (int w = 0; w < NW; ++w) v += base[w * warp_floats(QP) + e];
+        part[e] = v;
+    }
 }
 
-static size_t grad_smem_bytes(const Geom& g) {
-    const size_t f = 8 * (size_t)MM + 5 * NP + 2 * NP * QMAX + 32 + align4(NP * g.d_in) + 2 * align4(g.QP * NP * g.d_in) +
-                     align4((1 + 2 * g.QP) * NP * g.d_in) + 2 * (size_t)loc_width(g.QP);
-    return f * sizeof(float);
+// Table gradients and dx from the vector cotangents of a chunk: with the coefficient rows
+// c_t = [ds1 | dU_a | dV_a] and the table rows T = [F | G_a | H_a] (one row per (block, state index)),
+//   dT += sum_t c_t dx_t^T,   dx_t = T^T c_t,
+// in blocks of TB intervals, every sum in a fixed order.
+__global__ void __launch_bounds__(128) table_grad_kernel(Params p) {
+    using namespace gm;
+    extern __shared__ __align__(16) float smem[];
+    const Geom& g = p.g;
+    const int N = g.N, d = g.d_in, QP = g.QP, LW = loc_width(QP), CS = coef_stride(QP);
+    const int tid = threadIdx.x;
+    float* Tab = smem;                      // LW x d
+    float* tacc = Tab + align4(LW * d);     // LW x d
+    float* cbuf = tacc + align4(LW * d);    // TB x CS
+    float* xb = cbuf + TB * CS;             // TB x d
+    const int tile = blockIdx.x;
+    const int c = tile / g.B, b = tile - c * g.B;
+    const int t0 = c * g.Lc;
+    const int len = min(g.Lc, g.T - t0);
+    for (int e = tid; e < LW * d; e += blockDim.x) {
+        const int row = e / d, cc = e - row * d;
+        const int blk = row / NP, i = row - blk * NP;
+        float v = 0.f;
+        if (i < N) {
+            if (blk == 0)
+                v = p.tab_f[((size_t)b * N + i) * d + cc];
+            else if (blk <= QP)
+                v = p.tab_g[(((size_t)b * QP + blk - 1) * N + i) * d + cc];
+            else
+                v = p.tab_h[(((size_t)b * QP + blk - 1 - QP) * N + i) * d + cc];
+        }
+        Tab[e] = v;
+        tacc[e] = 0.f;
+    }
+    for (int k0 = 0; k0 < len; k0 += TB) {
+        const int n = min(TB, len - k0);
+        __syncthreads();
+        const float* src = p.coef + ((size_t)b * g.T + t0 + k0) * LW;
+        for (int v = tid; v < n * (LW / 4); v += blockDim.x) {
+            const int kk = v / (LW / 4), q = v - kk * (LW / 4);
+            cp_async16(cbuf + kk * CS + 4 * q, src + (size_t)kk * LW + 4 * q);
+        }
+        cp_async_commit();
+        for (int e = tid; e < n * d; e += blockDim.x) {
+            const int kk = e / d, cc = e - kk * d;
+            xb[e] = input_increment(p.path, b, t0 + k0 + kk, cc, g.T, d, g.flags);
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+        for (int e = tid; e < LW; e += blockDim.x) {
+            for (int cc = 0; cc < d; ++cc) {
+                float acc = tacc[e * d + cc];
+                for (int kk = 0; kk < n; ++kk) acc = fmaf(cbuf[kk * CS + e], xb[kk * d + cc], acc);
+                tacc[e * d + cc] = acc;
+            }
+        }
+        for (int q = tid; q < n * d; q += blockDim.x) {
+            const int kk = q / d, cc = q - kk * d;
+            const float* cr = cbuf + kk * CS;
+            float a0 = 0.f, a1 = 0.f;
+            for (int e = 0; e < LW; e += 2) {
+                a0 = fmaf(Tab[e * d + cc], cr[e], a0);
+                a1 = fmaf(Tab[(e + 1) * d + cc], cr[e + 1], a1);
+            }
+            p.grad_dx[((size_t)b * g.T + t0 + k0 + kk) * d + cc] = a0 + a1;
+        }
+    }
+    __syncthreads();
+    float* part = p.partials + (size_t)tile * (MM + (size_t)LW * d) + MM;
+    for (int e = tid; e < LW * d; e += blockDim.x) part[e] = tacc[e];
 }
+
 
 // Deterministic per-sample reduction over chunks, compacted to the real dimensions.
 __global__ void reduce_kernel(Params p, float* grad_d, float* grad_f, float* grad_g, float* grad_h) {
@@ -2177,7 +2274,7 @@ static WsLayout fwd_layout(const Geom& g) {
     o += slots;
     L.pw = o;
     o += al256(sizeof(float) * (size_t)g.B * 2 * MM);
-    L.loc = o;  // the intervals' local terms, written by local_kernel and read by both chains and grad_kernel
+    L.loc = o;  // the intervals' local terms, written by local_kernel and read by both chains and grad_map_kernel
     o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
     L.total = o;
     return L;
@@ -2201,6 +2298,8 @@ static WsLayout bwd_layout(const Geom& g) {
     o += slots;
     L.pw = o;     // the cotangent stream l~_t, laid out as the prefix output
     o += al256(sizeof(float) * (size_t)g.B * g.T * g.W);
+    L.loc = o;    // the vector cotangents [ds1 | dU_a | dV_a] per interval
+    o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
     L.total = o;
     return L;
 }
@@ -2342,12 +2441,18 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         bwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     }
+    p.coef = (float*)(ws + L.loc);
     {
-        const size_t smem = grad_smem_bytes(g);
-        if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
-        cudaFuncSetAttribute(grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(grad_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-        grad_kernel<<<g.C * g.B, GNT, smem, s>>>(p);
+        const size_t smem = gm::map_smem_bytes(g);
+        const size_t tsmem = gm::table_smem_bytes(g);
+        if (smem > 227 * 1024 || tsmem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+        auto* kern = g.N == NP ? grad_map_kernel<true> : grad_map_kernel<false>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+        kern<<<g.C * g.B, gm::NW * 32, smem, s>>>(p);
+        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        cudaFuncSetAttribute(table_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
+        table_grad_kernel<<<g.C * g.B, 128, tsmem, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     }
     const size_t total = (size_t)g.B * (g.N * g.N + (1 + 2 * g.QP) * g.N * g.d_in);

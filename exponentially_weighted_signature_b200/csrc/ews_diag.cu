@@ -588,27 +588,19 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
                 chen_step_u(tb, dys + k * NP, i0, j0, S, dd);
                 emit_row_all(orow, S, Nr, i0, j0);
             }
-            continue;
-        }
-        for (int k = 0; k < len; ++k, orow += g.W) {
-            float fr[RI], fc[RJ];
-            if (NU) tb.at(p, dts[k]);
-            const bool bp = basepoint && (t0 + k == 0);
-            step_flow(tb, bp, fr, fc);
-            if (NU || bp) {
+        } else {
+            // per-interval clock (no basepoint interval): the tables and pair complements of every step
+            for (int k = 0; k < len; ++k, orow += g.W) {
+                float fr[RI], fc[RJ];
+                tb.at(p, dts[k]);
+                step_flow(tb, false, fr, fc);
 #pragma unroll
                 for (int r = 0; r < RI; ++r)
 #pragma unroll
                     for (int c = 0; c < RJ; ++c) dd[r][c] = comp_mul(fr[r], fc[c]);
+                chen_step_emit(tb, dys + k * NP, i0, j0, S, fr, fc, dd, false);
+                emit_row(orow, S, Nr, i0, j0, tj, lane);
             }
-            chen_step_emit(tb, dys + k * NP, i0, j0, S, fr, fc, dd, bp);
-            if (bp && !NU) {
-#pragma unroll
-                for (int r = 0; r < RI; ++r)
-#pragma unroll
-                    for (int c = 0; c < RJ; ++c) dd[r][c] = comp_mul(tb.dr[r], tb.dc[c]);
-            }
-            emit_row(orow, S, Nr, i0, j0, tj, lane);
         }
     }
 }
