@@ -98,11 +98,13 @@ def _diag_setup(cfg, rank, world, device, precision, batch=None):
     d_in = x_host.shape[-1]
     in_bytes = 2 if x_host.dtype == torch.bfloat16 else 4
     # algorithmic bytes per unit (one sample-interval) of each kernel: inputs read once, outputs written
-    # once; the backward reads the output gradient and writes the input-increment gradient
+    # once; the backward reads the output gradient and the saved prefix rows (the forward's residuals: the
+    # reference's custom VJP keeps `out` for its backward, ews/core/kernels/pallas_combine.py:1691-1695)
+    # and writes the input-increment gradient
     out_row = 4 * (1 + D) if readout == "prefix" else 0
     alg = {
         "ews_diag_fwd": in_bytes * d_in + out_row,
-        "ews_diag_bwd": in_bytes * d_in + out_row + 4 * d_in,
+        "ews_diag_bwd": in_bytes * d_in + 2 * out_row + 4 * d_in,
     }
     meta = dict(B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout=readout, dtype="f32",
                 precision=("bf16 increments, f32 accumulation" if in_bytes == 2 else "f32"))
