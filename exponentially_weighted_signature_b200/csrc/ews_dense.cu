@@ -1887,7 +1887,7 @@ __device__ __forceinline__ int at(int r, int c) {
 template <int MA, int MB>
 __device__ __forceinline__ void gemm84(const float* __restrict__ a, const float* __restrict__ b, float acc[8][4],
                                        int rb, int cb) {
-#pragma unroll 4
+#pragma unroll 8
     for (int k = 0; k < NP; ++k) {
         const float4 a0 = *reinterpret_cast<const float4*>(a + at<MA>(k, 8 * rb));
         const float4 a1 = *reinterpret_cast<const float4*>(a + at<MA>(k, 8 * rb + 4));
