@@ -37,6 +37,18 @@ KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 3, "e
 TERMINAL_KERNELS = {"ews_diag_fwd": 2, "ews_diag_bwd": 4}
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per sample-interval of each entry point's
+# kernels, from one ncu capture of a smaller case whose streams exceed L2 (config 1 at B = 64, config 2 at
+# B = 4, config 5 at B = 128; the commands and per-kernel figures are in profiles/ews_dense_config2.md,
+# profiles/kernels_configs_1_3_5.md and profiles/ews_diag_terminal_config5.md). The streams grow in
+# proportion to the sample-intervals, so `roofline.traffic` is this figure times the launch's units.
+TRAFFIC_PER_UNIT = {
+    "config1": {"ews_diag_fwd": 926.0, "ews_diag_bwd": 3227.0},
+    "config2": {"ews_dense_fwd": 6368.0, "ews_dense_bwd": 24801.0},
+    "config5": {"ews_diag_fwd": 78.0, "ews_diag_bwd": 90.0},
+}
+
+
 def _peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -545,14 +557,9 @@ def run_b200(args, rank, world, local_rank):
     _, tflops, _ = _peaks()
     peak = tflops if tensor_bound else hbm
     traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            tr = json.load(f)
-        per_unit = tr.get(args.config, {}).get(dom_name)
-        if per_unit:
-            traffic = per_unit * dom_units
-    except Exception:
-        pass
+    per_unit = TRAFFIC_PER_UNIT.get(args.config, {}).get(dom_name)
+    if per_unit:
+        traffic = per_unit * dom_units
 
     # end to end: host inputs copied in, loss read back, every step
     xh = setup["x_host"].pin_memory()
