@@ -103,7 +103,7 @@ def _diag_setup(cfg, rank, world, device, precision, batch=None):
 
     def step(x, clock):
         out = layer(x, clock, readout=readout, lift=lift.full_matrix(), increments=increments)
-        loss = (out * w).sum()
+        loss = torch.dot(out.reshape(-1), w.reshape(-1))  # <out, w>: one read of out; its backward writes w once
         loss.backward()
         return loss
 
@@ -154,7 +154,7 @@ def _dense_setup(cfg, rank, world, device, precision, batch=None):
 
     def step(x, clock):
         out = layer(x, clock, readout="prefix", lift=lift.full_matrix())
-        loss = (out * w).sum()
+        loss = torch.dot(out.reshape(-1), w.reshape(-1))  # <out, w>: one read of out; its backward writes w once
         loss.backward()
         return loss
 
@@ -199,7 +199,7 @@ def _block_setup(cfg, rank, world, device, precision, batch=None):
     def step(x, clock):
         clock = clock.detach().requires_grad_(True)  # the input-dependent clock: d/dtheta flows back
         out = layer(x, clock, readout="prefix", lift=lift.full_matrix())
-        loss = (out * w).sum()
+        loss = torch.dot(out.reshape(-1), w.reshape(-1))  # <out, w>: one read of out; its backward writes w once
         loss.backward()
         return loss
 
