@@ -54,31 +54,26 @@ __device__ __forceinline__ void publish(int* flag, int value) {
 
 // Warp-wide bounded wait for a slot's flag to reach at least `want` (kFlagAgg: any published value;
 // kFlagIncl: the inclusive value). Returns the flag value, or -1 when the wait ran out (the error word is
-// then set) or another tile already failed. Never spins without a limit.
+// then set) or another tile already failed. Never spins without a limit. Every lane issues the acquire
+// load (one request for the warp), so each lane's later reads of the slot are ordered after the
+// publisher's writes; the loop follows lane 0's value.
 __device__ __forceinline__ int wait_slot(const int* flag, DeviceStatus* st, int limit, int tile, int want = kFlagAgg) {
     int v = kFlagEmpty;
-    if ((threadIdx.x & 31) == 0) {
-        unsigned ns = 32;
-        int it = 0;
-        for (; it < limit; ++it) {
-            v = ld_acquire(flag);
-            if (v >= want) break;
-            if (*((volatile int*)&st->error) != 0) {
-                v = -1;
-                break;
-            }
-            __nanosleep(ns);
-            if (ns < 256) ns <<= 1;
-        }
-        if (v >= 0 && v < want) {
-            if (atomicCAS(&st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) st->err_tile = tile;
+    unsigned ns = 32;
+    for (int it = 0; it < limit; ++it) {
+        v = __shfl_sync(kFull, ld_acquire(flag), 0);
+        if (v >= want) break;
+        if (__shfl_sync(kFull, *((volatile int*)&st->error), 0) != 0) {
             v = -1;
+            break;
         }
+        __nanosleep(ns);
+        if (ns < 256) ns <<= 1;
     }
-    v = __shfl_sync(kFull, v, 0);
-    // every lane acquires the flag itself (the value is at least what lane 0 saw), so each lane's reads of the
-    // slot are ordered after the publisher's writes without a full fence
-    if (v >= 0) (void)ld_acquire(flag);
+    if (v >= 0 && v < want) {
+        if ((threadIdx.x & 31) == 0 && atomicCAS(&st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) st->err_tile = tile;
+        v = -1;
+    }
     return v;
 }
 
