@@ -804,7 +804,40 @@ __device__ __forceinline__ void apply_JT_e3(A3& a, const E3& G, int i, int jb) {
     apply_JT(a, G.D, G.S1, G.S2b, i, jb);
 }
 
-// Adds gradient row t (real dimension N) to the lane's cotangent.
+// The backward stages state and gradient rows with levels 0-2 as in the row and the level-3 rows (index i)
+// N^2 + 4 floats apart: the lanes' reads of one staged row then fall on different banks (at a stride of
+// N^2 = 64, sixteen lanes shared a bank).
+__host__ __device__ inline int row_floats_padded(int N) { return 1 + N + N * N + N * (N * N + 4); }
+
+// Position of row element e in the padded layout; inv = ceil(2^16 / N^2) turns the division by N^2 into a
+// multiply and shift, exact for the at most 512 level-3 entries.
+__device__ __forceinline__ int pad_index(int e, int off3, unsigned inv) {
+    return e < off3 ? e : e + 4 * (int)(((unsigned)(e - off3) * inv) >> 16);
+}
+
+// warp_load_span of one state row (real dimension N) into the padded layout (whole warp).
+__device__ void warp_load_row_padded(float* __restrict__ s, const float* __restrict__ g, int N) {
+    const int lane = threadIdx.x & 31;
+    const int N2 = N * N, off3 = 1 + N + N2, n = off3 + N * N2;
+    const unsigned inv = (65536u + N2 - 1) / N2;
+    int head = (int)(((16u - ((uintptr_t)g & 15u)) & 15u) >> 2);
+    if (head > n) head = n;
+    if (lane < head) s[pad_index(lane, off3, inv)] = __ldcg(g + lane);
+    const int nvec = (n - head) >> 2;
+    const float4* gv = reinterpret_cast<const float4*>(g + head);
+    for (int v = lane; v < nvec; v += 32) {
+        const float4 q = __ldcg(gv + v);
+        const int e = head + 4 * v;
+        s[pad_index(e, off3, inv)] = q.x;
+        s[pad_index(e + 1, off3, inv)] = q.y;
+        s[pad_index(e + 2, off3, inv)] = q.z;
+        s[pad_index(e + 3, off3, inv)] = q.w;
+    }
+    const int done = head + 4 * nvec;
+    if (lane < n - done) s[pad_index(done + lane, off3, inv)] = __ldcg(g + done + lane);
+}
+
+// Adds gradient row t (real dimension N, padded layout) to the lane's cotangent.
 __device__ __forceinline__ void add_grad_row(A3& a, const float* row, int N, int i, int jb) {
     const int N2 = N * N;
 #pragma unroll
@@ -818,19 +851,19 @@ __device__ __forceinline__ void add_grad_row(A3& a, const float* row, int N, int
                 a.L2a[r] += row[1 + N + i * N + j];
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
-                    if (k < N) a.L3[r][k] += row[1 + N + N2 + i * N2 + j * N + k];
+                    if (k < N) a.L3[r][k] += row[1 + N + N2 + i * (N2 + 4) + j * N + k];
             }
         }
     }
 }
 
-// Entry (i, j) of level 2 / (i, j, k) of level 3 from a staged state row, zero beyond N.
+// Entry (i, j) of level 2 / (i, j, k) of level 3 from a staged state row (padded layout), zero beyond N.
 __device__ __forceinline__ float row_s1(const float* row, int N, int k) { return k < N ? row[1 + k] : 0.f; }
 __device__ __forceinline__ float row_s2(const float* row, int N, int i, int j) {
     return (i < N && j < N) ? row[1 + N + i * N + j] : 0.f;
 }
 __device__ __forceinline__ float row_s3(const float* row, int N, int i, int j, int k) {
-    return (i < N && j < N && k < N) ? row[1 + N + N * N + i * N * N + j * N + k] : 0.f;
+    return (i < N && j < N && k < N) ? row[1 + N + N * N + i * (N * N + 4) + j * N + k] : 0.f;
 }
 
 // Adjoint of expm at a 2x2 block: out = L(Y, G) with Y = X^T, the Frechet derivative of expm at Y in
@@ -881,10 +914,13 @@ struct AdjBuf {
     float* dV;    // NPAIR x 8
     float* yz;    // 2 x KQ x 8: y_r[j] = sum_k ds2[j][k] b_r[k], z_p[k] = sum_j b_p[j] ds2[j][k]
     float* db;    // KQ x 8
-    static constexpr int floats = 512 + 64 + 8 + 64 + KQ * 64 + NPAIR * 8 + 2 * KQ * 8 + KQ * 8;
+    // l3' rows (index i) are L3S = 68 floats apart: the lanes' stores (rows i, columns 16 jb..) and the
+    // float4 reads of a row per lane land on different banks (a 64-float stride put them all on one)
+    static constexpr int L3S = 68;
+    static constexpr int floats = 8 * L3S + 64 + 8 + 64 + KQ * 64 + NPAIR * 8 + 2 * KQ * 8 + KQ * 8;
     __device__ AdjBuf(float* base) {
         L3 = base;
-        L2 = L3 + 512;
+        L2 = L3 + 8 * L3S;
         ds1 = L2 + 64;
         ds2 = ds1 + 8;
         dT = ds2 + 64;
@@ -906,7 +942,7 @@ __device__ void letters_adjoint(const Params& p, const Loc& lc, const AdjBuf& ab
         const int e = lane + 32 * h2;
         float col[8];
 #pragma unroll
-        for (int ii = 0; ii < 8; ++ii) col[ii] = ab.L3[ii * 64 + e];
+        for (int ii = 0; ii < 8; ++ii) col[ii] = ab.L3[ii * AdjBuf::L3S + e];
         for (int pp = 0; pp <= q; ++pp) {
             float acc = 0.f;
 #pragma unroll
@@ -948,7 +984,7 @@ __device__ void letters_adjoint(const Params& p, const Loc& lc, const AdjBuf& ab
         float acc = 0.f;
         // slot 1 of level 3: sum_{jk} l3[a][j][k] T[p][j][k]
         {
-            const float4* Lr = reinterpret_cast<const float4*>(ab.L3 + a * 64);
+            const float4* Lr = reinterpret_cast<const float4*>(ab.L3 + a * AdjBuf::L3S);
             const float4* Tr = reinterpret_cast<const float4*>(lc.T + pp * 64);
 #pragma unroll 4
             for (int v = 0; v < 16; ++v) {
@@ -1007,7 +1043,7 @@ __device__ void bwd_step(const Params& p, const float* Ablk, const Loc& lc, cons
     for (int r = 0; r < 2; ++r) {
         ab.L2[i * 8 + 2 * jb + r] = a.L2a[r];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) ab.L3[i * 64 + (2 * jb + r) * 8 + k] = a.L3[r][k];
+        for (int k = 0; k < 8; ++k) ab.L3[i * AdjBuf::L3S + (2 * jb + r) * 8 + k] = a.L3[r][k];
     }
     // F1 = M S1p (all)
     float S1p[8], F1[8];
@@ -1345,7 +1381,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         float* lst = dxs + g.b_loc;
         fetch_local(p, b, t0 + len - 1, lst + ((len - 1) & 1) * LROW);
         for (int k = len - 1; k >= 0; --k) {
-            warp_load_span(gst, p.grad_out + ((size_t)b * g.T + t0 + k) * g.W, g.W);
+            warp_load_row_padded(gst, p.grad_out + ((size_t)b * g.T + t0 + k) * g.W, g.N);
             cp_async_wait<0>();
             __syncwarp();
             if (k >= 1) fetch_local(p, b, t0 + k - 1, lst + ((k - 1) & 1) * LROW);
@@ -1398,11 +1434,11 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         A3 a = lam;
         for (int k = len - 1; k >= 0; --k) {
             const int t = t0 + k;
-            warp_load_span(gst, p.grad_out + ((size_t)b * g.T + t) * g.W, g.W);
+            warp_load_row_padded(gst, p.grad_out + ((size_t)b * g.T + t) * g.W, g.N);
             if (t > 0) {
-                warp_load_span(sst, p.out + ((size_t)b * g.T + t - 1) * g.W, g.W);
+                warp_load_row_padded(sst, p.out + ((size_t)b * g.T + t - 1) * g.W, g.N);
             } else {
-                for (int e = lane; e < g.W; e += 32) sst[e] = 0.f;
+                for (int e = lane; e < row_floats_padded(g.N); e += 32) sst[e] = 0.f;
             }
             build_local(p, Ablk, dys + k * NB, dts[k], lc, true);
             add_grad_row(a, gst, g.N, i, jb);
@@ -1515,8 +1551,8 @@ int make_geom(const ews_block_args* a, Geom* g) {
     g->b_loc = g->b_dyg + ys;
     g->b_adj = g->b_loc + align4(Loc::floats);
     g->b_gst = g->b_adj + align4(AdjBuf::floats);
-    g->b_sst = g->b_gst + align4(std::max(g->W, g->Lc * g->d_in));
-    g->b_per_warp = g->b_sst + align4(g->W);
+    g->b_sst = g->b_gst + align4(std::max(row_floats_padded(g->N), g->Lc * g->d_in));
+    g->b_per_warp = g->b_sst + align4(row_floats_padded(g->N));
     return EWS_OK;
 }
 
