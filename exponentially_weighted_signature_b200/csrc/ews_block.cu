@@ -310,10 +310,13 @@ struct Loc {
 };
 
 // Builds the interval's local terms in lc (whole warp): dy (8, in shared memory), clock step h, blocks A.
+// QT >= 0 fixes the series order at compile time (the loops unroll and the coefficients are read at fixed
+// offsets); QT = -1 reads it from the parameters.
+template <int QT = -1>
 __device__ void build_local(const Params& p, const float* Ablk, const float* dy, float h, const Loc& lc,
                             bool level3 = true) {
     const int lane = threadIdx.x & 31;
-    const int q = p.g.q;
+    const int q = QT >= 0 ? QT : p.g.q;
     // flow complement of the interval, one block per lane 0..3
     if (lane < 4) {
         const float* A = Ablk + 4 * lane;
@@ -394,9 +397,10 @@ __device__ void build_local(const Params& p, const float* Ablk, const float* dy,
 }
 
 // The lane's view of the local element of the interval in lc.
+template <int QT = -1>
 __device__ __forceinline__ void local_view(const Params& p, const Loc& lc, int i, int jb, float s2a[2],
                                            float s2b[2][8], float s3[2][8]) {
-    const int q = p.g.q;
+    const int q = QT >= 0 ? QT : p.g.q;
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int j = 2 * jb + r;
@@ -498,6 +502,7 @@ __device__ void load_chunk(const Params& p, const float* liftS, float* dxs, floa
 // The local element of every interval, a parallel map ahead of the chains: one warp per chunk of one
 // sample builds each interval's flow complement, letters and series terms (build_local, as the chain did)
 // and writes [D | s1 | s2 | s3] (s3[i][j][k] at 88 + 64 i + 8 j + k) to p.loc.
+template <int QT>
 __global__ void __launch_bounds__(kWarps * 32) local_kernel(Params p) {
     extern __shared__ float smem[];
     const Geom& g = p.g;
@@ -521,9 +526,9 @@ __global__ void __launch_bounds__(kWarps * 32) local_kernel(Params p) {
     const int n = min(g.Lc, g.T - t0);
     load_chunk(p, liftS, dxs, dys, dts, b, t0, n);
     for (int k = 0; k < n; ++k) {
-        build_local(p, Ablk, dys + k * NB, dts[k], lc);
+        build_local<QT>(p, Ablk, dys + k * NB, dts[k], lc);
         float s2a[2], s2b[2][8], s3[2][8];
-        local_view(p, lc, i, jb, s2a, s2b, s3);
+        local_view<QT>(p, lc, i, jb, s2a, s2b, s3);
         float* row = p.loc + ((size_t)b * g.T + t0 + k) * LROW;
         if (lane < 16) row[lane] = lc.D[lane];
         if (lane < 8) row[16 + lane] = lc.s1[lane];
@@ -1666,8 +1671,13 @@ extern "C" int ews_block_fwd(const ews_block_args* a, ews_stream_t stream) {
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     {
         // every interval's local element first: a parallel map
-        cudaFuncSetAttribute(local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        local_kernel<<<(g.B * g.C + kWarps - 1) / kWarps, kWarps * 32, smem, s>>>(p);
+        using LK = void (*)(Params);
+        static const LK kernels[KQ] = {local_kernel<0>, local_kernel<1>, local_kernel<2>,
+                                       local_kernel<3>, local_kernel<4>, local_kernel<5>,
+                                       local_kernel<6>, local_kernel<7>, local_kernel<8>};
+        const LK lk = kernels[g.q];
+        cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        lk<<<(g.B * g.C + kWarps - 1) / kWarps, kWarps * 32, smem, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     }
     cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
