@@ -1345,6 +1345,7 @@ __device__ __forceinline__ void mu_step_row(const float* row, A3& a, int i, int 
     apply_JT(a, row, row + 16, U2b, i, jb);
 }
 
+template <int QT>
 __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     extern __shared__ float smem[];
     const Geom& g = p.g;
@@ -1445,7 +1446,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
             } else {
                 for (int e = lane; e < row_floats_padded(g.N); e += 32) sst[e] = 0.f;
             }
-            build_local(p, Ablk, dys + k * NB, dts[k], lc, true);
+            build_local<QT>(p, Ablk, dys + k * NB, dts[k], lc, true);
             add_grad_row(a, gst, g.N, i, jb);
             bwd_step(p, Ablk, lc, ab, sst, dts[k], a, bo, dyg + k * NB, dtg + k, i, jb);
         }
@@ -1729,15 +1730,19 @@ extern "C" int ews_block_bwd(const ews_block_args* a, ews_stream_t stream) {
     series_coefficients(g.q, &p);
     const size_t smem = bwd_smem(g);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
-    cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    using BK = void (*)(Params);
+    static const BK kernels[KQ] = {bwd_kernel<0>, bwd_kernel<1>, bwd_kernel<2>, bwd_kernel<3>, bwd_kernel<4>,
+                                   bwd_kernel<5>, bwd_kernel<6>, bwd_kernel<7>, bwd_kernel<8>};
+    const BK bk = kernels[g.q];  // the series order fixed at compile time for the letters of the exact pass
+    cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(bk, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     int per_sm = 0;
-    per_sm = resident_ctas((const void*)bwd_kernel, kWarps * 32, smem);
+    per_sm = resident_ctas((const void*)bk, kWarps * 32, smem);
     if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
     int grid = per_sm * num_sms();
     const int need = (g.ntiles + kWarps - 1) / kWarps;
     if (grid > need) grid = need;
-    bwd_kernel<<<grid, kWarps * 32, smem, s>>>(p);
+    bk<<<grid, kWarps * 32, smem, s>>>(p);
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     reduce_kernel<<<1, 256, 0, s>>>(p, a->grad_blocks, a->grad_lift);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
