@@ -937,9 +937,10 @@ struct AdjBuf {
 
 // The gradient of the interval's letters db[p][a] from ds1, ds2 (in ab) and ds3 = l3' (ab.L3), through
 // the series assembly s1 = sum c1 b, s2 = sum c2 b (x) b, s3 = sum_p b_p (x) T_p (whole warp).
+template <int QT = -1>
 __device__ void letters_adjoint(const Params& p, const Loc& lc, const AdjBuf& ab) {
     const int lane = threadIdx.x & 31;
-    const int q = p.g.q;
+    const int q = QT >= 0 ? QT : p.g.q;
     const int npair = (q + 1) * (q + 2) / 2;
     // dT[p][j][k] = sum_i b_p[i] l3[i][j][k]; y, z for level 2
 #pragma unroll
@@ -1034,6 +1035,7 @@ struct BwdOut {
 // One exact adjoint step at interval t. a holds l' (gradient row added); prow is S_{t-1} (real dims);
 // lc holds the interval's local terms. Accumulates dA partials, writes dy_t (dyg, lanes 0..7) and
 // dL/dh_t (lane 0 to *dtg); turns a into the cotangent of S_{t-1}.
+template <int QT = -1>
 __device__ void bwd_step(const Params& p, const float* Ablk, const Loc& lc, const AdjBuf& ab, const float* prow,
                          float h, A3& a, BwdOut& bo, float* dyg, float* dtg, int i, int jb) {
     const int lane = threadIdx.x & 31;
@@ -1261,7 +1263,7 @@ __device__ void bwd_step(const Params& p, const float* Ablk, const Loc& lc, cons
     }
     // ---- letters: db, then the letter recursion on lanes 0..7
     __syncwarp();
-    letters_adjoint(p, lc, ab);
+    letters_adjoint<QT>(p, lc, ab);
     float dX[16];
 #pragma unroll
     for (int blk = 0; blk < 4; ++blk) {
@@ -1275,9 +1277,10 @@ __device__ void bwd_step(const Params& p, const float* Ablk, const Loc& lc, cons
         const float* A = Ablk + 4 * blk;
         const float xd = -h * (u ? A[3] : A[0]);   // X[a][a]
         const float xt = -h * (u ? A[1] : A[2]);   // X[a^1][a]
-        float cur = ab.db[p.g.q * 8 + ar];
+        const int q = QT >= 0 ? QT : p.g.q;
+        float cur = ab.db[q * 8 + ar];
         float dxa0 = 0.f, dxa1 = 0.f;  // dX[a][2blk], dX[a][2blk+1]
-        for (int pp = p.g.q; pp >= 1; --pp) {
+        for (int pp = q; pp >= 1; --pp) {
             const float inv = 1.f / (float)pp;
             const float curo = __shfl_xor_sync(kFull, cur, 1);
             dxa0 = fmaf(cur * inv, lc.b[(pp - 1) * 8 + 2 * blk], dxa0);
@@ -1448,7 +1451,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
             }
             build_local<QT>(p, Ablk, dys + k * NB, dts[k], lc, true);
             add_grad_row(a, gst, g.N, i, jb);
-            bwd_step(p, Ablk, lc, ab, sst, dts[k], a, bo, dyg + k * NB, dtg + k, i, jb);
+            bwd_step<QT>(p, Ablk, lc, ab, sst, dts[k], a, bo, dyg + k * NB, dtg + k, i, jb);
         }
         // ---- chunk outputs: dx = lift^T dy, dtheta, per-tile partials (dA, dlift)
         __syncwarp();
