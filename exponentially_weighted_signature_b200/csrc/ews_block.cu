@@ -1494,14 +1494,25 @@ __global__ void reduce_kernel(Params p, float* grad_blocks, float* grad_lift) {
     const int stride = 16 + NB * g.d_in;
     const int K = g.N / 2;
     const int total = 4 * K + (grad_lift ? g.N * g.d_in : 0);
-    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    // one CTA per output entry: each thread sums a strided set of tiles in order, then a fixed tree
+    __shared__ float red[256];
+    for (int e = blockIdx.x; e < total; e += gridDim.x) {
         const int off = e < 4 * K ? e : 16 + (e - 4 * K);
         float acc = 0.f;
-        for (int t = 0; t < g.ntiles; ++t) acc += p.partials[(size_t)t * stride + off];
-        if (e < 4 * K)
-            grad_blocks[e] = acc;
-        else
-            grad_lift[e - 4 * K] = acc;
+        for (int t = threadIdx.x; t < g.ntiles; t += blockDim.x) acc += ldcg(p.partials + (size_t)t * stride + off);
+        red[threadIdx.x] = acc;
+        __syncthreads();
+        for (int h = blockDim.x / 2; h > 0; h >>= 1) {
+            if (threadIdx.x < h) red[threadIdx.x] += red[threadIdx.x + h];
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) {
+            if (e < 4 * K)
+                grad_blocks[e] = red[0];
+            else
+                grad_lift[e - 4 * K] = red[0];
+        }
+        __syncthreads();
     }
 }
 
@@ -1747,6 +1758,6 @@ extern "C" int ews_block_bwd(const ews_block_args* a, ews_stream_t stream) {
     if (grid > need) grid = need;
     bk<<<grid, kWarps * 32, smem, s>>>(p);
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
-    reduce_kernel<<<1, 256, 0, s>>>(p, a->grad_blocks, a->grad_lift);
+    reduce_kernel<<<2 * g.N + (a->grad_lift ? g.N * g.d_in : 0), 256, 0, s>>>(p, a->grad_blocks, a->grad_lift);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
