@@ -39,12 +39,13 @@ TERMINAL_KERNELS = {"ews_diag_fwd": 2, "ews_diag_bwd": 4}
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per sample-interval of each entry point's
 # kernels, from one ncu capture of a smaller case whose streams exceed L2 (config 1 at B = 64, config 2 at
-# B = 4, config 5 at B = 128; the commands and per-kernel figures are in profiles/ews_dense_config2.md,
+# B = 4, config 3 at B = 32, config 5 at B = 128; the commands and per-kernel figures are in profiles/ews_dense_config2.md,
 # profiles/kernels_configs_1_3_5.md and profiles/ews_diag_terminal_config5.md). The streams grow in
 # proportion to the sample-intervals, so `roofline.traffic` is this figure times the launch's units.
 TRAFFIC_PER_UNIT = {
     "config1": {"ews_diag_fwd": 926.0, "ews_diag_bwd": 3227.0},
     "config2": {"ews_dense_fwd": 6368.0, "ews_dense_bwd": 24801.0},
+    "config3": {"ews_block_fwd": 7721.0, "ews_block_bwd": 9754.0},
     "config5": {"ews_diag_fwd": 78.0, "ews_diag_bwd": 90.0},
 }
 
