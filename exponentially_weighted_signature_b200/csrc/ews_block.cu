@@ -46,7 +46,7 @@ struct Geom {
     int lift_n;
     // per-warp shared memory (floats)
     int f_dys, f_dts, f_loc, f_stage, f_per_warp;  // f_loc: two staged local rows in the forward
-    int b_dys, b_dts, b_dtg, b_dyg, b_loc, b_adj, b_gst, b_sst, b_per_warp;
+    int b_dys, b_dts, b_dtg, b_dyg, b_loc, b_adj, b_gst, b_sst, b_gst2, b_sst2, b_per_warp;
 };
 
 struct Params {
@@ -842,6 +842,14 @@ __device__ void warp_load_row_padded(float* __restrict__ s, const float* __restr
     if (lane < n - done) s[pad_index(done + lane, off3, inv)] = __ldcg(g + done + lane);
 }
 
+// The same copy with cp.async (4-byte copies into the padded positions; the caller commits and waits).
+__device__ void warp_copy_row_padded_async(float* __restrict__ s, const float* __restrict__ g, int N) {
+    const int lane = threadIdx.x & 31;
+    const int N2 = N * N, off3 = 1 + N + N2, n = off3 + N * N2;
+    const unsigned inv = (65536u + N2 - 1) / N2;
+    for (int e = lane; e < n; e += 32) cp_async4(s + pad_index(e, off3, inv), g + e);
+}
+
 // Adds gradient row t (real dimension N, padded layout) to the lane's cotangent.
 __device__ __forceinline__ void add_grad_row(A3& a, const float* row, int N, int i, int jb) {
     const int N2 = N * N;
@@ -1441,18 +1449,36 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) bo.dA[e] = 0.f;
         A3 a = lam;
+        // the rows of interval t (gradient row t, state row t-1) are copied in with cp.async one interval
+        // ahead, into alternating buffers
+        float* gst2 = dxs + g.b_gst2;
+        float* sst2 = dxs + g.b_sst2;
+        auto issue_rows = [&](int k, int buf) {
+            const int t = t0 + k;
+            warp_copy_row_padded_async(buf ? gst2 : gst, p.grad_out + ((size_t)b * g.T + t) * g.W, g.N);
+            if (t > 0) warp_copy_row_padded_async(buf ? sst2 : sst, p.out + ((size_t)b * g.T + t - 1) * g.W, g.N);
+            cp_async_commit();
+        };
+        issue_rows(len - 1, 0);
         for (int k = len - 1; k >= 0; --k) {
             const int t = t0 + k;
-            warp_load_row_padded(gst, p.grad_out + ((size_t)b * g.T + t) * g.W, g.N);
-            if (t > 0) {
-                warp_load_row_padded(sst, p.out + ((size_t)b * g.T + t - 1) * g.W, g.N);
-            } else {
-                for (int e = lane; e < row_floats_padded(g.N); e += 32) sst[e] = 0.f;
-            }
+            const int buf = (len - 1 - k) & 1;
+            if (k >= 1)
+                issue_rows(k - 1, buf ^ 1);
+            else
+                cp_async_commit();
+            cp_async_wait<1>();
+            float* grow = buf ? gst2 : gst;
+            float* srow = buf ? sst2 : sst;
+            if (t == 0)
+                for (int e = lane; e < row_floats_padded(g.N); e += 32) srow[e] = 0.f;
+            __syncwarp();
             build_local<QT>(p, Ablk, dys + k * NB, dts[k], lc, true);
-            add_grad_row(a, gst, g.N, i, jb);
-            bwd_step<QT>(p, Ablk, lc, ab, sst, dts[k], a, bo, dyg + k * NB, dtg + k, i, jb);
+            add_grad_row(a, grow, g.N, i, jb);
+            bwd_step<QT>(p, Ablk, lc, ab, srow, dts[k], a, bo, dyg + k * NB, dtg + k, i, jb);
+            __syncwarp();
         }
+        cp_async_wait<0>();
         // ---- chunk outputs: dx = lift^T dy, dtheta, per-tile partials (dA, dlift)
         __syncwarp();
         for (int e = lane; e < len * g.d_in; e += 32) {
@@ -1572,7 +1598,9 @@ int make_geom(const ews_block_args* a, Geom* g) {
     g->b_adj = g->b_loc + align4(Loc::floats);
     g->b_gst = g->b_adj + align4(AdjBuf::floats);
     g->b_sst = g->b_gst + align4(std::max(row_floats_padded(g->N), g->Lc * g->d_in));
-    g->b_per_warp = g->b_sst + align4(row_floats_padded(g->N));
+    g->b_gst2 = g->b_sst + align4(row_floats_padded(g->N));  // second buffers of the exact pass
+    g->b_sst2 = g->b_gst2 + align4(row_floats_padded(g->N));
+    g->b_per_warp = g->b_sst2 + align4(row_floats_padded(g->N));
     return EWS_OK;
 }
 
