@@ -1396,16 +1396,27 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         A3 mu;
         mu.zero();
         float* lst = dxs + g.b_loc;
-        fetch_local(p, b, t0 + len - 1, lst + ((len - 1) & 1) * LROW);
+        // gradient row and local element of interval k, copied in with cp.async one interval ahead (the
+        // rows into alternating buffers; fetch_local commits the group)
+        float* gst2 = dxs + g.b_gst2;
+        auto issue_zero_carry = [&](int k) {
+            const int buf = (len - 1 - k) & 1;
+            warp_copy_row_padded_async(buf ? gst2 : gst, p.grad_out + ((size_t)b * g.T + t0 + k) * g.W, g.N);
+            fetch_local(p, b, t0 + k, lst + (k & 1) * LROW);
+        };
+        issue_zero_carry(len - 1);
         for (int k = len - 1; k >= 0; --k) {
-            warp_load_row_padded(gst, p.grad_out + ((size_t)b * g.T + t0 + k) * g.W, g.N);
-            cp_async_wait<0>();
+            if (k >= 1)
+                issue_zero_carry(k - 1);
+            else
+                cp_async_commit();
+            cp_async_wait<1>();
             __syncwarp();
-            if (k >= 1) fetch_local(p, b, t0 + k - 1, lst + ((k - 1) & 1) * LROW);
-            add_grad_row(mu, gst, g.N, i, jb);
+            add_grad_row(mu, ((len - 1 - k) & 1) ? gst2 : gst, g.N, i, jb);
             mu_step_row(lst + (k & 1) * LROW, mu, i, jb);
             __syncwarp();
         }
+        cp_async_wait<0>();
         // ---- 2. look-back over the later chunks: the cotangent at the chunk's end
         A3 lam;
         lam.zero();
@@ -1451,7 +1462,6 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         A3 a = lam;
         // the rows of interval t (gradient row t, state row t-1) are copied in with cp.async one interval
         // ahead, into alternating buffers
-        float* gst2 = dxs + g.b_gst2;
         float* sst2 = dxs + g.b_sst2;
         auto issue_rows = [&](int k, int buf) {
             const int t = t0 + k;
