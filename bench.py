@@ -45,7 +45,7 @@ TERMINAL_KERNELS = {"ews_diag_fwd": 2, "ews_diag_bwd": 4}
 TRAFFIC_PER_UNIT = {
     "config1": {"ews_diag_fwd": 926.0, "ews_diag_bwd": 3227.0},
     "config2": {"ews_dense_fwd": 6368.0, "ews_dense_bwd": 24801.0},
-    "config3": {"ews_block_fwd": 7721.0, "ews_block_bwd": 9754.0},
+    "config3": {"ews_block_fwd": 8009.0, "ews_block_bwd": 9850.0},
     "config5": {"ews_diag_fwd": 78.0, "ews_diag_bwd": 90.0},
 }
 

@@ -36,13 +36,14 @@ constexpr int NB = 8;        // padded state dimension: 4 blocks of 2
 constexpr int KQ = 9;        // coefficient slots: series order <= 8
 constexpr int kWarps = 4;    // warps per CTA, each an independent tile worker
 constexpr int SLOT = 16 + 8 + 64 + 512;  // chunk element: D blocks | S1 | S2 | S3
-constexpr int LROW = 608;                // an interval's local element D | s1 | s2 | s3, padded to 16 B rows
+constexpr int L3ROW = 68;                 // stride of the s3 rows (index i) in a local element: bank spread
+constexpr int LROW = 88 + 8 * L3ROW;       // an interval's local element D | s1 | s2 | s3, 16-byte rows
 constexpr int NPAIR = KQ * (KQ + 1) / 2;  // (p, r) with p + r <= 8
 
 struct Geom {
     int B, T, d_in, N, Lc, C, W, readout, depth;
     unsigned flags;
-    int spin_limit, q, ntiles, SR;
+    int spin_limit, q, ntiles;
     int lift_n;
     // per-warp shared memory (floats)
     int f_dys, f_dts, f_loc, f_stage, f_per_warp;  // f_loc: two staged local rows in the forward
@@ -436,7 +437,83 @@ __device__ __forceinline__ void chen_step(const Params& p, const Loc& lc, E3& S,
     chen_mul_r(S, lc.D, lc.s1, s2a, s2b, s3, i, jb);
 }
 
-// Prefix row [1, S1, S2, S3] of a lane element into a staged row (real dimension N).
+// Rows staged in shared memory (the backward's state and gradient rows, the forward's prefix rows) keep
+// levels 0-2 as in the row and put the level-3 rows (index i) N^2 + 4 floats apart: the lanes' accesses
+// to one staged row then fall on different banks (at a stride of N^2 = 64, sixteen lanes shared a bank).
+__host__ __device__ inline int row_floats_padded(int N) { return 1 + N + N * N + N * (N * N + 4); }
+
+// Position of row element e in the padded layout; inv = ceil(2^16 / N^2) turns the division by N^2 into a
+// multiply and shift, exact for the at most 512 level-3 entries.
+__device__ __forceinline__ int pad_index(int e, int off3, unsigned inv) {
+    return e < off3 ? e : e + 4 * (int)(((unsigned)(e - off3) * inv) >> 16);
+}
+
+// warp_load_span of one state row (real dimension N) into the padded layout (whole warp).
+__device__ void warp_load_row_padded(float* __restrict__ s, const float* __restrict__ g, int N) {
+    const int lane = threadIdx.x & 31;
+    const int N2 = N * N, off3 = 1 + N + N2, n = off3 + N * N2;
+    const unsigned inv = (65536u + N2 - 1) / N2;
+    int head = (int)(((16u - ((uintptr_t)g & 15u)) & 15u) >> 2);
+    if (head > n) head = n;
+    if (lane < head) s[pad_index(lane, off3, inv)] = __ldcg(g + lane);
+    const int nvec = (n - head) >> 2;
+    const float4* gv = reinterpret_cast<const float4*>(g + head);
+    for (int v = lane; v < nvec; v += 32) {
+        const float4 q = __ldcg(gv + v);
+        const int e = head + 4 * v;
+        s[pad_index(e, off3, inv)] = q.x;
+        s[pad_index(e + 1, off3, inv)] = q.y;
+        s[pad_index(e + 2, off3, inv)] = q.z;
+        s[pad_index(e + 3, off3, inv)] = q.w;
+    }
+    const int done = head + 4 * nvec;
+    if (lane < n - done) s[pad_index(done + lane, off3, inv)] = __ldcg(g + done + lane);
+}
+
+// The same copy with cp.async (4-byte copies into the padded positions; the caller commits and waits).
+__device__ void warp_copy_row_padded_async(float* __restrict__ s, const float* __restrict__ g, int N) {
+    const int lane = threadIdx.x & 31;
+    const int N2 = N * N, off3 = 1 + N + N2, n = off3 + N * N2;
+    const unsigned inv = (65536u + N2 - 1) / N2;
+    for (int e = lane; e < n; e += 32) cp_async4(s + pad_index(e, off3, inv), g + e);
+}
+
+// Stores a staged prefix row (padded layout) to global memory: s is placed at g's 16-byte phase (s + k is
+// 16-byte aligned where g + k is), so every float4 of the row that does not straddle two level-3 rows is
+// one aligned shared load; the straddling ones and the ragged ends go element by element.
+__device__ void warp_store_row_padded(float* __restrict__ g, const float* __restrict__ s, int N) {
+    const int lane = threadIdx.x & 31;
+    const int N2 = N * N, off3 = 1 + N + N2, n = off3 + N * N2;
+    const unsigned inv = (65536u + N2 - 1) / N2;
+    int head = (int)(((16u - ((uintptr_t)g & 15u)) & 15u) >> 2);
+    if (head > n) head = n;
+    if (lane < head) g[lane] = s[pad_index(lane, off3, inv)];
+    const int nvec = (n - head) >> 2;
+    float4* gv = reinterpret_cast<float4*>(g + head);
+    for (int v = lane; v < nvec; v += 32) {
+        const int e = head + 4 * v;
+        const int p0 = pad_index(e, off3, inv), p3 = pad_index(e + 3, off3, inv);
+        float4 q;
+        if (p3 == p0 + 3) {
+            q = *reinterpret_cast<const float4*>(s + p0);
+        } else {
+            q.x = s[p0];
+            q.y = s[pad_index(e + 1, off3, inv)];
+            q.z = s[pad_index(e + 2, off3, inv)];
+            q.w = s[p3];
+        }
+        gv[v] = q;
+    }
+    const int done = head + 4 * nvec;
+    if (lane < n - done) g[done + lane] = s[pad_index(done + lane, off3, inv)];
+}
+
+// The shared-memory position at which a row bound for global address g is staged (16-byte phase of g).
+__device__ __forceinline__ float* phase_matched(float* stage, const float* g) {
+    return stage + (((uintptr_t)g & 15u) >> 2);
+}
+
+// Prefix row [1, S1, S2, S3] of a lane element into a staged row (real dimension N, padded layout).
 __device__ __forceinline__ void stage_row(float* row, const E3& S, int N, int i, int jb) {
     const int lane = threadIdx.x & 31;
     const int N2 = N * N;
@@ -463,7 +540,7 @@ __device__ __forceinline__ void stage_row(float* row, const E3& S, int N, int i,
             if (j < N)
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
-                    if (k < N) row[1 + N + N2 + i * N2 + j * N + k] = S.S3[r][k];
+                    if (k < N) row[1 + N + N2 + i * (N2 + 4) + j * N + k] = S.S3[r][k];
         }
     }
 }
@@ -501,7 +578,7 @@ __device__ void load_chunk(const Params& p, const float* liftS, float* dxs, floa
 
 // The local element of every interval, a parallel map ahead of the chains: one warp per chunk of one
 // sample builds each interval's flow complement, letters and series terms (build_local, as the chain did)
-// and writes [D | s1 | s2 | s3] (s3[i][j][k] at 88 + 64 i + 8 j + k) to p.loc.
+// and writes [D | s1 | s2 | s3] (s3[i][j][k] at 88 + L3ROW i + 8 j + k) to p.loc.
 template <int QT>
 __global__ void __launch_bounds__(kWarps * 32) local_kernel(Params p) {
     extern __shared__ float smem[];
@@ -536,7 +613,7 @@ __global__ void __launch_bounds__(kWarps * 32) local_kernel(Params p) {
         row[56 + lane] = lc.s2[32 + lane];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            float* d3 = row + 88 + 64 * i + 8 * (2 * jb + r);
+            float* d3 = row + 88 + L3ROW * i + 8 * (2 * jb + r);
             *reinterpret_cast<float4*>(d3) = make_float4(s3[r][0], s3[r][1], s3[r][2], s3[r][3]);
             *reinterpret_cast<float4*>(d3 + 4) = make_float4(s3[r][4], s3[r][5], s3[r][6], s3[r][7]);
         }
@@ -559,7 +636,7 @@ __device__ __forceinline__ void chen_step_row(const float* row, E3& S, int i, in
         const int j = 2 * jb + r;
         s2a[r] = row[24 + 8 * i + j];
         const float4* b2 = reinterpret_cast<const float4*>(row + 24 + 8 * j);
-        const float4* b3 = reinterpret_cast<const float4*>(row + 88 + 64 * i + 8 * j);
+        const float4* b3 = reinterpret_cast<const float4*>(row + 88 + L3ROW * i + 8 * j);
         const float4 u0 = b2[0], u1 = b2[1], w0 = b3[0], w1 = b3[1];
         s2b[r][0] = u0.x; s2b[r][1] = u0.y; s2b[r][2] = u0.z; s2b[r][3] = u0.w;
         s2b[r][4] = u1.x; s2b[r][5] = u1.y; s2b[r][6] = u1.z; s2b[r][7] = u1.w;
@@ -654,29 +731,28 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_kernel(Params p) {
                     load_e3(p.agg + slot, A, i, jb);
                     chen_mul(fin, A, i, jb);
                 }
-                stage_row(stage, fin, g.N, i, jb);
+                float* dst = p.out + (size_t)b * g.W;
+                float* srow = phase_matched(stage, dst);
+                stage_row(srow, fin, g.N, i, jb);
                 __syncwarp();
-                warp_store_span(p.out + (size_t)b * g.W, stage, g.W);
+                warp_store_row_padded(dst, srow, g.N);
                 __syncwarp();
             }
             continue;
         }
         // pass 2: re-run the chunk from its carry and emit the prefix rows
         E3 S = excl;
-        int k0 = 0;
         fetch_local(p, b, t0, lrow);
         for (int k = 0; k < len; ++k) {
             cp_async_wait<0>();
             __syncwarp();
             if (k + 1 < len) fetch_local(p, b, t0 + k + 1, lrow + ((k + 1) & 1) * LROW);
             chen_step_row(lrow + (k & 1) * LROW, S, i, jb);
-            stage_row(stage + (k - k0) * g.W, S, g.N, i, jb);
-            if (k - k0 == g.SR - 1 || k == len - 1) {
-                __syncwarp();
-                warp_store_span(p.out + ((size_t)b * g.T + t0 + k0) * g.W, stage, (k - k0 + 1) * g.W);
-                __syncwarp();
-                k0 = k + 1;
-            }
+            float* dst = p.out + ((size_t)b * g.T + t0 + k) * g.W;
+            float* srow = phase_matched(stage, dst);
+            stage_row(srow, S, g.N, i, jb);
+            __syncwarp();
+            warp_store_row_padded(dst, srow, g.N);
             __syncwarp();
         }
     }
@@ -807,47 +883,6 @@ __device__ __forceinline__ void apply_JT(A3& a, const float* D, const float* U1,
 
 __device__ __forceinline__ void apply_JT_e3(A3& a, const E3& G, int i, int jb) {
     apply_JT(a, G.D, G.S1, G.S2b, i, jb);
-}
-
-// The backward stages state and gradient rows with levels 0-2 as in the row and the level-3 rows (index i)
-// N^2 + 4 floats apart: the lanes' reads of one staged row then fall on different banks (at a stride of
-// N^2 = 64, sixteen lanes shared a bank).
-__host__ __device__ inline int row_floats_padded(int N) { return 1 + N + N * N + N * (N * N + 4); }
-
-// Position of row element e in the padded layout; inv = ceil(2^16 / N^2) turns the division by N^2 into a
-// multiply and shift, exact for the at most 512 level-3 entries.
-__device__ __forceinline__ int pad_index(int e, int off3, unsigned inv) {
-    return e < off3 ? e : e + 4 * (int)(((unsigned)(e - off3) * inv) >> 16);
-}
-
-// warp_load_span of one state row (real dimension N) into the padded layout (whole warp).
-__device__ void warp_load_row_padded(float* __restrict__ s, const float* __restrict__ g, int N) {
-    const int lane = threadIdx.x & 31;
-    const int N2 = N * N, off3 = 1 + N + N2, n = off3 + N * N2;
-    const unsigned inv = (65536u + N2 - 1) / N2;
-    int head = (int)(((16u - ((uintptr_t)g & 15u)) & 15u) >> 2);
-    if (head > n) head = n;
-    if (lane < head) s[pad_index(lane, off3, inv)] = __ldcg(g + lane);
-    const int nvec = (n - head) >> 2;
-    const float4* gv = reinterpret_cast<const float4*>(g + head);
-    for (int v = lane; v < nvec; v += 32) {
-        const float4 q = __ldcg(gv + v);
-        const int e = head + 4 * v;
-        s[pad_index(e, off3, inv)] = q.x;
-        s[pad_index(e + 1, off3, inv)] = q.y;
-        s[pad_index(e + 2, off3, inv)] = q.z;
-        s[pad_index(e + 3, off3, inv)] = q.w;
-    }
-    const int done = head + 4 * nvec;
-    if (lane < n - done) s[pad_index(done + lane, off3, inv)] = __ldcg(g + done + lane);
-}
-
-// The same copy with cp.async (4-byte copies into the padded positions; the caller commits and waits).
-__device__ void warp_copy_row_padded_async(float* __restrict__ s, const float* __restrict__ g, int N) {
-    const int lane = threadIdx.x & 31;
-    const int N2 = N * N, off3 = 1 + N + N2, n = off3 + N * N2;
-    const unsigned inv = (65536u + N2 - 1) / N2;
-    for (int e = lane; e < n; e += 32) cp_async4(s + pad_index(e, off3, inv), g + e);
 }
 
 // Adds gradient row t (real dimension N, padded layout) to the lane's cotangent.
@@ -1592,14 +1627,13 @@ int make_geom(const ews_block_args* a, Geom* g) {
     g->Lc = a->chunk > 0 ? a->chunk : pick_chunk(a->batch, a->steps);
     g->C = (g->T + g->Lc - 1) / g->Lc;
     g->ntiles = g->B * g->C;
-    g->SR = g->W >= 512 ? 1 : (512 + g->W - 1) / g->W;
     g->lift_n = align4(NB * g->d_in);
     const int xs = align4(g->Lc * g->d_in), ys = g->Lc * NB, ts = align4(g->Lc);
     g->f_dys = xs;
     g->f_dts = xs + ys;
     g->f_loc = g->f_dts + ts;
     g->f_stage = g->f_loc + align4(std::max(2 * LROW, (int)Loc::floats));
-    g->f_per_warp = g->f_stage + align4(g->SR * g->W);
+    g->f_per_warp = g->f_stage + align4(row_floats_padded(g->N) + 4);  // one staged row at any phase
     g->b_dys = xs;
     g->b_dts = xs + ys;
     g->b_dtg = g->b_dts + ts;
