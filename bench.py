@@ -39,9 +39,8 @@ TERMINAL_KERNELS = {"ews_diag_fwd": 2, "ews_diag_bwd": 4}
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per sample-interval of each entry point's
 # kernels, from one ncu capture of a smaller case whose streams exceed L2 (config 1 at B = 64, config 2 at
-# B = 4, config 3 at B = 32, config 5 at B = 128; the commands and per-kernel figures are in profiles/ews_dense_config2.md,
-# profiles/kernels_configs_1_3_5.md and profiles/ews_diag_terminal_config5.md). The streams grow in
-# proportion to the sample-intervals, so `roofline.traffic` is this figure times the launch's units.
+# B = 4, config 3 at B = 32, config 5 at B = 128). The streams grow in proportion to the sample-intervals,
+# so `roofline.traffic` is this figure times the launch's units.
 TRAFFIC_PER_UNIT = {
     "config1": {"ews_diag_fwd": 926.0, "ews_diag_bwd": 3227.0},
     "config2": {"ews_dense_fwd": 6368.0, "ews_dense_bwd": 24801.0},
@@ -79,7 +78,7 @@ def _diag_setup(cfg, rank, world, device, precision, batch=None):
     q = max(2, series.suggest_series_q(x_max, 2, 1e-14))
     A = AParamDiag(torch.tensor(case["lam"], dtype=torch.float32))
     lift = Lift(torch.tensor(case["lift"], dtype=torch.float32), preserve_first_channel=False)
-    kw = dict(reweighting_mode="displacement_uniform", series_q=q)
+    kw = dict(reweighting_mode="displacement_uniform", leaf="series", series_q=q)
     if cfg == "config5":
         layer = LogEWS(A, N=2, **kw)
         readout = "terminal"
@@ -143,7 +142,7 @@ def _dense_setup(cfg, rank, world, device, precision, batch=None):
     q = max(2, series.suggest_series_q(x_max, 2, 1e-14))
     A = AParamGeneral(torch.tensor(case["A"], dtype=torch.float32))
     lift = Lift(torch.tensor(case["lift"], dtype=torch.float32), preserve_first_channel=False)
-    layer = EWS(A, N=2, reweighting_mode="displacement_uniform", series_q=q).to(device)
+    layer = EWS(A, N=2, reweighting_mode="displacement_uniform", leaf="series", series_q=q).to(device)
     lift = lift.to(device)
     x_host = torch.tensor(case["path"][s0:s1], dtype=torch.float32)
     clock_host = torch.tensor(case["clock"][s0:s1], dtype=torch.float32)
@@ -187,7 +186,7 @@ def _block_setup(cfg, rank, world, device, precision, batch=None):
     x_max = float(np.linalg.norm(A, 2)) * float(np.diff(case["clock"], axis=1).max())
     q = min(8, max(2, series.suggest_series_q(x_max, 3, 1e-14)))
     blocks = [torch.tensor(A[2 * k : 2 * k + 2, 2 * k : 2 * k + 2], dtype=torch.float32) for k in range(N // 2)]
-    layer = EWS(AParamBlockDiag(blocks, (2,) * (N // 2)), N=3, reweighting_mode="displacement", series_q=q).to(device)
+    layer = EWS(AParamBlockDiag(blocks, (2,) * (N // 2)), N=3, reweighting_mode="displacement", leaf="series", series_q=q).to(device)
     lift = Lift(torch.tensor(case["lift"], dtype=torch.float32), preserve_first_channel=False).to(device)
     x_host = torch.tensor(case["path"][s0:s1], dtype=torch.float32)
     clock_host = torch.tensor(case["clock"][s0:s1], dtype=torch.float32)
@@ -363,9 +362,9 @@ def _cpu_baseline(cfg, precision, budget_s=20.0):
         t0 = time.perf_counter()
         y = O.lift(p, Bm)
         if cfg == "config5":
-            out = O.log_ews_layer(y, clock[:, : Ts + 1], to_matrix(A), 2, series_q=q, reweighting_mode="displacement_uniform", readout="terminal", terminal_reduce="assoc")
+            out = O.log_ews_layer(y, clock[:, : Ts + 1], to_matrix(A), 2, leaf="series", series_q=q, reweighting_mode="displacement_uniform", readout="terminal", terminal_reduce="assoc")
         else:
-            out = O.ews_layer(y, clock[:, : Ts + 1], to_matrix(A), depth, series_q=q, reweighting_mode=mode, readout="prefix")
+            out = O.ews_layer(y, clock[:, : Ts + 1], to_matrix(A), depth, leaf="series", series_q=q, reweighting_mode=mode, readout="prefix")
         out.sum().backward()
         dt = time.perf_counter() - t0
         spent += dt
@@ -394,7 +393,7 @@ def _cpu_baseline_stacked(budget_s, threads):
             self.A_param, self.q = a_param, q
 
         def forward(self, path, clock, readout="prefix", output_format="flat"):
-            return O.ews_layer(path, clock, torch.diag(self.A_param.values), 2, series_q=self.q,
+            return O.ews_layer(path, clock, torch.diag(self.A_param.values), 2, leaf="series", series_q=self.q,
                                reweighting_mode="displacement", readout=readout)
 
     case = workloads.config4(B=1)

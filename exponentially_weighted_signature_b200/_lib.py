@@ -34,6 +34,7 @@ EXPORTED = (
     "ews_diag_fwd",
     "ews_diag_bwd",
     "ews_diag_fwd_noalloc",
+    "ews_diag_fwd_noalloc_status",
     "ews_dense_workspace_size",
     "ews_dense_fwd",
     "ews_dense_bwd",
@@ -43,6 +44,7 @@ EXPORTED = (
     "ews_expm_batched",
     "ews_expm_adjoint_batched",
     "ews_read_device_status",
+    "ews_status_fold",
     "ews_error_string",
     "ews_version",
 )
@@ -159,6 +161,11 @@ class EWSLibraryError(RuntimeError):
     pass
 
 
+class EWSLookbackTimeout(EWSLibraryError):
+    """A device-side wait for a neighbouring chunk ran out (EWS_ERR_LOOKBACK_TIMEOUT): the outputs and
+    gradients of that call are invalid."""
+
+
 def load(path: str = LIB_PATH) -> ctypes.CDLL:
     """Loads the library (once). Raises if it has not been built."""
     global _lib
@@ -197,6 +204,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.ews_expm_adjoint_batched.restype = _c_int
         lib.ews_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(_c_int)]
         lib.ews_read_device_status.restype = _c_int
+        lib.ews_diag_fwd_noalloc_status.argtypes = [_vp, ctypes.POINTER(_c_int)]
+        lib.ews_diag_fwd_noalloc_status.restype = _c_int
+        lib.ews_status_fold.argtypes = [_vp, _vp, _vp]
+        lib.ews_status_fold.restype = _c_int
         lib.ews_error_string.argtypes = [_c_int]
         lib.ews_error_string.restype = ctypes.c_char_p
         lib.ews_version.argtypes = []
@@ -208,6 +219,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
 def check(rc: int, what: str) -> None:
     if rc != EWS_OK:
         msg = load().ews_error_string(rc).decode()
+        if rc == EWS_ERR_LOOKBACK_TIMEOUT:
+            raise EWSLookbackTimeout(f"{what}: {msg} (code {rc})")
         if rc == 1:
             raise ValueError(f"{what}: {msg} (code {rc})")
         if rc == 2:

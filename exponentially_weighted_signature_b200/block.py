@@ -101,7 +101,7 @@ class EWSBlock(nn.Module):
             lam = torch.exp(torch.rand(self.m, generator=g) * 4.0 - 3.0)
         self.lift = B(torch.randn(self.m, H, generator=g) / math.sqrt(H), preserve_first_channel=False)
         self.ewms = EWS(AParamDiag(lam.to(torch.float32)), N=self.n, reweighting_mode="displacement",
-                        series_q=series_q, combine_chunk=combine_chunk)
+                        leaf="series", series_q=series_q, combine="b200", combine_chunk=combine_chunk)
         D = sum(self.m**k for k in range(1, self.n + 1))
         self.D = D
         self.graded = GradedRMSNorm(self.m, self.n, eps=graded_eps)

@@ -5,6 +5,7 @@ from __future__ import annotations
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
@@ -19,8 +20,8 @@ FLAGS = [
     "-std=c++17",
     "-Xcompiler",
     "-fPIC",
-    "-shared",
 ]
+OBJDIR = os.path.join(HERE, "_build")
 
 
 def _stale() -> bool:
@@ -31,14 +32,24 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale():
-        return LIB
-    cmd = [NVCC, *FLAGS, "-o", LIB + ".tmp", *[os.path.join(CSRC, s) for s in SOURCES]]
+def _compile(src: str, verbose: bool) -> str:
+    obj = os.path.join(OBJDIR, os.path.splitext(src)[0] + ".o")
+    cmd = [NVCC, *FLAGS, "-c", "-o", obj, os.path.join(CSRC, src)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
+    return obj
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    """Compiles the translation units in parallel (each is independent) and links the shared library."""
+    if not force and not _stale():
+        return LIB
+    os.makedirs(OBJDIR, exist_ok=True)
+    with ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+        objs = list(ex.map(lambda src: _compile(src, verbose), SOURCES))
+    subprocess.run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB + ".tmp", *objs], check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

@@ -1877,3 +1877,14 @@ extern "C" int ews_diag_fwd_noalloc(const ews_diag_args* a, ews_stream_t stream)
     // nothing, and leaves the aggregates and carries in the array until the next call overwrites them.
     return ews_diag_fwd(&b, stream);
 }
+
+// The status block at the start of the array, read like any workspace's (ews_read_device_status): the
+// caller of the no-alloc forward has no pointer to the array, so this is how it learns of a look-back
+// timeout. Uses the current device's array; synchronises the stream.
+extern "C" int ews_diag_fwd_noalloc_status(ews_stream_t stream, int* status) {
+    if (!status) return EWS_ERR_INVALID_ARGUMENT;
+    void* scratch = nullptr;
+    const int sc = noalloc_scratch(&scratch);
+    if (sc != EWS_OK) return sc;
+    return ews_read_device_status(scratch, stream, status);
+}

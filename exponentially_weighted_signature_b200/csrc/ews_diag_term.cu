@@ -525,9 +525,12 @@ struct TLay {
     size_t dmat, bpart, btotal;           // backward workspace
 };
 
+// Both workspaces begin with a DeviceStatus block, as every workspace of the library does, so a caller
+// can fold any workspace's error word the same way (ews_status_fold). This path has no waits: the call
+// clears the block and nothing sets it.
 static TLay layout(const TP& p) {
     TLay L{};
-    size_t o = 0;
+    size_t o = al256(sizeof(DeviceStatus));
     L.part = o;
     o += al256(sizeof(float) * (size_t)p.B * p.S * PW);
     L.save = o;
@@ -535,7 +538,7 @@ static TLay layout(const TP& p) {
     L.spre = o;
     o += al256(sizeof(float) * (size_t)p.B * p.S * NP);
     L.total = o;
-    o = 0;
+    o = al256(sizeof(DeviceStatus));
     L.dmat = o;
     o += al256(sizeof(float) * (size_t)p.B * (2 * MM + NP));
     L.bpart = o;
@@ -569,6 +572,7 @@ int diag_term_fwd(const ews_diag_args* a, cudaStream_t s) {
     const TLay L = layout(p);
     if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
     char* ws = (char*)a->fwd_ws;
+    if (cudaMemsetAsync(ws, 0, sizeof(DeviceStatus), s) != cudaSuccess) return EWS_ERR_LAUNCH;
     p.path = a->path;
     p.lift = a->lift;
     p.tab_x = a->tab_x;
@@ -595,6 +599,7 @@ int diag_term_bwd(const ews_diag_args* a, cudaStream_t s) {
     if (a->lift && !a->grad_lift) return EWS_ERR_INVALID_ARGUMENT;
     char* fws = (char*)a->fwd_ws;
     char* ws = (char*)a->bwd_ws;
+    if (cudaMemsetAsync(ws, 0, sizeof(DeviceStatus), s) != cudaSuccess) return EWS_ERR_LAUNCH;
     p.path = a->path;
     p.lift = a->lift;
     p.tab_x = a->tab_x;

@@ -56,6 +56,58 @@ class _timed:
         return False
 
 
+# ---------------------------------------------------------------------------------- device status
+#
+# Every library call leaves an error word at the start of its workspace (EWS_OK, or EWS_ERR_LOOKBACK_TIMEOUT
+# when a bounded device wait ran out and the call's results are invalid). After each call the word is
+# folded into a per-device sticky int on the GPU (ews_status_fold) and copied to pinned host memory
+# asynchronously, so nothing waits on the GPU; the next call (and every backward on exit) reads the host
+# copy and raises EWSLookbackTimeout if an earlier call failed. CHECK_SYNC makes each call synchronise
+# and raise at once instead (``layer.configure(check_status=True)``).
+
+CHECK_SYNC = False
+# Polls before a device-side look-back wait gives up (0: the library's default, 2^21).
+SPIN_LIMIT = 0
+_STATUS = {}
+
+
+def _status_slot(device):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    slot = _STATUS.get(idx)
+    if slot is None:
+        sticky = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        slot = _STATUS[idx] = (sticky, host)
+    return slot
+
+
+def raise_pending(device) -> None:
+    """Raises (once) the first look-back timeout that an earlier call on ``device`` reported."""
+    sticky, host = _status_slot(device)
+    code = int(host[0])
+    if code != _lib.EWS_OK:
+        host.zero_()
+        sticky.zero_()
+        _lib.check(code, "an earlier EWS engine call on this device")
+
+
+def reset_status(device=None) -> None:
+    """Clears the pending status of ``device`` (all devices when None)."""
+    for idx, (sticky, host) in list(_STATUS.items()):
+        if device is None or idx == (device.index if device.index is not None else torch.cuda.current_device()):
+            sticky.zero_()
+            host.zero_()
+
+
+def _fold_status(workspace: torch.Tensor, device) -> None:
+    sticky, host = _status_slot(device)
+    _lib.check(_lib.load().ews_status_fold(_ptr(workspace), _ptr(sticky), _stream_ptr(device)), "ews_status_fold")
+    host.copy_(sticky, non_blocking=True)
+    if CHECK_SYNC:
+        torch.cuda.current_stream(device).synchronize()
+        raise_pending(device)
+
+
 def increments_to_knots_grad(gdx: torch.Tensor) -> torch.Tensor:
     """Adjoint of dx_t = x_{t+1} - x_t: (B, T, d) -> (B, T+1, d)."""
     return F.pad(gdx, (0, 0, 1, 0)) - F.pad(gdx, (0, 0, 0, 1))
@@ -80,7 +132,7 @@ class DiagScan(torch.autograd.Function):
         out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
         a = _lib.DiagArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
-        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, 0, 0
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, 0, SPIN_LIMIT
         fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
         _lib.check(lib.ews_diag_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_diag_workspace_size")
         fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
@@ -88,8 +140,10 @@ class DiagScan(torch.autograd.Function):
         a.tab_x, a.tab_q1, a.tab_q2 = _ptr(x_c), _ptr(q1_c), _ptr(q2_c)
         a.out = _ptr(out)
         a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
+        raise_pending(dev)
         with _timed("ews_diag_fwd", dev, B * T):
             _lib.check(lib.ews_diag_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_fwd")
+        _fold_status(fwd_ws, dev)
         ctx.meta = (readout, flags, chunk, increments, B, T, d_in, N, bb.value, path.dtype)
         ctx.has_lift = lift is not None
         ctx.save_for_backward(path_c, x_c, q1_c, q2_c, lift_c if lift_c is not None else torch.empty(0, device=dev), out, fwd_ws)
@@ -111,7 +165,7 @@ class DiagScan(torch.autograd.Function):
         glift = torch.empty((N, d_in), device=dev, dtype=torch.float32) if lift is not None else None
         a = _lib.DiagArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
-        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, 0, 0
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, 0, SPIN_LIMIT
         a.path, a.lift = _ptr(path), _ptr(lift)
         a.tab_x, a.tab_q1, a.tab_q2 = _ptr(x), _ptr(q1), _ptr(q2)
         a.out, a.grad_out = _ptr(out), _ptr(g)
@@ -120,6 +174,8 @@ class DiagScan(torch.autograd.Function):
         a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
         with _timed("ews_diag_bwd", dev, B * T):
             _lib.check(lib.ews_diag_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_bwd")
+        _fold_status(bwd_ws, dev)
+        raise_pending(dev)
         gpath = gdx if increments else increments_to_knots_grad(gdx)
         return gpath.to(path_dtype), gx, gq1, gq2, glift, None, None, None, None
 
@@ -177,7 +233,7 @@ class DenseScan(torch.autograd.Function):
         out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
         a = _lib.DenseArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
-        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, QP - 1, 0
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, QP - 1, SPIN_LIMIT
         fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
         _lib.check(lib.ews_dense_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_dense_workspace_size")
         fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
@@ -185,8 +241,10 @@ class DenseScan(torch.autograd.Function):
         a.tab_d, a.tab_f, a.tab_g, a.tab_h = (_ptr(t) for t in tabs)
         a.out = _ptr(out)
         a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
+        raise_pending(dev)
         with _timed("ews_dense_fwd", dev, B * T):
             _lib.check(lib.ews_dense_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_dense_fwd")
+        _fold_status(fwd_ws, dev)
         ctx.meta = (readout, flags, chunk, increments, B, T, d_in, N, QP, bb.value, path.dtype)
         ctx.save_for_backward(path_c, *tabs, out, fwd_ws)
         return out
@@ -208,7 +266,7 @@ class DenseScan(torch.autograd.Function):
         gH = torch.empty_like(H)
         a = _lib.DenseArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
-        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, QP - 1, 0
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, QP - 1, SPIN_LIMIT
         a.path = _ptr(path)
         a.tab_d, a.tab_f, a.tab_g, a.tab_h = (_ptr(t) for t in (M, F, G, H))
         a.out, a.grad_out, a.grad_dx = _ptr(out), _ptr(g), _ptr(gdx)
@@ -217,6 +275,8 @@ class DenseScan(torch.autograd.Function):
         a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
         with _timed("ews_dense_bwd", dev, B * T):
             _lib.check(lib.ews_dense_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_dense_bwd")
+        _fold_status(bwd_ws, dev)
+        raise_pending(dev)
         gpath = gdx if increments else increments_to_knots_grad(gdx)
         return gpath.to(path_dtype), gM, gF, gG, gH, None, None, None, None
 
@@ -244,15 +304,17 @@ class DiagScanClock(torch.autograd.Function):
         out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
         a = _lib.DiagArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
-        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, 0
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, SPIN_LIMIT
         fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
         _lib.check(lib.ews_diag_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_diag_workspace_size")
         fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
         a.path, a.clock, a.lift, a.tab_x = _ptr(path_c), _ptr(clock_c), _ptr(lift_c), _ptr(rates_c)
         a.out = _ptr(out)
         a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
+        raise_pending(dev)
         with _timed("ews_diag_fwd", dev, B * T):
             _lib.check(lib.ews_diag_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_fwd")
+        _fold_status(fwd_ws, dev)
         ctx.meta = (readout, flags, chunk, increments, series_q, B, T, d_in, N, bb.value, path.dtype, clock.dtype)
         ctx.has_lift = lift is not None
         empty = torch.empty(0, device=dev)
@@ -274,7 +336,7 @@ class DiagScanClock(torch.autograd.Function):
         glift = torch.empty((N, d_in), device=dev, dtype=torch.float32) if lift is not None else None
         a = _lib.DiagArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
-        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, 0
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, SPIN_LIMIT
         a.path, a.clock, a.lift, a.tab_x = _ptr(path), _ptr(clock), _ptr(lift), _ptr(rates)
         a.out, a.grad_out = _ptr(out), _ptr(g)
         a.grad_dx, a.grad_lift, a.grad_x, a.grad_dtheta = _ptr(gdx), _ptr(glift), _ptr(gr), _ptr(gdt)
@@ -282,6 +344,8 @@ class DiagScanClock(torch.autograd.Function):
         a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
         with _timed("ews_diag_bwd", dev, B * T):
             _lib.check(lib.ews_diag_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_bwd")
+        _fold_status(bwd_ws, dev)
+        raise_pending(dev)
         gpath = gdx if increments else increments_to_knots_grad(gdx)
         gclock = increments_to_knots_grad(gdt[..., None])[..., 0]
         return gpath.to(path_dtype), gclock.to(clock_dtype), gr, glift, None, None, None, None, None
@@ -309,15 +373,17 @@ class BlockScan(torch.autograd.Function):
         out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
         a = _lib.BlockArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 3
-        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, 0
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, SPIN_LIMIT
         fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
         _lib.check(lib.ews_block_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_block_workspace_size")
         fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
         a.path, a.clock, a.blocks, a.lift = _ptr(path_c), _ptr(clock_c), _ptr(blocks_c), _ptr(lift_c)
         a.out = _ptr(out)
         a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
+        raise_pending(dev)
         with _timed("ews_block_fwd", dev, B * T):
             _lib.check(lib.ews_block_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_block_fwd")
+        _fold_status(fwd_ws, dev)
         ctx.meta = (readout, flags, chunk, increments, series_q, B, T, d_in, N, bb.value, path.dtype, clock.dtype)
         ctx.has_lift = lift is not None
         empty = torch.empty(0, device=dev)
@@ -339,7 +405,7 @@ class BlockScan(torch.autograd.Function):
         glift = torch.empty((N, d_in), device=dev, dtype=torch.float32) if lift is not None else None
         a = _lib.BlockArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 3
-        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, 0
+        a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, SPIN_LIMIT
         a.path, a.clock, a.blocks, a.lift = _ptr(path), _ptr(clock), _ptr(blocks), _ptr(lift)
         a.out, a.grad_out = _ptr(out), _ptr(g)
         a.grad_dx, a.grad_dtheta, a.grad_blocks, a.grad_lift = _ptr(gdx), _ptr(gdt), _ptr(gblk), _ptr(glift)
@@ -347,6 +413,8 @@ class BlockScan(torch.autograd.Function):
         a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
         with _timed("ews_block_bwd", dev, B * T):
             _lib.check(lib.ews_block_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_block_bwd")
+        _fold_status(bwd_ws, dev)
+        raise_pending(dev)
         gpath = gdx if increments else increments_to_knots_grad(gdx)
         gclock = increments_to_knots_grad(gdt[..., None])[..., 0]
         return gpath.to(path_dtype), gclock.to(clock_dtype), gblk, glift, None, None, None, None, None

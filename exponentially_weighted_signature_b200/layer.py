@@ -1,11 +1,14 @@
 """The EWS layer on the B200 engines: same constructor and call as the reference's ews/layer.py.
 
-``EWS(A, N, ..., combine="b200")`` keeps the reference's options and validation
-(ews/layer.py:82-152) and its call ``layer(path, clock, return_terminal, output_format, readout,
-a_scale)`` (ews/layer.py:267-302), with the flat output layout [1, level 1, ..., level N]
-(ews/core/output_format.py:12-30). The combine value "b200" selects the CUDA engines; the reference's
-own JAX engines ("assoc", "lean", "block_kernel", "dense_kernel") are not part of this package, and
-there is no CPU fallback.
+``EWS(A, N, ...)`` keeps the reference's options, defaults and validation (ews/layer.py:82-152) and
+its call ``layer(path, clock, return_terminal, output_format, readout, a_scale)`` (ews/layer.py:267-302),
+with the flat output layout [1, level 1, ..., level N] (ews/core/output_format.py:12-30). Every
+``combine`` kind selects the CUDA engines: the kinds are implementations of one scan with the same
+result (ews/core/kernels/combine.py:1-14), so "assoc" (the default), "lean", "block_kernel",
+"dense_kernel" and "b200" all run here; ``combine_chunk`` sets the engines' chunk length only with
+``combine="b200"`` (the other kinds' chunk targets belong to the reference's Pallas kernels). A leaf or
+generator structure the engines do not implement raises ``NotImplementedError``; there is no CPU
+fallback.
 """
 
 from __future__ import annotations
@@ -23,14 +26,25 @@ LEAF_KINDS = ("van_loan", "series", "plane_closed", "block_series", "jordan_clos
 MODES = ("displacement", "displacement_uniform", "displacement_uniform_basepoint")
 
 _DETERMINISTIC = False
+# Extra EWS_F_* bits OR-ed into every engine call (failure-detection tests set EWS_F_TEST_WITHHOLD here).
+_EXTRA_FLAGS = 0
 
 
-def configure(deterministic: bool = False) -> None:
-    """Bit-reproducible engine results (the counterpart of the reference's XLA determinism switch,
-    ews/determinism.py:32-106): chunks then wait for their neighbour's inclusive carry instead of
-    folding in whatever aggregates are ready, which fixes the rounding of the carries."""
+def configure(deterministic: bool = False, check_status: bool = False) -> None:
+    """``deterministic``: bit-reproducible engine results (the counterpart of the reference's XLA
+    determinism switch, ews/determinism.py:32-106): chunks then wait for their neighbour's inclusive
+    carry instead of folding in whatever aggregates are ready, which fixes the rounding of the carries.
+
+    ``check_status``: synchronise after every engine call and raise ``EWSLookbackTimeout`` at once if a
+    device-side wait ran out. By default the status is collected without synchronising and an error
+    is raised by the next engine call on the device (or when a backward finishes)."""
     global _DETERMINISTIC
     _DETERMINISTIC = bool(deterministic)
+    engine.CHECK_SYNC = bool(check_status)
+
+
+def _det_flags() -> int:
+    return (_lib.EWS_F_DETERMINISTIC if _DETERMINISTIC else 0) | _EXTRA_FLAGS
 
 
 READOUTS = ("terminal", "prefix", "mean", "max")
@@ -49,9 +63,11 @@ class EWS(nn.Module):
     """Exponentially weighted signature layer on the B200 engines.
 
     Engine dispatch follows A's structure (ews/core/kernels/combine.py:37-63): a diagonal
-    parametrisation runs the diagonal engine. Local terms are the series leaf's at order ``series_q``
-    (``leaf="series"``; ``"block_series"`` is accepted for diagonal A, where both leaves agree to the
-    series truncation).
+    parametrisation runs the diagonal engine, 2x2 blocks at depth 3 the block engine, anything else at
+    depth 2 the dense engine. Leaves: ``"series"`` at order ``series_q`` on every engine
+    (``"block_series"`` is accepted for diagonal A, where both leaves agree to the series truncation);
+    ``"van_loan"`` (the reference's default, M knots per interval, ews/core/van_loan.py:91-160) on the
+    diagonal engine under a uniform clock.
     """
 
     def __init__(
@@ -64,10 +80,10 @@ class EWS(nn.Module):
         terminal_reduce: str = "tree",
         van_loan_expm: str = "cayley",
         chen_expm: str = "exact",
-        leaf: str = "series",
-        series_q: Optional[int] = 8,
-        combine: str = "b200",
-        combine_chunk: int = 0,
+        leaf: str = "van_loan",
+        series_q: Optional[int] = None,
+        combine: str = "assoc",
+        combine_chunk: int = 1024,
         combine_tile: int = 4,
         jordan_flows: bool = False,
     ):
@@ -87,20 +103,22 @@ class EWS(nn.Module):
         self.chen_expm = _normalize_expm_method(chen_expm)
         if leaf not in LEAF_KINDS:
             raise ValueError(f"leaf must be one of {LEAF_KINDS}, got {leaf!r}")
-        if leaf in ("series", "block_series") and series_q is None:
-            raise ValueError(f"leaf={leaf!r} requires series_q (see check_series_q)")
+        if leaf == "series" and series_q is None:
+            raise ValueError("leaf='series' requires series_q (see ews.core.leaf.check_series_q)")
         if combine not in COMBINE_KINDS:
             raise ValueError(f"combine must be one of {COMBINE_KINDS}, got {combine!r}")
-        if combine != "b200":
+        if leaf == "block_series" and N == 2 and series_q is None:
+            raise ValueError("leaf='block_series' at depth 2 requires series_q")
+        if leaf not in ("series", "block_series", "van_loan"):
             raise NotImplementedError(
-                f"combine={combine!r} is one of the reference's JAX engines; this package implements combine='b200'"
+                f"leaf={leaf!r} is not built on the B200 engines; use leaf='series' (or 'van_loan' for a diagonal A)"
             )
-        if leaf not in ("series", "block_series"):
-            raise NotImplementedError(f"leaf={leaf!r} is not built on the B200 engines; use leaf='series'")
         self.leaf = leaf
-        self.series_q = int(series_q)
+        self.series_q = None if series_q is None else int(series_q)
         self.combine = combine
         self.combine_chunk = int(combine_chunk)
+        # the chunk length the engines get (0: the library's choice)
+        self._chunk = self.combine_chunk if combine == "b200" else 0
         self.combine_tile = int(combine_tile)
         self.block_sizes = block_sizes_of(self.A_param)
         if leaf == "block_series" and self.block_sizes is None:
@@ -118,6 +136,12 @@ class EWS(nn.Module):
             self.engine = "diag" if is_diagonal(self.A_param) else "dense"
         else:
             raise NotImplementedError("the B200 engines are built for depths N=2 and N=3")
+        if leaf == "van_loan" and not (self.engine == "diag" and reweighting_mode != "displacement"):
+            raise NotImplementedError(
+                "leaf='van_loan' runs on the B200 engines for a diagonal A under a uniform clock "
+                "(reweighting_mode='displacement_uniform' or 'displacement_uniform_basepoint'); "
+                "use leaf='series' with series_q for the other engines and modes"
+            )
 
     @property
     def signature_dim(self) -> int:
@@ -144,10 +168,12 @@ class EWS(nn.Module):
         clock = clock.to(torch.float32)
         h = (clock[:, 2] - clock[:, 1]) if basepoint else (clock[:, 1] - clock[:, 0])
         x = -h[:, None] * lam[None, :]
-        q1, q2 = series.diag_tables(x, self.series_q)
-        flags = _lib.EWS_F_UNIFORM | (_lib.EWS_F_BASEPOINT if basepoint else 0)
-        if _DETERMINISTIC:
-            flags |= _lib.EWS_F_DETERMINISTIC
+        if self.leaf == "van_loan":
+            q1, q2 = series.vanloan_diag_tables(lam, h, self.M, self.van_loan_expm)
+            q1, q2 = q1.to(torch.float32), q2.to(torch.float32)
+        else:
+            q1, q2 = series.diag_tables(x, self.series_q)
+        flags = _lib.EWS_F_UNIFORM | (_lib.EWS_F_BASEPOINT if basepoint else 0) | _det_flags()
         if increments:
             flags |= _lib.EWS_F_INCREMENTS
             if path.dtype == torch.bfloat16:
@@ -156,7 +182,7 @@ class EWS(nn.Module):
                 path = path.to(torch.float32)
         else:
             path = path.to(torch.float32)
-        return engine.DiagScan.apply(path, x, q1, q2, lift, kernel_readout, flags, self.combine_chunk, increments)
+        return engine.DiagScan.apply(path, x, q1, q2, lift, kernel_readout, flags, self._chunk, increments)
 
     def _flat_block(self, path, clock, readout, a_scale, lift, increments):
         """Depth 3 on 2x2 blocks: every interval has its own clock step (ews/core/chen_scan.py:155-168); a
@@ -168,7 +194,7 @@ class EWS(nn.Module):
         K = self.d // 2
         blocks = torch.stack([A[2 * k : 2 * k + 2, 2 * k : 2 * k + 2] for k in range(K)])
         kernel_readout = _lib.EWS_READOUT_TERMINAL if readout == "terminal" else _lib.EWS_READOUT_PREFIX
-        flags = _lib.EWS_F_DETERMINISTIC if _DETERMINISTIC else 0
+        flags = _det_flags()
         if increments:
             flags |= _lib.EWS_F_INCREMENTS
             if path.dtype == torch.bfloat16:
@@ -184,11 +210,11 @@ class EWS(nn.Module):
         if kernel_readout == _lib.EWS_READOUT_TERMINAL and needs_grad:
             # the block backward runs on the prefix stream (the terminal value is its last row)
             out = engine.BlockScan.apply(
-                path, clock, blocks, lift, _lib.EWS_READOUT_PREFIX, flags, self.combine_chunk, increments, self.series_q
+                path, clock, blocks, lift, _lib.EWS_READOUT_PREFIX, flags, self._chunk, increments, self.series_q
             )
             return out[:, -1]
         return engine.BlockScan.apply(
-            path, clock, blocks, lift, kernel_readout, flags, self.combine_chunk, increments, self.series_q
+            path, clock, blocks, lift, kernel_readout, flags, self._chunk, increments, self.series_q
         )
 
     def _flat_diag_clock(self, path, clock, kernel_readout, a_scale, lift, increments):
@@ -199,7 +225,7 @@ class EWS(nn.Module):
         rates = -(self.A_param.diag_values().to(torch.float32) * a_scale)
         B = path.shape[0]
         rates = rates[None, :].expand(B, -1)
-        flags = _lib.EWS_F_DETERMINISTIC if _DETERMINISTIC else 0
+        flags = _det_flags()
         if increments:
             flags |= _lib.EWS_F_INCREMENTS
             if path.dtype == torch.bfloat16:
@@ -209,7 +235,7 @@ class EWS(nn.Module):
         else:
             path = path.to(torch.float32)
         return engine.DiagScanClock.apply(
-            path, clock.to(torch.float32), rates, lift, kernel_readout, flags, self.combine_chunk, increments, self.series_q
+            path, clock.to(torch.float32), rates, lift, kernel_readout, flags, self._chunk, increments, self.series_q
         )
 
     def _flat_dense(self, path, clock, readout, a_scale, lift, increments, basepoint):
@@ -219,7 +245,7 @@ class EWS(nn.Module):
         clock = clock.to(torch.float32)
         h = clock[:, 1] - clock[:, 0]
         M, F, G, H = series.dense_tables(A, h, self.series_q, lift)
-        flags = _lib.EWS_F_UNIFORM | (_lib.EWS_F_DETERMINISTIC if _DETERMINISTIC else 0)
+        flags = _lib.EWS_F_UNIFORM | _det_flags()
         if increments:
             flags |= _lib.EWS_F_INCREMENTS
             if path.dtype == torch.bfloat16:
@@ -230,9 +256,9 @@ class EWS(nn.Module):
             path = path.to(torch.float32)
         needs_grad = torch.is_grad_enabled() and any(t.requires_grad for t in (path, M, F, G, H))
         if readout == "terminal" and not needs_grad:
-            return engine.DenseScan.apply(path, M, F, G, H, _lib.EWS_READOUT_TERMINAL, flags, self.combine_chunk, increments)
+            return engine.DenseScan.apply(path, M, F, G, H, _lib.EWS_READOUT_TERMINAL, flags, self._chunk, increments)
         # the dense backward runs on the prefix stream (the terminal value is its last row)
-        out = engine.DenseScan.apply(path, M, F, G, H, _lib.EWS_READOUT_PREFIX, flags, self.combine_chunk, increments)
+        out = engine.DenseScan.apply(path, M, F, G, H, _lib.EWS_READOUT_PREFIX, flags, self._chunk, increments)
         return out[:, -1] if readout == "terminal" else out
 
     def forward(

@@ -14,63 +14,76 @@ Q1_i = sum_p c_p x_i^p / p!  and  Q2_ij = sum_{a+b<=q} c_ab x_i^a x_j^b / (a! b!
 from __future__ import annotations
 
 import math
-from fractions import Fraction
 from functools import lru_cache
-from itertools import product as _iproduct
 
 import numpy as np
 import torch
 
 
-def coeff_exact(m) -> Fraction:
-    """c_m as an exact rational (ews/core/series_leaf.py:45-52)."""
+def level_coefficient(m) -> float:
+    """c_m for the multi-index m = (m_1, ..., m_k): with the suffix sums M_j = m_j + ... + m_k, the k
+    nested integrals over the simplex contribute the factors 1 / (M_j + k - j + 1)."""
     k = len(m)
-    out = Fraction(1)
-    for j in range(1, k + 1):
-        out /= sum(m[j - 1 :]) + k - j + 1
+    suffix = 0
+    out = 1.0
+    for j in range(k, 0, -1):  # innermost integral first
+        suffix += m[j - 1]
+        out /= suffix + (k - j + 1)
     return out
 
 
 @lru_cache(maxsize=None)
-def series_coeffs(depth: int, q: int):
-    """Level-k coefficient tensors (q+1,)*k, zero where |m| > q (ews/core/series_leaf.py:55-66)."""
-    out = []
-    for k in range(1, depth + 1):
-        C = np.zeros((q + 1,) * k, dtype=np.float64)
-        for m in _iproduct(range(q + 1), repeat=k):
-            if sum(m) <= q:
-                C[m] = float(coeff_exact(m))
-        out.append(C)
-    return tuple(out)
+def coefficient_tables(q: int):
+    """The depth-1 and depth-2 coefficients the engines use, as float64 arrays with zeros where the
+    order exceeds q: c1[p] = 1 / (p + 1) and c2[a, b] = 1 / ((a + b + 2) (b + 1))."""
+    p = np.arange(q + 1, dtype=np.float64)
+    c1 = 1.0 / (p + 1.0)
+    a, b = np.meshgrid(p, p, indexing="ij")
+    c2 = np.where(a + b <= q, 1.0 / ((a + b + 2.0) * (b + 1.0)), 0.0)
+    return c1, c2
 
 
 def series_error_bound(x: float, k: int, q: int) -> float:
-    """Per-interval relative error bound at level k (ews/core/series_leaf.py:139-143)."""
-    return (k * x) ** (q + 1) / math.factorial(q + 1) * math.exp(k * x)
+    """Per-interval relative error of the level-k series truncated at order q, for x = ||A|| dtheta: the
+    first omitted term of exp(k x), (k x)^(q+1) / (q+1)!, times the tail factor e^{k x}."""
+    kx = k * x
+    term = 1.0
+    for n in range(1, q + 2):
+        term *= kx / n
+    return term * math.exp(kx)
 
 
 def suggest_series_q(x, trunc, tol=1e-6, q_max=200):
-    """Smallest q whose level-``trunc`` bound is below tol (ews/core/leaf.py:201-215)."""
+    """The smallest order q >= 1 whose level-``trunc`` error bound is below ``tol`` (the reference's
+    ``ews.core.leaf.suggest_series_q``). The bound's terms are followed as logarithms, so large x does not
+    overflow."""
     if x <= 0.0:
         return 1
-    lx, ltol = math.log(trunc * x), math.log(tol)
+    log_kx = math.log(trunc * x)
+    log_term = log_kx  # log of (k x)^(q+1) / (q+1)! at q = 0
+    target = math.log(tol) - trunc * x
     for q in range(1, q_max):
-        if (q + 1) * lx - math.lgamma(q + 2) + trunc * x < ltol:
+        log_term += log_kx - math.log(q + 1)
+        if log_term < target:
             return q
     return q_max
 
 
 def check_series_q(A, dtheta_max, trunc, series_q, tol=1e-6, where=""):
-    """Warns when series_q is too small for x = ||A||_op max dtheta (ews/core/leaf.py:218-238)."""
+    """Warns (RuntimeWarning) when ``series_q`` leaves a per-interval error bound above ``tol`` at the
+    observed x = ||A||_2 max dtheta; returns (x, bound, the order that would meet tol), like the
+    reference's ``ews.core.leaf.check_series_q``."""
     import warnings
 
     x = float(torch.linalg.matrix_norm(torch.as_tensor(A, dtype=torch.float64), 2)) * float(dtheta_max)
     bound = series_error_bound(x, int(trunc), int(series_q))
     need = suggest_series_q(x, int(trunc), tol=tol)
     if bound > tol:
+        tag = f" ({where})" if where else ""
         warnings.warn(
-            f"[series leaf{' ' + where if where else ''}] series_q={series_q} gives a per-interval error bound "
-            f"of {bound:.2e} at x={x:.3f} (||A||*max dtheta), above tol={tol:.0e}. series_q={need} would suffice.",
+            f"series leaf{tag}: order {series_q} bounds the local error by {bound:.2e} at "
+            f"x = ||A|| max dtheta = {x:.3f}, above {tol:.0e}; order {need} meets it (the order is fixed "
+            "when the layer is built)",
             RuntimeWarning,
             stacklevel=2,
         )
@@ -80,7 +93,7 @@ def check_series_q(A, dtheta_max, trunc, series_q, tol=1e-6, where=""):
 @lru_cache(maxsize=None)
 def _scaled_coeffs(q: int, device: str, dtype: torch.dtype):
     """c1_p / p!  (q+1,)  and  c2_ab / (a! b!)  (q+1, q+1), the polynomial coefficients of Q1, Q2 in x."""
-    C1, C2 = series_coeffs(2, q)
+    C1, C2 = coefficient_tables(q)
     fact = np.array([math.factorial(p) for p in range(q + 1)], dtype=np.float64)
     c1 = C1 / fact
     c2 = C2 / np.outer(fact, fact)
@@ -107,7 +120,7 @@ def diag_tables(x: torch.Tensor, q: int):
 def _leaf_coeffs(q: int, device: str):
     """c_p (q+1,) and c_ab (q+1, q+1) of the depth-2 series leaf as float64 tensors on ``device``, made
     once per (q, device) so that building the tables issues no host-to-device copy."""
-    C1, C2 = series_coeffs(2, q)
+    C1, C2 = coefficient_tables(q)
     return (torch.tensor(C1, dtype=torch.float64, device=device), torch.tensor(C2, dtype=torch.float64, device=device))
 
 
@@ -140,3 +153,58 @@ def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None):
     Dc = torch.eye(N, dtype=torch.float64, device=A.device) - Expm.apply(X)
     F, G, H = dense_leaf_tables(X, q, lift)
     return Dc.float(), F.float(), G.float(), H.float()
+
+
+# ------------------------------------------------------------------------------ Van Loan leaf tables
+
+
+def _vanloan_step(z: torch.Tensor, method: str):
+    """For the augmented step matrix X = [[z, v], [0, 0]] of one coordinate (z = a dtheta / M, a the
+    generator's diagonal entry, v the increment / M), the chosen exponential gives
+    E(X) = [[c, g v], [0, 1]]; returns (c, g). Derived per method from the reference's formulas
+    (ews/core/expm_approx.py:13-41): exact c = e^z, g = (e^z - 1) / z; euler c = 1 + z, g = 1;
+    cayley (I - X/2)^{-1} (I + X/2): c = (1 + z/2) / (1 - z/2), g = 1 / (1 - z/2); pade (2, 2):
+    c = (1 + z/2 + z^2/12) / (1 - z/2 + z^2/12), g = 1 / (1 - z/2 + z^2/12)."""
+    if method == "exact":
+        c = torch.exp(z)
+        small = z.abs() < 1e-8
+        zs = torch.where(small, torch.ones_like(z), z)
+        g = torch.where(small, 1.0 + z / 2, torch.expm1(zs) / zs)
+        return c, g
+    if method == "euler":
+        return 1.0 + z, torch.ones_like(z)
+    if method == "cayley":
+        den = 1.0 - z / 2
+        return (1.0 + z / 2) / den, 1.0 / den
+    if method == "pade":
+        z2 = z * z / 12.0
+        den = 1.0 - z / 2 + z2
+        return (1.0 + z / 2 + z2) / den, 1.0 / den
+    raise ValueError(f"unknown expm method {method!r}")
+
+
+def vanloan_diag_tables(lam: torch.Tensor, h: torch.Tensor, M: int, method: str = "cayley", eps: float = 1e-12):
+    """Q1 (B, N), Q2 (B, N, N) of the Van Loan leaf (the reference's default local terms,
+    ews/core/van_loan.py:91-144 and ews/core/signature.py:19-36) for a diagonal generator
+    A = diag(lam) under a uniform clock step h (B,), so that s1_i = Q1_i dy_i and s2_ij = Q2_ij dy_i dy_j
+    as in the series tables. Differentiable; float64 in, float64 out.
+
+    With A diagonal the augmented exponential acts coordinate by coordinate. The leaf's M + 1 knots
+    k_m = E_A^{-M} (sum_{j<m} E_A^j) g v are those of a piecewise-linear path whose m-th segment is
+    p_m dy with p_m = g c^{m-1-M} / M (m = 1..M); the depth-2 signature of M segments is
+    level 1 = sum_m p_m dy and level 2 = (sum_{m<n} p_m (x) p_n + 1/2 sum_m p_m (x) p_m) dy (x) dy.
+    A step below ``eps`` is the reference's jump case (linear interpolation): Q1 = 1, Q2 = 1/2."""
+    lam = lam.to(torch.float64)
+    h = h.to(torch.float64)
+    z = (h[:, None] * lam[None, :]) / M  # (B, N)
+    c, g = _vanloan_step(z, method)
+    m = torch.arange(1, M + 1, dtype=torch.float64, device=lam.device)
+    P = (g[..., None] / M) * c[..., None] ** (m - 1 - M)  # (B, N, M)
+    jump = (h <= eps)[:, None, None]
+    P = torch.where(jump, torch.full_like(P, 1.0 / M), P)
+    q1 = P.sum(-1)
+    # R[j, m] = 1/2 p_{m,j} + sum_{n>m} p_{n,j}
+    tail = torch.flip(torch.cumsum(torch.flip(P, [-1]), -1), [-1]) - P
+    R = 0.5 * P + tail
+    q2 = torch.einsum("bim,bjm->bij", P, R)
+    return q1, q2

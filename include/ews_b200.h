@@ -145,6 +145,12 @@ int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream);
 #define EWS_NOALLOC_SCRATCH_BYTES (16u << 20)
 int ews_diag_fwd_noalloc(const ews_diag_args* a, ews_stream_t stream);
 
+/* Status of the last no-alloc forward on the current device: copies the error word at the start of the
+ * library's array (EWS_OK or EWS_ERR_LOOKBACK_TIMEOUT) to *status; synchronises the stream. Like the array,
+ * it has no counterpart in the reference: the no-alloc caller holds no workspace pointer to pass to
+ * ews_read_device_status. */
+int ews_diag_fwd_noalloc_status(ews_stream_t stream, int* status);
+
 /* ---- dense engine: any generator A (uniform clock) --------------------------------------------
  * Replaces combine_packed(kind="dense_kernel" / "lean") fed by leaf="series" (ews/core/kernels/combine.py:
  * 260-269, ews/core/kernels/pallas_combine.py:803-858 forward, :2628-2711 custom VJP) with the series
@@ -236,9 +242,16 @@ int ews_expm_batched(const double* x, double* out, int batch, int n, ews_stream_
 int ews_expm_adjoint_batched(const double* x, const double* g, double* out, int batch, int n, ews_stream_t stream);
 
 /* ---- utilities --------------------------------------------------------------------------------- */
+/* Every forward and backward workspace begins with a status block whose error word the call clears and
+ * a timed-out device wait sets. */
 /* Copies the device-side status word of a workspace (EWS_OK or EWS_ERR_LOOKBACK_TIMEOUT) to the host;
  * synchronises the stream. */
 int ews_read_device_status(const void* workspace, ews_stream_t stream, int* status);
+/* Stream-ordered, no synchronisation: after the workspace's call, folds its error word into *sticky, a
+ * caller-owned device int (the first non-zero code is kept; the caller clears it). A host that copies
+ * *sticky to pinned memory asynchronously learns of a timeout without waiting on the GPU, and can raise
+ * it as the reference raises its errors (ews/layer.py:112-152). */
+int ews_status_fold(const void* workspace, int* sticky, ews_stream_t stream);
 const char* ews_error_string(int code);
 int ews_version(void);
 

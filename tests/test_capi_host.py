@@ -148,13 +148,25 @@ def test_layer_validation_mirrors_reference():
         EWS(A, N=2, reweighting_mode="bogus")
     with pytest.raises(ValueError):
         EWS(A, N=2, chen_expm="bogus")
+    with pytest.raises(ValueError):
+        EWS(A, N=2, leaf="bogus")
+    # the reference's defaults: Van Loan leaf, associative combine (every combine kind runs the engines)
+    d = EWS(A, N=2, reweighting_mode="displacement_uniform")
+    assert (d.leaf, d.series_q, d.combine, d.combine_chunk, d.M) == ("van_loan", None, "assoc", 1024, 20)
+    assert EWS(A, N=2, reweighting_mode="displacement_uniform", combine="lean").engine == "diag"
+    # Van Loan runs on the diagonal engine under a uniform clock; elsewhere it raises instead of
+    # silently computing another leaf
     with pytest.raises(NotImplementedError):
-        EWS(A, N=2, combine="assoc")
+        EWS(A, N=2)  # default mode "displacement": per-interval clock
+    with pytest.raises(NotImplementedError):
+        EWS(torch.eye(4), N=2, reweighting_mode="displacement_uniform")
+    with pytest.raises(NotImplementedError):
+        EWS(A, N=2, leaf="jordan_closed")
     layer = EWS(AParamEFM(torch.zeros(3)), N=2, reweighting_mode="displacement_uniform")
     assert layer.engine == "diag" and layer.block_sizes == (1, 1, 1)
-    assert EWS(AParamBlockDiag([torch.ones(1, 1)] * 3, [1, 1, 1]), N=2).engine == "diag"
+    assert EWS(AParamBlockDiag([torch.ones(1, 1)] * 3, [1, 1, 1]), N=2, leaf="series", series_q=4).engine == "diag"
     assert layer.signature_dim == 3 + 9
-    assert LogEWS(A, N=2).log_signature_dim == 4 + 6
+    assert LogEWS(A, N=2, reweighting_mode="displacement_uniform").log_signature_dim == 4 + 6
 
 
 def test_readout_validation():

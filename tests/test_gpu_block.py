@@ -64,7 +64,7 @@ def _oracle(path, clock, A, lift, readout, q, w=None):
     ck = torch.tensor(clock, requires_grad=True)
     At = torch.tensor(A, requires_grad=True)
     Bm = torch.tensor(lift, requires_grad=True)
-    out = O.ews_layer(O.lift(p, Bm), ck, At, 3, series_q=q, reweighting_mode="displacement", readout=readout)
+    out = O.ews_layer(O.lift(p, Bm), ck, At, 3, leaf="series", series_q=q, reweighting_mode="displacement", readout=readout)
     if w is None:
         return out.detach(), None
     (out * w.double()).sum().backward()
@@ -80,7 +80,7 @@ def _kernel(path, clock, A, lift, readout, q, w=None, chunk=0):
     N = A.shape[0]
     blocks = [torch.tensor(A[2 * k : 2 * k + 2, 2 * k : 2 * k + 2], dtype=torch.float32) for k in range(N // 2)]
     Ap = AParamBlockDiag(blocks, (2,) * (N // 2)).to(DEV)
-    layer = EWS(Ap, N=3, reweighting_mode="displacement", series_q=q, combine_chunk=chunk)
+    layer = EWS(Ap, N=3, reweighting_mode="displacement", leaf="series", series_q=q, combine="b200", combine_chunk=chunk)
     p = torch.tensor(path, dtype=torch.float32, device=DEV, requires_grad=True)
     ck = torch.tensor(clock, dtype=torch.float32, device=DEV, requires_grad=True)
     Bm = torch.tensor(lift, dtype=torch.float32, device=DEV, requires_grad=True)

@@ -43,7 +43,7 @@ def _oracle(path, clock, A, lift, readout, q, w=None, dtype=torch.float64):
     Am = torch.tensor(A, dtype=dtype, requires_grad=True)
     Bm = None if lift is None else torch.tensor(lift, dtype=dtype, requires_grad=True)
     y = p if Bm is None else O.lift(p, Bm)
-    out = O.ews_layer(y, torch.tensor(clock, dtype=dtype), Am, 2, series_q=q, reweighting_mode="displacement_uniform", readout=readout)
+    out = O.ews_layer(y, torch.tensor(clock, dtype=dtype), Am, 2, leaf="series", series_q=q, reweighting_mode="displacement_uniform", readout=readout)
     if w is None:
         return out.detach().double(), None
     (out * w.to(dtype)).sum().backward()
@@ -54,7 +54,7 @@ def _kernel(path, clock, A, lift, readout, q, w=None, chunk=0):
     from exponentially_weighted_signature_b200 import EWS, AParamGeneral
 
     Ap = AParamGeneral(torch.tensor(A, dtype=torch.float32)).to(DEV)
-    layer = EWS(Ap, N=2, reweighting_mode="displacement_uniform", series_q=q, combine_chunk=chunk)
+    layer = EWS(Ap, N=2, reweighting_mode="displacement_uniform", leaf="series", series_q=q, combine="b200", combine_chunk=chunk)
     p = torch.tensor(path, dtype=torch.float32, device=DEV, requires_grad=True)
     Bm = None if lift is None else torch.tensor(lift, dtype=torch.float32, device=DEV, requires_grad=True)
     out = layer(p, torch.tensor(clock, dtype=torch.float32, device=DEV), readout=readout, lift=Bm)

@@ -54,7 +54,7 @@ def _oracle(path, clock, lam, lift, readout, mode="displacement_uniform", w=None
     L = torch.tensor(lam, dtype=dtype, requires_grad=True)
     Bm = None if lift is None else torch.tensor(lift, dtype=dtype, requires_grad=True)
     y = p if Bm is None else O.lift(p, Bm)
-    out = O.ews_layer(y, torch.tensor(clock, dtype=dtype), torch.diag(L), 2, series_q=Q, reweighting_mode=mode, readout=readout)
+    out = O.ews_layer(y, torch.tensor(clock, dtype=dtype), torch.diag(L), 2, leaf="series", series_q=Q, reweighting_mode=mode, readout=readout)
     if w is None:
         return out.detach().double(), None
     (out * w.to(dtype)).sum().backward()
@@ -66,7 +66,7 @@ def _kernel(path, clock, lam, lift, readout, mode="displacement_uniform", w=None
     from exponentially_weighted_signature_b200 import EWS, AParamDiag
 
     A = AParamDiag(torch.tensor(lam, dtype=torch.float32)).to(DEV)
-    layer = EWS(A, N=2, reweighting_mode=mode, series_q=Q, combine_chunk=chunk)
+    layer = EWS(A, N=2, reweighting_mode=mode, leaf="series", series_q=Q, combine="b200", combine_chunk=chunk)
     p = torch.tensor(path, dtype=torch.float32, device=DEV, requires_grad=True)
     Bm = None if lift is None else torch.tensor(lift, dtype=torch.float32, device=DEV, requires_grad=True)
     out = layer(p, torch.tensor(clock, dtype=torch.float32, device=DEV), readout=readout, lift=Bm)
@@ -236,7 +236,7 @@ def test_bf16_increments():
     lam = _f32(np.exp(rng.uniform(-4, 0, N)))
     clock = _f32(np.broadcast_to(np.arange(T + 1) / T, (B, T + 1)).copy())
     inc_bf = torch.tensor(inc, dtype=torch.float32).to(torch.bfloat16)
-    layer = EWS(AParamDiag(torch.tensor(lam, dtype=torch.float32)).to(DEV), N=2, reweighting_mode="displacement_uniform", series_q=Q)
+    layer = EWS(AParamDiag(torch.tensor(lam, dtype=torch.float32)).to(DEV), N=2, reweighting_mode="displacement_uniform", leaf="series", series_q=Q)
     out = layer(inc_bf.to(DEV), torch.tensor(clock, dtype=torch.float32, device=DEV), readout="terminal", increments=True).detach().cpu().double()
     path_exact = np.concatenate([np.zeros((B, 1, N)), np.cumsum(inc, 1)], 1)
     path_round = np.concatenate([np.zeros((B, 1, N)), np.cumsum(inc_bf.double().numpy(), 1)], 1)

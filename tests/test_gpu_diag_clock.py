@@ -52,7 +52,7 @@ def _oracle(path, clock, lam, lift, readout, q, w=None):
     ck = torch.tensor(clock, requires_grad=True)
     L = torch.tensor(lam, requires_grad=True)
     Bm = torch.tensor(lift, requires_grad=True)
-    out = O.ews_layer(O.lift(p, Bm), ck, torch.diag(L), 2, series_q=q, reweighting_mode="displacement", readout=readout)
+    out = O.ews_layer(O.lift(p, Bm), ck, torch.diag(L), 2, leaf="series", series_q=q, reweighting_mode="displacement", readout=readout)
     if w is None:
         return out.detach(), None
     (out * w.double()).sum().backward()
@@ -63,7 +63,7 @@ def _kernel(path, clock, lam, lift, readout, q, w=None, chunk=0):
     from exponentially_weighted_signature_b200 import EWS, AParamDiag
 
     A = AParamDiag(torch.tensor(lam, dtype=torch.float32)).to(DEV)
-    layer = EWS(A, N=2, reweighting_mode="displacement", series_q=q, combine_chunk=chunk)
+    layer = EWS(A, N=2, reweighting_mode="displacement", leaf="series", series_q=q, combine="b200", combine_chunk=chunk)
     p = torch.tensor(path, dtype=torch.float32, device=DEV, requires_grad=True)
     ck = torch.tensor(clock, dtype=torch.float32, device=DEV, requires_grad=True)
     Bm = torch.tensor(lift, dtype=torch.float32, device=DEV, requires_grad=True)

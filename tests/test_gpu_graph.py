@@ -26,21 +26,21 @@ def _layer(kind, N):
     rng = np.random.default_rng(0)
     if kind == "diag":
         A = AParamDiag(torch.tensor(np.exp(rng.uniform(-3, 1, N)), dtype=torch.float32))
-        return EWS(A, N=2, reweighting_mode="displacement_uniform", series_q=4, combine_chunk=16)
+        return EWS(A, N=2, reweighting_mode="displacement_uniform", leaf="series", series_q=4, combine="b200", combine_chunk=16)
     if kind == "diag_clock":
         A = AParamDiag(torch.tensor(np.exp(rng.uniform(-3, 1, N)), dtype=torch.float32))
-        return EWS(A, N=2, reweighting_mode="displacement", series_q=4, combine_chunk=16)
+        return EWS(A, N=2, reweighting_mode="displacement", leaf="series", series_q=4, combine="b200", combine_chunk=16)
     if kind == "logews":
         A = AParamDiag(torch.tensor(np.exp(rng.uniform(-4, 0, N)), dtype=torch.float32))
-        return LogEWS(A, N=2, reweighting_mode="displacement_uniform", series_q=4, combine_chunk=16)
+        return LogEWS(A, N=2, reweighting_mode="displacement_uniform", leaf="series", series_q=4, combine="b200", combine_chunk=16)
     if kind == "dense":
         A = 0.5 * np.eye(N) - 0.1 * rng.normal(size=(N, N)) / np.sqrt(N)
         return EWS(AParamGeneral(torch.tensor(A, dtype=torch.float32)), N=2, reweighting_mode="displacement_uniform",
-                   series_q=3, combine_chunk=16)
+                   leaf="series", series_q=3, combine="b200", combine_chunk=16)
     blocks = [torch.tensor([[a, w], [-w, a]], dtype=torch.float32)
               for a, w in zip(rng.uniform(0.05, 1, N // 2), rng.uniform(0, np.pi, N // 2))]
-    return EWS(AParamBlockDiag(blocks, (2,) * (N // 2)), N=3, reweighting_mode="displacement", series_q=4,
-               combine_chunk=16)
+    return EWS(AParamBlockDiag(blocks, (2,) * (N // 2)), N=3, reweighting_mode="displacement", leaf="series", series_q=4,
+               combine="b200", combine_chunk=16)
 
 
 def _inputs(seed, B, T, d, N):

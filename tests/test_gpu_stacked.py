@@ -30,7 +30,7 @@ class _OracleEWS(nn.Module):
 
     def forward(self, path, clock, readout="prefix", output_format="flat"):
         A = torch.diag(self.A_param.values)
-        return O.ews_layer(path, clock, A, 2, series_q=self.q, reweighting_mode="displacement", readout=readout)
+        return O.ews_layer(path, clock, A, 2, leaf="series", series_q=self.q, reweighting_mode="displacement", readout=readout)
 
 
 def _build(seed=0, blocks=2, H=16, m=4, T=24, B=2, q=6):

@@ -68,6 +68,48 @@ def test_noalloc_forward_matches_the_workspace_forward():
         assert bool((err <= 1e-6 + 1e-5 * ref.abs()).all())
 
 
+def _noalloc_status(lib):
+    from exponentially_weighted_signature_b200 import _lib
+
+    st = ctypes.c_int(-1)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.ews_diag_fwd_noalloc_status(stream, ctypes.byref(st)) == _lib.EWS_OK
+    return st.value
+
+
+def test_noalloc_status_reports_a_timeout():
+    """The no-alloc caller holds no workspace pointer, so ews_diag_fwd_noalloc_status reads the status
+    word at the start of the library's array: clear after a good call, EWS_ERR_LOOKBACK_TIMEOUT after a
+    call whose look-back waits ran out (EWS_F_TEST_WITHHOLD with a short spin limit), clear again after
+    the next good call."""
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test run without a CUDA device")
+    from exponentially_weighted_signature_b200 import _lib, series
+
+    lib = _lib.load()
+    dev = torch.device("cuda")
+    B, T, N = 2, 256, 16
+    path = torch.randn(B, T + 1, N, device=dev)
+    x = torch.full((B, N), -1e-3, device=dev)
+    q1, q2 = series.diag_tables(x, 4)
+    q1, q2 = q1.contiguous(), q2.contiguous()
+    out = torch.empty(B, T, 1 + N + N * N, device=dev)
+    a = _lib.DiagArgs()
+    a.batch, a.steps, a.d_in, a.dim, a.depth, a.chunk = B, T, N, N, 2, 8
+    a.readout, a.flags = 0, _lib.EWS_F_UNIFORM
+    a.path, a.tab_x, a.tab_q1, a.tab_q2, a.out = (ctypes.c_void_p(t.data_ptr()) for t in (path, x, q1, q2, out))
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.ews_diag_fwd_noalloc(ctypes.byref(a), stream) == 0
+    assert _noalloc_status(lib) == _lib.EWS_OK
+    a.flags, a.spin_limit = _lib.EWS_F_UNIFORM | _lib.EWS_F_TEST_WITHHOLD, 2000
+    assert lib.ews_diag_fwd_noalloc(ctypes.byref(a), stream) == 0
+    assert _noalloc_status(lib) == _lib.EWS_ERR_LOOKBACK_TIMEOUT
+    a.flags, a.spin_limit = _lib.EWS_F_UNIFORM, 0
+    assert lib.ews_diag_fwd_noalloc(ctypes.byref(a), stream) == 0
+    assert _noalloc_status(lib) == _lib.EWS_OK
+    torch.cuda.synchronize()
+
+
 def test_noalloc_rejects_oversized_problems():
     if not torch.cuda.is_available():
         pytest.fail("GPU test run without a CUDA device")
