@@ -86,6 +86,7 @@ class DiagArgs(ctypes.Structure):
         ("bwd_ws", _vp),
         ("bwd_ws_bytes", _c_size),
         ("grad_dtheta", _vp),
+        ("leaf_coef", _vp),
     ]
 
 

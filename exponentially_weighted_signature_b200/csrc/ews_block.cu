@@ -74,7 +74,7 @@ struct Params {
     float c3[KQ * KQ * KQ];   // c3_prs = 1 / ((p + r + s + 3)(r + s + 2)(s + 1))
 };
 
-__host__ __device__ inline int align4(int n) { return (n + 3) & ~3; }
+__host__ __device__ constexpr int align4(int n) { return (n + 3) & ~3; }
 
 // ------------------------------------------------------------------------------ 2x2 block flows
 
@@ -1604,6 +1604,11 @@ int pick_chunk(int B, int T) {
     int Lc = (T + C - 1) / C;
     return std::max(8, std::min(64, Lc));
 }
+
+// The backward's zero-carry pass stages two local elements (2 LROW floats) at b_loc, across the Loc and
+// AdjBuf areas that pass leaves idle; b_gst, which the same loop fills with cp.async, starts right after.
+static_assert(2 * LROW <= align4(Loc::floats) + align4(AdjBuf::floats),
+              "the zero-carry pass's two staged local elements must fit in the Loc + AdjBuf areas");
 
 int make_geom(const ews_block_args* a, Geom* g) {
     if (!a || a->batch <= 0 || a->steps <= 0 || a->d_in <= 0 || a->dim <= 0) return EWS_ERR_INVALID_ARGUMENT;

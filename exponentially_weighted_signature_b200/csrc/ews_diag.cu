@@ -1698,7 +1698,12 @@ static int launch_bwd(const Params& p, cudaStream_t s) {
 
 // Coefficients of the in-kernel series tables: c1_p / p! = 1 / ((p+1) p!) and
 // c2_ab / (a! b!) = 1 / ((a+b+2)(b+1) a! b!) for a + b <= q (ews/core/series_leaf.py:45-66), zero above.
-static void series_coefficients(int q, Params* p) {
+static void series_coefficients(int q, Params* p, const float* leaf_coef) {
+    if (leaf_coef) {  // the caller's polynomial coefficients (another leaf, e.g. Van Loan's): k1 | k2 rows
+        for (int a = 0; a < kQNU; ++a) p->c1[a] = leaf_coef[a];
+        for (int e = 0; e < kQNU * kQNU; ++e) p->c2[e] = leaf_coef[kQNU + e];
+        return;
+    }
     double fact[kQNU];
     fact[0] = 1.0;
     for (int i = 1; i < kQNU; ++i) fact[i] = fact[i - 1] * i;
@@ -1763,7 +1768,7 @@ extern "C" int ews_diag_fwd(const ews_diag_args* a, ews_stream_t stream) {
     p.incl = (float*)(ws + L.incl);
     p.carry = (float*)(ws + L.carry);
     p.clock = a->clock;
-    series_coefficients(a->series_q, &p);
+    series_coefficients(a->series_q, &p, a->leaf_coef);
     switch (g.NP) {
         case 8: return launch_fwd<8>(p, s);
         case 16: return launch_fwd<16>(p, s);
@@ -1810,7 +1815,7 @@ extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
     p.fcarry = (const float*)(fws + F.carry);
     p.clock = a->clock;
     p.grad_dtheta = a->grad_dtheta;
-    series_coefficients(a->series_q, &p);
+    series_coefficients(a->series_q, &p, a->leaf_coef);
     switch (g.NP) {
         case 8: rc = launch_bwd<8>(p, s); break;
         case 16: rc = launch_bwd<16>(p, s); break;

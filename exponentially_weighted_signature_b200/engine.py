@@ -108,6 +108,13 @@ def _fold_status(workspace: torch.Tensor, device) -> None:
         raise_pending(device)
 
 
+def _coef_buffer(coef):
+    """Host buffer of a leaf's polynomial coefficients (9 + 81 floats) for ews_diag_args.leaf_coef, or None."""
+    if coef is None:
+        return None
+    return (ctypes.c_float * len(coef))(*[float(v) for v in coef])
+
+
 def increments_to_knots_grad(gdx: torch.Tensor) -> torch.Tensor:
     """Adjoint of dx_t = x_{t+1} - x_t: (B, T, d) -> (B, T+1, d)."""
     return F.pad(gdx, (0, 0, 1, 0)) - F.pad(gdx, (0, 0, 0, 1))
@@ -288,7 +295,7 @@ class DiagScanClock(torch.autograd.Function):
     the rates and the lift."""
 
     @staticmethod
-    def forward(ctx, path, clock, rates, lift, readout, flags, chunk, increments, series_q):
+    def forward(ctx, path, clock, rates, lift, readout, flags, chunk, increments, series_q, leaf_coef=None):
         _require_cuda(path, clock, rates, lift)
         lib = _lib.load()
         B = path.shape[0]
@@ -305,6 +312,8 @@ class DiagScanClock(torch.autograd.Function):
         a = _lib.DiagArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
         a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, SPIN_LIMIT
+        coef_buf = _coef_buffer(leaf_coef)  # kept alive until the call returns
+        a.leaf_coef = None if coef_buf is None else ctypes.cast(coef_buf, ctypes.c_void_p)
         fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
         _lib.check(lib.ews_diag_workspace_size(ctypes.byref(a), ctypes.byref(fb), ctypes.byref(bb)), "ews_diag_workspace_size")
         fwd_ws = torch.empty(fb.value, dtype=torch.uint8, device=dev)
@@ -316,6 +325,7 @@ class DiagScanClock(torch.autograd.Function):
             _lib.check(lib.ews_diag_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_diag_fwd")
         _fold_status(fwd_ws, dev)
         ctx.meta = (readout, flags, chunk, increments, series_q, B, T, d_in, N, bb.value, path.dtype, clock.dtype)
+        ctx.leaf_coef = leaf_coef
         ctx.has_lift = lift is not None
         empty = torch.empty(0, device=dev)
         ctx.save_for_backward(path_c, clock_c, rates_c, lift_c if lift_c is not None else empty, out, fwd_ws)
@@ -337,6 +347,8 @@ class DiagScanClock(torch.autograd.Function):
         a = _lib.DiagArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
         a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, series_q, SPIN_LIMIT
+        coef_buf = _coef_buffer(ctx.leaf_coef)
+        a.leaf_coef = None if coef_buf is None else ctypes.cast(coef_buf, ctypes.c_void_p)
         a.path, a.clock, a.lift, a.tab_x = _ptr(path), _ptr(clock), _ptr(lift), _ptr(rates)
         a.out, a.grad_out = _ptr(out), _ptr(g)
         a.grad_dx, a.grad_lift, a.grad_x, a.grad_dtheta = _ptr(gdx), _ptr(glift), _ptr(gr), _ptr(gdt)
@@ -348,7 +360,7 @@ class DiagScanClock(torch.autograd.Function):
         raise_pending(dev)
         gpath = gdx if increments else increments_to_knots_grad(gdx)
         gclock = increments_to_knots_grad(gdt[..., None])[..., 0]
-        return gpath.to(path_dtype), gclock.to(clock_dtype), gr, glift, None, None, None, None, None
+        return gpath.to(path_dtype), gclock.to(clock_dtype), gr, glift, None, None, None, None, None, None
 
 
 class BlockScan(torch.autograd.Function):

@@ -48,6 +48,7 @@ def _det_flags() -> int:
 
 
 READOUTS = ("terminal", "prefix", "mean", "max")
+VANLOAN_DEGREE = 8
 
 
 def _normalize_expm_method(method: str) -> str:
@@ -136,12 +137,17 @@ class EWS(nn.Module):
             self.engine = "diag" if is_diagonal(self.A_param) else "dense"
         else:
             raise NotImplementedError("the B200 engines are built for depths N=2 and N=3")
-        if leaf == "van_loan" and not (self.engine == "diag" and reweighting_mode != "displacement"):
+        if leaf == "block_series" and self.N > 2:
+            raise NotImplementedError("leaf='block_series': blockwise series local terms exist for depths 1 and 2")
+        if leaf == "van_loan" and self.engine == "block":
             raise NotImplementedError(
-                "leaf='van_loan' runs on the B200 engines for a diagonal A under a uniform clock "
-                "(reweighting_mode='displacement_uniform' or 'displacement_uniform_basepoint'); "
-                "use leaf='series' with series_q for the other engines and modes"
+                "leaf='van_loan' runs on the diagonal and dense engines (depth 2); use leaf='series' with "
+                "series_q for depth 3"
             )
+        # The Van Loan leaf with a per-interval clock (diagonal engine) and on the dense engine is the
+        # series leaf's evaluation with the Van Loan leaf's coefficients, truncated at degree 8
+        # (series.vanloan_poly_coeffs); under a uniform clock the diagonal engine takes its exact tables.
+        self._q = VANLOAN_DEGREE if leaf == "van_loan" else self.series_q
 
     @property
     def signature_dim(self) -> int:
@@ -188,7 +194,7 @@ class EWS(nn.Module):
         """Depth 3 on 2x2 blocks: every interval has its own clock step (ews/core/chen_scan.py:155-168); a
         uniform clock is that with equal steps (the cached flow of displacement_uniform agrees with the
         per-interval one up to the rounding of the clock steps)."""
-        if self.series_q > 8:
+        if self._q > 8:
             raise NotImplementedError("the block engine evaluates series local terms up to series_q=8")
         A = self.A_param().to(torch.float32) * a_scale
         K = self.d // 2
@@ -210,18 +216,22 @@ class EWS(nn.Module):
         if kernel_readout == _lib.EWS_READOUT_TERMINAL and needs_grad:
             # the block backward runs on the prefix stream (the terminal value is its last row)
             out = engine.BlockScan.apply(
-                path, clock, blocks, lift, _lib.EWS_READOUT_PREFIX, flags, self._chunk, increments, self.series_q
+                path, clock, blocks, lift, _lib.EWS_READOUT_PREFIX, flags, self._chunk, increments, self._q
             )
             return out[:, -1]
         return engine.BlockScan.apply(
-            path, clock, blocks, lift, kernel_readout, flags, self._chunk, increments, self.series_q
+            path, clock, blocks, lift, kernel_readout, flags, self._chunk, increments, self._q
         )
 
     def _flat_diag_clock(self, path, clock, kernel_readout, a_scale, lift, increments):
         """The "displacement" mode: every interval has its own clock step, flow and series tables
         (ews/core/chen_scan.py:155-168 with cached=False; ews/core/series_leaf.py:72-127 per interval)."""
-        if self.series_q > 8:
+        if self._q > 8:
             raise NotImplementedError("the per-interval diagonal engine evaluates series tables up to series_q=8")
+        coef = None
+        if self.leaf == "van_loan":
+            k1, k2 = series.vanloan_poly_coeffs(self.M, self.van_loan_expm, VANLOAN_DEGREE)
+            coef = list(k1) + list(k2.ravel())
         rates = -(self.A_param.diag_values().to(torch.float32) * a_scale)
         B = path.shape[0]
         rates = rates[None, :].expand(B, -1)
@@ -235,7 +245,7 @@ class EWS(nn.Module):
         else:
             path = path.to(torch.float32)
         return engine.DiagScanClock.apply(
-            path, clock.to(torch.float32), rates, lift, kernel_readout, flags, self._chunk, increments, self.series_q
+            path, clock.to(torch.float32), rates, lift, kernel_readout, flags, self._chunk, increments, self._q, coef
         )
 
     def _flat_dense(self, path, clock, readout, a_scale, lift, increments, basepoint):
@@ -244,7 +254,10 @@ class EWS(nn.Module):
         A = self.A_param().to(torch.float32) * a_scale
         clock = clock.to(torch.float32)
         h = clock[:, 1] - clock[:, 0]
-        M, F, G, H = series.dense_tables(A, h, self.series_q, lift)
+        coeffs = None
+        if self.leaf == "van_loan":
+            coeffs = series.vanloan_device_coeffs(self.M, self.van_loan_expm, VANLOAN_DEGREE, str(A.device))
+        M, F, G, H = series.dense_tables(A, h, self._q, lift, coeffs)
         flags = _lib.EWS_F_UNIFORM | _det_flags()
         if increments:
             flags |= _lib.EWS_F_INCREMENTS

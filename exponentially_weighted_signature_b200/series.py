@@ -14,6 +14,7 @@ Q1_i = sum_p c_p x_i^p / p!  and  Q2_ij = sum_{a+b<=q} c_ab x_i^a x_j^b / (a! b!
 from __future__ import annotations
 
 import math
+from fractions import Fraction
 from functools import lru_cache
 
 import numpy as np
@@ -124,7 +125,22 @@ def _leaf_coeffs(q: int, device: str):
     return (torch.tensor(C1, dtype=torch.float64, device=device), torch.tensor(C2, dtype=torch.float64, device=device))
 
 
-def dense_leaf_tables(X: torch.Tensor, q: int, lift=None):
+def vanloan_series_coeffs(M: int, method: str, q: int):
+    """The Van Loan leaf in the series leaf's normalisation: c1_p = k1_p p! and c_ab = k2_ab a! b! (the
+    coefficients of b_p = (X^p / p!) dy), so the series leaf's dense tables evaluate it unchanged."""
+    k1, k2 = vanloan_poly_coeffs(int(M), method, int(q))
+    fact = np.array([math.factorial(p) for p in range(q + 1)], dtype=np.float64)
+    return k1 * fact, k2 * np.outer(fact, fact)
+
+
+@lru_cache(maxsize=None)
+def vanloan_device_coeffs(M: int, method: str, q: int, device: str):
+    """``vanloan_series_coeffs`` as float64 tensors on ``device``, made once per key (no copy per call)."""
+    c1, c2 = vanloan_series_coeffs(M, method, q)
+    return (torch.tensor(c1, dtype=torch.float64, device=device), torch.tensor(c2, dtype=torch.float64, device=device))
+
+
+def dense_leaf_tables(X: torch.Tensor, q: int, lift=None, coeffs=None):
     """The series-leaf tables of the dense engine at X = -h A (B, N, N), float64: F = K1 W, G_a = P_a W,
     H_a = K2_a W with P_a = X^a / a!, K1 = sum_p c_p P_p, K2_a = sum_b c_ab P_b (the series leaf with
     shared letters, ews/core/series_leaf.py:72-113) and the lift W (identity when None). Differentiable."""
@@ -134,14 +150,17 @@ def dense_leaf_tables(X: torch.Tensor, q: int, lift=None):
     for a in range(1, q + 1):
         P.append(P[-1] @ X / a)
     P = torch.stack(P, dim=1)  # (B, q+1, N, N)
-    c1, c2 = _leaf_coeffs(int(q), str(X.device))
+    if coeffs is None:
+        c1, c2 = _leaf_coeffs(int(q), str(X.device))
+    else:
+        c1, c2 = coeffs
     K1 = torch.einsum("p,bpij->bij", c1, P)
     K2 = torch.einsum("ab,zbij->zaij", c2, P)
     W = torch.eye(N, dtype=X.dtype, device=X.device) if lift is None else lift.to(X.dtype)
     return K1 @ W, P @ W, K2 @ W
 
 
-def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None):
+def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None, coeffs=None):
     """Per-sample tables of the dense engine for generator A (N, N), clock steps h (B,) and lift W (N, d_in):
     the flow complement D = I - expm(-hA) and the series-leaf tables F, G, H (dense_leaf_tables).
     Differentiable; evaluated in float64 and returned in float32. The exponential
@@ -151,7 +170,7 @@ def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None):
     X = -h.to(torch.float64)[:, None, None] * A.to(torch.float64)  # (B, N, N)
     N = A.shape[-1]
     Dc = torch.eye(N, dtype=torch.float64, device=A.device) - Expm.apply(X)
-    F, G, H = dense_leaf_tables(X, q, lift)
+    F, G, H = dense_leaf_tables(X, q, lift, coeffs)
     return Dc.float(), F.float(), G.float(), H.float()
 
 
@@ -208,3 +227,86 @@ def vanloan_diag_tables(lam: torch.Tensor, h: torch.Tensor, M: int, method: str 
     R = 0.5 * P + tail
     q2 = torch.einsum("bim,bjm->bij", P, R)
     return q1, q2
+
+
+def _ps_mul(a, b, n):
+    out = [Fraction(0)] * (n + 1)
+    for i, ai in enumerate(a):
+        if ai == 0:
+            continue
+        for j in range(n + 1 - i):
+            out[i + j] += ai * b[j]
+    return out
+
+
+def _ps_inv(a, n):
+    """1 / a as a power series (a[0] != 0)."""
+    out = [Fraction(0)] * (n + 1)
+    out[0] = 1 / a[0]
+    for k in range(1, n + 1):
+        acc = Fraction(0)
+        for j in range(1, k + 1):
+            if j < len(a):
+                acc += a[j] * out[k - j]
+        out[k] = -acc / a[0]
+    return out
+
+
+def _ps_pow(a, e, n):
+    base = a if e >= 0 else _ps_inv(a, n)
+    out = [Fraction(1)] + [Fraction(0)] * n
+    for _ in range(abs(e)):
+        out = _ps_mul(out, base, n)
+    return out
+
+
+@lru_cache(maxsize=None)
+def vanloan_poly_coeffs(M: int, method: str, degree: int):
+    """Polynomial coefficients, in the log-flow x = -dtheta a, of the Van Loan leaf's diagonal tables:
+    Q1(x) = sum_a k1[a] x^a and Q2(x_i, x_j) = sum_{a,b} k2[a, b] x_i^a x_j^b, truncated at ``degree`` in
+    each variable (float64 arrays).
+
+    The leaf's m-th segment is p_m(x) dy with p_m(x) = g(z) c(z)^{m-1-M} / M, z = -x / M (c, g the
+    chosen exponential of the augmented step, ``_vanloan_step``), so Q1 = sum_m p_m and
+    Q2 = sum_{m<n} p_m(x_i) p_n(x_j) + 1/2 sum_m p_m(x_i) p_m(x_j). For a generator that is not diagonal
+    the same coefficients apply to the powers of X = -dtheta A (every factor is a function of one
+    matrix), i.e. they are the series leaf's coefficients c_p / p! and c_ab / (a! b!) with the Van Loan
+    leaf's values. The power series are exact rationals; the truncation error is of order
+    |x|^(degree+1) / (degree+1)! relative."""
+    n = degree
+    half = Fraction(1, 2)
+    if method == "exact":
+        ez = [Fraction(1, math.factorial(k)) for k in range(n + 2)]
+        c = ez[: n + 1]
+        g = [Fraction(1, math.factorial(k + 1)) for k in range(n + 1)]  # (e^z - 1) / z
+    elif method == "euler":
+        c = [Fraction(1), Fraction(1)] + [Fraction(0)] * (n - 1)
+        g = [Fraction(1)] + [Fraction(0)] * n
+    elif method == "cayley":
+        den = _ps_inv([Fraction(1), -half], n)
+        c = _ps_mul([Fraction(1), half], den, n)
+        g = den
+    elif method == "pade":
+        den = _ps_inv([Fraction(1), -half, Fraction(1, 12)], n)
+        c = _ps_mul([Fraction(1), half, Fraction(1, 12)], den, n)
+        g = den
+    else:
+        raise ValueError(f"unknown expm method {method!r}")
+    c = (c + [Fraction(0)] * (n + 1))[: n + 1]
+    g = (g + [Fraction(0)] * (n + 1))[: n + 1]
+    # series in z -> series in x (z = -x / M): coefficient k scales by (-1/M)^k
+    scale = [Fraction(-1, M) ** k for k in range(n + 1)]
+    segs = []
+    for m in range(1, M + 1):
+        pz = _ps_mul(g, _ps_pow(c, m - 1 - M, n), n)
+        segs.append([pz[k] * scale[k] / M for k in range(n + 1)])
+    k1 = [sum(s[a] for s in segs) for a in range(n + 1)]
+    # tails[m][b] = sum_{n > m} p_n[b]
+    tails = [[Fraction(0)] * (n + 1) for _ in range(M)]
+    run = [Fraction(0)] * (n + 1)
+    for m in range(M - 1, -1, -1):
+        tails[m] = list(run)
+        run = [run[b] + segs[m][b] for b in range(n + 1)]
+    k2 = [[sum(segs[m][a] * (tails[m][b] + half * segs[m][b]) for m in range(M)) for b in range(n + 1)]
+          for a in range(n + 1)]
+    return np.array([float(v) for v in k1]), np.array([[float(v) for v in row] for row in k2])

@@ -123,6 +123,13 @@ typedef struct ews_diag_args {
     size_t bwd_ws_bytes;
     /* backward, per-interval clock only */
     float* grad_dtheta;      /* (B, T): dL/d(dtheta_t) */
+    /* per-interval clock only, optional (NULL: the series leaf of order series_q): HOST pointer to 9 + 81
+       floats, the polynomial coefficients of the local tables in the log-flow x,
+       Q1(x) = sum_a k1[a] x^a and Q2(x_i, x_j) = sum_{a,b} k2[9 a + b] x_i^a x_j^b (k1 then k2). Another
+       leaf whose diagonal tables are such power series runs through the same kernels: the Van Loan leaf
+       (ews/core/van_loan.py:30-88 with ews/core/signature.py:19-36, the reference's default) truncated
+       at degree 8 in each variable. Read during the call; not kept. */
+    const float* leaf_coef;
 } ews_diag_args;
 
 int ews_diag_workspace_size(const ews_diag_args* a, size_t* fwd_bytes, size_t* bwd_bytes);

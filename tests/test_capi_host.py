@@ -154,12 +154,12 @@ def test_layer_validation_mirrors_reference():
     d = EWS(A, N=2, reweighting_mode="displacement_uniform")
     assert (d.leaf, d.series_q, d.combine, d.combine_chunk, d.M) == ("van_loan", None, "assoc", 1024, 20)
     assert EWS(A, N=2, reweighting_mode="displacement_uniform", combine="lean").engine == "diag"
-    # Van Loan runs on the diagonal engine under a uniform clock; elsewhere it raises instead of
-    # silently computing another leaf
+    # Van Loan runs on the diagonal engine (any mode) and the dense engine; at depth 3 it raises instead
+    # of silently computing another leaf
+    assert EWS(A, N=2).engine == "diag"  # the reference's full defaults
+    assert EWS(torch.eye(4), N=2, reweighting_mode="displacement_uniform").engine == "dense"
     with pytest.raises(NotImplementedError):
-        EWS(A, N=2)  # default mode "displacement": per-interval clock
-    with pytest.raises(NotImplementedError):
-        EWS(torch.eye(4), N=2, reweighting_mode="displacement_uniform")
+        EWS(AParamBlockDiag([torch.ones(2, 2)] * 2, [2, 2]), N=3)
     with pytest.raises(NotImplementedError):
         EWS(A, N=2, leaf="jordan_closed")
     layer = EWS(AParamEFM(torch.zeros(3)), N=2, reweighting_mode="displacement_uniform")

@@ -89,7 +89,7 @@ def test_timeout_in_other_engines(withheld, engine_kind):
     rng = np.random.default_rng(0)
     T = 256
     if engine_kind == "block":
-        N, d = 8, 4
+        N, d = 8, 8
         blocks = [torch.tensor([[0.3, 1.0], [-1.0, 0.3]], dtype=torch.float32) for _ in range(N // 2)]
         layer = EWS(AParamBlockDiag(blocks, (2,) * (N // 2)).to(DEV), N=3, reweighting_mode="displacement",
                     leaf="series", series_q=4, combine="b200", combine_chunk=8)
