@@ -35,6 +35,7 @@ struct Geom {
     unsigned flags;
     int spin_limit;
     int SR, ntiles;
+    int agg_pre;      // forward: the chunk aggregates come from agg_kernel (the chain runs the output pass only)
     int tab_n;        // floats of the F, G, H tables (N x d_in each, padded to NP rows)
     int smem_floats;  // forward
     int bsmem_floats; // backward
@@ -62,6 +63,7 @@ struct Params {
     float* lcarry;     // backward: per chunk the cotangent arriving at its end [- | L1 | L2] (SW)
     float* loc;        // local terms per (sample, interval): [s1 | U_0..U_{QP-1} | V_0..V_{QP-1}], NP each
     float* coef;       // backward: per (sample, interval) the vector cotangents [ds1 | dU_a | dV_a], NP each
+    float* pows;       // forward: per sample the power complements E_j = I - M^j, j = 0..Lc, row-major (Lc+1) MM
 };
 
 // Width (floats) of one interval's local terms in `loc`.
@@ -963,10 +965,12 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
             }
             __syncwarp();
             float* saved = s.stage + warp * tc_stage_stride(g.W);
+            // with precomputed aggregates (agg_kernel) the first pass only publishes them and looks back
+            const bool skip = pass == 0 && g.agg_pre;
             // the intervals' local terms (computed by local_kernel), copied in one interval ahead
-            if (len_me > 0) fetch_loc(p, b, t0_me, vt + 2 * NP, LW);
+            if (len_me > 0 && !skip) fetch_loc(p, b, t0_me, vt + 2 * NP, LW);
             cp_async_commit();
-            for (int k = 0; k < steps; ++k) {
+            for (int k = 0; k < (skip ? 0 : steps); ++k) {
                 const bool live = k < len_me;
                 cp_async_wait<0>();
                 __syncwarp();
@@ -1070,14 +1074,14 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                 }
             }
             if (failed) break;
-            if (len_me < steps) {
+            if (len_me < steps && !skip) {
 #pragma unroll
                 for (int n = 0; n < 32; ++n) col[n] = saved[n * 32 + lane];
             }
             __syncthreads();
             if (pass == 1) break;
             // ---- aggregates of the 4 chunks (flow complement, S1, S2) -> agg slots
-            if (valid_me) {
+            if (valid_me && !g.agg_pre) {
                 float* as = p.agg + ((size_t)b * g.C + c_me) * g.SW;
 #pragma unroll
                 for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = col[n];
@@ -1092,14 +1096,16 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
             float* W5 = s.Alo + MM;
             float* W6 = s.Alo + 2 * MM;   // C(Lc) row-major
             float* W7 = s.Alo + 3 * MM;   // C(last) row-major
-            for (int e = tid; e < 2 * MM; e += blockDim.x) W6[e] = p.pw[(size_t)b * 2 * MM + e];
-            __syncthreads();
-            for (int t = 0; t < TILES; ++t) {
-                const int c = grp * TILES + t;
-                if (c >= g.C) break;
-                const float* C = (c == g.C - 1) ? W7 : W6;
-                float* as = p.agg + ((size_t)b * g.C + c) * g.SW;
-                for (int e = tid; e < MM; e += blockDim.x) as[e] = C[e];
+            if (!g.agg_pre) {
+                for (int e = tid; e < 2 * MM; e += blockDim.x) W6[e] = p.pw[(size_t)b * 2 * MM + e];
+                __syncthreads();
+                for (int t = 0; t < TILES; ++t) {
+                    const int c = grp * TILES + t;
+                    if (c >= g.C) break;
+                    const float* C = (c == g.C - 1) ? W7 : W6;
+                    float* as = p.agg + ((size_t)b * g.C + c) * g.SW;
+                    for (int e = tid; e < MM; e += blockDim.x) as[e] = C[e];
+                }
             }
             __syncthreads();
             // publish the aggregates (the first chunk of the sequence publishes its inclusive value)
@@ -1193,6 +1199,206 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
     __syncthreads();
     fence_after();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64));
+}
+
+// ---------------------------------------------------------------------------------- chunk aggregates
+
+// Power complements E_j = I - M^j for j = 0..Lc of each sample (one CTA per sample, four 64-thread groups),
+// by doubling: with E_1..E_m known, E_{m+i} = E_m + E_i - E_m E_i for i = 1..m (all powers of M commute, so
+// the complement composition needs no order). E_0 = 0, E_1 = D.
+constexpr int PWT = 256;
+
+__global__ void __launch_bounds__(PWT) powers_kernel(Params p) {
+    __shared__ __align__(16) float Emt[MM];       // E_m, k-major
+    __shared__ __align__(16) float Ei[4][MM];     // per group: E_i, row-major
+    const Geom& g = p.g;
+    const int b = blockIdx.x, N = g.N, Lc = g.Lc;
+    const int grp = threadIdx.x >> 6, gt = threadIdx.x & 63;
+    const int i0 = 4 * (gt >> 3), j0 = 4 * (gt & 7);
+    float* E = p.pows + (size_t)b * (Lc + 1) * MM;
+    const float* d = p.tab_d + (size_t)b * N * N;
+    for (int e = threadIdx.x; e < MM; e += PWT) {
+        const int i = e / NP, k = e - i * NP;
+        E[e] = 0.f;
+        E[MM + e] = (i < N && k < N) ? d[i * N + k] : 0.f;
+    }
+    __syncthreads();
+    for (int m = 1; m < Lc; m *= 2) {
+        for (int e = threadIdx.x; e < MM; e += PWT) {
+            const int i = e / NP, k = e - i * NP;
+            Emt[k * NP + i] = E[(size_t)m * MM + e];
+        }
+        __syncthreads();
+        const int cnt = min(m, Lc - m);
+        for (int i = 1 + grp; i <= cnt; i += 4) {
+            for (int e = gt; e < MM; e += 64) Ei[grp][e] = E[(size_t)i * MM + e];
+            asm volatile("bar.sync %0, 64;" ::"r"(1 + grp));
+            float blk[4][4], em[4][4], ei[4][4];
+            gemm44(Emt, Ei[grp], blk, i0, j0, false);
+            load_rowmajor(Ei[grp], ei, i0, j0);
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) em[r][c] = Emt[(j0 + c) * NP + i0 + r];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) blk[r][c] = em[r][c] + ei[r][c] - blk[r][c];
+            store_rowmajor(E + (size_t)(m + i) * MM, blk, i0, j0);
+            asm volatile("bar.sync %0, 64;" ::"r"(1 + grp));
+        }
+        __syncthreads();
+    }
+}
+
+// Zero-carry aggregates of every chunk without running its chain. With the chunk's local terms
+// Z_t = u_t s1_t^T + sum_a U_{t,a} V_{t,a}^T (u_t = M S1_{t-1} from the chunk's own level-1 recursion) the
+// level-2 aggregate is A2 = sum_t M^{L-1-t} Z_t M^{(L-1-t)T} = sum_t sum_r (M^{L-1-t} x_{t,r}) (M^{L-1-t} y_{t,r})^T,
+// a rank-(q+2) update per interval instead of a 32 x 32 x 32 conjugation, and every interval is independent
+// once the powers are known (applied as complements, w = x - E x). One warp per chunk, lane = state row;
+// the interval's local terms and its power complement E are copied in with cp.async one interval ahead
+// (E rows padded to AGS floats so that the lanes' 16-byte reads of their rows fall in distinct banks).
+constexpr int AGW = 4;   // warps per CTA
+constexpr int AGS = 36;  // row stride of a staged power complement
+
+__host__ __device__ inline int agg_warp_floats(int QP) {
+    return 2 * loc_width(QP) + 2 * NP * AGS + 2 * NP + (QMAX + 1) * NP;
+}
+
+template <int QP>
+__global__ void __launch_bounds__(AGW * 32, 4) agg_kernel(Params p) {
+    extern __shared__ __align__(16) float agsm[];
+    const Geom& g = p.g;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int chunk = blockIdx.x * AGW + warp;
+    if (chunk >= g.B * g.C) return;
+    const int b = chunk / g.C, c = chunk - b * g.C;
+    const int N = g.N, LW = loc_width(QP), Lc = g.Lc;
+    const int t0 = c * Lc, len = min(Lc, g.T - t0);
+    float* locb = agsm + (size_t)warp * agg_warp_floats(QP);  // 2 x LW
+    float* Eb = locb + 2 * LW;                                 // 2 x NP x AGS
+    float* S1v = Eb + 2 * NP * AGS;                            // the chunk's level 1 (broadcast copy)
+    float* uv = S1v + NP;                                      // u = M S1_{t-1}
+    float* wy = uv + NP;                                       // (QP + 1) x NP: the flowed y vectors
+    float drow[NP];
+    {
+        const float* d = p.tab_d + (size_t)b * N * N;
+#pragma unroll
+        for (int k = 0; k < NP; ++k) drow[k] = (lane < N && k < N) ? d[lane * N + k] : 0.f;
+    }
+    float a2[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) a2[k] = 0.f;
+    float s1 = 0.f;
+    S1v[lane] = 0.f;
+    const float* Ebase = p.pows + (size_t)b * (Lc + 1) * MM;
+    auto fetch = [&](int k) {
+        float* eb = Eb + (k & 1) * NP * AGS;
+        const float* src = Ebase + (size_t)(len - 1 - k) * MM;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const int e = lane + 32 * v;  // 16-byte piece e: row e / 8, column 4 (e % 8)
+            cp_async16(eb + (e >> 3) * AGS + 4 * (e & 7), src + 4 * e);
+        }
+        tc::fetch_loc(p, b, t0 + k, locb + (k & 1) * LW, LW);
+        cp_async_commit();
+    };
+    fetch(0);
+    for (int k = 0; k < len; ++k) {
+        cp_async_wait<0>();
+        __syncwarp();
+        const float* loc = locb + (k & 1) * LW;  // [s1 | U_0..U_{QP-1} | V_0..V_{QP-1}]
+        const float* er = Eb + (k & 1) * NP * AGS + lane * AGS;
+        if (k + 1 < len) fetch(k + 1);
+        // u = S1 - D S1 (the level-1 state before this interval, flowed one step)
+        float du0 = 0.f, du1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < NP; q += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(S1v + q);
+            du0 = fmaf(drow[q], v.x, du0);
+            du1 = fmaf(drow[q + 1], v.y, du1);
+            du0 = fmaf(drow[q + 2], v.z, du0);
+            du1 = fmaf(drow[q + 3], v.w, du1);
+        }
+        const float u = s1 - (du0 + du1);
+        uv[lane] = u;
+        __syncwarp();
+        // (E x_r)[lane], (E y_r)[lane] for every term at once: x = u, U_a; y = s1, V_a
+        float ex[QP + 1], ey[QP + 1];
+#pragma unroll
+        for (int r = 0; r <= QP; ++r) ex[r] = ey[r] = 0.f;
+#pragma unroll
+        for (int q = 0; q < NP; q += 4) {
+            const float4 e4 = *reinterpret_cast<const float4*>(er + q);
+#pragma unroll
+            for (int r = 0; r <= QP; ++r) {
+                const float* x = r == 0 ? uv : loc + NP * r;
+                const float* y = r == 0 ? loc : loc + NP * (QP + r);
+                const float4 xv = *reinterpret_cast<const float4*>(x + q);
+                const float4 yv = *reinterpret_cast<const float4*>(y + q);
+                ex[r] = fmaf(e4.x, xv.x, fmaf(e4.y, xv.y, fmaf(e4.z, xv.z, fmaf(e4.w, xv.w, ex[r]))));
+                ey[r] = fmaf(e4.x, yv.x, fmaf(e4.y, yv.y, fmaf(e4.z, yv.z, fmaf(e4.w, yv.w, ey[r]))));
+            }
+        }
+        float wx[QP + 1];
+#pragma unroll
+        for (int r = 0; r <= QP; ++r) {
+            const float* x = r == 0 ? uv : loc + NP * r;
+            const float* y = r == 0 ? loc : loc + NP * (QP + r);
+            wx[r] = x[lane] - ex[r];
+            wy[r * NP + lane] = y[lane] - ey[r];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r <= QP; ++r) {
+#pragma unroll
+            for (int q = 0; q < NP; q += 4) {
+                const float4 yv = *reinterpret_cast<const float4*>(wy + r * NP + q);
+                a2[q] = fmaf(wx[r], yv.x, a2[q]);
+                a2[q + 1] = fmaf(wx[r], yv.y, a2[q + 1]);
+                a2[q + 2] = fmaf(wx[r], yv.z, a2[q + 2]);
+                a2[q + 3] = fmaf(wx[r], yv.w, a2[q + 3]);
+            }
+        }
+        // S1 <- u + s1 of this interval (every lane has read S1v and uv before the barrier above)
+        s1 = u + loc[lane];
+        S1v[lane] = s1;
+    }
+    cp_async_wait<0>();
+    // the slot: [flow complement C(len) | S1 | S2 row-major]
+    float* as = p.agg + ((size_t)b * g.C + c) * g.SW;
+    const float* C = p.pw + ((size_t)b * 2 + (c == g.C - 1 ? 1 : 0)) * MM;
+    for (int e = lane; e < MM; e += 32) as[e] = C[e];
+    as[MM + lane] = s1;
+    float4* row = reinterpret_cast<float4*>(as + MM + NP + lane * NP);
+#pragma unroll
+    for (int q = 0; q < NP / 4; ++q) row[q] = make_float4(a2[4 * q], a2[4 * q + 1], a2[4 * q + 2], a2[4 * q + 3]);
+}
+
+template <int QP>
+static int launch_agg(const Params& p, cudaStream_t s) {
+    const size_t smem = sizeof(float) * (size_t)AGW * agg_warp_floats(QP);
+    cudaFuncSetAttribute(agg_kernel<QP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    agg_kernel<QP><<<(p.g.B * p.g.C + AGW - 1) / AGW, AGW * 32, smem, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+static int launch_agg_q(const Params& p, cudaStream_t s) {
+    switch (p.g.QP) {
+        case 1: return launch_agg<1>(p, s);
+        case 2: return launch_agg<2>(p, s);
+        case 3: return launch_agg<3>(p, s);
+        case 4: return launch_agg<4>(p, s);
+        case 5: return launch_agg<5>(p, s);
+        case 6: return launch_agg<6>(p, s);
+        case 7: return launch_agg<7>(p, s);
+        case 8: return launch_agg<8>(p, s);
+        case 9: return launch_agg<9>(p, s);
+        case 10: return launch_agg<10>(p, s);
+        case 11: return launch_agg<11>(p, s);
+        case 12: return launch_agg<12>(p, s);
+    }
+    return EWS_ERR_UNSUPPORTED;
 }
 
 // ---------------------------------------------------------------------------------- backward
@@ -2255,7 +2461,7 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 struct WsLayout {
-    size_t status, flags, agg, incl, carry, partials, pw, loc, total;
+    size_t status, flags, agg, incl, carry, partials, pw, loc, pows, total;
 };
 
 static WsLayout fwd_layout(const Geom& g) {
@@ -2276,6 +2482,8 @@ static WsLayout fwd_layout(const Geom& g) {
     o += al256(sizeof(float) * (size_t)g.B * 2 * MM);
     L.loc = o;  // the intervals' local terms, written by local_kernel and read by both chains and grad_map_kernel
     o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
+    L.pows = o;  // power complements for agg_kernel
+    o += al256(sizeof(float) * (size_t)g.B * (g.Lc + 1) * MM);
     L.total = o;
     return L;
 }
@@ -2379,6 +2587,14 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
         local_kernel<<<g.B * spans, LNT, lsmem, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     }
+    p.pows = (float*)(ws + L.pows);
+    p.g.agg_pre = 1;
+    powers_kernel<<<g.B, PWT, 0, s>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    {
+        const int arc = launch_agg_q(p, s);
+        if (arc != EWS_OK) return arc;
+    }
     const size_t smem = tc::tc_smem_bytes(g.W, g.QP);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -2389,7 +2605,7 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     const int groups = (g.C + tc::TILES - 1) / tc::TILES;
     int grid = per_sm * num_sms();
     if (grid > g.B * groups) grid = g.B * groups;
-    fwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
+    fwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);  // p.g.agg_pre: the output pass and the look-back only
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 
