@@ -64,6 +64,7 @@ struct Params {
     float* loc;        // local terms per (sample, interval): [s1 | U_0..U_{QP-1} | V_0..V_{QP-1}], NP each
     float* coef;       // backward: per (sample, interval) the vector cotangents [ds1 | dU_a | dV_a], NP each
     float* pows;       // forward: per sample the power complements E_j = I - M^j, j = 0..Lc, row-major (Lc+1) MM
+    float* gex;        // forward: per (sample, scan group) the exclusive product of the earlier groups (SW)
 };
 
 // Width (floats) of one interval's local terms in `loc`.
@@ -952,6 +953,8 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
 
         float col[32];
         for (int pass = 0; pass < 2 && !failed; ++pass) {
+            // with precomputed aggregates and carries (agg_kernel, scan_*_kernel) only the output pass runs
+            if (pass == 0 && g.agg_pre) continue;
             // ---- initial state: identity (pass 1) or the chunk's carry (pass 2)
             if (pass == 0) {
 #pragma unroll
@@ -1399,6 +1402,91 @@ static int launch_agg_q(const Params& p, cudaStream_t s) {
         case 12: return launch_agg<12>(p, s);
     }
     return EWS_ERR_UNSUPPORTED;
+}
+
+// Carries of every chunk from the precomputed aggregates, by a two-level scan over each sample's chunks
+// instead of the chain kernel's look-back (whose first wave would walk back through every earlier aggregate):
+//   scan_local_kernel:  per group of CG chunks, the inclusive products within the group (into `incl`);
+//   scan_groups_kernel: per sample, the exclusive products of the group totals (into `gex`);
+//   scan_fix_kernel:    per chunk, carry = gex(group) (x) incl(previous chunk of the group), and for the
+//                       terminal readout the sample's total as its output row.
+// Chen products are chen_mul_smem (the look-back's), in a fixed order, so the carries are deterministic.
+constexpr int CG = 8;
+constexpr int CST = 64;
+
+struct ScanSmem {
+    float P0[MM], S10[NP], S20[MM];  // accumulator
+    float P1[MM], S11[NP], S21[MM];  // operand
+    float T0[MM], T1[MM], vtmp[NP];
+};
+
+__host__ __device__ inline int scan_groups(int C) { return (C + CG - 1) / CG; }
+
+__global__ void __launch_bounds__(CST) scan_local_kernel(Params p) {
+    __shared__ __align__(16) ScanSmem sm;
+    const Geom& g = p.g;
+    const int ng = scan_groups(g.C);
+    const int b = blockIdx.x / ng, k = blockIdx.x - b * ng;
+    const int c0 = k * CG, c1 = min(g.C, c0 + CG);
+    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
+    const size_t base = (size_t)b * g.C;
+    load_slot_smem(p.agg + (base + c0) * g.SW, sm.P0, sm.S10, sm.S20);
+    __syncthreads();
+    store_slot(p.incl + (base + c0) * g.SW, sm.P0, sm.S10, sm.S20);
+    for (int c = c0 + 1; c < c1; ++c) {
+        load_slot_smem(p.agg + (base + c) * g.SW, sm.P1, sm.S11, sm.S21);
+        __syncthreads();
+        chen_mul_smem(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp, i0, j0);
+        store_slot(p.incl + (base + c) * g.SW, sm.P0, sm.S10, sm.S20);
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(CST) scan_groups_kernel(Params p) {
+    __shared__ __align__(16) ScanSmem sm;
+    const Geom& g = p.g;
+    const int ng = scan_groups(g.C);
+    const int b = blockIdx.x;
+    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
+    identity_smem(sm.P0, sm.S10, sm.S20);
+    __syncthreads();
+    for (int k = 0; k < ng; ++k) {
+        store_slot(p.gex + ((size_t)b * ng + k) * g.SW, sm.P0, sm.S10, sm.S20);
+        if (k + 1 == ng) break;
+        const int last = min(g.C, (k + 1) * CG) - 1;
+        load_slot_smem(p.incl + ((size_t)b * g.C + last) * g.SW, sm.P1, sm.S11, sm.S21);
+        __syncthreads();
+        chen_mul_smem(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp, i0, j0);
+    }
+}
+
+__global__ void __launch_bounds__(CST) scan_fix_kernel(Params p) {
+    __shared__ __align__(16) ScanSmem sm;
+    const Geom& g = p.g;
+    const int ng = scan_groups(g.C);
+    const int b = blockIdx.x / g.C, c = blockIdx.x - b * g.C;
+    const int k = c / CG;
+    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
+    const size_t base = (size_t)b * g.C;
+    load_slot_smem(p.gex + ((size_t)b * ng + k) * g.SW, sm.P0, sm.S10, sm.S20);
+    __syncthreads();
+    if (c > k * CG) {
+        load_slot_smem(p.incl + (base + c - 1) * g.SW, sm.P1, sm.S11, sm.S21);
+        __syncthreads();
+        chen_mul_smem(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp, i0, j0);
+    }
+    store_slot(p.carry + (base + c) * g.SW, sm.P0, sm.S10, sm.S20);
+    if (c == g.C - 1 && g.readout == EWS_READOUT_TERMINAL) {
+        // the sample's terminal value: carry (x) the last chunk's aggregate
+        load_slot_smem(p.agg + (base + c) * g.SW, sm.P1, sm.S11, sm.S21);
+        __syncthreads();
+        chen_mul_smem(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp, i0, j0);
+        const int N = g.N;
+        float* row = p.out + (size_t)b * g.W;
+        if (threadIdx.x == 0) row[0] = 1.f;
+        for (int e = threadIdx.x; e < N; e += blockDim.x) row[1 + e] = sm.S10[e];
+        for (int e = threadIdx.x; e < N * N; e += blockDim.x) row[1 + N + e] = sm.S20[(e / N) * NP + (e % N)];
+    }
 }
 
 // ---------------------------------------------------------------------------------- backward
@@ -2045,7 +2133,8 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
                     if (tid < NP) is[MM + tid] = ve[tid];
                 }
                 __syncthreads();
-                cta_publish(p.flags + (size_t)b * g.C + c, kFlagIncl);
+                // failure-detection test: no inclusive value reaches the earlier chunks, whose waits then run out
+                if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(p.flags + (size_t)b * g.C + c, kFlagIncl);
                 __syncthreads();
             }
             __syncthreads();
@@ -2461,7 +2550,7 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 struct WsLayout {
-    size_t status, flags, agg, incl, carry, partials, pw, loc, pows, total;
+    size_t status, flags, agg, incl, carry, partials, pw, loc, pows, gex, total;
 };
 
 static WsLayout fwd_layout(const Geom& g) {
@@ -2484,6 +2573,8 @@ static WsLayout fwd_layout(const Geom& g) {
     o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
     L.pows = o;  // power complements for agg_kernel
     o += al256(sizeof(float) * (size_t)g.B * (g.Lc + 1) * MM);
+    L.gex = o;   // group prefixes of the carry scan
+    o += al256(sizeof(float) * (size_t)g.B * scan_groups(g.C) * g.SW);
     L.total = o;
     return L;
 }
@@ -2595,6 +2686,14 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
         const int arc = launch_agg_q(p, s);
         if (arc != EWS_OK) return arc;
     }
+    p.gex = (float*)(ws + L.gex);
+    scan_local_kernel<<<g.B * scan_groups(g.C), CST, 0, s>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    scan_groups_kernel<<<g.B, CST, 0, s>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    scan_fix_kernel<<<g.B * g.C, CST, 0, s>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    if (g.readout == EWS_READOUT_TERMINAL) return EWS_OK;  // the scan wrote the terminal rows
     const size_t smem = tc::tc_smem_bytes(g.W, g.QP);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
