@@ -36,6 +36,7 @@ struct Geom {
     int spin_limit;
     int SR, ntiles;
     int agg_pre;      // forward: the chunk aggregates come from agg_kernel (the chain runs the output pass only)
+    int bwd_mode;     // backward chain: 1 = the zero-carry pass only (local adjoints), 2 = the exact pass only
     int tab_n;        // floats of the F, G, H tables (N x d_in each, padded to NP rows)
     int smem_floats;  // forward
     int bsmem_floats; // backward
@@ -64,7 +65,9 @@ struct Params {
     float* loc;        // local terms per (sample, interval): [s1 | U_0..U_{QP-1} | V_0..V_{QP-1}], NP each
     float* coef;       // backward: per (sample, interval) the vector cotangents [ds1 | dU_a | dV_a], NP each
     float* pows;       // forward: per sample the power complements E_j = I - M^j, j = 0..Lc, row-major (Lc+1) MM
-    float* gex;        // forward: per (sample, scan group) the exclusive product of the earlier groups (SW)
+    float* gex;        // forward: per (sample, scan group) the exclusive product of the earlier groups (SW);
+                       // backward: per (sample, scan group) the cotangent arriving at the group's end
+    float* gsuf;       // backward: per chunk the forward aggregate of the chunks from it to its group's end
 };
 
 // Width (floats) of one interval's local terms in `loc`.
@@ -1527,6 +1530,113 @@ __device__ void apply_JT_smem(const float* Pr, const float* U1v, float* L1, floa
     __syncthreads();
 }
 
+// The backward's carries by a two-level reverse scan, the counterpart of the forward's (scan_*_kernel).
+// The element of a range of chunks is (G, mu): the forward aggregate G of the range and the cotangent mu at
+// the range's start from the range's own output gradients (zero carry). An earlier range a and a later b
+// combine to (G_a (x) G_b, J(G_a)^T mu_b + mu_a), with J(G)^T the transposed Chen map (apply_JT_smem).
+//   bscan_local_kernel:  per group, the suffix elements from every chunk to the group's end (gsuf, incl);
+//   bscan_groups_kernel: per sample, the cotangent arriving at each group's end (gex);
+//   bscan_fix_kernel:    per chunk, the cotangent arriving at its end (lcarry), J(suffix after it)^T lam + mu.
+struct BScanSmem {
+    float P0[MM], S10[NP], S20[MM];  // accumulated G
+    float P1[MM], S11[NP], S21[MM];  // G of a chunk
+    float L2r[MM], L1[NP];           // accumulated cotangent
+    float T0[MM], T1[MM], v1[NP], v2[NP], v3[NP];
+};
+
+__device__ void bscan_add_mu(BScanSmem& sm, const float* slot) {
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) sm.L2r[e] += ldcg(slot + MM + NP + e);
+    if (threadIdx.x < NP) sm.L1[threadIdx.x] += ldcg(slot + MM + threadIdx.x);
+}
+
+__device__ void bscan_store_lam(float* slot, const BScanSmem& sm) {
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) slot[MM + NP + e] = sm.L2r[e];
+    if (threadIdx.x < NP) slot[MM + threadIdx.x] = sm.L1[threadIdx.x];
+}
+
+// L <- J(G)^T L for G in (P1, S11) (its flow complement row-major and level 1)
+__device__ void bscan_apply(BScanSmem& sm, int i0, int j0) {
+    float X2[4][4];
+    load_rowmajor(sm.L2r, X2, i0, j0);
+    __syncthreads();
+    apply_JT_smem(sm.P1, sm.S11, sm.L1, X2, sm.L2r, sm.T0, sm.v1, sm.v2, i0, j0);
+}
+
+__global__ void __launch_bounds__(CST) bscan_local_kernel(Params p) {
+    __shared__ __align__(16) BScanSmem sm;
+    const Geom& g = p.g;
+    const int ng = scan_groups(g.C);
+    const int b = blockIdx.x / ng, k = blockIdx.x - b * ng;
+    const int c0 = k * CG, c1 = min(g.C, c0 + CG) - 1;
+    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
+    const size_t base = (size_t)b * g.C;
+    load_slot_smem(p.fagg + (base + c1) * g.SW, sm.P0, sm.S10, sm.S20);
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) sm.L2r[e] = 0.f;
+    if (threadIdx.x < NP) sm.L1[threadIdx.x] = 0.f;
+    __syncthreads();
+    bscan_add_mu(sm, p.agg + (base + c1) * g.SW);
+    __syncthreads();
+    store_slot(p.gsuf + (base + c1) * g.SW, sm.P0, sm.S10, sm.S20);
+    bscan_store_lam(p.incl + (base + c1) * g.SW, sm);
+    for (int c = c1 - 1; c >= c0; --c) {
+        load_slot_smem(p.fagg + (base + c) * g.SW, sm.P1, sm.S11, sm.S21);
+        __syncthreads();
+        bscan_apply(sm, i0, j0);                 // mu <- J(G_c)^T mu
+        bscan_add_mu(sm, p.agg + (base + c) * g.SW);  //      + mu_c
+        __syncthreads();
+        chen_mul_smem(sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.v3, i0, j0);
+        store_slot(p.gsuf + (base + c) * g.SW, sm.P0, sm.S10, sm.S20);
+        bscan_store_lam(p.incl + (base + c) * g.SW, sm);
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(CST) bscan_groups_kernel(Params p) {
+    __shared__ __align__(16) BScanSmem sm;
+    const Geom& g = p.g;
+    const int ng = scan_groups(g.C);
+    const int b = blockIdx.x;
+    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
+    for (int e = threadIdx.x; e < MM; e += blockDim.x) sm.L2r[e] = 0.f;
+    if (threadIdx.x < NP) sm.L1[threadIdx.x] = 0.f;
+    __syncthreads();
+    for (int k = ng - 1; k >= 0; --k) {
+        bscan_store_lam(p.gex + ((size_t)b * ng + k) * g.SW, sm);
+        if (k == 0) break;
+        const size_t first = (size_t)b * g.C + (size_t)k * CG;
+        __syncthreads();
+        load_slot_smem(p.gsuf + first * g.SW, sm.P1, sm.S11, sm.S21);
+        __syncthreads();
+        bscan_apply(sm, i0, j0);
+        bscan_add_mu(sm, p.incl + first * g.SW);
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(CST) bscan_fix_kernel(Params p) {
+    __shared__ __align__(16) BScanSmem sm;
+    const Geom& g = p.g;
+    const int ng = scan_groups(g.C);
+    const int b = blockIdx.x / g.C, c = blockIdx.x - b * g.C;
+    const int k = c / CG, last = min(g.C, (k + 1) * CG) - 1;
+    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
+    const size_t base = (size_t)b * g.C;
+    {
+        const float* src = p.gex + ((size_t)b * ng + k) * g.SW;
+        for (int e = threadIdx.x; e < MM; e += blockDim.x) sm.L2r[e] = ldcg(src + MM + NP + e);
+        if (threadIdx.x < NP) sm.L1[threadIdx.x] = ldcg(src + MM + threadIdx.x);
+    }
+    __syncthreads();
+    if (c < last) {
+        load_slot_smem(p.gsuf + (base + c + 1) * g.SW, sm.P1, sm.S11, sm.S21);
+        __syncthreads();
+        bscan_apply(sm, i0, j0);
+        bscan_add_mu(sm, p.incl + (base + c + 1) * g.SW);
+        __syncthreads();
+    }
+    bscan_store_lam(p.lcarry + (base + c) * g.SW, sm);
+}
+
 // Adds a gradient row (real dims) to the cotangent (L1 vector, L2 block regs).
 __device__ void add_grad_row(const Geom& g, const float* row, float* L1, float L2[4][4], int i0, int j0) {
     const int N = g.N;
@@ -1894,6 +2004,7 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
 
         float col[32];  // column `lane` of l2
         for (int pass = 0; pass < 2 && !failed; ++pass) {
+            if (pass == 0 && g.bwd_mode == 2) continue;  // the carries come from the backward scan
             if (pass == 0) {
 #pragma unroll
                 for (int n = 0; n < 32; ++n) col[n] = 0.f;
@@ -2032,12 +2143,13 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
             if (pass == 1) break;
             // ---- local adjoints mu of the 4 chunks -> adjoint slots (the sequence's last chunk: inclusive)
             if (valid_me) {
-                float* as = (c_me == g.C - 1 ? p.incl : p.agg) + ((size_t)b * g.C + c_me) * g.SW;
+                float* as = (c_me == g.C - 1 && g.bwd_mode == 0 ? p.incl : p.agg) + ((size_t)b * g.C + c_me) * g.SW;
 #pragma unroll
                 for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = col[n];
                 as[MM + lane] = vt[lane];
             }
             __syncthreads();
+            if (g.bwd_mode == 1) break;  // the backward scan combines the local adjoints
             for (int t = 0; t < TILES; ++t) {
                 const int c = grp * TILES + t;
                 if (c >= g.C) break;
@@ -2599,6 +2711,10 @@ static WsLayout bwd_layout(const Geom& g) {
     o += al256(sizeof(float) * (size_t)g.B * g.T * g.W);
     L.loc = o;    // the vector cotangents [ds1 | dU_a | dV_a] per interval
     o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
+    L.pows = o;   // the reverse scan's suffix aggregates (gsuf)
+    o += slots;
+    L.gex = o;    // the reverse scan's per-group cotangents
+    o += al256(sizeof(float) * (size_t)g.B * scan_groups(g.C) * g.SW);
     L.total = o;
     return L;
 }
@@ -2753,8 +2869,24 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         const int groups = (g.C + tc::TILES - 1) / tc::TILES;
         int grid = per_sm * num_sms();
         if (grid > g.B * groups) grid = g.B * groups;
+        // zero-carry pass (local adjoints) -> reverse scan over the chunks -> exact pass from the carries
+        p.g.bwd_mode = 1;
         bwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        p.gsuf = (float*)(ws + L.pows);
+        p.gex = (float*)(ws + L.gex);
+        const int ng = scan_groups(g.C);
+        bscan_local_kernel<<<g.B * ng, CST, 0, s>>>(p);
+        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        bscan_groups_kernel<<<g.B, CST, 0, s>>>(p);
+        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        bscan_fix_kernel<<<g.B * g.C, CST, 0, s>>>(p);
+        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        if (cudaMemsetAsync(ws + L.status, 0, sizeof(int), s) != cudaSuccess) return EWS_ERR_LAUNCH;  // the ticket
+        p.g.bwd_mode = 2;
+        bwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
+        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        p.g.bwd_mode = 0;
     }
     p.coef = (float*)(ws + L.loc);
     {
