@@ -1407,15 +1407,141 @@ static int launch_agg_q(const Params& p, cudaStream_t s) {
     return EWS_ERR_UNSUPPORTED;
 }
 
+// ---------------------------------------------------------------------------------- 256-thread products
+// The scans' Chen products and transposed Chen maps with 256 threads (a 2 x 2 block each) instead of the
+// look-back's 64: the scans are sequential chains of these products, so their latency is the scans' cost.
+constexpr int CST = 256;
+
+// acc = A B on the thread's 2 x 2 block; At is A stored k-major, Bm row-major.
+__device__ __forceinline__ void gemm22(const float* __restrict__ At, const float* __restrict__ Bm, float acc[2][2],
+                                       int i0, int j0) {
+    acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < NP; ++k) {
+        const float2 a = *reinterpret_cast<const float2*>(At + k * NP + i0);
+        const float2 b = *reinterpret_cast<const float2*>(Bm + k * NP + j0);
+        acc[0][0] = fmaf(a.x, b.x, acc[0][0]);
+        acc[0][1] = fmaf(a.x, b.y, acc[0][1]);
+        acc[1][0] = fmaf(a.y, b.x, acc[1][0]);
+        acc[1][1] = fmaf(a.y, b.y, acc[1][1]);
+    }
+}
+
+__device__ __forceinline__ void ld22(const float* M, float v[2][2], int i0, int j0) {
+    const float2 r0 = *reinterpret_cast<const float2*>(M + i0 * NP + j0);
+    const float2 r1 = *reinterpret_cast<const float2*>(M + (i0 + 1) * NP + j0);
+    v[0][0] = r0.x;
+    v[0][1] = r0.y;
+    v[1][0] = r1.x;
+    v[1][1] = r1.y;
+}
+
+__device__ __forceinline__ void st22(float* M, const float v[2][2], int i0, int j0) {
+    *reinterpret_cast<float2*>(M + i0 * NP + j0) = make_float2(v[0][0], v[0][1]);
+    *reinterpret_cast<float2*>(M + (i0 + 1) * NP + j0) = make_float2(v[1][0], v[1][1]);
+}
+
+// (Po, S1o, S2o) = (PL, L1, L2) (x) (PR, R1, R2), flows as complements (the same product as chen_mul_smem).
+// Outputs may alias the left operand. Scratch T0, T1 (MM), vtmp (NP). Barrier-complete on return.
+__device__ void chen_mul_256(const float* PL, const float* L1, const float* L2, const float* PR, const float* R1,
+                             const float* R2, float* Po, float* S1o, float* S2o, float* T0, float* T1, float* vtmp) {
+    const int i0 = 2 * (threadIdx.x >> 4), j0 = 2 * (threadIdx.x & 15);
+    for (int e = threadIdx.x; e < MM; e += CST) {
+        const int i = e / NP, k = e - i * NP;
+        T0[k * NP + i] = L2[e];
+        T1[k * NP + i] = PR[e];
+    }
+    if (threadIdx.x < NP) {
+        float a0 = 0.f, a1 = 0.f;
+        for (int k = 0; k < NP; k += 2) {
+            a0 = fmaf(PR[threadIdx.x * NP + k], L1[k], a0);
+            a1 = fmaf(PR[threadIdx.x * NP + k + 1], L1[k + 1], a1);
+        }
+        vtmp[threadIdx.x] = L1[threadIdx.x] - (a0 + a1);  // P_R L1
+    }
+    __syncthreads();
+    float L2b[2][2], CLb[2][2], CRb[2][2], X[2][2], Pq[2][2], Y[2][2];
+    ld22(L2, L2b, i0, j0);
+    ld22(PL, CLb, i0, j0);
+    ld22(PR, CRb, i0, j0);
+    gemm22(T0, T1, X, i0, j0);  // L2 C_R^T
+    gemm22(T1, PL, Pq, i0, j0);  // C_R C_L
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            X[r][c] = L2b[r][c] - X[r][c];
+            Pq[r][c] = CLb[r][c] + CRb[r][c] - Pq[r][c];
+        }
+    __syncthreads();
+    st22(T0, X, i0, j0);
+    __syncthreads();
+    gemm22(T1, T0, Y, i0, j0);  // C_R X
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+            Y[r][c] = (X[r][c] - Y[r][c]) + fmaf(vtmp[i0 + r], R1[j0 + c], R2[(i0 + r) * NP + j0 + c]);
+    __syncthreads();
+    st22(S2o, Y, i0, j0);
+    st22(Po, Pq, i0, j0);
+    if (threadIdx.x < NP) S1o[threadIdx.x] = vtmp[threadIdx.x] + R1[threadIdx.x];
+    __syncthreads();
+}
+
+// (L1, L2r) <- J(G)^T (L1, L2r) for G = (C row-major in Pr, level 1 U1v): L2 <- P^T L2 P,
+// L1 <- P^T (L1 + L2 U1), P = I - C. Scratch T0 (MM), T1, vt (NP). Barrier-complete on return.
+__device__ void apply_JT_256(const float* Pr, const float* U1v, float* L1, float* L2r, float* T0, float* T1, float* vt) {
+    const int i0 = 2 * (threadIdx.x >> 4), j0 = 2 * (threadIdx.x & 15);
+    if (threadIdx.x < NP) {
+        float a0 = 0.f, a1 = 0.f;
+        for (int k = 0; k < NP; k += 2) {
+            a0 = fmaf(L2r[threadIdx.x * NP + k], U1v[k], a0);
+            a1 = fmaf(L2r[threadIdx.x * NP + k + 1], U1v[k + 1], a1);
+        }
+        vt[threadIdx.x] = L1[threadIdx.x] + (a0 + a1);
+    }
+    float Z[2][2], L2b[2][2];
+    gemm22(Pr, L2r, Z, i0, j0);  // C^T L2 (Pr read k-major is C^T)
+    ld22(L2r, L2b, i0, j0);
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) Z[r][c] = L2b[r][c] - Z[r][c];  // P^T L2
+    __syncthreads();
+    // Z k-major
+    T0[j0 * NP + i0] = Z[0][0];
+    T0[(j0 + 1) * NP + i0] = Z[0][1];
+    T0[j0 * NP + i0 + 1] = Z[1][0];
+    T0[(j0 + 1) * NP + i0 + 1] = Z[1][1];
+    if (threadIdx.x < NP) {
+        float a0 = 0.f, a1 = 0.f;
+        for (int k = 0; k < NP; k += 2) {
+            a0 = fmaf(Pr[k * NP + threadIdx.x], vt[k], a0);
+            a1 = fmaf(Pr[(k + 1) * NP + threadIdx.x], vt[k + 1], a1);
+        }
+        T1[threadIdx.x] = vt[threadIdx.x] - (a0 + a1);  // P^T (L1 + L2 U1)
+    }
+    __syncthreads();
+    float W[2][2];
+    gemm22(T0, Pr, W, i0, j0);  // Z C
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) W[r][c] = Z[r][c] - W[r][c];  // Z P
+    st22(L2r, W, i0, j0);
+    if (threadIdx.x < NP) L1[threadIdx.x] = T1[threadIdx.x];
+    __syncthreads();
+}
+
 // Carries of every chunk from the precomputed aggregates, by a two-level scan over each sample's chunks
 // instead of the chain kernel's look-back (whose first wave would walk back through every earlier aggregate):
 //   scan_local_kernel:  per group of CG chunks, the inclusive products within the group (into `incl`);
 //   scan_groups_kernel: per sample, the exclusive products of the group totals (into `gex`);
 //   scan_fix_kernel:    per chunk, carry = gex(group) (x) incl(previous chunk of the group), and for the
 //                       terminal readout the sample's total as its output row.
-// Chen products are chen_mul_smem (the look-back's), in a fixed order, so the carries are deterministic.
+// Chen products are chen_mul_256, in a fixed order, so the carries are deterministic.
 constexpr int CG = 8;
-constexpr int CST = 64;
 
 struct ScanSmem {
     float P0[MM], S10[NP], S20[MM];  // accumulator
@@ -1431,7 +1557,6 @@ __global__ void __launch_bounds__(CST) scan_local_kernel(Params p) {
     const int ng = scan_groups(g.C);
     const int b = blockIdx.x / ng, k = blockIdx.x - b * ng;
     const int c0 = k * CG, c1 = min(g.C, c0 + CG);
-    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
     const size_t base = (size_t)b * g.C;
     load_slot_smem(p.agg + (base + c0) * g.SW, sm.P0, sm.S10, sm.S20);
     __syncthreads();
@@ -1439,7 +1564,7 @@ __global__ void __launch_bounds__(CST) scan_local_kernel(Params p) {
     for (int c = c0 + 1; c < c1; ++c) {
         load_slot_smem(p.agg + (base + c) * g.SW, sm.P1, sm.S11, sm.S21);
         __syncthreads();
-        chen_mul_smem(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp, i0, j0);
+        chen_mul_256(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp);
         store_slot(p.incl + (base + c) * g.SW, sm.P0, sm.S10, sm.S20);
         __syncthreads();
     }
@@ -1450,7 +1575,6 @@ __global__ void __launch_bounds__(CST) scan_groups_kernel(Params p) {
     const Geom& g = p.g;
     const int ng = scan_groups(g.C);
     const int b = blockIdx.x;
-    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
     identity_smem(sm.P0, sm.S10, sm.S20);
     __syncthreads();
     for (int k = 0; k < ng; ++k) {
@@ -1459,7 +1583,7 @@ __global__ void __launch_bounds__(CST) scan_groups_kernel(Params p) {
         const int last = min(g.C, (k + 1) * CG) - 1;
         load_slot_smem(p.incl + ((size_t)b * g.C + last) * g.SW, sm.P1, sm.S11, sm.S21);
         __syncthreads();
-        chen_mul_smem(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp, i0, j0);
+        chen_mul_256(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp);
     }
 }
 
@@ -1469,21 +1593,20 @@ __global__ void __launch_bounds__(CST) scan_fix_kernel(Params p) {
     const int ng = scan_groups(g.C);
     const int b = blockIdx.x / g.C, c = blockIdx.x - b * g.C;
     const int k = c / CG;
-    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
     const size_t base = (size_t)b * g.C;
     load_slot_smem(p.gex + ((size_t)b * ng + k) * g.SW, sm.P0, sm.S10, sm.S20);
     __syncthreads();
     if (c > k * CG) {
         load_slot_smem(p.incl + (base + c - 1) * g.SW, sm.P1, sm.S11, sm.S21);
         __syncthreads();
-        chen_mul_smem(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp, i0, j0);
+        chen_mul_256(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp);
     }
     store_slot(p.carry + (base + c) * g.SW, sm.P0, sm.S10, sm.S20);
     if (c == g.C - 1 && g.readout == EWS_READOUT_TERMINAL) {
         // the sample's terminal value: carry (x) the last chunk's aggregate
         load_slot_smem(p.agg + (base + c) * g.SW, sm.P1, sm.S11, sm.S21);
         __syncthreads();
-        chen_mul_smem(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp, i0, j0);
+        chen_mul_256(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp);
         const int N = g.N;
         float* row = p.out + (size_t)b * g.W;
         if (threadIdx.x == 0) row[0] = 1.f;
@@ -1533,7 +1656,7 @@ __device__ void apply_JT_smem(const float* Pr, const float* U1v, float* L1, floa
 // The backward's carries by a two-level reverse scan, the counterpart of the forward's (scan_*_kernel).
 // The element of a range of chunks is (G, mu): the forward aggregate G of the range and the cotangent mu at
 // the range's start from the range's own output gradients (zero carry). An earlier range a and a later b
-// combine to (G_a (x) G_b, J(G_a)^T mu_b + mu_a), with J(G)^T the transposed Chen map (apply_JT_smem).
+// combine to (G_a (x) G_b, J(G_a)^T mu_b + mu_a), with J(G)^T the transposed Chen map (apply_JT_256).
 //   bscan_local_kernel:  per group, the suffix elements from every chunk to the group's end (gsuf, incl);
 //   bscan_groups_kernel: per sample, the cotangent arriving at each group's end (gex);
 //   bscan_fix_kernel:    per chunk, the cotangent arriving at its end (lcarry), J(suffix after it)^T lam + mu.
@@ -1555,11 +1678,9 @@ __device__ void bscan_store_lam(float* slot, const BScanSmem& sm) {
 }
 
 // L <- J(G)^T L for G in (P1, S11) (its flow complement row-major and level 1)
-__device__ void bscan_apply(BScanSmem& sm, int i0, int j0) {
-    float X2[4][4];
-    load_rowmajor(sm.L2r, X2, i0, j0);
+__device__ void bscan_apply(BScanSmem& sm) {
     __syncthreads();
-    apply_JT_smem(sm.P1, sm.S11, sm.L1, X2, sm.L2r, sm.T0, sm.v1, sm.v2, i0, j0);
+    apply_JT_256(sm.P1, sm.S11, sm.L1, sm.L2r, sm.T0, sm.v1, sm.v2);
 }
 
 __global__ void __launch_bounds__(CST) bscan_local_kernel(Params p) {
@@ -1568,7 +1689,6 @@ __global__ void __launch_bounds__(CST) bscan_local_kernel(Params p) {
     const int ng = scan_groups(g.C);
     const int b = blockIdx.x / ng, k = blockIdx.x - b * ng;
     const int c0 = k * CG, c1 = min(g.C, c0 + CG) - 1;
-    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
     const size_t base = (size_t)b * g.C;
     load_slot_smem(p.fagg + (base + c1) * g.SW, sm.P0, sm.S10, sm.S20);
     for (int e = threadIdx.x; e < MM; e += blockDim.x) sm.L2r[e] = 0.f;
@@ -1581,10 +1701,10 @@ __global__ void __launch_bounds__(CST) bscan_local_kernel(Params p) {
     for (int c = c1 - 1; c >= c0; --c) {
         load_slot_smem(p.fagg + (base + c) * g.SW, sm.P1, sm.S11, sm.S21);
         __syncthreads();
-        bscan_apply(sm, i0, j0);                 // mu <- J(G_c)^T mu
+        bscan_apply(sm);                 // mu <- J(G_c)^T mu
         bscan_add_mu(sm, p.agg + (base + c) * g.SW);  //      + mu_c
         __syncthreads();
-        chen_mul_smem(sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.v3, i0, j0);
+        chen_mul_256(sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.v3);
         store_slot(p.gsuf + (base + c) * g.SW, sm.P0, sm.S10, sm.S20);
         bscan_store_lam(p.incl + (base + c) * g.SW, sm);
         __syncthreads();
@@ -1596,7 +1716,6 @@ __global__ void __launch_bounds__(CST) bscan_groups_kernel(Params p) {
     const Geom& g = p.g;
     const int ng = scan_groups(g.C);
     const int b = blockIdx.x;
-    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
     for (int e = threadIdx.x; e < MM; e += blockDim.x) sm.L2r[e] = 0.f;
     if (threadIdx.x < NP) sm.L1[threadIdx.x] = 0.f;
     __syncthreads();
@@ -1607,7 +1726,7 @@ __global__ void __launch_bounds__(CST) bscan_groups_kernel(Params p) {
         __syncthreads();
         load_slot_smem(p.gsuf + first * g.SW, sm.P1, sm.S11, sm.S21);
         __syncthreads();
-        bscan_apply(sm, i0, j0);
+        bscan_apply(sm);
         bscan_add_mu(sm, p.incl + first * g.SW);
         __syncthreads();
     }
@@ -1619,7 +1738,6 @@ __global__ void __launch_bounds__(CST) bscan_fix_kernel(Params p) {
     const int ng = scan_groups(g.C);
     const int b = blockIdx.x / g.C, c = blockIdx.x - b * g.C;
     const int k = c / CG, last = min(g.C, (k + 1) * CG) - 1;
-    const int i0 = 4 * (threadIdx.x >> 3), j0 = 4 * (threadIdx.x & 7);
     const size_t base = (size_t)b * g.C;
     {
         const float* src = p.gex + ((size_t)b * ng + k) * g.SW;
@@ -1630,7 +1748,7 @@ __global__ void __launch_bounds__(CST) bscan_fix_kernel(Params p) {
     if (c < last) {
         load_slot_smem(p.gsuf + (base + c + 1) * g.SW, sm.P1, sm.S11, sm.S21);
         __syncthreads();
-        bscan_apply(sm, i0, j0);
+        bscan_apply(sm);
         bscan_add_mu(sm, p.incl + (base + c + 1) * g.SW);
         __syncthreads();
     }
