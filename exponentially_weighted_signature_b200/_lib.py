@@ -25,6 +25,7 @@ EWS_F_BASEPOINT = 8
 EWS_F_DETERMINISTIC = 16
 EWS_F_TEST_WITHHOLD = 32
 EWS_F_TERMINAL_SCAN = 64
+EWS_F_LOGSIG = 128
 
 EWS_READOUT_PREFIX = 0
 EWS_READOUT_TERMINAL = 1

@@ -1749,6 +1749,7 @@ extern "C" int ews_diag_fwd(const ews_diag_args* a, ews_stream_t stream) {
     if (g.nu ? !a->clock : (!a->tab_q1 || !a->tab_q2)) return EWS_ERR_INVALID_ARGUMENT;
     if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
     if (diag_term_applies(a)) return diag_term_fwd(a, (cudaStream_t)stream);
+    if (a->flags & EWS_F_LOGSIG) return EWS_ERR_UNSUPPORTED;  // the log epilogue rides on the closed form
     const WsLayout L = fwd_layout(g);
     if (!a->fwd_ws || a->fwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
@@ -1788,6 +1789,7 @@ extern "C" int ews_diag_bwd(const ews_diag_args* a, ews_stream_t stream) {
     if (g.readout == EWS_READOUT_PREFIX && !a->out) return EWS_ERR_INVALID_ARGUMENT;
     if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
     if (diag_term_applies(a)) return diag_term_bwd(a, (cudaStream_t)stream);
+    if (a->flags & EWS_F_LOGSIG) return EWS_ERR_UNSUPPORTED;
     const WsLayout F = fwd_layout(g);
     const WsLayout L = bwd_layout(g);
     if (!a->fwd_ws || a->fwd_ws_bytes < F.total) return EWS_ERR_WORKSPACE;

@@ -84,6 +84,11 @@ __device__ __forceinline__ TS carve(float* sm, int d_in) {
 
 __host__ __device__ inline size_t smem_bytes() { return sizeof(float) * (2 * TL * NP + 32 * LTS + 32 * XTS + 10 * NP); }
 
+// The compressed depth-2 log-signature: N letters, then the Lyndon words (i, j), i < j, in lexicographic
+// order (signax 0.2.1's coordinates); (i, j) sits at i (2N - i - 1) / 2 + (j - i - 1) after the letters.
+__host__ __device__ inline int logsig_width(int N) { return N + N * (N - 1) / 2; }
+__host__ __device__ inline int lyndon2_index(int i, int j, int N) { return i * (2 * N - i - 1) / 2 + (j - i - 1); }
+
 // w = exp(x k) for an integer k >= 0: x k = hi + lo exactly, exp(hi) (1 + lo).
 __device__ __forceinline__ float weight(float x, int k) {
     const float kf = (float)k;
@@ -253,6 +258,28 @@ __global__ void __launch_bounds__(TNT) fin_kernel(TP p) {
     float* sv = p.save + (size_t)b * PW;
     const float* q1 = p.tab_q1 + (size_t)b * N;
     const float* q2 = p.tab_q2 + (size_t)b * N * N;
+    if (p.flags & EWS_F_LOGSIG) {
+        // the log-signature epilogue (ews/layer.py:488-498): log(1 + X) = (X1, X2 - X1 X1^T / 2) at depth 2,
+        // compressed to the Lyndon words (level 1: every letter; level 2: i < j, lexicographic)
+        float* x1 = ss;  // the segment sums are no longer needed
+        if (threadIdx.x < NP) x1[threadIdx.x] = threadIdx.x < N ? q1[threadIdx.x] * Sc[threadIdx.x] : 0.f;
+        __syncthreads();
+        float* row = p.out + (size_t)b * logsig_width(N);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const int e = threadIdx.x + TNT * m, i = e >> 5, j = e & 31;
+            sv[e] = M[m];
+            sv[MM + e] = G[m];
+            if (i < j && j < N)
+                row[N + lyndon2_index(i, j, N)] =
+                    fmaf(q1[i] * M[m], q1[j], q2[i * N + j] * G[m]) - 0.5f * x1[i] * x1[j];
+        }
+        if (threadIdx.x < NP) {
+            sv[2 * MM + threadIdx.x] = Sc[threadIdx.x];
+            if (threadIdx.x < N) row[threadIdx.x] = x1[threadIdx.x];
+        }
+        return;
+    }
     float* row = p.out + (size_t)b * (1 + N + N * N);
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
@@ -272,17 +299,37 @@ __global__ void __launch_bounds__(TNT) fin_kernel(TP p) {
 
 // Per sample: the coefficients of dr_t (A1, A2, c) and the table gradients dL/dQ1, dL/dQ2.
 __global__ void __launch_bounds__(TNT) prep_kernel(TP p) {
-    __shared__ float G2[MM], Ms[MM], dMs[MM], q1s[NP];
+    __shared__ float G2[MM], Ms[MM], dMs[MM], q1s[NP], g1s[NP];
     const int b = blockIdx.x, N = p.N, W = 1 + N + N * N;
-    const float* go = p.grad_out + (size_t)b * W;
+    const bool logsig = (p.flags & EWS_F_LOGSIG) != 0;
+    const float* go = p.grad_out + (size_t)b * (logsig ? logsig_width(N) : W);
     const float* sv = p.save + (size_t)b * PW;
     const float* q2 = p.tab_q2 + (size_t)b * N * N;
     float* dm = p.dmat + (size_t)b * (2 * MM + NP);
     if (threadIdx.x < NP) q1s[threadIdx.x] = threadIdx.x < N ? p.tab_q1[(size_t)b * N + threadIdx.x] : 0.f;
     for (int e = threadIdx.x; e < MM; e += TNT) {
         const int i = e >> 5, j = e & 31;
-        G2[e] = (i < N && j < N) ? go[1 + N + i * N + j] : 0.f;
+        if (logsig)  // the log epilogue's adjoint at level 2: only the Lyndon entries i < j carry a cotangent
+            G2[e] = (i < j && j < N) ? go[N + lyndon2_index(i, j, N)] : 0.f;
+        else
+            G2[e] = (i < N && j < N) ? go[1 + N + i * N + j] : 0.f;
         Ms[e] = sv[e];
+    }
+    __syncthreads();
+    if (threadIdx.x < NP) {
+        // level 1: g1 = dlog1 - (G2 + G2^T) X1 / 2 with X1 = Q1 s under the log epilogue, else the row's own
+        const int i = threadIdx.x;
+        float g1 = 0.f;
+        if (i < N) {
+            if (logsig) {
+                float acc = 0.f;
+                for (int j = 0; j < N; ++j) acc = fmaf(G2[i * NP + j] + G2[j * NP + i], q1s[j] * sv[2 * MM + j], acc);
+                g1 = go[i] - 0.5f * acc;
+            } else {
+                g1 = go[1 + i];
+            }
+        }
+        g1s[i] = g1;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < MM; e += TNT) {
@@ -302,7 +349,7 @@ __global__ void __launch_bounds__(TNT) prep_kernel(TP p) {
     }
     if (threadIdx.x < NP) {
         const int i = threadIdx.x;
-        const float g1 = i < N ? go[1 + i] : 0.f;
+        const float g1 = g1s[i];
         float cs = q1s[i] * g1;
         for (int k = 0; k < NP; ++k) cs = fmaf(dMs[i * NP + k], sv[2 * MM + k], cs);
         dm[2 * MM + i] = cs;

@@ -136,7 +136,10 @@ class DiagScan(torch.autograd.Function):
         path_c = path.contiguous()
         x_c, q1_c, q2_c = x.contiguous().float(), q1.contiguous().float(), q2.contiguous().float()
         lift_c = None if lift is None else lift.contiguous().float()
-        out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
+        if flags & _lib.EWS_F_LOGSIG:  # the fused log-signature epilogue: letters, then the Lyndon pairs
+            out = torch.empty((B, N + N * (N - 1) // 2), device=dev, dtype=torch.float32)
+        else:
+            out = torch.empty((B, T, 1 + D) if readout == _lib.EWS_READOUT_PREFIX else (B, 1 + D), device=dev, dtype=torch.float32)
         a = _lib.DiagArgs()
         a.batch, a.steps, a.d_in, a.dim, a.depth = B, T, d_in, N, 2
         a.chunk, a.readout, a.flags, a.series_q, a.spin_limit = chunk, readout, flags, 0, SPIN_LIMIT

@@ -155,8 +155,16 @@ class EWS(nn.Module):
 
     # ------------------------------------------------------------------ the engine call
 
-    def _flat(self, path, clock, readout, a_scale=1.0, lift=None, increments=False):
-        """Batched flat EWS: path (B, L, d_in) knots [(B, L-1, d_in) increments], clock (B, L)."""
+    def fused_logsig_applies(self, d_in: int) -> bool:
+        """Whether the terminal log-signature can come out of the engine's closed-form terminal kernels
+        (EWS_F_LOGSIG): diagonal engine, depth 2, uniform clock without a basepoint, d_in <= 32 and
+        dim * d_in <= 1024."""
+        return (self.engine == "diag" and self.N == 2 and self.reweighting_mode == "displacement_uniform"
+                and self.d <= 32 and d_in <= 32 and self.d * d_in <= 1024)
+
+    def _flat(self, path, clock, readout, a_scale=1.0, lift=None, increments=False, log_epilogue=False):
+        """Batched flat EWS: path (B, L, d_in) knots [(B, L-1, d_in) increments], clock (B, L). With
+        ``log_epilogue`` (terminal readout, ``fused_logsig_applies``) the compressed log-signature instead."""
         uniform = self.reweighting_mode != "displacement"
         basepoint = self.reweighting_mode == "displacement_uniform_basepoint"
         if self.engine == "dense":
@@ -180,6 +188,8 @@ class EWS(nn.Module):
         else:
             q1, q2 = series.diag_tables(x, self.series_q)
         flags = _lib.EWS_F_UNIFORM | (_lib.EWS_F_BASEPOINT if basepoint else 0) | _det_flags()
+        if log_epilogue:
+            flags |= _lib.EWS_F_LOGSIG
         if increments:
             flags |= _lib.EWS_F_INCREMENTS
             if path.dtype == torch.bfloat16:
@@ -356,6 +366,15 @@ class LogEWS(nn.Module):
         if readout not in READOUTS:
             raise ValueError("readout must be 'terminal', 'prefix', 'mean', or 'max'")
         inner = "terminal" if readout == "terminal" else "prefix"
+        d_in = path.shape[-1]
+        if readout == "terminal" and output_format == "flat" and self.ewms.fused_logsig_applies(d_in):
+            # the log / Lyndon epilogue fused into the engine's terminal kernels (EWS_F_LOGSIG)
+            single = path.dim() == 2
+            p3, c3 = (path[None], clock[None]) if single else (path, clock)
+            if p3.dim() != 3 or c3.dim() != 2:
+                raise ValueError("clock must be 2D for batched paths")
+            feat = self.ewms._flat(p3, c3, "terminal", lift=lift, increments=increments, log_epilogue=True)
+            return feat[0] if single else feat
         flat = self.ewms(path, clock, readout=inner, output_format="flat", lift=lift, increments=increments)
         levels = logsig.split_levels(flat[..., 1:], self.d, self.N)
         log_levels = logsig.tensor_log(levels)

@@ -57,6 +57,13 @@ typedef struct CUstream_st* ews_stream_t; /* = cudaStream_t */
 #define EWS_F_TERMINAL_SCAN 64u /* diagonal engine, uniform clock, terminal readout: evaluate the terminal
                                    value with the chunked scan instead of its closed form (see below) */
 
+#define EWS_F_LOGSIG 128u      /* diagonal engine, closed-form terminal path (uniform clock, terminal readout,
+                                   depth 2): `out` receives the compressed log-signature (B, N + N (N - 1) / 2),
+                                   the letters then the Lyndon words (i, j), i < j, in lexicographic order, of
+                                   log(1 + X) = (X1, X2 - X1 X1^T / 2) (the LogEWS epilogue, ews/layer.py:488-498),
+                                   and the backward's `grad_out` is its cotangent; other paths return
+                                   EWS_ERR_UNSUPPORTED */
+
 #define EWS_READOUT_PREFIX 0    /* out: (B, T, 1 + D), row t = [1, S_1,t, ..., S_n,t] */
 #define EWS_READOUT_TERMINAL 1  /* out: (B, 1 + D), the last row only */
 

@@ -87,3 +87,32 @@ def test_small_batch_splits_the_path():
     for name, a, b in zip(("out", "x", "q1", "q2", "lift", "increments"), closed, scan):
         e = relerr(a.double().cpu(), b.double().cpu())
         assert e <= 1e-5, f"{name}: relerr {e:.2e}"
+
+
+def test_fused_log_epilogue_matches_the_unfused_one():
+    """LogEWS's terminal log-signature from the closed-form kernels with the log / Lyndon epilogue fused
+    (EWS_F_LOGSIG) against the same layer's EWS terminal followed by the tensor log and the Lyndon gather
+    as separate device ops (ews/layer.py:488-498): forward and every gradient within relerr 1e-5."""
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test run without a CUDA device")
+    from exponentially_weighted_signature_b200 import LogEWS, AParamDiag, logsig
+
+    g = torch.Generator().manual_seed(3)
+    B, T, N, d = 4, 300, 32, 16
+    inc = (torch.randn(B, T, d, generator=g) / T**0.5).cuda().requires_grad_(True)
+    lam = torch.exp(torch.rand(N, generator=g) * 4 - 4)
+    lift = (torch.randn(N, d, generator=g) / 4).cuda().requires_grad_(True)
+    clock = (torch.arange(T + 1, dtype=torch.float32) / T).expand(B, T + 1).contiguous().cuda()
+    layer = LogEWS(AParamDiag(lam).cuda(), 2, reweighting_mode="displacement_uniform", leaf="series", series_q=6)
+    assert layer.ewms.fused_logsig_applies(d)
+    fused = layer(inc, clock, readout="terminal", lift=lift, increments=True)
+    w = torch.randn(fused.shape, generator=g).cuda()
+    gf = torch.autograd.grad((fused * w).sum(), [inc, lift, layer.ewms.A_param.values])
+    flat = layer.ewms(inc, clock, readout="terminal", lift=lift, increments=True)
+    levels = logsig.split_levels(flat[..., 1:], N, 2)
+    ref = logsig.compress(logsig.tensor_log(levels), N)
+    gr = torch.autograd.grad((ref * w).sum(), [inc, lift, layer.ewms.A_param.values])
+    rel = lambda a, b: float((a - b).abs().max() / b.abs().max())  # noqa: E731
+    assert rel(fused, ref) <= 1e-5
+    for a, b in zip(gf, gr):
+        assert rel(a, b) <= 1e-5
