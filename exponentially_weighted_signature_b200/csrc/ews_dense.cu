@@ -711,7 +711,7 @@ __device__ void tc_load_tables(const Params& p, const TcSmem& s, int b, bool tra
     for (int e = threadIdx.x; e < MM; e += blockDim.x) {
         const int i = e / NP, k = e - i * NP;
         const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
-        s.Dr[i * NP + k] = v;
+        if (s.Dr) s.Dr[i * NP + k] = v;
         s.Dt[k * NP + i] = v;
         const float hi = __uint_as_float(tf32_bits(v));
         const int o = transpose ? bk_off(k, i) : bk_off(i, k);
@@ -896,15 +896,41 @@ __global__ void __launch_bounds__(NT) power_kernel(Params p) {
     }
 }
 
-__global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
+namespace tc {
+// Smem of the output pass (fwd_tc_kernel): operands, transposition buffers, D k-major and the per-tile vectors
+// only (72 KB at q = 3, three CTAs per SM).
+__host__ __device__ inline size_t tc_out_smem_bytes(int QP) {
+    const size_t f = 2 * MM + 2 * 4 * MM + TILES * 32 * RQS + MM + TILES * vec_per_tile(QP);
+    return f * sizeof(float) + 64 + 128;
+}
+
+__device__ TcSmem tc_carve_out(unsigned char* raw, const Geom& g) {
+    uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 127) & ~(uintptr_t)127;
+    float* p = reinterpret_cast<float*>(base);
+    TcSmem s{};
+    s.Bhi = p; p += MM;
+    s.Blo = p; p += MM;
+    s.Ahi = p; p += 4 * MM;
+    s.Alo = p; p += 4 * MM;
+    s.RQ = p; p += TILES * 32 * RQS;
+    s.Dt = p; p += MM;
+    s.vec = p; p += TILES * vec_per_tile(g.QP);
+    s.bar = reinterpret_cast<uint64_t*>(p);
+    s.tmem = reinterpret_cast<uint32_t*>(p + 2);
+    s.bcast = reinterpret_cast<int*>(p + 4);
+    return s;
+}
+}  // namespace tc
+
+// The forward's output pass on tcgen05: a CTA of 4 warps stacks 4 chunks of one sample (M = 128 rows), runs
+// each from its carry (computed by agg_kernel and the carry scan) and writes the prefix rows. Per step
+// X = S2 - S2 D^T and M X = X - D X are 3xTF32 products in TMEM.
+__global__ void __launch_bounds__(tc::NTH, 3) fwd_tc_kernel(Params p) {
     using namespace tc;
     extern __shared__ unsigned char smem_raw[];
     const Geom& g = p.g;
-    TcSmem s = tc_carve(smem_raw, g);
+    TcSmem s = tc_carve_out(smem_raw, g);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int bi = tid >> 3, bj = tid & 7;  // 4x4 blocks of the first 64 threads (look-back products)
-    const int i0 = 4 * (bi & 7), j0 = 4 * bj;
-    const bool deterministic = (g.flags & EWS_F_DETERMINISTIC) != 0;
     const int N = g.N;
     const int mbar_limit = 1 << 20;
 
@@ -954,40 +980,25 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
         tc_load_tables(p, s, b);
         __syncthreads();
 
+        // the chunk's carry; a chunk that ends early keeps feeding the MMAs (its rows are not written)
         float col[32];
-        for (int pass = 0; pass < 2 && !failed; ++pass) {
-            // with precomputed aggregates and carries (agg_kernel, scan_*_kernel) only the output pass runs
-            if (pass == 0 && g.agg_pre) continue;
-            // ---- initial state: identity (pass 1) or the chunk's carry (pass 2)
-            if (pass == 0) {
+        {
+            const float* cs = p.carry + ((size_t)b * g.C + (valid_me ? c_me : 0)) * g.SW;
 #pragma unroll
-                for (int n = 0; n < 32; ++n) col[n] = 0.f;
-                vt[lane] = 0.f;
-            } else {
-                const float* cs = p.carry + ((size_t)b * g.C + (valid_me ? c_me : 0)) * g.SW;
-#pragma unroll
-                for (int n = 0; n < 32; ++n) col[n] = valid_me ? ldcg(cs + MM + NP + n * NP + lane) : 0.f;
-                vt[lane] = valid_me ? ldcg(cs + MM + lane) : 0.f;
-            }
-            __syncwarp();
-            float* saved = s.stage + warp * tc_stage_stride(g.W);
-            // with precomputed aggregates (agg_kernel) the first pass only publishes them and looks back
-            const bool skip = pass == 0 && g.agg_pre;
-            // the intervals' local terms (computed by local_kernel), copied in one interval ahead
-            if (len_me > 0 && !skip) fetch_loc(p, b, t0_me, vt + 2 * NP, LW);
-            cp_async_commit();
-            for (int k = 0; k < (skip ? 0 : steps); ++k) {
+            for (int n = 0; n < 32; ++n) col[n] = valid_me ? ldcg(cs + MM + NP + n * NP + lane) : 0.f;
+            vt[lane] = valid_me ? ldcg(cs + MM + lane) : 0.f;
+        }
+        __syncwarp();
+        // the intervals' local terms (computed by local_kernel), copied in one interval ahead
+        if (len_me > 0) fetch_loc(p, b, t0_me, vt + 2 * NP, LW);
+        cp_async_commit();
+            for (int k = 0; k < steps; ++k) {
                 const bool live = k < len_me;
                 cp_async_wait<0>();
                 __syncwarp();
                 const float* stg = vt + 2 * NP + (k & 1) * LW;  // this interval's [s1 | U | V]
                 if (k + 1 < len_me) fetch_loc(p, b, t0_me + k + 1, vt + 2 * NP + ((k + 1) & 1) * LW, LW);
                 cp_async_commit();
-                if (k == len_me) {
-                    // this tile's chunk has ended: park its state; the remaining steps only feed the MMAs
-#pragma unroll
-                    for (int n = 0; n < 32; ++n) saved[n * 32 + lane] = col[n];
-                }
                 // E0: the lane's column of S2 -> its row (through the exchange buffer) -> A operand row
                 float srow[32];
 #pragma unroll
@@ -1068,7 +1079,7 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                     if (live) vt[lane] = s1new;
                     fence_before();
                     __syncwarp();
-                    if (pass == 1 && live && g.readout == EWS_READOUT_PREFIX && lane < N) {
+                    if (live && lane < N) {
                         // the prefix row straight from registers: each level-2 row is one contiguous run
                         float* row = p.out + ((size_t)b * g.T + t0_me + k) * g.W;
                         if (lane == 0) row[0] = 1.f;
@@ -1079,120 +1090,8 @@ __global__ void __launch_bounds__(tc::NTH) fwd_tc_kernel(Params p) {
                     }
                 }
             }
-            if (failed) break;
-            if (len_me < steps && !skip) {
-#pragma unroll
-                for (int n = 0; n < 32; ++n) col[n] = saved[n * 32 + lane];
-            }
-            __syncthreads();
-            if (pass == 1) break;
-            // ---- aggregates of the 4 chunks (flow complement, S1, S2) -> agg slots
-            if (valid_me && !g.agg_pre) {
-                float* as = p.agg + ((size_t)b * g.C + c_me) * g.SW;
-#pragma unroll
-                for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = col[n];
-                as[MM + lane] = vt[lane];
-            }
-            // flow complements C(len) of the full and the last chunk (computed per sample by power_kernel)
-            float* W0 = s.Ahi;            // scratch matrices live in the idle operand buffers
-            float* W1 = s.Ahi + MM;
-            float* W2 = s.Ahi + 2 * MM;
-            float* W3 = s.Ahi + 3 * MM;
-            float* W4 = s.Alo;
-            float* W5 = s.Alo + MM;
-            float* W6 = s.Alo + 2 * MM;   // C(Lc) row-major
-            float* W7 = s.Alo + 3 * MM;   // C(last) row-major
-            if (!g.agg_pre) {
-                for (int e = tid; e < 2 * MM; e += blockDim.x) W6[e] = p.pw[(size_t)b * 2 * MM + e];
-                __syncthreads();
-                for (int t = 0; t < TILES; ++t) {
-                    const int c = grp * TILES + t;
-                    if (c >= g.C) break;
-                    const float* C = (c == g.C - 1) ? W7 : W6;
-                    float* as = p.agg + ((size_t)b * g.C + c) * g.SW;
-                    for (int e = tid; e < MM; e += blockDim.x) as[e] = C[e];
-                }
-            }
-            __syncthreads();
-            // publish the aggregates (the first chunk of the sequence publishes its inclusive value)
-            for (int t = 0; t < TILES; ++t) {
-                const int c = grp * TILES + t;
-                if (c >= g.C) break;
-                if (c == 0) {
-                    float* is = p.incl + (size_t)b * g.C * g.SW;
-                    const float* as = p.agg + (size_t)b * g.C * g.SW;
-                    for (int e = tid; e < g.SW; e += blockDim.x) is[e] = as[e];
-                    __syncthreads();
-                    if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(p.flags + (size_t)b * g.C, kFlagIncl);
-                } else {
-                    cta_publish(p.flags + (size_t)b * g.C + c, kFlagAgg);
-                }
-                __syncthreads();
-            }
-            // ---- carries: look back for the group's first chunk, then fold the group's own aggregates
-            float* ve = s.misc;           // excl S1
-            float* va = s.misc + NP;      // acc / scratch S1
-            float* vx = s.misc + 2 * NP;  // loaded S1
-            float* vtmp = s.misc + 3 * NP;
-            float* T0 = s.stage;
-            float* T1 = s.stage + MM;
-            // excl -> (W2 C, ve S1, W3 S2)
-            identity_smem(W2, ve, W3);
-            __syncthreads();
-            const int c_first = grp * TILES;
-            if (c_first > 0) {
-                identity_smem(W4, va, W5);  // acc
-                __syncthreads();
-                int j = c_first - 1;
-                for (;;) {
-                    const int f = tc_cta_wait(p, s, p.flags + (size_t)b * g.C + j, deterministic ? kFlagIncl : kFlagAgg, tile);
-                    if (f < 0) {
-                        failed = true;
-                        break;
-                    }
-                    const size_t sj = ((size_t)b * g.C + j) * g.SW;
-                    load_slot_smem((f == kFlagIncl ? p.incl : p.agg) + sj, W0, vx, W1);
-                    __syncthreads();
-                    chen_mul_smem(W0, vx, W1, W4, va, W5, W4, va, W5, T0, T1, vtmp, i0, j0);  // acc = X (x) acc
-                    if (f == kFlagIncl) break;
-                    --j;
-                }
-                if (failed) break;
-                for (int e = tid; e < MM; e += blockDim.x) {
-                    W2[e] = W4[e];
-                    W3[e] = W5[e];
-                }
-                if (tid < NP) ve[tid] = va[tid];
-                __syncthreads();
-            }
-            for (int t = 0; t < TILES; ++t) {
-                const int c = c_first + t;
-                if (c >= g.C) break;
-                const size_t sc = ((size_t)b * g.C + c) * g.SW;
-                store_slot(p.carry + sc, W2, ve, W3);
-                // incl_c = excl (x) agg_c
-                load_slot_smem(p.agg + sc, W0, vx, W1);
-                __syncthreads();
-                chen_mul_smem(W2, ve, W3, W0, vx, W1, W2, ve, W3, T0, T1, vtmp, i0, j0);
-                if (c > 0) {
-                    store_slot(p.incl + sc, W2, ve, W3);
-                    cta_publish(p.flags + (size_t)b * g.C + c, kFlagIncl);
-                }
-                __syncthreads();
-                if (c == g.C - 1 && g.readout == EWS_READOUT_TERMINAL) {
-                    float* row = s.stage;
-                    if (tid == 0) row[0] = 1.f;
-                    for (int e = tid; e < N; e += blockDim.x) row[1 + e] = ve[e];
-                    for (int e = tid; e < N * N; e += blockDim.x) row[1 + N + e] = W3[(e / N) * NP + (e % N)];
-                    __syncthreads();
-                    if (warp == 0) warp_store_span(p.out + (size_t)b * g.W, row, g.W);
-                    __syncthreads();
-                }
-            }
-            __syncthreads();
-            if (g.readout == EWS_READOUT_TERMINAL) break;
-        }
         if (failed) break;
+        __syncthreads();
     }
     // every exit drains the tensor core and frees TMEM
     if (failed && tid == 0) {
@@ -2743,6 +2642,17 @@ __global__ void reduce_kernel(Params p, float* grad_d, float* grad_f, float* gra
 
 // ---------------------------------------------------------------------------------- host side
 
+static int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
 static int make_geom(const ews_dense_args* a, Geom* g) {
     if (!a || a->batch <= 0 || a->steps <= 0 || a->d_in <= 0 || a->dim <= 0) return EWS_ERR_INVALID_ARGUMENT;
     if (a->depth != 2 || a->dim > NP || a->d_in > 32) return EWS_ERR_UNSUPPORTED;
@@ -2763,11 +2673,23 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
     if (a->chunk > 0) {
         g->Lc = a->chunk;
     } else {
-        // the forward stacks 4 chunks of a sample per CTA (2 CTAs per SM): aim for one wave of groups
-        const int groups = std::max(1, (2 * 148) / g->B);
-        const int C = 4 * groups;
-        const int Lc = (g->T + C - 1) / C;
-        g->Lc = std::max(16, std::min(256, Lc));
+        // The chains stack 4 chunks of a sample per CTA: the forward's output pass runs 3 CTAs per SM, the
+        // backward's two passes 2 per SM. Pick the chunk length that minimises the chains' waves x steps
+        // (plus a per-tile overhead of ~10 steps and the scans' sequential products).
+        const int sms = num_sms();
+        double best = 1e30;
+        int bestL = 256;
+        for (int L = 16; L <= 512; ++L) {
+            const int C = (g->T + L - 1) / L;
+            const long G = (long)g->B * ((C + 3) / 4);
+            const long wf = (G + 3L * sms - 1) / (3L * sms), wb = (G + 2L * sms - 1) / (2L * sms);
+            const double cost = (L + 10.0) * (double)(wf + 2 * wb) + 0.6 * C / 8.0;
+            if (cost < best) {
+                best = cost;
+                bestL = L;
+            }
+        }
+        g->Lc = bestL;
     }
     g->C = (g->T + g->Lc - 1) / g->Lc;
     g->SR = 1;
@@ -2837,16 +2759,6 @@ static WsLayout bwd_layout(const Geom& g) {
     return L;
 }
 
-static int num_sms() {
-    static int n = 0;
-    if (n == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
 
 template <typename K>
 static int launch(K kernel, const Params& p, size_t smem, cudaStream_t s) {
@@ -2928,7 +2840,7 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     scan_fix_kernel<<<g.B * g.C, CST, 0, s>>>(p);
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     if (g.readout == EWS_READOUT_TERMINAL) return EWS_OK;  // the scan wrote the terminal rows
-    const size_t smem = tc::tc_smem_bytes(g.W, g.QP);
+    const size_t smem = tc::tc_out_smem_bytes(g.QP);
     if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
@@ -2938,7 +2850,7 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     const int groups = (g.C + tc::TILES - 1) / tc::TILES;
     int grid = per_sm * num_sms();
     if (grid > g.B * groups) grid = g.B * groups;
-    fwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);  // p.g.agg_pre: the output pass and the look-back only
+    fwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 
