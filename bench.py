@@ -32,9 +32,9 @@ METRIC = "EWS fwd+bwd (batch·steps)/s at 1/2/4/8 B200, % HBM/TC roofline vs JAX
 UNIT = "batch·steps/s"
 L2_BYTES = 126 * 1024 * 1024
 # kernels each library call launches (the diagonal engine's closed-form terminal path: fwd 2, bwd 4)
-KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 5, "ews_dense_bwd": 4,
+KERNELS_PER_CALL = {"ews_diag_fwd": 1, "ews_diag_bwd": 3, "ews_dense_fwd": 8, "ews_dense_bwd": 7,
                     "ews_block_fwd": 2, "ews_block_bwd": 2, "ews_expm": 1, "ews_expm_adjoint": 1}
-TERMINAL_KERNELS = {"ews_diag_fwd": 2, "ews_diag_bwd": 4}
+TERMINAL_KERNELS = {"ews_diag_fwd": 2, "ews_diag_bwd": 4, "ews_dense_fwd": 7}
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per sample-interval of each entry point's

@@ -60,7 +60,6 @@ struct Params {
     float* carry;
     const float* fagg;
     float* pw;  // per sample: flow complements C(Lc) and C(last chunk), row-major (2 MM)
-    float* lam;        // backward: the cotangent stream l~_t = l_t + g_t, same layout as the prefix output
     float* lcarry;     // backward: per chunk the cotangent arriving at its end [- | L1 | L2] (SW)
     float* loc;        // local terms per (sample, interval): [s1 | U_0..U_{QP-1} | V_0..V_{QP-1}], NP each
     float* coef;       // backward: per (sample, interval) the vector cotangents [ds1 | dU_a | dV_a], NP each
@@ -712,7 +711,7 @@ __device__ void tc_load_tables(const Params& p, const TcSmem& s, int b, bool tra
         const int i = e / NP, k = e - i * NP;
         const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
         if (s.Dr) s.Dr[i * NP + k] = v;
-        s.Dt[k * NP + i] = v;
+        if (s.Dt) s.Dt[k * NP + i] = v;
         const float hi = __uint_as_float(tf32_bits(v));
         const int o = transpose ? bk_off(k, i) : bk_off(i, k);
         s.Bhi[o] = hi;
@@ -720,19 +719,53 @@ __device__ void tc_load_tables(const Params& p, const TcSmem& s, int b, bool tra
     }
 }
 
-// u = S1 - D S1 for the lane's row (v: S1 (NP) | u (NP)); independent accumulators.
-__device__ __forceinline__ void tc_u(const TcSmem& s, float* v) {
-    const int l = threadIdx.x & 31;
-    const float* S1 = v;
+// Warp-broadcast reads of 16-byte aligned shared vectors, four entries per load (every lane reads the same
+// address, one shared-memory wavefront per load).
+// sum_n r[n] v[n]
+__device__ __forceinline__ float dot32_bc(const float (&r)[32], const float* __restrict__ v) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int n = 0; n < 32; n += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(v + n);
+        a0 = fmaf(r[n], q.x, a0);
+        a1 = fmaf(r[n + 1], q.y, a1);
+        a2 = fmaf(r[n + 2], q.z, a2);
+        a3 = fmaf(r[n + 3], q.w, a3);
+    }
+    return (a0 + a1) + (a2 + a3);
+}
+
+// c[n] += v[n] s
+__device__ __forceinline__ void axpy32_bc(float (&c)[32], const float* __restrict__ v, float s) {
+#pragma unroll
+    for (int n = 0; n < 32; n += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(v + n);
+        c[n] = fmaf(q.x, s, c[n]);
+        c[n + 1] = fmaf(q.y, s, c[n + 1]);
+        c[n + 2] = fmaf(q.z, s, c[n + 2]);
+        c[n + 3] = fmaf(q.w, s, c[n + 3]);
+    }
+}
+
+// sum_k Mk[k][lane] v[k] for a row-major 32 x 32 shared matrix Mk (the lane reads its column, conflict-free)
+// and a broadcast vector v.
+__device__ __forceinline__ float coldot_bc(const float* __restrict__ Mk, const float* __restrict__ v, int lane) {
     float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll
     for (int k = 0; k < NP; k += 4) {
-        d0 = fmaf(s.Dt[k * NP + l], S1[k], d0);
-        d1 = fmaf(s.Dt[(k + 1) * NP + l], S1[k + 1], d1);
-        d2 = fmaf(s.Dt[(k + 2) * NP + l], S1[k + 2], d2);
-        d3 = fmaf(s.Dt[(k + 3) * NP + l], S1[k + 3], d3);
+        const float4 q = *reinterpret_cast<const float4*>(v + k);
+        d0 = fmaf(Mk[k * NP + lane], q.x, d0);
+        d1 = fmaf(Mk[(k + 1) * NP + lane], q.y, d1);
+        d2 = fmaf(Mk[(k + 2) * NP + lane], q.z, d2);
+        d3 = fmaf(Mk[(k + 3) * NP + lane], q.w, d3);
     }
-    v[NP + l] = S1[l] - ((d0 + d1) + (d2 + d3));
+    return (d0 + d1) + (d2 + d3);
+}
+
+// u = S1 - D S1 for the lane's row (v: S1 (NP) | u (NP)).
+__device__ __forceinline__ void tc_u(const TcSmem& s, float* v) {
+    const int l = threadIdx.x & 31;
+    v[NP + l] = v[l] - coldot_bc(s.Dt, v, l);
     __syncwarp();
 }
 
@@ -1067,13 +1100,10 @@ __global__ void __launch_bounds__(tc::NTH, 3) fwd_tc_kernel(Params p) {
                     const float* s1 = stg;
                     const float s1l = s1[lane];
 #pragma unroll
-                    for (int n = 0; n < 32; ++n) col[n] = fmaf(u[n], s1l, xcol[n] - q2[n]);
-                    for (int a = 0; a < g.QP; ++a) {
-                        const float* Ua = stg + NP + a * NP;
-                        const float va = stg[NP + g.QP * NP + a * NP + lane];
-#pragma unroll
-                        for (int n = 0; n < 32; ++n) col[n] = fmaf(Ua[n], va, col[n]);
-                    }
+                    for (int n = 0; n < 32; ++n) col[n] = xcol[n] - q2[n];
+                    axpy32_bc(col, u, s1l);
+                    for (int a = 0; a < g.QP; ++a)
+                        axpy32_bc(col, stg + NP + a * NP, stg[NP + g.QP * NP + a * NP + lane]);
                     const float s1new = u[lane] + s1l;
                     __syncwarp();
                     if (live) vt[lane] = s1new;
@@ -1940,19 +1970,55 @@ __global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
 // gradient) the reverse recursion of one interval is
 //     l~2_{t-1} = M^T l~2_t M + g2_{t-1},      l~1_{t-1} = M^T (l~1_t + l~2_t s1_t) + g1_{t-1},
 // the forward's M S M^T with D replaced by D^T: the same two tcgen05 products per step (B operand D^T),
-// four chunks of one sample stacked into M = 128. Chunks run in reverse; the zero-carry pass gives the
-// chunk's local adjoint mu, a look-back over the later chunks (transposed chunk maps from the forward
-// aggregates) gives the cotangent arriving at the chunk's end, and the exact pass writes l~_t for every
-// interval. The gradients are then a parallel map over (sample, interval): grad_map_kernel, table_grad_kernel.
-__global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
+// four chunks of one sample stacked into M = 128. Chunks run in reverse: this zero-carry pass leaves each
+// chunk's local adjoint mu in `agg`, the reverse scan (bscan_*) turns those into the cotangent arriving at
+// every chunk's end (`lcarry`), and the exact pass (bwd_exact_kernel) runs every chunk again from its carry
+// with the gradient map fused in; table_grad_kernel forms the table gradients and dx.
+//
+// Shared memory holds the operands, the transposition buffers, D row-major and per tile l1 | v | s1 of two
+// intervals (64 KB, three CTAs per SM). The gradient rows are not staged: each lane loads its column of the
+// next interval's g2 (coalesced, one 4-byte word per row of the warp) while the second product runs, after
+// an L2 prefetch one interval earlier, and adds it in the epilogue.
+namespace tc {
+constexpr int BVEC = 4 * NP;  // per tile: l1 | v | s1 of two intervals
+
+__host__ __device__ inline size_t tc_bwd_smem_bytes() {
+    const size_t f = 2 * MM + 2 * 4 * MM + TILES * 32 * RQS + MM + TILES * BVEC;
+    return f * sizeof(float) + 64 + 128;  // + barrier / tmem slot / broadcast, + alignment slack
+}
+
+__device__ TcSmem tc_carve_bwd(unsigned char* raw) {
+    uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 127) & ~(uintptr_t)127;
+    float* p = reinterpret_cast<float*>(base);
+    TcSmem s{};
+    s.Bhi = p; p += MM;
+    s.Blo = p; p += MM;
+    s.Ahi = p; p += 4 * MM;
+    s.Alo = p; p += 4 * MM;
+    s.RQ = p; p += TILES * 32 * RQS;
+    s.Dr = p; p += MM;
+    s.vec = p; p += TILES * BVEC;
+    s.bar = reinterpret_cast<uint64_t*>(p);
+    s.tmem = reinterpret_cast<uint32_t*>(p + 2);
+    s.bcast = reinterpret_cast<int*>(p + 4);
+    return s;
+}
+
+// The cache lines of one output-gradient row (W floats) into L2, spread over the warp's lanes.
+__device__ __forceinline__ void prefetch_row_l2(const float* row, int W) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(row) & ~(uintptr_t)127;
+    const uintptr_t a1 = reinterpret_cast<uintptr_t>(row + W);
+    for (uintptr_t a = a0 + 128 * (threadIdx.x & 31); a < a1; a += 32 * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+}
+}  // namespace tc
+
+__global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
     using namespace tc;
     extern __shared__ unsigned char smem_raw[];
     const Geom& g = p.g;
-    TcSmem s = tc_carve(smem_raw, g);
+    TcSmem s = tc_carve_bwd(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int bi = tid >> 3, bj = tid & 7;
-    const int i0 = 4 * (bi & 7), j0 = 4 * bj;
-    const bool deterministic = (g.flags & EWS_F_DETERMINISTIC) != 0;
     const int N = g.N;
     const int mbar_limit = 1 << 20;
 
@@ -1973,30 +2039,14 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
     const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
     uint32_t phase = 0;
     bool failed = false;
-    bool mma_pending = false;
-    int b_cur = 0;
+    bool mma_pending = false;  // an MMA commit of `phase` may still be outstanding after a failed wait
 
     const uint64_t dA_hi = smem_desc(smem_u32(s.Ahi), 2048, 128), dA_lo = smem_desc(smem_u32(s.Alo), 2048, 128);
     const uint64_t dB_hi = smem_desc(smem_u32(s.Bhi), 512, 128), dB_lo = smem_desc(smem_u32(s.Blo), 512, 128);
     const int groups = (g.C + TILES - 1) / TILES;
     const int ntiles = g.B * groups;
-    float* vt = s.vec + warp * vec_per_tile(g.QP);  // L1 (NP) | v (NP) | s1 of two intervals (NP each)
+    float* vt = s.vec + warp * BVEC;  // l1 (NP) | v (NP) | s1 of two intervals (NP each)
     float* RQt = s.RQ + warp * 32 * RQS;
-    // the next interval's gradient row and s1, copied in (cp.async) while the current one runs:
-    // gb[0..N) level 1, gb[32 + 32 n + j] level 2 (idle stage space during the passes); s1 of interval
-    // t0_me + k in vt[2 NP + (k & 1) NP ..]
-    float* gb = s.stage + warp * tc_stage_stride(g.W);
-    auto fetch_grad = [&](int t, int k) {
-        const float* grow = p.grad_out + ((size_t)b_cur * g.T + t) * g.W;
-        if (lane < N) {
-#pragma unroll
-            for (int n = 0; n < 32; ++n)
-                if (n < N) cp_async4(gb + 32 + 32 * n + lane, grow + 1 + N + n * N + lane);
-            cp_async4(gb + lane, grow + 1 + lane);
-        }
-        fetch_loc(p, b_cur, t, vt + 2 * NP + (k & 1) * NP, NP);
-        cp_async_commit();
-    };
 
     for (;;) {
         if (tid == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
@@ -2004,9 +2054,7 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
         const int tile = s.bcast[0];
         __syncthreads();
         if (tile >= ntiles) break;
-        const int grp_r = tile / g.B, b = tile - grp_r * g.B;
-        b_cur = b;
-        const int grp = groups - 1 - grp_r;  // later groups first: the look-back reads later chunks
+        const int grp = tile / g.B, b = tile - grp * g.B;
         const int c_me = grp * TILES + warp;
         const bool valid_me = c_me < g.C;
         const int t0_me = c_me * g.Lc;
@@ -2016,260 +2064,148 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
             const int c = grp * TILES + t;
             if (c < g.C) steps = max(steps, min(g.Lc, g.T - c * g.Lc));
         }
+        const float* grows = p.grad_out + ((size_t)b * g.T + t0_me) * g.W;  // the chunk's gradient rows
+        auto fetch_s1 = [&](int k) { fetch_loc(p, b, t0_me + k, vt + 2 * NP + (k & 1) * NP, NP); };
         tc_load_tables(p, s, b, true);
         __syncthreads();
 
-        float col[32];  // column `lane` of l2
-        for (int pass = 0; pass < 2 && !failed; ++pass) {
-            if (pass == 0 && g.bwd_mode == 2) continue;  // the carries come from the backward scan
-            if (pass == 0) {
+        // zero carry: the chunk's local adjoint
+        float col[32];  // column `lane` of l~2
 #pragma unroll
-                for (int n = 0; n < 32; ++n) col[n] = 0.f;
-                vt[lane] = 0.f;
-            } else {
-                const float* cs = p.lcarry + ((size_t)b * g.C + (valid_me ? c_me : 0)) * g.SW;
+        for (int n = 0; n < 32; ++n) col[n] = 0.f;
+        vt[lane] = 0.f;
+        // Steps run in reverse; a chunk shorter than the tile's longest one (only the sequence's last, whose
+        // carry is zero) idles on zero state until its last interval, k = len_me - 1. The gradient of the
+        // interval a step starts from is added before it: here for the first step, else in the epilogue of
+        // the step before.
+        if (len_me == steps && len_me > 0) {
+            const float* gr = grows + (size_t)(len_me - 1) * g.W;
+            if (lane < N) {
 #pragma unroll
-                for (int n = 0; n < 32; ++n) col[n] = valid_me ? ldcg(cs + MM + NP + n * NP + lane) : 0.f;
-                vt[lane] = valid_me ? ldcg(cs + MM + lane) : 0.f;
+                for (int n = 0; n < 32; ++n)
+                    if (n < N) col[n] += __ldg(gr + 1 + N + n * N + lane);
+                vt[lane] += __ldg(gr + 1 + lane);
             }
-            __syncwarp();
-            // steps run in reverse; the chunk's last interval is len_me - 1 (shorter chunks idle on zero state)
-            if (len_me > 0) fetch_grad(t0_me + len_me - 1, len_me - 1);
-            for (int k = steps - 1; k >= 0; --k) {
-                const bool live = k < len_me;
-                const int t = t0_me + k;
-                // E0: l~ = l + g_t; the exact pass writes l~_t; rows of l~2 -> A operand
-                if (live) {
-                    cp_async_wait<0>();
-                    __syncwarp();
-                    if (lane < N) {
-#pragma unroll
-                        for (int n = 0; n < 32; ++n)
-                            if (n < N) col[n] += gb[32 + 32 * n + lane];
-                        vt[lane] += gb[lane];
-                    }
-                    __syncwarp();
-                    if (k >= 1) fetch_grad(t - 1, k - 1);
-                }
-                __syncwarp();
-                if (pass == 1 && live && lane < N) {
-                    float* row = p.lam + ((size_t)b * g.T + t) * g.W;
-                    if (lane == 0) row[0] = 0.f;
-                    row[1 + lane] = vt[lane];
-#pragma unroll
-                    for (int n = 0; n < 32; ++n)
-                        if (n < N) row[1 + N + n * N + lane] = col[n];
-                }
-                float srow[32];
-#pragma unroll
-                for (int n = 0; n < 32; ++n) RQt[n * RQS + lane] = col[n];
-                __syncwarp();
-#pragma unroll
-                for (int n = 0; n < 32; ++n) srow[n] = RQt[lane * RQS + n];
-                __syncwarp();
-                store_a_row(s.Ahi, s.Alo, 32 * warp + lane, srow);
-                fence_proxy_async();
-                fence_before();
-                __syncthreads();
-                if (tid == 0) {
-                    fence_after();
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
-                    mma_commit(s.bar);
-                }
-                // v = l~1 + l~2 s1_t (row `lane` of l~2 against this interval's s1; idle steps add nothing)
-                {
-                    const float* s1 = vt + 2 * NP + (k & 1) * NP;
-                    float w0 = 0.f, w1 = 0.f;
-#pragma unroll
-                    for (int n = 0; n < 32; n += 2) {
-                        w0 = fmaf(srow[n], s1[n], w0);
-                        w1 = fmaf(srow[n + 1], s1[n + 1], w1);
-                    }
-                    vt[NP + lane] = vt[lane] + (live ? w0 + w1 : 0.f);
-                    __syncwarp();
-                }
-                if (!tc_wait(s, phase, mbar_limit)) {
-                    failed = mma_pending = true;
-                    break;
-                }
-                phase ^= 1;
-                // E1: row `lane` of X = l~2 - l~2 D = l~2 M -> column `lane` -> A operand row of X^T
-                float xcol[32];
-                {
-                    float pr[32];
-                    tmem_ld32(tP1 + lane_off, pr);
-#pragma unroll
-                    for (int n = 0; n < 32; ++n) RQt[lane * RQS + n] = srow[n] - pr[n];
-                    __syncwarp();
-#pragma unroll
-                    for (int n = 0; n < 32; ++n) xcol[n] = RQt[n * RQS + lane];
-                    __syncwarp();
-                    store_a_row(s.Ahi, s.Alo, 32 * warp + lane, xcol);
-                }
-                fence_proxy_async();
-                fence_before();
-                __syncthreads();
-                if (tid == 0) {
-                    fence_after();
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
-                    mma_commit(s.bar);
-                }
-                // l1 <- M^T v = v - D^T v while the tensor core runs
-                {
-                    const float* v = vt + NP;
-                    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-#pragma unroll
-                    for (int kk = 0; kk < NP; kk += 4) {
-                        d0 = fmaf(s.Dr[kk * NP + lane], v[kk], d0);
-                        d1 = fmaf(s.Dr[(kk + 1) * NP + lane], v[kk + 1], d1);
-                        d2 = fmaf(s.Dr[(kk + 2) * NP + lane], v[kk + 2], d2);
-                        d3 = fmaf(s.Dr[(kk + 3) * NP + lane], v[kk + 3], d3);
-                    }
-                    const float nv = v[lane] - ((d0 + d1) + (d2 + d3));
-                    __syncwarp();
-                    vt[lane] = nv;
-                    __syncwarp();
-                }
-                if (!tc_wait(s, phase, mbar_limit)) {
-                    failed = mma_pending = true;
-                    break;
-                }
-                phase ^= 1;
-                // E2: column `lane` of M^T X = X - D^T X
-                {
-                    float q2[32];
-                    tmem_ld32(tP2 + lane_off, q2);
-#pragma unroll
-                    for (int n = 0; n < 32; ++n) col[n] = xcol[n] - q2[n];
-                    fence_before();
-                    __syncwarp();
-                }
-            }
-            if (failed) break;
-            __syncthreads();
-            if (pass == 1) break;
-            // ---- local adjoints mu of the 4 chunks -> adjoint slots (the sequence's last chunk: inclusive)
-            if (valid_me) {
-                float* as = (c_me == g.C - 1 && g.bwd_mode == 0 ? p.incl : p.agg) + ((size_t)b * g.C + c_me) * g.SW;
-#pragma unroll
-                for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = col[n];
-                as[MM + lane] = vt[lane];
-            }
-            __syncthreads();
-            if (g.bwd_mode == 1) break;  // the backward scan combines the local adjoints
-            for (int t = 0; t < TILES; ++t) {
-                const int c = grp * TILES + t;
-                if (c >= g.C) break;
-                if (c == g.C - 1) {
-                    if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(p.flags + (size_t)b * g.C + c, kFlagIncl);
-                } else {
-                    cta_publish(p.flags + (size_t)b * g.C + c, kFlagAgg);
-                }
-                __syncthreads();
-            }
-            // ---- look-back from the group's last chunk over the later chunks
-            float* W0 = s.Ahi;            // G_j (C)
-            float* W1 = s.Ahi + MM;       // X (l2 row-major)
-            float* W2 = s.Ahi + 2 * MM;   // G_j (S2)
-            float* W3 = s.Ahi + 3 * MM;   // lam (l2 row-major)
-            float* W4 = s.Alo;            // Gacc (C)
-            float* W5 = s.Alo + MM;       // Gacc (S2)
-            float* ve = s.misc;           // lam l1
-            float* va = s.misc + NP;      // Gacc S1
-            float* vx = s.misc + 2 * NP;  // X l1
-            float* vg = s.misc + 3 * NP;  // G_j S1
-            float* v1 = s.misc + 4 * NP;  // scratch
-            float* v2 = s.misc + 5 * NP;  // scratch
-            float* v3 = s.misc + 6 * NP;  // scratch
-            float* T0 = s.stage;
-            float* T1 = s.stage + MM;
-            for (int e = tid; e < MM; e += blockDim.x) W3[e] = 0.f;
-            if (tid < NP) ve[tid] = 0.f;
-            __syncthreads();
-            const int c_last = min(grp * TILES + TILES - 1, g.C - 1);
-            if (c_last < g.C - 1) {
-                identity_smem(W4, va, W5);
-                __syncthreads();
-                int j = c_last + 1;
-                for (;;) {
-                    const int f = tc_cta_wait(p, s, p.flags + (size_t)b * g.C + j, deterministic ? kFlagIncl : kFlagAgg, tile);
-                    if (f < 0) {
-                        failed = true;
-                        break;
-                    }
-                    const size_t sj = ((size_t)b * g.C + j) * g.SW;
-                    {
-                        const float* src = (f == kFlagIncl ? p.incl : p.agg) + sj;
-                        for (int e = tid; e < MM; e += blockDim.x) W1[e] = ldcg(src + MM + NP + e);
-                        if (tid < NP) vx[tid] = ldcg(src + MM + tid);
-                    }
-                    __syncthreads();
-                    float X2[4][4];
-                    load_rowmajor(W1, X2, i0, j0);
-                    __syncthreads();
-                    apply_JT_smem(W4, va, vx, X2, W1, T0, v1, v2, i0, j0);  // X <- J(Gacc)^T X
-                    for (int e = tid; e < MM; e += blockDim.x) W3[e] += W1[e];
-                    if (tid < NP) ve[tid] += vx[tid];
-                    __syncthreads();
-                    if (f == kFlagIncl) break;
-                    load_slot_smem(p.fagg + sj, W0, vg, W2);
-                    __syncthreads();
-                    chen_mul_smem(W4, va, W5, W0, vg, W2, W4, va, W5, T0, T1, v3, i0, j0);  // Gacc <- Gacc (x) G_j
-                    ++j;
-                }
-                if (failed) break;
-            }
-            // ---- the group's chunks, last to first: lam_in(c) -> carry slot; incl(c) = J(G_c)^T lam + mu_c
-            for (int t = TILES - 1; t >= 0; --t) {
-                const int c = grp * TILES + t;
-                if (c >= g.C) continue;
-                const size_t sc = ((size_t)b * g.C + c) * g.SW;
-                for (int e = tid; e < MM; e += blockDim.x) p.lcarry[sc + MM + NP + e] = W3[e];
-                if (tid < NP) p.lcarry[sc + MM + tid] = ve[tid];
-                if (c == g.C - 1) {
-                    // nothing arrives after the last chunk: incl = mu (already published)
-                    const float* mu = p.incl + sc;
-                    for (int e = tid; e < MM; e += blockDim.x) W3[e] = ldcg(mu + MM + NP + e);
-                    if (tid < NP) ve[tid] = ldcg(mu + MM + tid);
-                    __syncthreads();
-                    continue;
-                }
-                load_slot_smem(p.fagg + sc, W0, vg, W2);
-                __syncthreads();
-                float X2[4][4];
-                load_rowmajor(W3, X2, i0, j0);
-                __syncthreads();
-                apply_JT_smem(W0, vg, ve, X2, W3, T0, v1, v2, i0, j0);  // lam <- J(G_c)^T lam
-                {
-                    const float* mu = p.agg + sc;
-                    for (int e = tid; e < MM; e += blockDim.x) W3[e] += ldcg(mu + MM + NP + e);
-                    if (tid < NP) ve[tid] += ldcg(mu + MM + tid);
-                }
-                __syncthreads();
-                {
-                    float* is = p.incl + sc;
-                    for (int e = tid; e < MM; e += blockDim.x) is[MM + NP + e] = W3[e];
-                    if (tid < NP) is[MM + tid] = ve[tid];
-                }
-                __syncthreads();
-                // failure-detection test: no inclusive value reaches the earlier chunks, whose waits then run out
-                if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(p.flags + (size_t)b * g.C + c, kFlagIncl);
-                __syncthreads();
-            }
-            __syncthreads();
+            fetch_s1(len_me - 1);
+            if (len_me >= 2) prefetch_row_l2(gr - g.W, g.W);
         }
+        cp_async_commit();
+        __syncwarp();
+        for (int k = steps - 1; k >= 0; --k) {
+            const bool live = k < len_me;
+            const bool next = k >= 1 && k - 1 < len_me;  // the step after this one is live
+            cp_async_wait<0>();
+            __syncwarp();
+            if (next) fetch_s1(k - 1);
+            cp_async_commit();
+            if (k >= 2 && k - 2 < len_me) prefetch_row_l2(grows + (size_t)(k - 2) * g.W, g.W);
+            // E0: rows of l~2 -> A operand
+            float srow[32];
+#pragma unroll
+            for (int n = 0; n < 32; ++n) RQt[n * RQS + lane] = col[n];
+            __syncwarp();
+#pragma unroll
+            for (int n = 0; n < 32; ++n) srow[n] = RQt[lane * RQS + n];
+            __syncwarp();
+            store_a_row(s.Ahi, s.Alo, 32 * warp + lane, srow);
+            fence_proxy_async();
+            fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                fence_after();
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
+                mma_commit(s.bar);
+            }
+            // v = l~1 + l~2 s1_t (row `lane` of l~2 against this interval's s1; idle steps add nothing)
+            {
+                const float w = dot32_bc(srow, vt + 2 * NP + (k & 1) * NP);
+                vt[NP + lane] = vt[lane] + (live ? w : 0.f);
+                __syncwarp();
+            }
+            if (!tc_wait(s, phase, mbar_limit)) {
+                failed = mma_pending = true;
+                break;
+            }
+            phase ^= 1;
+            // E1: row `lane` of X = l~2 - l~2 D = l~2 M -> column `lane` -> A operand row of X^T
+            float xcol[32];
+            {
+                float pr[32];
+                tmem_ld32(tP1 + lane_off, pr);
+#pragma unroll
+                for (int n = 0; n < 32; ++n) RQt[lane * RQS + n] = srow[n] - pr[n];
+                __syncwarp();
+#pragma unroll
+                for (int n = 0; n < 32; ++n) xcol[n] = RQt[n * RQS + lane];
+                __syncwarp();
+                store_a_row(s.Ahi, s.Alo, 32 * warp + lane, xcol);
+            }
+            fence_proxy_async();
+            fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                fence_after();
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
+                mma_commit(s.bar);
+            }
+            // the next interval's gradient, loaded while the tensor core runs
+            float gn[32];
+            float gn1 = 0.f;
+            {
+                const float* gr = grows + (size_t)(k - 1) * g.W;
+                const bool ld = next && lane < N;
+#pragma unroll
+                for (int n = 0; n < 32; ++n) gn[n] = (ld && n < N) ? __ldg(gr + 1 + N + n * N + lane) : 0.f;
+                if (ld) gn1 = __ldg(gr + 1 + lane);
+            }
+            // l1 <- M^T v + g1 = v - D^T v + g1
+            {
+                const float* v = vt + NP;
+                const float nv = v[lane] - coldot_bc(s.Dr, v, lane);
+                __syncwarp();
+                vt[lane] = nv + gn1;
+                __syncwarp();
+            }
+#pragma unroll
+            for (int n = 0; n < 32; ++n) xcol[n] += gn[n];  // X + g2 (X - D^T X + g2 below)
+            if (!tc_wait(s, phase, mbar_limit)) {
+                failed = mma_pending = true;
+                break;
+            }
+            phase ^= 1;
+            // E2: column `lane` of M^T X = X - D^T X, plus the next interval's gradient
+            {
+                float q2[32];
+                tmem_ld32(tP2 + lane_off, q2);
+#pragma unroll
+                for (int n = 0; n < 32; ++n) col[n] = xcol[n] - q2[n];
+                fence_before();
+                __syncwarp();
+            }
+        }
+        cp_async_wait<0>();
         if (failed) break;
+        __syncthreads();
+        // the local adjoints mu of the 4 chunks -> `agg` (the backward scan combines them)
+        if (valid_me) {
+            float* as = p.agg + ((size_t)b * g.C + c_me) * g.SW;
+#pragma unroll
+            for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = col[n];
+            as[MM + lane] = vt[lane];
+        }
+        __syncthreads();
     }
+    // every exit drains the tensor core and frees TMEM
     if (failed && tid == 0) {
         if (atomicCAS(&p.st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) p.st->err_tile = -1;
         if (mma_pending)
@@ -2282,262 +2218,378 @@ __global__ void __launch_bounds__(tc::NTH) bwd_tc_kernel(Params p) {
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64));
 }
 
-// The gradients as a parallel map over (sample, interval), from the cotangent stream l~_t and the forward
-// states S_{t-1} (prefix output row t-1): with u = M S1p, X = S2p M^T, Z = M^T l~2,
-//   dM += l~2 X^T + Z^T S2p + du S1p^T,   du = l~1 + l~2 s1,   ds1 = l~1 + l~2^T u,
-//   dU_a = l~2 V_a,  dV_a = l~2^T U_a,    dF += ds1 dx^T,  dG_a += dU_a dx^T,  dH_a += dV_a dx^T,
-//   dx_t = F^T ds1 + sum_a G_a^T dU_a + H_a^T dV_a.
-// One CTA of four warps per (chunk, sample), one warp per interval: the CTA's four warps take the chunk's intervals round robin and
-// lane (rb, cb) = (lane / 8, lane % 8) owns the 8 x 4 block at rows 8 rb, columns 4 cb of each 32 x 32 x 32
-// product, reading two float4s of A and one of B per k (32 FMAs per three shared loads). Each warp keeps its
-// own dM block in registers over its intervals (summed in warp order at the end) and writes the interval's
-// vector cotangents [ds1 | dU_a | dV_a] to a stream, from which table_grad_kernel forms the table gradients
-// and dx as small GEMMs per chunk.
-namespace gm {
-constexpr int NW = 4;  // warps per CTA
-constexpr int TB = 8;  // intervals per block of table_grad_kernel
+// The exact pass of the adjoint chain with the gradient map fused in (bwd_mode 2). Per step, besides the
+// chain's products P = l~2 M (row `lane` in TMEM after the first product) and M^T X, a third product gives
+// Z^T = l~2^T M (A operand = the columns of l~2, same B). With S = S2_{t-1} and S1p = S1_{t-1} (prefix row
+// t - 1, staged per warp) the interval contributes
+//     dM += P S^T + Z^T S + du S1p^T,   du = l~1 + l~2 s1,   ds1 = l~1 + Z^T S1p  (= l~1 + l~2^T M S1p),
+//     dU_a = l~2 V_a,   dV_a = l~2^T U_a,
+// the same terms as the reverse of ews/core/chen_scan.py:124-152 with the series leaf's local terms. Lane l
+// owns row l of dM for its chunk (registers, 32 floats); the S blocks are read as broadcast 4 x 4 tiles,
+// each tile serving both the P S^T and the Z^T S terms. The vector cotangents [ds1 | dU_a | dV_a] go to
+// `coef` for table_grad_kernel, dM to the chunk's partial slot; no cotangent stream is written.
+//
+// Shared memory: B (D, transposed orientation), the A operands of l~2 (rows) and of l~2^T (rows = columns
+// of l~2), D row-major and per warp l1 | v | the interval's local terms | the staged prefix row. The row /
+// column exchanges of the epilogues use the l~2^T operand's space, free at those points (101 KB, two CTAs
+// per SM).
+namespace tc {
+constexpr int XSTG = 1064;  // staged prefix row: S1 at +4, S2 (stride NP) at +36
 
-// 32 x 32 buffers with float4 groups permuted per row: element (r, c) at r * 32 + 4 (c / 4 ^ s(r)) + c % 4,
-// s = 0 (MODE 0), r % 8 (MODE 1: transposed scalar stores, 4-way), r / 4 % 8 (MODE 2: the float4 stores of
-// a transposed 8 x 4 block, conflict-free per quarter warp).
-template <int MODE>
-__device__ __forceinline__ int at(int r, int c) {
-    if (MODE == 0) return r * NP + c;
-    const int s = MODE == 1 ? (r & 7) : ((r >> 2) & 7);
-    return r * NP + ((((c >> 2) ^ s) << 2) | (c & 3));
+__host__ __device__ inline int xvec_floats(int QP) { return 2 * NP + loc_width(QP) + XSTG; }
+
+__host__ __device__ inline size_t tc_exact_smem_bytes(int QP) {
+    const size_t f = 2 * MM + 4 * 4 * MM + MM + TILES * (size_t)xvec_floats(QP);
+    return f * sizeof(float) + 64 + 128;
 }
 
-// acc (+)= A B on the lane's 8 x 4 block; A given k-major (A[i][k] at a[at<MA>(k, i)]), B row-major.
-template <int MA, int MB>
-__device__ __forceinline__ void gemm84(const float* __restrict__ a, const float* __restrict__ b, float acc[8][4],
-                                       int rb, int cb) {
-#pragma unroll 8
-    for (int k = 0; k < NP; ++k) {
-        const float4 a0 = *reinterpret_cast<const float4*>(a + at<MA>(k, 8 * rb));
-        const float4 a1 = *reinterpret_cast<const float4*>(a + at<MA>(k, 8 * rb + 4));
-        const float4 bv = *reinterpret_cast<const float4*>(b + at<MB>(k, 4 * cb));
-        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const float bw[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(av[r], bw[c], acc[r][c]);
+struct XSmem {
+    float *Bhi, *Blo, *A1hi, *A1lo, *A3hi, *A3lo, *Dr, *vec;
+    uint64_t* bar;
+    uint32_t* tmem;
+    int* bcast;
+};
+
+__device__ XSmem tc_carve_exact(unsigned char* raw, int QP) {
+    uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 127) & ~(uintptr_t)127;
+    float* p = reinterpret_cast<float*>(base);
+    XSmem s;
+    s.Bhi = p; p += MM;
+    s.Blo = p; p += MM;
+    s.A1hi = p; p += 4 * MM;
+    s.A1lo = p; p += 4 * MM;
+    s.A3hi = p; p += 4 * MM;
+    s.A3lo = p; p += 4 * MM;
+    s.Dr = p; p += MM;
+    s.vec = p; p += TILES * xvec_floats(QP);
+    s.bar = reinterpret_cast<uint64_t*>(p);
+    s.tmem = reinterpret_cast<uint32_t*>(p + 2);
+    s.bcast = reinterpret_cast<int*>(p + 4);
+    return s;
+}
+
+// CTA-uniform bounded wait for the MMA commit of the given parity (the exact pass's smem view).
+__device__ bool tc_wait_x(const XSmem& s, uint32_t parity, int limit) {
+    if (threadIdx.x == 0) {
+        int ok = 0;
+        for (int it = 0; it < limit; ++it) {
+            if (mbar_try(s.bar, parity)) {
+                ok = 1;
+                break;
+            }
+        }
+        s.bcast[1] = ok;
     }
+    __syncthreads();
+    const bool ok = s.bcast[1] != 0;
+    fence_after();
+    return ok;
 }
 
-__host__ __device__ inline int warp_floats(int QP) { return 4 * MM + 4 * NP + 2 * loc_width(QP); }
-inline size_t map_smem_bytes(const Geom& g) { return sizeof(float) * (2 * (size_t)MM + NW * (size_t)warp_floats(g.QP)); }
+// The three 3xTF32 K-loops of one product (hi hi, hi lo, lo hi) into the TMEM columns at `d`.
+__device__ __forceinline__ void mma3x(uint32_t d, uint64_t a_hi, uint64_t a_lo, uint64_t b_hi, uint64_t b_lo) {
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) mma_tf32(d, a_hi + (ks * 4096 >> 4), b_hi + (ks * 1024 >> 4), ks > 0);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) mma_tf32(d, a_hi + (ks * 4096 >> 4), b_lo + (ks * 1024 >> 4), 1);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) mma_tf32(d, a_lo + (ks * 4096 >> 4), b_hi + (ks * 1024 >> 4), 1);
+}
+}  // namespace tc
+
+template <bool FULL>
+__global__ void __launch_bounds__(tc::NTH, 2) bwd_exact_kernel(Params p) {
+    using namespace tc;
+    extern __shared__ unsigned char smem_raw[];
+    const Geom& g = p.g;
+    const int QP = g.QP, LW = loc_width(QP);
+    XSmem s = tc_carve_exact(smem_raw, QP);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int N = FULL ? NP : g.N;
+    const int mbar_limit = 1 << 20;
+
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(s.bar)), "r"(1));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s.tmem)),
+                     "r"(128));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *s.tmem;
+    const uint32_t tP1 = tmem, tP2 = tmem + 32, tP3 = tmem + 64;
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    uint32_t phase = 0;
+    bool failed = false;
+    bool mma_pending = false;  // an MMA commit of `phase` may still be outstanding after a failed wait
+
+    const uint64_t dA1_hi = smem_desc(smem_u32(s.A1hi), 2048, 128), dA1_lo = smem_desc(smem_u32(s.A1lo), 2048, 128);
+    const uint64_t dA3_hi = smem_desc(smem_u32(s.A3hi), 2048, 128), dA3_lo = smem_desc(smem_u32(s.A3lo), 2048, 128);
+    const uint64_t dB_hi = smem_desc(smem_u32(s.Bhi), 512, 128), dB_lo = smem_desc(smem_u32(s.Blo), 512, 128);
+    const int groups = (g.C + TILES - 1) / TILES;
+    const int ntiles = g.B * groups;
+    float* vt = s.vec + warp * xvec_floats(QP);  // l1 (NP) | v (NP) | local terms (LW) | staged prefix row
+    float* lb = vt + 2 * NP;                      // [s1 | U_a | V_a] of the current interval
+    float* stg = lb + LW;                         // S1p at +4, S2p row-major (stride NP) at +36
+    float* RQt = s.A3hi + warp * 32 * RQS;        // exchange buffer, inside the l~2^T operand's space
+
+    // The warp's copy of prefix row t - 1 (the state the interval starts from) into the staging rows.
+    auto stage_prev = [&](int b, int t) {
+        const float* row = p.out + ((size_t)b * g.T + t - 1) * g.W;
+        if (FULL) {
+            for (int e = lane; e < g.W; e += 32) cp_async4(stg + 3 + e, row + e);
+        } else {
+            stg[4 + lane] = lane < N ? __ldg(row + 1 + lane) : 0.f;
+#pragma unroll 4
+            for (int i = 0; i < NP; ++i)
+                stg[36 + i * NP + lane] = (i < N && lane < N) ? __ldg(row + 1 + N + i * N + lane) : 0.f;
+        }
+    };
+
+    for (;;) {
+        if (tid == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
+        __syncthreads();
+        const int tile = s.bcast[0];
+        __syncthreads();
+        if (tile >= ntiles) break;
+        const int grp = tile / g.B, b = tile - grp * g.B;
+        const int c_me = grp * TILES + warp;
+        const bool valid_me = c_me < g.C;
+        const int t0_me = c_me * g.Lc;
+        const int len_me = valid_me ? min(g.Lc, g.T - t0_me) : 0;
+        int steps = 0;
+        for (int t = 0; t < TILES; ++t) {
+            const int c = grp * TILES + t;
+            if (c < g.C) steps = max(steps, min(g.Lc, g.T - c * g.Lc));
+        }
+        const float* grows = p.grad_out + ((size_t)b * g.T + t0_me) * g.W;  // the chunk's gradient rows
+        {
+            const float* m = p.tab_d + (size_t)b * N * N;
+            for (int e = tid; e < MM; e += blockDim.x) {
+                const int i = e / NP, k = e - i * NP;
+                const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
+                s.Dr[i * NP + k] = v;
+                const float hi = __uint_as_float(tf32_bits(v));
+                s.Bhi[bk_off(k, i)] = hi;
+                s.Blo[bk_off(k, i)] = v - hi;
+            }
+        }
+        __syncthreads();
+
+        float dM[32];  // row `lane` of the chunk's dM
+#pragma unroll
+        for (int j = 0; j < 32; ++j) dM[j] = 0.f;
+        float col[32];  // column `lane` of l~2
+        {
+            const float* cs = p.lcarry + ((size_t)b * g.C + (valid_me ? c_me : 0)) * g.SW;
+#pragma unroll
+            for (int n = 0; n < 32; ++n) col[n] = valid_me ? ldcg(cs + MM + NP + n * NP + lane) : 0.f;
+            vt[lane] = valid_me ? ldcg(cs + MM + lane) : 0.f;
+        }
+        // Steps run in reverse; a chunk shorter than the tile's longest one (only the sequence's last, whose
+        // carry is zero) idles on zero state until its last interval. The gradient, local terms and prefix
+        // row of the interval a step starts from are fetched one step ahead (here for the first step).
+        // cp.async groups per step: the local terms (waited for at the step's start), then the prefix row
+        // (waited for before the dM update).
+        if (len_me == steps && len_me > 0) {
+            const float* gr = grows + (size_t)(len_me - 1) * g.W;
+            if (lane < N) {
+#pragma unroll
+                for (int n = 0; n < 32; ++n)
+                    if (n < N) col[n] += __ldg(gr + 1 + N + n * N + lane);
+                vt[lane] += __ldg(gr + 1 + lane);
+            }
+            fetch_loc(p, b, t0_me + len_me - 1, lb, LW);
+            cp_async_commit();
+            if (t0_me + len_me - 1 > 0) stage_prev(b, t0_me + len_me - 1);
+            cp_async_commit();
+        } else {
+            cp_async_commit();
+            cp_async_commit();
+        }
+        __syncwarp();
+        for (int k = steps - 1; k >= 0; --k) {
+            const bool live = k < len_me;
+            const bool next = k >= 1 && k - 1 < len_me;  // the step after this one is live
+            const int t = t0_me + k;
+            cp_async_wait<1>();
+            __syncwarp();
+            if (k >= 2 && k - 2 < len_me) {
+                prefetch_row_l2(grows + (size_t)(k - 2) * g.W, g.W);
+                if (t >= 3) prefetch_row_l2(p.out + ((size_t)b * g.T + t - 3) * g.W, g.W);
+            }
+            // E0: rows of l~2 (through the exchange buffer) -> A1; columns of l~2 -> A3
+            float srow[32];
+#pragma unroll
+            for (int n = 0; n < 32; ++n) RQt[n * RQS + lane] = col[n];
+            __syncwarp();
+#pragma unroll
+            for (int n = 0; n < 32; ++n) srow[n] = RQt[lane * RQS + n];
+            __syncthreads();  // every warp's exchange is read before A3 is written over it
+            store_a_row(s.A1hi, s.A1lo, 32 * warp + lane, srow);
+            store_a_row(s.A3hi, s.A3lo, 32 * warp + lane, col);
+            fence_proxy_async();
+            fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                fence_after();
+                mma3x(tP1, dA1_hi, dA1_lo, dB_hi, dB_lo);  // l~2 D (rows)
+                mma3x(tP3, dA3_hi, dA3_lo, dB_hi, dB_lo);  // l~2^T D (rows)
+                mma_commit(s.bar);
+            }
+            // vectors while the tensor core runs: du = v = l~1 + l~2 s1; dU_a = l~2 V_a; dV_a = l~2^T U_a
+            const float l1t = vt[lane];
+            float du = l1t;
+            if (live) {
+                du += dot32_bc(srow, lb);
+                float* co = p.coef + ((size_t)b * g.T + t) * LW;
+                for (int a = 0; a < QP; ++a) {
+                    co[(1 + a) * NP + lane] = dot32_bc(srow, lb + NP + (QP + a) * NP);  // dU_a = l~2 V_a
+                    co[(1 + QP + a) * NP + lane] = dot32_bc(col, lb + NP + a * NP);   // dV_a = l~2^T U_a
+                }
+            }
+            vt[NP + lane] = du;
+            __syncwarp();
+            // the next interval's local terms (this one's are consumed)
+            if (next) fetch_loc(p, b, t - 1, lb, LW);
+            cp_async_commit();
+            if (!tc_wait_x(s, phase, mbar_limit)) {
+                failed = mma_pending = true;
+                break;
+            }
+            phase ^= 1;
+            // E1: P = l~2 M (row `lane`), Z^T = l~2^T M (row `lane`); X^T rows -> A1
+            float P[32], Zt[32];
+            {
+                float r[32], xcol[32];
+                tmem_ld32(tP1 + lane_off, r);
+#pragma unroll
+                for (int n = 0; n < 32; ++n) P[n] = srow[n] - r[n];
+                tmem_ld32(tP3 + lane_off, r);
+#pragma unroll
+                for (int n = 0; n < 32; ++n) Zt[n] = col[n] - r[n];
+#pragma unroll
+                for (int n = 0; n < 32; ++n) RQt[lane * RQS + n] = P[n];
+                __syncwarp();
+#pragma unroll
+                for (int n = 0; n < 32; ++n) xcol[n] = RQt[n * RQS + lane];
+                store_a_row(s.A1hi, s.A1lo, 32 * warp + lane, xcol);
+            }
+            fence_proxy_async();
+            fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                fence_after();
+                mma3x(tP2, dA1_hi, dA1_lo, dB_hi, dB_lo);  // X^T D (rows) = columns of D^T X
+                mma_commit(s.bar);
+            }
+            // the next interval's gradient, loaded while the tensor core runs
+            float gn[32];
+            float gn1 = 0.f;
+            {
+                const float* gr = grows + (size_t)(k - 1) * g.W;
+                const bool ld = next && lane < N;
+#pragma unroll
+                for (int n = 0; n < 32; ++n) gn[n] = (ld && n < N) ? __ldg(gr + 1 + N + n * N + lane) : 0.f;
+                if (ld) gn1 = __ldg(gr + 1 + lane);
+            }
+            // l1 <- M^T v + g1 = v - D^T v + g1
+            {
+                const float* v = vt + NP;
+                const float nv = v[lane] - coldot_bc(s.Dr, v, lane);
+                __syncwarp();
+                vt[lane] = nv + gn1;
+            }
+            // the gradient of the interval: ds1 and dM (the prefix row t - 1 is needed from here on)
+            cp_async_wait<1>();
+            __syncwarp();
+            if (live) {
+                float* co = p.coef + ((size_t)b * g.T + t) * LW;
+                if (t > 0) {
+                    const float* S1p = stg + 4;
+                    const float* S2p = stg + 36;
+                    co[lane] = l1t + dot32_bc(Zt, S1p);
+                    axpy32_bc(dM, S1p, du);
+#pragma unroll
+                    for (int jb = 0; jb < 8; ++jb) {
+#pragma unroll
+                        for (int kb = 0; kb < 8; ++kb) {
+                            float sv[4][4];
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) {
+                                const float4 q = *reinterpret_cast<const float4*>(S2p + (4 * jb + r) * NP + 4 * kb);
+                                sv[r][0] = q.x;
+                                sv[r][1] = q.y;
+                                sv[r][2] = q.z;
+                                sv[r][3] = q.w;
+                            }
+#pragma unroll
+                            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                                for (int c = 0; c < 4; ++c) {
+                                    dM[4 * jb + r] = fmaf(P[4 * kb + c], sv[r][c], dM[4 * jb + r]);  // P S^T
+                                    dM[4 * kb + c] = fmaf(Zt[4 * jb + r], sv[r][c], dM[4 * kb + c]);  // Z^T S
+                                }
+                        }
+                    }
+                } else {
+                    co[lane] = l1t;  // the first interval starts from the zero state
+                }
+            }
+            __syncwarp();
+            if (next && t - 1 > 0) stage_prev(b, t - 1);
+            cp_async_commit();
+            if (!tc_wait_x(s, phase, mbar_limit)) {
+                failed = mma_pending = true;
+                break;
+            }
+            phase ^= 1;
+            // E2: column `lane` of M^T X = X - D^T X (X's column re-read from the exchange buffer), plus the
+            // next interval's gradient
+            {
+                float q2[32];
+                tmem_ld32(tP2 + lane_off, q2);
+#pragma unroll
+                for (int n = 0; n < 32; ++n) col[n] = (RQt[n * RQS + lane] + gn[n]) - q2[n];
+                fence_before();
+                __syncwarp();
+            }
+        }
+        cp_async_wait<0>();
+        if (failed) break;
+        // the chunk's dM row -> its partial slot (chunk-major, the reduction's order)
+        if (valid_me) {
+            float* part = p.partials + (size_t)(c_me * g.B + b) * (MM + (size_t)LW * g.d_in) + lane * NP;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(part + j) = make_float4(dM[j], dM[j + 1], dM[j + 2], dM[j + 3]);
+        }
+        __syncthreads();
+    }
+    // every exit drains the tensor core and frees TMEM
+    if (failed && tid == 0) {
+        if (atomicCAS(&p.st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) p.st->err_tile = -1;
+        if (mma_pending)
+            for (int it = 0; it < (1 << 20); ++it)
+                if (mbar_try(s.bar, phase)) break;
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128));
+}
+
+namespace gm {
+constexpr int TB = 8;  // intervals per block of table_grad_kernel
 __host__ __device__ inline int coef_stride(int QP) { return loc_width(QP) + 4; }  // padded row of a staged coefficient block
 inline size_t table_smem_bytes(const Geom& g) {
     const size_t rows = (size_t)loc_width(g.QP);
     return sizeof(float) * (2 * align4((int)(rows * g.d_in)) + TB * (size_t)coef_stride(g.QP) + align4(TB * g.d_in));
 }
 }  // namespace gm
-
-template <bool FULL>
-__global__ void __launch_bounds__(gm::NW * 32, 2) grad_map_kernel(Params p) {
-    using namespace gm;
-    extern __shared__ __align__(16) float smem[];
-    const Geom& g = p.g;
-    const int N = FULL ? NP : g.N;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int rb = lane >> 3, cb = lane & 7;
-    const int QP = g.QP, LW = loc_width(QP);
-    float* Dr = smem;     // D row-major
-    float* Dt = Dr + MM;  // D k-major (Dt[k][j] = D[j][k])
-    float* Sr = Dt + MM + warp * warp_floats(QP);  // S2p row-major
-    float* Sk = Sr + MM;  // S2p k-major (MODE 1); then X^T (MODE 2)
-    float* Lr = Sk + MM;  // l~2 row-major; then Z row-major
-    float* Lk = Lr + MM;  // l~2 k-major (MODE 1)
-    float* S1v = Lk + MM;
-    float* L1v = S1v + NP;
-    float* uv = L1v + NP;
-    float* duv = uv + NP;
-    float* locb = duv + NP;  // two intervals' [s1 | U_a | V_a]
-
-    const int tile = blockIdx.x;  // c * B + b, the reduction's order
-    const int c = tile / g.B, b = tile - c * g.B;
-    const int t0 = c * g.Lc;
-    const int len = min(g.Lc, g.T - t0);
-    {
-        const float* m = p.tab_d + (size_t)b * N * N;
-        for (int e = tid; e < MM; e += blockDim.x) {
-            const int i = e >> 5, k = e & 31;
-            const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
-            Dr[e] = v;
-            Dt[k * NP + i] = v;
-        }
-    }
-    __syncthreads();
-    float dM[8][4];
-#pragma unroll
-    for (int r = 0; r < 8; ++r)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) dM[r][q] = 0.f;
-    // the warp's next interval, in flight while this one runs: lane j holds column j of S_{t-1} and of
-    // l~2_t, entry j of S1_{t-1} and of l~1_t; its local terms are copied in with cp.async
-    float ps[NP], pl[NP], ps1 = 0.f, pl1 = 0.f;
-    auto prefetch = [&](int t) {
-        const float* lrow = p.lam + ((size_t)b * g.T + t) * g.W;
-        const bool has_s = t > 0;
-        const float* srow = has_s ? p.out + ((size_t)b * g.T + t - 1) * g.W : lrow;
-        const bool okj = lane < N;
-#pragma unroll
-        for (int i = 0; i < NP; ++i) {
-            const bool ok = okj && i < N;
-            pl[i] = ok ? ldcg(lrow + 1 + N + i * N + lane) : 0.f;
-            ps[i] = (ok && has_s) ? ldcg(srow + 1 + N + i * N + lane) : 0.f;
-        }
-        pl1 = okj ? ldcg(lrow + 1 + lane) : 0.f;
-        ps1 = (okj && has_s) ? ldcg(srow + 1 + lane) : 0.f;
-        const float* lsrc = p.loc + ((size_t)b * g.T + t) * LW;
-        float* ldst = locb + (((t - t0) >> 2) & 1) * LW;
-        for (int v = lane; v < LW / 4; v += 32) cp_async16(ldst + 4 * v, lsrc + 4 * v);
-    };
-    if (warp < len) prefetch(t0 + warp);
-    cp_async_commit();
-    for (int k = warp; k < len; k += NW) {
-        const int t = t0 + k;
-        __syncwarp();
-        // (1) the interval's rows into the warp's buffers; the warp's next interval goes out
-#pragma unroll
-        for (int i = 0; i < NP; ++i) {
-            Sr[at<0>(i, lane)] = ps[i];
-            Sk[at<1>(lane, i)] = ps[i];
-            Lr[at<0>(i, lane)] = pl[i];
-            Lk[at<1>(lane, i)] = pl[i];
-        }
-        S1v[lane] = ps1;
-        L1v[lane] = pl1;
-        if (k + NW < len) prefetch(t + NW);
-        cp_async_commit();
-        cp_async_wait<1>();
-        __syncwarp();
-        const float* s1 = locb + ((k >> 2) & 1) * LW;  // s1, U_a = s1 + NP + a NP, V_a = U_a + QP NP
-        const float* U = s1 + NP;
-        const float* V = U + QP * NP;
-        float* co = p.coef + ((size_t)b * g.T + t) * LW;
-        // (2) vectors: u = M S1p, du = l~1 + l~2 s1, dU_a = l~2 V_a (row `lane` of l~2)
-        {
-            float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-            for (int kk = 0; kk < NP; kk += 2) {
-                a0 = fmaf(Dt[kk * NP + lane], S1v[kk], a0);
-                a1 = fmaf(Dt[(kk + 1) * NP + lane], S1v[kk + 1], a1);
-            }
-            uv[lane] = S1v[lane] - (a0 + a1);
-            float lv[NP];
-#pragma unroll
-            for (int j = 0; j < NP; ++j) lv[j] = Lk[at<1>(j, lane)];
-            a0 = L1v[lane];
-            a1 = 0.f;
-#pragma unroll
-            for (int j = 0; j < NP; j += 2) {
-                a0 = fmaf(lv[j], s1[j], a0);
-                a1 = fmaf(lv[j + 1], s1[j + 1], a1);
-            }
-            duv[lane] = a0 + a1;
-            for (int a = 0; a < QP; ++a) {
-                a0 = 0.f;
-                a1 = 0.f;
-#pragma unroll
-                for (int j = 0; j < NP; j += 2) {
-                    a0 = fmaf(lv[j], V[a * NP + j], a0);
-                    a1 = fmaf(lv[j + 1], V[a * NP + j + 1], a1);
-                }
-                co[(1 + a) * NP + lane] = a0 + a1;
-            }
-        }
-        __syncwarp();
-        // ds1 = l~1 + l~2^T u, dV_a = l~2^T U_a (column `lane` of l~2)
-        {
-            float lv[NP];
-#pragma unroll
-            for (int i = 0; i < NP; ++i) lv[i] = Lr[at<0>(i, lane)];
-            float a0 = L1v[lane], a1 = 0.f;
-#pragma unroll
-            for (int i = 0; i < NP; i += 2) {
-                a0 = fmaf(lv[i], uv[i], a0);
-                a1 = fmaf(lv[i + 1], uv[i + 1], a1);
-            }
-            co[lane] = a0 + a1;
-            for (int a = 0; a < QP; ++a) {
-                a0 = 0.f;
-                a1 = 0.f;
-#pragma unroll
-                for (int i = 0; i < NP; i += 2) {
-                    a0 = fmaf(lv[i], U[a * NP + i], a0);
-                    a1 = fmaf(lv[i + 1], U[a * NP + i + 1], a1);
-                }
-                co[(1 + QP + a) * NP + lane] = a0 + a1;
-            }
-        }
-        float acc[8][4];
-        // (3) X = S2p - S2p D^T, stored transposed over the k-major copy of S2p
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
-        gemm84<1, 0>(Sk, Dt, acc, rb, cb);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            const float4 sv = *reinterpret_cast<const float4*>(Sr + at<0>(8 * rb + r, 4 * cb));
-            acc[r][0] = sv.x - acc[r][0];
-            acc[r][1] = sv.y - acc[r][1];
-            acc[r][2] = sv.z - acc[r][2];
-            acc[r][3] = sv.w - acc[r][3];
-        }
-        __syncwarp();
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            *reinterpret_cast<float4*>(Sk + at<2>(4 * cb + q, 8 * rb)) =
-                make_float4(acc[0][q], acc[1][q], acc[2][q], acc[3][q]);
-            *reinterpret_cast<float4*>(Sk + at<2>(4 * cb + q, 8 * rb + 4)) =
-                make_float4(acc[4][q], acc[5][q], acc[6][q], acc[7][q]);
-        }
-        // (4) Z = l~2 - D^T l~2, stored row-major over l~2's row-major copy
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
-        gemm84<0, 0>(Dr, Lr, acc, rb, cb);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            const float4 lv = *reinterpret_cast<const float4*>(Lr + at<0>(8 * rb + r, 4 * cb));
-            acc[r][0] = lv.x - acc[r][0];
-            acc[r][1] = lv.y - acc[r][1];
-            acc[r][2] = lv.z - acc[r][2];
-            acc[r][3] = lv.w - acc[r][3];
-        }
-        __syncwarp();
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-            *reinterpret_cast<float4*>(Lr + at<0>(8 * rb + r, 4 * cb)) =
-                make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-        __syncwarp();
-        // (5) dM += l~2 X^T + Z^T S2p + du S1p^T
-        gemm84<1, 2>(Lk, Sk, dM, rb, cb);
-        gemm84<0, 0>(Lr, Sr, dM, rb, cb);
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dM[r][q] = fmaf(duv[8 * rb + r], S1v[4 * cb + q], dM[r][q]);
-    }
-    cp_async_wait<0>();
-    // the warps' dM blocks, summed in warp order
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < 8; ++r)
-        *reinterpret_cast<float4*>(Sr + at<0>(8 * rb + r, 4 * cb)) = make_float4(dM[r][0], dM[r][1], dM[r][2], dM[r][3]);
-    __syncthreads();
-    float* part = p.partials + (size_t)tile * (MM + (size_t)LW * g.d_in);
-    const float* base = Dt + MM;
-    for (int e = tid; e < MM; e += blockDim.x) {
-        float v = 0.f;
-        for (int w = 0; w < NW; ++w) v += base[w * warp_floats(QP) + e];
-        part[e] = v;
-    }
-}
 
 // Table gradients and dx from the vector cotangents of a chunk: with the coefficient rows
 // c_t = [ds1 | dU_a | dV_a] and the table rows T = [F | G_a | H_a] (one row per (block, state index)),
@@ -2673,17 +2725,17 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
     if (a->chunk > 0) {
         g->Lc = a->chunk;
     } else {
-        // The chains stack 4 chunks of a sample per CTA: the forward's output pass runs 3 CTAs per SM, the
-        // backward's two passes 2 per SM. Pick the chunk length that minimises the chains' waves x steps
-        // (plus a per-tile overhead of ~10 steps and the scans' sequential products).
+        // The chains stack 4 chunks of a sample per CTA and run 3 CTAs per SM: the forward's output pass and
+        // the backward's two passes. Pick the chunk length that minimises the chains' waves x steps (plus a
+        // per-tile overhead of ~10 steps and the scans' sequential products).
         const int sms = num_sms();
         double best = 1e30;
         int bestL = 256;
         for (int L = 16; L <= 512; ++L) {
             const int C = (g->T + L - 1) / L;
             const long G = (long)g->B * ((C + 3) / 4);
-            const long wf = (G + 3L * sms - 1) / (3L * sms), wb = (G + 2L * sms - 1) / (2L * sms);
-            const double cost = (L + 10.0) * (double)(wf + 2 * wb) + 0.6 * C / 8.0;
+            const long waves = (G + 3L * sms - 1) / (3L * sms);
+            const double cost = (L + 10.0) * (double)(3 * waves) + 0.6 * C / 8.0;
             if (cost < best) {
                 best = cost;
                 bestL = L;
@@ -2721,7 +2773,7 @@ static WsLayout fwd_layout(const Geom& g) {
     o += slots;
     L.pw = o;
     o += al256(sizeof(float) * (size_t)g.B * 2 * MM);
-    L.loc = o;  // the intervals' local terms, written by local_kernel and read by both chains and grad_map_kernel
+    L.loc = o;  // the intervals' local terms, written by local_kernel and read by agg_kernel and both chains
     o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
     L.pows = o;  // power complements for agg_kernel
     o += al256(sizeof(float) * (size_t)g.B * (g.Lc + 1) * MM);
@@ -2747,8 +2799,6 @@ static WsLayout bwd_layout(const Geom& g) {
     o += al256(sizeof(float) * (size_t)g.ntiles * (MM + (1 + 2 * g.QP) * NP * g.d_in));
     L.carry = o;  // per chunk: the cotangent arriving at its end
     o += slots;
-    L.pw = o;     // the cotangent stream l~_t, laid out as the prefix output
-    o += al256(sizeof(float) * (size_t)g.B * g.T * g.W);
     L.loc = o;    // the vector cotangents [ds1 | dU_a | dV_a] per interval
     o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
     L.pows = o;   // the reverse scan's suffix aggregates (gsuf)
@@ -2887,9 +2937,8 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     p.fagg = (const float*)(fws + F.agg);
     p.loc = (float*)(fws + F.loc);
     p.lcarry = (float*)(ws + L.carry);
-    p.lam = (float*)(ws + L.pw);
     {
-        const size_t smem = tc::tc_smem_bytes(g.W, g.QP);
+        const size_t smem = tc::tc_bwd_smem_bytes();
         if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
         cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
@@ -2913,21 +2962,25 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         bscan_fix_kernel<<<g.B * g.C, CST, 0, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
         if (cudaMemsetAsync(ws + L.status, 0, sizeof(int), s) != cudaSuccess) return EWS_ERR_LAUNCH;  // the ticket
+        // the exact pass with the gradient map: vector cotangents to `coef`, dM to the chunk partials
+        p.coef = (float*)(ws + L.loc);
+        const size_t xsmem = tc::tc_exact_smem_bytes(g.QP);
+        if (xsmem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+        auto* xk = g.N == NP ? bwd_exact_kernel<true> : bwd_exact_kernel<false>;
+        cudaFuncSetAttribute(xk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xsmem);
+        cudaFuncSetAttribute(xk, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+        const int xper = resident_ctas((const void*)xk, tc::NTH, xsmem);
+        if (xper < 1) return EWS_ERR_UNSUPPORTED;
+        int xgrid = xper * num_sms();
+        if (xgrid > g.B * groups) xgrid = g.B * groups;
         p.g.bwd_mode = 2;
-        bwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
+        xk<<<xgrid, tc::NTH, xsmem, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
         p.g.bwd_mode = 0;
     }
-    p.coef = (float*)(ws + L.loc);
     {
-        const size_t smem = gm::map_smem_bytes(g);
         const size_t tsmem = gm::table_smem_bytes(g);
-        if (smem > 227 * 1024 || tsmem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
-        auto* kern = g.N == NP ? grad_map_kernel<true> : grad_map_kernel<false>;
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-        kern<<<g.C * g.B, gm::NW * 32, smem, s>>>(p);
-        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        if (tsmem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
         cudaFuncSetAttribute(table_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
         table_grad_kernel<<<g.C * g.B, 128, tsmem, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
