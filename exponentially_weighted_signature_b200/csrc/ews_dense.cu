@@ -565,11 +565,10 @@ constexpr int RQS = 33;  // padded row stride of the row/column exchange buffer
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ uint32_t tf32_bits(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
+// x rounded to tf32 (10 explicit mantissa bits), nearest with ties away from zero, on the integer pipe: add
+// half a tf32 unit to the magnitude bits, then clear the 13 low bits (a carry into the exponent is the
+// correct rounding). The result is exact in tf32, so the tensor core reads it unchanged. Finite inputs only.
+__device__ __forceinline__ uint32_t tf32_bits(float x) { return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u; }
 
 // SM100 shared-memory matrix descriptor, no swizzle (start, leading / stride byte offsets, version 1).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -2099,6 +2098,16 @@ __global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
             if (next) fetch_s1(k - 1);
             cp_async_commit();
             if (k >= 2 && k - 2 < len_me) prefetch_row_l2(grows + (size_t)(k - 2) * g.W, g.W);
+            // the next interval's gradient: loads in flight for the whole step, added in the epilogue
+            float gn[32];
+            float gn1 = 0.f;
+            {
+                const float* gr = grows + (size_t)(k - 1) * g.W;
+                const bool ld = next && lane < N;
+#pragma unroll
+                for (int n = 0; n < 32; ++n) gn[n] = (ld && n < N) ? __ldg(gr + 1 + N + n * N + lane) : 0.f;
+                if (ld) gn1 = __ldg(gr + 1 + lane);
+            }
             // E0: rows of l~2 -> A operand
             float srow[32];
 #pragma unroll
@@ -2132,10 +2141,10 @@ __global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
                 break;
             }
             phase ^= 1;
-            // E1: row `lane` of X = l~2 - l~2 D = l~2 M -> column `lane` -> A operand row of X^T
-            float xcol[32];
+            // E1: row `lane` of X = l~2 - l~2 D = l~2 M -> column `lane` -> A operand row of X^T (the column
+            // stays in the exchange buffer for the epilogue)
             {
-                float pr[32];
+                float pr[32], xcol[32];
                 tmem_ld32(tP1 + lane_off, pr);
 #pragma unroll
                 for (int n = 0; n < 32; ++n) RQt[lane * RQS + n] = srow[n] - pr[n];
@@ -2158,16 +2167,6 @@ __global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
                 for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
                 mma_commit(s.bar);
             }
-            // the next interval's gradient, loaded while the tensor core runs
-            float gn[32];
-            float gn1 = 0.f;
-            {
-                const float* gr = grows + (size_t)(k - 1) * g.W;
-                const bool ld = next && lane < N;
-#pragma unroll
-                for (int n = 0; n < 32; ++n) gn[n] = (ld && n < N) ? __ldg(gr + 1 + N + n * N + lane) : 0.f;
-                if (ld) gn1 = __ldg(gr + 1 + lane);
-            }
             // l1 <- M^T v + g1 = v - D^T v + g1
             {
                 const float* v = vt + NP;
@@ -2176,8 +2175,6 @@ __global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
                 vt[lane] = nv + gn1;
                 __syncwarp();
             }
-#pragma unroll
-            for (int n = 0; n < 32; ++n) xcol[n] += gn[n];  // X + g2 (X - D^T X + g2 below)
             if (!tc_wait(s, phase, mbar_limit)) {
                 failed = mma_pending = true;
                 break;
@@ -2188,7 +2185,7 @@ __global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
                 float q2[32];
                 tmem_ld32(tP2 + lane_off, q2);
 #pragma unroll
-                for (int n = 0; n < 32; ++n) col[n] = xcol[n] - q2[n];
+                for (int n = 0; n < 32; ++n) col[n] = (RQt[n * RQS + lane] + gn[n]) - q2[n];
                 fence_before();
                 __syncwarp();
             }
