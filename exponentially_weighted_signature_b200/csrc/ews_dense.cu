@@ -2722,9 +2722,10 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
     if (a->chunk > 0) {
         g->Lc = a->chunk;
     } else {
-        // The chains stack 4 chunks of a sample per CTA and run 3 CTAs per SM: the forward's output pass and
-        // the backward's two passes. Pick the chunk length that minimises the chains' waves x steps (plus a
-        // per-tile overhead of ~10 steps and the scans' sequential products).
+        // The chains stack 4 chunks of a sample per CTA: the forward's output pass and the backward's
+        // zero-carry pass run 3 CTAs per SM, the exact pass 2 (its steps cost more; the model counts all three
+        // passes at 3). Pick the chunk length that minimises the chains' waves x steps (plus a per-tile
+        // overhead of ~10 steps and the scans' sequential products).
         const int sms = num_sms();
         double best = 1e30;
         int bestL = 256;
