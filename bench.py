@@ -538,15 +538,16 @@ def run_b200(args, rank, world, local_rank):
 
     # kernel timing from the launching stream
     per = {}
-    for name, e0, e1, units in prof:
+    counts = dict(KERNELS_PER_CALL)
+    if setup["meta"].get("readout") == "terminal":
+        counts.update(TERMINAL_KERNELS)
+    launches = 0
+    for name, e0, e1, units, nl in prof:
         d = per.setdefault(name, [0.0, 0, 0])
         d[0] += e0.elapsed_time(e1)
         d[1] += 1
         d[2] = units
-    counts = dict(KERNELS_PER_CALL)
-    if setup["meta"].get("readout") == "terminal":
-        counts.update(TERMINAL_KERNELS)
-    launches = sum(counts.get(n, 1) * v[1] for n, v in per.items())
+        launches += nl if nl is not None else counts.get(name, 1)  # the library's own count where it reports one
     # every engine call also launches ews_status_fold's one-thread kernel (the expm calls do not)
     launches += sum(v[1] for n, v in per.items() if not n.startswith("ews_expm"))
     dom = max(((n, v) for n, v in per.items() if n in setup["alg"]), key=lambda kv: kv[1][0])

@@ -37,6 +37,7 @@ EXPORTED = (
     "ews_diag_fwd_noalloc",
     "ews_diag_fwd_noalloc_status",
     "ews_dense_workspace_size",
+    "ews_dense_launches",
     "ews_dense_fwd",
     "ews_dense_bwd",
     "ews_block_workspace_size",
@@ -190,6 +191,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             fn.restype = _c_int
         lib.ews_dense_workspace_size.argtypes = [ctypes.POINTER(DenseArgs), ctypes.POINTER(_c_size), ctypes.POINTER(_c_size)]
         lib.ews_dense_workspace_size.restype = _c_int
+        lib.ews_dense_launches.argtypes = [ctypes.POINTER(DenseArgs), ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]
+        lib.ews_dense_launches.restype = _c_int
         for name in ("ews_dense_fwd", "ews_dense_bwd"):
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.POINTER(DenseArgs), _vp]

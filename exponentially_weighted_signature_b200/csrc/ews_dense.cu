@@ -1370,7 +1370,7 @@ __device__ __forceinline__ void st22(float* M, const float v[2][2], int i0, int 
 }
 
 // (Po, S1o, S2o) = (PL, L1, L2) (x) (PR, R1, R2), flows as complements (the same product as chen_mul_smem).
-// Outputs may alias the left operand. Scratch T0, T1 (MM), vtmp (NP). Barrier-complete on return.
+// Outputs may alias either operand. Scratch T0, T1 (MM), vtmp (NP). Barrier-complete on return.
 __device__ void chen_mul_256(const float* PL, const float* L1, const float* L2, const float* PR, const float* R1,
                              const float* R2, float* Po, float* S1o, float* S2o, float* T0, float* T1, float* vtmp) {
     const int i0 = 2 * (threadIdx.x >> 4), j0 = 2 * (threadIdx.x & 15);
@@ -1465,8 +1465,8 @@ __device__ void apply_JT_256(const float* Pr, const float* U1v, float* L1, float
 // Carries of every chunk from the precomputed aggregates, by a two-level scan over each sample's chunks
 // instead of the chain kernel's look-back (whose first wave would walk back through every earlier aggregate):
 //   scan_local_kernel:  per group of CG chunks, the inclusive products within the group (into `incl`);
-//   scan_groups_kernel: per sample, the exclusive products of the group totals (into `gex`);
-//   scan_fix_kernel:    per chunk, carry = gex(group) (x) incl(previous chunk of the group), and for the
+//   scan_round_kernel:  the inclusive products of the group totals, in log2(groups) parallel rounds;
+//   scan_fix_kernel:    per chunk, carry = (groups before) (x) incl(previous chunk of the group), and for the
 //                       terminal readout the sample's total as its output row.
 // Chen products are chen_mul_256, in a fixed order, so the carries are deterministic.
 constexpr int CG = 8;
@@ -1498,21 +1498,26 @@ __global__ void __launch_bounds__(CST) scan_local_kernel(Params p) {
     }
 }
 
-__global__ void __launch_bounds__(CST) scan_groups_kernel(Params p) {
+// One round of the group scan (Hillis-Steele, log2 of the group count rounds over B x groups CTAs):
+// X_k <- X_{k-d} (x) X_k for k >= d. Round 0 (src == nullptr) reads the group totals, the inclusive value of
+// each group's last chunk; after the last round X_k is the product of groups 0..k.
+__global__ void __launch_bounds__(CST) scan_round_kernel(Params p, const float* src, float* dst, int d) {
     __shared__ __align__(16) ScanSmem sm;
     const Geom& g = p.g;
     const int ng = scan_groups(g.C);
-    const int b = blockIdx.x;
-    identity_smem(sm.P0, sm.S10, sm.S20);
-    __syncthreads();
-    for (int k = 0; k < ng; ++k) {
-        store_slot(p.gex + ((size_t)b * ng + k) * g.SW, sm.P0, sm.S10, sm.S20);
-        if (k + 1 == ng) break;
-        const int last = min(g.C, (k + 1) * CG) - 1;
-        load_slot_smem(p.incl + ((size_t)b * g.C + last) * g.SW, sm.P1, sm.S11, sm.S21);
+    const int b = blockIdx.x / ng, k = blockIdx.x - b * ng;
+    auto elem = [&](int j) -> const float* {
+        return src ? src + ((size_t)b * ng + j) * g.SW
+                   : p.incl + ((size_t)b * g.C + min(g.C, (j + 1) * CG) - 1) * g.SW;
+    };
+    load_slot_smem(elem(k), sm.P1, sm.S11, sm.S21);
+    if (k >= d) {
+        load_slot_smem(elem(k - d), sm.P0, sm.S10, sm.S20);
         __syncthreads();
-        chen_mul_256(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp);
+        chen_mul_256(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P1, sm.S11, sm.S21, sm.T0, sm.T1, sm.vtmp);
     }
+    __syncthreads();
+    store_slot(dst + ((size_t)b * ng + k) * g.SW, sm.P1, sm.S11, sm.S21);
 }
 
 __global__ void __launch_bounds__(CST) scan_fix_kernel(Params p) {
@@ -1522,7 +1527,11 @@ __global__ void __launch_bounds__(CST) scan_fix_kernel(Params p) {
     const int b = blockIdx.x / g.C, c = blockIdx.x - b * g.C;
     const int k = c / CG;
     const size_t base = (size_t)b * g.C;
-    load_slot_smem(p.gex + ((size_t)b * ng + k) * g.SW, sm.P0, sm.S10, sm.S20);
+    // the product of the earlier groups (the group scan's value of group k - 1; the identity for group 0)
+    if (k > 0)
+        load_slot_smem(p.gex + ((size_t)b * ng + k - 1) * g.SW, sm.P0, sm.S10, sm.S20);
+    else
+        identity_smem(sm.P0, sm.S10, sm.S20);
     __syncthreads();
     if (c > k * CG) {
         load_slot_smem(p.incl + (base + c - 1) * g.SW, sm.P1, sm.S11, sm.S21);
@@ -1586,7 +1595,7 @@ __device__ void apply_JT_smem(const float* Pr, const float* U1v, float* L1, floa
 // the range's start from the range's own output gradients (zero carry). An earlier range a and a later b
 // combine to (G_a (x) G_b, J(G_a)^T mu_b + mu_a), with J(G)^T the transposed Chen map (apply_JT_256).
 //   bscan_local_kernel:  per group, the suffix elements from every chunk to the group's end (gsuf, incl);
-//   bscan_groups_kernel: per sample, the cotangent arriving at each group's end (gex);
+//   bscan_round_kernel:  the suffix elements of the groups, in log2(groups) parallel rounds;
 //   bscan_fix_kernel:    per chunk, the cotangent arriving at its end (lcarry), J(suffix after it)^T lam + mu.
 struct BScanSmem {
     float P0[MM], S10[NP], S20[MM];  // accumulated G
@@ -1639,25 +1648,39 @@ __global__ void __launch_bounds__(CST) bscan_local_kernel(Params p) {
     }
 }
 
-__global__ void __launch_bounds__(CST) bscan_groups_kernel(Params p) {
+// One round of the reverse group scan (Hillis-Steele over the groups): Y_k <- Y_k . Y_{k+d} for k + d < ng,
+// elements (G, mu) combined as above. Round 0 (src == nullptr) reads each group's element (the suffix
+// aggregate and local cotangent of its first chunk); after the last round Y_k is the element of groups
+// k..ng-1. Elements are stored as two slots: G, then mu in the cotangent positions of a slot.
+__global__ void __launch_bounds__(CST) bscan_round_kernel(Params p, const float* src, float* dst, int d) {
     __shared__ __align__(16) BScanSmem sm;
     const Geom& g = p.g;
     const int ng = scan_groups(g.C);
-    const int b = blockIdx.x;
+    const int b = blockIdx.x / ng, k = blockIdx.x - b * ng;
+    auto gslot = [&](int j) -> const float* {
+        return src ? src + ((size_t)b * ng + j) * 2 * g.SW : p.gsuf + ((size_t)b * g.C + (size_t)j * CG) * g.SW;
+    };
+    auto mslot = [&](int j) -> const float* {
+        return src ? src + (((size_t)b * ng + j) * 2 + 1) * g.SW : p.incl + ((size_t)b * g.C + (size_t)j * CG) * g.SW;
+    };
+    float* out = dst + ((size_t)b * ng + k) * 2 * g.SW;
+    const int kb = k + d < ng ? k + d : k;  // the later range (or the element itself, copied)
+    load_slot_smem(gslot(kb), sm.P0, sm.S10, sm.S20);
     for (int e = threadIdx.x; e < MM; e += blockDim.x) sm.L2r[e] = 0.f;
     if (threadIdx.x < NP) sm.L1[threadIdx.x] = 0.f;
     __syncthreads();
-    for (int k = ng - 1; k >= 0; --k) {
-        bscan_store_lam(p.gex + ((size_t)b * ng + k) * g.SW, sm);
-        if (k == 0) break;
-        const size_t first = (size_t)b * g.C + (size_t)k * CG;
+    bscan_add_mu(sm, mslot(kb));
+    if (kb != k) {
+        load_slot_smem(gslot(k), sm.P1, sm.S11, sm.S21);
         __syncthreads();
-        load_slot_smem(p.gsuf + first * g.SW, sm.P1, sm.S11, sm.S21);
+        bscan_apply(sm);             // mu_b <- J(G_a)^T mu_b
+        bscan_add_mu(sm, mslot(k));  //        + mu_a
         __syncthreads();
-        bscan_apply(sm);
-        bscan_add_mu(sm, p.incl + first * g.SW);
-        __syncthreads();
+        chen_mul_256(sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.v3);
     }
+    __syncthreads();
+    store_slot(out, sm.P0, sm.S10, sm.S20);
+    bscan_store_lam(out + g.SW, sm);
 }
 
 __global__ void __launch_bounds__(CST) bscan_fix_kernel(Params p) {
@@ -1667,10 +1690,14 @@ __global__ void __launch_bounds__(CST) bscan_fix_kernel(Params p) {
     const int b = blockIdx.x / g.C, c = blockIdx.x - b * g.C;
     const int k = c / CG, last = min(g.C, (k + 1) * CG) - 1;
     const size_t base = (size_t)b * g.C;
-    {
-        const float* src = p.gex + ((size_t)b * ng + k) * g.SW;
+    if (k + 1 < ng) {
+        // the cotangent arriving at the group's end: the mu of the later groups' combined element
+        const float* src = p.gex + (((size_t)b * ng + k + 1) * 2 + 1) * g.SW;
         for (int e = threadIdx.x; e < MM; e += blockDim.x) sm.L2r[e] = ldcg(src + MM + NP + e);
         if (threadIdx.x < NP) sm.L1[threadIdx.x] = ldcg(src + MM + threadIdx.x);
+    } else {
+        for (int e = threadIdx.x; e < MM; e += blockDim.x) sm.L2r[e] = 0.f;
+        if (threadIdx.x < NP) sm.L1[threadIdx.x] = 0.f;
     }
     __syncthreads();
     if (c < last) {
@@ -2775,8 +2802,8 @@ static WsLayout fwd_layout(const Geom& g) {
     o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
     L.pows = o;  // power complements for agg_kernel
     o += al256(sizeof(float) * (size_t)g.B * (g.Lc + 1) * MM);
-    L.gex = o;   // group prefixes of the carry scan
-    o += al256(sizeof(float) * (size_t)g.B * scan_groups(g.C) * g.SW);
+    L.gex = o;   // the group scan's two round buffers
+    o += 2 * al256(sizeof(float) * (size_t)g.B * scan_groups(g.C) * g.SW);
     L.total = o;
     return L;
 }
@@ -2801,8 +2828,8 @@ static WsLayout bwd_layout(const Geom& g) {
     o += al256(sizeof(float) * (size_t)g.B * g.T * loc_width(g.QP));
     L.pows = o;   // the reverse scan's suffix aggregates (gsuf)
     o += slots;
-    L.gex = o;    // the reverse scan's per-group cotangents
-    o += al256(sizeof(float) * (size_t)g.B * scan_groups(g.C) * g.SW);
+    L.gex = o;    // the reverse group scan's two round buffers of (G, mu) elements
+    o += 2 * al256(sizeof(float) * (size_t)g.B * scan_groups(g.C) * 2 * g.SW);
     L.total = o;
     return L;
 }
@@ -2834,6 +2861,19 @@ extern "C" int ews_dense_workspace_size(const ews_dense_args* a, size_t* fwd_byt
     if (rc != EWS_OK) return rc;
     if (fwd_bytes) *fwd_bytes = fwd_layout(g).total;
     if (bwd_bytes) *bwd_bytes = bwd_layout(g).total;
+    return EWS_OK;
+}
+
+extern "C" int ews_dense_launches(const ews_dense_args* a, int* fwd_launches, int* bwd_launches) {
+    Geom g;
+    const int rc = make_geom(a, &g);
+    if (rc != EWS_OK) return rc;
+    int rounds = 1;  // the group scans' rounds
+    while ((1 << rounds) < scan_groups(g.C)) ++rounds;
+    // forward: power, local, powers, agg, scan_local, rounds, scan_fix [, fwd_tc for the prefix readout];
+    // backward: bwd_tc, bscan_local, rounds, bscan_fix, bwd_exact, table_grad, reduce
+    if (fwd_launches) *fwd_launches = 6 + rounds + (g.readout == EWS_READOUT_PREFIX ? 1 : 0);
+    if (bwd_launches) *bwd_launches = 6 + rounds;
     return EWS_OK;
 }
 
@@ -2883,8 +2923,18 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     p.gex = (float*)(ws + L.gex);
     scan_local_kernel<<<g.B * scan_groups(g.C), CST, 0, s>>>(p);
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
-    scan_groups_kernel<<<g.B, CST, 0, s>>>(p);
-    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+    {
+        const int ng = scan_groups(g.C);
+        float* h0 = (float*)(ws + L.gex);
+        float* h1 = h0 + al256(sizeof(float) * (size_t)g.B * ng * g.SW) / sizeof(float);
+        int rounds = 1;
+        while ((1 << rounds) < ng) ++rounds;
+        for (int r = 0; r < rounds; ++r) {
+            scan_round_kernel<<<g.B * ng, CST, 0, s>>>(p, r == 0 ? nullptr : ((r & 1) ? h0 : h1), (r & 1) ? h1 : h0, 1 << r);
+            if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        }
+        p.gex = ((rounds - 1) & 1) ? h1 : h0;  // the inclusive group products
+    }
     scan_fix_kernel<<<g.B * g.C, CST, 0, s>>>(p);
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     if (g.readout == EWS_READOUT_TERMINAL) return EWS_OK;  // the scan wrote the terminal rows
@@ -2955,8 +3005,18 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         const int ng = scan_groups(g.C);
         bscan_local_kernel<<<g.B * ng, CST, 0, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
-        bscan_groups_kernel<<<g.B, CST, 0, s>>>(p);
-        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        {
+            float* h0 = (float*)(ws + L.gex);
+            float* h1 = h0 + al256(sizeof(float) * (size_t)g.B * ng * 2 * g.SW) / sizeof(float);
+            int rounds = 1;
+            while ((1 << rounds) < ng) ++rounds;
+            for (int r = 0; r < rounds; ++r) {
+                bscan_round_kernel<<<g.B * ng, CST, 0, s>>>(p, r == 0 ? nullptr : ((r & 1) ? h0 : h1), (r & 1) ? h1 : h0,
+                                                           1 << r);
+                if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+            }
+            p.gex = ((rounds - 1) & 1) ? h1 : h0;  // the suffix elements of the groups
+        }
         bscan_fix_kernel<<<g.B * g.C, CST, 0, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
         if (cudaMemsetAsync(ws + L.status, 0, sizeof(int), s) != cudaSuccess) return EWS_ERR_LAUNCH;  // the ticket

@@ -39,8 +39,8 @@ PROFILE = None
 
 
 class _timed:
-    def __init__(self, name, device, units):
-        self.name, self.device, self.units = name, device, units
+    def __init__(self, name, device, units, launches=None):
+        self.name, self.device, self.units, self.launches = name, device, units, launches
 
     def __enter__(self):
         if PROFILE is not None:
@@ -52,8 +52,15 @@ class _timed:
     def __exit__(self, *exc):
         if PROFILE is not None:
             self.e1.record(torch.cuda.current_stream(self.device))
-            PROFILE.append((self.name, self.e0, self.e1, self.units))
+            PROFILE.append((self.name, self.e0, self.e1, self.units, self.launches))
         return False
+
+
+def _dense_launches(a):
+    """(forward, backward) kernel launches of one dense call with these arguments."""
+    f, b = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(_lib.load().ews_dense_launches(ctypes.byref(a), ctypes.byref(f), ctypes.byref(b)), "ews_dense_launches")
+    return f.value, b.value
 
 
 # ---------------------------------------------------------------------------------- device status
@@ -252,7 +259,7 @@ class DenseScan(torch.autograd.Function):
         a.out = _ptr(out)
         a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fb.value
         raise_pending(dev)
-        with _timed("ews_dense_fwd", dev, B * T):
+        with _timed("ews_dense_fwd", dev, B * T, _dense_launches(a)[0] if PROFILE is not None else None):
             _lib.check(lib.ews_dense_fwd(ctypes.byref(a), _stream_ptr(dev)), "ews_dense_fwd")
         _fold_status(fwd_ws, dev)
         ctx.meta = (readout, flags, chunk, increments, B, T, d_in, N, QP, bb.value, path.dtype)
@@ -283,7 +290,7 @@ class DenseScan(torch.autograd.Function):
         a.grad_d, a.grad_f, a.grad_g, a.grad_h = (_ptr(t) for t in (gM, gF, gG, gH))
         a.fwd_ws, a.fwd_ws_bytes = _ptr(fwd_ws), fwd_ws.numel()
         a.bwd_ws, a.bwd_ws_bytes = _ptr(bwd_ws), bwd_bytes
-        with _timed("ews_dense_bwd", dev, B * T):
+        with _timed("ews_dense_bwd", dev, B * T, _dense_launches(a)[1] if PROFILE is not None else None):
             _lib.check(lib.ews_dense_bwd(ctypes.byref(a), _stream_ptr(dev)), "ews_dense_bwd")
         _fold_status(bwd_ws, dev)
         raise_pending(dev)

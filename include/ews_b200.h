@@ -202,6 +202,9 @@ typedef struct ews_dense_args {
 } ews_dense_args;
 
 int ews_dense_workspace_size(const ews_dense_args* a, size_t* fwd_bytes, size_t* bwd_bytes);
+/* Kernel launches of one ews_dense_fwd / ews_dense_bwd call with these arguments (the carry scans take
+ * log2(chunk groups) rounds). A query of this library with no counterpart in the reference. */
+int ews_dense_launches(const ews_dense_args* a, int* fwd_launches, int* bwd_launches);
 int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream);
 int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream);
 
