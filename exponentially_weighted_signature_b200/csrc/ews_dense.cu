@@ -2615,6 +2615,123 @@ inline size_t table_smem_bytes(const Geom& g) {
 }
 }  // namespace gm
 
+// Table gradients and dx with the tables held in registers (q + 1 <= 4, d_in <= 8): lane l of each warp owns
+// the table rows 32 r + l (row r of its block: F, G_a, H_a), all d_in columns, for the whole chunk; the
+// warps take the chunk's intervals round robin. Per interval the lane reads its entries of c_t (coalesced),
+//   dT[rows, :] += c_t[rows] dx_t^T     (registers),
+//   dx_t = sum over the warp of T[rows, :]^T c_t[rows]   (a reduce-scatter of the 8 column sums, 9 shuffles),
+// and the warps' dT are summed in warp order at the end.
+template <int ROWS>
+__global__ void __launch_bounds__(128) table_grad_reg_kernel(Params p) {
+    __shared__ __align__(16) float red[ROWS * 32 * 8];
+    extern __shared__ __align__(16) float xs[];  // the chunk's increments, 8 per interval
+    const Geom& g = p.g;
+    const int N = g.N, d = g.d_in, QP = g.QP, LW = loc_width(QP);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tile = blockIdx.x;
+    const int c = tile / g.B, b = tile - c * g.B;
+    const int t0 = c * g.Lc;
+    const int len = min(g.Lc, g.T - t0);
+    float tab[ROWS][8], acc[ROWS][8];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+        const bool ok = lane < N;
+        const float* src = r == 0 ? p.tab_f + ((size_t)b * N + lane) * d
+                           : r <= QP ? p.tab_g + (((size_t)b * QP + r - 1) * N + lane) * d
+                                     : p.tab_h + (((size_t)b * QP + r - 1 - QP) * N + lane) * d;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            tab[r][cc] = (ok && cc < d) ? src[cc] : 0.f;
+            acc[r][cc] = 0.f;
+        }
+    }
+    for (int e = tid; e < len * 8; e += blockDim.x) {
+        const int k = e >> 3, cc = e & 7;
+        xs[e] = cc < d ? input_increment(p.path, b, t0 + k, cc, g.T, d, g.flags) : 0.f;
+    }
+    __syncthreads();
+    // column owned after the reduce-scatter: bits 4, 3, 2 of the lane
+    const int mycol = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    float cv[ROWS];
+    int kk = warp;
+    if (kk < len) {
+        const float* cr = p.coef + ((size_t)b * g.T + t0 + kk) * LW + lane;
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) cv[r] = ldcg(cr + 32 * r);
+    }
+    for (; kk < len; kk += 4) {
+        const int t = t0 + kk;
+        float x[8];
+        {
+            const float4 x0 = *reinterpret_cast<const float4*>(xs + kk * 8);
+            const float4 x1 = *reinterpret_cast<const float4*>(xs + kk * 8 + 4);
+            x[0] = x0.x; x[1] = x0.y; x[2] = x0.z; x[3] = x0.w;
+            x[4] = x1.x; x[5] = x1.y; x[6] = x1.z; x[7] = x1.w;
+        }
+        float cur[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) cur[r] = cv[r];
+        if (kk + 4 < len) {  // the warp's next interval, in flight during this one
+            const float* cr = p.coef + ((size_t)b * g.T + t + 4) * LW + lane;
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) cv[r] = ldcg(cr + 32 * r);
+        }
+        float sv[8];
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) sv[cc] = 0.f;
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                acc[r][cc] = fmaf(cur[r], x[cc], acc[r][cc]);
+                sv[cc] = fmaf(tab[r][cc], cur[r], sv[cc]);
+            }
+        // reduce-scatter of the 8 column sums over the warp
+        const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0, hi4 = (lane & 4) != 0;
+        float s4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float send = hi16 ? sv[i] : sv[i + 4];
+            const float keep = hi16 ? sv[i + 4] : sv[i];
+            s4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        }
+        float s2[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const float send = hi8 ? s4[i] : s4[i + 2];
+            const float keep = hi8 ? s4[i + 2] : s4[i];
+            s2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+        float s1;
+        {
+            const float send = hi4 ? s2[0] : s2[1];
+            const float keep = hi4 ? s2[1] : s2[0];
+            s1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+        if ((lane & 3) == 0 && mycol < d) p.grad_dx[((size_t)b * g.T + t) * d + mycol] = s1;
+    }
+    // the warps' table gradients, summed in warp order
+    for (int w = 0; w < 4; ++w) {
+        if (warp == w) {
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    float* q = red + (r * 32 + lane) * 8 + cc;
+                    *q = w == 0 ? acc[r][cc] : *q + acc[r][cc];
+                }
+        }
+        __syncthreads();
+    }
+    float* part = p.partials + (size_t)tile * (MM + (size_t)LW * d) + MM;
+    for (int e = tid; e < LW * d; e += blockDim.x) {
+        const int row = e / d, cc = e - row * d;
+        part[e] = red[row * 8 + cc];
+    }
+}
+
 // Table gradients and dx from the vector cotangents of a chunk: with the coefficient rows
 // c_t = [ds1 | dU_a | dV_a] and the table rows T = [F | G_a | H_a] (one row per (block, state index)),
 //   dT += sum_t c_t dx_t^T,   dx_t = T^T c_t,
@@ -3039,8 +3156,17 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     {
         const size_t tsmem = gm::table_smem_bytes(g);
         if (tsmem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
-        cudaFuncSetAttribute(table_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
-        table_grad_kernel<<<g.C * g.B, 128, tsmem, s>>>(p);
+        if (g.QP <= 4 && g.d_in <= 8) {
+            const int rows = 1 + 2 * g.QP;
+            const size_t xsm = sizeof(float) * 8 * (size_t)g.Lc;  // the chunk's increments
+            if (rows == 3) table_grad_reg_kernel<3><<<g.C * g.B, 128, xsm, s>>>(p);
+            else if (rows == 5) table_grad_reg_kernel<5><<<g.C * g.B, 128, xsm, s>>>(p);
+            else if (rows == 7) table_grad_reg_kernel<7><<<g.C * g.B, 128, xsm, s>>>(p);
+            else table_grad_reg_kernel<9><<<g.C * g.B, 128, xsm, s>>>(p);
+        } else {
+            cudaFuncSetAttribute(table_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
+            table_grad_kernel<<<g.C * g.B, 128, tsmem, s>>>(p);
+        }
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     }
     const size_t total = (size_t)g.B * (g.N * g.N + (1 + 2 * g.QP) * g.N * g.d_in);
