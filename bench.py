@@ -43,7 +43,7 @@ TERMINAL_KERNELS = {"ews_diag_fwd": 2, "ews_diag_bwd": 4, "ews_dense_fwd": 7}
 # so `roofline.traffic` is this figure times the launch's units.
 TRAFFIC_PER_UNIT = {
     "config1": {"ews_diag_fwd": 926.0, "ews_diag_bwd": 3227.0},
-    "config2": {"ews_dense_fwd": 6538.0, "ews_dense_bwd": 17306.0},
+    "config2": {"ews_dense_fwd": 6660.0, "ews_dense_bwd": 17527.0},
     "config3": {"ews_block_fwd": 8009.0, "ews_block_bwd": 9850.0},
     "config5": {"ews_diag_fwd": 78.0, "ews_diag_bwd": 90.0},
 }
