@@ -96,6 +96,7 @@ def raise_pending(device) -> None:
         host.zero_()
         sticky.zero_()
         _lib.check(code, "an earlier EWS engine call on this device")
+    raise_guard(device)
 
 
 def reset_status(device=None) -> None:
@@ -113,6 +114,45 @@ def _fold_status(workspace: torch.Tensor, device) -> None:
     if CHECK_SYNC:
         torch.cuda.current_stream(device).synchronize()
         raise_pending(device)
+
+
+# Range guards of leaves that the engines evaluate as truncated series (the plane leaf): the condition is
+# computed on the device, folded into a per-device flag and copied to pinned host memory without a wait;
+# the next engine call on the device raises. No host synchronisation in the call itself.
+_GUARD = {}
+
+
+def _guard_slot(device):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    slot = _GUARD.get(idx)
+    if slot is None:
+        flag = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        slot = _GUARD[idx] = [flag, host, ""]
+    return slot
+
+
+def guard(bad: torch.Tensor, device, message: str) -> None:
+    """Records (without waiting) that an input violated a leaf's range (``bad``: a 0-dim bool tensor on the
+    device); ``raise_guard`` raises ``message`` on the next call."""
+    slot = _guard_slot(device)
+    slot[0].copy_(torch.maximum(slot[0], bad.to(torch.int32).reshape(1)))
+    slot[1].copy_(slot[0], non_blocking=True)
+    slot[2] = message
+    if CHECK_SYNC:
+        torch.cuda.current_stream(device).synchronize()
+        raise_guard(device)
+
+
+def raise_guard(device) -> None:
+    """Raises (once) the range violation that an earlier call on ``device`` recorded."""
+    if not _GUARD:
+        return
+    slot = _guard_slot(device)
+    if int(slot[1][0]) != 0:
+        slot[0].zero_()
+        slot[1].zero_()
+        raise NotImplementedError(slot[2])
 
 
 def _coef_buffer(coef):

@@ -110,7 +110,12 @@ class EWS(nn.Module):
             raise ValueError(f"combine must be one of {COMBINE_KINDS}, got {combine!r}")
         if leaf == "block_series" and N == 2 and series_q is None:
             raise ValueError("leaf='block_series' at depth 2 requires series_q")
-        if leaf not in ("series", "block_series", "van_loan"):
+        if leaf == "plane_closed":
+            if N > 2:
+                raise NotImplementedError("leaf='plane_closed': closed-form local terms exist for depths 1 and 2")
+            if self.d % 2:
+                raise ValueError("leaf='plane_closed' needs an even dimension (2x2 planes)")
+        if leaf not in ("series", "block_series", "van_loan", "plane_closed"):
             raise NotImplementedError(
                 f"leaf={leaf!r} is not built on the B200 engines; use leaf='series' (or 'van_loan' for a diagonal A)"
             )
@@ -134,7 +139,8 @@ class EWS(nn.Module):
                 raise NotImplementedError("depth N=3 runs on the block engine: 2x2 (or 1x1) blocks, state dim even and <= 8")
             self.engine = "block"
         elif self.N == 2:
-            self.engine = "diag" if is_diagonal(self.A_param) else "dense"
+            # the plane leaf reads its own generator from A (per plane [[d, w], [-w, d]]): dense engine
+            self.engine = "diag" if is_diagonal(self.A_param) and leaf != "plane_closed" else "dense"
         else:
             raise NotImplementedError("the B200 engines are built for depths N=2 and N=3")
         if leaf == "block_series" and self.N > 2:
@@ -147,7 +153,7 @@ class EWS(nn.Module):
         # The Van Loan leaf with a per-interval clock (diagonal engine) and on the dense engine is the
         # series leaf's evaluation with the Van Loan leaf's coefficients, truncated at degree 8
         # (series.vanloan_poly_coeffs); under a uniform clock the diagonal engine takes its exact tables.
-        self._q = VANLOAN_DEGREE if leaf == "van_loan" else self.series_q
+        self._q = VANLOAN_DEGREE if leaf == "van_loan" else series.PLANE_Q if leaf == "plane_closed" else self.series_q
 
     @property
     def signature_dim(self) -> int:
@@ -265,9 +271,19 @@ class EWS(nn.Module):
         clock = clock.to(torch.float32)
         h = clock[:, 1] - clock[:, 0]
         coeffs = None
+        A_leaf = None
         if self.leaf == "van_loan":
             coeffs = series.vanloan_device_coeffs(self.M, self.van_loan_expm, VANLOAN_DEGREE, str(A.device))
-        M, F, G, H = series.dense_tables(A, h, self._q, lift, coeffs)
+        if self.leaf == "plane_closed":
+            # The plane leaf's closed form (ews/core/kernels/plane_engine.py:134-155) is the series leaf's
+            # limit; evaluated at order PLANE_Q it agrees to float32 rounding while ||h A_planes|| <= PLANE_X_MAX,
+            # which a device-side check guards (the next call raises otherwise).
+            A_leaf = series.plane_generator(A)
+            x = h.abs().max() * A_leaf.abs().sum(-1).max()
+            engine.guard(x > series.PLANE_X_MAX, A.device,
+                         f"leaf='plane_closed' is evaluated as its series at order {series.PLANE_Q}, exact to float32 "
+                         f"for ||h A|| <= {series.PLANE_X_MAX}; an earlier call on this device exceeded that range")
+        M, F, G, H = series.dense_tables(A, h, self._q, lift, coeffs, A_leaf)
         flags = _lib.EWS_F_UNIFORM | _det_flags()
         if increments:
             flags |= _lib.EWS_F_INCREMENTS

@@ -160,18 +160,47 @@ def dense_leaf_tables(X: torch.Tensor, q: int, lift=None, coeffs=None):
     return K1 @ W, P @ W, K2 @ W
 
 
-def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None, coeffs=None):
+def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None, coeffs=None, A_leaf=None):
     """Per-sample tables of the dense engine for generator A (N, N), clock steps h (B,) and lift W (N, d_in):
-    the flow complement D = I - expm(-hA) and the series-leaf tables F, G, H (dense_leaf_tables).
+    the flow complement D = I - expm(-hA) and the series-leaf tables F, G, H (dense_leaf_tables), the
+    latter of ``A_leaf`` when given (a leaf that reads its own generator from A, e.g. the plane leaf).
     Differentiable; evaluated in float64 and returned in float32. The exponential
     (ews/core/chen_scan.py:155-168) and its VJP run in the library's expm kernels (CUDA tensors only)."""
     from .engine import Expm
 
-    X = -h.to(torch.float64)[:, None, None] * A.to(torch.float64)  # (B, N, N)
+    h64 = h.to(torch.float64)[:, None, None]
+    X = -h64 * A.to(torch.float64)  # (B, N, N)
     N = A.shape[-1]
     Dc = torch.eye(N, dtype=torch.float64, device=A.device) - Expm.apply(X)
-    F, G, H = dense_leaf_tables(X, q, lift, coeffs)
+    Xl = X if A_leaf is None else -h64 * A_leaf.to(torch.float64)
+    F, G, H = dense_leaf_tables(Xl, q, lift, coeffs)
     return Dc.float(), F.float(), G.float(), H.float()
+
+
+# ------------------------------------------------------------------------------ plane leaf
+
+
+# The series order at which the plane leaf is evaluated, and the largest ||h A_planes||_inf for which that
+# order reproduces the closed form to float32 rounding: the truncation error of the level-2 local terms is
+# below series_error_bound(x, 2, q) = (2x)^(q+1) / (q+1)! e^(2x), 5.7e-9 relative at q = 11, x = 0.5.
+PLANE_Q = 11
+PLANE_X_MAX = 0.5
+
+
+def plane_generator(A: torch.Tensor) -> torch.Tensor:
+    """The generator whose local terms the plane leaf computes (ews/core/leaf.py:116-136 reads
+    d = A[2j, 2j] and w = A[2j, 2j+1] of each 2x2 plane and treats the plane as [[d, w], [-w, d]]): a
+    block-diagonal matrix of those rotation-scaling blocks. Differentiable in A."""
+    N = A.shape[-1]
+    ii = torch.arange(0, N, 2, device=A.device)
+    d = A[ii, ii]
+    w = A[ii, ii + 1]
+    P = torch.zeros_like(A)
+    P[ii, ii] = d
+    P[ii + 1, ii + 1] = d
+    P[ii, ii + 1] = w
+    P[ii + 1, ii] = -w
+    return P
 
 
 # ------------------------------------------------------------------------------ Van Loan leaf tables

@@ -162,6 +162,12 @@ def test_layer_validation_mirrors_reference():
         EWS(AParamBlockDiag([torch.ones(2, 2)] * 2, [2, 2]), N=3)
     with pytest.raises(NotImplementedError):
         EWS(A, N=2, leaf="jordan_closed")
+    # the plane leaf (ews/core/leaf.py:116-136): depths 1-2, even dimension; the dense engine runs it
+    assert EWS(A, N=2, reweighting_mode="displacement_uniform", leaf="plane_closed").engine == "dense"
+    with pytest.raises(NotImplementedError):
+        EWS(AParamBlockDiag([torch.ones(2, 2)] * 2, [2, 2]), N=3, leaf="plane_closed")
+    with pytest.raises(ValueError):
+        EWS(torch.eye(3), N=2, leaf="plane_closed")
     layer = EWS(AParamEFM(torch.zeros(3)), N=2, reweighting_mode="displacement_uniform")
     assert layer.engine == "diag" and layer.block_sizes == (1, 1, 1)
     assert EWS(AParamBlockDiag([torch.ones(1, 1)] * 3, [1, 1, 1]), N=2, leaf="series", series_q=4).engine == "diag"

@@ -151,3 +151,79 @@ def test_config2_full_length():
     _assert_fwd(out, ref, ref32, elementwise=False)
     for name, a, b, c in zip(("path", "A", "lift"), gk, g64, g32):
         _assert_close(f"{name} grad", a, b, c)
+
+
+def _plane_case(B, T, K, d_in, seed=5, hmax=0.4):
+    """2x2 planes with general blocks [[a, w], [v, b]] (the plane leaf reads only a and w of each block),
+    uniform clock with ||h A_planes|| below the leaf's series range."""
+    rng = np.random.default_rng(seed)
+    N = 2 * K
+    inc = rng.normal(size=(B, T, d_in)) / np.sqrt(T)
+    path = np.concatenate([np.zeros((B, 1, d_in)), np.cumsum(inc, 1)], 1)
+    A = np.zeros((N, N))
+    for j in range(K):
+        a, b = rng.uniform(0.05, 1.0, size=2)
+        w, v = rng.uniform(-3.0, 3.0, size=2)
+        A[2 * j : 2 * j + 2, 2 * j : 2 * j + 2] = [[a, w], [v, b]]
+    lift = rng.normal(size=(N, d_in)) / np.sqrt(d_in)
+    planes = np.abs([A[2 * j, 2 * j] for j in range(K)]) + np.abs([A[2 * j, 2 * j + 1] for j in range(K)])
+    h = hmax / planes.max()
+    clock = np.broadcast_to(np.arange(T + 1) * h, (B, T + 1)).copy()
+    return _f32(path), _f32(clock), _f32(A), _f32(lift)
+
+
+@pytest.mark.parametrize("readout", ["prefix", "terminal"])
+def test_plane_closed_leaf_matches_oracle(readout):
+    """leaf='plane_closed' (ews/core/kernels/plane_engine.py:134-155, via ews/core/leaf.py:116-136) against the
+    oracle's closed form (complex phi and divided differences) in float64: outputs and the gradients of the
+    path, the generator and the lift."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import EWS, AParamGeneral
+
+    path, clock, A, lift = _plane_case(2, 96, 4, 3)
+    rng = np.random.default_rng(9)
+    L, N = path.shape[1], A.shape[0]
+    D = 1 + N + N * N
+    w = torch.tensor(rng.normal(size=(2, L - 1, D) if readout == "prefix" else (2, D)))
+    p64 = torch.tensor(path, requires_grad=True)
+    A64 = torch.tensor(A, requires_grad=True)
+    B64 = torch.tensor(lift, requires_grad=True)
+    ref = O.ews_layer(O.lift(p64, B64), torch.tensor(clock), A64, 2, leaf="plane_closed",
+                      reweighting_mode="displacement_uniform", readout=readout)
+    (ref * w).sum().backward()
+    Ap = AParamGeneral(torch.tensor(A, dtype=torch.float32)).to(DEV)
+    layer = EWS(Ap, N=2, reweighting_mode="displacement_uniform", leaf="plane_closed", combine="b200")
+    assert layer.engine == "dense"
+    p = torch.tensor(path, dtype=torch.float32, device=DEV, requires_grad=True)
+    Bm = torch.tensor(lift, dtype=torch.float32, device=DEV, requires_grad=True)
+    out = layer(p, torch.tensor(clock, dtype=torch.float32, device=DEV), readout=readout, lift=Bm)
+    (out * w.to(DEV, torch.float32)).sum().backward()
+    torch.cuda.synchronize()
+    _assert_close("forward", out.detach().cpu().double(), ref.detach())
+    _assert_close("d path", p.grad.cpu().double(), p64.grad)
+    _assert_close("d A", Ap.matrix.grad.cpu().double(), A64.grad)
+    _assert_close("d lift", Bm.grad.cpu().double(), B64.grad)
+
+
+def test_plane_closed_range_guard_raises_on_the_next_call():
+    """Outside ||h A|| <= PLANE_X_MAX the series evaluation of the plane leaf is not the closed form: the
+    device-side check records it and an engine call raises at the latest on the next call (no host
+    synchronisation in the call itself)."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import EWS, AParamGeneral, engine
+
+    path, clock, A, lift = _plane_case(1, 32, 2, 2, hmax=3.0)
+    Ap = AParamGeneral(torch.tensor(A, dtype=torch.float32)).to(DEV)
+    layer = EWS(Ap, N=2, reweighting_mode="displacement_uniform", leaf="plane_closed", combine="b200")
+    p = torch.tensor(path, dtype=torch.float32, device=DEV)
+    c = torch.tensor(clock, dtype=torch.float32, device=DEV)
+    Bm = torch.tensor(lift, dtype=torch.float32, device=DEV)
+    try:
+        with pytest.raises(NotImplementedError, match="plane_closed"):
+            layer(p, c, readout="prefix", lift=Bm)  # may already raise: the flag's copy can land before the call
+            torch.cuda.synchronize()
+            layer(p, c, readout="prefix", lift=Bm)
+    finally:
+        for slot in engine._GUARD.values():
+            slot[0].zero_()
+            slot[1].zero_()
