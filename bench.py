@@ -698,7 +698,7 @@ def main():
 
         torch.cuda.set_device(local_rank)
         # NCCL's own initialisation lines (rank / nranks per communicator) confirm the N-rank run in the log
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ["NCCL_DEBUG"] = "INFO"  # the image presets VERSION; the INFO lines record the ranks
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     try:
         run_b200(args, rank, world, local_rank)
