@@ -9,10 +9,13 @@
 // s1 = sum_p c_p P_p dy = K1 dy and s2 = sum_a (P_a dy)(K2_a dy)^T with K2_a = sum_b c_ab P_b; the lift W
 // is folded into F = K1 W, G_a = P_a W, H_a = K2_a W by the caller.
 //
-// Work decomposition: one CTA of 64 threads owns one tile (sample, chunk). Thread (bi, bj) holds the 4x4
-// block (rows 4bi.., cols 4bj..) of every 32x32 matrix; a 32x32x32 product reads two float4 operands per k
-// from shared memory (A k-major, B row-major) into 16 FMAs. Chunks are combined with the decoupled
-// look-back of the diagonal engine (chunk aggregates (I - M^L, S1, S2), Chen products by GEMMs).
+// Work decomposition. Forward: the local terms of every interval (local_kernel), the power complements
+// I - M^j (powers_kernel), every chunk's zero-carry aggregate as a parallel map (agg_kernel), the carries by
+// a two-level scan over the chunks (scan_local, log-depth rounds over the groups, scan_fix), then the output
+// pass on tcgen05 (fwd_tc_kernel: four chunks of a sample stacked into M = 128, two 3xTF32 products per
+// step). Backward: the zero-carry adjoint pass (bwd_tc_kernel), the reverse scan of the local adjoints
+// (bscan_*), the exact adjoint pass with the gradient map fused in (bwd_exact_kernel), the table gradients
+// (table_grad_*) and a fixed-order reduction. No kernel waits on another CTA.
 //
 // Flows are carried as complements D = I - M (the caller evaluates D in float64): M X = X - D X. An M
 // within 1e-4 of the identity, rounded once and applied T times, drifts by ~T 2^-24; the complement keeps
@@ -34,12 +37,10 @@ struct Geom {
     int B, T, d_in, N, Lc, C, W, SW, QP, readout;
     unsigned flags;
     int spin_limit;
-    int SR, ntiles;
+    int ntiles;
     int agg_pre;      // forward: the chunk aggregates come from agg_kernel (the chain runs the output pass only)
     int bwd_mode;     // backward chain: 1 = the zero-carry pass only (local adjoints), 2 = the exact pass only
     int tab_n;        // floats of the F, G, H tables (N x d_in each, padded to NP rows)
-    int smem_floats;  // forward
-    int bsmem_floats; // backward
 };
 
 struct Params {
@@ -122,182 +123,6 @@ __device__ __forceinline__ void load_rowmajor(const float* M, float blk[4][4], i
     }
 }
 
-// ---------------------------------------------------------------------------------- shared memory
-
-struct Smem {
-    float* Mr;   // D = I - M row-major
-    float* Mt;   // D k-major
-    float* A0;   // work matrices
-    float* A1;
-    float* A2;
-    float* A3;
-    float* A4;
-    float* A5;
-    float* S1;   // level 1 (NP)
-    float* u;    // M S1 (NP)
-    float* s1;   // local level 1 (NP)
-    float* v0;   // scratch vectors (NP each)
-    float* v1;
-    float* U;    // NP x QP (row-major, stride QMAX)
-    float* V;
-    float* F;    // NP x d_in
-    float* G;    // QP x NP x d_in
-    float* H;
-    float* dx;   // Lc x d_in
-    float* stage;
-    float* stage2;
-    float* red;  // backward: [du (NP) | dU (NP*QMAX) | ds1 (NP) | dV (NP*QMAX)]
-    float* tacc; // backward: table-gradient accumulators of the tile ((1+2QP) NP d_in)
-    float* ddx;  // backward: dx gradient rows of the chunk (Lc x d_in)
-    int* bcast;
-};
-
-__device__ Smem carve(float* base, const Geom& g, bool bwd) {
-    Smem s;
-    float* p = base;
-    s.Mr = p; p += MM;
-    s.Mt = p; p += MM;
-    s.A0 = p; p += MM;
-    s.A1 = p; p += MM;
-    s.A2 = p; p += MM;
-    s.A3 = p; p += MM;
-    s.A4 = p; p += MM;
-    s.A5 = p; p += MM;
-    s.S1 = p; p += NP;
-    s.u = p; p += NP;
-    s.s1 = p; p += NP;
-    s.v0 = p; p += NP;
-    s.v1 = p; p += NP;
-    s.U = p; p += NP * QMAX;
-    s.V = p; p += NP * QMAX;
-    s.F = p; p += align4(NP * g.d_in);
-    s.G = p; p += align4(g.QP * NP * g.d_in);
-    s.H = p; p += align4(g.QP * NP * g.d_in);
-    s.dx = p; p += align4(g.Lc * g.d_in);
-    const int st_n = align4(imax(imax(g.SR * g.W, g.Lc * g.d_in), 2 * MM));
-    s.stage = p; p += st_n;
-    s.stage2 = p; p += bwd ? align4(g.SR * g.W) : 0;
-    s.red = p; p += bwd ? 2 * NP * (QMAX + 1) : 0;
-    s.tacc = p; p += bwd ? align4((1 + 2 * g.QP) * NP * g.d_in) : 0;
-    s.ddx = p; p += bwd ? align4(g.Lc * g.d_in) : 0;
-    s.bcast = reinterpret_cast<int*>(p);
-    return s;
-}
-
-__host__ int smem_floats(const Geom& g, bool bwd) {
-    int n = 8 * MM + 5 * NP + 2 * NP * QMAX + align4(NP * g.d_in) + 2 * align4(g.QP * NP * g.d_in) +
-            align4(g.Lc * g.d_in) + align4(imax(imax(g.SR * g.W, g.Lc * g.d_in), 2 * MM));
-    if (bwd)
-        n += align4(g.SR * g.W) + 2 * NP * (QMAX + 1) + align4((1 + 2 * g.QP) * NP * g.d_in) + align4(g.Lc * g.d_in);
-    return n + 4;
-}
-
-// Loads the per-sample tables (D padded with zeros, i.e. the identity flow, F/G/H with zero rows).
-__device__ void load_tables(const Params& p, const Smem& s, int b) {
-    const Geom& g = p.g;
-    const int N = g.N, d = g.d_in;
-    const float* m = p.tab_d + (size_t)b * N * N;
-    for (int e = threadIdx.x; e < MM; e += blockDim.x) {
-        const int i = e / NP, k = e - i * NP;
-        const float v = (i < N && k < N) ? m[i * N + k] : 0.f;
-        s.Mr[i * NP + k] = v;
-        s.Mt[k * NP + i] = v;
-    }
-    const float* f = p.tab_f + (size_t)b * N * d;
-    for (int e = threadIdx.x; e < NP * d; e += blockDim.x) {
-        const int i = e / d;
-        s.F[e] = i < N ? f[e - i * d + i * d] : 0.f;
-    }
-    const size_t gq = (size_t)g.QP * N * d;
-    const float* gg = p.tab_g + (size_t)b * gq;
-    const float* hh = p.tab_h + (size_t)b * gq;
-    for (int e = threadIdx.x; e < g.QP * NP * d; e += blockDim.x) {
-        const int a = e / (NP * d), r = e - a * NP * d, i = r / d, c = r - i * d;
-        const bool ok = i < N;
-        s.G[e] = ok ? gg[((size_t)a * N + i) * d + c] : 0.f;
-        s.H[e] = ok ? hh[((size_t)a * N + i) * d + c] : 0.f;
-    }
-}
-
-__device__ void load_dx(const Params& p, const Smem& s, int b, int t0, int n) {
-    const Geom& g = p.g;
-    for (int e = threadIdx.x; e < n * g.d_in; e += blockDim.x) {
-        const int k = e / g.d_in, c = e - k * g.d_in;
-        s.dx[e] = input_increment(p.path, b, t0 + k, c, g.T, g.d_in, g.flags);
-    }
-}
-
-// Local vectors of step k: s1 = F dx, U = [G_a dx], V = [H_a dx]; and u = M S1 (from s.S1).
-__device__ void local_terms(const Geom& g, const Smem& s, int k) {
-    const float* x = s.dx + k * g.d_in;
-    const int tid = threadIdx.x;
-    // thread i < 32: s1_i and u_i; threads handle U/V entries round robin
-    if (tid < NP) {
-        float acc = 0.f;
-        for (int c = 0; c < g.d_in; ++c) acc = fmaf(s.F[tid * g.d_in + c], x[c], acc);
-        s.s1[tid] = acc;
-    } else {
-        const int i = tid - NP;
-        float acc = 0.f;
-#pragma unroll 8
-        for (int kk = 0; kk < NP; ++kk) acc = fmaf(s.Mt[kk * NP + i], s.S1[kk], acc);
-        s.u[i] = s.S1[i] - acc;  // M S1 = S1 - D S1
-    }
-    for (int e = tid; e < 2 * g.QP * NP; e += blockDim.x) {
-        const int which = e / (g.QP * NP), r = e - which * g.QP * NP, a = r / NP, i = r - a * NP;
-        const float* T = (which == 0 ? s.G : s.H) + ((size_t)a * NP + i) * g.d_in;
-        float acc = 0.f;
-        for (int c = 0; c < g.d_in; ++c) acc = fmaf(T[c], x[c], acc);
-        (which == 0 ? s.U : s.V)[i * QMAX + a] = acc;
-    }
-}
-
-// One forward step on the thread's block: S2 (regs, also s.A0 k-major) <- M S2 M^T + u s1^T + U V^T.
-// Uses s.A1 for X = S2 M^T. Three barriers.
-__device__ void fwd_step(const Geom& g, const Smem& s, int k, float S2[4][4], int i0, int j0) {
-    local_terms(g, s, k);
-    __syncthreads();
-    float X[4][4], Y[4][4];
-    gemm44(s.A0, s.Mt, X, i0, j0, false);  // S2 D^T   (A = S2 k-major, B[k][j] = D[j][k])
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) X[r][c] = S2[r][c] - X[r][c];  // X = S2 M^T
-    store_rowmajor(s.A1, X, i0, j0);
-    __syncthreads();
-    gemm44(s.Mt, s.A1, Y, i0, j0, false);  // D X      (A = D k-major, B = X row-major)
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const float ur = s.u[i0 + r];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            float acc = fmaf(ur, s.s1[j0 + c], X[r][c] - Y[r][c]);  // M X = X - D X
-            for (int a = 0; a < g.QP; ++a) acc = fmaf(s.U[(i0 + r) * QMAX + a], s.V[(j0 + c) * QMAX + a], acc);
-            S2[r][c] = acc;
-        }
-    }
-    if (threadIdx.x < NP) s.S1[threadIdx.x] = s.u[threadIdx.x] + s.s1[threadIdx.x];
-    store_kmajor(s.A0, S2, i0, j0);
-    __syncthreads();
-}
-
-// Writes row [1, S1, S2] (real dimension N) into a staged row.
-__device__ void stage_row(const Geom& g, const Smem& s, float* row, const float S2[4][4], int i0, int j0) {
-    const int N = g.N;
-    if (threadIdx.x == 0) row[0] = 1.f;
-    if (threadIdx.x < N) row[1 + threadIdx.x] = s.S1[threadIdx.x];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int i = i0 + r;
-        if (i >= N) continue;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int j = j0 + c;
-            if (j < N) row[1 + N + i * N + j] = S2[r][c];
-        }
-    }
-}
-
 // ---------------------------------------------------------------------------------- Chen elements
 // Slot layout (floats): [P row-major (NP*NP) | S1 (NP) | S2 row-major (NP*NP)].
 
@@ -307,61 +132,6 @@ __device__ void store_slot(float* slot, const float* Pr, const float* S1, const 
         slot[MM + NP + e] = S2r[e];
     }
     if (threadIdx.x < NP) slot[MM + threadIdx.x] = S1[threadIdx.x];
-}
-
-// out = L (x) R with L, R given as (flow complement C row-major, S1, S2 row-major) in shared memory; result
-// written to (Co, S1o, S2o) row-major (outputs may alias the inputs). With P_R = I - C_R:
-//   S2 = P_R L2 P_R^T + (P_R L1) R1^T + R2,  S1 = P_R L1 + R1,  C = C_L + C_R - C_R C_L.
-// Needs two scratch matrices T0, T1 and a vector vtmp. Barrier-complete on return.
-__device__ void chen_mul_smem(const float* PL, const float* L1, const float* L2, const float* PR, const float* R1,
-                              const float* R2, float* Po, float* S1o, float* S2o, float* T0, float* T1, float* vtmp,
-                              int i0, int j0) {
-    for (int e = threadIdx.x; e < MM; e += blockDim.x) {
-        const int i = e / NP, k = e - i * NP;
-        T0[k * NP + i] = L2[e];   // L2 k-major
-        T1[k * NP + i] = PR[e];   // C_R k-major
-    }
-    if (threadIdx.x < NP) {
-        float acc = 0.f;
-        for (int k = 0; k < NP; ++k) acc = fmaf(PR[threadIdx.x * NP + k], L1[k], acc);
-        vtmp[threadIdx.x] = L1[threadIdx.x] - acc;  // P_R L1
-    }
-    __syncthreads();
-    const bool act = threadIdx.x < NT;  // 4x4 blocks of the first 64 threads cover the 32x32 matrices
-    float L2b[4][4], CLb[4][4], CRb[4][4];
-    float X[4][4], Y[4][4], P[4][4];
-    if (act) {
-        load_rowmajor(L2, L2b, i0, j0);
-        load_rowmajor(PL, CLb, i0, j0);
-        load_rowmajor(PR, CRb, i0, j0);
-        gemm44(T0, T1, X, i0, j0, false);  // L2 C_R^T
-        gemm44(T1, PL, P, i0, j0, false);  // C_R C_L
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                X[r][c] = L2b[r][c] - X[r][c];                  // X = L2 P_R^T
-                P[r][c] = CLb[r][c] + CRb[r][c] - P[r][c];      // complement of P_R P_L
-            }
-    }
-    __syncthreads();
-    if (act) store_rowmajor(T0, X, i0, j0);
-    __syncthreads();
-    if (act) {
-        gemm44(T1, T0, Y, i0, j0, false);  // C_R X
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                Y[r][c] = (X[r][c] - Y[r][c]) + fmaf(vtmp[i0 + r], R1[j0 + c], R2[(i0 + r) * NP + j0 + c]);
-    }
-    __syncthreads();
-    if (act) {
-        store_rowmajor(S2o, Y, i0, j0);
-        store_rowmajor(Po, P, i0, j0);
-    }
-    if (threadIdx.x < NP) S1o[threadIdx.x] = vtmp[threadIdx.x] + R1[threadIdx.x];
-    __syncthreads();
 }
 
 __device__ void load_slot_smem(const float* slot, float* P, float* S1, float* S2) {
@@ -379,183 +149,6 @@ __device__ void identity_smem(float* P, float* S1, float* S2) {
     }
     if (threadIdx.x < NP) S1[threadIdx.x] = 0.f;
 }
-
-// CTA-wide ticket and bounded flag wait (thread 0 polls; the warp-level helpers act on warp 0).
-__device__ int cta_ticket(const Params& p, const Smem& s) {
-    if (threadIdx.x == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
-    __syncthreads();
-    const int t = s.bcast[0];
-    __syncthreads();
-    return t;
-}
-
-__device__ int cta_wait(const Params& p, const Smem& s, const int* flag, int want, int tile) {
-    if (threadIdx.x < 32) {
-        const int v = wait_slot(flag, p.st, p.g.spin_limit, tile, want);
-        if (threadIdx.x == 0) s.bcast[0] = v;
-    }
-    __syncthreads();
-    const int v = s.bcast[0];
-    __threadfence();
-    __syncthreads();
-    return v;
-}
-
-__device__ void cta_publish(int* flag, int value) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) st_release(flag, value);
-}
-
-// ---------------------------------------------------------------------------------- forward kernel
-
-__global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
-    extern __shared__ float smem[];
-    const Geom& g = p.g;
-    Smem s = carve(smem, g, false);
-    const int bi = threadIdx.x >> 3, bj = threadIdx.x & 7;
-    const int i0 = 4 * bi, j0 = 4 * bj;
-    const bool deterministic = (g.flags & EWS_F_DETERMINISTIC) != 0;
-    for (;;) {
-        const int tile = cta_ticket(p, s);
-        if (tile >= g.ntiles) break;
-        const int c = tile / g.B, b = tile - c * g.B;
-        const int t0 = c * g.Lc;
-        const int len = min(g.Lc, g.T - t0);
-        load_tables(p, s, b);
-        load_dx(p, s, b, t0, len);
-        // pass 1: aggregate from the identity (state S2 in regs + s.A0 k-major, S1 in s.S1)
-        float S2[4][4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) S2[r][q] = 0.f;
-        store_kmajor(s.A0, S2, i0, j0);
-        if (threadIdx.x < NP) s.S1[threadIdx.x] = 0.f;
-        __syncthreads();
-        for (int k = 0; k < len; ++k) fwd_step(g, s, k, S2, i0, j0);
-        // aggregate (C = I - M^len by binary powering of complements, S1, S2) -> A2 (C), v0 (S1), A3 (S2)
-        store_rowmajor(s.A3, S2, i0, j0);
-        if (threadIdx.x < NP) s.v0[threadIdx.x] = s.S1[threadIdx.x];
-        {
-            // R = 0 (identity); base = D (row-major in A4, k-major in A5)
-            for (int e = threadIdx.x; e < MM; e += blockDim.x) {
-                s.A2[e] = 0.f;
-                s.A4[e] = s.Mr[e];
-                s.A5[e] = s.Mt[e];
-            }
-            __syncthreads();
-            int e = len;
-            while (e > 0) {
-                float blk[4][4], Rb[4][4], Bb[4][4];
-                load_rowmajor(s.A4, Bb, i0, j0);
-                if (e & 1) {
-                    load_rowmajor(s.A2, Rb, i0, j0);
-                    gemm44(s.A5, s.A2, blk, i0, j0, false);  // base R
-                    __syncthreads();
-#pragma unroll
-                    for (int r = 0; r < 4; ++r)
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) blk[r][q] = Rb[r][q] + Bb[r][q] - blk[r][q];
-                    store_rowmajor(s.A2, blk, i0, j0);
-                    __syncthreads();
-                }
-                e >>= 1;
-                if (e > 0) {
-                    gemm44(s.A5, s.A4, blk, i0, j0, false);  // base base
-                    __syncthreads();
-#pragma unroll
-                    for (int r = 0; r < 4; ++r)
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) blk[r][q] = 2.f * Bb[r][q] - blk[r][q];
-                    store_rowmajor(s.A4, blk, i0, j0);
-                    store_kmajor(s.A5, blk, i0, j0);
-                    __syncthreads();
-                }
-            }
-        }
-        const size_t slot = ((size_t)b * g.C + c) * g.SW;
-        int* flag = p.flags + (size_t)b * g.C + c;
-        store_slot(p.agg + slot, s.A2, s.v0, s.A3);
-        // exclusive prefix -> (A4 P, v1 S1, A5 S2) via look-back
-        if (c == 0) {
-            store_slot(p.incl + slot, s.A2, s.v0, s.A3);
-            if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(flag, kFlagIncl);
-            identity_smem(s.A4, s.v1, s.A5);
-            __syncthreads();
-        } else {
-            cta_publish(flag, kFlagAgg);
-            // acc (A4, v1, A5) = identity; X loaded into (A0.., ) -- A0 is free now
-            identity_smem(s.A4, s.v1, s.A5);
-            __syncthreads();
-            int j = c - 1;
-            for (;;) {
-                const int f = cta_wait(p, s, p.flags + (size_t)b * g.C + j, deterministic ? kFlagIncl : kFlagAgg, tile);
-                if (f < 0) return;
-                const size_t sj = ((size_t)b * g.C + j) * g.SW;
-                // X -> (A0 P, u S1, A1 S2); acc <- X (x) acc
-                load_slot_smem((f == kFlagIncl ? p.incl : p.agg) + sj, s.A0, s.u, s.A1);
-                __syncthreads();
-                chen_mul_smem(s.A0, s.u, s.A1, s.A4, s.v1, s.A5, s.A4, s.v1, s.A5, s.stage, s.stage + MM, s.s1, i0, j0);
-                if (f == kFlagIncl) break;
-                --j;
-            }
-            // incl = excl (x) agg -> (A0, u, A1)
-            chen_mul_smem(s.A4, s.v1, s.A5, s.A2, s.v0, s.A3, s.A0, s.u, s.A1, s.stage, s.stage + MM, s.s1, i0, j0);
-            store_slot(p.incl + slot, s.A0, s.u, s.A1);
-            cta_publish(flag, kFlagIncl);
-        }
-        __syncthreads();
-        store_slot(p.carry + slot, s.A4, s.v1, s.A5);
-        if (g.readout == EWS_READOUT_TERMINAL) {
-            if (c == g.C - 1) {
-                // final = excl (x) agg, staged as one row
-                chen_mul_smem(s.A4, s.v1, s.A5, s.A2, s.v0, s.A3, s.A0, s.u, s.A1, s.stage, s.stage + MM, s.s1, i0, j0);
-                float fin[4][4];
-                load_rowmajor(s.A1, fin, i0, j0);
-                if (threadIdx.x < NP) s.S1[threadIdx.x] = s.u[threadIdx.x];
-                __syncthreads();
-                stage_row(g, s, s.stage, fin, i0, j0);
-                __syncthreads();
-                if (threadIdx.x < 32) warp_store_span(p.out + (size_t)b * g.W, s.stage, g.W);
-                __syncthreads();
-            }
-            continue;
-        }
-        // pass 2 from the carry, emitting prefix rows
-        load_rowmajor(s.A5, S2, i0, j0);
-        __syncthreads();
-        store_kmajor(s.A0, S2, i0, j0);
-        if (threadIdx.x < NP) s.S1[threadIdx.x] = s.v1[threadIdx.x];
-        __syncthreads();
-        int k0 = 0;
-        for (int k = 0; k < len; ++k) {
-            fwd_step(g, s, k, S2, i0, j0);
-            stage_row(g, s, s.stage + (k - k0) * g.W, S2, i0, j0);
-            if (k - k0 == g.SR - 1 || k == len - 1) {
-                __syncthreads();
-                if (threadIdx.x < 32)
-                    warp_store_span(p.out + ((size_t)b * g.T + t0 + k0) * g.W, s.stage, (k - k0 + 1) * g.W);
-                __syncthreads();
-                k0 = k + 1;
-            }
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------------- forward on tcgen05
-//
-// The flow products run on the 5th-generation tensor cores. A CTA of 4 warps stacks 4 consecutive chunks of
-// one sample (tile t = warp t); the two products of a step are single tcgen05.mma chains with M = 128 (the
-// 4 stacked 32-row tiles), N = 32, K = 32, in 3xTF32 (hi/lo splits, K-concatenated: a_hi b_hi + a_hi b_lo +
-// a_lo b_hi), accumulated in TMEM:
-//     P1 = S2 D^T        (A = S2, MN-major, written column by column)   -> X  = S2 - P1       (rows)
-//     P2 = (D X)^T       (A = X^T, MN-major, written row by row)        -> MX = X - P2^T      (columns)
-// The identity parts are exact fp32 subtractions on the CUDA cores, so the flow keeps its complement form.
-// After MMA1 lane i of warp t owns row i of tile t (TMEM lane 32t+i), after MMA2 it owns column i. Both A
-// operands are K-major (a row of A per lane, 16-byte stores); the orientation a lane needs next comes
-// through a warp-private padded 33-stride buffer (conflict-free by rows and by columns). One elected
-// thread issues the MMAs and commits them to an mbarrier; the waits are bounded.
 
 namespace tc {
 
@@ -656,14 +249,12 @@ __device__ __forceinline__ void store_a_row(float* Ahi, float* Alo, int m, const
 struct TcSmem {
     float* Bhi;   // D hi, K-major (MM)
     float* Blo;   // D lo
-    float* Ahi;   // A operand hi, K-major (4 MM); also look-back scratch
+    float* Ahi;   // A operand hi, K-major (4 MM)
     float* Alo;   // A operand lo
     float* RQ;    // TILES x 32 x RQS exchange buffer
-    float* stage; // TILES x W prefix rows; also look-back scratch (>= 2 MM)
-    float* Dr;    // D row-major
-    float* Dt;    // D k-major
+    float* Dr;    // D row-major (or null)
+    float* Dt;    // D k-major (or null)
     float* vec;   // per tile: S1 (l1) | u (v) | two staging slots of local terms
-    float* misc;  // small vectors for the look-back
     uint64_t* bar;
     uint32_t* tmem;
     int* bcast;
@@ -671,36 +262,6 @@ struct TcSmem {
 
 // Per-tile vectors: S1 (or l1) | u (or v) | two staging slots for an interval's local terms.
 __host__ __device__ inline int vec_per_tile(int QP) { return 2 * NP + 2 * loc_width(QP); }
-
-// Per-tile stage stride: a prefix row, or the tile's saved level-2 state while its chunk has ended.
-__host__ __device__ inline int tc_stage_stride(int W) { return align4(imax(W, MM)); }
-__host__ __device__ inline int tc_stage_floats(int W) { return TILES * tc_stage_stride(W); }
-
-__host__ __device__ inline size_t tc_smem_bytes(int W, int QP) {
-    size_t f = 2 * MM + 2 * 4 * MM + TILES * 32 * RQS + align4(tc_stage_floats(W)) + 2 * MM +
-               TILES * vec_per_tile(QP) + 8 * NP;
-    return f * sizeof(float) + 64 + 128;  // + barrier / tmem slot / broadcast, + alignment slack
-}
-
-__device__ TcSmem tc_carve(unsigned char* raw, const Geom& g) {
-    uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 127) & ~(uintptr_t)127;
-    float* p = reinterpret_cast<float*>(base);
-    TcSmem s;
-    s.Bhi = p; p += MM;
-    s.Blo = p; p += MM;
-    s.Ahi = p; p += 4 * MM;
-    s.Alo = p; p += 4 * MM;
-    s.RQ = p; p += TILES * 32 * RQS;
-    s.stage = p; p += align4(tc_stage_floats(g.W));
-    s.Dr = p; p += MM;
-    s.Dt = p; p += MM;
-    s.vec = p; p += TILES * vec_per_tile(g.QP);
-    s.misc = p; p += 8 * NP;
-    s.bar = reinterpret_cast<uint64_t*>(p);
-    s.tmem = reinterpret_cast<uint32_t*>(p + 2);
-    s.bcast = reinterpret_cast<int*>(p + 4);
-    return s;
-}
 
 // Flow table of sample b; the B operand is D (forward) or D^T (the adjoint chain, transpose = true).
 __device__ void tc_load_tables(const Params& p, const TcSmem& s, int b, bool transpose = false) {
@@ -849,18 +410,6 @@ __device__ bool tc_wait(const TcSmem& s, uint32_t parity, int limit) {
     const bool ok = s.bcast[1] != 0;
     fence_after();
     return ok;
-}
-
-__device__ int tc_cta_wait(const Params& p, const TcSmem& s, const int* flag, int want, int tile) {
-    if (threadIdx.x < 32) {
-        const int v = wait_slot(flag, p.st, p.g.spin_limit, tile, want);
-        if (threadIdx.x == 0) s.bcast[2] = v;
-    }
-    __syncthreads();
-    const int v = s.bcast[2];
-    __threadfence();
-    __syncthreads();
-    return v;
 }
 
 }  // namespace tc
@@ -1369,7 +918,8 @@ __device__ __forceinline__ void st22(float* M, const float v[2][2], int i0, int 
     *reinterpret_cast<float2*>(M + (i0 + 1) * NP + j0) = make_float2(v[1][0], v[1][1]);
 }
 
-// (Po, S1o, S2o) = (PL, L1, L2) (x) (PR, R1, R2), flows as complements (the same product as chen_mul_smem).
+// (Po, S1o, S2o) = (PL, L1, L2) (x) (PR, R1, R2), flows as complements:
+//   S2 = P_R L2 P_R^T + (P_R L1) R1^T + R2,  S1 = P_R L1 + R1,  C = C_L + C_R - C_R C_L  (P_R = I - C_R).
 // Outputs may alias either operand. Scratch T0, T1 (MM), vtmp (NP). Barrier-complete on return.
 __device__ void chen_mul_256(const float* PL, const float* L1, const float* L2, const float* PR, const float* R1,
                              const float* R2, float* Po, float* S1o, float* S2o, float* T0, float* T1, float* vtmp) {
@@ -1554,42 +1104,6 @@ __global__ void __launch_bounds__(CST) scan_fix_kernel(Params p) {
 
 // ---------------------------------------------------------------------------------- backward
 
-// Transposed map of right-multiplication by G = (P, U1, U2), P = I - C, applied to the cotangent (L1 in
-// smem, L2 block regs + row-major copy in L2r): L2 <- P^T L2 P, L1 <- P^T (L1 + L2 U1). C row-major in Pr,
-// U1 in U1v. Scratch T0 (matrix), T1 (vector), vt. Barrier-complete on return.
-__device__ void apply_JT_smem(const float* Pr, const float* U1v, float* L1, float L2[4][4], float* L2r, float* T0,
-                              float* T1, float* vt, int i0, int j0) {
-    if (threadIdx.x < NP) {
-        float acc = 0.f;
-        for (int k = 0; k < NP; ++k) acc = fmaf(L2r[threadIdx.x * NP + k], U1v[k], acc);
-        vt[threadIdx.x] = L1[threadIdx.x] + acc;
-    }
-    // Z = P^T L2 = L2 - C^T L2  (A = C^T: k-major of C^T is C row-major)
-    float Z[4][4];
-    gemm44(Pr, L2r, Z, i0, j0, false);
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) Z[r][c] = L2[r][c] - Z[r][c];
-    __syncthreads();
-    store_kmajor(T0, Z, i0, j0);
-    if (threadIdx.x < NP) {
-        float acc = 0.f;
-        for (int k = 0; k < NP; ++k) acc = fmaf(Pr[k * NP + threadIdx.x], vt[k], acc);
-        T1[threadIdx.x] = vt[threadIdx.x] - acc;  // P^T (L1 + w)
-    }
-    __syncthreads();
-    gemm44(T0, Pr, L2, i0, j0, false);  // Z C
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) L2[r][c] = Z[r][c] - L2[r][c];  // Z P
-    __syncthreads();
-    store_rowmajor(L2r, L2, i0, j0);
-    if (threadIdx.x < NP) L1[threadIdx.x] = T1[threadIdx.x];
-    __syncthreads();
-}
-
 // The backward's carries by a two-level reverse scan, the counterpart of the forward's (scan_*_kernel).
 // The element of a range of chunks is (G, mu): the forward aggregate G of the range and the cotangent mu at
 // the range's start from the range's own output gradients (zero carry). An earlier range a and a later b
@@ -1709,286 +1223,6 @@ __global__ void __launch_bounds__(CST) bscan_fix_kernel(Params p) {
     }
     bscan_store_lam(p.lcarry + (base + c) * g.SW, sm);
 }
-
-// Adds a gradient row (real dims) to the cotangent (L1 vector, L2 block regs).
-__device__ void add_grad_row(const Geom& g, const float* row, float* L1, float L2[4][4], int i0, int j0) {
-    const int N = g.N;
-    if (threadIdx.x < N) L1[threadIdx.x] += row[1 + threadIdx.x];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int i = i0 + r;
-        if (i >= N) continue;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int j = j0 + c;
-            if (j < N) L2[r][c] += row[1 + N + i * N + j];
-        }
-    }
-}
-
-__device__ void read_state_row(const Geom& g, const float* row, float* S1, float S2[4][4], int i0, int j0) {
-    const int N = g.N;
-    if (threadIdx.x < NP) S1[threadIdx.x] = threadIdx.x < N ? row[1 + threadIdx.x] : 0.f;
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int i = i0 + r, j = j0 + c;
-            S2[r][c] = (i < N && j < N) ? row[1 + N + i * N + j] : 0.f;
-        }
-}
-
-// The transposed step alone: L2 <- M^T L2 M, L1 <- M^T (L1 + L2 s1). Uses local_terms for s1.
-__device__ void adj_step(const Geom& g, const Smem& s, int k, float* L1, float L2[4][4], int i0, int j0) {
-    local_terms(g, s, k);  // s1 (and u, U, V, unused here)
-    store_rowmajor(s.A1, L2, i0, j0);
-    __syncthreads();
-    apply_JT_smem(s.Mr, s.s1, L1, L2, s.A1, s.A2, s.A3, s.v0, i0, j0);
-}
-
-__global__ void __launch_bounds__(NT) bwd_kernel(Params p) {
-    extern __shared__ float smem[];
-    const Geom& g = p.g;
-    Smem s = carve(smem, g, true);
-    const int bi = threadIdx.x >> 3, bj = threadIdx.x & 7;
-    const int i0 = 4 * bi, j0 = 4 * bj;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool deterministic = (g.flags & EWS_F_DETERMINISTIC) != 0;
-    float* L1 = s.v1;  // cotangent of level 1
-    for (;;) {
-        const int tile = cta_ticket(p, s);
-        if (tile >= g.ntiles) break;
-        const int cr = tile / g.B, b = tile - cr * g.B;
-        const int c = g.C - 1 - cr;
-        const int t0 = c * g.Lc;
-        const int len = min(g.Lc, g.T - t0);
-        load_tables(p, s, b);
-        load_dx(p, s, b, t0, len);
-        __syncthreads();
-        const size_t slot = ((size_t)b * g.C + c) * g.SW;
-        int* flag = p.flags + (size_t)b * g.C + c;
-
-        // ---- 1. zero-carry local adjoint (mu): L1 in s.v1, L2 block regs (+ row-major in A1 inside adj_step)
-        float L2[4][4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) L2[r][q] = 0.f;
-        if (threadIdx.x < NP) L1[threadIdx.x] = 0.f;
-        __syncthreads();
-        for (int kb = len; kb > 0; kb -= g.SR) {
-            const int k0 = max(0, kb - g.SR);
-            __syncthreads();
-            if (threadIdx.x < 32) warp_load_span(s.stage, p.grad_out + ((size_t)b * g.T + t0 + k0) * g.W, (kb - k0) * g.W);
-            __syncthreads();
-            for (int k = kb - 1; k >= k0; --k) {
-                add_grad_row(g, s.stage + (k - k0) * g.W, L1, L2, i0, j0);
-                __syncthreads();
-                adj_step(g, s, k, L1, L2, i0, j0);
-            }
-        }
-        // mu -> slot layout [L1 (NP) in the S1 position, L2 row-major in the S2 position]
-        store_rowmajor(s.A1, L2, i0, j0);
-        __syncthreads();
-        {
-            float* dst = (c == g.C - 1 ? p.incl : p.agg) + slot;
-            for (int e = threadIdx.x; e < MM; e += blockDim.x) dst[MM + NP + e] = s.A1[e];
-            if (threadIdx.x < NP) dst[MM + threadIdx.x] = L1[threadIdx.x];
-        }
-        // ---- 2. look-back over later chunks: Lam_in (L1 in s.u, L2 row-major in s.A4)
-        for (int e = threadIdx.x; e < MM; e += blockDim.x) s.A4[e] = 0.f;
-        if (threadIdx.x < NP) s.u[threadIdx.x] = 0.f;
-        if (c == g.C - 1) {
-            if (!(g.flags & EWS_F_TEST_WITHHOLD)) cta_publish(flag, kFlagIncl);
-            __syncthreads();
-        } else {
-            cta_publish(flag, kFlagAgg);
-            __syncthreads();
-            // Gacc = identity in (A5 P, v0 S1, A0 S2)
-            identity_smem(s.A5, s.v0, s.A0);
-            __syncthreads();
-            int j = c + 1;
-            for (;;) {
-                const int f = cta_wait(p, s, p.flags + (size_t)b * g.C + j, deterministic ? kFlagIncl : kFlagAgg, tile);
-                if (f < 0) return;
-                const size_t sj = ((size_t)b * g.C + j) * g.SW;
-                // X (cotangent) -> (s1 L1, A1 L2 row-major), then X <- J(Gacc)^T X, acc += X
-                {
-                    const float* src = (f == kFlagIncl ? p.incl : p.agg) + sj;
-                    for (int e = threadIdx.x; e < MM; e += blockDim.x) s.A1[e] = ldcg(src + MM + NP + e);
-                    if (threadIdx.x < NP) s.s1[threadIdx.x] = ldcg(src + MM + threadIdx.x);
-                }
-                __syncthreads();
-                float X2[4][4];
-                load_rowmajor(s.A1, X2, i0, j0);
-                __syncthreads();
-                apply_JT_smem(s.A5, s.v0, s.s1, X2, s.A1, s.A2, s.A3, s.stage, i0, j0);
-                for (int e = threadIdx.x; e < MM; e += blockDim.x) s.A4[e] += s.A1[e];
-                if (threadIdx.x < NP) s.u[threadIdx.x] += s.s1[threadIdx.x];
-                __syncthreads();
-                if (f == kFlagIncl) break;
-                // Gacc <- Gacc (x) G_j (forward aggregate of chunk j), G_j into (A1 P, s1 S1, A2 S2)
-                load_slot_smem(p.fagg + sj, s.A1, s.s1, s.A2);
-                __syncthreads();
-                chen_mul_smem(s.A5, s.v0, s.A0, s.A1, s.s1, s.A2, s.A5, s.v0, s.A0, s.A3, s.stage, s.stage + MM, i0, j0);
-                ++j;
-            }
-            // Lam_out = mu + J(G_c)^T Lam_in : G_c -> (A1 P, s1 S1, A2 S2)
-            load_slot_smem(p.fagg + slot, s.A1, s.s1, s.A2);
-            __syncthreads();
-            float X2[4][4];
-            load_rowmajor(s.A4, X2, i0, j0);
-            for (int e = threadIdx.x; e < MM; e += blockDim.x) s.A3[e] = s.A4[e];
-            if (threadIdx.x < NP) s.v0[threadIdx.x] = s.u[threadIdx.x];
-            __syncthreads();
-            apply_JT_smem(s.A1, s.s1, s.v0, X2, s.A3, s.A5, s.A0, s.stage, i0, j0);
-            {
-                float* dst = p.incl + slot;
-                const float* mu = p.agg + slot;
-                for (int e = threadIdx.x; e < MM; e += blockDim.x) dst[MM + NP + e] = s.A3[e] + ldcg(mu + MM + NP + e);
-                if (threadIdx.x < NP) dst[MM + threadIdx.x] = s.v0[threadIdx.x] + ldcg(mu + MM + threadIdx.x);
-            }
-            cta_publish(flag, kFlagIncl);
-            __syncthreads();
-        }
-
-        // ---- 3. exact adjoint from Lam_in with the gradients
-        load_rowmajor(s.A4, L2, i0, j0);
-        if (threadIdx.x < NP) L1[threadIdx.x] = s.u[threadIdx.x];
-        const int tabn = (1 + 2 * g.QP) * NP * g.d_in;
-        for (int e = threadIdx.x; e < tabn; e += blockDim.x) s.tacc[e] = 0.f;
-        __syncthreads();
-        float dM[4][4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dM[r][q] = 0.f;
-        float* du = s.red;                       // NP
-        float* dU = s.red + NP;                  // NP x QMAX
-        float* ds1 = s.red + NP + NP * QMAX;     // NP
-        float* dV = s.red + 2 * NP + NP * QMAX;  // NP x QMAX
-        for (int kb = len; kb > 0; kb -= g.SR) {
-            const int k0 = max(0, kb - g.SR);
-            const int n = kb - k0;
-            __syncthreads();
-            if (threadIdx.x < 32) {
-                warp_load_span(s.stage, p.grad_out + ((size_t)b * g.T + t0 + k0) * g.W, n * g.W);
-                const int first = t0 + k0 - 1;  // S_{t-1} rows; row -1 is the zero state
-                if (first >= 0) {
-                    warp_load_span(s.stage2, p.out + ((size_t)b * g.T + first) * g.W, n * g.W);
-                } else {
-                    for (int e = lane; e < g.W; e += 32) s.stage2[e] = 0.f;
-                    if (n > 1) warp_load_span(s.stage2 + g.W, p.out + (size_t)b * g.T * g.W, (n - 1) * g.W);
-                }
-            }
-            __syncthreads();
-            for (int k = kb - 1; k >= k0; --k) {
-                // (1) cotangent of S_t and the state S_{t-1}
-                add_grad_row(g, s.stage + (k - k0) * g.W, L1, L2, i0, j0);
-                float S2p[4][4];
-                read_state_row(g, s.stage2 + (k - k0) * g.W, s.S1, S2p, i0, j0);
-                __syncthreads();
-                local_terms(g, s, k);               // s1, U, V, u = M S1p
-                store_kmajor(s.A0, S2p, i0, j0);    // S2p k-major
-                store_rowmajor(s.A1, L2, i0, j0);   // L2 row-major
-                store_kmajor(s.A2, L2, i0, j0);     // L2 k-major
-                __syncthreads();
-                // (2) X = S2p M^T = S2p - S2p D^T, Z = M^T L2 = L2 - D^T L2
-                float X[4][4], Z[4][4];
-                gemm44(s.A0, s.Mt, X, i0, j0, false);
-                gemm44(s.Mr, s.A1, Z, i0, j0, false);
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        X[r][q] = S2p[r][q] - X[r][q];
-                        Z[r][q] = L2[r][q] - Z[r][q];
-                    }
-                // (3) contractions of L2 with the local vectors: w = L2 s1, dU = L2 V, y = L2^T u, dV = L2^T U
-                for (int o = threadIdx.x; o < 2 * NP * (g.QP + 1); o += NT) {
-                    const int side = o / (NP * (g.QP + 1)), rem = o - side * NP * (g.QP + 1);
-                    const int i = rem / (g.QP + 1), col = rem - i * (g.QP + 1);
-                    float acc = 0.f;
-                    if (side == 0) {  // row i of L2 against s1 / V[:, col-1]
-                        const float* Lr = s.A1 + i * NP;
-                        if (col == 0) {
-                            for (int j = 0; j < NP; ++j) acc = fmaf(Lr[j], s.s1[j], acc);
-                            du[i] = L1[i] + acc;
-                        } else {
-                            for (int j = 0; j < NP; ++j) acc = fmaf(Lr[j], s.V[j * QMAX + col - 1], acc);
-                            dU[i * QMAX + col - 1] = acc;
-                        }
-                    } else {  // column i of L2 against u / U[:, col-1]
-                        const float* Lc = s.A2 + i * NP;
-                        if (col == 0) {
-                            for (int j = 0; j < NP; ++j) acc = fmaf(Lc[j], s.u[j], acc);
-                            ds1[i] = L1[i] + acc;
-                        } else {
-                            for (int j = 0; j < NP; ++j) acc = fmaf(Lc[j], s.U[j * QMAX + col - 1], acc);
-                            dV[i * QMAX + col - 1] = acc;
-                        }
-                    }
-                }
-                __syncthreads();  // A0..A2 reads done, contractions visible
-                store_kmajor(s.A3, X, i0, j0);      // X k-major: B[k][j] = X[j][k]
-                store_rowmajor(s.A4, Z, i0, j0);    // Z row-major = (Z^T) k-major
-                store_kmajor(s.A5, Z, i0, j0);      // Z k-major
-                store_rowmajor(s.A1, S2p, i0, j0);  // S2p row-major
-                __syncthreads();
-                // (4) dM += L2 X^T + Z^T S2p + du S1p^T
-                gemm44(s.A2, s.A3, dM, i0, j0, true);
-                gemm44(s.A4, s.A1, dM, i0, j0, true);
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) dM[r][q] = fmaf(du[i0 + r], s.S1[j0 + q], dM[r][q]);
-                // (5) table gradients: dF += ds1 dx^T, dG_a += dU_a dx^T, dH_a += dV_a dx^T
-                const float* x = s.dx + k * g.d_in;
-                for (int e = threadIdx.x; e < tabn; e += blockDim.x) {
-                    const int blk = e / (NP * g.d_in), rem = e - blk * NP * g.d_in, i = rem / g.d_in, cc = rem - i * g.d_in;
-                    const float coef = blk == 0 ? ds1[i] : (blk <= g.QP ? dU[i * QMAX + blk - 1] : dV[i * QMAX + blk - 1 - g.QP]);
-                    s.tacc[e] = fmaf(coef, x[cc], s.tacc[e]);
-                }
-                // (6) dx_t = F^T ds1 + sum_a G_a^T dU_a + H_a^T dV_a (warp per channel, lane per row)
-                for (int cc = warp; cc < g.d_in; cc += NT / 32) {
-                    const int i = lane;
-                    float acc = s.F[i * g.d_in + cc] * ds1[i];
-                    for (int a = 0; a < g.QP; ++a) {
-                        acc = fmaf(s.G[((size_t)a * NP + i) * g.d_in + cc], dU[i * QMAX + a], acc);
-                        acc = fmaf(s.H[((size_t)a * NP + i) * g.d_in + cc], dV[i * QMAX + a], acc);
-                    }
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
-                    if (lane == 0) s.ddx[k * g.d_in + cc] = acc;
-                }
-                // (7) cotangent of S_{t-1}: L1 <- M^T du = du - D^T du, L2 <- Z M = Z - Z D
-                if (threadIdx.x < NP) {
-                    float acc = 0.f;
-                    for (int kk = 0; kk < NP; ++kk) acc = fmaf(s.Mr[kk * NP + threadIdx.x], du[kk], acc);
-                    s.v0[threadIdx.x] = du[threadIdx.x] - acc;
-                }
-                gemm44(s.A5, s.Mr, L2, i0, j0, false);
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) L2[r][q] = Z[r][q] - L2[r][q];
-                __syncthreads();
-                if (threadIdx.x < NP) L1[threadIdx.x] = s.v0[threadIdx.x];
-                __syncthreads();
-            }
-        }
-        // chunk outputs: dx rows (one span) and the tile's gradient partials
-        if (threadIdx.x < 32) warp_store_span(p.grad_dx + ((size_t)b * g.T + t0) * g.d_in, s.ddx, len * g.d_in);
-        float* part = p.partials + (size_t)tile * (MM + tabn);
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) part[(i0 + r) * NP + j0 + q] = dM[r][q];
-        for (int e = threadIdx.x; e < tabn; e += blockDim.x) part[MM + e] = s.tacc[e];
-        __syncthreads();
-    }
-}
-
 
 // ---------------------------------------------------------------------------------- tensor-core backward
 //
@@ -2886,10 +2120,7 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
         g->Lc = bestL;
     }
     g->C = (g->T + g->Lc - 1) / g->Lc;
-    g->SR = 1;
     g->ntiles = g->B * g->C;
-    g->smem_floats = smem_floats(*g, false);
-    g->bsmem_floats = smem_floats(*g, true);
     return EWS_OK;
 }
 
@@ -2951,20 +2182,6 @@ static WsLayout bwd_layout(const Geom& g) {
     return L;
 }
 
-
-template <typename K>
-static int launch(K kernel, const Params& p, size_t smem, cudaStream_t s) {
-    if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-    int per_sm = 0;
-    per_sm = resident_ctas((const void*)kernel, NT, smem);
-    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
-    int grid = per_sm * num_sms();
-    if (grid > p.g.ntiles) grid = p.g.ntiles;
-    kernel<<<grid, NT, smem, s>>>(p);
-    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
-}
 
 }  // namespace dense
 }  // namespace ews
