@@ -114,9 +114,10 @@ def test_gradients_match_oracle(N, readout):
         _assert_close(f"{name} grad", a, b)
 
 
-@pytest.mark.parametrize("N,d_in,q,T,chunk", [(32, 7, 6, 75, 7), (5, 3, 2, 33, 5), (16, 11, 8, 40, 8)])
+@pytest.mark.parametrize("N,d_in,q,T,chunk", [(32, 7, 6, 75, 7), (5, 3, 2, 33, 5), (16, 11, 8, 40, 8), (8, 4, 0, 30, 6), (12, 8, 1, 37, 9)])
 def test_gradients_odd_chunks_and_table_sizes(N, d_in, q, T, chunk):
-    """Odd chunk lengths, a padded state (N = 5) and large series tables (q = 8, d_in = 11)."""
+    """Odd chunk lengths, a padded state (N = 5), large series tables (q = 8, d_in = 11) and the register
+    table-gradient kernel's sizes (q + 1 <= 4 with d_in <= 8: 3, 5, 7 and 9 table rows per lane)."""
     _require_gpu()
     path, clock, A, lift = _case(2, T, N, d_in=d_in, seed=40 + N)
     ref, _ = _oracle(path, clock, A, lift, "prefix", q)
