@@ -45,6 +45,8 @@ EXPORTED = (
     "ews_block_bwd",
     "ews_expm_batched",
     "ews_expm_adjoint_batched",
+    "ews_series_tables",
+    "ews_series_tables_adjoint",
     "ews_read_device_status",
     "ews_status_fold",
     "ews_error_string",
@@ -207,6 +209,11 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.ews_expm_batched.restype = _c_int
         lib.ews_expm_adjoint_batched.argtypes = [_vp, _vp, _vp, _c_int, _c_int, _vp]
         lib.ews_expm_adjoint_batched.restype = _c_int
+        lib.ews_series_tables.argtypes = [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp]
+        lib.ews_series_tables.restype = _c_int
+        lib.ews_series_tables_adjoint.argtypes = [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
+                                                  _vp, _vp, _vp]
+        lib.ews_series_tables_adjoint.restype = _c_int
         lib.ews_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(_c_int)]
         lib.ews_read_device_status.restype = _c_int
         lib.ews_diag_fwd_noalloc_status.argtypes = [_vp, ctypes.POINTER(_c_int)]

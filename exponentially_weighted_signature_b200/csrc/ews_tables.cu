@@ -183,6 +183,181 @@ __global__ void __launch_bounds__(XT) expm_adjoint_kernel(const double* __restri
     }
 }
 
+// ---------------------------------------------------------------------------------- series-leaf tables
+//
+// The dense engine's local-term tables for a uniform clock (the series leaf with shared letters,
+// ews/core/series_leaf.py:72-113): with X_b = -h_b A and the lift W,
+//     P_a = X^a / a!,  G_a = P_a W,  F = sum_p c1_p G_p,  H_a = sum_b c2_ab G_b      (a, b = 0..q),
+// one CTA per sample in float64, float32 outputs. F and H are linear in the G's, so the VJP maps the three
+// cotangents to one per G: dG~_b = dG_b + c1_b dF + sum_a c2_ab dH_a, then dP_b = dG~_b W^T, dW += P_b^T dG~_b,
+// and back through P_b = P_{b-1} X / b (R_b = dP_b + R_{b+1} X^T / (b+1), dX = sum_b P_{b-1}^T R_b / b).
+constexpr int TQ = 12;  // q + 1 <= 12
+
+// C = A^T B (A, B, C padded 32 x 32 row-major float64); the caller synchronises before and after.
+__device__ __forceinline__ void matmul_tn(const double* A, const double* B, double* C) {
+    const int r = threadIdx.x >> 4, c = threadIdx.x & 15;
+    double acc[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
+#pragma unroll 4
+    for (int k = 0; k < 32; ++k) {
+        const double a0 = A[k * 32 + 2 * r], a1 = A[k * 32 + 2 * r + 1];
+        const double b0 = B[k * 32 + 2 * c], b1 = B[k * 32 + 2 * c + 1];
+        acc[0][0] = fma(a0, b0, acc[0][0]);
+        acc[0][1] = fma(a0, b1, acc[0][1]);
+        acc[1][0] = fma(a1, b0, acc[1][0]);
+        acc[1][1] = fma(a1, b1, acc[1][1]);
+    }
+    C[(2 * r) * 32 + 2 * c] = acc[0][0];
+    C[(2 * r) * 32 + 2 * c + 1] = acc[0][1];
+    C[(2 * r + 1) * 32 + 2 * c] = acc[1][0];
+    C[(2 * r + 1) * 32 + 2 * c + 1] = acc[1][1];
+}
+
+// C = A B^T.
+__device__ __forceinline__ void matmul_nt(const double* A, const double* B, double* C) {
+    const int r = threadIdx.x >> 4, c = threadIdx.x & 15;
+    double acc[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
+#pragma unroll 4
+    for (int k = 0; k < 32; ++k) {
+        const double a0 = A[(2 * r) * 32 + k], a1 = A[(2 * r + 1) * 32 + k];
+        const double b0 = B[(2 * c) * 32 + k], b1 = B[(2 * c + 1) * 32 + k];
+        acc[0][0] = fma(a0, b0, acc[0][0]);
+        acc[0][1] = fma(a0, b1, acc[0][1]);
+        acc[1][0] = fma(a1, b0, acc[1][0]);
+        acc[1][1] = fma(a1, b1, acc[1][1]);
+    }
+    C[(2 * r) * 32 + 2 * c] = acc[0][0];
+    C[(2 * r) * 32 + 2 * c + 1] = acc[0][1];
+    C[(2 * r + 1) * 32 + 2 * c] = acc[1][0];
+    C[(2 * r + 1) * 32 + 2 * c + 1] = acc[1][1];
+}
+
+// X_b (n x n) and W (n x d, or the identity) into padded 32 x 32 shared copies.
+__device__ void load_xw(const double* x, const double* w, int n, int d, double* X, double* W) {
+    for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+        const int i = e >> 5, j = e & 31;
+        X[e] = (i < n && j < n) ? x[i * n + j] : 0.0;
+        W[e] = (i < n && j < d) ? (w ? w[i * d + j] : (i == j ? 1.0 : 0.0)) : 0.0;
+    }
+}
+
+__global__ void __launch_bounds__(XT) series_tables_kernel(const double* __restrict__ x, const double* __restrict__ w,
+                                                           const double* __restrict__ c1, const double* __restrict__ c2,
+                                                           int n, int d, int q, float* __restrict__ F,
+                                                           float* __restrict__ G, float* __restrict__ H) {
+    extern __shared__ double tsm[];
+    double* X = tsm;
+    double* W = X + 1024;
+    double* P = W + 1024;
+    double* Pn = P + 1024;
+    double* Gs = Pn + 1024;  // (q + 1) x 1024
+    const int b = blockIdx.x, QP = q + 1;
+    load_xw(x + (size_t)b * n * n, w, n, d, X, W);
+    for (int e = threadIdx.x; e < 1024; e += blockDim.x) P[e] = ((e >> 5) == (e & 31)) ? 1.0 : 0.0;
+    __syncthreads();
+    for (int a = 0; a < QP; ++a) {
+        matmul<32>(P, W, Gs + a * 1024);  // G_a = P_a W
+        if (a + 1 < QP) matmul<32>(P, X, Pn);
+        __syncthreads();
+        if (a + 1 < QP) {
+            const double inv = 1.0 / (double)(a + 1);
+            for (int e = threadIdx.x; e < 1024; e += blockDim.x) P[e] = Pn[e] * inv;
+        }
+        __syncthreads();
+    }
+    // outputs (n x d each): G_a, F = sum_p c1_p G_p, H_a = sum_b c2_ab G_b
+    for (int e = threadIdx.x; e < n * d; e += blockDim.x) {
+        const int i = e / d, j = e - i * d, o = i * 32 + j;
+        double f = 0.0;
+        for (int p2 = 0; p2 < QP; ++p2) {
+            const double g = Gs[p2 * 1024 + o];
+            f = fma(c1[p2], g, f);
+            G[((size_t)b * QP + p2) * n * d + e] = (float)g;
+        }
+        F[(size_t)b * n * d + e] = (float)f;
+        for (int a = 0; a < QP; ++a) {
+            double hv = 0.0;
+            for (int p2 = 0; p2 < QP; ++p2) hv = fma(c2[a * QP + p2], Gs[p2 * 1024 + o], hv);
+            H[((size_t)b * QP + a) * n * d + e] = (float)hv;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(XT) series_tables_adjoint_kernel(
+    const double* __restrict__ x, const double* __restrict__ w, const double* __restrict__ c1,
+    const double* __restrict__ c2, int n, int d, int q, const float* __restrict__ dF, const float* __restrict__ dG,
+    const float* __restrict__ dH, double* __restrict__ dX, double* __restrict__ dW) {
+    extern __shared__ double tsm[];
+    double* X = tsm;
+    double* W = X + 1024;
+    double* R = W + 1024;
+    double* T1 = R + 1024;
+    double* T2 = T1 + 1024;
+    double* dXs = T2 + 1024;
+    double* dWs = dXs + 1024;
+    double* P = dWs + 1024;  // (q + 1) x 1024: P_0 .. P_q
+    const int b = blockIdx.x, QP = q + 1;
+    load_xw(x + (size_t)b * n * n, w, n, d, X, W);
+    for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+        P[e] = ((e >> 5) == (e & 31)) ? 1.0 : 0.0;
+        dXs[e] = 0.0;
+        dWs[e] = 0.0;
+    }
+    __syncthreads();
+    for (int a = 1; a < QP; ++a) {
+        matmul<32>(P + (a - 1) * 1024, X, T1);
+        __syncthreads();
+        const double inv = 1.0 / (double)a;
+        for (int e = threadIdx.x; e < 1024; e += blockDim.x) P[a * 1024 + e] = T1[e] * inv;
+        __syncthreads();
+    }
+    // R_b = dG~_b W^T + R_{b+1} X^T / (b + 1); dX += P_{b-1}^T R_b / b; dW += P_b^T dG~_b
+    for (int bb = QP - 1; bb >= 0; --bb) {
+        // T1 = dG~_b (padded n x d)
+        for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+            const int i = e >> 5, j = e & 31;
+            double v = 0.0;
+            if (i < n && j < d) {
+                const size_t o = (size_t)i * d + j;
+                v = (double)dG[((size_t)b * QP + bb) * n * d + o] + c1[bb] * (double)dF[(size_t)b * n * d + o];
+                for (int a = 0; a < QP; ++a) v = fma(c2[a * QP + bb], (double)dH[((size_t)b * QP + a) * n * d + o], v);
+            }
+            T1[e] = v;
+        }
+        __syncthreads();
+        matmul_tn(P + bb * 1024, T1, T2);  // P_b^T dG~_b
+        __syncthreads();
+        for (int e = threadIdx.x; e < 1024; e += blockDim.x) dWs[e] += T2[e];
+        __syncthreads();
+        matmul_nt(T1, W, T2);              // dG~_b W^T
+        __syncthreads();
+        if (bb == QP - 1) {
+            for (int e = threadIdx.x; e < 1024; e += blockDim.x) R[e] = T2[e];
+        } else {
+            matmul_nt(R, X, T1);           // R_{b+1} X^T
+            __syncthreads();
+            const double inv = 1.0 / (double)(bb + 1);
+            for (int e = threadIdx.x; e < 1024; e += blockDim.x) R[e] = T2[e] + T1[e] * inv;
+        }
+        __syncthreads();
+        if (bb >= 1) {
+            matmul_tn(P + (bb - 1) * 1024, R, T1);  // P_{b-1}^T R_b
+            __syncthreads();
+            const double inv = 1.0 / (double)bb;
+            for (int e = threadIdx.x; e < 1024; e += blockDim.x) dXs[e] += T1[e] * inv;
+            __syncthreads();
+        }
+    }
+    for (int e = threadIdx.x; e < n * n; e += blockDim.x) {
+        const int i = e / n, j = e - i * n;
+        dX[(size_t)b * n * n + e] = dXs[i * 32 + j];
+    }
+    if (dW)
+        for (int e = threadIdx.x; e < n * d; e += blockDim.x) {
+            const int i = e / d, j = e - i * d;
+            dW[(size_t)b * n * d + e] = dWs[i * 32 + j];
+        }
+}
+
 template <int NP>
 static size_t smem_bytes() {
     return sizeof(double) * (3 * NP * NP + NP);
@@ -206,6 +381,34 @@ extern "C" int ews_expm_batched(const double* x, double* out, int batch, int n, 
         cudaFuncSetAttribute(expm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         expm_kernel<64><<<batch, XT, smem, s>>>(x, out, n);
     }
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+extern "C" int ews_series_tables(const double* x, const double* lift, const double* c1, const double* c2, int batch,
+                                 int n, int d_in, int order, float* F, float* G, float* H, ews_stream_t stream) {
+    if (batch < 0 || n <= 0 || d_in <= 0 || order < 0) return EWS_ERR_INVALID_ARGUMENT;
+    if (n > 32 || d_in > 32 || order + 1 > TQ) return EWS_ERR_UNSUPPORTED;
+    if (!lift && d_in != n) return EWS_ERR_INVALID_ARGUMENT;
+    if (batch == 0) return EWS_OK;
+    if (!x || !c1 || !c2 || !F || !G || !H) return EWS_ERR_INVALID_ARGUMENT;
+    const size_t smem = sizeof(double) * 1024 * (4 + (size_t)order + 1);
+    cudaFuncSetAttribute(series_tables_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    series_tables_kernel<<<batch, XT, smem, (cudaStream_t)stream>>>(x, lift, c1, c2, n, d_in, order, F, G, H);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+extern "C" int ews_series_tables_adjoint(const double* x, const double* lift, const double* c1, const double* c2,
+                                         int batch, int n, int d_in, int order, const float* dF, const float* dG,
+                                         const float* dH, double* dX, double* dW, ews_stream_t stream) {
+    if (batch < 0 || n <= 0 || d_in <= 0 || order < 0) return EWS_ERR_INVALID_ARGUMENT;
+    if (n > 32 || d_in > 32 || order + 1 > TQ) return EWS_ERR_UNSUPPORTED;
+    if (!lift && d_in != n) return EWS_ERR_INVALID_ARGUMENT;
+    if (batch == 0) return EWS_OK;
+    if (!x || !c1 || !c2 || !dF || !dG || !dH || !dX) return EWS_ERR_INVALID_ARGUMENT;
+    const size_t smem = sizeof(double) * 1024 * (7 + (size_t)order + 1);
+    cudaFuncSetAttribute(series_tables_adjoint_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    series_tables_adjoint_kernel<<<batch, XT, smem, (cudaStream_t)stream>>>(x, lift, c1, c2, n, d_in, order, dF, dG,
+                                                                            dH, dX, dW);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 

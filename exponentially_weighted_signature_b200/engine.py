@@ -271,6 +271,50 @@ class Expm(torch.autograd.Function):
         return out
 
 
+class SeriesTables(torch.autograd.Function):
+    """The dense engine's series-leaf tables in one library kernel per direction: (X = -h A (B, n, n)
+    float64, lift W (n, d_in) float64 or None, coefficients c1 (q+1,), c2 (q+1, q+1) float64) ->
+    F (B, n, d_in), G, H (B, q+1, n, d_in) float32, with P_a = X^a / a!, G_a = P_a W, F = sum_p c1_p G_p,
+    H_a = sum_b c2_ab G_b (series.dense_leaf_tables in one pass); the VJP returns dX and dW."""
+
+    @staticmethod
+    def forward(ctx, X, W, c1, c2):
+        _require_cuda(X)
+        X = X.contiguous()
+        B, n = X.shape[0], X.shape[-1]
+        q = c1.shape[0] - 1
+        Wc = None if W is None else W.to(torch.float64).contiguous()
+        d = n if Wc is None else Wc.shape[-1]
+        F = torch.empty((B, n, d), dtype=torch.float32, device=X.device)
+        G = torch.empty((B, q + 1, n, d), dtype=torch.float32, device=X.device)
+        H = torch.empty_like(G)
+        c1c, c2c = c1.contiguous(), c2.contiguous()
+        _lib.check(_lib.load().ews_series_tables(_ptr(X), None if Wc is None else _ptr(Wc), _ptr(c1c), _ptr(c2c), B, n,
+                                                 d, q, _ptr(F), _ptr(G), _ptr(H), _stream_ptr(X.device)),
+                   "ews_series_tables")
+        ctx.save_for_backward(X, Wc, c1c, c2c)
+        ctx.has_w = W is not None
+        return F, G, H
+
+    @staticmethod
+    def backward(ctx, dF, dG, dH):
+        X, Wc, c1, c2 = ctx.saved_tensors
+        B, n = X.shape[0], X.shape[-1]
+        q = c1.shape[0] - 1
+        d = n if Wc is None else Wc.shape[-1]
+        z = lambda t, shape: torch.zeros(shape, dtype=torch.float32, device=X.device) if t is None else t.float().contiguous()
+        dF = z(dF, (B, n, d))
+        dG = z(dG, (B, q + 1, n, d))
+        dH = z(dH, (B, q + 1, n, d))
+        dX = torch.empty_like(X)
+        dW = torch.empty((B, n, d), dtype=torch.float64, device=X.device) if ctx.has_w else None
+        _lib.check(_lib.load().ews_series_tables_adjoint(_ptr(X), None if Wc is None else _ptr(Wc), _ptr(c1), _ptr(c2), B, n,
+                                                         d, q, _ptr(dF), _ptr(dG), _ptr(dH), _ptr(dX),
+                                                         None if dW is None else _ptr(dW), _stream_ptr(X.device)),
+                   "ews_series_tables_adjoint")
+        return dX, (dW.sum(0) if dW is not None else None), None, None
+
+
 class DenseScan(torch.autograd.Function):
     """Dense engine, uniform clock: (path, D = I - M, F, G, H) -> flat EWS (prefix or terminal)."""
 

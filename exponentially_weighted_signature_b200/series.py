@@ -173,8 +173,11 @@ def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None, coeffs=Non
     N = A.shape[-1]
     Dc = torch.eye(N, dtype=torch.float64, device=A.device) - Expm.apply(X)
     Xl = X if A_leaf is None else -h64 * A_leaf.to(torch.float64)
-    F, G, H = dense_leaf_tables(Xl, q, lift, coeffs)
-    return Dc.float(), F.float(), G.float(), H.float()
+    from .engine import SeriesTables
+
+    c1, c2 = _leaf_coeffs(int(q), str(A.device)) if coeffs is None else coeffs
+    F, G, H = SeriesTables.apply(Xl.contiguous(), lift, c1, c2)  # one library kernel each way
+    return Dc.float(), F, G, H
 
 
 # ------------------------------------------------------------------------------ plane leaf

@@ -258,6 +258,20 @@ int ews_block_bwd(const ews_block_args* a, ews_stream_t stream);
 int ews_expm_batched(const double* x, double* out, int batch, int n, ews_stream_t stream);
 int ews_expm_adjoint_batched(const double* x, const double* g, double* out, int batch, int n, ews_stream_t stream);
 
+/* ---- series-leaf tables of the dense engine ----------------------------------------------------------
+ * Replaces the letters and level assembly of series_local_signatures (ews/core/series_leaf.py:72-113) for a
+ * uniform clock, as per-sample tables: with x_b = -h_b A (batch, n, n) float64 and the lift W (n, d_in)
+ * float64 (NULL: the identity, d_in == n), P_a = x^a / a!, G_a = P_a W, F = sum_p c1_p G_p and
+ * H_a = sum_b c2_ab G_b for a, b = 0..order (c1 (order+1), c2 (order+1, order+1) float64 on the device).
+ * Outputs float32: F (batch, n, d_in), G and H (batch, order+1, n, d_in). n, d_in <= 32, order <= 11.
+ *   ews_series_tables_adjoint: from dF, dG, dH (float32, same shapes) the per-sample gradients
+ *   dX (batch, n, n) and dW (batch, n, d_in; may be NULL) in float64, summed over samples by the caller. */
+int ews_series_tables(const double* x, const double* lift, const double* c1, const double* c2, int batch, int n,
+                      int d_in, int order, float* F, float* G, float* H, ews_stream_t stream);
+int ews_series_tables_adjoint(const double* x, const double* lift, const double* c1, const double* c2, int batch,
+                              int n, int d_in, int order, const float* dF, const float* dG, const float* dH,
+                              double* dX, double* dW, ews_stream_t stream);
+
 /* ---- utilities --------------------------------------------------------------------------------- */
 /* Every forward and backward workspace begins with a status block whose error word the call clears and
  * a timed-out device wait sets. */
