@@ -47,6 +47,9 @@ EXPORTED = (
     "ews_expm_adjoint_batched",
     "ews_series_tables",
     "ews_series_tables_adjoint",
+    "ews_dense_leaf",
+    "ews_dense_leaf_adjoint",
+    "ews_dense_leaf_work_size",
     "ews_read_device_status",
     "ews_status_fold",
     "ews_error_string",
@@ -214,6 +217,13 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.ews_series_tables_adjoint.argtypes = [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
                                                   _vp, _vp, _vp]
         lib.ews_series_tables_adjoint.restype = _c_int
+        lib.ews_dense_leaf.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp]
+        lib.ews_dense_leaf.restype = _c_int
+        lib.ews_dense_leaf_adjoint.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
+                                               _vp, _vp, _c_size, _vp, _vp, _vp, _vp, _vp]
+        lib.ews_dense_leaf_adjoint.restype = _c_int
+        lib.ews_dense_leaf_work_size.argtypes = [_c_int, _c_int, _c_int]
+        lib.ews_dense_leaf_work_size.restype = _c_size
         lib.ews_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(_c_int)]
         lib.ews_read_device_status.restype = _c_int
         lib.ews_diag_fwd_noalloc_status.argtypes = [_vp, ctypes.POINTER(_c_int)]

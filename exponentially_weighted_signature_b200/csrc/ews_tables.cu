@@ -358,6 +358,319 @@ __global__ void __launch_bounds__(XT) series_tables_adjoint_kernel(
         }
 }
 
+// ------------------------------------------------------------------------- the dense leaf, fused
+//
+// Both tables of the dense engine from the generator in one launch per direction: the flow complement
+// D_b = I - expm(X_b) with X_b = -h_b A, and the series tables F, G, H of X^l_b = -h_b A_l (A_l the leaf's
+// own generator, A itself unless given). CTAs [0, batch) evaluate the flows, CTAs [batch, 2 batch) the
+// series tables, side by side. 1024 threads: thread (i, j) = (tid >> 5, tid & 31) owns element (i, j) of
+// every padded 32 x 32 float64 tile (row stride LD = 33 doubles, so the transposed reads do not collide
+// on banks). The backward evaluates the Frechet derivative of the exponential as the coupled recursion of
+// the block-triangular identity (the [[X^T, G], [0, X^T]] exponential without its zero and repeated
+// blocks: three 32 x 32 products per step instead of a 64 x 64 one) beside the series adjoint, and one
+// more launch sums the per-sample gradients over the batch in a fixed order.
+constexpr int LT = 1024;
+constexpr int LD = 33;
+constexpr int LTILE = 32 * LD;
+
+__device__ __forceinline__ double mm_nn(const double* A, const double* B, int i, int j) {
+    double acc = 0.0;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) acc = fma(A[i * LD + k], B[k * LD + j], acc);
+    return acc;
+}
+__device__ __forceinline__ double mm_tn(const double* A, const double* B, int i, int j) {  // (A^T B)[i][j]
+    double acc = 0.0;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) acc = fma(A[k * LD + i], B[k * LD + j], acc);
+    return acc;
+}
+__device__ __forceinline__ double mm_nt(const double* A, const double* B, int i, int j) {  // (A B^T)[i][j]
+    double acc = 0.0;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) acc = fma(A[i * LD + k], B[j * LD + k], acc);
+    return acc;
+}
+
+// Largest column sum of |T0| + |T1| (T1 may be NULL) over the padded tile, to every thread; `red` holds 32.
+__device__ double col_norm1(const double* T0, const double* T1, double* red) {
+    const int t = threadIdx.x;
+    if (t < 32) {
+        double s = 0.0;
+        for (int i = 0; i < 32; ++i) s += fabs(T0[i * LD + t]) + (T1 ? fabs(T1[i * LD + t]) : 0.0);
+        red[t] = s;
+    }
+    __syncthreads();
+    double m = 0.0;
+    for (int c = 0; c < 32; ++c) {
+        const double v = red[c];
+        m = (v > m || v != v) ? v : m;  // a NaN column wins
+    }
+    __syncthreads();
+    return m;
+}
+
+// Squarings that bring a matrix of 1-norm `nrm` to <= 1/2 (none for a non-finite norm).
+__device__ __forceinline__ int halvings(double nrm) {
+    int s = 0;
+    if (nrm == nrm && nrm <= 1.0e300) {
+        double v = nrm;
+        while (v > 0.5 && s < 1100) {
+            v *= 0.5;
+            ++s;
+        }
+    }
+    return s;
+}
+
+// Block-wide fixed-order sum of one double per thread (every thread gets it); `red` holds 32.
+__device__ double block_sum(double v, double* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    double s = 0.0;
+    for (int k = 0; k < 32; ++k) s += red[k];
+    __syncthreads();
+    return s;
+}
+
+struct LeafArgs {
+    const float *A, *A_leaf, *h, *W;
+    const double *c1, *c2;
+    int batch, n, d, q;
+};
+
+// The sample's generator tile -h_b G (G = A, or the leaf's A_l) into X.
+__device__ void load_generator(const LeafArgs& a, int b, bool leaf, double* X) {
+    const int i = threadIdx.x >> 5, j = threadIdx.x & 31;
+    const float* g = (leaf && a.A_leaf) ? a.A_leaf : a.A;
+    const double hb = (double)a.h[b];
+    X[i * LD + j] = (i < a.n && j < a.n) ? -hb * (double)g[i * a.n + j] : 0.0;
+}
+
+__device__ void load_lift(const LeafArgs& a, double* W) {
+    const int i = threadIdx.x >> 5, j = threadIdx.x & 31;
+    W[i * LD + j] = (i < a.n && j < a.d) ? (a.W ? (double)a.W[i * a.d + j] : (i == j ? 1.0 : 0.0)) : 0.0;
+}
+
+__global__ void __launch_bounds__(LT) dense_leaf_kernel(LeafArgs a, float* __restrict__ Dc, float* __restrict__ F,
+                                                        float* __restrict__ G, float* __restrict__ H) {
+    extern __shared__ double lsm[];
+    double* X = lsm;
+    double* T0 = X + LTILE;
+    double* T1 = T0 + LTILE;
+    double* red = T1 + LTILE;
+    const int i = threadIdx.x >> 5, j = threadIdx.x & 31;
+    const bool leaf = blockIdx.x >= a.batch;
+    const int b = leaf ? blockIdx.x - a.batch : blockIdx.x;
+    const int n = a.n, d = a.d, QP = a.q + 1;
+    const double dij = (i == j) ? 1.0 : 0.0;
+    load_generator(a, b, leaf, X);
+    if (!leaf) {
+        // D = I - expm(X): scaling, degree-14 Taylor by Horner, squarings
+        __syncthreads();
+        const int s = halvings(col_norm1(X, nullptr, red));
+        const double x = X[i * LD + j] * ldexp(1.0, -s);
+        __syncthreads();
+        X[i * LD + j] = x;
+        constexpr int DEG = 14;
+        T0[i * LD + j] = dij + x / DEG;
+        __syncthreads();
+        for (int k = DEG - 1; k >= 1; --k) {
+            const double t = mm_nn(X, T0, i, j);
+            __syncthreads();
+            T0[i * LD + j] = dij + t / k;
+            __syncthreads();
+        }
+        for (int r = 0; r < s; ++r) {
+            const double t = mm_nn(T0, T0, i, j);
+            __syncthreads();
+            T0[i * LD + j] = t;
+            __syncthreads();
+        }
+        if (i < n && j < n) Dc[((size_t)b * n + i) * n + j] = (float)(dij - T0[i * LD + j]);
+        return;
+    }
+    // series tables: P_a = X^a / a! (T0), G_a = P_a W (registers), then F and H from the G's
+    load_lift(a, T1);
+    T0[i * LD + j] = dij;
+    __syncthreads();
+    double g[TQ];
+#pragma unroll
+    for (int p = 0; p < TQ; ++p) {
+        g[p] = 0.0;
+        if (p < QP) {
+            g[p] = mm_nn(T0, T1, i, j);
+            if (p + 1 < QP) {
+                const double t = mm_nn(T0, X, i, j) / (double)(p + 1);
+                __syncthreads();
+                T0[i * LD + j] = t;
+                __syncthreads();
+            }
+        }
+    }
+    if (i < n && j < d) {
+        const size_t e = (size_t)i * d + j, nd = (size_t)n * d;
+        double f = 0.0;
+#pragma unroll
+        for (int p = 0; p < TQ; ++p)
+            if (p < QP) {
+                f = fma(a.c1[p], g[p], f);
+                G[((size_t)b * QP + p) * nd + e] = (float)g[p];
+            }
+        F[(size_t)b * nd + e] = (float)f;
+        for (int r = 0; r < QP; ++r) {
+            double hv = 0.0;
+#pragma unroll
+            for (int p = 0; p < TQ; ++p)
+                if (p < QP) hv = fma(a.c2[r * QP + p], g[p], hv);
+            H[((size_t)b * QP + r) * nd + e] = (float)hv;
+        }
+    }
+}
+
+// Per-sample gradients into `work` (float64, per sample: dX of the flows n x n, dX of the leaf n x n, dW
+// n x d, then the two parts of dh), summed over the batch by dense_leaf_reduce_kernel.
+__host__ __device__ inline size_t leaf_work_stride(int n, int d) { return 2 * (size_t)n * n + (size_t)n * d + 2; }
+
+__global__ void __launch_bounds__(LT) dense_leaf_adjoint_kernel(LeafArgs a, const float* __restrict__ dDc,
+                                                                const float* __restrict__ dF,
+                                                                const float* __restrict__ dG,
+                                                                const float* __restrict__ dH,
+                                                                double* __restrict__ work) {
+    extern __shared__ double lsm[];
+    double* X = lsm;
+    double* T0 = X + LTILE;
+    double* T1 = T0 + LTILE;
+    double* T2 = T1 + LTILE;
+    double* red = T2 + LTILE;
+    double* P = red + 32;  // leaf role: P_0 .. P_q
+    const int i = threadIdx.x >> 5, j = threadIdx.x & 31;
+    const bool leaf = blockIdx.x >= a.batch;
+    const int b = leaf ? blockIdx.x - a.batch : blockIdx.x;
+    const int n = a.n, d = a.d, QP = a.q + 1;
+    const double dij = (i == j) ? 1.0 : 0.0;
+    const size_t ws = leaf_work_stride(n, d);
+    double* wb = work + (size_t)b * ws;
+    const float* gsrc = (leaf && a.A_leaf) ? a.A_leaf : a.A;
+    const double gen = (i < n && j < n) ? (double)gsrc[i * n + j] : 0.0;
+    load_generator(a, b, leaf, X);
+    if (!leaf) {
+        // dX = L(X^T, C) with C = -dD (the cotangent of expm(X)); C scaled to unit 1-norm first
+        double c = 0.0;
+        if (dDc && i < n && j < n) c = -(double)dDc[((size_t)b * n + i) * n + j];
+        T1[i * LD + j] = c;
+        __syncthreads();
+        const double cn = col_norm1(T1, nullptr, red);
+        const double cs = cn > 0.0 ? 1.0 / cn : 0.0;
+        // Y = X^T and C / ||C|| (T2, T1); the scaling is that of the block matrix [[Y, C'], [0, Y]]
+        T2[i * LD + j] = X[j * LD + i];
+        T1[i * LD + j] = c * cs;
+        __syncthreads();
+        const int s = halvings(col_norm1(T2, T1, red));  // (synchronises before returning)
+        const double sc = ldexp(1.0, -s);
+        const double y = T2[i * LD + j] * sc, cc = T1[i * LD + j] * sc;
+        __syncthreads();
+        T2[i * LD + j] = y;  // Y
+        T1[i * LD + j] = cc; // C'
+        // the block [[Pm, Qm], [0, Pm]]: Pm in X, Qm in T0
+        constexpr int DEG = 14;
+        X[i * LD + j] = dij + y / DEG;
+        T0[i * LD + j] = cc / DEG;
+        __syncthreads();
+        for (int k = DEG - 1; k >= 1; --k) {
+            const double tp = mm_nn(T2, X, i, j);
+            const double tq = mm_nn(T2, T0, i, j) + mm_nn(T1, X, i, j);
+            __syncthreads();
+            X[i * LD + j] = dij + tp / k;
+            T0[i * LD + j] = tq / k;
+            __syncthreads();
+        }
+        for (int r = 0; r < s; ++r) {
+            const double tp = mm_nn(X, X, i, j);
+            const double tq = mm_nn(X, T0, i, j) + mm_nn(T0, X, i, j);
+            __syncthreads();
+            X[i * LD + j] = tp;
+            T0[i * LD + j] = tq;
+            __syncthreads();
+        }
+        const double dx = T0[i * LD + j] * cn;
+        if (i < n && j < n) wb[(size_t)i * n + j] = dx;
+        const double dh = block_sum(-gen * dx, red);
+        if (threadIdx.x == 0) wb[ws - 2] = dh;
+        return;
+    }
+    // series adjoint: dG~_b = dG_b + c1_b dF + sum_a c2_ab dH_a; dW += P_b^T dG~_b;
+    // R_b = dG~_b W^T + R_{b+1} X^T / (b + 1); dX += P_{b-1}^T R_b / b
+    load_lift(a, T2);
+    P[i * LD + j] = dij;
+    __syncthreads();
+    for (int p = 1; p < QP; ++p) {
+        P[p * LTILE + i * LD + j] = mm_nn(P + (p - 1) * LTILE, X, i, j) / (double)p;
+        __syncthreads();
+    }
+    const size_t nd = (size_t)n * d, e = (size_t)i * d + j;
+    const bool in = i < n && j < d;
+    double dw = 0.0, dx = 0.0;
+    for (int bb = QP - 1; bb >= 0; --bb) {
+        double v = 0.0;
+        if (in) {
+            if (dG) v = (double)dG[((size_t)b * QP + bb) * nd + e];
+            if (dF) v = fma(a.c1[bb], (double)dF[(size_t)b * nd + e], v);
+            if (dH)
+                for (int r = 0; r < QP; ++r) v = fma(a.c2[r * QP + bb], (double)dH[((size_t)b * QP + r) * nd + e], v);
+        }
+        T1[i * LD + j] = v;  // dG~_b
+        __syncthreads();
+        dw += mm_tn(P + bb * LTILE, T1, i, j);
+        double r = mm_nt(T1, T2, i, j);
+        if (bb < QP - 1) r += mm_nt(T0, X, i, j) / (double)(bb + 1);
+        __syncthreads();
+        T0[i * LD + j] = r;  // R_b
+        __syncthreads();
+        if (bb >= 1) dx += mm_tn(P + (bb - 1) * LTILE, T0, i, j) / (double)bb;
+    }
+    if (i < n && j < n) wb[(size_t)n * n + (size_t)i * n + j] = dx;
+    if (in) wb[2 * (size_t)n * n + e] = dw;
+    const double dh = block_sum(-gen * dx, red);
+    if (threadIdx.x == 0) wb[ws - 1] = dh;
+}
+
+// dA = sum_b -h_b (dX_b + dX^l_b) (the leaf's part goes to dA_l when the leaf has its own generator),
+// dW = sum_b dW_b, dh_b = both parts; every sum over samples in sample order.
+__global__ void dense_leaf_reduce_kernel(LeafArgs a, const double* __restrict__ work, float* __restrict__ dA,
+                                         float* __restrict__ dA_leaf, float* __restrict__ dW, float* __restrict__ dh) {
+    const int n = a.n, d = a.d, nn = n * n, nd = n * d;
+    const size_t ws = leaf_work_stride(n, d);
+    const int total = 2 * nn + nd + a.batch;
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+        if (e < nn) {
+            double s = 0.0;
+            for (int b = 0; b < a.batch; ++b) {
+                const double* wb = work + (size_t)b * ws;
+                const double x = a.A_leaf ? wb[e] : wb[e] + wb[nn + e];
+                s = fma(-(double)a.h[b], x, s);
+            }
+            dA[e] = (float)s;
+        } else if (e < 2 * nn) {
+            if (!a.A_leaf || !dA_leaf) continue;
+            double s = 0.0;
+            for (int b = 0; b < a.batch; ++b) s = fma(-(double)a.h[b], work[(size_t)b * ws + e], s);
+            dA_leaf[e - nn] = (float)s;
+        } else if (e < 2 * nn + nd) {
+            if (!dW) continue;
+            double s = 0.0;
+            for (int b = 0; b < a.batch; ++b) s += work[(size_t)b * ws + e];
+            dW[e - 2 * nn] = (float)s;
+        } else {
+            const int b = e - 2 * nn - nd;
+            if (dh) dh[b] = (float)(work[(size_t)b * ws + ws - 2] + work[(size_t)b * ws + ws - 1]);
+        }
+    }
+}
+
 template <int NP>
 static size_t smem_bytes() {
     return sizeof(double) * (3 * NP * NP + NP);
@@ -421,5 +734,53 @@ extern "C" int ews_expm_adjoint_batched(const double* x, const double* g, double
     const size_t smem = smem_bytes<64>();
     cudaFuncSetAttribute(expm_adjoint_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     expm_adjoint_kernel<<<batch, XT, smem, s>>>(x, g, out, n);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+static int leaf_check(const LeafArgs& a) {
+    if (a.batch < 0 || a.n <= 0 || a.d <= 0 || a.q < 0) return EWS_ERR_INVALID_ARGUMENT;
+    if (a.n > 32 || a.d > 32 || a.q + 1 > TQ) return EWS_ERR_UNSUPPORTED;
+    if (!a.W && a.d != a.n) return EWS_ERR_INVALID_ARGUMENT;
+    if (a.batch > 0 && (!a.A || !a.h || !a.c1 || !a.c2)) return EWS_ERR_INVALID_ARGUMENT;
+    return EWS_OK;
+}
+
+extern "C" size_t ews_dense_leaf_work_size(int batch, int n, int d_in) {
+    if (batch <= 0 || n <= 0 || d_in <= 0) return 0;
+    return sizeof(double) * (size_t)batch * leaf_work_stride(n, d_in);
+}
+
+extern "C" int ews_dense_leaf(const float* A, const float* A_leaf, const float* h, const float* lift, const double* c1,
+                              const double* c2, int batch, int n, int d_in, int order, float* Dc, float* F, float* G,
+                              float* H, ews_stream_t stream) {
+    const LeafArgs a{A, A_leaf, h, lift, c1, c2, batch, n, d_in, order};
+    const int rc = leaf_check(a);
+    if (rc != EWS_OK || batch == 0) return rc;
+    if (!Dc || !F || !G || !H) return EWS_ERR_INVALID_ARGUMENT;
+    const size_t smem = sizeof(double) * (3 * (size_t)LTILE + 32);
+    cudaFuncSetAttribute(dense_leaf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dense_leaf_kernel<<<2 * batch, LT, smem, (cudaStream_t)stream>>>(a, Dc, F, G, H);
+    return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+}
+
+extern "C" int ews_dense_leaf_adjoint(const float* A, const float* A_leaf, const float* h, const float* lift,
+                                      const double* c1, const double* c2, int batch, int n, int d_in, int order,
+                                      const float* dDc, const float* dF, const float* dG, const float* dH, void* work,
+                                      size_t work_bytes, float* dA, float* dA_leaf, float* dh, float* dW,
+                                      ews_stream_t stream) {
+    const LeafArgs a{A, A_leaf, h, lift, c1, c2, batch, n, d_in, order};
+    const int rc = leaf_check(a);
+    if (rc != EWS_OK || batch == 0) return rc;
+    if (!dA || !work || work_bytes < ews_dense_leaf_work_size(batch, n, d_in)) return EWS_ERR_INVALID_ARGUMENT;
+    if (A_leaf && !dA_leaf) return EWS_ERR_INVALID_ARGUMENT;
+    if (lift && !dW) return EWS_ERR_INVALID_ARGUMENT;
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t smem = sizeof(double) * ((4 + (size_t)order + 1) * LTILE + 32);
+    cudaFuncSetAttribute(dense_leaf_adjoint_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    double* wk = static_cast<double*>(work);
+    dense_leaf_adjoint_kernel<<<2 * batch, LT, smem, s>>>(a, dDc, dF, dG, dH, wk);
+    const int total = 2 * n * n + n * d_in + batch;
+    dense_leaf_reduce_kernel<<<(total + 255) / 256, 256, 0, s>>>(a, wk, dA, A_leaf ? dA_leaf : nullptr,
+                                                                  lift ? dW : nullptr, dh);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }

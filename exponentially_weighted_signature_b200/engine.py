@@ -315,6 +315,61 @@ class SeriesTables(torch.autograd.Function):
         return dX, (dW.sum(0) if dW is not None else None), None, None
 
 
+class DenseLeaf(torch.autograd.Function):
+    """Both per-sample tables of the dense engine for a uniform clock, one library launch each way:
+    (A (n, n), h (B,), A_leaf (n, n) or None, W (n, d_in) or None, c1, c2 float64) -> D = I - expm(-h_b A)
+    (B, n, n) and the series tables F, G, H of -h_b A_leaf (A unless given), all float32 (evaluated in
+    float64). The VJP returns dA, dh, dA_leaf and dW, summed over samples in sample order on the device."""
+
+    @staticmethod
+    def forward(ctx, A, h, A_leaf, W, c1, c2):
+        _require_cuda(A, h, A_leaf, W)
+        A = A.to(torch.float32).contiguous()
+        h = h.to(torch.float32).contiguous()
+        Al = None if A_leaf is None else A_leaf.to(torch.float32).contiguous()
+        Wc = None if W is None else W.to(torch.float32).contiguous()
+        B, n = h.shape[0], A.shape[-1]
+        d = n if Wc is None else Wc.shape[-1]
+        q = c1.shape[0] - 1
+        dev = A.device
+        Dc = torch.empty((B, n, n), dtype=torch.float32, device=dev)
+        F = torch.empty((B, n, d), dtype=torch.float32, device=dev)
+        G = torch.empty((B, q + 1, n, d), dtype=torch.float32, device=dev)
+        H = torch.empty_like(G)
+        c1c, c2c = c1.contiguous(), c2.contiguous()
+        with _timed("ews_dense_leaf", dev, B, 1):
+            _lib.check(_lib.load().ews_dense_leaf(_ptr(A), _ptr(Al), _ptr(h), _ptr(Wc), _ptr(c1c), _ptr(c2c), B, n, d, q,
+                                                  _ptr(Dc), _ptr(F), _ptr(G), _ptr(H), _stream_ptr(dev)),
+                       "ews_dense_leaf")
+        ctx.save_for_backward(A, h, Al, Wc, c1c, c2c)
+        return Dc, F, G, H
+
+    @staticmethod
+    def backward(ctx, dDc, dF, dG, dH):
+        A, h, Al, Wc, c1, c2 = ctx.saved_tensors
+        B, n = h.shape[0], A.shape[-1]
+        d = n if Wc is None else Wc.shape[-1]
+        q = c1.shape[0] - 1
+        dev = A.device
+        f32 = lambda t: None if t is None else t.to(torch.float32).contiguous()
+        dDc, dF, dG, dH = f32(dDc), f32(dF), f32(dG), f32(dH)
+        lib = _lib.load()
+        work = torch.empty(int(lib.ews_dense_leaf_work_size(B, n, d)) // 8, dtype=torch.float64, device=dev)
+        dA = torch.empty((n, n), dtype=torch.float32, device=dev)
+        dAl = torch.empty_like(dA) if Al is not None else None
+        dh = torch.empty((B,), dtype=torch.float32, device=dev)
+        dW = torch.empty((n, d), dtype=torch.float32, device=dev) if Wc is not None else None
+        with _timed("ews_dense_leaf_adjoint", dev, B, 2):
+            _lib.check(lib.ews_dense_leaf_adjoint(_ptr(A), _ptr(Al), _ptr(h), _ptr(Wc), _ptr(c1), _ptr(c2), B, n, d, q,
+                                                  _ptr(dDc), _ptr(dF), _ptr(dG), _ptr(dH), _ptr(work),
+                                                  work.numel() * 8, _ptr(dA), _ptr(dAl), _ptr(dh), _ptr(dW),
+                                                  _stream_ptr(dev)),
+                       "ews_dense_leaf_adjoint")
+        need = ctx.needs_input_grad
+        return (dA if need[0] else None, dh if need[1] else None, dAl if need[2] else None,
+                dW if need[3] else None, None, None)
+
+
 class DenseScan(torch.autograd.Function):
     """Dense engine, uniform clock: (path, D = I - M, F, G, H) -> flat EWS (prefix or terminal)."""
 

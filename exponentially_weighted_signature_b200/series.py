@@ -162,22 +162,14 @@ def dense_leaf_tables(X: torch.Tensor, q: int, lift=None, coeffs=None):
 
 def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None, coeffs=None, A_leaf=None):
     """Per-sample tables of the dense engine for generator A (N, N), clock steps h (B,) and lift W (N, d_in):
-    the flow complement D = I - expm(-hA) and the series-leaf tables F, G, H (dense_leaf_tables), the
-    latter of ``A_leaf`` when given (a leaf that reads its own generator from A, e.g. the plane leaf).
-    Differentiable; evaluated in float64 and returned in float32. The exponential
-    (ews/core/chen_scan.py:155-168) and its VJP run in the library's expm kernels (CUDA tensors only)."""
-    from .engine import Expm
-
-    h64 = h.to(torch.float64)[:, None, None]
-    X = -h64 * A.to(torch.float64)  # (B, N, N)
-    N = A.shape[-1]
-    Dc = torch.eye(N, dtype=torch.float64, device=A.device) - Expm.apply(X)
-    Xl = X if A_leaf is None else -h64 * A_leaf.to(torch.float64)
-    from .engine import SeriesTables
+    the flow complement D = I - expm(-hA) (ews/core/chen_scan.py:155-168) and the series-leaf tables F, G, H
+    (dense_leaf_tables), the latter of ``A_leaf`` when given (a leaf that reads its own generator from A,
+    e.g. the plane leaf). Differentiable in A, h, A_leaf and W; evaluated in float64 by one library launch
+    each way (CUDA tensors only) and returned in float32."""
+    from .engine import DenseLeaf
 
     c1, c2 = _leaf_coeffs(int(q), str(A.device)) if coeffs is None else coeffs
-    F, G, H = SeriesTables.apply(Xl.contiguous(), lift, c1, c2)  # one library kernel each way
-    return Dc.float(), F, G, H
+    return DenseLeaf.apply(A, h, A_leaf, lift, c1, c2)
 
 
 # ------------------------------------------------------------------------------ plane leaf

@@ -272,6 +272,26 @@ int ews_series_tables_adjoint(const double* x, const double* lift, const double*
                               int n, int d_in, int order, const float* dF, const float* dG, const float* dH,
                               double* dX, double* dW, ews_stream_t stream);
 
+/* ---- the dense leaf, fused ------------------------------------------------------------------------------
+ * Both per-sample tables of the dense engine for a uniform clock in one launch, from the generator itself:
+ * the flow complement D_b = I - expm(x_b), x_b = -h_b A (ews/core/chen_scan.py:155-168), and the series
+ * tables F, G, H of x^l_b = -h_b A_leaf (A_leaf NULL: A) as ews_series_tables defines them. A, A_leaf (n, n),
+ * h (batch,), lift (n, d_in; NULL: the identity, d_in == n) float32; c1, c2 float64 on the device; outputs
+ * float32 D (batch, n, n), F (batch, n, d_in), G, H (batch, order+1, n, d_in). Evaluated in float64 (the
+ * exponential as ews_expm_batched). n, d_in <= 32, order <= 11.
+ *   ews_dense_leaf_adjoint: from the cotangents dD, dF, dG, dH (float32; any may be NULL: zeros) the
+ *   gradients dA (n, n), dA_leaf (n, n; required iff A_leaf), dh (batch,; may be NULL) and dW (n, d_in;
+ *   required iff lift), float32, each summed over samples in sample order (bit-reproducible). `work` is
+ *   caller-owned device memory of at least ews_dense_leaf_work_size(batch, n, d_in) bytes. Two launches. */
+size_t ews_dense_leaf_work_size(int batch, int n, int d_in);
+int ews_dense_leaf(const float* A, const float* A_leaf, const float* h, const float* lift, const double* c1,
+                   const double* c2, int batch, int n, int d_in, int order, float* D, float* F, float* G, float* H,
+                   ews_stream_t stream);
+int ews_dense_leaf_adjoint(const float* A, const float* A_leaf, const float* h, const float* lift, const double* c1,
+                           const double* c2, int batch, int n, int d_in, int order, const float* dD, const float* dF,
+                           const float* dG, const float* dH, void* work, size_t work_bytes, float* dA, float* dA_leaf,
+                           float* dh, float* dW, ews_stream_t stream);
+
 /* ---- utilities --------------------------------------------------------------------------------- */
 /* Every forward and backward workspace begins with a status block whose error word the call clears and
  * a timed-out device wait sets. */

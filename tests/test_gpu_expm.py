@@ -109,3 +109,91 @@ def test_series_tables_match_torch(n, d, q, lifted):
             assert float(a.abs().max()) == 0.0
         else:
             assert relerr(a.detach().cpu(), b2.detach().cpu()) <= 1e-6
+
+
+@pytest.mark.parametrize(
+    "B,n,d,q,lifted,own_leaf",
+    [(4, 32, 7, 3, True, False), (1, 5, 3, 0, True, True), (33, 16, 16, 11, False, False), (6, 32, 32, 8, True, True),
+     (3, 9, 4, 6, False, True)],
+)
+def test_dense_leaf_matches_the_torch_composition(B, n, d, q, lifted, own_leaf):
+    """ews_dense_leaf / _adjoint (the flow complement D = I - expm(-h_b A) and the series tables of
+    -h_b A_l in one launch each way, with dA, dh, dA_l and dW summed over samples on the device) against
+    the same composition in float64 torch (matrix_exp, series.dense_leaf_tables): relative error <= 1e-6
+    for every output and gradient (float32 outputs and cotangents). The clock steps span 1e-5 .. 3, so
+    the flows run from no squaring to several."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import series
+    from exponentially_weighted_signature_b200.engine import DenseLeaf
+
+    if not lifted:
+        d = n
+    g = torch.Generator().manual_seed(B * 1000 + n * 10 + q)
+    A = (0.5 * torch.eye(n, dtype=torch.float64) - torch.randn(n, n, generator=g, dtype=torch.float64) / np.sqrt(n))
+    A = A.float().cuda().requires_grad_(True)
+    h = torch.logspace(-5, 0.5, B, dtype=torch.float64).float().cuda().requires_grad_(True)
+    Al = (torch.randn(n, n, generator=g, dtype=torch.float64) / np.sqrt(n)).float().cuda().requires_grad_(True) if own_leaf else None
+    W = (torch.randn(n, d, generator=g, dtype=torch.float64) / np.sqrt(d)).float().cuda().requires_grad_(True) if lifted else None
+    c1, c2 = series._leaf_coeffs(q, "cuda")
+    Dc, F, G, H = DenseLeaf.apply(A, h, Al, W, c1, c2)
+
+    A64 = A.detach().double().requires_grad_(True)
+    h64 = h.detach().double().requires_grad_(True)
+    Al64 = None if Al is None else Al.detach().double().requires_grad_(True)
+    W64 = None if W is None else W.detach().double().requires_grad_(True)
+    X = -h64[:, None, None] * A64
+    Dr = torch.eye(n, dtype=torch.float64, device="cuda") - torch.linalg.matrix_exp(X)
+    Xl = X if Al64 is None else -h64[:, None, None] * Al64
+    Fr, Gr, Hr = series.dense_leaf_tables(Xl, q, W64, (c1, c2))
+    for a, b2 in ((Dc, Dr), (F, Fr), (G, Gr), (H, Hr)):
+        assert a.dtype == torch.float32
+        assert relerr(a.double().detach().cpu(), b2.detach().cpu()) <= 1e-6
+
+    ws = [torch.randn(t.shape, generator=g, dtype=torch.float32).cuda() for t in (Dc, F, G, H)]
+    ins = [A, h] + ([Al] if Al is not None else []) + ([W] if W is not None else [])
+    ins64 = [A64, h64] + ([Al64] if Al64 is not None else []) + ([W64] if W64 is not None else [])
+    got = torch.autograd.grad(sum((t * w).sum() for t, w in zip((Dc, F, G, H), ws)), ins)
+    ref = torch.autograd.grad(sum((t * w.double()).sum() for t, w in zip((Dr, Fr, Gr, Hr), ws)), ins64, allow_unused=True)
+    for a, b2, t in zip(got, ref, ins):
+        assert a.dtype == torch.float32 and a.shape == t.shape
+        b2 = torch.zeros_like(t, dtype=torch.float64) if b2 is None else b2
+        if float(b2.abs().max()) == 0.0:
+            assert float(a.abs().max()) == 0.0
+        else:
+            assert relerr(a.double().detach().cpu(), b2.detach().cpu()) <= 1e-6
+
+
+def test_dense_leaf_partial_cotangents():
+    """Only some of the tables reach the loss: the missing cotangents count as zeros (flows only, series
+    tables only), and the gradients match the float64 composition as above."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import series
+    from exponentially_weighted_signature_b200.engine import DenseLeaf
+
+    g = torch.Generator().manual_seed(7)
+    n, d, q, B = 12, 5, 4, 3
+    A = (torch.randn(n, n, generator=g) / np.sqrt(n)).cuda().requires_grad_(True)
+    h = torch.tensor([0.01, 0.3, 2.0]).cuda()
+    W = (torch.randn(n, d, generator=g) / np.sqrt(d)).cuda().requires_grad_(True)
+    c1, c2 = series._leaf_coeffs(q, "cuda")
+    for use in ("flow", "tables"):
+        Dc, F, G, H = DenseLeaf.apply(A, h, None, W, c1, c2)
+        A64 = A.detach().double().requires_grad_(True)
+        W64 = W.detach().double().requires_grad_(True)
+        X = -h.double()[:, None, None] * A64
+        if use == "flow":
+            loss = (Dc * Dc.detach()).sum()
+            loss64 = ((torch.eye(n, dtype=torch.float64, device="cuda") - torch.linalg.matrix_exp(X)) * Dc.detach().double()).sum()
+        else:
+            Fr, Gr, Hr = series.dense_leaf_tables(X, q, W64, (c1, c2))
+            loss = F.sum() + (H * 0.5).sum()
+            loss64 = Fr.sum() + (Hr * 0.5).sum()
+        got = torch.autograd.grad(loss, [A, W], allow_unused=True)
+        ref = torch.autograd.grad(loss64, [A64, W64], allow_unused=True)
+        for a, b2, t in zip(got, ref, (A, W)):
+            a = torch.zeros_like(t) if a is None else a
+            b2 = torch.zeros_like(t, dtype=torch.float64) if b2 is None else b2
+            if float(b2.abs().max()) == 0.0:
+                assert float(a.abs().max()) == 0.0
+            else:
+                assert relerr(a.double().detach().cpu(), b2.detach().cpu()) <= 1e-6
