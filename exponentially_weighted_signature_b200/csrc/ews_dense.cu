@@ -142,6 +142,30 @@ __device__ void load_slot_smem(const float* slot, float* P, float* S1, float* S2
     if (threadIdx.x < NP) S1[threadIdx.x] = ldcg(slot + MM + threadIdx.x);
 }
 
+// One slot held in registers by a 256-thread CTA (4 + 4 floats per thread, level 1 in the first 32
+// threads): the scans fetch the next element while the current product runs.
+struct SlotRegs {
+    float p[MM / 256], s2[MM / 256], s1;
+};
+
+__device__ __forceinline__ void slot_fetch(const float* slot, SlotRegs& r) {
+#pragma unroll
+    for (int k = 0; k < MM / 256; ++k) {
+        r.p[k] = ldcg(slot + threadIdx.x + 256 * k);
+        r.s2[k] = ldcg(slot + MM + NP + threadIdx.x + 256 * k);
+    }
+    r.s1 = threadIdx.x < NP ? ldcg(slot + MM + threadIdx.x) : 0.f;
+}
+
+__device__ __forceinline__ void slot_put(const SlotRegs& r, float* P, float* S1, float* S2) {
+#pragma unroll
+    for (int k = 0; k < MM / 256; ++k) {
+        P[threadIdx.x + 256 * k] = r.p[k];
+        S2[threadIdx.x + 256 * k] = r.s2[k];
+    }
+    if (threadIdx.x < NP) S1[threadIdx.x] = r.s1;
+}
+
 __device__ void identity_smem(float* P, float* S1, float* S2) {
     for (int e = threadIdx.x; e < MM; e += blockDim.x) {
         P[e] = 0.f;  // flow complement of the identity
@@ -1037,11 +1061,14 @@ __global__ void __launch_bounds__(CST) scan_local_kernel(Params p) {
     const int c0 = k * CG, c1 = min(g.C, c0 + CG);
     const size_t base = (size_t)b * g.C;
     load_slot_smem(p.agg + (base + c0) * g.SW, sm.P0, sm.S10, sm.S20);
+    SlotRegs nx;
+    if (c0 + 1 < c1) slot_fetch(p.agg + (base + c0 + 1) * g.SW, nx);
     __syncthreads();
     store_slot(p.incl + (base + c0) * g.SW, sm.P0, sm.S10, sm.S20);
     for (int c = c0 + 1; c < c1; ++c) {
-        load_slot_smem(p.agg + (base + c) * g.SW, sm.P1, sm.S11, sm.S21);
+        slot_put(nx, sm.P1, sm.S11, sm.S21);
         __syncthreads();
+        if (c + 1 < c1) slot_fetch(p.agg + (base + c + 1) * g.SW, nx);  // in flight during the product
         chen_mul_256(sm.P0, sm.S10, sm.S20, sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.vtmp);
         store_slot(p.incl + (base + c) * g.SW, sm.P0, sm.S10, sm.S20);
         __syncthreads();
@@ -1149,11 +1176,24 @@ __global__ void __launch_bounds__(CST) bscan_local_kernel(Params p) {
     __syncthreads();
     store_slot(p.gsuf + (base + c1) * g.SW, sm.P0, sm.S10, sm.S20);
     bscan_store_lam(p.incl + (base + c1) * g.SW, sm);
+    // the next chunk's aggregate G_c and local cotangent mu_c, fetched one step ahead
+    SlotRegs ng_, nm_;
+    if (c1 - 1 >= c0) {
+        slot_fetch(p.fagg + (base + c1 - 1) * g.SW, ng_);
+        slot_fetch(p.agg + (base + c1 - 1) * g.SW, nm_);
+    }
     for (int c = c1 - 1; c >= c0; --c) {
-        load_slot_smem(p.fagg + (base + c) * g.SW, sm.P1, sm.S11, sm.S21);
+        slot_put(ng_, sm.P1, sm.S11, sm.S21);
+        SlotRegs mu = nm_;
+        if (c - 1 >= c0) {
+            slot_fetch(p.fagg + (base + c - 1) * g.SW, ng_);
+            slot_fetch(p.agg + (base + c - 1) * g.SW, nm_);
+        }
         __syncthreads();
-        bscan_apply(sm);                 // mu <- J(G_c)^T mu
-        bscan_add_mu(sm, p.agg + (base + c) * g.SW);  //      + mu_c
+        bscan_apply(sm);  // mu <- J(G_c)^T mu
+#pragma unroll
+        for (int k = 0; k < MM / 256; ++k) sm.L2r[threadIdx.x + 256 * k] += mu.s2[k];  // + mu_c
+        if (threadIdx.x < NP) sm.L1[threadIdx.x] += mu.s1;
         __syncthreads();
         chen_mul_256(sm.P1, sm.S11, sm.S21, sm.P0, sm.S10, sm.S20, sm.P0, sm.S10, sm.S20, sm.T0, sm.T1, sm.v3);
         store_slot(p.gsuf + (base + c) * g.SW, sm.P0, sm.S10, sm.S20);
@@ -1855,10 +1895,28 @@ inline size_t table_smem_bytes(const Geom& g) {
 //   dT[rows, :] += c_t[rows] dx_t^T     (registers),
 //   dx_t = sum over the warp of T[rows, :]^T c_t[rows]   (a reduce-scatter of the 8 column sums, 9 shuffles),
 // and the warps' dT are summed in warp order at the end.
+constexpr int TG_SLAB = 8;    // intervals per staged slab of vector cotangents
+constexpr int TG_STAGES = 3;  // slabs in flight
+
+__host__ __device__ inline size_t table_reg_smem_bytes(int Lc, int QP) {
+    return sizeof(float) * (8 * (size_t)Lc + (size_t)TG_STAGES * TG_SLAB * loc_width(QP));
+}
+
+// Plain (non-multicast) bulk copy of `bytes` from global to this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tc::smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+                 : "memory");
+}
+
 template <int ROWS>
 __global__ void __launch_bounds__(128) table_grad_reg_kernel(Params p) {
     __shared__ __align__(16) float red[ROWS * 32 * 8];
-    extern __shared__ __align__(16) float xs[];  // the chunk's increments, 8 per interval
+    __shared__ __align__(8) uint64_t tbar[TG_STAGES];
+    extern __shared__ __align__(16) float xs[];  // the chunk's increments (8 per interval), then the slab ring
     const Geom& g = p.g;
     const int N = g.N, d = g.d_in, QP = g.QP, LW = loc_width(QP);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1866,6 +1924,21 @@ __global__ void __launch_bounds__(128) table_grad_reg_kernel(Params p) {
     const int c = tile / g.B, b = tile - c * g.B;
     const int t0 = c * g.Lc;
     const int len = min(g.Lc, g.T - t0);
+    const int nslab = (len + TG_SLAB - 1) / TG_SLAB;
+    float* ring = xs + 8 * g.Lc;
+    // the chunk's rows of [ds1 | dU_a | dV_a] are contiguous: slabs of TG_SLAB rows by bulk copies
+    const float* cbase = p.coef + ((size_t)b * g.T + t0) * LW;
+    auto issue = [&](int sl) {
+        const int k0 = sl * TG_SLAB, n = min(TG_SLAB, len - k0);
+        bulk_load(ring + (size_t)(sl % TG_STAGES) * TG_SLAB * LW, cbase + (size_t)k0 * LW,
+                  (uint32_t)(n * LW * sizeof(float)), tbar + sl % TG_STAGES);
+    };
+    if (tid == 0) {
+        for (int k = 0; k < TG_STAGES; ++k)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc::smem_u32(tbar + k)), "r"(1));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int sl = 0; sl < min(TG_STAGES, nslab); ++sl) issue(sl);
+    }
     float tab[ROWS][8], acc[ROWS][8];
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
@@ -1886,65 +1959,78 @@ __global__ void __launch_bounds__(128) table_grad_reg_kernel(Params p) {
     __syncthreads();
     // column owned after the reduce-scatter: bits 4, 3, 2 of the lane
     const int mycol = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-    float cv[ROWS];
-    int kk = warp;
-    if (kk < len) {
-        const float* cr = p.coef + ((size_t)b * g.T + t0 + kk) * LW + lane;
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) cv[r] = ldcg(cr + 32 * r);
-    }
-    for (; kk < len; kk += 4) {
-        const int t = t0 + kk;
-        float x[8];
-        {
-            const float4 x0 = *reinterpret_cast<const float4*>(xs + kk * 8);
-            const float4 x1 = *reinterpret_cast<const float4*>(xs + kk * 8 + 4);
-            x[0] = x0.x; x[1] = x0.y; x[2] = x0.z; x[3] = x0.w;
-            x[4] = x1.x; x[5] = x1.y; x[6] = x1.z; x[7] = x1.w;
-        }
-        float cur[ROWS];
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) cur[r] = cv[r];
-        if (kk + 4 < len) {  // the warp's next interval, in flight during this one
-            const float* cr = p.coef + ((size_t)b * g.T + t + 4) * LW + lane;
-#pragma unroll
-            for (int r = 0; r < ROWS; ++r) cv[r] = ldcg(cr + 32 * r);
-        }
-        float sv[8];
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) sv[cc] = 0.f;
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                acc[r][cc] = fmaf(cur[r], x[cc], acc[r][cc]);
-                sv[cc] = fmaf(tab[r][cc], cur[r], sv[cc]);
+    const int lim = 1 << 20;
+    int sl = 0;
+    for (; sl < nslab; ++sl) {
+        const int slot = sl % TG_STAGES;
+        const uint32_t par = (uint32_t)(sl / TG_STAGES) & 1u;
+        bool ok = false;
+        for (int it = 0; it < lim && !ok; ++it) ok = tc::mbar_try(tbar + slot, par);
+        if (__syncthreads_or(!ok)) break;  // a copy that never landed: reported below
+        const float* cs = ring + (size_t)slot * TG_SLAB * LW + lane;
+        const int k0 = sl * TG_SLAB, kend = min(len, k0 + TG_SLAB);
+        for (int kk = k0 + warp; kk < kend; kk += 4) {
+            const int t = t0 + kk;
+            float x[8];
+            {
+                const float4 x0 = *reinterpret_cast<const float4*>(xs + kk * 8);
+                const float4 x1 = *reinterpret_cast<const float4*>(xs + kk * 8 + 4);
+                x[0] = x0.x; x[1] = x0.y; x[2] = x0.z; x[3] = x0.w;
+                x[4] = x1.x; x[5] = x1.y; x[6] = x1.z; x[7] = x1.w;
             }
-        // reduce-scatter of the 8 column sums over the warp
-        const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0, hi4 = (lane & 4) != 0;
-        float s4[4];
+            float cur[ROWS];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float send = hi16 ? sv[i] : sv[i + 4];
-            const float keep = hi16 ? sv[i + 4] : sv[i];
-            s4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-        }
-        float s2[2];
+            for (int r = 0; r < ROWS; ++r) cur[r] = cs[(kk - k0) * LW + 32 * r];
+            float sv[8];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const float send = hi8 ? s4[i] : s4[i + 2];
-            const float keep = hi8 ? s4[i + 2] : s4[i];
-            s2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+            for (int cc = 0; cc < 8; ++cc) sv[cc] = 0.f;
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    acc[r][cc] = fmaf(cur[r], x[cc], acc[r][cc]);
+                    sv[cc] = fmaf(tab[r][cc], cur[r], sv[cc]);
+                }
+            // reduce-scatter of the 8 column sums over the warp
+            const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0, hi4 = (lane & 4) != 0;
+            float s4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float send = hi16 ? sv[i] : sv[i + 4];
+                const float keep = hi16 ? sv[i + 4] : sv[i];
+                s4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+            }
+            float s2[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const float send = hi8 ? s4[i] : s4[i + 2];
+                const float keep = hi8 ? s4[i + 2] : s4[i];
+                s2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+            }
+            float s1;
+            {
+                const float send = hi4 ? s2[0] : s2[1];
+                const float keep = hi4 ? s2[1] : s2[0];
+                s1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+            s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+            if ((lane & 3) == 0 && mycol < d) p.grad_dx[((size_t)b * g.T + t) * d + mycol] = s1;
         }
-        float s1;
-        {
-            const float send = hi4 ? s2[0] : s2[1];
-            const float keep = hi4 ? s2[1] : s2[0];
-            s1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        __syncthreads();  // the slot is read: refill it
+        if (tid == 0 && sl + TG_STAGES < nslab) issue(sl + TG_STAGES);
+    }
+    if (sl < nslab) {
+        // a bounded wait ran out: report it, let the copies in flight land (bounded) and leave the partial
+        if (tid == 0) {
+            if (atomicCAS(&p.st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) p.st->err_tile = tile;
+            for (int k = sl; k < min(nslab, sl + TG_STAGES); ++k) {
+                bool done = false;
+                for (int it = 0; it < lim && !done; ++it)
+                    done = tc::mbar_try(tbar + k % TG_STAGES, (uint32_t)(k / TG_STAGES) & 1u);
+            }
         }
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-        if ((lane & 3) == 0 && mycol < d) p.grad_dx[((size_t)b * g.T + t) * d + mycol] = s1;
+        return;
     }
     // the warps' table gradients, summed in warp order
     for (int w = 0; w < 4; ++w) {
@@ -2038,18 +2124,27 @@ __global__ void __launch_bounds__(128) table_grad_kernel(Params p) {
 }
 
 
-// Deterministic per-sample reduction over chunks, compacted to the real dimensions.
-__global__ void reduce_kernel(Params p, float* grad_d, float* grad_f, float* grad_g, float* grad_h) {
+// Deterministic per-sample reduction over chunks, compacted to the real dimensions. A CTA takes 32
+// consecutive outputs; its eight warps sum interleaved eighths of the chunks (warp w: chunks w, w + 8, ...)
+// and the eight partial sums are added in warp order, so the result does not depend on the schedule.
+constexpr int RED_SLICES = 8;
+
+__global__ void __launch_bounds__(32 * RED_SLICES) reduce_kernel(Params p, float* grad_d, float* grad_f, float* grad_g,
+                                                                 float* grad_h) {
+    __shared__ float part[RED_SLICES][32];
     const Geom& g = p.g;
     const int N = g.N, d = g.d_in;
     const int tabn = (1 + 2 * g.QP) * NP * d;
     const int stride = MM + tabn;
     const int per_sample = N * N + (1 + 2 * g.QP) * N * d;
     const size_t total = (size_t)g.B * per_sample;
-    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-        const int b = (int)(e / per_sample), r = (int)(e - (size_t)b * per_sample);
-        int off;
-        float* dst;
+    const int lane = threadIdx.x & 31, slice = threadIdx.x >> 5;
+    const size_t e = (size_t)blockIdx.x * 32 + lane;
+    int b = 0, r = 0, off = 0;
+    float* dst = nullptr;
+    if (e < total) {
+        b = (int)(e / per_sample);
+        r = (int)(e - (size_t)b * per_sample);
         if (r < N * N) {
             const int i = r / N, j = r - i * N;
             off = i * NP + j;
@@ -2061,13 +2156,53 @@ __global__ void reduce_kernel(Params p, float* grad_d, float* grad_f, float* gra
             else if (blk <= g.QP) dst = grad_g + ((size_t)b * g.QP + (blk - 1)) * N * d + rem;
             else dst = grad_h + ((size_t)b * g.QP + (blk - 1 - g.QP)) * N * d + rem;
         }
-        float acc = 0.f;
-        for (int cr = 0; cr < g.C; ++cr) acc += p.partials[((size_t)cr * g.B + b) * stride + off];
-        *dst = r < N * N ? -acc : acc;  // the flow block accumulates dL/dM; dL/dD = -dL/dM
+    }
+    float acc = 0.f;
+    if (dst)
+#pragma unroll 4
+        for (int cr = slice; cr < g.C; cr += RED_SLICES) acc += p.partials[((size_t)cr * g.B + b) * stride + off];
+    part[slice][lane] = acc;
+    __syncthreads();
+    if (slice == 0 && dst) {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < RED_SLICES; ++k) s += part[k][lane];
+        *dst = r < N * N ? -s : s;  // the flow block accumulates dL/dM; dL/dD = -dL/dM
     }
 }
 
 // ---------------------------------------------------------------------------------- host side
+
+// A second stream per (host thread, device) for the forward's independent prologue kernels, forked from
+// and joined back into the caller's stream with events (both capture into a CUDA graph as a fork / join).
+// Created on the first call outside a capture; while none exists a capturing call stays on one stream.
+struct SideStream {
+    cudaStream_t s2 = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+static SideStream* side_stream(cudaStream_t s) {
+    constexpr int kMaxDev = 64;
+    thread_local SideStream per_dev[kMaxDev];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
+    SideStream& ss = per_dev[dev];
+    if (!ss.s2) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+        if (cudaStreamCreateWithFlags(&ss.s2, cudaStreamNonBlocking) != cudaSuccess) {
+            ss.s2 = nullptr;
+            return nullptr;
+        }
+        if (cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
+            cudaStreamDestroy(ss.s2);
+            ss.s2 = nullptr;
+            return nullptr;
+        }
+    }
+    return &ss;
+}
 
 static int num_sms() {
     static int n = 0;
@@ -2101,17 +2236,19 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
         g->Lc = a->chunk;
     } else {
         // The chains stack 4 chunks of a sample per CTA: the forward's output pass and the backward's
-        // zero-carry pass run 3 CTAs per SM, the exact pass 2 (its steps cost more; the model counts all three
-        // passes at 3). Pick the chunk length that minimises the chains' waves x steps (plus a per-tile
-        // overhead of ~10 steps and the scans' sequential products).
+        // zero-carry pass run 3 CTAs per SM, the exact pass 2. Pick the chunk length that minimises the
+        // passes' waves x (steps + a per-tile overhead of ~10 steps), weighted by their measured costs per
+        // wave-step (~5.8 us for each of the first two, ~11.7 us for the exact pass at N = 32), plus the
+        // scans and per-chunk kernels, which grow with the number of chunks (~0.13 us each).
         const int sms = num_sms();
         double best = 1e30;
         int bestL = 256;
         for (int L = 16; L <= 512; ++L) {
             const int C = (g->T + L - 1) / L;
             const long G = (long)g->B * ((C + 3) / 4);
-            const long waves = (G + 3L * sms - 1) / (3L * sms);
-            const double cost = (L + 10.0) * (double)(3 * waves) + 0.6 * C / 8.0;
+            const long w3 = (G + 3L * sms - 1) / (3L * sms);
+            const long w2 = (G + 2L * sms - 1) / (2L * sms);
+            const double cost = (L + 10.0) * (11.6 * (double)w3 + 11.7 * (double)w2) + 0.13 * (double)g->B * C;
             if (cost < best) {
                 best = cost;
                 bestL = L;
@@ -2236,19 +2373,22 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     p.carry = (float*)(ws + L.carry);
     p.pw = (float*)(ws + L.pw);
     p.loc = (float*)(ws + L.loc);
-    power_kernel<<<g.B, NT, 5 * MM * sizeof(float), s>>>(p);
-    if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
-    {
-        const size_t lsmem = local_smem_bytes(g.d_in, g.QP);
-        if (lsmem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
-        cudaFuncSetAttribute(local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem);
-        const int spans = (g.T + LSPAN - 1) / LSPAN;
-        local_kernel<<<g.B * spans, LNT, lsmem, s>>>(p);
-        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
-    }
+    const size_t lsmem = local_smem_bytes(g.d_in, g.QP);
+    if (lsmem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+    cudaFuncSetAttribute(local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem);
     p.pows = (float*)(ws + L.pows);
     p.g.agg_pre = 1;
-    powers_kernel<<<g.B, PWT, 0, s>>>(p);
+    // the flow powers (B CTAs each) beside the local terms (B x spans CTAs): independent until agg_kernel
+    SideStream* ss = side_stream(s);
+    cudaStream_t sp = s;
+    if (ss && cudaEventRecord(ss->fork, s) == cudaSuccess && cudaStreamWaitEvent(ss->s2, ss->fork, 0) == cudaSuccess)
+        sp = ss->s2;
+    power_kernel<<<g.B, NT, 5 * MM * sizeof(float), sp>>>(p);
+    powers_kernel<<<g.B, PWT, 0, sp>>>(p);
+    const int spans = (g.T + LSPAN - 1) / LSPAN;
+    local_kernel<<<g.B * spans, LNT, lsmem, s>>>(p);
+    if (sp != s && (cudaEventRecord(ss->join, sp) != cudaSuccess || cudaStreamWaitEvent(s, ss->join, 0) != cudaSuccess))
+        return EWS_ERR_LAUNCH;
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     {
         const int arc = launch_agg_q(p, s);
@@ -2375,7 +2515,12 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         if (tsmem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
         if (g.QP <= 4 && g.d_in <= 8) {
             const int rows = 1 + 2 * g.QP;
-            const size_t xsm = sizeof(float) * 8 * (size_t)g.Lc;  // the chunk's increments
+            const size_t xsm = table_reg_smem_bytes(g.Lc, g.QP);  // the chunk's increments and the slab ring
+            const void* tk = rows == 3 ? (const void*)table_grad_reg_kernel<3>
+                             : rows == 5 ? (const void*)table_grad_reg_kernel<5>
+                             : rows == 7 ? (const void*)table_grad_reg_kernel<7>
+                                         : (const void*)table_grad_reg_kernel<9>;
+            cudaFuncSetAttribute(tk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xsm);
             if (rows == 3) table_grad_reg_kernel<3><<<g.C * g.B, 128, xsm, s>>>(p);
             else if (rows == 5) table_grad_reg_kernel<5><<<g.C * g.B, 128, xsm, s>>>(p);
             else if (rows == 7) table_grad_reg_kernel<7><<<g.C * g.B, 128, xsm, s>>>(p);
@@ -2387,8 +2532,7 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     }
     const size_t total = (size_t)g.B * (g.N * g.N + (1 + 2 * g.QP) * g.N * g.d_in);
-    const int threads = 256;
-    reduce_kernel<<<(int)std::min<size_t>((total + threads - 1) / threads, 65535), threads, 0, s>>>(
-        p, a->grad_d, a->grad_f, a->grad_g, a->grad_h);
+    reduce_kernel<<<(unsigned)((total + 31) / 32), 32 * RED_SLICES, 0, s>>>(p, a->grad_d, a->grad_f, a->grad_g,
+                                                                           a->grad_h);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
