@@ -363,33 +363,67 @@ __global__ void __launch_bounds__(XT) series_tables_adjoint_kernel(
 // Both tables of the dense engine from the generator in one launch per direction: the flow complement
 // D_b = I - expm(X_b) with X_b = -h_b A, and the series tables F, G, H of X^l_b = -h_b A_l (A_l the leaf's
 // own generator, A itself unless given). CTAs [0, batch) evaluate the flows, CTAs [batch, 2 batch) the
-// series tables, side by side. 1024 threads: thread (i, j) = (tid >> 5, tid & 31) owns element (i, j) of
-// every padded 32 x 32 float64 tile (row stride LD = 33 doubles, so the transposed reads do not collide
-// on banks). The backward evaluates the Frechet derivative of the exponential as the coupled recursion of
-// the block-triangular identity (the [[X^T, G], [0, X^T]] exponential without its zero and repeated
-// blocks: three 32 x 32 products per step instead of a 64 x 64 one) beside the series adjoint, and one
-// more launch sums the per-sample gradients over the batch in a fixed order.
-constexpr int LT = 1024;
-constexpr int LD = 33;
+// series tables, side by side. 256 threads: thread (r, c) = (tid >> 4, tid & 15) owns the 2 x 2 block at
+// rows 2r, 2r+1 and columns 2c, 2c+1 of every padded 32 x 32 float64 tile (row stride LD = 34 doubles: 16-byte
+// aligned column pairs, rows 2r and 2r+2 on different banks). A product step reads two A values and one
+// pair of B values per k for four FMAs, so the shared-memory pipe no longer bounds it. The backward
+// evaluates the Frechet derivative of the exponential as the coupled recursion of the block-triangular
+// identity (the [[X^T, G], [0, X^T]] exponential without its zero and repeated blocks: three 32 x 32 products
+// per step instead of a 64 x 64 one) beside the series adjoint, and one more launch sums the per-sample
+// gradients over the batch in a fixed order.
+constexpr int LT = 256;
+constexpr int LD = 34;
 constexpr int LTILE = 32 * LD;
 
-__device__ __forceinline__ double mm_nn(const double* A, const double* B, int i, int j) {
-    double acc = 0.0;
+__device__ __forceinline__ int blk_r() { return 2 * (threadIdx.x >> 4); }
+__device__ __forceinline__ int blk_c() { return 2 * (threadIdx.x & 15); }
+
+// acc (+)= A B on the thread's 2 x 2 block
+template <bool ADD>
+__device__ __forceinline__ void bm_nn(const double* A, const double* B, double acc[2][2]) {
+    const int r0 = blk_r(), c0 = blk_c();
+    if (!ADD) acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.0;
 #pragma unroll 8
-    for (int k = 0; k < 32; ++k) acc = fma(A[i * LD + k], B[k * LD + j], acc);
-    return acc;
+    for (int k = 0; k < 32; ++k) {
+        const double a0 = A[r0 * LD + k], a1 = A[(r0 + 1) * LD + k];
+        const double2 bb = *reinterpret_cast<const double2*>(B + k * LD + c0);
+        acc[0][0] = fma(a0, bb.x, acc[0][0]);
+        acc[0][1] = fma(a0, bb.y, acc[0][1]);
+        acc[1][0] = fma(a1, bb.x, acc[1][0]);
+        acc[1][1] = fma(a1, bb.y, acc[1][1]);
+    }
 }
-__device__ __forceinline__ double mm_tn(const double* A, const double* B, int i, int j) {  // (A^T B)[i][j]
-    double acc = 0.0;
+
+// acc (+)= A^T B on the thread's 2 x 2 block
+template <bool ADD>
+__device__ __forceinline__ void bm_tn(const double* A, const double* B, double acc[2][2]) {
+    const int r0 = blk_r(), c0 = blk_c();
+    if (!ADD) acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.0;
 #pragma unroll 8
-    for (int k = 0; k < 32; ++k) acc = fma(A[k * LD + i], B[k * LD + j], acc);
-    return acc;
+    for (int k = 0; k < 32; ++k) {
+        const double2 aa = *reinterpret_cast<const double2*>(A + k * LD + r0);
+        const double2 bb = *reinterpret_cast<const double2*>(B + k * LD + c0);
+        acc[0][0] = fma(aa.x, bb.x, acc[0][0]);
+        acc[0][1] = fma(aa.x, bb.y, acc[0][1]);
+        acc[1][0] = fma(aa.y, bb.x, acc[1][0]);
+        acc[1][1] = fma(aa.y, bb.y, acc[1][1]);
+    }
 }
-__device__ __forceinline__ double mm_nt(const double* A, const double* B, int i, int j) {  // (A B^T)[i][j]
-    double acc = 0.0;
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) acc = fma(A[i * LD + k], B[j * LD + k], acc);
-    return acc;
+
+__device__ __forceinline__ void blk_store(double* T, const double v[2][2]) {
+    const int r0 = blk_r(), c0 = blk_c();
+    *reinterpret_cast<double2*>(T + r0 * LD + c0) = make_double2(v[0][0], v[0][1]);
+    *reinterpret_cast<double2*>(T + (r0 + 1) * LD + c0) = make_double2(v[1][0], v[1][1]);
+}
+
+__device__ __forceinline__ void blk_load(const double* T, double v[2][2]) {
+    const int r0 = blk_r(), c0 = blk_c();
+    const double2 x0 = *reinterpret_cast<const double2*>(T + r0 * LD + c0);
+    const double2 x1 = *reinterpret_cast<const double2*>(T + (r0 + 1) * LD + c0);
+    v[0][0] = x0.x;
+    v[0][1] = x0.y;
+    v[1][0] = x1.x;
+    v[1][1] = x1.y;
 }
 
 // Largest column sum of |T0| + |T1| (T1 may be NULL) over the padded tile, to every thread; `red` holds 32.
@@ -427,11 +461,11 @@ __device__ __forceinline__ int halvings(double nrm) {
 __device__ double block_sum(double v, double* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const int w = threadIdx.x >> 5;
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     if ((threadIdx.x & 31) == 0) red[w] = v;
     __syncthreads();
     double s = 0.0;
-    for (int k = 0; k < 32; ++k) s += red[k];
+    for (int k = 0; k < nw; ++k) s += red[k];
     __syncthreads();
     return s;
 }
@@ -442,17 +476,33 @@ struct LeafArgs {
     int batch, n, d, q;
 };
 
-// The sample's generator tile -h_b G (G = A, or the leaf's A_l) into X.
-__device__ void load_generator(const LeafArgs& a, int b, bool leaf, double* X) {
-    const int i = threadIdx.x >> 5, j = threadIdx.x & 31;
+// The sample's generator tile -h_b G (G = A, or the leaf's A_l) into X; the thread's block of G to `gen`.
+__device__ void load_generator(const LeafArgs& a, int b, bool leaf, double* X, double gen[2][2]) {
     const float* g = (leaf && a.A_leaf) ? a.A_leaf : a.A;
     const double hb = (double)a.h[b];
-    X[i * LD + j] = (i < a.n && j < a.n) ? -hb * (double)g[i * a.n + j] : 0.0;
+    const int r0 = blk_r(), c0 = blk_c();
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+            const int i = r0 + u, j = c0 + v;
+            gen[u][v] = (i < a.n && j < a.n) ? (double)g[i * a.n + j] : 0.0;
+            X[i * LD + j] = -hb * gen[u][v];
+        }
 }
 
-__device__ void load_lift(const LeafArgs& a, double* W) {
-    const int i = threadIdx.x >> 5, j = threadIdx.x & 31;
-    W[i * LD + j] = (i < a.n && j < a.d) ? (a.W ? (double)a.W[i * a.d + j] : (i == j ? 1.0 : 0.0)) : 0.0;
+// The lift W (the identity when NULL) into W, and optionally its transpose into WT.
+__device__ void load_lift(const LeafArgs& a, double* W, double* WT) {
+    const int r0 = blk_r(), c0 = blk_c();
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+            const int i = r0 + u, j = c0 + v;
+            const double w = (i < a.n && j < a.d) ? (a.W ? (double)a.W[i * a.d + j] : (i == j ? 1.0 : 0.0)) : 0.0;
+            W[i * LD + j] = w;
+            if (WT) WT[j * LD + i] = w;
+        }
 }
 
 __global__ void __launch_bounds__(LT) dense_leaf_kernel(LeafArgs a, float* __restrict__ Dc, float* __restrict__ F,
@@ -462,73 +512,107 @@ __global__ void __launch_bounds__(LT) dense_leaf_kernel(LeafArgs a, float* __res
     double* T0 = X + LTILE;
     double* T1 = T0 + LTILE;
     double* red = T1 + LTILE;
-    const int i = threadIdx.x >> 5, j = threadIdx.x & 31;
+    const int r0 = blk_r(), c0 = blk_c();
     const bool leaf = blockIdx.x >= a.batch;
     const int b = leaf ? blockIdx.x - a.batch : blockIdx.x;
     const int n = a.n, d = a.d, QP = a.q + 1;
-    const double dij = (i == j) ? 1.0 : 0.0;
-    load_generator(a, b, leaf, X);
+    double id[2][2], gen[2][2], t[2][2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int v = 0; v < 2; ++v) id[u][v] = (r0 + u == c0 + v) ? 1.0 : 0.0;
+    load_generator(a, b, leaf, X, gen);
     if (!leaf) {
         // D = I - expm(X): scaling, degree-14 Taylor by Horner, squarings
         __syncthreads();
         const int s = halvings(col_norm1(X, nullptr, red));
-        const double x = X[i * LD + j] * ldexp(1.0, -s);
+        const double sc = ldexp(1.0, -s);
+        double x[2][2];
+        blk_load(X, x);
         __syncthreads();
-        X[i * LD + j] = x;
         constexpr int DEG = 14;
-        T0[i * LD + j] = dij + x / DEG;
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                x[u][v] *= sc;
+                t[u][v] = id[u][v] + x[u][v] / DEG;
+            }
+        blk_store(X, x);
+        blk_store(T0, t);
         __syncthreads();
         for (int k = DEG - 1; k >= 1; --k) {
-            const double t = mm_nn(X, T0, i, j);
+            bm_nn<false>(X, T0, t);
             __syncthreads();
-            T0[i * LD + j] = dij + t / k;
-            __syncthreads();
-        }
-        for (int r = 0; r < s; ++r) {
-            const double t = mm_nn(T0, T0, i, j);
-            __syncthreads();
-            T0[i * LD + j] = t;
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int v = 0; v < 2; ++v) t[u][v] = id[u][v] + t[u][v] / k;
+            blk_store(T0, t);
             __syncthreads();
         }
-        if (i < n && j < n) Dc[((size_t)b * n + i) * n + j] = (float)(dij - T0[i * LD + j]);
+        for (int rr = 0; rr < s; ++rr) {
+            bm_nn<false>(T0, T0, t);
+            __syncthreads();
+            blk_store(T0, t);
+            __syncthreads();
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                const int i = r0 + u, j = c0 + v;
+                if (i < n && j < n) Dc[((size_t)b * n + i) * n + j] = (float)(id[u][v] - t[u][v]);
+            }
         return;
     }
     // series tables: P_a = X^a / a! (T0), G_a = P_a W (registers), then F and H from the G's
-    load_lift(a, T1);
-    T0[i * LD + j] = dij;
+    load_lift(a, T1, nullptr);
+    blk_store(T0, id);
     __syncthreads();
-    double g[TQ];
+    double g[TQ][2][2];
 #pragma unroll
     for (int p = 0; p < TQ; ++p) {
-        g[p] = 0.0;
+        g[p][0][0] = g[p][0][1] = g[p][1][0] = g[p][1][1] = 0.0;
         if (p < QP) {
-            g[p] = mm_nn(T0, T1, i, j);
+            bm_nn<false>(T0, T1, g[p]);
             if (p + 1 < QP) {
-                const double t = mm_nn(T0, X, i, j) / (double)(p + 1);
+                bm_nn<false>(T0, X, t);
                 __syncthreads();
-                T0[i * LD + j] = t;
+                const double inv = 1.0 / (double)(p + 1);
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+#pragma unroll
+                    for (int v = 0; v < 2; ++v) t[u][v] *= inv;
+                blk_store(T0, t);
                 __syncthreads();
             }
         }
     }
-    if (i < n && j < d) {
-        const size_t e = (size_t)i * d + j, nd = (size_t)n * d;
-        double f = 0.0;
+    const size_t nd = (size_t)n * d;
 #pragma unroll
-        for (int p = 0; p < TQ; ++p)
-            if (p < QP) {
-                f = fma(a.c1[p], g[p], f);
-                G[((size_t)b * QP + p) * nd + e] = (float)g[p];
-            }
-        F[(size_t)b * nd + e] = (float)f;
-        for (int r = 0; r < QP; ++r) {
-            double hv = 0.0;
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+            const int i = r0 + u, j = c0 + v;
+            if (i >= n || j >= d) continue;
+            const size_t e = (size_t)i * d + j;
+            double f = 0.0;
 #pragma unroll
             for (int p = 0; p < TQ; ++p)
-                if (p < QP) hv = fma(a.c2[r * QP + p], g[p], hv);
-            H[((size_t)b * QP + r) * nd + e] = (float)hv;
+                if (p < QP) {
+                    f = fma(a.c1[p], g[p][u][v], f);
+                    G[((size_t)b * QP + p) * nd + e] = (float)g[p][u][v];
+                }
+            F[(size_t)b * nd + e] = (float)f;
+            for (int rr = 0; rr < QP; ++rr) {
+                double hv = 0.0;
+#pragma unroll
+                for (int p = 0; p < TQ; ++p)
+                    if (p < QP) hv = fma(a.c2[rr * QP + p], g[p][u][v], hv);
+                H[((size_t)b * QP + rr) * nd + e] = (float)hv;
+            }
         }
-    }
 }
 
 // Per-sample gradients into `work` (float64, per sample: dX of the flows n x n, dX of the leaf n x n, dW
@@ -545,96 +629,179 @@ __global__ void __launch_bounds__(LT) dense_leaf_adjoint_kernel(LeafArgs a, cons
     double* T0 = X + LTILE;
     double* T1 = T0 + LTILE;
     double* T2 = T1 + LTILE;
-    double* red = T2 + LTILE;
+    double* XT = T2 + LTILE;
+    double* WT = XT + LTILE;
+    double* red = WT + LTILE;
     double* P = red + 32;  // leaf role: P_0 .. P_q
-    const int i = threadIdx.x >> 5, j = threadIdx.x & 31;
+    const int r0 = blk_r(), c0 = blk_c();
     const bool leaf = blockIdx.x >= a.batch;
     const int b = leaf ? blockIdx.x - a.batch : blockIdx.x;
     const int n = a.n, d = a.d, QP = a.q + 1;
-    const double dij = (i == j) ? 1.0 : 0.0;
     const size_t ws = leaf_work_stride(n, d);
     double* wb = work + (size_t)b * ws;
-    const float* gsrc = (leaf && a.A_leaf) ? a.A_leaf : a.A;
-    const double gen = (i < n && j < n) ? (double)gsrc[i * n + j] : 0.0;
-    load_generator(a, b, leaf, X);
+    double id[2][2], gen[2][2], tp[2][2], tq[2][2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int v = 0; v < 2; ++v) id[u][v] = (r0 + u == c0 + v) ? 1.0 : 0.0;
+    load_generator(a, b, leaf, X, gen);
     if (!leaf) {
         // dX = L(X^T, C) with C = -dD (the cotangent of expm(X)); C scaled to unit 1-norm first
-        double c = 0.0;
-        if (dDc && i < n && j < n) c = -(double)dDc[((size_t)b * n + i) * n + j];
-        T1[i * LD + j] = c;
+        double cv[2][2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                const int i = r0 + u, j = c0 + v;
+                cv[u][v] = (dDc && i < n && j < n) ? -(double)dDc[((size_t)b * n + i) * n + j] : 0.0;
+            }
+        blk_store(T1, cv);
         __syncthreads();
         const double cn = col_norm1(T1, nullptr, red);
         const double cs = cn > 0.0 ? 1.0 / cn : 0.0;
         // Y = X^T and C / ||C|| (T2, T1); the scaling is that of the block matrix [[Y, C'], [0, Y]]
-        T2[i * LD + j] = X[j * LD + i];
-        T1[i * LD + j] = c * cs;
+        double y[2][2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                y[u][v] = X[(c0 + v) * LD + r0 + u];
+                cv[u][v] *= cs;
+            }
+        blk_store(T2, y);
+        blk_store(T1, cv);
         __syncthreads();
         const int s = halvings(col_norm1(T2, T1, red));  // (synchronises before returning)
         const double sc = ldexp(1.0, -s);
-        const double y = T2[i * LD + j] * sc, cc = T1[i * LD + j] * sc;
-        __syncthreads();
-        T2[i * LD + j] = y;  // Y
-        T1[i * LD + j] = cc; // C'
-        // the block [[Pm, Qm], [0, Pm]]: Pm in X, Qm in T0
         constexpr int DEG = 14;
-        X[i * LD + j] = dij + y / DEG;
-        T0[i * LD + j] = cc / DEG;
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                y[u][v] *= sc;
+                cv[u][v] *= sc;
+                tp[u][v] = id[u][v] + y[u][v] / DEG;
+                tq[u][v] = cv[u][v] / DEG;
+            }
+        blk_store(T2, y);   // Y
+        blk_store(T1, cv);  // C'
+        blk_store(X, tp);   // the block [[Pm, Qm], [0, Pm]]: Pm in X, Qm in T0
+        blk_store(T0, tq);
         __syncthreads();
         for (int k = DEG - 1; k >= 1; --k) {
-            const double tp = mm_nn(T2, X, i, j);
-            const double tq = mm_nn(T2, T0, i, j) + mm_nn(T1, X, i, j);
+            bm_nn<false>(T2, X, tp);
+            bm_nn<false>(T2, T0, tq);
+            bm_nn<true>(T1, X, tq);
             __syncthreads();
-            X[i * LD + j] = dij + tp / k;
-            T0[i * LD + j] = tq / k;
+            const double inv = 1.0 / (double)k;
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int v = 0; v < 2; ++v) {
+                    tp[u][v] = id[u][v] + tp[u][v] * inv;
+                    tq[u][v] *= inv;
+                }
+            blk_store(X, tp);
+            blk_store(T0, tq);
             __syncthreads();
         }
-        for (int r = 0; r < s; ++r) {
-            const double tp = mm_nn(X, X, i, j);
-            const double tq = mm_nn(X, T0, i, j) + mm_nn(T0, X, i, j);
+        for (int rr = 0; rr < s; ++rr) {
+            bm_nn<false>(X, X, tp);
+            bm_nn<false>(X, T0, tq);
+            bm_nn<true>(T0, X, tq);
             __syncthreads();
-            X[i * LD + j] = tp;
-            T0[i * LD + j] = tq;
+            blk_store(X, tp);
+            blk_store(T0, tq);
             __syncthreads();
         }
-        const double dx = T0[i * LD + j] * cn;
-        if (i < n && j < n) wb[(size_t)i * n + j] = dx;
-        const double dh = block_sum(-gen * dx, red);
+        double dh = 0.0;
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                const int i = r0 + u, j = c0 + v;
+                const double dx = tq[u][v] * cn;
+                if (i < n && j < n) wb[(size_t)i * n + j] = dx;
+                dh = fma(-gen[u][v], dx, dh);
+            }
+        dh = block_sum(dh, red);
         if (threadIdx.x == 0) wb[ws - 2] = dh;
         return;
     }
     // series adjoint: dG~_b = dG_b + c1_b dF + sum_a c2_ab dH_a; dW += P_b^T dG~_b;
     // R_b = dG~_b W^T + R_{b+1} X^T / (b + 1); dX += P_{b-1}^T R_b / b
-    load_lift(a, T2);
-    P[i * LD + j] = dij;
+    load_lift(a, T2, WT);
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int v = 0; v < 2; ++v) XT[(c0 + v) * LD + r0 + u] = X[(r0 + u) * LD + c0 + v];
+    blk_store(P, id);
     __syncthreads();
     for (int p = 1; p < QP; ++p) {
-        P[p * LTILE + i * LD + j] = mm_nn(P + (p - 1) * LTILE, X, i, j) / (double)p;
+        bm_nn<false>(P + (p - 1) * LTILE, X, tp);
+        const double inv = 1.0 / (double)p;
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int v = 0; v < 2; ++v) tp[u][v] *= inv;
+        blk_store(P + p * LTILE, tp);
         __syncthreads();
     }
-    const size_t nd = (size_t)n * d, e = (size_t)i * d + j;
-    const bool in = i < n && j < d;
-    double dw = 0.0, dx = 0.0;
+    const size_t nd = (size_t)n * d;
+    double dw[2][2] = {{0.0, 0.0}, {0.0, 0.0}}, dx[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
     for (int bb = QP - 1; bb >= 0; --bb) {
-        double v = 0.0;
-        if (in) {
-            if (dG) v = (double)dG[((size_t)b * QP + bb) * nd + e];
-            if (dF) v = fma(a.c1[bb], (double)dF[(size_t)b * nd + e], v);
-            if (dH)
-                for (int r = 0; r < QP; ++r) v = fma(a.c2[r * QP + bb], (double)dH[((size_t)b * QP + r) * nd + e], v);
+        double gt[2][2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                const int i = r0 + u, j = c0 + v;
+                double val = 0.0;
+                if (i < n && j < d) {
+                    const size_t e = (size_t)i * d + j;
+                    if (dG) val = (double)dG[((size_t)b * QP + bb) * nd + e];
+                    if (dF) val = fma(a.c1[bb], (double)dF[(size_t)b * nd + e], val);
+                    if (dH)
+                        for (int rr = 0; rr < QP; ++rr)
+                            val = fma(a.c2[rr * QP + bb], (double)dH[((size_t)b * QP + rr) * nd + e], val);
+                }
+                gt[u][v] = val;
+            }
+        blk_store(T1, gt);  // dG~_b
+        __syncthreads();
+        bm_tn<true>(P + bb * LTILE, T1, dw);
+        bm_nn<false>(T1, WT, tp);  // dG~_b W^T
+        if (bb < QP - 1) {
+            bm_nn<false>(T0, XT, tq);  // R_{b+1} X^T
+            const double inv = 1.0 / (double)(bb + 1);
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int v = 0; v < 2; ++v) tp[u][v] = fma(tq[u][v], inv, tp[u][v]);
         }
-        T1[i * LD + j] = v;  // dG~_b
         __syncthreads();
-        dw += mm_tn(P + bb * LTILE, T1, i, j);
-        double r = mm_nt(T1, T2, i, j);
-        if (bb < QP - 1) r += mm_nt(T0, X, i, j) / (double)(bb + 1);
+        blk_store(T0, tp);  // R_b
         __syncthreads();
-        T0[i * LD + j] = r;  // R_b
-        __syncthreads();
-        if (bb >= 1) dx += mm_tn(P + (bb - 1) * LTILE, T0, i, j) / (double)bb;
+        if (bb >= 1) {
+            bm_tn<false>(P + (bb - 1) * LTILE, T0, tq);
+            const double inv = 1.0 / (double)bb;
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int v = 0; v < 2; ++v) dx[u][v] = fma(tq[u][v], inv, dx[u][v]);
+        }
     }
-    if (i < n && j < n) wb[(size_t)n * n + (size_t)i * n + j] = dx;
-    if (in) wb[2 * (size_t)n * n + e] = dw;
-    const double dh = block_sum(-gen * dx, red);
+    double dh = 0.0;
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+            const int i = r0 + u, j = c0 + v;
+            if (i < n && j < n) wb[(size_t)n * n + (size_t)i * n + j] = dx[u][v];
+            if (i < n && j < d) wb[2 * (size_t)n * n + (size_t)i * d + j] = dw[u][v];
+            dh = fma(-gen[u][v], dx[u][v], dh);
+        }
+    dh = block_sum(dh, red);
     if (threadIdx.x == 0) wb[ws - 1] = dh;
 }
 
@@ -757,7 +924,7 @@ extern "C" int ews_dense_leaf(const float* A, const float* A_leaf, const float* 
     const int rc = leaf_check(a);
     if (rc != EWS_OK || batch == 0) return rc;
     if (!Dc || !F || !G || !H) return EWS_ERR_INVALID_ARGUMENT;
-    const size_t smem = sizeof(double) * (3 * (size_t)LTILE + 32);
+    const size_t smem = sizeof(double) * (3 * (size_t)LTILE + 32);  // X, T0, T1, red
     cudaFuncSetAttribute(dense_leaf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dense_leaf_kernel<<<2 * batch, LT, smem, (cudaStream_t)stream>>>(a, Dc, F, G, H);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
@@ -775,7 +942,7 @@ extern "C" int ews_dense_leaf_adjoint(const float* A, const float* A_leaf, const
     if (A_leaf && !dA_leaf) return EWS_ERR_INVALID_ARGUMENT;
     if (lift && !dW) return EWS_ERR_INVALID_ARGUMENT;
     cudaStream_t s = (cudaStream_t)stream;
-    const size_t smem = sizeof(double) * ((4 + (size_t)order + 1) * LTILE + 32);
+    const size_t smem = sizeof(double) * ((6 + (size_t)order + 1) * LTILE + 32);  // X, T0-T2, XT, WT, P_0..P_q, red
     cudaFuncSetAttribute(dense_leaf_adjoint_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     double* wk = static_cast<double*>(work);
     dense_leaf_adjoint_kernel<<<2 * batch, LT, smem, s>>>(a, dDc, dF, dG, dH, wk);
