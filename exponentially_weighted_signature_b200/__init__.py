@@ -8,7 +8,7 @@ the reference's layer API (alexandre-bloch/exponentially-weighted-signature, ews
 from . import params, series
 from .layer import COMBINE_KINDS, EWS, BToSignature, LogEWS, configure
 from .logsig import log_level_sizes, log_signature_dim
-from .params import AParamBlockDiag, AParamConstant, AParamDiag, AParamEFM, AParamGeneral, B
+from .params import AParamBlockDiag, AParamConstant, AParamDiag, AParamEFM, AParamGeneral, AParamJordanRepeated, B
 from .series import check_series_q, series_error_bound, suggest_series_q
 
 __all__ = [
@@ -22,6 +22,7 @@ __all__ = [
     "AParamDiag",
     "AParamEFM",
     "AParamGeneral",
+    "AParamJordanRepeated",
     "B",
     "check_series_q",
     "series_error_bound",

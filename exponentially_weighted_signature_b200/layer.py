@@ -19,10 +19,11 @@ import torch
 from torch import nn
 
 from . import _lib, engine, logsig, series
-from .params import AParamConstant, B, block_sizes_of, is_diagonal
+from .params import AParamConstant, B, block_sizes_of, is_diagonal, jordan_chains_of
 
 COMBINE_KINDS = ("assoc", "lean", "block_kernel", "dense_kernel", "b200")
 LEAF_KINDS = ("van_loan", "series", "plane_closed", "block_series", "jordan_closed", "jordan_closed_tables")
+JORDAN_LEAVES = ("jordan_closed", "jordan_closed_tables")
 MODES = ("displacement", "displacement_uniform", "displacement_uniform_basepoint")
 
 _DETERMINISTIC = False
@@ -115,7 +116,16 @@ class EWS(nn.Module):
                 raise NotImplementedError("leaf='plane_closed': closed-form local terms exist for depths 1 and 2")
             if self.d % 2:
                 raise ValueError("leaf='plane_closed' needs an even dimension (2x2 planes)")
-        if leaf not in ("series", "block_series", "van_loan", "plane_closed"):
+        self._jordan_chain = jordan_chains_of(self.A_param)
+        if leaf in JORDAN_LEAVES:
+            if self._jordan_chain is None:
+                raise ValueError(
+                    f"leaf={leaf!r} needs a jordan_repeated A with uniform chains (every block the same kind and size: "
+                    "real 2-4 or complex 4, 6, 8); use leaf='series' or 'block_series' otherwise"
+                )
+            if N > 2:
+                raise NotImplementedError(f"leaf={leaf!r}: closed-form local terms exist for depths 1 and 2")
+        if leaf not in ("series", "block_series", "van_loan", "plane_closed") + JORDAN_LEAVES:
             raise NotImplementedError(
                 f"leaf={leaf!r} is not built on the B200 engines; use leaf='series' (or 'van_loan' for a diagonal A)"
             )
@@ -129,9 +139,11 @@ class EWS(nn.Module):
         self.block_sizes = block_sizes_of(self.A_param)
         if leaf == "block_series" and self.block_sizes is None:
             raise ValueError("leaf='block_series' needs a block-diagonal A parametrisation")
-        if jordan_flows:
+        if jordan_flows and (combine != "block_kernel" or self._jordan_chain is None):
             raise ValueError("jordan_flows needs combine='block_kernel' and a jordan_repeated A with uniform chains")
-        self.jordan_flows = False
+        # The closed-form chain flows (ews/core/kernels/combine.py:143-190) and the engines' float64
+        # exponential of -h A are the same matrices to float64 rounding, so the flag selects nothing else here.
+        self.jordan_flows = bool(jordan_flows)
         sizes = self.block_sizes
         if self.N == 3:
             pairs = sizes is not None and (all(s == 2 for s in sizes) or all(s == 1 for s in sizes))
@@ -140,7 +152,8 @@ class EWS(nn.Module):
             self.engine = "block"
         elif self.N == 2:
             # the plane leaf reads its own generator from A (per plane [[d, w], [-w, d]]): dense engine
-            self.engine = "diag" if is_diagonal(self.A_param) and leaf != "plane_closed" else "dense"
+            closed = leaf == "plane_closed" or leaf in JORDAN_LEAVES
+            self.engine = "diag" if is_diagonal(self.A_param) and not closed else "dense"
         else:
             raise NotImplementedError("the B200 engines are built for depths N=2 and N=3")
         if leaf == "block_series" and self.N > 2:
@@ -153,7 +166,12 @@ class EWS(nn.Module):
         # The Van Loan leaf with a per-interval clock (diagonal engine) and on the dense engine is the
         # series leaf's evaluation with the Van Loan leaf's coefficients, truncated at degree 8
         # (series.vanloan_poly_coeffs); under a uniform clock the diagonal engine takes its exact tables.
-        self._q = VANLOAN_DEGREE if leaf == "van_loan" else series.PLANE_Q if leaf == "plane_closed" else self.series_q
+        if leaf == "van_loan":
+            self._q = VANLOAN_DEGREE
+        elif leaf == "plane_closed" or leaf in JORDAN_LEAVES:
+            self._q = series.CLOSED_Q
+        else:
+            self._q = self.series_q
 
     @property
     def signature_dim(self) -> int:
@@ -279,10 +297,15 @@ class EWS(nn.Module):
             # limit; evaluated at order PLANE_Q it agrees to float32 rounding while ||h A_planes|| <= PLANE_X_MAX,
             # which a device-side check guards (the next call raises otherwise).
             A_leaf = series.plane_generator(A)
+        elif self.leaf in JORDAN_LEAVES:
+            # The Jordan leaf's closed forms (ews/core/kernels/jordan_engine.py:324-353) are the series leaf's
+            # limit for the chain generator; the same order and range check as the plane leaf.
+            A_leaf = series.jordan_generator(A, *self._jordan_chain)
+        if A_leaf is not None:
             x = h.abs().max() * A_leaf.abs().sum(-1).max()
-            engine.guard(x > series.PLANE_X_MAX, A.device,
-                         f"leaf='plane_closed' is evaluated as its series at order {series.PLANE_Q}, exact to float32 "
-                         f"for ||h A|| <= {series.PLANE_X_MAX}; an earlier call on this device exceeded that range")
+            engine.guard(x > series.CLOSED_X_MAX, A.device,
+                         f"leaf={self.leaf!r} is evaluated as its series at order {series.CLOSED_Q}, exact to float32 "
+                         f"for ||h A|| <= {series.CLOSED_X_MAX}; an earlier call on this device exceeded that range")
         M, F, G, H = series.dense_tables(A, h, self._q, lift, coeffs, A_leaf)
         flags = _lib.EWS_F_UNIFORM | _det_flags()
         if increments:

@@ -86,10 +86,70 @@ class AParamBlockDiag(nn.Module):
         return torch.block_diag(*self.blocks)
 
 
+class AParamJordanRepeated(nn.Module):
+    """Block-diagonal generator of Jordan blocks, one eigenvalue repeated down each block
+    (ews/params.py:412-460): a real block of size n is lam = softplus(v) on the diagonal with ones
+    directly above; a complex block of size 2k is R = [[a, -b], [b, a]] (a = softplus(v), b free) in
+    every diagonal slot with the 2x2 identity above. ``block_params[j]`` holds (v,) for a real block
+    and (v, b) for a complex one."""
+
+    def __init__(self, block_sizes: Sequence[int], block_kinds: Sequence[str], block_params: Sequence[torch.Tensor]):
+        super().__init__()
+        self.block_sizes = tuple(int(x) for x in block_sizes)
+        self.block_kinds = tuple(str(x) for x in block_kinds)
+        for size, kind in zip(self.block_sizes, self.block_kinds):
+            if kind not in ("real", "complex"):
+                raise ValueError(f"Unknown Jordan block kind '{kind}'")
+            if kind == "real" and size < 2:
+                raise ValueError("a real Jordan block needs size >= 2 for the eigenvalue to repeat; "
+                                 "size 1 is a plain diagonal entry")
+            if kind == "complex" and (size % 2 != 0 or size < 4):
+                raise ValueError(f"a complex Jordan block needs an even size >= 4, got {size}")
+        self.block_params = nn.ParameterList([nn.Parameter(torch.as_tensor(p).reshape(-1)) for p in block_params])
+        self.dim = int(sum(self.block_sizes))
+
+    def forward(self) -> torch.Tensor:
+        blocks = []
+        for size, kind, p in zip(self.block_sizes, self.block_kinds, self.block_params):
+            if kind == "real":
+                lam = F.softplus(p[0])
+                eye = torch.eye(size, dtype=p.dtype, device=p.device)
+                blocks.append(lam * eye + torch.diag(torch.ones(size - 1, dtype=p.dtype, device=p.device), 1))
+            else:
+                k = size // 2
+                a, b = F.softplus(p[0]), p[1]
+                R = torch.stack([torch.stack([a, -b]), torch.stack([b, a])])
+                shift = torch.diag(torch.ones(k - 1, dtype=p.dtype, device=p.device), 1)
+                blocks.append(torch.kron(torch.eye(k, dtype=p.dtype, device=p.device), R)
+                              + torch.kron(shift, torch.eye(2, dtype=p.dtype, device=p.device)))
+        if not blocks:
+            return torch.zeros((0, 0))
+        return torch.block_diag(*blocks)
+
+
+JORDAN_REAL_SIZES, JORDAN_COMPLEX_SIZES = (2, 3, 4), (4, 6, 8)
+
+
+def jordan_chains_of(a_param) -> Optional[tuple]:
+    """(kind, size) when A is an AParamJordanRepeated whose blocks all have one supported kind and size
+    (real 2-4, complex 4 / 6 / 8), else None (ews/core/kernels/jordan_engine.py:29-43)."""
+    if not isinstance(a_param, AParamJordanRepeated) or not a_param.block_sizes:
+        return None
+    sizes, kinds = set(a_param.block_sizes), set(a_param.block_kinds)
+    if len(sizes) != 1 or len(kinds) != 1:
+        return None
+    kind, size = kinds.pop(), int(sizes.pop())
+    if size not in (JORDAN_REAL_SIZES if kind == "real" else JORDAN_COMPLEX_SIZES):
+        return None
+    return kind, size
+
+
 def block_sizes_of(a_param) -> Optional[tuple]:
     """Block structure of a parametrisation, decided from its class (ews/core/kernels/combine.py:37-58)."""
     if isinstance(a_param, AParamBlockDiag):
         return a_param.sizes
+    if isinstance(a_param, AParamJordanRepeated):
+        return a_param.block_sizes
     if isinstance(a_param, (AParamDiag, AParamEFM)):
         return (1,) * a_param.dim
     return None

@@ -180,6 +180,10 @@ def dense_tables(A: torch.Tensor, h: torch.Tensor, q: int, lift=None, coeffs=Non
 # below series_error_bound(x, 2, q) = (2x)^(q+1) / (q+1)! e^(2x), 5.7e-9 relative at q = 11, x = 0.5.
 PLANE_Q = 11
 PLANE_X_MAX = 0.5
+# The Jordan leaf is evaluated the same way (the closed forms of ews/core/kernels/jordan_engine.py are the
+# series leaf's limit for the chain generator), at the same order and range.
+CLOSED_Q = PLANE_Q
+CLOSED_X_MAX = PLANE_X_MAX
 
 
 def plane_generator(A: torch.Tensor) -> torch.Tensor:
@@ -196,6 +200,36 @@ def plane_generator(A: torch.Tensor) -> torch.Tensor:
     P[ii, ii + 1] = w
     P[ii + 1, ii] = -w
     return P
+
+
+def jordan_generator(A: torch.Tensor, kind: str, size: int) -> torch.Tensor:
+    """The generator whose local terms the Jordan leaf computes: its chains' parameters read off the first
+    rows of each chain of A (ews/core/kernels/jordan_engine.py:324-353) and the chains rebuilt,
+    J_j = D_j + eps_j Nil with Nil the shift by one coordinate (real chain, D = lam I; lam = A[f, f],
+    eps = A[f, f+1]) or by one 2x2 slot (complex chain, D = diag(C, .., C), C = [[a, -b], [b, a]];
+    a = A[f, f], b = A[f+1, f], eps = A[f, f+2]); f is the chain's first index. Equals A when A is the
+    Jordan-structured matrix itself. Differentiable in A."""
+    m = A.shape[-1]
+    size = int(size)
+    if m % size:
+        raise ValueError(f"the Jordan leaf needs chains of size {size} that tile A; dimension {m}")
+    first = torch.arange(0, m, size, device=A.device)
+    K = first.numel()
+    if kind == "real":
+        lam, eps = A[first, first], A[first, first + 1]
+        eye = torch.eye(size, dtype=A.dtype, device=A.device)
+        nil = torch.diag(torch.ones(size - 1, dtype=A.dtype, device=A.device), 1)
+        blocks = lam[:, None, None] * eye + eps[:, None, None] * nil  # (K, n, n)
+    else:
+        k = size // 2
+        a, b, eps = A[first, first], A[first + 1, first], A[first, first + 2]
+        C = torch.stack([torch.stack([a, -b], -1), torch.stack([b, a], -1)], -2)  # (K, 2, 2)
+        eye_k = torch.eye(k, dtype=A.dtype, device=A.device)
+        shift = torch.diag(torch.ones(k - 1, dtype=A.dtype, device=A.device), 1)
+        eye2 = torch.eye(2, dtype=A.dtype, device=A.device)
+        blocks = (torch.einsum("ij,nab->niajb", eye_k, C)
+                  + eps[:, None, None, None, None] * torch.einsum("ij,ab->iajb", shift, eye2)[None]).reshape(K, size, size)
+    return torch.block_diag(*blocks.unbind(0))
 
 
 # ------------------------------------------------------------------------------ Van Loan leaf tables

@@ -280,8 +280,164 @@ def plane_closed_local_terms(path, clock, A, N):
     return levels
 
 
-def local_signatures(path, clock, A, trunc, kind="series", series_q=None):
+# ------------------------------------------------------------------------ Jordan closed forms
+# Restatement of the float64 / complex128 table forms of ews/core/kernels/jordan_engine.py:159-320 (the
+# leaves "jordan_closed" and "jordan_closed_tables"; the fast forms of :46-157 compute the same closed
+# forms by forward-mode derivatives, which agree to rounding).
+J_PHI_TERMS, J_PHI_SWITCH = 64, 8.0
+J_PAIR_TERMS, J_PAIR_SWITCH, J_PAIR_S, J_PAIR_DELTA0 = 24, 1.5, 10, 0.25
+
+
+def _cplx(x):
+    return torch.is_complex(x)
+
+
+def phi_derivative_table(y, r_max, n_terms=J_PHI_TERMS, switch=J_PHI_SWITCH):
+    """phi^(r)(y), r = 0..r_max, phi(y) = (e^y - 1)/y, real or complex y with Re y <= 0 (``jordan_engine.py:175-199``):
+    the entire series sum_j y^j / ((j + r + 1) j!) for |y| <= switch, else phi^(r) = (e^y - r phi^(r-1)) / y from
+    expm1(y)/y. y (...) -> (..., r_max + 1)."""
+    small = y.abs() <= switch
+    ys = torch.where(small, y, torch.zeros_like(y))
+    yl = torch.where(small, torch.full_like(y, -2.0 * switch), y)
+    j = torch.arange(int(n_terms), dtype=torch.float64)
+    ratios = torch.where(j == 0, torch.ones_like(ys[..., None]), ys[..., None] / torch.clamp(j, min=1.0))
+    ypow = torch.cumprod(ratios, dim=-1)  # y^j / j!
+    r = torch.arange(r_max + 1, dtype=torch.float64)
+    C = 1.0 / (j[None, :] + r[:, None] + 1.0)  # (R, J)
+    series = ypow @ (C.T.to(ypow.dtype))
+    ey = torch.exp(yl)
+    cols = [torch.expm1(yl) / yl]
+    for rr in range(1, r_max + 1):
+        cols.append((ey - rr * cols[-1]) / yl)
+    return torch.where(small[..., None], series, torch.stack(cols, dim=-1))
+
+
+def pair_integral_derivatives(x, delta, p_max, q_max):
+    """d_x^p d_delta^q of D(x, delta) = (phi(x + delta) - phi(x)) / delta on the chain-pair grid, x (L, K), delta (L, K)
+    -> {(p, q): (L, K, K)} (``jordan_engine.py:202-243``): the delta expansion below J_PAIR_DELTA0, Leibniz on
+    F(delta) / delta above."""
+    if _cplx(x) != _cplx(delta):
+        x, delta = x.to(torch.complex128), delta.to(torch.complex128)
+    small = delta.abs() < J_PAIR_DELTA0
+    ds = torch.where(small, delta, torch.zeros_like(delta))
+    dl = torch.where(small, torch.full_like(delta, -1.0), delta)
+    tab_x = phi_derivative_table(x, p_max + q_max + 1 + J_PAIR_S)  # (L, K_j, R)
+    s_idx = torch.arange(J_PAIR_S, dtype=torch.float64)
+    ratios = torch.where(s_idx == 0, torch.ones_like(ds[..., None]), ds[..., None] / torch.clamp(s_idx, min=1.0))
+    dpow = torch.cumprod(ratios, dim=-1)  # delta^s / s!
+    tab_xd = phi_derivative_table(x[:, :, None] + dl[:, None, :], p_max + q_max, J_PAIR_TERMS, J_PAIR_SWITCH)
+    inv = 1.0 / dl
+    out = {}
+    for pp in range(p_max + 1):
+        for qq in range(q_max + 1):
+            base = pp + qq + 1
+            ser = torch.einsum("njs,nks->njk", tab_x[:, :, base : base + J_PAIR_S], dpow / (qq + s_idx + 1.0))
+            lei = 0.0
+            for ss in range(qq + 1):
+                F = tab_xd[..., pp + ss] - (tab_x[:, :, None, pp] if ss == 0 else 0.0)
+                coef = math.comb(qq, ss) * (-1.0) ** (qq - ss) * math.factorial(qq - ss)
+                lei = lei + coef * F * inv[:, None, :] ** (qq - ss + 1)
+            out[(pp, qq)] = torch.where(small[:, None, :], ser, lei)
+    return out
+
+
+def _jordan_shifted(P, eps, n):
+    """[(eps Nil)^p P for p < n]; P (L, K, n), eps (K,) (``jordan_engine.py:246-252``)."""
+    L, K, _ = P.shape
+    e = eps.to(P.real.dtype if _cplx(P) else P.dtype)[None, :, None]
+    return [torch.cat([P[:, :, p:], torch.zeros((L, K, p), dtype=P.dtype)], -1) * e**p for p in range(n)]
+
+
+def _jordan_real(v, lam, eps, dtheta, N, n):
+    """Real chains of length n (``jordan_engine.py:255-285``). v (L, m), lam, eps (K,), dtheta (L,)."""
+    L, m = v.shape
+    K = m // n
+    h = dtheta[:, None]
+    x = -h * lam[None, :]
+    shifted = _jordan_shifted(v.reshape(L, K, n), eps, n)
+    tab = phi_derivative_table(x, n - 1)
+    s1 = torch.zeros((L, K, n), dtype=v.dtype)
+    for p in range(n):
+        s1 = s1 + ((-h) ** p * tab[:, :, p] / math.factorial(p))[:, :, None] * shifted[p]
+    s1 = s1.reshape(L, m)
+    if N == 1:
+        return [s1]
+    D = pair_integral_derivatives(x, x, n - 1, n - 1)
+    Q = torch.zeros((L, K, K, n, n), dtype=v.dtype)
+    for p in range(n):
+        for q in range(n):
+            coef = (-h[:, :, None]) ** (p + q) * D[(p, q)] / (math.factorial(p) * math.factorial(q))
+            Q = Q + coef[..., None, None] * shifted[p][:, :, None, :, None] * shifted[q][:, None, :, None, :]
+    return [s1, Q.transpose(2, 3).reshape(L, m, m)]
+
+
+def _jordan_complex(v, c, eps, dtheta, N, k):
+    """Complex chains of k complex coordinates (``jordan_engine.py:288-320``); c (K,) = a + ib."""
+    L, m = v.shape
+    K = m // (2 * k)
+    h = dtheta[:, None].to(torch.float64)
+    x = -h * c[None, :]
+    vv = v.reshape(L, K, k, 2)
+    shifted = _jordan_shifted(torch.complex(vv[..., 0], vv[..., 1]), eps, k)
+    tab = phi_derivative_table(x, k - 1)
+    s1c = torch.zeros((L, K, k), dtype=torch.complex128)
+    for p in range(k):
+        s1c = s1c + ((-h) ** p * tab[:, :, p] / math.factorial(p))[:, :, None] * shifted[p]
+    s1 = torch.stack([s1c.real, s1c.imag], -1).reshape(L, m)
+    if N == 1:
+        return [s1]
+    DA = pair_integral_derivatives(x, torch.conj(x), k - 1, k - 1)
+    DB = pair_integral_derivatives(x, x, k - 1, k - 1)
+    Ab = torch.zeros((L, K, K, k, k), dtype=torch.complex128)
+    Bb = torch.zeros((L, K, K, k, k), dtype=torch.complex128)
+    for p in range(k):
+        for q in range(k):
+            scale = (-h[:, :, None]) ** (p + q) / (math.factorial(p) * math.factorial(q))
+            Pj = shifted[p][:, :, None, :, None]
+            Pk = shifted[q][:, None, :, None, :]
+            Ab = Ab + (scale * DA[(p, q)])[..., None, None] * Pj * torch.conj(Pk)
+            Bb = Bb + (scale * DB[(p, q)])[..., None, None] * Pj * Pk
+    # real 2x2 blocks of the complex coordinate pairs (``jordan_engine.py:79-91``)
+    q00 = (Ab.real + Bb.real) / 2
+    q11 = (Ab.real - Bb.real) / 2
+    q01 = (Bb.imag - Ab.imag) / 2
+    q10 = (Ab.imag + Bb.imag) / 2
+    Qb = torch.stack([torch.stack([q00, q01], -1), torch.stack([q10, q11], -1)], -2)  # (L, Kj, Kk, ki, kl, 2, 2)
+    Qb = Qb.permute(0, 1, 3, 5, 2, 4, 6)
+    return [s1, Qb.reshape(L, m, m)]
+
+
+def jordan_local_terms(path, clock, A, trunc, chain):
+    """``leaf='jordan_closed'`` / ``'jordan_closed_tables'`` (``ews/core/leaf.py:173-192``,
+    ``ews/core/kernels/jordan_engine.py:324-353``): the chains' eigenvalue and coupling read off A's first rows.
+    path (..., L, d) knots, clock (..., L); broadcast over leading axes."""
+    if trunc > 2:
+        raise NotImplementedError("the closed-form Jordan leaf exists for depths 1 and 2")
+    kind, size = chain
+    lead = path.shape[:-2]
+    v_all = (path[..., 1:, :] - path[..., :-1, :]).reshape(-1, path.shape[-2] - 1, path.shape[-1])
+    dth_all = (clock[..., 1:] - clock[..., :-1]).reshape(-1, clock.shape[-1] - 1)
+    m = A.shape[-1]
+    first = torch.arange(0, m, size)
+    outs = []
+    for i in range(v_all.shape[0]):
+        v, dth = v_all[i], dth_all[i]
+        if kind == "real":
+            lv = _jordan_real(v, A[first, first], A[first, first + 1], dth, trunc, size)
+        else:
+            c = torch.complex(A[first, first].to(torch.float64), A[first + 1, first].to(torch.float64))
+            lv = _jordan_complex(v, c, A[first, first + 2], dth, trunc, size // 2)
+        outs.append([lv[0]] + ([lv[1].reshape(lv[1].shape[0], -1)] if trunc == 2 else []))
+    L1 = v_all.shape[1]
+    return [torch.stack([o[k] for o in outs]).reshape(lead + (L1, -1)) for k in range(trunc)]
+
+
+def local_signatures(path, clock, A, trunc, kind="series", series_q=None, jordan_chain=None):
     """Leaf dispatcher for the exact leaves (``ews/core/leaf.py:50-198``)."""
+    if kind in ("jordan_closed", "jordan_closed_tables"):
+        if jordan_chain is None:
+            raise ValueError(f"leaf={kind!r} needs jordan_chain (uniform Jordan chains)")
+        return jordan_local_terms(path, clock, A, trunc, jordan_chain)
     if kind == "series":
         if series_q is None:
             raise ValueError("kind='series' requires series_q (see check_series_q).")
@@ -465,6 +621,7 @@ def ews_layer(
     combine="assoc",
     chen_expm="exact",
     a_scale=1.0,
+    jordan_chain=None,
 ):
     """``EWS._single_path`` for exact leaves, broadcast over leading batch axes (``ews/layer.py:154-265``).
 
@@ -479,7 +636,7 @@ def ews_layer(
     A = A * a_scale
     d = A.shape[-1]
     interval_times = clock[..., 1:] - clock[..., :-1]
-    levels = local_signatures(path, clock, A, N, kind=leaf, series_q=series_q)
+    levels = local_signatures(path, clock, A, N, kind=leaf, series_q=series_q, jordan_chain=jordan_chain)
     cached = reweighting_mode in ("displacement_uniform", "displacement_uniform_basepoint")
     basepoint = reweighting_mode == "displacement_uniform_basepoint"
     if readout == "terminal":

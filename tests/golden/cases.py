@@ -76,6 +76,22 @@ def _block_generator(prng, N):
     return A
 
 
+def _jordan_generator(prng, N, chain):
+    """A Jordan-repeated A (the reference's AParamJordanRepeated, ews/params.py:412-460): real chains lam I + Nil,
+    lam ~ U(0.2, 2); complex chains of [[a, -b], [b, a]] slots with the 2x2 identity above, a ~ U(0.2, 1.5),
+    b ~ U(0, 1.2)."""
+    kind, size = chain
+    A = np.zeros((N, N))
+    for f in range(0, N, size):
+        if kind == "real":
+            A[f : f + size, f : f + size] = prng.uniform(0.2, 2.0) * np.eye(size) + np.eye(size, k=1)
+        else:
+            a, b = prng.uniform(0.2, 1.5), prng.uniform(0.0, 1.2)
+            k = size // 2
+            A[f : f + size, f : f + size] = np.kron(np.eye(k), [[a, -b], [b, a]]) + np.kron(np.eye(k, k=1), np.eye(2))
+    return A
+
+
 def _ar1(rng, B, T, channels, phi):
     x = np.zeros((B, T + 1, channels))
     eps = rng.normal(size=(B, T + 1, channels))
@@ -113,10 +129,15 @@ def _build(spec):
         x = np.concatenate([np.zeros((B, 1, 16)), np.cumsum(inc.astype(np.float64), 1)], 1)
         A = _diag_generator(prng, N, -4.0, 0.0)
         lift = prng.normal(size=(N, 16)) / 4.0
+    elif kind == "jordan":  # 3 Brownian channels + time, lift 4 -> N, Jordan chains, clock of total time 8
+        x = _brownian_knots(rng, B, T, 3)
+        A = _jordan_generator(prng, N, spec["jordan"])
+        lift = prng.normal(size=(N, 4)) / 2.0
+        clock = 8.0 * _uniform_clock(B, T)
     else:
         raise ValueError(kind)
     mode = spec["mode"]
-    if kind != "c3":
+    if kind not in ("c3", "jordan"):
         if mode == "displacement_uniform":
             clock = _uniform_clock(B, T)
         elif mode == "displacement_uniform_basepoint":
@@ -190,6 +211,19 @@ CASES = {
     "c5_full": dict(family="c5", seed=51, B=1, T=8192, N=32, depth=2, layer="LogEWS", mode="displacement_uniform",
                     kw=dict(leaf="series", series_q=4), a_struct="diag", readouts=("terminal",), grads=("terminal",),
                     dirs=("x", "A", "lift")),
+    # Jordan chains (AParamJordanRepeated), depth 2, uniform clock: the closed-form Jordan leaf
+    "jordan_real2_short": dict(family="jordan", seed=60, B=2, T=64, N=8, depth=2, layer="EWS",
+                               mode="displacement_uniform", jordan=("real", 2), kw=dict(leaf="jordan_closed_tables"),
+                               a_struct="jordan", readouts=("prefix", "terminal"), grads=("prefix",),
+                               dirs=("x", "A", "lift")),
+    "jordan_real3_short": dict(family="jordan", seed=61, B=2, T=64, N=9, depth=2, layer="EWS",
+                               mode="displacement_uniform", jordan=("real", 3), kw=dict(leaf="jordan_closed"),
+                               a_struct="jordan", readouts=("prefix", "terminal"), grads=("prefix",),
+                               dirs=("x", "A", "lift")),
+    "jordan_complex4_short": dict(family="jordan", seed=62, B=2, T=64, N=8, depth=2, layer="EWS",
+                                  mode="displacement_uniform", jordan=("complex", 4),
+                                  kw=dict(leaf="jordan_closed_tables"), a_struct="jordan",
+                                  readouts=("prefix", "terminal"), grads=("prefix",), dirs=("x", "A", "lift")),
     "c5_bf16_full": dict(family="c5", seed=51, B=1, T=8192, N=32, depth=2, layer="LogEWS", mode="displacement_uniform",
                          bf16=True, kw=dict(leaf="series", series_q=4), a_struct="diag", readouts=("terminal",),
                          grads=(), dirs=()),
@@ -233,6 +267,15 @@ def directions(name):
     elif spec["a_struct"] == "block2":
         mask = np.kron(np.eye(N // 2), np.ones((2, 2)))
         S = S * mask
+    elif spec["a_struct"] == "jordan":  # within the family: each chain's eigenvalue (and frequency)
+        kind, size = spec["jordan"]
+        S = np.zeros((N, N))
+        for f in range(0, N, size):
+            if kind == "real":
+                S[f : f + size, f : f + size] = rng.normal() * np.eye(size)
+            else:
+                da, db = rng.normal(size=2)
+                S[f : f + size, f : f + size] = np.kron(np.eye(size // 2), [[da, -db], [db, da]])
     out["A"] = S * float(np.max(np.abs(inp["A"])))
     out["lift"] = rng.normal(size=inp["lift"].shape) * float(np.std(inp["lift"]))
     return out
@@ -251,3 +294,17 @@ def load_fixture(name):
         if key in fx and str(fx[key]) != sha(v):
             raise AssertionError(f"golden {name}: regenerated input {k!r} differs from the one the fixture was made from")
     return fx, inp
+
+
+def jordan_params(A, chain):
+    """(block_sizes, block_kinds, block_params) of an AParamJordanRepeated that materialises A (ews/params.py:412-460):
+    the softplus inverse of each chain's eigenvalue (real) or real part (complex, with the frequency b)."""
+    kind, size = chain
+    N = A.shape[0]
+    sizes, kinds, ps = [], [], []
+    for f in range(0, N, size):
+        v = float(np.log(np.expm1(float(A[f, f]))))
+        sizes.append(size)
+        kinds.append(kind)
+        ps.append(np.array([v]) if kind == "real" else np.array([v, float(A[f + 1, f])]))
+    return sizes, kinds, ps

@@ -50,9 +50,12 @@ def _init(ref_root):
 def _forward(name, b, readout, x, clock, A, lift, combine="lean"):
     """Reference output of one sample, float64."""
     spec = cases.CASES[name]
-    layer_mod, _ = _REF
+    layer_mod, params_mod = _REF
     cls = layer_mod.LogEWS if spec["layer"] == "LogEWS" else layer_mod.EWS
-    m = cls(np.asarray(A, np.float64), spec["depth"], dtype=np.float64, reweighting_mode=spec["mode"],
+    A_arg = np.asarray(A, np.float64)
+    if "jordan" in spec:  # the Jordan leaf reads its chains from the parametrisation's class
+        A_arg = params_mod.AParamJordanRepeated(*cases.jordan_params(A_arg, spec["jordan"]))
+    m = cls(A_arg, spec["depth"], dtype=np.float64, reweighting_mode=spec["mode"],
             combine=combine, **spec["kw"])
     lifted = np.asarray(x, np.float64) @ np.asarray(lift, np.float64).T
     return np.asarray(m(lifted, np.asarray(clock, np.float64), readout=readout), np.float64)

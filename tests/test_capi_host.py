@@ -12,7 +12,7 @@ import torch
 from exponentially_weighted_signature_b200 import _lib, series
 from exponentially_weighted_signature_b200 import logsig
 from exponentially_weighted_signature_b200.layer import EWS, LogEWS
-from exponentially_weighted_signature_b200.params import AParamBlockDiag, AParamDiag, AParamEFM, B
+from exponentially_weighted_signature_b200.params import AParamBlockDiag, AParamDiag, AParamEFM, AParamJordanRepeated, B
 from oracle import ews_oracle as O
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -160,8 +160,24 @@ def test_layer_validation_mirrors_reference():
     assert EWS(torch.eye(4), N=2, reweighting_mode="displacement_uniform").engine == "dense"
     with pytest.raises(NotImplementedError):
         EWS(AParamBlockDiag([torch.ones(2, 2)] * 2, [2, 2]), N=3)
-    with pytest.raises(NotImplementedError):
+    # the Jordan leaves (ews/layer.py:148-152): uniform Jordan chains required; the dense engine runs them
+    with pytest.raises(ValueError):
         EWS(A, N=2, leaf="jordan_closed")
+    J = AParamJordanRepeated([3, 3], ["real", "real"], [torch.zeros(1), torch.ones(1)])
+    assert EWS(J, N=2, reweighting_mode="displacement_uniform", leaf="jordan_closed").engine == "dense"
+    assert EWS(J, N=2, leaf="jordan_closed_tables")._jordan_chain == ("real", 3)
+    with pytest.raises(ValueError):  # mixed chain sizes are not uniform chains
+        EWS(AParamJordanRepeated([2, 3], ["real"] * 2, [torch.zeros(1)] * 2), N=2, leaf="jordan_closed")
+    with pytest.raises(NotImplementedError):
+        EWS(J, N=3, leaf="jordan_closed")
+    # jordan_flows (ews/layer.py:134-138): needs combine='block_kernel' and uniform chains
+    assert EWS(J, N=2, leaf="jordan_closed", combine="block_kernel", jordan_flows=True).jordan_flows
+    with pytest.raises(ValueError):
+        EWS(J, N=2, leaf="jordan_closed", jordan_flows=True)
+    with pytest.raises(ValueError):
+        EWS(A, N=2, combine="block_kernel", jordan_flows=True)
+    with pytest.raises(ValueError):
+        AParamJordanRepeated([2], ["complex"], [torch.zeros(2)])
     # the plane leaf (ews/core/leaf.py:116-136): depths 1-2, even dimension; the dense engine runs it
     assert EWS(A, N=2, reweighting_mode="displacement_uniform", leaf="plane_closed").engine == "dense"
     with pytest.raises(NotImplementedError):

@@ -27,7 +27,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(HERE, "golden"))
 import cases  # noqa: E402
 
-ORACLE_LEAVES = ("series", "block_series", "plane_closed")
+ORACLE_LEAVES = ("series", "block_series", "plane_closed", "jordan_closed", "jordan_closed_tables")
 # full-length cases the oracle finishes in seconds on the CPU; the others are checked on the GPU only
 CPU_CASES = [n for n, s in cases.CASES.items() if s["T"] <= 256 or n in ("c1_full", "c3_full")]
 
@@ -50,7 +50,8 @@ def oracle_forward(name, b, readout, inp, requires_grad=False):
     path = O.lift(x, lift)
     fn = O.log_ews_layer if spec["layer"] == "LogEWS" else O.ews_layer
     out = fn(path, clock, A, spec["depth"], readout=readout, reweighting_mode=spec["mode"],
-             leaf=kw.get("leaf", "series"), series_q=kw.get("series_q"), combine="assoc", terminal_reduce="assoc")
+             leaf=kw.get("leaf", "series"), series_q=kw.get("series_q"), combine="assoc", terminal_reduce="assoc",
+             **({"jordan_chain": spec["jordan"]} if "jordan" in spec else {}))
     return out, dict(x=leaf_x, clock=clock, A=A, lift=lift)
 
 

@@ -228,3 +228,106 @@ def test_plane_closed_range_guard_raises_on_the_next_call():
         for slot in engine._GUARD.values():
             slot[0].zero_()
             slot[1].zero_()
+
+
+def _jordan_case(B, T, chain, K, d_in, seed=7, hmax=0.4, extra=0.2):
+    """K uniform Jordan chains (ews/params.py:412-460) plus `extra`-sized entries inside each chain's block that
+    the Jordan leaf does not read (it rebuilds the chains from their first rows) but the flows do; uniform
+    clock with ||h J|| (the chain generator) at most hmax."""
+    kind, size = chain
+    rng = np.random.default_rng(seed)
+    N = K * size
+    inc = rng.normal(size=(B, T, d_in)) / np.sqrt(T)
+    path = np.concatenate([np.zeros((B, 1, d_in)), np.cumsum(inc, 1)], 1)
+    A = np.zeros((N, N))
+    for f in range(0, N, size):
+        if kind == "real":
+            blk = rng.uniform(0.1, 2.0) * np.eye(size) + rng.uniform(0.5, 1.5) * np.eye(size, k=1)
+            blk += extra * np.tril(rng.normal(size=(size, size)), -1)
+        else:
+            a, b, e = rng.uniform(0.1, 1.5), rng.uniform(-2.0, 2.0), rng.uniform(0.5, 1.5)
+            k = size // 2
+            blk = np.kron(np.eye(k), [[a, -b], [b, a]]) + e * np.kron(np.eye(k, k=1), np.eye(2))
+            blk += extra * np.tril(rng.normal(size=(size, size)), -2)
+        A[f : f + size, f : f + size] = blk
+    lift = rng.normal(size=(N, d_in)) / np.sqrt(d_in)
+    import torch as _t
+    from exponentially_weighted_signature_b200 import series as _s
+
+    J = _s.jordan_generator(_t.tensor(A), kind, size).numpy()
+    h = hmax / np.abs(J).sum(-1).max()
+    clock = np.broadcast_to(np.arange(T + 1) * h, (B, T + 1)).copy()
+    return _f32(path), _f32(clock), _f32(A), _f32(lift)
+
+
+def _jordan_param(A, chain):
+    """An AParamJordanRepeated (the layer reads the chains from the class) that materialises the given matrix."""
+    from exponentially_weighted_signature_b200 import AParamJordanRepeated
+
+    class JordanMatrix(AParamJordanRepeated):
+        def forward(self):
+            return self.matrix
+
+    kind, size = chain
+    K = A.shape[0] // size
+    ap = JordanMatrix([size] * K, [kind] * K, [torch.zeros(1 if kind == "real" else 2)] * K)
+    ap.matrix = torch.nn.Parameter(torch.tensor(A, dtype=torch.float32))
+    return ap
+
+
+@pytest.mark.parametrize("chain,K,readout", [(("real", 4), 8, "prefix"), (("real", 2), 4, "terminal"),
+                                             (("complex", 4), 4, "prefix"), (("complex", 8), 2, "terminal"),
+                                             (("real", 3), 3, "prefix")])
+def test_jordan_closed_leaf_matches_oracle(chain, K, readout):
+    """leaf='jordan_closed' (ews/core/kernels/jordan_engine.py:324-353, via ews/core/leaf.py:173-192) against the
+    oracle's restatement of the reference's float64 / complex128 table forms: outputs and the gradients of the
+    path, the generator (flows from the whole A, the leaf from the chains' first rows) and the lift."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import EWS
+
+    path, clock, A, lift = _jordan_case(2, 80, chain, K, 3)
+    rng = np.random.default_rng(11)
+    L, N = path.shape[1], A.shape[0]
+    D = 1 + N + N * N
+    w = torch.tensor(rng.normal(size=(2, L - 1, D) if readout == "prefix" else (2, D)))
+    p64 = torch.tensor(path, requires_grad=True)
+    A64 = torch.tensor(A, requires_grad=True)
+    B64 = torch.tensor(lift, requires_grad=True)
+    ref = O.ews_layer(O.lift(p64, B64), torch.tensor(clock), A64, 2, leaf="jordan_closed",
+                      reweighting_mode="displacement_uniform", readout=readout, jordan_chain=chain)
+    (ref * w).sum().backward()
+    Ap = _jordan_param(A, chain).to(DEV)
+    layer = EWS(Ap, N=2, reweighting_mode="displacement_uniform", leaf="jordan_closed", combine="b200")
+    assert layer.engine == "dense" and layer._jordan_chain == chain
+    p = torch.tensor(path, dtype=torch.float32, device=DEV, requires_grad=True)
+    Bm = torch.tensor(lift, dtype=torch.float32, device=DEV, requires_grad=True)
+    out = layer(p, torch.tensor(clock, dtype=torch.float32, device=DEV), readout=readout, lift=Bm)
+    (out * w.to(DEV, torch.float32)).sum().backward()
+    torch.cuda.synchronize()
+    _assert_close("forward", out.detach().cpu().double(), ref.detach())
+    _assert_close("d path", p.grad.cpu().double(), p64.grad)
+    _assert_close("d A", Ap.matrix.grad.cpu().double(), A64.grad)
+    _assert_close("d lift", Bm.grad.cpu().double(), B64.grad)
+
+
+def test_jordan_closed_range_guard_raises_on_the_next_call():
+    """The Jordan leaf outside ||h J|| <= CLOSED_X_MAX: recorded on the device, raised on the next call."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import EWS, engine
+
+    chain = ("complex", 4)
+    path, clock, A, lift = _jordan_case(1, 32, chain, 2, 2, hmax=3.0)
+    layer = EWS(_jordan_param(A, chain).to(DEV), N=2, reweighting_mode="displacement_uniform", leaf="jordan_closed",
+                combine="b200")
+    p = torch.tensor(path, dtype=torch.float32, device=DEV)
+    c = torch.tensor(clock, dtype=torch.float32, device=DEV)
+    Bm = torch.tensor(lift, dtype=torch.float32, device=DEV)
+    try:
+        with pytest.raises(NotImplementedError, match="jordan_closed"):
+            layer(p, c, readout="prefix", lift=Bm)  # may already raise: the flag's copy can land before the call
+            torch.cuda.synchronize()
+            layer(p, c, readout="prefix", lift=Bm)
+    finally:
+        for slot in engine._GUARD.values():
+            slot[0].zero_()
+            slot[1].zero_()

@@ -40,13 +40,31 @@ def _require_gpu():
         pytest.fail("GPU test run without a CUDA device")
 
 
+def _jordan_matrix_param(A, chain):
+    """An AParamJordanRepeated (so the layer sees the chains) that materialises the given matrix itself, so that
+    the gradient is the full dL/dA the fixtures' directions are projected on."""
+    from exponentially_weighted_signature_b200 import AParamJordanRepeated
+
+    class JordanMatrix(AParamJordanRepeated):
+        def forward(self):
+            return self.matrix
+
+    kind, size = chain
+    K = A.shape[0] // size
+    ap = JordanMatrix([size] * K, [kind] * K, [torch.zeros(1 if kind == "real" else 2)] * K)
+    ap.matrix = torch.nn.Parameter(A.clone())
+    return ap
+
+
 def _model(name, inp):
     from exponentially_weighted_signature_b200 import EWS, LogEWS, AParamBlockDiag, AParamDiag, AParamGeneral
 
     spec = cases.CASES[name]
     A = torch.tensor(inp["A"], dtype=torch.float32)
     N = A.shape[0]
-    if spec["a_struct"] == "diag":
+    if spec["a_struct"] == "jordan":
+        Ap = _jordan_matrix_param(A, spec["jordan"])
+    elif spec["a_struct"] == "diag":
         Ap = AParamDiag(torch.diagonal(A).clone())
     elif spec["a_struct"] == "block2":
         Ap = AParamBlockDiag([A[2 * k : 2 * k + 2, 2 * k : 2 * k + 2].clone() for k in range(N // 2)], (2,) * (N // 2))
