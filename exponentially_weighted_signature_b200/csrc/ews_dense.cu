@@ -438,6 +438,52 @@ __device__ bool tc_wait(const TcSmem& s, uint32_t parity, int limit) {
 
 }  // namespace tc
 
+// The same local terms with the lane's rows of the tables held in registers for the whole span (d_in <= 8,
+// q <= 3: ROWS = 1 + 2 QP tables): per interval two broadcast loads of the increments, ROWS x 8 FMAs and
+// ROWS coalesced stores.
+constexpr int LSPAN_REG = 256;
+
+template <int ROWS>
+__global__ void __launch_bounds__(LNT) local_reg_kernel(Params p) {
+    __shared__ __align__(16) float X[LSPAN_REG * 8];  // the span's increments, 8 per interval (zero padded)
+    const Geom& g = p.g;
+    const int N = g.N, d = g.d_in, QP = g.QP, LW = loc_width(QP);
+    const int spans = (g.T + LSPAN_REG - 1) / LSPAN_REG;
+    const int b = blockIdx.x / spans, t0 = (blockIdx.x - b * spans) * LSPAN_REG;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float tab[ROWS][8];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+        const float* src = r == 0 ? p.tab_f + ((size_t)b * N + lane) * d
+                           : r <= QP ? p.tab_g + (((size_t)b * QP + r - 1) * N + lane) * d
+                                     : p.tab_h + (((size_t)b * QP + r - 1 - QP) * N + lane) * d;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) tab[r][c] = (lane < N && c < d) ? __ldg(src + c) : 0.f;
+    }
+    for (int e = threadIdx.x; e < LSPAN_REG * 8; e += LNT) {
+        const int tt = e >> 3, c = e & 7, t = t0 + tt;
+        X[e] = (t < g.T && c < d) ? input_increment(p.path, b, t, c, g.T, d, g.flags) : 0.f;
+    }
+    __syncthreads();
+    const int tend = min(LSPAN_REG, g.T - t0);
+    for (int tt = warp; tt < tend; tt += LNT / 32) {
+        const float4 x0 = *reinterpret_cast<const float4*>(X + tt * 8);
+        const float4 x1 = *reinterpret_cast<const float4*>(X + tt * 8 + 4);
+        const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        float* dst = p.loc + ((size_t)b * g.T + t0 + tt) * LW + lane;
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; c += 2) {
+                a0 = fmaf(tab[r][c], x[c], a0);
+                a1 = fmaf(tab[r][c + 1], x[c + 1], a1);
+            }
+            dst[r * NP] = a0 + a1;  // [s1 | U_0 .. U_{QP-1} | V_0 .. V_{QP-1}]
+        }
+    }
+}
+
 // Flow complements of whole chunks, per sample: C(e) = I - M^e for e = Lc and e = the last chunk's
 // length, by binary powering of complements (C(a + b) = C(a) + C(b) - C(a) C(b), C(2a) = 2 C(a) - C(a)^2),
 // so that no I - (a matrix near I) is ever formed. One CTA of NT threads per sample.
@@ -2385,8 +2431,17 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
         sp = ss->s2;
     power_kernel<<<g.B, NT, 5 * MM * sizeof(float), sp>>>(p);
     powers_kernel<<<g.B, PWT, 0, sp>>>(p);
-    const int spans = (g.T + LSPAN - 1) / LSPAN;
-    local_kernel<<<g.B * spans, LNT, lsmem, s>>>(p);
+    if (g.QP <= 4 && g.d_in <= 8) {
+        const int rspans = (g.T + LSPAN_REG - 1) / LSPAN_REG;
+        const int rows = 1 + 2 * g.QP;
+        if (rows == 3) local_reg_kernel<3><<<g.B * rspans, LNT, 0, s>>>(p);
+        else if (rows == 5) local_reg_kernel<5><<<g.B * rspans, LNT, 0, s>>>(p);
+        else if (rows == 7) local_reg_kernel<7><<<g.B * rspans, LNT, 0, s>>>(p);
+        else local_reg_kernel<9><<<g.B * rspans, LNT, 0, s>>>(p);
+    } else {
+        const int spans = (g.T + LSPAN - 1) / LSPAN;
+        local_kernel<<<g.B * spans, LNT, lsmem, s>>>(p);
+    }
     if (sp != s && (cudaEventRecord(ss->join, sp) != cudaSuccess || cudaStreamWaitEvent(s, ss->join, 0) != cudaSuccess))
         return EWS_ERR_LAUNCH;
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
