@@ -50,6 +50,9 @@ EXPORTED = (
     "ews_dense_leaf",
     "ews_dense_leaf_adjoint",
     "ews_dense_leaf_work_size",
+    "ews_graded_norm_work_size",
+    "ews_graded_norm_fwd",
+    "ews_graded_norm_bwd",
     "ews_read_device_status",
     "ews_status_fold",
     "ews_error_string",
@@ -224,6 +227,13 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.ews_dense_leaf_adjoint.restype = _c_int
         lib.ews_dense_leaf_work_size.argtypes = [_c_int, _c_int, _c_int]
         lib.ews_dense_leaf_work_size.restype = _c_size
+        lib.ews_graded_norm_work_size.argtypes = [_c_int, _c_int, _c_int, _c_int]
+        lib.ews_graded_norm_work_size.restype = _c_size
+        lib.ews_graded_norm_fwd.argtypes = [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp]
+        lib.ews_graded_norm_fwd.restype = _c_int
+        lib.ews_graded_norm_bwd.argtypes = [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_size,
+                                            _vp]
+        lib.ews_graded_norm_bwd.restype = _c_int
         lib.ews_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(_c_int)]
         lib.ews_read_device_status.restype = _c_int
         lib.ews_diag_fwd_noalloc_status.argtypes = [_vp, ctypes.POINTER(_c_int)]

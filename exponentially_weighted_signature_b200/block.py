@@ -52,6 +52,17 @@ class GradedRMSNorm(nn.Module):
             self.slices.append((start, start + self.d**k))
             start += self.d**k
 
+    def from_prefix(self, flat):
+        """The norm of the block's mixer levels straight from the EWS prefix rows flat (B, L, 1 + D): level 0
+        dropped, a zero row prepended (ews/block.py:282-306), then this norm. On CUDA one library pass each
+        way (engine.GradedNorm); elsewhere the same steps as torch ops."""
+        if flat.is_cuda:
+            from .engine import GradedNorm
+
+            return GradedNorm.apply(flat, self.gains, self.d, self.N, tuple(self.eps))
+        levels = flat[..., 1:]
+        return self(torch.cat([torch.zeros_like(levels[:, :1]), levels], 1))
+
     def forward(self, x):
         out = []
         for k, (s, e) in enumerate(self.slices):
@@ -124,8 +135,8 @@ class EWSBlock(nn.Module):
     def forward(self, x):
         theta = self.clock(x)  # the block-input driver
         branch_in = self.norm1(x)
-        levels = self.mixer_levels(branch_in, theta)
-        r = self.c_down(self.graded(levels))
+        flat = self.ewms(self.lift(branch_in), theta, readout="prefix", output_format="flat")
+        r = self.c_down(self.graded.from_prefix(flat))  # = c_down(graded(mixer_levels(branch_in, theta)))
         x = x + self.drop(r)
         mch = self.ff2(F.gelu(self.ff1(self.norm2(x))))
         return x + self.drop(mch)

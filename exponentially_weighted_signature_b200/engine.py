@@ -370,6 +370,45 @@ class DenseLeaf(torch.autograd.Function):
                 dW if need[3] else None, None, None)
 
 
+class GradedNorm(torch.autograd.Function):
+    """The block's stream consumer in one library pass each way: EWS prefix rows flat (B, T, 1 + D) ->
+    y (B, T + 1, D), level 0 dropped, a zero row prepended and every level normalised by its live RMS
+    (ews/block.py:282-306, ews/norms.py:47-135, "live_rms"): y level k = g_k x_k / (RMS(x_k) + eps_k)."""
+
+    @staticmethod
+    def forward(ctx, flat, gains, d, levels, eps):
+        _require_cuda(flat, gains)
+        flat = flat.to(torch.float32).contiguous()
+        g = gains.to(torch.float32).contiguous()
+        B, T, W = flat.shape
+        y = torch.empty((B, T + 1, W - 1), dtype=torch.float32, device=flat.device)
+        ep = (ctypes.c_float * levels)(*[float(e) for e in eps])
+        with _timed("ews_graded_norm_fwd", flat.device, B * T, 1):
+            _lib.check(_lib.load().ews_graded_norm_fwd(_ptr(flat), _ptr(g), ep, B, T, d, levels, _ptr(y),
+                                                        _stream_ptr(flat.device)), "ews_graded_norm_fwd")
+        ctx.save_for_backward(flat, g)
+        ctx.meta = (d, levels, tuple(float(e) for e in eps))
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        flat, g = ctx.saved_tensors
+        d, levels, eps = ctx.meta
+        B, T, _ = flat.shape
+        lib = _lib.load()
+        dyc = dy.to(torch.float32).contiguous()
+        dflat = torch.empty_like(flat)
+        dg = torch.empty((levels,), dtype=torch.float32, device=flat.device)
+        work = torch.empty(max(1, int(lib.ews_graded_norm_work_size(B, T, d, levels)) // 4), dtype=torch.float32,
+                           device=flat.device)
+        ep = (ctypes.c_float * levels)(*eps)
+        with _timed("ews_graded_norm_bwd", flat.device, B * T, 2):
+            _lib.check(lib.ews_graded_norm_bwd(_ptr(flat), _ptr(g), ep, _ptr(dyc), B, T, d, levels, _ptr(dflat),
+                                               _ptr(dg), _ptr(work), work.numel() * 4, _stream_ptr(flat.device)),
+                       "ews_graded_norm_bwd")
+        return dflat, dg, None, None, None
+
+
 class DenseScan(torch.autograd.Function):
     """Dense engine, uniform clock: (path, D = I - M, F, G, H) -> flat EWS (prefix or terminal)."""
 

@@ -292,6 +292,22 @@ int ews_dense_leaf_adjoint(const float* A, const float* A_leaf, const float* h, 
                            const float* dG, const float* dH, void* work, size_t work_bytes, float* dA, float* dA_leaf,
                            float* dh, float* dW, ews_stream_t stream);
 
+/* ---- the block's stream consumer: graded RMS norm of the prefix stream --------------------------------
+ * Replaces the block's level-0 drop, zero-row prepend and GradedRMSNorm "live_rms" (ews/block.py:282-306 and
+ * :406, ews/norms.py:47-135) in one pass over the EWS prefix output: flat (batch, steps, 1 + D) float32 with
+ * D = d + d^2 (+ d^3) for `levels` = 2 (3) -> y (batch, steps + 1, D): y[:, 0] = 0 and row t + 1 level k =
+ * gains[k] x_k / (RMS(x_k) + eps[k]), x = flat[:, t, 1:], RMS 0 for an all-zero level. gains on the device
+ * (levels floats), eps a host array of `levels` positive floats.
+ *   ews_graded_norm_bwd: from dy (batch, steps + 1, D) the input gradient dflat (batch, steps, 1 + D; level-0
+ *   column zero) and dgains (levels), the latter summed in a fixed order; `work` is caller-owned device memory
+ *   of ews_graded_norm_work_size bytes. */
+size_t ews_graded_norm_work_size(int batch, int steps, int d, int levels);
+int ews_graded_norm_fwd(const float* flat, const float* gains, const float* eps, int batch, int steps, int d,
+                        int levels, float* y, ews_stream_t stream);
+int ews_graded_norm_bwd(const float* flat, const float* gains, const float* eps, const float* dy, int batch,
+                        int steps, int d, int levels, float* dflat, float* dgains, void* work, size_t work_bytes,
+                        ews_stream_t stream);
+
 /* ---- utilities --------------------------------------------------------------------------------- */
 /* Every forward and backward workspace begins with a status block whose error word the call clears and
  * a timed-out device wait sets. */

@@ -83,3 +83,51 @@ def test_stacked_adam_step_runs_and_lowers_the_loss():
         losses.append(float(loss))
     assert all(torch.isfinite(torch.tensor(losses)))
     assert losses[-1] < losses[0]
+
+
+@pytest.mark.parametrize("d,N,eps", [(16, 2, 1e-3), (4, 3, 1e-2), (7, 2, 0.5)])
+def test_graded_norm_kernel_matches_torch(d, N, eps):
+    """ews_graded_norm_fwd / _bwd (the block's level-0 drop, zero-row prepend and live-RMS graded norm in one
+    pass each way, ews/block.py:282-306, ews/norms.py:47-135) against the same steps as torch ops in float64:
+    relative error <= 1e-5 for the output, the input gradient and the gain gradients, including rows whose
+    level is all zero (RMS 0: the output is 0 and the gradient g / eps)."""
+    import numpy as np
+
+    from exponentially_weighted_signature_b200.block import GradedRMSNorm
+
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test run without a CUDA device")
+    g = torch.Generator().manual_seed(d * 10 + N)
+    B, L = 3, 37
+    D = sum(d**k for k in range(1, N + 1))
+    flat = torch.randn(B, L, 1 + D, generator=g) * torch.logspace(-3, 1, 1 + D)[None, None, :]
+    flat[0, 5, 1 : 1 + d] = 0.0  # an all-zero level 1
+    flat[1, 7, 1 + d :] = 0.0    # all-zero higher levels
+    norm = GradedRMSNorm(d, N, eps=eps)
+    with torch.no_grad():
+        norm.gains.copy_(torch.linspace(0.5, 1.5, N))
+    w = torch.randn(B, L + 1, D, generator=g)
+
+    f64 = flat.double().requires_grad_(True)
+    ref_norm = GradedRMSNorm(d, N, eps=eps).double()
+    with torch.no_grad():
+        ref_norm.gains.copy_(norm.gains.double())
+    ref = ref_norm.from_prefix(f64)
+    (ref * w.double()).sum().backward()
+
+    norm = norm.cuda()
+    fc = flat.cuda().requires_grad_(True)
+    out = norm.from_prefix(fc)
+    (out * w.cuda()).sum().backward()
+    torch.cuda.synchronize()
+
+    def rel(a, b):
+        a, b = a.detach().double().cpu().numpy(), b.detach().double().cpu().numpy()
+        return float(np.max(np.abs(a - b)) / max(float(np.max(np.abs(b))), 1e-300))
+
+    assert out.shape == (B, L + 1, D)
+    assert float(out[:, 0].abs().max()) == 0.0
+    assert rel(out, ref) <= 1e-5
+    assert rel(fc.grad, f64.grad) <= 1e-5
+    assert float(fc.grad[..., 0].abs().max()) == 0.0
+    assert rel(norm.gains.grad, ref_norm.gains.grad) <= 1e-5
