@@ -928,8 +928,219 @@ __global__ void __launch_bounds__(AGW * 32, 4) agg_kernel(Params p) {
     for (int q = 0; q < NP / 4; ++q) row[q] = make_float4(a2[4 * q], a2[4 * q + 1], a2[4 * q + 2], a2[4 * q + 3]);
 }
 
+// The same chunk aggregates with both contractions of an interval on the tensor cores (warp-level
+// m16n8k8 tf32 MMAs, 3xTF32 split): the flowed vectors E [x_r | y_r] (E = E_j, 32 x 32, against the
+// interval's 2 (QP + 1) vectors, two 16-wide N tiles) and the rank-(QP + 1) update W_X W_Y^T of the level-2
+// aggregate. Operands are read from shared memory in fragment order (tiles padded so that every fragment
+// load is conflict-free), so the warp-wide broadcast reads of the vectors are gone. Each interval's update
+// is formed in a zeroed MMA accumulator and added to the running aggregate with CUDA-core (round to
+// nearest) additions, so the tensor core's accumulation rounding never applies to the growing sum.
+constexpr int AXS = 36;  // row stride of the vector tile (16 rows: x_0..x_7 | y_0..y_7)
+constexpr int AWS = 12;  // row stride of the W_X / W_Y tiles (32 rows x 8)
+
+__host__ __device__ inline int agg_mma_warp_floats() { return 2 * 16 * AXS + 2 * NP * AGS + NP + 2 * NP * AWS; }
+
+__device__ __forceinline__ uint32_t tf32_hi(float v) { return tc::tf32_bits(v); }
+__device__ __forceinline__ uint32_t tf32_lo(float v, uint32_t hi) { return tc::tf32_bits(v - __uint_as_float(hi)); }
+
+__device__ __forceinline__ void mma_m16n8k8(float d[4], const uint32_t a[4], const uint32_t b[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// d += A B in 3xTF32 (hi hi + hi lo + lo hi) from fp32 fragments
+__device__ __forceinline__ void mma3_m16n8k8(float d[4], const float a[4], const float b[2]) {
+    uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        ah[i] = tf32_hi(a[i]);
+        al[i] = tf32_lo(a[i], ah[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        bh[i] = tf32_hi(b[i]);
+        bl[i] = tf32_lo(b[i], bh[i]);
+    }
+    mma_m16n8k8(d, ah, bh);
+    mma_m16n8k8(d, ah, bl);
+    mma_m16n8k8(d, al, bh);
+}
+
+template <int QP>
+__global__ void __launch_bounds__(AGW * 32, 3) agg_mma_kernel(Params p) {
+    extern __shared__ __align__(16) float agsm[];
+    const Geom& g = p.g;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int chunk = blockIdx.x * AGW + warp;
+    if (chunk >= g.B * g.C) return;
+    const int b = chunk / g.C, c = chunk - b * g.C;
+    const int N = g.N, Lc = g.Lc;
+    const int t0 = c * Lc, len = min(Lc, g.T - t0);
+    const int gq = lane >> 2, cq = lane & 3;  // fragment coordinates
+    float* Xb = agsm + (size_t)warp * agg_mma_warp_floats();  // 2 x 16 x AXS: rows x_0 = u, x_{1+a} = U_a, y_0 = s1, y_{1+a} = V_a
+    float* Eb = Xb + 2 * 16 * AXS;                             // 2 x NP x AGS
+    float* S1v = Eb + 2 * NP * AGS;                            // the chunk's level 1 (broadcast copy)
+    float* WX = S1v + NP;                                      // NP x AWS: W_X[i][r]
+    float* WY = WX + NP * AWS;                                 // NP x AWS: W_Y[i][r]
+    // the pad rows of both vector tiles stay zero (the copies fill rows 1..QP, 8..8+QP; row 0 is u)
+    for (int e = lane; e < 2 * 16 * AXS; e += 32) Xb[e] = 0.f;
+    float drow[NP];
+    {
+        const float* d = p.tab_d + (size_t)b * N * N;
+#pragma unroll
+        for (int k = 0; k < NP; ++k) drow[k] = (lane < N && k < N) ? d[lane * N + k] : 0.f;
+    }
+    float a2[2][4][4];  // the aggregate's level 2 in accumulator-fragment order: [m tile][n tile][value]
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) a2[mt][nt][v] = 0.f;
+    float s1 = 0.f;
+    S1v[lane] = 0.f;
+    __syncwarp();
+    const float* Ebase = p.pows + (size_t)b * (Lc + 1) * MM;
+    auto fetch = [&](int k) {
+        float* eb = Eb + (k & 1) * NP * AGS;
+        const float* src = Ebase + (size_t)(len - 1 - k) * MM;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const int e = lane + 32 * v;  // 16-byte piece e: row e / 8, column 4 (e % 8)
+            cp_async16(eb + (e >> 3) * AGS + 4 * (e & 7), src + 4 * e);
+        }
+        // [s1 | U_0..U_{QP-1} | V_0..V_{QP-1}] -> rows 8, 1..QP, 9..8+QP of the vector tile
+        float* xb = Xb + (k & 1) * 16 * AXS;
+        const float* lsrc = p.loc + ((size_t)b * g.T + t0 + k) * loc_width(QP);
+        for (int v = lane; v < (1 + 2 * QP) * 8; v += 32) {
+            const int vec = v >> 3, piece = v & 7;
+            const int row = vec == 0 ? 8 : vec <= QP ? vec : 8 + (vec - QP);
+            cp_async16(xb + row * AXS + 4 * piece, lsrc + 4 * v);
+        }
+        cp_async_commit();
+    };
+    fetch(0);
+    for (int k = 0; k < len; ++k) {
+        cp_async_wait<0>();
+        __syncwarp();
+        float* X = Xb + (k & 1) * 16 * AXS;
+        const float* E = Eb + (k & 1) * NP * AGS;
+        if (k + 1 < len) fetch(k + 1);
+        // u = S1 - D S1 (the level-1 state before this interval, flowed one step) -> row 0
+        float du0 = 0.f, du1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < NP; q += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(S1v + q);
+            du0 = fmaf(drow[q], v.x, du0);
+            du1 = fmaf(drow[q + 1], v.y, du1);
+            du0 = fmaf(drow[q + 2], v.z, du0);
+            du1 = fmaf(drow[q + 3], v.w, du1);
+        }
+        const float u = s1 - (du0 + du1);
+        X[lane] = u;
+        __syncwarp();
+        // EX[i][n] = sum_k E[i][k] X[n][k]: A = E (row-major), B[k][n] = X[n][k]
+        float ex[2][2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int v = 0; v < 4; ++v) ex[mt][nt][v] = 0.f;
+#pragma unroll
+        for (int sk = 0; sk < 4; ++sk) {
+            float af[2][4], bf[2][2];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const float* er = E + (16 * mt + gq) * AGS + 8 * sk + cq;
+                af[mt][0] = er[0];
+                af[mt][1] = er[8 * AGS];
+                af[mt][2] = er[4];
+                af[mt][3] = er[8 * AGS + 4];
+            }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                const float* xr = X + (8 * nt + gq) * AXS + 8 * sk + cq;
+                bf[nt][0] = xr[0];
+                bf[nt][1] = xr[4];
+            }
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) mma3_m16n8k8(ex[mt][nt], af[mt], bf[nt]);
+        }
+        // W = X^T - EX at the accumulator positions -> W_X (n < 8) and W_Y (n >= 8)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    const int i = 16 * mt + gq + 8 * (v >> 1), n = 2 * cq + (v & 1);
+                    const float w = X[(8 * nt + n) * AXS + i] - ex[mt][nt][v];
+                    (nt == 0 ? WX : WY)[i * AWS + n] = w;
+                }
+        __syncwarp();
+        // a2 += W_X W_Y^T (K = the vectors r, zero beyond QP): A[i][r] = W_X, B[r][q] = W_Y[q][r]
+        {
+            float af[2][4], bf[4][2];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const float* wr = WX + (16 * mt + gq) * AWS + cq;
+                af[mt][0] = wr[0];
+                af[mt][1] = wr[8 * AWS];
+                af[mt][2] = wr[4];
+                af[mt][3] = wr[8 * AWS + 4];
+            }
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                const float* wr = WY + (8 * nt + gq) * AWS + cq;
+                bf[nt][0] = wr[0];
+                bf[nt][1] = wr[4];
+            }
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+                    float dd[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma3_m16n8k8(dd, af[mt], bf[nt]);
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) a2[mt][nt][v] += dd[v];
+                }
+        }
+        // S1 <- u + s1 of this interval (every lane has read S1v, X and the W tiles before the barriers above)
+        s1 = u + X[8 * AXS + lane];
+        __syncwarp();
+        S1v[lane] = s1;
+    }
+    cp_async_wait<0>();
+    // the slot: [flow complement C(len) | S1 | S2 row-major]
+    float* as = p.agg + ((size_t)b * g.C + c) * g.SW;
+    const float* C = p.pw + ((size_t)b * 2 + (c == g.C - 1 ? 1 : 0)) * MM;
+    for (int e = lane; e < MM; e += 32) as[e] = C[e];
+    as[MM + lane] = s1;
+    float* S2 = as + MM + NP;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int i = 16 * mt + gq + 8 * h, q = 8 * nt + 2 * cq;
+                *reinterpret_cast<float2*>(S2 + i * NP + q) = make_float2(a2[mt][nt][2 * h], a2[mt][nt][2 * h + 1]);
+            }
+}
+
 template <int QP>
 static int launch_agg(const Params& p, cudaStream_t s) {
+    if (QP <= 7) {  // the tensor-core form (2 (QP + 1) <= 16 vectors); the CUDA-core one beyond
+        const size_t smem = sizeof(float) * (size_t)AGW * agg_mma_warp_floats();
+        cudaFuncSetAttribute(agg_mma_kernel<(QP <= 7 ? QP : 7)>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        agg_mma_kernel<(QP <= 7 ? QP : 7)><<<(p.g.B * p.g.C + AGW - 1) / AGW, AGW * 32, smem, s>>>(p);
+        return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
+    }
     const size_t smem = sizeof(float) * (size_t)AGW * agg_warp_floats(QP);
     cudaFuncSetAttribute(agg_kernel<QP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     agg_kernel<QP><<<(p.g.B * p.g.C + AGW - 1) / AGW, AGW * 32, smem, s>>>(p);
