@@ -549,7 +549,7 @@ def run_b200(args, rank, world, local_rank):
         d[2] = units
         launches += nl if nl is not None else counts.get(name, 1)  # the library's own count where it reports one
     # every engine call also launches ews_status_fold's one-thread kernel (the table calls do not)
-    launches += sum(v[1] for n, v in per.items() if not n.startswith(("ews_expm", "ews_dense_leaf", "ews_graded")))
+    launches += sum(v[1] for n, v in per.items() if not n.startswith(("ews_expm", "ews_dense_leaf", "ews_graded", "ews_gated")))
     dom = max(((n, v) for n, v in per.items() if n in setup["alg"]), key=lambda kv: kv[1][0])
     dom_name, (dom_ms, dom_n, dom_units) = dom
     avg_s = dom_ms / dom_n / 1e3

@@ -53,6 +53,9 @@ EXPORTED = (
     "ews_graded_norm_work_size",
     "ews_graded_norm_fwd",
     "ews_graded_norm_bwd",
+    "ews_gated_clock_work_size",
+    "ews_gated_clock_fwd",
+    "ews_gated_clock_bwd",
     "ews_read_device_status",
     "ews_status_fold",
     "ews_error_string",
@@ -234,6 +237,14 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.ews_graded_norm_bwd.argtypes = [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_size,
                                             _vp]
         lib.ews_graded_norm_bwd.restype = _c_int
+        _f = ctypes.c_float
+        lib.ews_gated_clock_work_size.argtypes = [_c_int, _c_int, _c_int]
+        lib.ews_gated_clock_work_size.restype = _c_size
+        lib.ews_gated_clock_fwd.argtypes = [_vp, _vp, _vp, _f, _f, _c_int, _c_int, _c_int, _vp, _vp]
+        lib.ews_gated_clock_fwd.restype = _c_int
+        lib.ews_gated_clock_bwd.argtypes = [_vp, _vp, _vp, _f, _f, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp,
+                                            _c_size, _vp]
+        lib.ews_gated_clock_bwd.restype = _c_int
         lib.ews_read_device_status.argtypes = [_vp, _vp, ctypes.POINTER(_c_int)]
         lib.ews_read_device_status.restype = _c_int
         lib.ews_diag_fwd_noalloc_status.argtypes = [_vp, ctypes.POINTER(_c_int)]

@@ -11,7 +11,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libews_b200.so")
 SOURCES = ["ews_capi.cu", "ews_diag.cu", "ews_dense.cu", "ews_block.cu", "ews_tables.cu", "ews_diag_term.cu",
-           "ews_graded.cu"]
+           "ews_graded.cu", "ews_clock.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode",

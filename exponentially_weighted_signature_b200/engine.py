@@ -409,6 +409,44 @@ class GradedNorm(torch.autograd.Function):
         return dflat, dg, None, None, None
 
 
+class GatedClock(torch.autograd.Function):
+    """The block's token-gated clock in one library pass each way (ews/clocks.py:409-466, no mask):
+    theta = [0, cumsum(relu(diff(in_scale x) @ w - b))] / norm_constant for x (B, L, H)."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, in_scale, norm_constant):
+        _require_cuda(x, w, b)
+        xc = x.to(torch.float32).contiguous()
+        wc, bc = w.to(torch.float32).contiguous(), b.to(torch.float32).reshape(1).contiguous()
+        B, L, H = xc.shape
+        theta = torch.empty((B, L), dtype=torch.float32, device=xc.device)
+        with _timed("ews_gated_clock_fwd", xc.device, B * L, 2):
+            _lib.check(_lib.load().ews_gated_clock_fwd(_ptr(xc), _ptr(wc), _ptr(bc), float(in_scale), float(norm_constant),
+                                                        B, L, H, _ptr(theta), _stream_ptr(xc.device)),
+                       "ews_gated_clock_fwd")
+        ctx.save_for_backward(xc, wc, bc)
+        ctx.consts = (float(in_scale), float(norm_constant))
+        return theta
+
+    @staticmethod
+    def backward(ctx, dtheta):
+        xc, wc, bc = ctx.saved_tensors
+        s, c = ctx.consts
+        B, L, H = xc.shape
+        lib = _lib.load()
+        dt = dtheta.to(torch.float32).contiguous()
+        dx = torch.empty_like(xc)
+        dw = torch.empty_like(wc)
+        db = torch.empty((1,), dtype=torch.float32, device=xc.device)
+        work = torch.empty(max(1, int(lib.ews_gated_clock_work_size(B, L, H)) // 4), dtype=torch.float32,
+                           device=xc.device)
+        with _timed("ews_gated_clock_bwd", xc.device, B * L, 4):
+            _lib.check(lib.ews_gated_clock_bwd(_ptr(xc), _ptr(wc), _ptr(bc), s, c, _ptr(dt), B, L, H, _ptr(dx), _ptr(dw),
+                                               _ptr(db), _ptr(work), work.numel() * 4, _stream_ptr(xc.device)),
+                       "ews_gated_clock_bwd")
+        return dx, dw, db.reshape(()), None, None
+
+
 class DenseScan(torch.autograd.Function):
     """Dense engine, uniform clock: (path, D = I - M, F, G, H) -> flat EWS (prefix or terminal)."""
 

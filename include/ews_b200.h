@@ -308,6 +308,20 @@ int ews_graded_norm_bwd(const float* flat, const float* gains, const float* eps,
                         int steps, int d, int levels, float* dflat, float* dgains, void* work, size_t work_bytes,
                         ews_stream_t stream);
 
+/* ---- the block's clock prologue: the token-gated clock ---------------------------------------------
+ * Replaces GatedClock "token_gated" without a mask (ews/clocks.py:409-466) on the block input: x (batch,
+ * steps, dim) float32, w (dim) and b (one float) on the device -> theta (batch, steps), theta_0 = 0 and
+ * theta_{t+1} = (1/norm_constant) sum_{tau <= t} relu(<in_scale x_{tau+1} - in_scale x_tau, w> - b).
+ *   ews_gated_clock_bwd: from dtheta the gradients dx (batch, steps, dim), dw (dim) and db (one float), the
+ *   latter two summed over samples in a fixed order; `work` is caller-owned device memory of
+ *   ews_gated_clock_work_size bytes. dim <= 8192. */
+size_t ews_gated_clock_work_size(int batch, int steps, int dim);
+int ews_gated_clock_fwd(const float* x, const float* w, const float* b, float in_scale, float norm_constant, int batch,
+                        int steps, int dim, float* theta, ews_stream_t stream);
+int ews_gated_clock_bwd(const float* x, const float* w, const float* b, float in_scale, float norm_constant,
+                        const float* dtheta, int batch, int steps, int dim, float* dx, float* dw, float* db, void* work,
+                        size_t work_bytes, ews_stream_t stream);
+
 /* ---- utilities --------------------------------------------------------------------------------- */
 /* Every forward and backward workspace begins with a status block whose error word the call clears and
  * a timed-out device wait sets. */
