@@ -69,7 +69,9 @@ class EWS(nn.Module):
     depth 2 the dense engine. Leaves: ``"series"`` at order ``series_q`` on every engine
     (``"block_series"`` is accepted for diagonal A, where both leaves agree to the series truncation);
     ``"van_loan"`` (the reference's default, M knots per interval, ews/core/van_loan.py:91-160) on the
-    diagonal engine under a uniform clock.
+    diagonal and dense engines; the closed-form leaves ``"plane_closed"`` and ``"jordan_closed"`` /
+    ``"jordan_closed_tables"`` (an ``AParamJordanRepeated`` A with uniform chains) on the dense engine, as
+    the series leaf's limit for the generator they read from A (uniform clock, ``||h A|| <= 0.5``).
     """
 
     def __init__(
