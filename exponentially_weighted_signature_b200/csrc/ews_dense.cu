@@ -2214,8 +2214,6 @@ __global__ void __launch_bounds__(128) table_grad_reg_kernel(Params p) {
         xs[e] = cc < d ? input_increment(p.path, b, t0 + k, cc, g.T, d, g.flags) : 0.f;
     }
     __syncthreads();
-    // column owned after the reduce-scatter: bits 4, 3, 2 of the lane
-    const int mycol = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
     const int lim = 1 << 20;
     int sl = 0;
     for (; sl < nslab; ++sl) {
@@ -2226,53 +2224,67 @@ __global__ void __launch_bounds__(128) table_grad_reg_kernel(Params p) {
         if (__syncthreads_or(!ok)) break;  // a copy that never landed: reported below
         const float* cs = ring + (size_t)slot * TG_SLAB * LW + lane;
         const int k0 = sl * TG_SLAB, kend = min(len, k0 + TG_SLAB);
-        for (int kk = k0 + warp; kk < kend; kk += 4) {
-            const int t = t0 + kk;
-            float x[8];
-            {
-                const float4 x0 = *reinterpret_cast<const float4*>(xs + kk * 8);
-                const float4 x1 = *reinterpret_cast<const float4*>(xs + kk * 8 + 4);
-                x[0] = x0.x; x[1] = x0.y; x[2] = x0.z; x[3] = x0.w;
-                x[4] = x1.x; x[5] = x1.y; x[6] = x1.z; x[7] = x1.w;
-            }
-            float cur[ROWS];
+        // the warp's two intervals of the slab (kk, kk + 4), their column sums reduce-scattered together:
+        // after the exchanges lane l holds interval l / 16, column 4 bit3(l) + 2 bit2(l) + bit1(l)
+        {
+            const int kk = k0 + warp;
+            const bool two = kk + 4 < kend;
+            float sv[16];
 #pragma unroll
-            for (int r = 0; r < ROWS; ++r) cur[r] = cs[(kk - k0) * LW + 32 * r];
-            float sv[8];
+            for (int i = 0; i < 16; ++i) sv[i] = 0.f;
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc) sv[cc] = 0.f;
+            for (int j = 0; j < 2; ++j) {
+                if (j == 1 && !two) break;
+                if (kk + 4 * j >= kend) break;
+                const int kj = kk + 4 * j;
+                const float4 x0 = *reinterpret_cast<const float4*>(xs + kj * 8);
+                const float4 x1 = *reinterpret_cast<const float4*>(xs + kj * 8 + 4);
+                const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-            for (int r = 0; r < ROWS; ++r)
+                for (int r = 0; r < ROWS; ++r) {
+                    const float cur = cs[(kj - k0) * LW + 32 * r];
 #pragma unroll
-                for (int cc = 0; cc < 8; ++cc) {
-                    acc[r][cc] = fmaf(cur[r], x[cc], acc[r][cc]);
-                    sv[cc] = fmaf(tab[r][cc], cur[r], sv[cc]);
+                    for (int cc = 0; cc < 8; ++cc) {
+                        acc[r][cc] = fmaf(cur, x[cc], acc[r][cc]);
+                        sv[8 * j + cc] = fmaf(tab[r][cc], cur, sv[8 * j + cc]);
+                    }
                 }
-            // reduce-scatter of the 8 column sums over the warp
-            const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0, hi4 = (lane & 4) != 0;
-            float s4[4];
+            }
+            if (kk < kend) {
+                const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0, hi4 = (lane & 4) != 0;
+                const bool hi2 = (lane & 2) != 0;
+                float s8[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float send = hi16 ? sv[i] : sv[i + 4];
-                const float keep = hi16 ? sv[i + 4] : sv[i];
-                s4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-            }
-            float s2[2];
+                for (int i = 0; i < 8; ++i) {
+                    const float send = hi16 ? sv[i] : sv[i + 8];
+                    const float keep = hi16 ? sv[i + 8] : sv[i];
+                    s8[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                }
+                float s4[4];
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const float send = hi8 ? s4[i] : s4[i + 2];
-                const float keep = hi8 ? s4[i + 2] : s4[i];
-                s2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                for (int i = 0; i < 4; ++i) {
+                    const float send = hi8 ? s8[i] : s8[i + 4];
+                    const float keep = hi8 ? s8[i + 4] : s8[i];
+                    s4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                }
+                float s2[2];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const float send = hi4 ? s4[i] : s4[i + 2];
+                    const float keep = hi4 ? s4[i + 2] : s4[i];
+                    s2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                }
+                float s1;
+                {
+                    const float send = hi2 ? s2[0] : s2[1];
+                    const float keep = hi2 ? s2[1] : s2[0];
+                    s1 = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+                }
+                s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+                const int j = (lane >> 4) & 1, col = ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+                if ((lane & 1) == 0 && col < d && (j == 0 || two))
+                    p.grad_dx[((size_t)b * g.T + t0 + kk + 4 * j) * d + col] = s1;
             }
-            float s1;
-            {
-                const float send = hi4 ? s2[0] : s2[1];
-                const float keep = hi4 ? s2[1] : s2[0];
-                s1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-            }
-            s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-            s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-            if ((lane & 3) == 0 && mycol < d) p.grad_dx[((size_t)b * g.T + t) * d + mycol] = s1;
         }
         __syncthreads();  // the slot is read: refill it
         if (tid == 0 && sl + TG_STAGES < nslab) issue(sl + TG_STAGES);
