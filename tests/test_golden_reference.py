@@ -100,3 +100,27 @@ def test_oracle_matches_reference(name):
                 mag = float(np.abs(g.numpy() * v).sum())
                 ref_dd = float(fx[f"dd_{r}_{d}"][b])
                 assert abs(proj - ref_dd) <= 1e-7 * mag + 1e-12, (name, b, r, d, proj, ref_dd, mag)
+
+
+def test_token_cached_scan_is_the_gathered_per_interval_scan():
+    """The reference's token-cached scan (ews/core/token_scan.py:55-118, fixtures tests/golden/token_*.npz) equals
+    the oracle's per-interval-clock scan of the gathered path (segment t: the token's displacement and clock
+    step; padded steps: zero and zero), which is how token_scan.token_cached_prefix runs it on the engines."""
+    import token_cases as tc
+
+    for name, spec in tc.CASES.items():
+        fx = dict(np.load(tc.fixture_path(name), allow_pickle=False))
+        inp = tc.case_inputs(name)
+        for k, v in inp.items():
+            assert str(fx[f"sha_{k}"]) == tc.sha(v)
+        for b in range(spec["B"]):
+            m = inp["mask"][b].astype(np.float64)
+            dx = inp["vdx"].astype(np.float64)[inp["tok"][b]] * m[:, None]
+            dth = inp["vdt"].astype(np.float64)[inp["tok"][b]] * m
+            path = torch.tensor(np.concatenate([np.zeros((1, dx.shape[1])), np.cumsum(dx, 0)], 0))
+            clock = torch.tensor(np.concatenate([[0.0], np.cumsum(dth)]))
+            out = O.ews_layer(path, clock, torch.tensor(inp["A"], dtype=torch.float64), spec["N"], leaf=spec["leaf"],
+                              series_q=spec["series_q"], reweighting_mode="displacement", readout="prefix")
+            got = out[..., 1:].numpy()
+            ref = fx["out"][b]
+            assert np.max(np.abs(got - ref)) <= 1e-10 * max(1.0, float(np.max(np.abs(ref)))), name
