@@ -45,6 +45,7 @@ struct Geom {
     unsigned flags;
     int spin_limit, q, ntiles;
     int lift_n;
+    int RS;  // stride of a recomputed state row (padded layout, 16-byte multiple)
     // per-warp shared memory (floats)
     int f_dys, f_dts, f_loc, f_stage, f_per_warp;  // f_loc: two staged local rows in the forward
     int b_dys, b_dts, b_dtg, b_dyg, b_loc, b_adj, b_gst, b_sst, b_gst2, b_sst2, b_per_warp;
@@ -68,6 +69,8 @@ struct Params {
     float* grad_dtheta;
     float* partials;       // per tile: dA blocks (16) | dlift (8 x d_in)
     const float* fagg;     // the forward aggregates
+    const float* fcarry;   // the forward's chunk carries (terminal backward: the recomputed chunks' starts)
+    float* scratch;        // terminal backward: per warp worker, the chunk's recomputed states (Lc rows of RS)
     float* loc;            // (B, T, LROW): every interval's local element, written by local_kernel
     float c1[KQ];             // c1_p = 1 / (p + 1)
     float c2[KQ * KQ];        // c2_pr = 1 / ((p + r + 2)(r + 1))
@@ -1414,6 +1417,16 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
     const AdjBuf ab(dxs + g.b_adj);
     float* gst = dxs + g.b_gst;  // gradient row; also the dx staging at the end of a tile
     float* sst = dxs + g.b_sst;  // S_{t-1} row
+    // Terminal readout: the cotangent has one row per sample (t = T - 1), and the states S_{t-1} come from
+    // re-running the chunk from the forward's carry into this warp's scratch rows (the reference's
+    // block_terminal_vjp recomputes each chunk from its saved start the same way), not from a prefix stream.
+    const bool term = g.readout == EWS_READOUT_TERMINAL;
+    float* scr = term ? p.scratch + (size_t)(blockIdx.x * kWarps + warp) * g.Lc * g.RS : nullptr;
+    // source of the cotangent row of interval t (null where it is zero)
+    auto grad_row = [&](int b, int t) -> const float* {
+        if (term) return t == g.T - 1 ? p.grad_out + (size_t)b * g.W : nullptr;
+        return p.grad_out + ((size_t)b * g.T + t) * g.W;
+    };
 
     for (;;) {
         const int tile = next_ticket(p.st);
@@ -1436,22 +1449,26 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         float* gst2 = dxs + g.b_gst2;
         auto issue_zero_carry = [&](int k) {
             const int buf = (len - 1 - k) & 1;
-            warp_copy_row_padded_async(buf ? gst2 : gst, p.grad_out + ((size_t)b * g.T + t0 + k) * g.W, g.N);
+            const float* gsrc = grad_row(b, t0 + k);
+            if (gsrc) warp_copy_row_padded_async(buf ? gst2 : gst, gsrc, g.N);
             fetch_local(p, b, t0 + k, lst + (k & 1) * LROW);
         };
-        issue_zero_carry(len - 1);
-        for (int k = len - 1; k >= 0; --k) {
-            if (k >= 1)
-                issue_zero_carry(k - 1);
-            else
-                cp_async_commit();
-            cp_async_wait<1>();
-            __syncwarp();
-            add_grad_row(mu, ((len - 1 - k) & 1) ? gst2 : gst, g.N, i, jb);
-            mu_step_row(lst + (k & 1) * LROW, mu, i, jb);
-            __syncwarp();
+        // (terminal readout: every chunk but the last has a zero cotangent and a zero local adjoint)
+        if (!term || c == g.C - 1) {
+            issue_zero_carry(len - 1);
+            for (int k = len - 1; k >= 0; --k) {
+                if (k >= 1)
+                    issue_zero_carry(k - 1);
+                else
+                    cp_async_commit();
+                cp_async_wait<1>();
+                __syncwarp();
+                if (grad_row(b, t0 + k)) add_grad_row(mu, ((len - 1 - k) & 1) ? gst2 : gst, g.N, i, jb);
+                mu_step_row(lst + (k & 1) * LROW, mu, i, jb);
+                __syncwarp();
+            }
+            cp_async_wait<0>();
         }
-        cp_async_wait<0>();
         // ---- 2. look-back over the later chunks: the cotangent at the chunk's end
         A3 lam;
         lam.zero();
@@ -1490,6 +1507,25 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
             store_a3(p.incl + slot, out, i, jb);
             publish(flag, kFlagIncl);
         }
+        // ---- terminal readout: the chunk's states S_{t0-1} .. S_{t0+len-2} recomputed from the forward's carry
+        // into the scratch rows 0 .. len-1 (padded layout), the local elements staged as in pass 1
+        if (term) {
+            E3 S;
+            load_e3(p.fcarry + slot, S, i, jb);
+            stage_row(scr, S, g.N, i, jb);
+            if (len > 1) fetch_local(p, b, t0, lst);
+            for (int k = 0; k + 1 < len; ++k) {
+                cp_async_wait<0>();
+                __syncwarp();
+                if (k + 2 < len) fetch_local(p, b, t0 + k + 1, lst + ((k + 1) & 1) * LROW);
+                chen_step_row(lst + (k & 1) * LROW, S, i, jb);
+                stage_row(scr + (size_t)(k + 1) * g.RS, S, g.N, i, jb);
+                __syncwarp();
+            }
+            cp_async_wait<0>();
+            __threadfence_block();
+            __syncwarp();
+        }
         // ---- 3. exact adjoint from the carry, with the gradients
         BwdOut bo;
 #pragma unroll
@@ -1500,8 +1536,14 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
         float* sst2 = dxs + g.b_sst2;
         auto issue_rows = [&](int k, int buf) {
             const int t = t0 + k;
-            warp_copy_row_padded_async(buf ? gst2 : gst, p.grad_out + ((size_t)b * g.T + t) * g.W, g.N);
-            if (t > 0) warp_copy_row_padded_async(buf ? sst2 : sst, p.out + ((size_t)b * g.T + t - 1) * g.W, g.N);
+            const float* gsrc = grad_row(b, t);
+            if (gsrc) warp_copy_row_padded_async(buf ? gst2 : gst, gsrc, g.N);
+            if (t > 0) {
+                if (term)
+                    warp_load_span_async(buf ? sst2 : sst, scr + (size_t)k * g.RS, g.RS);  // 16-byte aligned: lands at the buffer start
+                else
+                    warp_copy_row_padded_async(buf ? sst2 : sst, p.out + ((size_t)b * g.T + t - 1) * g.W, g.N);
+            }
             cp_async_commit();
         };
         issue_rows(len - 1, 0);
@@ -1519,7 +1561,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_kernel(Params p) {
                 for (int e = lane; e < row_floats_padded(g.N); e += 32) srow[e] = 0.f;
             __syncwarp();
             build_local<QT>(p, Ablk, dys + k * NB, dts[k], lc, true);
-            add_grad_row(a, grow, g.N, i, jb);
+            if (!term || t == g.T - 1) add_grad_row(a, grow, g.N, i, jb);
             bwd_step<QT>(p, Ablk, lc, ab, srow, dts[k], a, bo, dyg + k * NB, dtg + k, i, jb);
             __syncwarp();
         }
@@ -1633,6 +1675,7 @@ int make_geom(const ews_block_args* a, Geom* g) {
     g->C = (g->T + g->Lc - 1) / g->Lc;
     g->ntiles = g->B * g->C;
     g->lift_n = align4(NB * g->d_in);
+    g->RS = align4(row_floats_padded(g->N));
     const int xs = align4(g->Lc * g->d_in), ys = g->Lc * NB, ts = align4(g->Lc);
     g->f_dys = xs;
     g->f_dts = xs + ys;
@@ -1656,10 +1699,39 @@ int make_geom(const ews_block_args* a, Geom* g) {
 size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 struct WsLayout {
-    size_t status, flags, agg, incl, carry, partials, loc, total;
+    size_t status, flags, agg, incl, carry, partials, loc, scratch, total;
 };
 
-WsLayout bwd_layout(const Geom& g) {
+size_t bwd_smem(const Geom& g);
+int num_sms();
+
+// The backward's kernel (series order fixed at compile time), its shared memory and its persistent grid.
+struct BwdPlan {
+    void (*kernel)(Params);
+    size_t smem;
+    int grid;
+};
+
+int bwd_plan(const Geom& g, BwdPlan* bp) {
+    using BK = void (*)(Params);
+    static const BK kernels[KQ] = {bwd_kernel<0>, bwd_kernel<1>, bwd_kernel<2>, bwd_kernel<3>, bwd_kernel<4>,
+                                   bwd_kernel<5>, bwd_kernel<6>, bwd_kernel<7>, bwd_kernel<8>};
+    bp->kernel = kernels[g.q];
+    bp->smem = bwd_smem(g);
+    if (bp->smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+    cudaFuncSetAttribute(bp->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bp->smem);
+    cudaFuncSetAttribute(bp->kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    const int per_sm = resident_ctas((const void*)bp->kernel, kWarps * 32, bp->smem);
+    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
+    int grid = per_sm * num_sms();
+    const int need = (g.ntiles + kWarps - 1) / kWarps;
+    if (grid > need) grid = need;
+    bp->grid = grid;
+    return EWS_OK;
+}
+
+// grid: the backward's CTA count (sizes the terminal readout's per-warp scratch rows)
+WsLayout bwd_layout(const Geom& g, int grid) {
     WsLayout L{};
     size_t o = 0;
     L.status = o;
@@ -1673,6 +1745,8 @@ WsLayout bwd_layout(const Geom& g) {
     o += slots;
     L.partials = o;
     o += al256(sizeof(float) * (size_t)g.ntiles * (16 + NB * g.d_in));
+    L.scratch = o;
+    if (g.readout == EWS_READOUT_TERMINAL) o += al256(sizeof(float) * (size_t)grid * kWarps * g.Lc * g.RS);
     L.total = o;
     return L;
 }
@@ -1730,7 +1804,12 @@ extern "C" int ews_block_workspace_size(const ews_block_args* a, size_t* fwd_byt
     const int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
     if (fwd_bytes) *fwd_bytes = fwd_layout(g).total;
-    if (bwd_bytes) *bwd_bytes = bwd_layout(g).total;
+    if (bwd_bytes) {
+        BwdPlan bp;
+        const int pr = bwd_plan(g, &bp);
+        if (pr != EWS_OK) return pr;
+        *bwd_bytes = bwd_layout(g, bp.grid).total;
+    }
     return EWS_OK;
 }
 
@@ -1788,13 +1867,15 @@ extern "C" int ews_block_bwd(const ews_block_args* a, ews_stream_t stream) {
     Geom g;
     const int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
-    if (g.readout != EWS_READOUT_PREFIX) return EWS_ERR_UNSUPPORTED;  // callers run the prefix for gradients
     if (!a->path || !a->clock || !a->blocks || !a->out || !a->grad_out || !a->grad_dx || !a->grad_dtheta ||
         !a->grad_blocks)
         return EWS_ERR_INVALID_ARGUMENT;
     if (!a->lift && a->d_in != a->dim) return EWS_ERR_INVALID_ARGUMENT;
+    BwdPlan bp;
+    const int pr = bwd_plan(g, &bp);
+    if (pr != EWS_OK) return pr;
     const WsLayout F = fwd_layout(g);
-    const WsLayout L = bwd_layout(g);
+    const WsLayout L = bwd_layout(g, bp.grid);
     if (!a->fwd_ws || a->fwd_ws_bytes < F.total) return EWS_ERR_WORKSPACE;
     if (!a->bwd_ws || a->bwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
@@ -1817,23 +1898,11 @@ extern "C" int ews_block_bwd(const ews_block_args* a, ews_stream_t stream) {
     p.incl = (float*)(ws + L.incl);
     p.partials = (float*)(ws + L.partials);
     p.fagg = (const float*)(fws + F.agg);
+    p.fcarry = (const float*)(fws + F.carry);
     p.loc = (float*)(fws + F.loc);
+    p.scratch = g.readout == EWS_READOUT_TERMINAL ? (float*)(ws + L.scratch) : nullptr;
     series_coefficients(g.q, &p);
-    const size_t smem = bwd_smem(g);
-    if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
-    using BK = void (*)(Params);
-    static const BK kernels[KQ] = {bwd_kernel<0>, bwd_kernel<1>, bwd_kernel<2>, bwd_kernel<3>, bwd_kernel<4>,
-                                   bwd_kernel<5>, bwd_kernel<6>, bwd_kernel<7>, bwd_kernel<8>};
-    const BK bk = kernels[g.q];  // the series order fixed at compile time for the letters of the exact pass
-    cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(bk, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-    int per_sm = 0;
-    per_sm = resident_ctas((const void*)bk, kWarps * 32, smem);
-    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
-    int grid = per_sm * num_sms();
-    const int need = (g.ntiles + kWarps - 1) / kWarps;
-    if (grid > need) grid = need;
-    bk<<<grid, kWarps * 32, smem, s>>>(p);
+    bp.kernel<<<bp.grid, kWarps * 32, bp.smem, s>>>(p);
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     reduce_kernel<<<2 * g.N + (a->grad_lift ? g.N * g.d_in : 0), 256, 0, s>>>(p, a->grad_blocks, a->grad_lift);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;

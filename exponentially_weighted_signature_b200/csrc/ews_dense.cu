@@ -41,6 +41,7 @@ struct Geom {
     int agg_pre;      // forward: the chunk aggregates come from agg_kernel (the chain runs the output pass only)
     int bwd_mode;     // backward chain: 1 = the zero-carry pass only (local adjoints), 2 = the exact pass only
     int tab_n;        // floats of the F, G, H tables (N x d_in each, padded to NP rows)
+    int grp0, ngrp;   // the chunk groups (TILES chunks each) that fwd_tc_kernel and bwd_exact_kernel cover
 };
 
 struct Params {
@@ -68,7 +69,22 @@ struct Params {
     float* gex;        // forward: per (sample, scan group) the exclusive product of the earlier groups (SW);
                        // backward: per (sample, scan group) the cotangent arriving at the group's end
     float* gsuf;       // backward: per chunk the forward aggregate of the chunks from it to its group's end
+    float* srows;      // terminal backward: the window's recomputed states, per chunk Lc rows of W (row k holds
+                       // S_{t0+k-1}: the carry, then the chunk's own states but its last)
 };
+
+// The cotangent row of interval t of sample b, or null where it is zero: a terminal readout has one row per
+// sample (t = T - 1), a prefix readout one per interval.
+__device__ __forceinline__ const float* grad_row(const Params& p, int b, int t) {
+    if (p.g.readout == EWS_READOUT_TERMINAL) return t == p.g.T - 1 ? p.grad_out + (size_t)b * p.g.W : nullptr;
+    return p.grad_out + ((size_t)b * p.g.T + t) * p.g.W;
+}
+
+// Terminal backward: the first of the scratch rows of chunk c_me (the tile's warp) of sample b in the window.
+__device__ __forceinline__ float* window_rows(const Params& p, int grp, int warp, int b) {
+    const Geom& g = p.g;
+    return p.srows + ((((size_t)(grp - g.grp0) * 4 + warp) * g.B + b) * g.Lc) * g.W;
+}
 
 // Width (floats) of one interval's local terms in `loc`.
 __host__ __device__ inline int loc_width(int QP) { return (1 + 2 * QP) * 32; }
@@ -177,6 +193,7 @@ __device__ void identity_smem(float* P, float* S1, float* S2) {
 namespace tc {
 
 constexpr int TILES = 4;
+static_assert(TILES == 4, "window_rows lays out 4 chunks per tile");
 constexpr int NTH = 128;
 constexpr int RQS = 33;  // padded row stride of the row/column exchange buffer
 
@@ -611,14 +628,17 @@ __global__ void __launch_bounds__(tc::NTH, 3) fwd_tc_kernel(Params p) {
     float* vt = s.vec + warp * vec_per_tile(g.QP);  // S1 | u | two local-term slots
     float* RQt = s.RQ + warp * 32 * RQS;
     const int LW = loc_width(g.QP);
+    // terminal readout (run by the backward): the window's states go to the scratch rows, not to `out`
+    const bool term = g.readout == EWS_READOUT_TERMINAL;
+    (void)ntiles;
 
     for (;;) {
         if (tid == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
         __syncthreads();
         const int tile = s.bcast[0];
         __syncthreads();
-        if (tile >= ntiles) break;
-        const int grp = tile / g.B, b = tile - grp * g.B;
+        if (tile >= g.B * g.ngrp) break;
+        const int grp = g.grp0 + tile / g.B, b = tile - (grp - g.grp0) * g.B;
         const int c_me = grp * TILES + warp;
         const bool valid_me = c_me < g.C;
         const int t0_me = c_me * g.Lc;
@@ -638,6 +658,15 @@ __global__ void __launch_bounds__(tc::NTH, 3) fwd_tc_kernel(Params p) {
 #pragma unroll
             for (int n = 0; n < 32; ++n) col[n] = valid_me ? ldcg(cs + MM + NP + n * NP + lane) : 0.f;
             vt[lane] = valid_me ? ldcg(cs + MM + lane) : 0.f;
+        }
+        float* wrows = term ? window_rows(p, grp, warp, b) : nullptr;
+        if (term && len_me > 0 && lane < N) {
+            // scratch row 0: the chunk's carry, the state its first interval starts from
+            if (lane == 0) wrows[0] = 1.f;
+            wrows[1 + lane] = vt[lane];
+#pragma unroll
+            for (int n = 0; n < 32; ++n)
+                if (n < N) wrows[1 + N + n * N + lane] = col[n];
         }
         __syncwarp();
         // the intervals' local terms (computed by local_kernel), copied in one interval ahead
@@ -727,9 +756,10 @@ __global__ void __launch_bounds__(tc::NTH, 3) fwd_tc_kernel(Params p) {
                     if (live) vt[lane] = s1new;
                     fence_before();
                     __syncwarp();
-                    if (live && lane < N) {
+                    if (live && lane < N && (!term || k + 1 < len_me)) {
                         // the prefix row straight from registers: each level-2 row is one contiguous run
-                        float* row = p.out + ((size_t)b * g.T + t0_me + k) * g.W;
+                        // (terminal: the state the next interval starts from, scratch row k + 1)
+                        float* row = term ? wrows + (size_t)(k + 1) * g.W : p.out + ((size_t)b * g.T + t0_me + k) * g.W;
                         if (lane == 0) row[0] = 1.f;
                         row[1 + lane] = s1new;
 #pragma unroll
@@ -1621,7 +1651,6 @@ __global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
             const int c = grp * TILES + t;
             if (c < g.C) steps = max(steps, min(g.Lc, g.T - c * g.Lc));
         }
-        const float* grows = p.grad_out + ((size_t)b * g.T + t0_me) * g.W;  // the chunk's gradient rows
         auto fetch_s1 = [&](int k) { fetch_loc(p, b, t0_me + k, vt + 2 * NP + (k & 1) * NP, NP); };
         tc_load_tables(p, s, b, true);
         __syncthreads();
@@ -1636,15 +1665,16 @@ __global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
         // interval a step starts from is added before it: here for the first step, else in the epilogue of
         // the step before.
         if (len_me == steps && len_me > 0) {
-            const float* gr = grows + (size_t)(len_me - 1) * g.W;
-            if (lane < N) {
+            const float* gr = grad_row(p, b, t0_me + len_me - 1);
+            if (lane < N && gr) {
 #pragma unroll
                 for (int n = 0; n < 32; ++n)
                     if (n < N) col[n] += __ldg(gr + 1 + N + n * N + lane);
                 vt[lane] += __ldg(gr + 1 + lane);
             }
             fetch_s1(len_me - 1);
-            if (len_me >= 2) prefetch_row_l2(gr - g.W, g.W);
+            const float* gp = len_me >= 2 ? grad_row(p, b, t0_me + len_me - 2) : nullptr;
+            if (gp) prefetch_row_l2(gp, g.W);
         }
         cp_async_commit();
         __syncwarp();
@@ -1655,13 +1685,16 @@ __global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
             __syncwarp();
             if (next) fetch_s1(k - 1);
             cp_async_commit();
-            if (k >= 2 && k - 2 < len_me) prefetch_row_l2(grows + (size_t)(k - 2) * g.W, g.W);
+            if (k >= 2 && k - 2 < len_me) {
+                const float* gp = grad_row(p, b, t0_me + k - 2);
+                if (gp) prefetch_row_l2(gp, g.W);
+            }
             // the next interval's gradient: loads in flight for the whole step, added in the epilogue
             float gn[32];
             float gn1 = 0.f;
             {
-                const float* gr = grows + (size_t)(k - 1) * g.W;
-                const bool ld = next && lane < N;
+                const float* gr = next ? grad_row(p, b, t0_me + k - 1) : nullptr;
+                const bool ld = gr && lane < N;
 #pragma unroll
                 for (int n = 0; n < 32; ++n) gn[n] = (ld && n < N) ? __ldg(gr + 1 + N + n * N + lane) : 0.f;
                 if (ld) gn1 = __ldg(gr + 1 + lane);
@@ -1892,9 +1925,19 @@ __global__ void __launch_bounds__(tc::NTH, 2) bwd_exact_kernel(Params p) {
     float* stg = lb + LW;                         // S1p at +4, S2p row-major (stride NP) at +36
     float* RQt = s.A3hi + warp * 32 * RQS;        // exchange buffer, inside the l~2^T operand's space
 
+    // terminal readout: the states come from the window's scratch rows (fwd_tc_kernel ran the window's
+    // chunks from their carries just before), not from a prefix stream
+    const bool term = g.readout == EWS_READOUT_TERMINAL;
+    const float* wrows = nullptr;  // the warp's chunk's scratch rows (terminal)
+    int t0_w = 0;                  // the warp's chunk's first interval
+    // the row holding S_{t-1}, the state interval t starts from
+    auto state_row = [&](int b, int t) -> const float* {
+        return term ? wrows + (size_t)(t - t0_w) * g.W : p.out + ((size_t)b * g.T + t - 1) * g.W;
+    };
+
     // The warp's copy of prefix row t - 1 (the state the interval starts from) into the staging rows.
     auto stage_prev = [&](int b, int t) {
-        const float* row = p.out + ((size_t)b * g.T + t - 1) * g.W;
+        const float* row = state_row(b, t);
         if (FULL) {
             for (int e = lane; e < g.W; e += 32) cp_async4(stg + 3 + e, row + e);
         } else {
@@ -1905,13 +1948,14 @@ __global__ void __launch_bounds__(tc::NTH, 2) bwd_exact_kernel(Params p) {
         }
     };
 
+    (void)ntiles;
     for (;;) {
         if (tid == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
         __syncthreads();
         const int tile = s.bcast[0];
         __syncthreads();
-        if (tile >= ntiles) break;
-        const int grp = tile / g.B, b = tile - grp * g.B;
+        if (tile >= g.B * g.ngrp) break;
+        const int grp = g.grp0 + tile / g.B, b = tile - (grp - g.grp0) * g.B;
         const int c_me = grp * TILES + warp;
         const bool valid_me = c_me < g.C;
         const int t0_me = c_me * g.Lc;
@@ -1921,7 +1965,10 @@ __global__ void __launch_bounds__(tc::NTH, 2) bwd_exact_kernel(Params p) {
             const int c = grp * TILES + t;
             if (c < g.C) steps = max(steps, min(g.Lc, g.T - c * g.Lc));
         }
-        const float* grows = p.grad_out + ((size_t)b * g.T + t0_me) * g.W;  // the chunk's gradient rows
+        if (term) {
+            wrows = window_rows(p, grp, warp, b);
+            t0_w = t0_me;
+        }
         {
             const float* m = p.tab_d + (size_t)b * N * N;
             for (int e = tid; e < MM; e += blockDim.x) {
@@ -1951,8 +1998,8 @@ __global__ void __launch_bounds__(tc::NTH, 2) bwd_exact_kernel(Params p) {
         // cp.async groups per step: the local terms (waited for at the step's start), then the prefix row
         // (waited for before the dM update).
         if (len_me == steps && len_me > 0) {
-            const float* gr = grows + (size_t)(len_me - 1) * g.W;
-            if (lane < N) {
+            const float* gr = grad_row(p, b, t0_me + len_me - 1);
+            if (lane < N && gr) {
 #pragma unroll
                 for (int n = 0; n < 32; ++n)
                     if (n < N) col[n] += __ldg(gr + 1 + N + n * N + lane);
@@ -1974,8 +2021,9 @@ __global__ void __launch_bounds__(tc::NTH, 2) bwd_exact_kernel(Params p) {
             cp_async_wait<1>();
             __syncwarp();
             if (k >= 2 && k - 2 < len_me) {
-                prefetch_row_l2(grows + (size_t)(k - 2) * g.W, g.W);
-                if (t >= 3) prefetch_row_l2(p.out + ((size_t)b * g.T + t - 3) * g.W, g.W);
+                const float* gp = grad_row(p, b, t - 2);
+                if (gp) prefetch_row_l2(gp, g.W);
+                if (t >= 3) prefetch_row_l2(state_row(b, t - 2), g.W);
             }
             // E0: rows of l~2 (through the exchange buffer) -> A1; columns of l~2 -> A3
             float srow[32];
@@ -2046,8 +2094,8 @@ __global__ void __launch_bounds__(tc::NTH, 2) bwd_exact_kernel(Params p) {
             float gn[32];
             float gn1 = 0.f;
             {
-                const float* gr = grows + (size_t)(k - 1) * g.W;
-                const bool ld = next && lane < N;
+                const float* gr = next ? grad_row(p, b, t - 1) : nullptr;
+                const bool ld = gr && lane < N;
 #pragma unroll
                 for (int n = 0; n < 32; ++n) gn[n] = (ld && n < N) ? __ldg(gr + 1 + N + n * N + lane) : 0.f;
                 if (ld) gn1 = __ldg(gr + 1 + lane);
@@ -2527,13 +2575,36 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
     }
     g->C = (g->T + g->Lc - 1) / g->Lc;
     g->ntiles = g->B * g->C;
+    g->grp0 = 0;
+    g->ngrp = (g->C + tc::TILES - 1) / tc::TILES;
+    return EWS_OK;
+}
+
+// The output pass's launch (fwd_tc_kernel: shared memory, persistent grid) and, for the terminal backward,
+// the chunk groups per window: enough tiles to fill that grid once, so the scratch rows are bounded by the
+// grid, not by the sequence.
+struct OutPlan {
+    size_t smem;
+    int grid, wgrp;
+};
+
+static int out_plan(const Geom& g, OutPlan* op) {
+    op->smem = tc::tc_out_smem_bytes(g.QP);
+    if (op->smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
+    cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)op->smem);
+    cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    const int per_sm = resident_ctas((const void*)fwd_tc_kernel, tc::NTH, op->smem);
+    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
+    op->grid = per_sm * num_sms();
+    const int groups = (g.C + tc::TILES - 1) / tc::TILES;
+    op->wgrp = std::min(groups, (op->grid + g.B - 1) / g.B);
     return EWS_OK;
 }
 
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 struct WsLayout {
-    size_t status, flags, agg, incl, carry, partials, pw, loc, pows, gex, total;
+    size_t status, flags, agg, incl, carry, partials, pw, loc, pows, gex, srows, total;
 };
 
 static WsLayout fwd_layout(const Geom& g) {
@@ -2562,7 +2633,8 @@ static WsLayout fwd_layout(const Geom& g) {
     return L;
 }
 
-static WsLayout bwd_layout(const Geom& g) {
+// wgrp: the terminal backward's chunk groups per window (out_plan); unused for the prefix readout
+static WsLayout bwd_layout(const Geom& g, int wgrp) {
     WsLayout L{};
     size_t o = 0;
     L.status = o;
@@ -2584,6 +2656,9 @@ static WsLayout bwd_layout(const Geom& g) {
     o += slots;
     L.gex = o;    // the reverse group scan's two round buffers of (G, mu) elements
     o += 2 * al256(sizeof(float) * (size_t)g.B * scan_groups(g.C) * 2 * g.SW);
+    L.srows = o;  // terminal: the window's recomputed states
+    if (g.readout == EWS_READOUT_TERMINAL)
+        o += al256(sizeof(float) * (size_t)wgrp * tc::TILES * g.B * g.Lc * g.W);
     L.total = o;
     return L;
 }
@@ -2600,7 +2675,16 @@ extern "C" int ews_dense_workspace_size(const ews_dense_args* a, size_t* fwd_byt
     const int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
     if (fwd_bytes) *fwd_bytes = fwd_layout(g).total;
-    if (bwd_bytes) *bwd_bytes = bwd_layout(g).total;
+    if (bwd_bytes) {
+        int wgrp = 0;
+        if (g.readout == EWS_READOUT_TERMINAL) {
+            OutPlan op;
+            const int pr = out_plan(g, &op);
+            if (pr != EWS_OK) return pr;
+            wgrp = op.wgrp;
+        }
+        *bwd_bytes = bwd_layout(g, wgrp).total;
+    }
     return EWS_OK;
 }
 
@@ -2611,9 +2695,19 @@ extern "C" int ews_dense_launches(const ews_dense_args* a, int* fwd_launches, in
     int rounds = 1;  // the group scans' rounds
     while ((1 << rounds) < scan_groups(g.C)) ++rounds;
     // forward: power, local, powers, agg, scan_local, rounds, scan_fix [, fwd_tc for the prefix readout];
-    // backward: bwd_tc, bscan_local, rounds, bscan_fix, bwd_exact, table_grad, reduce
+    // backward: bwd_tc, bscan_local, rounds, bscan_fix, bwd_exact, table_grad, reduce (terminal readout:
+    // fwd_tc and bwd_exact once per window of chunk groups)
     if (fwd_launches) *fwd_launches = 6 + rounds + (g.readout == EWS_READOUT_PREFIX ? 1 : 0);
-    if (bwd_launches) *bwd_launches = 6 + rounds;
+    if (bwd_launches) {
+        int windows = 1;
+        if (g.readout == EWS_READOUT_TERMINAL) {
+            OutPlan op;
+            const int pr = out_plan(g, &op);
+            if (pr != EWS_OK) return pr;
+            windows = (g.ngrp + op.wgrp - 1) / op.wgrp;
+        }
+        *bwd_launches = 5 + rounds + 2 * windows - (g.readout == EWS_READOUT_TERMINAL ? 0 : 1);
+    }
     return EWS_OK;
 }
 
@@ -2690,17 +2784,11 @@ extern "C" int ews_dense_fwd(const ews_dense_args* a, ews_stream_t stream) {
     scan_fix_kernel<<<g.B * g.C, CST, 0, s>>>(p);
     if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
     if (g.readout == EWS_READOUT_TERMINAL) return EWS_OK;  // the scan wrote the terminal rows
-    const size_t smem = tc::tc_out_smem_bytes(g.QP);
-    if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
-    cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-    int per_sm = 0;
-    per_sm = resident_ctas((const void*)fwd_tc_kernel, tc::NTH, smem);
-    if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
-    const int groups = (g.C + tc::TILES - 1) / tc::TILES;
-    int grid = per_sm * num_sms();
-    if (grid > g.B * groups) grid = g.B * groups;
-    fwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
+    OutPlan op;
+    const int pr = out_plan(g, &op);
+    if (pr != EWS_OK) return pr;
+    const int grid = std::min(op.grid, g.B * g.ngrp);
+    fwd_tc_kernel<<<grid, tc::NTH, op.smem, s>>>(p);
     return cudaGetLastError() == cudaSuccess ? EWS_OK : EWS_ERR_LAUNCH;
 }
 
@@ -2708,11 +2796,16 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     Geom g;
     int rc = make_geom(a, &g);
     if (rc != EWS_OK) return rc;
-    if (g.readout != EWS_READOUT_PREFIX) return EWS_ERR_UNSUPPORTED;
     if (!a->path || !a->out || !a->grad_out || !a->grad_dx || !a->grad_d || !a->grad_f || !a->grad_g || !a->grad_h)
         return EWS_ERR_INVALID_ARGUMENT;
+    const bool term = g.readout == EWS_READOUT_TERMINAL;
+    OutPlan op{};
+    if (term) {
+        rc = out_plan(g, &op);
+        if (rc != EWS_OK) return rc;
+    }
     const WsLayout F = fwd_layout(g);
-    const WsLayout L = bwd_layout(g);
+    const WsLayout L = bwd_layout(g, op.wgrp);
     if (!a->fwd_ws || a->fwd_ws_bytes < F.total) return EWS_ERR_WORKSPACE;
     if (!a->bwd_ws || a->bwd_ws_bytes < L.total) return EWS_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
@@ -2735,6 +2828,7 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     p.agg = (float*)(ws + L.agg);
     p.incl = (float*)(ws + L.incl);
     p.fagg = (const float*)(fws + F.agg);
+    p.carry = (float*)(fws + F.carry);  // the forward's chunk carries (the terminal backward re-runs the chunks)
     p.loc = (float*)(fws + F.loc);
     p.lcarry = (float*)(ws + L.carry);
     {
@@ -2771,7 +2865,6 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         }
         bscan_fix_kernel<<<g.B * g.C, CST, 0, s>>>(p);
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
-        if (cudaMemsetAsync(ws + L.status, 0, sizeof(int), s) != cudaSuccess) return EWS_ERR_LAUNCH;  // the ticket
         // the exact pass with the gradient map: vector cotangents to `coef`, dM to the chunk partials
         p.coef = (float*)(ws + L.loc);
         const size_t xsmem = tc::tc_exact_smem_bytes(g.QP);
@@ -2781,12 +2874,28 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
         cudaFuncSetAttribute(xk, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
         const int xper = resident_ctas((const void*)xk, tc::NTH, xsmem);
         if (xper < 1) return EWS_ERR_UNSUPPORTED;
-        int xgrid = xper * num_sms();
-        if (xgrid > g.B * groups) xgrid = g.B * groups;
-        p.g.bwd_mode = 2;
-        xk<<<xgrid, tc::NTH, xsmem, s>>>(p);
-        if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        // prefix readout: one window of every chunk group, the states read from `out`; terminal readout: per
+        // window of op.wgrp groups, the output pass re-runs the window's chunks from the forward's carries into
+        // the scratch rows, then the exact pass reads them
+        const int wgrp = term ? op.wgrp : groups;
+        if (term) p.srows = (float*)(ws + L.srows);
+        for (int g0 = 0; g0 < groups; g0 += wgrp) {
+            p.g.grp0 = g0;
+            p.g.ngrp = std::min(wgrp, groups - g0);
+            if (term) {
+                if (cudaMemsetAsync(ws + L.status, 0, sizeof(int), s) != cudaSuccess) return EWS_ERR_LAUNCH;
+                p.g.bwd_mode = 0;
+                fwd_tc_kernel<<<std::min(op.grid, g.B * p.g.ngrp), tc::NTH, op.smem, s>>>(p);
+                if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+            }
+            if (cudaMemsetAsync(ws + L.status, 0, sizeof(int), s) != cudaSuccess) return EWS_ERR_LAUNCH;  // the ticket
+            p.g.bwd_mode = 2;
+            xk<<<std::min(xper * num_sms(), g.B * p.g.ngrp), tc::NTH, xsmem, s>>>(p);
+            if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
+        }
         p.g.bwd_mode = 0;
+        p.g.grp0 = 0;
+        p.g.ngrp = groups;
     }
     {
         const size_t tsmem = gm::table_smem_bytes(g);

@@ -246,15 +246,8 @@ class EWS(nn.Module):
         else:
             path = path.to(torch.float32)
         clock = clock.to(torch.float32)
-        needs_grad = torch.is_grad_enabled() and any(
-            t is not None and t.requires_grad for t in (path, clock, blocks, lift)
-        )
-        if kernel_readout == _lib.EWS_READOUT_TERMINAL and needs_grad:
-            # the block backward runs on the prefix stream (the terminal value is its last row)
-            out = engine.BlockScan.apply(
-                path, clock, blocks, lift, _lib.EWS_READOUT_PREFIX, flags, self._chunk, increments, self._q
-            )
-            return out[:, -1]
+        # terminal readout: the backward re-runs each chunk from the forward's saved chunk start
+        # (ews/core/kernels/pallas_combine.py:1911-2027, block_terminal_vjp), no prefix stream
         return engine.BlockScan.apply(
             path, clock, blocks, lift, kernel_readout, flags, self._chunk, increments, self._q
         )
@@ -318,12 +311,10 @@ class EWS(nn.Module):
                 path = path.to(torch.float32)
         else:
             path = path.to(torch.float32)
-        needs_grad = torch.is_grad_enabled() and any(t.requires_grad for t in (path, M, F, G, H))
-        if readout == "terminal" and not needs_grad:
-            return engine.DenseScan.apply(path, M, F, G, H, _lib.EWS_READOUT_TERMINAL, flags, self._chunk, increments)
-        # the dense backward runs on the prefix stream (the terminal value is its last row)
-        out = engine.DenseScan.apply(path, M, F, G, H, _lib.EWS_READOUT_PREFIX, flags, self._chunk, increments)
-        return out[:, -1] if readout == "terminal" else out
+        # terminal readout: the backward re-runs windows of chunks from the forward's saved chunk starts
+        # (ews/core/kernels/pallas_combine.py:1911-2027, block_terminal_vjp), no prefix stream
+        kernel_readout = _lib.EWS_READOUT_TERMINAL if readout == "terminal" else _lib.EWS_READOUT_PREFIX
+        return engine.DenseScan.apply(path, M, F, G, H, kernel_readout, flags, self._chunk, increments)
 
     def forward(
         self,

@@ -164,3 +164,56 @@ def test_gradients_chunking_general_blocks(chunk):
     out, gout = _kernel(path, clock, A, lift, "prefix", q=6, w=w, chunk=chunk)
     assert relerr(out, ref) <= 1e-5
     _assert_grads(gout, gref)
+
+
+@pytest.mark.parametrize("chunk", [1, 7, 0])
+def test_terminal_gradients_recompute_the_chunks(chunk):
+    """Terminal readout with gradients: the backward re-runs every chunk from the forward's saved chunk
+    start into per-worker scratch rows (as the reference's block_terminal_vjp, pallas_combine.py:1911-2027)
+    instead of reading a prefix stream. One-interval chunks, a ragged last chunk (60 = 7 x 8 + 4) and the
+    engine's own chunk length."""
+    _require_gpu()
+    path, clock, A, lift = _case(2, 60, 8, seed=32, rot=False, step_scale=4.0)
+    w = torch.randn((2, 1 + 8 + 64 + 512), generator=torch.Generator().manual_seed(6), dtype=torch.float64)
+    ref, gref = _oracle(path, clock, A, lift, "terminal", q=6, w=w)
+    out, gout = _kernel(path, clock, A, lift, "terminal", q=6, w=w, chunk=chunk)
+    assert relerr(out, ref) <= 1e-5
+    _assert_grads(gout, gref)
+
+
+def test_terminal_training_step_keeps_no_prefix_stream():
+    """What autograd keeps for a terminal fwd+bwd is the (B, 1 + D) terminal row, not a (B, T, 1 + D)
+    prefix stream, and the gradients equal the prefix path's (its last row's cotangent)."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import EWS, AParamBlockDiag
+
+    B, T, N = 3, 200, 8
+    W = 1 + N + N * N + N * N * N
+    path, clock, A, lift = _case(B, T, N, seed=41)
+    blocks = [torch.tensor(A[2 * k : 2 * k + 2, 2 * k : 2 * k + 2], dtype=torch.float32) for k in range(N // 2)]
+    w = torch.randn((B, W), generator=torch.Generator().manual_seed(7)).to(DEV)
+    grads = {}
+    for readout in ("terminal", "prefix"):
+        Ap = AParamBlockDiag(blocks, (2,) * (N // 2)).to(DEV)
+        layer = EWS(Ap, N=3, reweighting_mode="displacement", leaf="series", series_q=5)
+        p = torch.tensor(path, dtype=torch.float32, device=DEV, requires_grad=True)
+        ck = torch.tensor(clock, dtype=torch.float32, device=DEV, requires_grad=True)
+        Bm = torch.tensor(lift, dtype=torch.float32, device=DEV, requires_grad=True)
+        shapes = []
+
+        def pack(t):
+            shapes.append(tuple(t.shape))
+            return t
+
+        with torch.autograd.graph.saved_tensors_hooks(pack, lambda t: t):
+            out = layer(p, ck, readout=readout, lift=Bm)
+        last = out if readout == "terminal" else out[:, -1]
+        (last * w).sum().backward()
+        torch.cuda.synchronize()
+        if readout == "terminal":
+            assert (B, T, W) not in shapes, shapes
+        gA = torch.block_diag(*[b.grad for b in Ap.blocks])
+        grads[readout] = (p.grad, ck.grad, gA, Bm.grad)
+    for name, a, b in zip(("path", "clock", "A", "lift"), grads["terminal"], grads["prefix"]):
+        e = relerr(a.double().cpu(), b.double().cpu())
+        assert e <= 1e-5, f"d/d{name}: terminal vs prefix relerr {e:.2e}"

@@ -136,16 +136,20 @@ def test_identity_lift():
     _assert_fwd(out, ref)
 
 
-def test_config2_full_length():
+@pytest.mark.parametrize("readout", ["prefix", "terminal"])
+def test_config2_full_length(readout):
     """BASELINE config 2 at full length (T = 17984, N = 32, d = 7, q from the bound), batch reduced to 2
-    for the oracle's memory; forward and gradients."""
+    for the oracle's memory; forward and gradients (terminal: the backward re-runs the chunks from the
+    forward's carries instead of reading a prefix stream)."""
     _require_gpu()
     from exponentially_weighted_signature_b200 import workloads
 
     case = workloads.config2(B=2)
     path, clock, A, lift = (_f32(case[k]) for k in ("path", "clock", "A", "lift"))
-    args = (path, clock, A, lift, "prefix", 4)
-    w = torch.tensor(np.random.default_rng(3).normal(size=(2, path.shape[1] - 1, 1 + 32 + 32 * 32)))
+    args = (path, clock, A, lift, readout, 4)
+    T = path.shape[1] - 1
+    shape = (2, T, 1 + 32 + 32 * 32) if readout == "prefix" else (2, 1 + 32 + 32 * 32)
+    w = torch.tensor(np.random.default_rng(3).normal(size=shape))
     ref, g64 = _oracle(*args, w=w)
     ref32, g32 = _oracle(*args, w=w, dtype=torch.float32)
     out, gk = _kernel(*args, w=w)
@@ -331,3 +335,54 @@ def test_jordan_closed_range_guard_raises_on_the_next_call():
         for slot in engine._GUARD.values():
             slot[0].zero_()
             slot[1].zero_()
+
+
+@pytest.mark.parametrize("B,T,N,chunk", [(2, 2000, 8, 1), (3, 75, 32, 7), (2, 130, 5, 0)])
+def test_terminal_gradients_in_windows(B, T, N, chunk):
+    """Terminal readout with gradients: the backward re-runs windows of chunk groups from the forward's carries
+    (the output pass into scratch rows, then the exact pass on them), as the reference's block_terminal_vjp
+    (pallas_combine.py:1911-2027) recomputes each chunk from its saved start. 2000 one-interval chunks make
+    several windows (the window holds one output-pass grid of tiles); a ragged last chunk; a padded state."""
+    _require_gpu()
+    path, clock, A, lift = _case(B, T, N, d_in=4, seed=60 + N)
+    w = torch.tensor(np.random.default_rng(8).normal(size=(B, 1 + N + N * N)))
+    ref, (gp_r, ga_r, gb_r) = _oracle(path, clock, A, lift, "terminal", 4, w=w)
+    out, (gp_n, ga_n, gb_n) = _kernel(path, clock, A, lift, "terminal", 4, w=w, chunk=chunk)
+    _assert_close("forward", out, ref)
+    for name, a, b in [("path", gp_n, gp_r), ("A", ga_n, ga_r), ("lift", gb_n, gb_r)]:
+        _assert_close(f"{name} grad", a, b)
+
+
+def test_terminal_training_step_keeps_no_prefix_stream():
+    """What autograd keeps for a terminal fwd+bwd is the (B, 1 + D) terminal row, not a (B, T, 1 + D) prefix
+    stream, and the gradients equal the prefix path's with the cotangent on its last row."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import EWS, AParamGeneral
+
+    B, T, N, d_in = 2, 300, 32, 7
+    W = 1 + N + N * N
+    path, clock, A, lift = _case(B, T, N, d_in=d_in, seed=9)
+    w = torch.tensor(np.random.default_rng(9).normal(size=(B, W)), dtype=torch.float32, device=DEV)
+    grads = {}
+    for readout in ("terminal", "prefix"):
+        Ap = AParamGeneral(torch.tensor(A, dtype=torch.float32)).to(DEV)
+        layer = EWS(Ap, N=2, reweighting_mode="displacement_uniform", leaf="series", series_q=4)
+        p = torch.tensor(path, dtype=torch.float32, device=DEV, requires_grad=True)
+        Bm = torch.tensor(lift, dtype=torch.float32, device=DEV, requires_grad=True)
+        shapes = []
+
+        def pack(t):
+            shapes.append(tuple(t.shape))
+            return t
+
+        with torch.autograd.graph.saved_tensors_hooks(pack, lambda t: t):
+            out = layer(p, torch.tensor(clock, dtype=torch.float32, device=DEV), readout=readout, lift=Bm)
+        last = out if readout == "terminal" else out[:, -1]
+        (last * w).sum().backward()
+        torch.cuda.synchronize()
+        if readout == "terminal":
+            assert (B, T, W) not in shapes, shapes
+        grads[readout] = (p.grad, Ap.matrix.grad, Bm.grad)
+    for name, a, b in zip(("path", "A", "lift"), grads["terminal"], grads["prefix"]):
+        e = relerr(a.double().cpu(), b.double().cpu())
+        assert e <= 1e-5, f"d/d{name}: terminal vs prefix relerr {e:.2e}"
