@@ -61,7 +61,7 @@ def _peaks():
 # ------------------------------------------------------------------------------------ workloads
 
 
-def _diag_setup(cfg, rank, world, device, precision, batch=None):
+def _diag_setup(cfg, rank, world, device, precision, batch=None, readout=None):
     """Per-rank inputs and model of a diagonal-engine configuration (config1, config5)."""
     from exponentially_weighted_signature_b200 import EWS, LogEWS, AParamDiag, B as Lift, workloads, series
     from exponentially_weighted_signature_b200.parallel import shard_range
@@ -125,7 +125,7 @@ def _diag_setup(cfg, rank, world, device, precision, batch=None):
                 ws_bytes=ws_bytes, units=Bl * T, case=case)
 
 
-def _dense_setup(cfg, rank, world, device, precision, batch=None):
+def _dense_setup(cfg, rank, world, device, precision, batch=None, readout="prefix"):
     """Per-rank inputs and model of the dense-A configuration (config2)."""
     from exponentially_weighted_signature_b200 import EWS, AParamGeneral, B as Lift, workloads, series
     from exponentially_weighted_signature_b200.parallel import shard_range
@@ -150,26 +150,26 @@ def _dense_setup(cfg, rank, world, device, precision, batch=None):
     Bl = s1 - s0
     D = N + N * N
     g = torch.Generator(device="cpu").manual_seed(1234 + rank)
-    w = torch.randn((Bl, T, 1 + D), generator=g).to(device)
+    w = torch.randn((Bl, T, 1 + D) if readout == "prefix" else (Bl, 1 + D), generator=g).to(device)
 
     def step(x, clock):
-        out = layer(x, clock, readout="prefix", lift=lift.full_matrix())
+        out = layer(x, clock, readout=readout, lift=lift.full_matrix())
         loss = torch.dot(out.reshape(-1), w.detach().reshape(-1))  # <out, w>: one read of out
         out.backward(w)  # d<out, w>/d out = w: the loss's backward without materialising w * 1 again
         return loss
 
     d_in = x_host.shape[-1]
-    out_row = 4 * (1 + D)
+    out_row = 4 * (1 + D) if readout == "prefix" else 0
     # the dense path is tensor-core bound: algorithmic GEMM flops per unit (one sample-interval) are the
     # two N x N x N flow products of the forward and the four of the backward, 2 N^3 flops each
     alg = {"ews_dense_fwd": 2 * 2 * N**3, "ews_dense_bwd": 4 * 2 * N**3}
-    meta = dict(bound="tensor", B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout="prefix", dtype="f32", precision="f32")
+    meta = dict(bound="tensor", B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout=readout, dtype="f32", precision="f32")
     ws_bytes = x_host.numel() * 4 + Bl * T * out_row
     return dict(step=step, params=params, x_host=x_host, clock_host=clock_host, alg=alg, meta=meta,
                 ws_bytes=ws_bytes, units=Bl * T, case=case)
 
 
-def _block_setup(cfg, rank, world, device, precision, batch=None):
+def _block_setup(cfg, rank, world, device, precision, batch=None, readout="prefix"):
     """Per-rank inputs and model of the 2x2-block, depth-3 configuration (config3)."""
     from exponentially_weighted_signature_b200 import EWS, AParamBlockDiag, B as Lift, workloads, series
     from exponentially_weighted_signature_b200.parallel import shard_range
@@ -194,28 +194,28 @@ def _block_setup(cfg, rank, world, device, precision, batch=None):
     Bl = s1 - s0
     D = N + N * N + N * N * N
     g = torch.Generator(device="cpu").manual_seed(1234 + rank)
-    w = torch.randn((Bl, T, 1 + D), generator=g).to(device)
+    w = torch.randn((Bl, T, 1 + D) if readout == "prefix" else (Bl, 1 + D), generator=g).to(device)
 
     def step(x, clock):
         clock = clock.detach().requires_grad_(True)  # the input-dependent clock: d/dtheta flows back
-        out = layer(x, clock, readout="prefix", lift=lift.full_matrix())
+        out = layer(x, clock, readout=readout, lift=lift.full_matrix())
         loss = torch.dot(out.reshape(-1), w.detach().reshape(-1))  # <out, w>: one read of out
         out.backward(w)  # d<out, w>/d out = w: the loss's backward without materialising w * 1 again
         return loss
 
     d_in = x_host.shape[-1]
-    out_row = 4 * (1 + D)
+    out_row = 4 * (1 + D) if readout == "prefix" else 0
     # algorithmic bytes per unit: increments and clock step in, prefix row out; the backward reads the
     # output gradient and writes the increment and clock-step gradients
     alg = {"ews_block_fwd": 4 * d_in + 4 + out_row, "ews_block_bwd": out_row + 4 * d_in + 4 + 4 * d_in + 4}
-    meta = dict(B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout="prefix", dtype="f32",
+    meta = dict(B_global=Bg, B_local=Bl, T=T, N=N, scaling=scaling, q=q, readout=readout, dtype="f32",
                 precision="f32", depth=3)
     ws_bytes = x_host.numel() * 4 + Bl * T * out_row
     return dict(step=step, params=params, x_host=x_host, clock_host=clock_host, alg=alg, meta=meta,
                 ws_bytes=ws_bytes, units=Bl * T, case=case)
 
 
-def _stacked_setup(cfg, rank, world, device, precision, batch=None):
+def _stacked_setup(cfg, rank, world, device, precision, batch=None, readout=None):
     """Per-rank inputs and model of the StackedEWS training step (config4): 4 pre-norm EWSBlocks (hidden
     128, lift 128 -> 16, depth 2, diagonal A = diag(e^u), u ~ U(-3, 1), token-gated learned clock), a
     Linear encoder 21 -> 128, a per-position head 128 -> 21, MSE, Adam; the gradients of every parameter
@@ -433,7 +433,9 @@ def run_b200(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     setup_fn = {"config2": _dense_setup, "config3": _block_setup, "config4": _stacked_setup}.get(args.config, _diag_setup)
-    setup = setup_fn(args.config, rank, world, device, args.precision, args.batch)
+    if args.readout == "terminal" and args.config not in ("config2", "config3"):
+        raise SystemExit("--readout terminal applies to config2 and config3")
+    setup = setup_fn(args.config, rank, world, device, args.precision, args.batch, args.readout)
     step, params = setup["step"], setup["params"]
     x = setup["x_host"].to(device)
     clock = setup["clock_host"].to(device)
@@ -612,7 +614,8 @@ def run_b200(args, rank, world, local_rank):
         "dtype": meta["dtype"],
         "data": "synthetic (seeded, BASELINE.json shapes and distributions)",
         "config": {
-            "workload": args.config + (f" (batch {args.batch})" if args.batch else ""),
+            "workload": args.config + (f" (batch {args.batch})" if args.batch else "")
+            + (" (terminal readout)" if args.readout == "terminal" else ""),
             "global_batch": meta["B_global"],
             "seq_len": meta["T"],
             "state_dim": meta["N"],
@@ -692,6 +695,8 @@ def main():
     ap.add_argument("--precision", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling on a smaller case)")
+    ap.add_argument("--readout", default="prefix", choices=["prefix", "terminal"],
+                    help="config2 / config3: the layer's readout (terminal: the loss on the final row only)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time the eager step instead of its CUDA-graph replay")
     args = ap.parse_args()

@@ -1651,6 +1651,17 @@ __global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
             const int c = grp * TILES + t;
             if (c < g.C) steps = max(steps, min(g.Lc, g.T - c * g.Lc));
         }
+        if (g.readout == EWS_READOUT_TERMINAL && grp != groups - 1) {
+            // terminal readout: only the sequence's last chunk has a cotangent, every other chunk's local
+            // adjoint is zero
+            if (valid_me) {
+                float* as = p.agg + ((size_t)b * g.C + c_me) * g.SW;
+#pragma unroll
+                for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = 0.f;
+                as[MM + lane] = 0.f;
+            }
+            continue;
+        }
         auto fetch_s1 = [&](int k) { fetch_loc(p, b, t0_me + k, vt + 2 * NP + (k & 1) * NP, NP); };
         tc_load_tables(p, s, b, true);
         __syncthreads();
