@@ -246,6 +246,10 @@ typedef struct ews_block_args {
 
 int ews_block_workspace_size(const ews_block_args* a, size_t* fwd_bytes, size_t* bwd_bytes);
 int ews_block_fwd(const ews_block_args* a, ews_stream_t stream);
+/* Terminal readout: grad_out is the (B, 1 + ...) terminal row's cotangent; the states are recomputed
+ * from the forward workspace's chunk carries (ews/core/kernels/pallas_combine.py:1911-2027,
+ * block_terminal_vjp), into rows of the backward workspace sized by ews_block_workspace_size for the
+ * same readout. The same holds for ews_dense_bwd. */
 int ews_block_bwd(const ews_block_args* a, ews_stream_t stream);
 
 /* ---- flow tables of the dense engine ---------------------------------------------------------------
