@@ -13,7 +13,7 @@
 // I - M^j (powers_kernel), every chunk's zero-carry aggregate as a parallel map (agg_kernel), the carries by
 // a two-level scan over the chunks (scan_local, log-depth rounds over the groups, scan_fix), then the output
 // pass on tcgen05 (fwd_tc_kernel: four chunks of a sample stacked into M = 128, two 3xTF32 products per
-// step). Backward: the zero-carry adjoint pass (bwd_tc_kernel), the reverse scan of the local adjoints
+// step). Backward: every chunk's zero-carry adjoint as power sums (bagg_kernel), the reverse scan of the local adjoints
 // (bscan_*), the exact adjoint pass with the gradient map fused in (bwd_exact_kernel), the table gradients
 // (table_grad_*) and a fixed-order reduction. No kernel waits on another CTA.
 //
@@ -39,7 +39,7 @@ struct Geom {
     int spin_limit;
     int ntiles;
     int agg_pre;      // forward: the chunk aggregates come from agg_kernel (the chain runs the output pass only)
-    int bwd_mode;     // backward chain: 1 = the zero-carry pass only (local adjoints), 2 = the exact pass only
+    int bwd_mode;     // backward: 2 while the exact pass runs (0 otherwise)
     int tab_n;        // floats of the F, G, H tables (N x d_in each, padded to NP rows)
     int grp0, ngrp;   // the chunk groups (TILES chunks each) that fwd_tc_kernel and bwd_exact_kernel cover
 };
@@ -1195,6 +1195,217 @@ static int launch_agg_q(const Params& p, cudaStream_t s) {
     return EWS_ERR_UNSUPPORTED;
 }
 
+// ---------------------------------------------------------------------------------- backward chunk aggregates
+
+constexpr int BGW = 4;   // warps per CTA of bagg_kernel
+constexpr int BES = 40;  // row stride of a staged power complement: B and transposed-A fragment reads conflict-free
+constexpr int BGS = 36;  // row stride of a staged gradient tile: A fragment and float4 row reads conflict-free
+constexpr int BHS = 40;  // row stride of the staged H = G M^(j+1): B fragment reads conflict-free
+__host__ __device__ inline int bagg_warp_floats() { return 2 * NP * BES + 2 * NP * BGS + NP * BHS + 6 * NP; }
+
+// The zero-carry local adjoints (mu1, mu2) of every chunk without a chain. Run from zero over a chunk, the
+// reverse recursion l2 <- M^T l2 M + G_j, l1 <- M^T (l1 + l2 s1_j) + g1_j telescopes into the flow powers
+// P_j = M^(j+1) = I - E_(j+1) (j the interval's index in its chunk, E the forward's power complements):
+//     mu2 = sum_j P_j^T G_j P_j,      mu1 = sum_j P_j^T (g1_j + G_j s^_j),
+// with s^_j = M s^_(j-1) + s1_j the chunk's level 1 from a zero start. Every term is independent: per interval
+// two 32 x 32 x 32 products on the tensor core (3xTF32 mma.sync), H = G - G E and mu2 += H - E^T H (each
+// through a zeroed accumulator, added on the CUDA cores), and mu1 += w - E^T w with w = g1 + G s^. One warp
+// per chunk; the next interval's E, G, s1 and g1 are copied in (cp.async) while this one's products run.
+__global__ void __launch_bounds__(BGW * 32, 2) bagg_kernel(Params p) {
+    extern __shared__ __align__(16) float bgsm[];
+    const Geom& g = p.g;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int chunk = blockIdx.x * BGW + warp;
+    if (chunk >= g.B * g.C) return;
+    const int b = chunk / g.C, c = chunk - b * g.C;
+    const int N = g.N, Lc = g.Lc;
+    const int t0 = c * Lc, len = min(Lc, g.T - t0);
+    float* as = p.agg + ((size_t)b * g.C + c) * g.SW;
+    if (g.readout == EWS_READOUT_TERMINAL && c != g.C - 1) {
+        // terminal readout: only the sequence's last chunk has a cotangent
+#pragma unroll 4
+        for (int n = 0; n < NP; ++n) as[MM + NP + n * NP + lane] = 0.f;
+        as[MM + lane] = 0.f;
+        return;
+    }
+    const int gq = lane >> 2, cq = lane & 3;  // fragment coordinates
+    float* Eb = bgsm + (size_t)warp * bagg_warp_floats();  // 2 x NP x BES: E_(j+1)
+    float* Gb = Eb + 2 * NP * BES;                          // 2 x NP x BGS: G_j (zero beyond N)
+    float* Hs = Gb + 2 * NP * BGS;                          // NP x BHS
+    float* Vb = Hs + NP * BHS;                              // 2 x [s1_j | g1_j]
+    float* sh = Vb + 4 * NP;                                // s^ (broadcast copy)
+    float* wv = sh + NP;                                    // w (broadcast copy)
+    for (int e = lane; e < 2 * NP * BGS; e += 32) Gb[e] = 0.f;
+    for (int e = lane; e < 6 * NP; e += 32) Vb[e] = 0.f;
+    float drow[NP];
+    {
+        const float* d = p.tab_d + (size_t)b * N * N;
+#pragma unroll
+        for (int k = 0; k < NP; ++k) drow[k] = (lane < N && k < N) ? d[lane * N + k] : 0.f;
+    }
+    float m2[2][4][4];  // mu2 in accumulator-fragment order: [m tile][n tile][value]
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) m2[mt][nt][v] = 0.f;
+    float m1 = 0.f, shat = 0.f;  // mu1[lane], s^[lane]
+    __syncwarp();
+    const float* Ebase = p.pows + (size_t)b * (Lc + 1) * MM;
+    const int LW = loc_width(g.QP);
+    auto fetch = [&](int k) {
+        float* eb = Eb + (k & 1) * NP * BES;
+        const float* src = Ebase + (size_t)(k + 1) * MM;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const int e = lane + 32 * v;  // 16-byte piece e: row e / 8, column 4 (e % 8)
+            cp_async16(eb + (e >> 3) * BES + 4 * (e & 7), src + 4 * e);
+        }
+        float* vb = Vb + (k & 1) * 2 * NP;
+        if (lane < 8) cp_async16(vb + 4 * lane, p.loc + ((size_t)b * g.T + t0 + k) * LW + 4 * lane);
+        float* gb = Gb + (k & 1) * NP * BGS;
+        const float* gr = grad_row(p, b, t0 + k);
+        if (lane < N) {
+            if (gr) {
+                cp_async4(vb + NP + lane, gr + 1 + lane);
+                for (int i = 0; i < N; ++i) cp_async4(gb + i * BGS + lane, gr + 1 + N + i * N + lane);
+            } else {
+                vb[NP + lane] = 0.f;
+                for (int i = 0; i < N; ++i) gb[i * BGS + lane] = 0.f;
+            }
+        }
+        cp_async_commit();
+    };
+    fetch(0);
+    for (int k = 0; k < len; ++k) {
+        cp_async_wait<0>();
+        __syncwarp();
+        const float* E = Eb + (k & 1) * NP * BES;
+        const float* G = Gb + (k & 1) * NP * BGS;
+        const float* vb = Vb + (k & 1) * 2 * NP;
+        if (k + 1 < len) fetch(k + 1);
+        // s^ <- s^ - D s^ + s1_j
+        float du0 = 0.f, du1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < NP; q += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(sh + q);
+            du0 = fmaf(drow[q], v.x, du0);
+            du1 = fmaf(drow[q + 1], v.y, du1);
+            du0 = fmaf(drow[q + 2], v.z, du0);
+            du1 = fmaf(drow[q + 3], v.w, du1);
+        }
+        shat = (shat - (du0 + du1)) + vb[lane];
+        __syncwarp();
+        sh[lane] = shat;
+        __syncwarp();
+        // w = g1 + G s^ (row `lane` of G)
+        float w0 = vb[NP + lane], w1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < NP; q += 4) {
+            const float4 gv = *reinterpret_cast<const float4*>(G + lane * BGS + q);
+            const float4 sv = *reinterpret_cast<const float4*>(sh + q);
+            w0 = fmaf(gv.x, sv.x, w0);
+            w1 = fmaf(gv.y, sv.y, w1);
+            w0 = fmaf(gv.z, sv.z, w0);
+            w1 = fmaf(gv.w, sv.w, w1);
+        }
+        const float w = w0 + w1;
+        wv[lane] = w;
+        // GE = G E (A = G row-major, B[k][n] = E[k][n]); H = G - GE at the accumulator positions
+        float h[2][4][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int v = 0; v < 4; ++v) h[mt][nt][v] = 0.f;
+#pragma unroll
+        for (int sk = 0; sk < 4; ++sk) {
+            float af[2][4], bf[4][2];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const float* gr = G + (16 * mt + gq) * BGS + 8 * sk + cq;
+                af[mt][0] = gr[0];
+                af[mt][1] = gr[8 * BGS];
+                af[mt][2] = gr[4];
+                af[mt][3] = gr[8 * BGS + 4];
+            }
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                const float* er = E + (8 * sk + cq) * BES + 8 * nt + gq;
+                bf[nt][0] = er[0];
+                bf[nt][1] = er[4 * BES];
+            }
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) mma3_m16n8k8(h[mt][nt], af[mt], bf[nt]);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    const int i = 16 * mt + gq + 8 * (v >> 1), n = 8 * nt + 2 * cq + (v & 1);
+                    h[mt][nt][v] = G[i * BGS + n] - h[mt][nt][v];
+                    Hs[i * BHS + n] = h[mt][nt][v];
+                }
+        __syncwarp();
+        // E^T H (A[i][k] = E[k][i], B[k][n] = H[k][n]); mu2 += H - E^T H
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+            float tt[4][4];
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int v = 0; v < 4; ++v) tt[nt][v] = 0.f;
+#pragma unroll
+            for (int sk = 0; sk < 4; ++sk) {
+                float af[4], bf[4][2];
+                const float* ec = E + (8 * sk + cq) * BES + 16 * mt + gq;
+                af[0] = ec[0];
+                af[1] = ec[8];
+                af[2] = ec[4 * BES];
+                af[3] = ec[4 * BES + 8];
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+                    const float* hr = Hs + (8 * sk + cq) * BHS + 8 * nt + gq;
+                    bf[nt][0] = hr[0];
+                    bf[nt][1] = hr[4 * BHS];
+                }
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) mma3_m16n8k8(tt[nt], af, bf[nt]);
+            }
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int v = 0; v < 4; ++v) m2[mt][nt][v] += h[mt][nt][v] - tt[nt][v];
+        }
+        // mu1 += w - E^T w
+        float tw0 = 0.f, tw1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < NP; q += 2) {
+            tw0 = fmaf(E[q * BES + lane], wv[q], tw0);
+            tw1 = fmaf(E[(q + 1) * BES + lane], wv[q + 1], tw1);
+        }
+        m1 += w - (tw0 + tw1);
+        __syncwarp();  // H, w and this interval's buffers are read before the next interval writes them
+    }
+    cp_async_wait<0>();
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int i = 16 * mt + gq + 8 * (v >> 1), n = 8 * nt + 2 * cq + (v & 1);
+                as[MM + NP + i * NP + n] = m2[mt][nt][v];
+            }
+    as[MM + lane] = m1;
+}
+
 // ---------------------------------------------------------------------------------- 256-thread products
 // The scans' Chen products and transposed Chen maps with 256 threads (a 2 x 2 block each) instead of the
 // look-back's 64: the scans are sequential chains of these products, so their latency is the scans' cost.
@@ -1556,41 +1767,12 @@ __global__ void __launch_bounds__(CST) bscan_fix_kernel(Params p) {
 // The adjoint chain. With l~_t = l_t + g_t (the cotangent of S_t after adding row t of the output
 // gradient) the reverse recursion of one interval is
 //     l~2_{t-1} = M^T l~2_t M + g2_{t-1},      l~1_{t-1} = M^T (l~1_t + l~2_t s1_t) + g1_{t-1},
-// the forward's M S M^T with D replaced by D^T: the same two tcgen05 products per step (B operand D^T),
-// four chunks of one sample stacked into M = 128. Chunks run in reverse: this zero-carry pass leaves each
-// chunk's local adjoint mu in `agg`, the reverse scan (bscan_*) turns those into the cotangent arriving at
-// every chunk's end (`lcarry`), and the exact pass (bwd_exact_kernel) runs every chunk again from its carry
-// with the gradient map fused in; table_grad_kernel forms the table gradients and dx.
-//
-// Shared memory holds the operands, the transposition buffers, D row-major and per tile l1 | v | s1 of two
-// intervals (64 KB, three CTAs per SM). The gradient rows are not staged: each lane loads its column of the
-// next interval's g2 (coalesced, one 4-byte word per row of the warp) while the second product runs, after
-// an L2 prefetch one interval earlier, and adds it in the epilogue.
+// the forward's M S M^T with D replaced by D^T. Each chunk's local adjoint mu (the recursion from zero over
+// the chunk) comes from bagg_kernel's power sums, the reverse scan (bscan_*) turns those into the cotangent
+// arriving at every chunk's end (`lcarry`), and the exact pass (bwd_exact_kernel) runs every chunk again from
+// its carry with the gradient map fused in: two tcgen05 products per step (B operand D^T), four chunks of
+// one sample stacked into M = 128; table_grad_kernel forms the table gradients and dx.
 namespace tc {
-constexpr int BVEC = 4 * NP;  // per tile: l1 | v | s1 of two intervals
-
-__host__ __device__ inline size_t tc_bwd_smem_bytes() {
-    const size_t f = 2 * MM + 2 * 4 * MM + TILES * 32 * RQS + MM + TILES * BVEC;
-    return f * sizeof(float) + 64 + 128;  // + barrier / tmem slot / broadcast, + alignment slack
-}
-
-__device__ TcSmem tc_carve_bwd(unsigned char* raw) {
-    uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 127) & ~(uintptr_t)127;
-    float* p = reinterpret_cast<float*>(base);
-    TcSmem s{};
-    s.Bhi = p; p += MM;
-    s.Blo = p; p += MM;
-    s.Ahi = p; p += 4 * MM;
-    s.Alo = p; p += 4 * MM;
-    s.RQ = p; p += TILES * 32 * RQS;
-    s.Dr = p; p += MM;
-    s.vec = p; p += TILES * BVEC;
-    s.bar = reinterpret_cast<uint64_t*>(p);
-    s.tmem = reinterpret_cast<uint32_t*>(p + 2);
-    s.bcast = reinterpret_cast<int*>(p + 4);
-    return s;
-}
-
 // The cache lines of one output-gradient row (W floats) into L2, spread over the warp's lanes.
 __device__ __forceinline__ void prefetch_row_l2(const float* row, int W) {
     const uintptr_t a0 = reinterpret_cast<uintptr_t>(row) & ~(uintptr_t)127;
@@ -1599,223 +1781,6 @@ __device__ __forceinline__ void prefetch_row_l2(const float* row, int W) {
         asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
 }
 }  // namespace tc
-
-__global__ void __launch_bounds__(tc::NTH, 3) bwd_tc_kernel(Params p) {
-    using namespace tc;
-    extern __shared__ unsigned char smem_raw[];
-    const Geom& g = p.g;
-    TcSmem s = tc_carve_bwd(smem_raw);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int N = g.N;
-    const int mbar_limit = 1 << 20;
-
-    if (tid == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(s.bar)), "r"(1));
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s.tmem)),
-                     "r"(64));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    fence_before();
-    __syncthreads();
-    fence_after();
-    const uint32_t tmem = *s.tmem;
-    const uint32_t tP1 = tmem, tP2 = tmem + 32;
-    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
-    uint32_t phase = 0;
-    bool failed = false;
-    bool mma_pending = false;  // an MMA commit of `phase` may still be outstanding after a failed wait
-
-    const uint64_t dA_hi = smem_desc(smem_u32(s.Ahi), 2048, 128), dA_lo = smem_desc(smem_u32(s.Alo), 2048, 128);
-    const uint64_t dB_hi = smem_desc(smem_u32(s.Bhi), 512, 128), dB_lo = smem_desc(smem_u32(s.Blo), 512, 128);
-    const int groups = (g.C + TILES - 1) / TILES;
-    const int ntiles = g.B * groups;
-    float* vt = s.vec + warp * BVEC;  // l1 (NP) | v (NP) | s1 of two intervals (NP each)
-    float* RQt = s.RQ + warp * 32 * RQS;
-
-    for (;;) {
-        if (tid == 0) s.bcast[0] = atomicAdd(&p.st->ticket, 1);
-        __syncthreads();
-        const int tile = s.bcast[0];
-        __syncthreads();
-        if (tile >= ntiles) break;
-        const int grp = tile / g.B, b = tile - grp * g.B;
-        const int c_me = grp * TILES + warp;
-        const bool valid_me = c_me < g.C;
-        const int t0_me = c_me * g.Lc;
-        const int len_me = valid_me ? min(g.Lc, g.T - t0_me) : 0;
-        int steps = 0;
-        for (int t = 0; t < TILES; ++t) {
-            const int c = grp * TILES + t;
-            if (c < g.C) steps = max(steps, min(g.Lc, g.T - c * g.Lc));
-        }
-        if (g.readout == EWS_READOUT_TERMINAL && grp != groups - 1) {
-            // terminal readout: only the sequence's last chunk has a cotangent, every other chunk's local
-            // adjoint is zero
-            if (valid_me) {
-                float* as = p.agg + ((size_t)b * g.C + c_me) * g.SW;
-#pragma unroll
-                for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = 0.f;
-                as[MM + lane] = 0.f;
-            }
-            continue;
-        }
-        auto fetch_s1 = [&](int k) { fetch_loc(p, b, t0_me + k, vt + 2 * NP + (k & 1) * NP, NP); };
-        tc_load_tables(p, s, b, true);
-        __syncthreads();
-
-        // zero carry: the chunk's local adjoint
-        float col[32];  // column `lane` of l~2
-#pragma unroll
-        for (int n = 0; n < 32; ++n) col[n] = 0.f;
-        vt[lane] = 0.f;
-        // Steps run in reverse; a chunk shorter than the tile's longest one (only the sequence's last, whose
-        // carry is zero) idles on zero state until its last interval, k = len_me - 1. The gradient of the
-        // interval a step starts from is added before it: here for the first step, else in the epilogue of
-        // the step before.
-        if (len_me == steps && len_me > 0) {
-            const float* gr = grad_row(p, b, t0_me + len_me - 1);
-            if (lane < N && gr) {
-#pragma unroll
-                for (int n = 0; n < 32; ++n)
-                    if (n < N) col[n] += __ldg(gr + 1 + N + n * N + lane);
-                vt[lane] += __ldg(gr + 1 + lane);
-            }
-            fetch_s1(len_me - 1);
-            const float* gp = len_me >= 2 ? grad_row(p, b, t0_me + len_me - 2) : nullptr;
-            if (gp) prefetch_row_l2(gp, g.W);
-        }
-        cp_async_commit();
-        __syncwarp();
-        for (int k = steps - 1; k >= 0; --k) {
-            const bool live = k < len_me;
-            const bool next = k >= 1 && k - 1 < len_me;  // the step after this one is live
-            cp_async_wait<0>();
-            __syncwarp();
-            if (next) fetch_s1(k - 1);
-            cp_async_commit();
-            if (k >= 2 && k - 2 < len_me) {
-                const float* gp = grad_row(p, b, t0_me + k - 2);
-                if (gp) prefetch_row_l2(gp, g.W);
-            }
-            // the next interval's gradient: loads in flight for the whole step, added in the epilogue
-            float gn[32];
-            float gn1 = 0.f;
-            {
-                const float* gr = next ? grad_row(p, b, t0_me + k - 1) : nullptr;
-                const bool ld = gr && lane < N;
-#pragma unroll
-                for (int n = 0; n < 32; ++n) gn[n] = (ld && n < N) ? __ldg(gr + 1 + N + n * N + lane) : 0.f;
-                if (ld) gn1 = __ldg(gr + 1 + lane);
-            }
-            // E0: rows of l~2 -> A operand
-            float srow[32];
-#pragma unroll
-            for (int n = 0; n < 32; ++n) RQt[n * RQS + lane] = col[n];
-            __syncwarp();
-#pragma unroll
-            for (int n = 0; n < 32; ++n) srow[n] = RQt[lane * RQS + n];
-            __syncwarp();
-            store_a_row(s.Ahi, s.Alo, 32 * warp + lane, srow);
-            fence_proxy_async();
-            fence_before();
-            __syncthreads();
-            if (tid == 0) {
-                fence_after();
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP1, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
-                mma_commit(s.bar);
-            }
-            // v = l~1 + l~2 s1_t (row `lane` of l~2 against this interval's s1; idle steps add nothing)
-            {
-                const float w = dot32_bc(srow, vt + 2 * NP + (k & 1) * NP);
-                vt[NP + lane] = vt[lane] + (live ? w : 0.f);
-                __syncwarp();
-            }
-            if (!tc_wait(s, phase, mbar_limit)) {
-                failed = mma_pending = true;
-                break;
-            }
-            phase ^= 1;
-            // E1: row `lane` of X = l~2 - l~2 D = l~2 M -> column `lane` -> A operand row of X^T (the column
-            // stays in the exchange buffer for the epilogue)
-            {
-                float pr[32], xcol[32];
-                tmem_ld32(tP1 + lane_off, pr);
-#pragma unroll
-                for (int n = 0; n < 32; ++n) RQt[lane * RQS + n] = srow[n] - pr[n];
-                __syncwarp();
-#pragma unroll
-                for (int n = 0; n < 32; ++n) xcol[n] = RQt[n * RQS + lane];
-                __syncwarp();
-                store_a_row(s.Ahi, s.Alo, 32 * warp + lane, xcol);
-            }
-            fence_proxy_async();
-            fence_before();
-            __syncthreads();
-            if (tid == 0) {
-                fence_after();
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), ks > 0);
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_hi + (ks * 4096 >> 4), dB_lo + (ks * 1024 >> 4), 1);
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) mma_tf32(tP2, dA_lo + (ks * 4096 >> 4), dB_hi + (ks * 1024 >> 4), 1);
-                mma_commit(s.bar);
-            }
-            // l1 <- M^T v + g1 = v - D^T v + g1
-            {
-                const float* v = vt + NP;
-                const float nv = v[lane] - coldot_bc(s.Dr, v, lane);
-                __syncwarp();
-                vt[lane] = nv + gn1;
-                __syncwarp();
-            }
-            if (!tc_wait(s, phase, mbar_limit)) {
-                failed = mma_pending = true;
-                break;
-            }
-            phase ^= 1;
-            // E2: column `lane` of M^T X = X - D^T X, plus the next interval's gradient
-            {
-                float q2[32];
-                tmem_ld32(tP2 + lane_off, q2);
-#pragma unroll
-                for (int n = 0; n < 32; ++n) col[n] = (RQt[n * RQS + lane] + gn[n]) - q2[n];
-                fence_before();
-                __syncwarp();
-            }
-        }
-        cp_async_wait<0>();
-        if (failed) break;
-        __syncthreads();
-        // the local adjoints mu of the 4 chunks -> `agg` (the backward scan combines them)
-        if (valid_me) {
-            float* as = p.agg + ((size_t)b * g.C + c_me) * g.SW;
-#pragma unroll
-            for (int n = 0; n < 32; ++n) as[MM + NP + n * NP + lane] = col[n];
-            as[MM + lane] = vt[lane];
-        }
-        __syncthreads();
-    }
-    // every exit drains the tensor core and frees TMEM
-    if (failed && tid == 0) {
-        if (atomicCAS(&p.st->error, 0, EWS_ERR_LOOKBACK_TIMEOUT) == 0) p.st->err_tile = -1;
-        if (mma_pending)
-            for (int it = 0; it < (1 << 20); ++it)
-                if (mbar_try(s.bar, phase)) break;
-    }
-    fence_before();
-    __syncthreads();
-    fence_after();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64));
-}
 
 // The exact pass of the adjoint chain with the gradient map fused in (bwd_mode 2). Per step, besides the
 // chain's products P = l~2 M (row `lane` in TMEM after the first product) and M^T X, a third product gives
@@ -2706,7 +2671,7 @@ extern "C" int ews_dense_launches(const ews_dense_args* a, int* fwd_launches, in
     int rounds = 1;  // the group scans' rounds
     while ((1 << rounds) < scan_groups(g.C)) ++rounds;
     // forward: power, local, powers, agg, scan_local, rounds, scan_fix [, fwd_tc for the prefix readout];
-    // backward: bwd_tc, bscan_local, rounds, bscan_fix, bwd_exact, table_grad, reduce (terminal readout:
+    // backward: bagg, bscan_local, rounds, bscan_fix, bwd_exact, table_grad, reduce (terminal readout:
     // fwd_tc and bwd_exact once per window of chunk groups)
     if (fwd_launches) *fwd_launches = 6 + rounds + (g.readout == EWS_READOUT_PREFIX ? 1 : 0);
     if (bwd_launches) {
@@ -2843,19 +2808,15 @@ extern "C" int ews_dense_bwd(const ews_dense_args* a, ews_stream_t stream) {
     p.loc = (float*)(fws + F.loc);
     p.lcarry = (float*)(ws + L.carry);
     {
-        const size_t smem = tc::tc_bwd_smem_bytes();
-        if (smem > 227 * 1024) return EWS_ERR_UNSUPPORTED;
-        cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(bwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-        int per_sm = 0;
-        per_sm = resident_ctas((const void*)bwd_tc_kernel, tc::NTH, smem);
-        if (per_sm < 1) return EWS_ERR_UNSUPPORTED;
         const int groups = (g.C + tc::TILES - 1) / tc::TILES;
-        int grid = per_sm * num_sms();
-        if (grid > g.B * groups) grid = g.B * groups;
-        // zero-carry pass (local adjoints) -> reverse scan over the chunks -> exact pass from the carries
-        p.g.bwd_mode = 1;
-        bwd_tc_kernel<<<grid, tc::NTH, smem, s>>>(p);
+        // zero-carry local adjoints (power sums, parallel over the chunks) -> reverse scan over the chunks ->
+        // exact pass from the carries
+        p.pows = (float*)(fws + F.pows);
+        {
+            const size_t bsm = sizeof(float) * (size_t)BGW * bagg_warp_floats();
+            cudaFuncSetAttribute(bagg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
+            bagg_kernel<<<(g.B * g.C + BGW - 1) / BGW, BGW * 32, bsm, s>>>(p);
+        }
         if (cudaGetLastError() != cudaSuccess) return EWS_ERR_LAUNCH;
         p.gsuf = (float*)(ws + L.pows);
         p.gex = (float*)(ws + L.gex);
