@@ -1197,6 +1197,23 @@ static int launch_agg_q(const Params& p, cudaStream_t s) {
 
 // ---------------------------------------------------------------------------------- backward chunk aggregates
 
+// mma.sync without `volatile`: the products have no side effects, so the compiler may interleave the three
+// 3xTF32 passes of independent accumulators instead of issuing each accumulator's passes back to back.
+__device__ __forceinline__ void mma_tf32_free(float d[4], const uint32_t a[4], const uint32_t b[2]) {
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+template <int K>
+__device__ __forceinline__ void tf32_split(const float (&v)[K], uint32_t (&hi)[K], uint32_t (&lo)[K]) {
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+        hi[i] = tf32_hi(v[i]);
+        lo[i] = tf32_lo(v[i], hi[i]);
+    }
+}
+
 constexpr int BGW = 4;   // warps per CTA of bagg_kernel
 constexpr int BES = 40;  // row stride of a staged power complement: B and transposed-A fragment reads conflict-free
 constexpr int BGS = 36;  // row stride of a staged gradient tile: A fragment and float4 row reads conflict-free
@@ -1323,6 +1340,7 @@ __global__ void __launch_bounds__(BGW * 32, 2) bagg_kernel(Params p) {
 #pragma unroll
         for (int sk = 0; sk < 4; ++sk) {
             float af[2][4], bf[4][2];
+            uint32_t ah[2][4], al[2][4], bh[4][2], bl[4][2];
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
                 const float* gr = G + (16 * mt + gq) * BGS + 8 * sk + cq;
@@ -1330,17 +1348,29 @@ __global__ void __launch_bounds__(BGW * 32, 2) bagg_kernel(Params p) {
                 af[mt][1] = gr[8 * BGS];
                 af[mt][2] = gr[4];
                 af[mt][3] = gr[8 * BGS + 4];
+                tf32_split(af[mt], ah[mt], al[mt]);
             }
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt) {
                 const float* er = E + (8 * sk + cq) * BES + 8 * nt + gq;
                 bf[nt][0] = er[0];
                 bf[nt][1] = er[4 * BES];
+                tf32_split(bf[nt], bh[nt], bl[nt]);
             }
+            // the three passes over all eight accumulators (hi hi, hi lo, lo hi: each accumulator's order as
+            // in mma3_m16n8k8)
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt) mma3_m16n8k8(h[mt][nt], af[mt], bf[nt]);
+                for (int nt = 0; nt < 4; ++nt) mma_tf32_free(h[mt][nt], ah[mt], bh[nt]);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) mma_tf32_free(h[mt][nt], ah[mt], bl[nt]);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) mma_tf32_free(h[mt][nt], al[mt], bh[nt]);
         }
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
@@ -1354,34 +1384,53 @@ __global__ void __launch_bounds__(BGW * 32, 2) bagg_kernel(Params p) {
                 }
         __syncwarp();
         // E^T H (A[i][k] = E[k][i], B[k][n] = H[k][n]); mu2 += H - E^T H
+        {
+            float tt[2][4][4];
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-            float tt[4][4];
+            for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt)
+                for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-                for (int v = 0; v < 4; ++v) tt[nt][v] = 0.f;
+                    for (int v = 0; v < 4; ++v) tt[mt][nt][v] = 0.f;
 #pragma unroll
             for (int sk = 0; sk < 4; ++sk) {
-                float af[4], bf[4][2];
-                const float* ec = E + (8 * sk + cq) * BES + 16 * mt + gq;
-                af[0] = ec[0];
-                af[1] = ec[8];
-                af[2] = ec[4 * BES];
-                af[3] = ec[4 * BES + 8];
+                float af[2][4], bf[4][2];
+                uint32_t ah[2][4], al[2][4], bh[4][2], bl[4][2];
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    const float* ec = E + (8 * sk + cq) * BES + 16 * mt + gq;
+                    af[mt][0] = ec[0];
+                    af[mt][1] = ec[8];
+                    af[mt][2] = ec[4 * BES];
+                    af[mt][3] = ec[4 * BES + 8];
+                    tf32_split(af[mt], ah[mt], al[mt]);
+                }
 #pragma unroll
                 for (int nt = 0; nt < 4; ++nt) {
                     const float* hr = Hs + (8 * sk + cq) * BHS + 8 * nt + gq;
                     bf[nt][0] = hr[0];
                     bf[nt][1] = hr[4 * BHS];
+                    tf32_split(bf[nt], bh[nt], bl[nt]);
                 }
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt) mma3_m16n8k8(tt[nt], af, bf[nt]);
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < 4; ++nt) mma_tf32_free(tt[mt][nt], ah[mt], bh[nt]);
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < 4; ++nt) mma_tf32_free(tt[mt][nt], ah[mt], bl[nt]);
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < 4; ++nt) mma_tf32_free(tt[mt][nt], al[mt], bh[nt]);
             }
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt)
+            for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int v = 0; v < 4; ++v) m2[mt][nt][v] += h[mt][nt][v] - tt[nt][v];
+                for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) m2[mt][nt][v] += h[mt][nt][v] - tt[mt][nt][v];
         }
         // mu1 += w - E^T w
         float tw0 = 0.f, tw1 = 0.f;
