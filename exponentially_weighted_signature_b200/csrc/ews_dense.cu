@@ -2577,11 +2577,12 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
     if (a->chunk > 0) {
         g->Lc = a->chunk;
     } else {
-        // The chains stack 4 chunks of a sample per CTA: the forward's output pass and the backward's
-        // zero-carry pass run 3 CTAs per SM, the exact pass 2. Pick the chunk length that minimises the
-        // passes' waves x (steps + a per-tile overhead of ~10 steps), weighted by their measured costs per
-        // wave-step (~5.8 us for each of the first two, ~11.7 us for the exact pass at N = 32), plus the
-        // scans and per-chunk kernels, which grow with the number of chunks (~0.13 us each).
+        // The chains stack 4 chunks of a sample per CTA: the forward's output pass runs 3 CTAs per SM, the
+        // backward's exact pass 2 (the zero-carry adjoints are power sums, whose cost does not depend on the
+        // chunk length). Pick the chunk length that minimises the passes' waves x (steps + a per-tile
+        // overhead of ~10 steps), weighted by their measured costs per wave-step (~5.8 us for the output
+        // pass, ~11.7 us for the exact pass at N = 32), plus the scans and per-chunk kernels, which grow
+        // with the number of chunks (~0.13 us each).
         const int sms = num_sms();
         double best = 1e30;
         int bestL = 256;
@@ -2590,7 +2591,7 @@ static int make_geom(const ews_dense_args* a, Geom* g) {
             const long G = (long)g->B * ((C + 3) / 4);
             const long w3 = (G + 3L * sms - 1) / (3L * sms);
             const long w2 = (G + 2L * sms - 1) / (2L * sms);
-            const double cost = (L + 10.0) * (11.6 * (double)w3 + 11.7 * (double)w2) + 0.13 * (double)g->B * C;
+            const double cost = (L + 10.0) * (5.8 * (double)w3 + 11.7 * (double)w2) + 0.13 * (double)g->B * C;
             if (cost < best) {
                 best = cost;
                 bestL = L;
