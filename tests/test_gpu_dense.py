@@ -136,17 +136,18 @@ def test_identity_lift():
     _assert_fwd(out, ref)
 
 
-@pytest.mark.parametrize("readout", ["prefix", "terminal"])
-def test_config2_full_length(readout):
-    """BASELINE config 2 at full length (T = 17984, N = 32, d = 7, q from the bound), batch reduced to 2
-    for the oracle's memory; forward and gradients (terminal: the backward re-runs the chunks from the
-    forward's carries instead of reading a prefix stream)."""
+@pytest.mark.parametrize("readout,q", [("prefix", 3), ("prefix", 4), ("terminal", 3)])
+def test_config2_full_length(readout, q):
+    """BASELINE config 2 at full length (T = 17984, N = 32, d = 7), batch reduced to 2 for the oracle's
+    memory; forward and gradients at the bench's series order (q = 3, from the truncation bound) and one
+    above it (terminal: the backward re-runs the chunks from the forward's carries instead of reading a
+    prefix stream)."""
     _require_gpu()
     from exponentially_weighted_signature_b200 import workloads
 
     case = workloads.config2(B=2)
     path, clock, A, lift = (_f32(case[k]) for k in ("path", "clock", "A", "lift"))
-    args = (path, clock, A, lift, readout, 4)
+    args = (path, clock, A, lift, readout, q)
     T = path.shape[1] - 1
     shape = (2, T, 1 + 32 + 32 * 32) if readout == "prefix" else (2, 1 + 32 + 32 * 32)
     w = torch.tensor(np.random.default_rng(3).normal(size=shape))
