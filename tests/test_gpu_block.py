@@ -217,3 +217,18 @@ def test_terminal_training_step_keeps_no_prefix_stream():
     for name, a, b in zip(("path", "clock", "A", "lift"), grads["terminal"], grads["prefix"]):
         e = relerr(a.double().cpu(), b.double().cpu())
         assert e <= 1e-5, f"d/d{name}: terminal vs prefix relerr {e:.2e}"
+
+
+def test_config3_terminal_full_length():
+    """Config 3 at full length (T = 2048, N = 8, depth 3, the softplus clock), batch 2: the terminal readout
+    with gradients (every chunk re-run from its carry in the backward) against the oracle."""
+    _require_gpu()
+    from exponentially_weighted_signature_b200 import workloads
+
+    case = workloads.config3(B=2)
+    path, clock, A, lift = (_f32(case[k]) for k in ("path", "clock", "A", "lift"))
+    w = torch.randn((2, 1 + 8 + 64 + 512), generator=torch.Generator().manual_seed(11), dtype=torch.float64)
+    ref, gref = _oracle(path, clock, A, lift, "terminal", q=5, w=w)
+    out, gout = _kernel(path, clock, A, lift, "terminal", q=5, w=w)
+    assert relerr(out, ref) <= 1e-5
+    _assert_grads(gout, gref)
